@@ -1,0 +1,574 @@
+// Warp-specialised persistent bf16 GEMM for sm_100a: TMA -> shared-memory ring
+// -> tcgen05.mma (one elected thread) -> double-buffered TMEM accumulators ->
+// four epilogue warps with fused epilogues (RoPE, SwiGLU, residual add,
+// split-K atomic accumulation).
+//
+// Replaces the nn.Linear forward/backward calls of the reference model
+// (chessdecoder/models/model.py:96-108, 119-136) that PyTorch dispatches to
+// cuBLAS.  Roles inside one CTA (192 threads, one CTA per SM):
+//   warp 0      TMA producer (lane 0)
+//   warp 1      TMEM allocator + MMA issuer (lane 0)
+//   warps 2..5  epilogue; warp w owns TMEM lanes 32*(w%4) .. +31
+#include "../../include/cdk.h"
+#include "cdk_common.cuh"
+
+#include <mutex>
+
+namespace cdk {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 bf16 = 128 B = one swizzle row
+constexpr int kThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kBytesA = kBM * kBK * 2;
+  static constexpr int kBytesB = BN * kBK * 2;
+  static constexpr int kStageBytes = kBytesA + kBytesB;
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
+};
+
+struct EpiDev {
+  int kind;
+  int seq_len;
+  int rope_cols;
+  void* out;
+  long long ldo;
+  const float* bias;
+  const float* resid;
+  long long ldr;
+  void* out2;
+  long long ldo2;
+  const __nv_bfloat16* aux;
+  long long ldaux;
+  long long half_n;
+  const float* rope;
+};
+
+struct GemmParams {
+  int M, N, K;
+  int m_tiles, n_tiles, splits, k_tiles, k_per_split;
+  int dual;      // SWIGLU: B tile = rows [n0, n0+BN/2) and [n0+b_off, ...)
+  int b_off;
+  EpiDev epi;
+};
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
+
+// ---- epilogue store helpers (one thread = one row, 32 consecutive columns) --
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float (&v)[32], int ncols) {
+  if (ncols >= 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+    #pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = pack_bf16(v[8 * q + 0], v[8 * q + 1]);
+      w.y = pack_bf16(v[8 * q + 2], v[8 * q + 3]);
+      w.z = pack_bf16(v[8 * q + 4], v[8 * q + 5]);
+      w.w = pack_bf16(v[8 * q + 6], v[8 * q + 7]);
+      d4[q] = w;
+    }
+  } else {
+    #pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < ncols) dst[i] = __float2bfloat16_rn(v[i]);
+  }
+}
+
+__device__ __forceinline__ void store_row_f32(float* dst, const float (&v)[32], int ncols) {
+  if (ncols >= 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    #pragma unroll
+    for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  } else {
+    #pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < ncols) dst[i] = v[i];
+  }
+}
+
+__device__ __forceinline__ void load_row_f32(const float* src, float (&v)[32], int ncols) {
+  if (ncols >= 32 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    #pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 t = s4[q];
+      v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+    }
+  } else {
+    #pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = i < ncols ? src[i] : 0.f;
+  }
+}
+
+__device__ __forceinline__ void load_row_bf16(const __nv_bfloat16* src, float (&v)[32]) {
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+  #pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w = s4[q];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __bfloat1622float2(h[j]);
+      v[8 * q + 2 * j] = f.x;
+      v[8 * q + 2 * j + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ void atomic_row_f32(float* dst, const float (&v)[32], int ncols) {
+  if (ncols >= 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    #pragma unroll
+    for (int q = 0; q < 8; ++q) atomicAdd(d4 + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+  } else {
+    #pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < ncols) atomicAdd(dst + i, v[i]);
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                     const GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int kStages = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages * Cfg::kBytesA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * Cfg::kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tma_a);
+    prefetch_tmap(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int tiles_mn = p.m_tiles * p.n_tiles;
+  const int units = tiles_mn * p.splits;
+  const int n_step = p.dual ? BN / 2 : BN;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        const int ks = u / tiles_mn;
+        const int rem = u - ks * tiles_mn;
+        const int mt = rem / p.n_tiles;
+        const int nt = rem - mt * p.n_tiles;
+        const int m0 = mt * kBM, n0 = nt * n_step;
+        const int kt0 = ks * p.k_per_split;
+        const int kt1 = min(kt0 + p.k_per_split, p.k_tiles);
+        for (int kt = kt0; kt < kt1; ++kt) {
+          mbar_wait(&empty[stage], phase ^ 1u, abort_flag);
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          uint8_t* a_dst = sA + stage * Cfg::kBytesA;
+          uint8_t* b_dst = sB + stage * Cfg::kBytesB;
+          const int k0 = kt * kBK;
+          if (!A_MN) {
+            tma_load_2d(a_dst, &tma_a, &full[stage], k0, m0);
+          } else {
+            tma_load_2d(a_dst, &tma_a, &full[stage], m0, k0);
+            tma_load_2d(a_dst + 8192, &tma_a, &full[stage], m0 + 64, k0);
+          }
+          if (!B_MN) {
+            if (p.dual) {
+              tma_load_2d(b_dst, &tma_b, &full[stage], k0, n0);
+              tma_load_2d(b_dst + (BN / 2) * 128, &tma_b, &full[stage], k0, n0 + p.b_off);
+            } else {
+              tma_load_2d(b_dst, &tma_b, &full[stage], k0, n0);
+            }
+          } else {
+            #pragma unroll
+            for (int i = 0; i < BN / 64; ++i) tma_load_2d(b_dst + i * 8192, &tma_b, &full[stage], n0 + 64 * i, k0);
+          }
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+        const int ks = u / tiles_mn;
+        const int kt0 = ks * p.k_per_split;
+        const int kt1 = min(kt0 + p.k_per_split, p.k_tiles);
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag);
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kt = kt0; kt < kt1; ++kt) {
+          mbar_wait(&full[stage], phase, abort_flag);
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * Cfg::kBytesA);
+          const uint32_t b_base = smem_u32(sB + stage * Cfg::kBytesB);
+          #pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad =
+                A_MN ? make_sdesc(a_base + kk * 2048, 8192, 1024) : make_sdesc(a_base + kk * 32, 16, 1024);
+            const uint64_t bd =
+                B_MN ? make_sdesc(b_base + kk * 2048, 8192, 1024) : make_sdesc(b_base + kk * 32, 16, 1024);
+            umma_f16(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        tc_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps ----------------
+    const int quad = warp & 3;
+    const EpiDev& e = p.epi;
+    int local = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      const int rem = u % tiles_mn;
+      const int mt = rem / p.n_tiles;
+      const int nt = rem - mt * p.n_tiles;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      mbar_wait(&tfull[acc], acc_phase, abort_flag);
+      tc_fence_after();
+      const int row = mt * kBM + quad * 32 + lane;
+      const bool row_ok = row < p.M;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
+
+      if (e.kind == CDK_EPI_SWIGLU) {
+        // TMEM columns [0, BN/2) = gate, [BN/2, BN) = up, for u-columns n0 ...
+        const int n0 = nt * (BN / 2);
+        #pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          const int col = n0 + c * 32;
+          if (col >= p.N) break;
+          float g[32], up[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, g);
+          tmem_ld_32x32b_x32(tbase + BN / 2 + c * 32, up);
+          if (row_ok) {
+            const int nc = min(32, p.N - col);
+            __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(e.out2) + (long long)row * e.ldo2;
+            store_row_bf16(gu + col, g, nc);
+            store_row_bf16(gu + e.half_n + col, up, nc);
+            float h[32];
+            #pragma unroll
+            for (int i = 0; i < 32; ++i) h[i] = silu_f(g[i]) * up[i];
+            store_row_bf16(reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo + col, h, nc);
+          }
+        }
+      } else {
+        const int n0 = nt * BN;
+        #pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          const int col = n0 + c * 32;
+          if (col >= p.N) break;
+          float v[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, v);
+          if (!row_ok) continue;
+          const int nc = min(32, p.N - col);
+          if (e.bias != nullptr) {
+            #pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < nc) v[i] += e.bias[col + i];
+          }
+          switch (e.kind) {
+            case CDK_EPI_STORE_BF16:
+              store_row_bf16(reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo + col, v, nc);
+              break;
+            case CDK_EPI_STORE_F32:
+              store_row_f32(reinterpret_cast<float*>(e.out) + (long long)row * e.ldo + col, v, nc);
+              break;
+            case CDK_EPI_RESID_F32: {
+              float r[32];
+              load_row_f32(e.resid + (long long)row * e.ldr + col, r, nc);
+              #pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] += r[i];
+              store_row_f32(reinterpret_cast<float*>(e.out) + (long long)row * e.ldo + col, v, nc);
+              break;
+            }
+            case CDK_EPI_ACCUM_F32: {
+              float* dst = reinterpret_cast<float*>(e.out) + (long long)row * e.ldo + col;
+              float r[32];
+              load_row_f32(dst, r, nc);
+              #pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] += r[i];
+              store_row_f32(dst, v, nc);
+              break;
+            }
+            case CDK_EPI_ATOMIC_F32:
+              atomic_row_f32(reinterpret_cast<float*>(e.out) + (long long)row * e.ldo + col, v, nc);
+              break;
+            case CDK_EPI_ROPE_BF16: {
+              if (col < e.rope_cols) {
+                const int pos = row % e.seq_len;
+                const float* cs = e.rope + ((long long)pos * 32 + ((col & 63) >> 1)) * 2;
+                #pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const float c0 = cs[2 * i], s0 = cs[2 * i + 1];
+                  const float x0 = v[2 * i], x1 = v[2 * i + 1];
+                  v[2 * i] = x0 * c0 - x1 * s0;
+                  v[2 * i + 1] = x1 * c0 + x0 * s0;
+                }
+              }
+              store_row_bf16(reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo + col, v, nc);
+              break;
+            }
+            case CDK_EPI_DSWIGLU: {
+              float g[32], up[32];
+              const __nv_bfloat16* gu = e.aux + (long long)row * e.ldaux;
+              load_row_bf16(gu + col, g);
+              load_row_bf16(gu + e.half_n + col, up);
+              float dg[32], du[32];
+              #pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const float sg = 1.f / (1.f + __expf(-g[i]));
+                const float sl = g[i] * sg;
+                du[i] = v[i] * sl;
+                dg[i] = v[i] * up[i] * (sg * (1.f + g[i] * (1.f - sg)));
+              }
+              __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo;
+              store_row_bf16(o + col, dg, nc);
+              store_row_bf16(o + e.half_n + col, du, nc);
+              break;
+            }
+            default:
+              break;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map, 128-byte swizzle: dims {inner, outer}, row pitch in elements.
+static bool make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
+                      uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+static int num_sms(int dev) {
+  static int cache[64] = {0};
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+template <int BN, bool A_MN, bool B_MN>
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
+                       cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kfn = gemm_bf16_kernel<BN, A_MN, B_MN>;
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return (int)e;
+    attr_set[dev] = true;
+  }
+  kfn<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+template <int BN>
+static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                          int grid, cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_gemm<BN, false, false>(ta, tb, p, grid, s);
+  if (!a_mn && b_mn) return launch_gemm<BN, false, true>(ta, tb, p, grid, s);
+  if (a_mn && !b_mn) return launch_gemm<BN, true, false>(ta, tb, p, grid, s);
+  return launch_gemm<BN, true, true>(ta, tb, p, grid, s);
+}
+
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace cdk
+
+extern "C" int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, int64_t M,
+                             int64_t N, int64_t K, const CdkGemmEpilogue* epi, int split_k, void* stream) {
+  using namespace cdk;
+  if (!a || !b || !epi || !epi->out) return -1;
+  if (M <= 0 || N <= 0 || K <= 0) return -2;
+  if (M > (1ll << 31) || N > (1ll << 31) || K > (1ll << 31)) return -2;
+  if (!aligned16(a) || !aligned16(b) || (lda % 8) || (ldb % 8)) return -3;
+  const int kind = epi->kind;
+  if (kind < CDK_EPI_STORE_BF16 || kind > CDK_EPI_ACCUM_F32) return -4;
+  const bool dual = kind == CDK_EPI_SWIGLU;
+  if (dual && (b_mn || epi->half_n != N || (N % 128) || !epi->out2)) return -5;
+  if (kind == CDK_EPI_DSWIGLU && (!epi->aux || epi->half_n < N || (N % 32) || (epi->ldaux % 8) ||
+                                  !aligned16(epi->aux)))
+    return -5;
+  if (kind == CDK_EPI_ROPE_BF16 && (!epi->rope || epi->seq_len <= 0 || (epi->rope_cols % 64))) return -6;
+  if (kind == CDK_EPI_RESID_F32 && !epi->resid) return -7;
+  if (split_k > 1 && kind != CDK_EPI_ATOMIC_F32) return -8;
+
+  // Leading-dimension sanity (the contiguous extent must fit in the pitch).
+  if (!a_mn ? lda < K : lda < M) return -9;
+  if (!b_mn ? ldb < K : ldb < (dual ? 2 * N : N)) return -9;
+
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = num_sms(dev);
+
+  // Tile width: 256 unless the grid would be badly under-filled.
+  int BN = 256;
+  const long long m_tiles = (M + kBM - 1) / kBM;
+  if (!dual) {
+    const long long t256 = m_tiles * ((N + 255) / 256);
+    const long long t128 = m_tiles * ((N + 127) / 128);
+    if (N <= 128) BN = 128;
+    else if (t256 < sms && kind != CDK_EPI_ATOMIC_F32 && t128 > t256) BN = 128;
+  }
+  const int n_step = dual ? BN / 2 : BN;
+  const long long n_tiles = (N + n_step - 1) / n_step;
+  const long long k_tiles = (K + kBK - 1) / kBK;
+
+  int splits = 1;
+  if (kind == CDK_EPI_ATOMIC_F32) {
+    if (split_k > 0) {
+      splits = split_k;
+    } else {
+      // Pick the split that best fills whole waves while keeping >= 8 k-tiles per unit.
+      const long long tiles = m_tiles * n_tiles;
+      double best = -1.0;
+      for (int s = 1; s <= 32; ++s) {
+        if (k_tiles / s < 8 && s > 1) break;
+        const long long units = tiles * s;
+        const long long waves = (units + sms - 1) / sms;
+        const double eff = (double)units / (double)(waves * sms);
+        if (eff > best + 0.02) {
+          best = eff;
+          splits = s;
+        }
+        if (eff > 0.97) break;
+      }
+    }
+  }
+  long long k_per = (k_tiles + splits - 1) / splits;
+  splits = (int)((k_tiles + k_per - 1) / k_per);
+
+  CUtensorMap ta, tb;
+  bool ok;
+  if (!a_mn) ok = make_tmap(&ta, a, K, M, lda, kBK, kBM);
+  else ok = make_tmap(&ta, a, M, K, lda, 64, kBK);
+  if (!ok) return -10;
+  if (!b_mn) ok = make_tmap(&tb, b, K, dual ? 2 * N : N, ldb, kBK, dual ? BN / 2 : BN);
+  else ok = make_tmap(&tb, b, N, K, ldb, 64, kBK);
+  if (!ok) return -11;
+
+  GemmParams p;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.m_tiles = (int)m_tiles;
+  p.n_tiles = (int)n_tiles;
+  p.splits = splits;
+  p.k_tiles = (int)k_tiles;
+  p.k_per_split = (int)k_per;
+  p.dual = dual ? 1 : 0;
+  p.b_off = dual ? (int)N : 0;
+  p.epi.kind = kind;
+  p.epi.seq_len = epi->seq_len;
+  p.epi.rope_cols = epi->rope_cols;
+  p.epi.out = epi->out;
+  p.epi.ldo = epi->ldo;
+  p.epi.bias = epi->bias;
+  p.epi.resid = epi->resid;
+  p.epi.ldr = epi->ldr;
+  p.epi.out2 = epi->out2;
+  p.epi.ldo2 = epi->ldo2;
+  p.epi.aux = reinterpret_cast<const __nv_bfloat16*>(epi->aux);
+  p.epi.ldaux = epi->ldaux;
+  p.epi.half_n = epi->half_n;
+  p.epi.rope = epi->rope;
+
+  const long long units = m_tiles * n_tiles * splits;
+  const int grid = (int)(units < sms ? units : sms);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (BN == 256) return dispatch_major<256>(a_mn, b_mn, ta, tb, p, grid, s);
+  return dispatch_major<128>(a_mn, b_mn, ta, tb, p, grid, s);
+}

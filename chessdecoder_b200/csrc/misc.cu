@@ -1,0 +1,192 @@
+// Small glue kernels: row gathers / scatter-adds around the heads, casts, the
+// device error word, and a tiled fp32 SIMT GEMM for the few contractions that
+// are too small (or too precision-sensitive, like the Fourier projection) to
+// route through the tensor-core path.
+#include "../../include/cdk.h"
+#include "cdk_common.cuh"
+
+namespace cdk {
+
+__device__ int g_error_flag = 0;
+
+__global__ void gather_rows_bf16_kernel(const __nv_bfloat16* __restrict__ src, long long ld_src,
+                                        const int32_t* __restrict__ rows, long long n, int dim8,
+                                        __nv_bfloat16* __restrict__ dst, long long ld_dst) {
+  const int lane = threadIdx.x & 31;
+  const long long k = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (k >= n) return;
+  const long long r = rows[k];
+  const uint4* s = reinterpret_cast<const uint4*>(src + r * ld_src);
+  uint4* d = reinterpret_cast<uint4*>(dst + k * ld_dst);
+  for (int i = lane; i < dim8; i += 32) d[i] = s[i];
+}
+
+__global__ void scatter_add_rows_kernel(const float* __restrict__ src, long long ld_src,
+                                        const int32_t* __restrict__ rows, long long n, int dim4,
+                                        float* __restrict__ dst, long long ld_dst) {
+  const int lane = threadIdx.x & 31;
+  const long long k = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (k >= n) return;
+  const long long r = rows[k];
+  const float4* s = reinterpret_cast<const float4*>(src + k * ld_src);
+  float4* d = reinterpret_cast<float4*>(dst + r * ld_dst);
+  for (int i = lane; i < dim4; i += 32) atomicAdd(d + i, s[i]);
+}
+
+__global__ void cast_f32_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    dst[i] = __float2bfloat16_rn(src[i]);
+}
+
+__global__ void add_f32_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ o,
+                               long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    o[i] = a[i] + b[i];
+}
+
+__global__ void scale_f32_kernel(float* __restrict__ x, long long n, float s) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    x[i] *= s;
+}
+
+// C[M,N] = beta*C + sum_k A(m,k) B(n,k) + bias[n]
+//   A(m,k) = a_t ? A[k*lda + m] : A[m*lda + k];  B(n,k) = b_t ? B[k*ldb + n] : B[n*ldb + k]
+// 64x64 tile, 16-deep k slices, 256 threads with a 4x4 micro-tile each.
+__global__ void __launch_bounds__(256) sgemm_kernel(const float* __restrict__ A, long long lda, int a_t,
+                                                    const float* __restrict__ B, long long ldb, int b_t,
+                                                    float* __restrict__ C, long long ldc, int M, int N, int K,
+                                                    const float* __restrict__ bias, int accumulate) {
+  __shared__ float sA[16][64 + 4];
+  __shared__ float sB[16][64 + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+      int kk, mm;
+      if (a_t) { kk = i / 64; mm = i % 64; } else { mm = i / 16; kk = i % 16; }
+      const int gm = m0 + mm, gk = k0 + kk;
+      float va = 0.f;
+      if (gm < M && gk < K) va = a_t ? A[(long long)gk * lda + gm] : A[(long long)gm * lda + gk];
+      sA[kk][mm] = va;
+      int nn;
+      if (b_t) { kk = i / 64; nn = i % 64; } else { nn = i / 16; kk = i % 16; }
+      const int gn = n0 + nn, gk2 = k0 + kk;
+      float vb = 0.f;
+      if (gn < N && gk2 < K) vb = b_t ? B[(long long)gk2 * ldb + gn] : B[(long long)gn * ldb + gk2];
+      sB[kk][nn] = vb;
+    }
+    __syncthreads();
+    #pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float a[4], b[4];
+      #pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = sA[kk][ty * 4 + i];
+      #pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = sB[kk][tx * 4 + j];
+      #pragma unroll
+      for (int i = 0; i < 4; ++i)
+        #pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  #pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int gm = m0 + ty * 4 + i;
+    if (gm >= M) continue;
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gn = n0 + tx * 4 + j;
+      if (gn >= N) continue;
+      float v = acc[i][j] + (bias ? bias[gn] : 0.f);
+      float* c = C + (long long)gm * ldc + gn;
+      *c = accumulate ? *c + v : v;
+    }
+  }
+}
+
+static inline int finish() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+static inline unsigned grid_for(long long n) {
+  long long b = (n + 255) / 256;
+  if (b > 148 * 16) b = 148 * 16;
+  return (unsigned)(b < 1 ? 1 : b);
+}
+
+}  // namespace cdk
+
+using namespace cdk;
+
+extern "C" int cdk_version(void) { return 1; }
+
+extern "C" int cdk_get_error(int* out_flags, int clear) {
+  int v = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return (int)e;
+  e = cudaMemcpyFromSymbol(&v, g_error_flag, sizeof(int));
+  if (e != cudaSuccess) return (int)e;
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_error_flag, &zero, sizeof(int));
+    if (e != cudaSuccess) return (int)e;
+  }
+  if (out_flags) *out_flags = v;
+  return 0;
+}
+
+extern "C" int cdk_gather_rows_bf16(const void* src, int64_t ld_src, const int32_t* rows, int64_t n, int64_t dim,
+                                    void* dst, int64_t ld_dst, void* stream) {
+  if (n == 0) return 0;
+  if (!src || !rows || !dst || dim % 8 || ld_src % 8 || ld_dst % 8) return -1;
+  gather_rows_bf16_kernel<<<(unsigned)((n + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(src), ld_src, rows, n, (int)(dim / 8),
+      reinterpret_cast<__nv_bfloat16*>(dst), ld_dst);
+  return finish();
+}
+
+extern "C" int cdk_scatter_add_rows_f32(const float* src, int64_t ld_src, const int32_t* rows, int64_t n, int64_t dim,
+                                        float* dst, int64_t ld_dst, void* stream) {
+  if (n == 0) return 0;
+  if (!src || !rows || !dst || dim % 4 || ld_src % 4 || ld_dst % 4) return -1;
+  scatter_add_rows_kernel<<<(unsigned)((n + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      src, ld_src, rows, n, (int)(dim / 4), dst, ld_dst);
+  return finish();
+}
+
+extern "C" int cdk_cast_f32_bf16(const float* src, void* dst, int64_t n, void* stream) {
+  if (n == 0) return 0;
+  if (!src || !dst) return -1;
+  cast_f32_bf16_kernel<<<grid_for(n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      src, reinterpret_cast<__nv_bfloat16*>(dst), n);
+  return finish();
+}
+
+extern "C" int cdk_add_f32(const float* a, const float* b, float* out, int64_t n, void* stream) {
+  if (n == 0) return 0;
+  if (!a || !b || !out) return -1;
+  add_f32_kernel<<<grid_for(n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a, b, out, n);
+  return finish();
+}
+
+extern "C" int cdk_scale_f32(float* x, int64_t n, float s, void* stream) {
+  if (n == 0) return 0;
+  if (!x) return -1;
+  scale_f32_kernel<<<grid_for(n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, n, s);
+  return finish();
+}
+
+extern "C" int cdk_gemm_f32(const float* a, int64_t lda, int a_t, const float* b, int64_t ldb, int b_t, float* c,
+                            int64_t ldc, int64_t M, int64_t N, int64_t K, const float* bias, int accumulate,
+                            void* stream) {
+  if (M == 0 || N == 0) return 0;
+  if (!a || !b || !c || M < 0 || N < 0 || K < 0) return -1;
+  if (M > (1 << 24) || N > (1 << 24)) return -2;
+  dim3 grid((unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64));
+  sgemm_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a, lda, a_t, b, ldb, b_t, c, ldc, (int)M,
+                                                                         (int)N, (int)K, bias, accumulate);
+  return finish();
+}

@@ -1,0 +1,216 @@
+// RMSNorm forward/backward (eps 1e-6, statistics in fp32).
+//
+// Replaces torchtune RMSNorm as used by chessdecoder/models/model.py:112-116
+// (restated torchtune-free by the reference at
+// chessdecoder/export/backbone_causal.py:61-64):
+//     y = x * rsqrt(mean(x^2) + eps) * scale
+// One warp per row, 128-bit loads; the row stays in registers between the
+// sum-of-squares and the scaling pass.  The forward writes the bf16 copy that
+// feeds the next GEMM (and optionally an fp32 copy); the backward fuses the
+// residual-gradient add, the bf16 copy of dx for the next GEMM and the
+// per-column scale gradient.
+#include "../../include/cdk.h"
+#include "cdk_common.cuh"
+
+namespace cdk {
+
+template <int VPT>  // float4 per lane; dim = 128 * VPT
+__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ scale,
+                                                          __nv_bfloat16* __restrict__ y16, float* __restrict__ y32,
+                                                          float* __restrict__ rstd, long long rows, float eps) {
+  constexpr int dim = 128 * VPT;
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * dim);
+  float4 v[VPT];
+  float ss = 0.f;
+  #pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    v[i] = xr[lane + 32 * i];
+    ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)dim + eps);
+  const float4* sc = reinterpret_cast<const float4*>(scale);
+  #pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const float4 s = sc[lane + 32 * i];
+    float4 o = make_float4(v[i].x * r * s.x, v[i].y * r * s.y, v[i].z * r * s.z, v[i].w * r * s.w);
+    if (y16) {
+      uint2 w;
+      w.x = pack_bf16(o.x, o.y);
+      w.y = pack_bf16(o.z, o.w);
+      reinterpret_cast<uint2*>(y16 + row * dim)[lane + 32 * i] = w;
+    }
+    if (y32) reinterpret_cast<float4*>(y32 + row * dim)[lane + 32 * i] = o;
+  }
+  if (lane == 0 && rstd) rstd[row] = r;
+}
+
+// Generic fallback for dims that are not a multiple of 128 (dim % 4 == 0 not required).
+__global__ void rmsnorm_fwd_generic(const float* __restrict__ x, const float* __restrict__ scale,
+                                    __nv_bfloat16* __restrict__ y16, float* __restrict__ y32, float* __restrict__ rstd,
+                                    long long rows, int dim, float eps) {
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* xr = x + row * dim;
+  float ss = 0.f;
+  for (int i = lane; i < dim; i += 32) ss += xr[i] * xr[i];
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)dim + eps);
+  for (int i = lane; i < dim; i += 32) {
+    const float o = xr[i] * r * scale[i];
+    if (y16) y16[row * dim + i] = __float2bfloat16_rn(o);
+    if (y32) y32[row * dim + i] = o;
+  }
+  if (lane == 0 && rstd) rstd[row] = r;
+}
+
+template <bool DY_F32>
+__device__ __forceinline__ float4 load_dy4(const void* dy, long long idx4) {
+  if (DY_F32) return reinterpret_cast<const float4*>(dy)[idx4];
+  const uint2 w = reinterpret_cast<const uint2*>(dy)[idx4];
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// dx = dres + r * (g - xhat * mean(g * xhat)),  g = dy * scale, xhat = x * r
+// dscale[c] += sum_rows dy[c] * xhat[c]
+template <int VPT, bool DY_F32>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const void* __restrict__ dy, const float* __restrict__ x,
+                                                          const float* __restrict__ scale,
+                                                          const float* __restrict__ rstd,
+                                                          const float* __restrict__ dres, float* __restrict__ dx,
+                                                          __nv_bfloat16* __restrict__ dx16,
+                                                          float* __restrict__ dscale, long long rows) {
+  constexpr int dim = 128 * VPT;
+  extern __shared__ float red[];  // [8][dim]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float4 ds[VPT];
+  #pragma unroll
+  for (int i = 0; i < VPT; ++i) ds[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 sc[VPT];
+  #pragma unroll
+  for (int i = 0; i < VPT; ++i) sc[i] = reinterpret_cast<const float4*>(scale)[lane + 32 * i];
+
+  for (long long row = (long long)blockIdx.x * 8 + warp; row < rows; row += (long long)gridDim.x * 8) {
+    const float r = rstd[row];
+    float4 xv[VPT], gv[VPT];
+    float dot = 0.f;
+    #pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const long long idx4 = row * (dim / 4) + lane + 32 * i;
+      xv[i] = reinterpret_cast<const float4*>(x)[idx4];
+      const float4 d = load_dy4<DY_F32>(dy, idx4);
+      xv[i] = make_float4(xv[i].x * r, xv[i].y * r, xv[i].z * r, xv[i].w * r);  // xhat
+      gv[i] = make_float4(d.x * sc[i].x, d.y * sc[i].y, d.z * sc[i].z, d.w * sc[i].w);
+      dot += gv[i].x * xv[i].x + gv[i].y * xv[i].y + gv[i].z * xv[i].z + gv[i].w * xv[i].w;
+      ds[i].x += d.x * xv[i].x;
+      ds[i].y += d.y * xv[i].y;
+      ds[i].z += d.z * xv[i].z;
+      ds[i].w += d.w * xv[i].w;
+    }
+    dot = warp_sum(dot) / (float)dim;
+    #pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const long long idx4 = row * (dim / 4) + lane + 32 * i;
+      float4 o = make_float4(r * (gv[i].x - xv[i].x * dot), r * (gv[i].y - xv[i].y * dot),
+                             r * (gv[i].z - xv[i].z * dot), r * (gv[i].w - xv[i].w * dot));
+      if (dres) {
+        const float4 q = reinterpret_cast<const float4*>(dres)[idx4];
+        o.x += q.x;
+        o.y += q.y;
+        o.z += q.z;
+        o.w += q.w;
+      }
+      if (dx) reinterpret_cast<float4*>(dx)[idx4] = o;
+      if (dx16) {
+        uint2 w;
+        w.x = pack_bf16(o.x, o.y);
+        w.y = pack_bf16(o.z, o.w);
+        reinterpret_cast<uint2*>(dx16)[idx4] = w;
+      }
+    }
+  }
+  if (dscale) {
+    #pragma unroll
+    for (int i = 0; i < VPT; ++i) reinterpret_cast<float4*>(red + warp * dim)[lane + 32 * i] = ds[i];
+    __syncthreads();
+    for (int c = threadIdx.x; c < dim; c += blockDim.x) {
+      float s = 0.f;
+      #pragma unroll
+      for (int w = 0; w < 8; ++w) s += red[w * dim + c];
+      atomicAdd(dscale + c, s);
+    }
+  }
+}
+
+static int num_sms_dev() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int VPT>
+static int launch_bwd(const void* dy, int dy_f32, const float* x, const float* scale, const float* rstd,
+                      const float* dres, float* dx, void* dx16, float* dscale, long long rows, cudaStream_t s) {
+  const size_t smem = (size_t)8 * 128 * VPT * sizeof(float);
+  long long blocks = (rows + 7) / 8;
+  const long long cap = (long long)num_sms_dev() * 4;
+  if (blocks > cap) blocks = cap;
+  if (dy_f32) {
+    auto k = rmsnorm_bwd_kernel<VPT, true>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k<<<(unsigned)blocks, 256, smem, s>>>(dy, x, scale, rstd, dres, dx, reinterpret_cast<__nv_bfloat16*>(dx16),
+                                          dscale, rows);
+  } else {
+    auto k = rmsnorm_bwd_kernel<VPT, false>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k<<<(unsigned)blocks, 256, smem, s>>>(dy, x, scale, rstd, dres, dx, reinterpret_cast<__nv_bfloat16*>(dx16),
+                                          dscale, rows);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+}  // namespace cdk
+
+using namespace cdk;
+
+extern "C" int cdk_rmsnorm_fwd(const float* x, const float* scale, void* y_bf16, float* y_f32, float* rstd,
+                               int64_t rows, int64_t dim, float eps, void* stream) {
+  if (!x || !scale || rows < 0 || dim <= 0) return -1;
+  if (rows == 0) return 0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  auto* y16 = reinterpret_cast<__nv_bfloat16*>(y_bf16);
+  switch (dim) {
+    case 256: rmsnorm_fwd_kernel<2><<<blocks, 256, 0, s>>>(x, scale, y16, y_f32, rstd, rows, eps); break;
+    case 512: rmsnorm_fwd_kernel<4><<<blocks, 256, 0, s>>>(x, scale, y16, y_f32, rstd, rows, eps); break;
+    case 768: rmsnorm_fwd_kernel<6><<<blocks, 256, 0, s>>>(x, scale, y16, y_f32, rstd, rows, eps); break;
+    case 1024: rmsnorm_fwd_kernel<8><<<blocks, 256, 0, s>>>(x, scale, y16, y_f32, rstd, rows, eps); break;
+    case 2048: rmsnorm_fwd_kernel<16><<<blocks, 256, 0, s>>>(x, scale, y16, y_f32, rstd, rows, eps); break;
+    default: rmsnorm_fwd_generic<<<blocks, 256, 0, s>>>(x, scale, y16, y_f32, rstd, rows, (int)dim, eps); break;
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+extern "C" int cdk_rmsnorm_bwd(const void* dy, int dy_is_f32, const float* x, const float* scale, const float* rstd,
+                               const float* dres, float* dx, void* dx_bf16, float* dscale, int64_t rows, int64_t dim,
+                               void* stream) {
+  if (!dy || !x || !scale || !rstd || rows < 0) return -1;
+  if (rows == 0) return 0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dim) {
+    case 256: return launch_bwd<2>(dy, dy_is_f32, x, scale, rstd, dres, dx, dx_bf16, dscale, rows, s);
+    case 512: return launch_bwd<4>(dy, dy_is_f32, x, scale, rstd, dres, dx, dx_bf16, dscale, rows, s);
+    case 768: return launch_bwd<6>(dy, dy_is_f32, x, scale, rstd, dres, dx, dx_bf16, dscale, rows, s);
+    case 1024: return launch_bwd<8>(dy, dy_is_f32, x, scale, rstd, dres, dx, dx_bf16, dscale, rows, s);
+    default: return -2;  // backbone widths are multiples of 256 up to 1024
+  }
+}

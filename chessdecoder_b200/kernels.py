@@ -1,0 +1,252 @@
+"""Thin torch-tensor wrappers over the libcdk.so C ABI.
+
+Each wrapper validates dtypes/devices, launches on the current CUDA stream and
+raises ``RuntimeError`` (naming the op and the library's status code) when the
+library rejects a call.  Nothing here computes on the CPU or falls back to
+PyTorch kernels.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+
+EPI_STORE_BF16 = 0
+EPI_STORE_F32 = 1
+EPI_RESID_F32 = 2
+EPI_ROPE_BF16 = 3
+EPI_SWIGLU = 4
+EPI_DSWIGLU = 5
+EPI_ATOMIC_F32 = 6
+EPI_ACCUM_F32 = 7
+
+
+def _p(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _check(rc: int, op: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"cdk op {op} failed with status {rc}")
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("chessdecoder_b200 ops need CUDA tensors (no CPU implementation exists)")
+
+
+def lib():
+    return _lib.load()
+
+
+def get_error(clear: bool = True) -> int:
+    v = C.c_int(0)
+    _check(lib().cdk_get_error(C.byref(v), 1 if clear else 0), "get_error")
+    return v.value
+
+
+# ---------------------------------------------------------------------------
+# GEMM
+# ---------------------------------------------------------------------------
+def _ld(t: torch.Tensor) -> int:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise RuntimeError("GEMM operands must be 2-D with unit inner stride")
+    return t.stride(0)
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False, kind: int = EPI_STORE_BF16,
+         out: torch.Tensor, bias=None, resid=None, out2=None, aux=None, half_n: int = 0, rope=None,
+         seq_len: int = 0, rope_cols: int = 0, split_k: int = 0, M=None, N=None, K=None) -> torch.Tensor:
+    """D = A @ B^T with a fused epilogue (see include/cdk.h for the kinds).
+
+    a: [M,K] (a_mn False) or [K,M] (a_mn True); b: [N,K] (b_mn False) or [K,N].
+    For SWIGLU, b is [2N, K] = [gate; up] and N is the number of output columns.
+    """
+    _need_cuda(a, b, out)
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise RuntimeError("GEMM inputs must be bf16")
+    if M is None:
+        M = a.shape[1] if a_mn else a.shape[0]
+    if K is None:
+        K = a.shape[0] if a_mn else a.shape[1]
+    if N is None:
+        N = b.shape[1] if b_mn else b.shape[0]
+        if kind == EPI_SWIGLU:
+            N //= 2
+    ep = _lib.CdkGemmEpilogue()
+    ep.kind = kind
+    ep.seq_len = seq_len
+    ep.rope_cols = rope_cols
+    ep.out = out.data_ptr()
+    ep.ldo = out.stride(0)
+    ep.bias = bias.data_ptr() if bias is not None else None
+    if resid is not None:
+        ep.resid = resid.data_ptr()
+        ep.ldr = resid.stride(0)
+    if out2 is not None:
+        ep.out2 = out2.data_ptr()
+        ep.ldo2 = out2.stride(0)
+    if aux is not None:
+        ep.aux = aux.data_ptr()
+        ep.ldaux = aux.stride(0)
+    ep.half_n = half_n
+    ep.rope = rope.data_ptr() if rope is not None else None
+    rc = lib().cdk_gemm_bf16(_p(a), _ld(a), int(a_mn), _p(b), _ld(b), int(b_mn), M, N, K, C.byref(ep), split_k,
+                             _stream())
+    _check(rc, f"gemm_bf16(kind={kind}, M={M}, N={N}, K={K}, a_mn={a_mn}, b_mn={b_mn})")
+    return out
+
+
+def gemm_f32(a, b, c, *, a_t=False, b_t=False, bias=None, accumulate=False, M=None, N=None, K=None):
+    """C (+)= op(A) op(B)^T + bias in fp32 (small contractions)."""
+    _need_cuda(a, b, c)
+    if M is None:
+        M = a.shape[1] if a_t else a.shape[0]
+    if K is None:
+        K = a.shape[0] if a_t else a.shape[1]
+    if N is None:
+        N = b.shape[1] if b_t else b.shape[0]
+    rc = lib().cdk_gemm_f32(_p(a), a.stride(0), int(a_t), _p(b), b.stride(0), int(b_t), _p(c), c.stride(0), M, N, K,
+                            _p(bias), int(accumulate), _stream())
+    _check(rc, "gemm_f32")
+    return c
+
+
+# ---------------------------------------------------------------------------
+# Attention
+# ---------------------------------------------------------------------------
+def attn_meta(bid32: torch.Tensor, S: int) -> torch.Tensor:
+    """Per-tile bounds for the prefix mask; bid32 int32 [nseq_prefix, S]."""
+    nseq = bid32.shape[0]
+    n = lib().cdk_attn_meta_elems(nseq, S)
+    meta = torch.empty(max(int(n), 1), dtype=torch.int32, device=bid32.device)
+    _check(lib().cdk_attn_prefix_meta(_p(bid32), nseq, S, _p(meta), _stream()), "attn_prefix_meta")
+    return meta
+
+
+def attn_fwd(qkv, out, lse, nseq, n_causal, S, H, bid32=None, meta=None):
+    _need_cuda(qkv, out, lse)
+    rc = lib().cdk_attn_fwd(_p(qkv), _p(out), _p(lse), nseq, n_causal, S, H, _p(bid32), _p(meta), _stream())
+    _check(rc, "attn_fwd")
+
+
+def attn_bwd(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid32=None, meta=None, rope=None):
+    _need_cuda(qkv, out, dout, lse, dsum, dqkv)
+    rc = lib().cdk_attn_bwd(_p(qkv), _p(out), _p(dout), _p(lse), _p(dsum), _p(dqkv), nseq, n_causal, S, H,
+                            _p(bid32), _p(meta), _p(rope), _stream())
+    _check(rc, "attn_bwd")
+
+
+# ---------------------------------------------------------------------------
+# RMSNorm
+# ---------------------------------------------------------------------------
+def rmsnorm_fwd(x, scale, y16=None, y32=None, rstd=None, eps=1e-6):
+    _need_cuda(x, scale)
+    rows, dim = x.shape
+    rc = lib().cdk_rmsnorm_fwd(_p(x), _p(scale), _p(y16), _p(y32), _p(rstd), rows, dim, eps, _stream())
+    _check(rc, "rmsnorm_fwd")
+
+
+def rmsnorm_bwd(dy, x, scale, rstd, dx=None, dx16=None, dscale=None, dres=None):
+    _need_cuda(dy, x, scale, rstd)
+    rows, dim = x.shape
+    rc = lib().cdk_rmsnorm_bwd(_p(dy), int(dy.dtype == torch.float32), _p(x), _p(scale), _p(rstd), _p(dres), _p(dx),
+                               _p(dx16), _p(dscale), rows, dim, _stream())
+    _check(rc, "rmsnorm_bwd")
+
+
+# ---------------------------------------------------------------------------
+# Embedding / Fourier
+# ---------------------------------------------------------------------------
+def fourier_features(wl_t, d_t, wl_pos_u8, d_pos_u8, wl_c, d_c, freqs, rows32, values_out, feat_out):
+    n = rows32.numel()
+    rc = lib().cdk_fourier_features(_p(wl_t), _p(d_t), _p(wl_pos_u8), _p(d_pos_u8), _p(wl_c), _p(d_c), wl_c.numel(),
+                                    _p(freqs), freqs.numel(), _p(rows32), n, _p(values_out), _p(feat_out), _stream())
+    _check(rc, "fourier_features")
+
+
+def embed_fwd(ids, emb, slot32, frows, out, n_copies=1):
+    n_tok = ids.numel()
+    rc = lib().cdk_embed_fwd(_p(ids), n_tok, emb.shape[0], _p(emb), emb.shape[1], _p(slot32), _p(frows), _p(out),
+                             n_copies, _stream())
+    _check(rc, "embed_fwd")
+
+
+def embed_bwd(ids, dh, slot32, demb, dfrows, n_copies=1):
+    n_tok = ids.numel()
+    rc = lib().cdk_embed_bwd(_p(ids), n_tok, demb.shape[0], _p(dh), demb.shape[1], n_copies, _p(slot32), _p(demb),
+                             _p(dfrows), _stream())
+    _check(rc, "embed_bwd")
+
+
+def fourier_bwd(values, freqs, dfeat, dfreqs):
+    rc = lib().cdk_fourier_bwd(_p(values), _p(freqs), freqs.numel(), _p(dfeat), values.numel(), _p(dfreqs),
+                               _stream())
+    _check(rc, "fourier_bwd")
+
+
+# ---------------------------------------------------------------------------
+# Heads
+# ---------------------------------------------------------------------------
+def softmax_ce(logits, target32, row_w, norm, loss_weight, dlogits=None, dbias=None, loss_out=None, argmax=None,
+               ncls=None):
+    rows = logits.shape[0]
+    ncls = logits.shape[1] if ncls is None else ncls
+    rc = lib().cdk_softmax_ce(_p(logits), logits.stride(0), rows, ncls, _p(target32), _p(row_w), _p(norm),
+                              float(loss_weight), _p(dlogits), dlogits.stride(0) if dlogits is not None else 0,
+                              _p(dbias), _p(loss_out), _p(argmax), _stream())
+    _check(rc, "softmax_ce")
+
+
+def value_tail(z1, w2, b2, target, valid, centers, norm, loss_weight, act_out, dlogits_out, dz1, db1=None,
+               loss_out=None, argmax=None):
+    rows, hidden = z1.shape
+    rc = lib().cdk_value_tail(_p(z1), rows, hidden, _p(w2), _p(b2), w2.shape[0], _p(target), _p(valid), _p(centers),
+                              _p(norm), float(loss_weight), _p(act_out), _p(dlogits_out), _p(dz1), dz1.stride(0),
+                              _p(db1), _p(loss_out), _p(argmax), _stream())
+    _check(rc, "value_tail")
+
+
+def gather_rows_bf16(src, rows32, dst):
+    rc = lib().cdk_gather_rows_bf16(_p(src), src.stride(0), _p(rows32), rows32.numel(), src.shape[1], _p(dst),
+                                    dst.stride(0), _stream())
+    _check(rc, "gather_rows_bf16")
+
+
+def scatter_add_rows(src, rows32, dst):
+    rc = lib().cdk_scatter_add_rows_f32(_p(src), src.stride(0), _p(rows32), rows32.numel(), dst.shape[1], _p(dst),
+                                        dst.stride(0), _stream())
+    _check(rc, "scatter_add_rows_f32")
+
+
+def cast_bf16(src, dst):
+    _check(lib().cdk_cast_f32_bf16(_p(src), _p(dst), src.numel(), _stream()), "cast_f32_bf16")
+
+
+def add_f32(a, b, out):
+    _check(lib().cdk_add_f32(_p(a), _p(b), _p(out), a.numel(), _stream()), "add_f32")
+
+
+def scale_f32(x, s):
+    _check(lib().cdk_scale_f32(_p(x), x.numel(), float(s), _stream()), "scale_f32")
+
+
+# ---------------------------------------------------------------------------
+# Optimizer
+# ---------------------------------------------------------------------------
+def sumsq(x, partial):
+    _check(lib().cdk_sumsq(_p(x), x.numel(), _p(partial), partial.numel(), _stream()), "sumsq")
+
+
+def adamw(p, g, m, v, p_bf16, partial, *, max_norm, lr, beta1, beta2, eps, wd, step, grad_scale=1.0):
+    rc = lib().cdk_adamw(_p(p), _p(g), _p(m), _p(v), _p(p_bf16), p.numel(), _p(partial),
+                         partial.numel() if partial is not None else 0, float(max_norm), float(lr), float(beta1),
+                         float(beta2), float(eps), float(wd), int(step), float(grad_scale), _stream())
+    _check(rc, "adamw")

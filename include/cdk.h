@@ -1,0 +1,168 @@
+/*
+ * cdk.h — C ABI of the chessdecoder_b200 kernel library (libcdk.so, sm_100a).
+ *
+ * Every entry point takes raw device pointers, int64 sizes/leading dimensions
+ * and a cudaStream_t (passed as void*).  The library never allocates or frees
+ * device memory and keeps no pointer past the call: the caller (PyTorch's
+ * caching allocator on the Python side) owns every buffer, including scratch.
+ *
+ * Return value: 0 = launched; < 0 = rejected on the host before launch
+ * (shape, alignment, unsupported combination); > 0 = CUDA error code from the
+ * launch.  Device-side conditions (a bounded wait that timed out, an index out
+ * of range) are latched in a device word read by cdk_get_error().
+ *
+ * The reference implements this step as PyTorch eager code on torchtune
+ * modules; each group below names the reference code it replaces
+ * (paths relative to the ChessDecoder repository).
+ */
+#ifndef CDK_H_
+#define CDK_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status ------------------------------------------------------------ */
+int cdk_version(void);
+/* Reads (and, if clear != 0, clears) the device error word of the current
+ * device.  Synchronises the current device. */
+int cdk_get_error(int* out_flags, int clear);
+
+/* ---- dense contractions (tcgen05 + TMEM + TMA) ---------------------------
+ * Replaces the nn.Linear calls of chessdecoder/models/model.py:96-108
+ * (q/k/v/output projections, SwiGLU gate/up/down) and their autograd
+ * backward, the heads at model.py:119-122 and ValueHead (model.py:39-52).
+ *
+ *   D[M,N] (op)= sum_k A[m,k] * B[n,k]
+ *   A: a_mn == 0 -> row-major [M,K] (K contiguous), pitch lda
+ *      a_mn == 1 -> row-major [K,M] (M contiguous), pitch lda
+ *   B: b_mn == 0 -> row-major [N,K], pitch ldb;  b_mn == 1 -> row-major [K,N]
+ * Inputs bf16, accumulation fp32, output per epilogue kind.
+ */
+enum {
+  CDK_EPI_STORE_BF16 = 0, /* out bf16 = acc (+bias)                               */
+  CDK_EPI_STORE_F32 = 1,  /* out f32  = acc (+bias)                               */
+  CDK_EPI_RESID_F32 = 2,  /* out f32  = resid + acc (+bias); out may alias resid  */
+  CDK_EPI_ROPE_BF16 = 3,  /* out bf16 = rope(acc) on cols < rope_cols, pos = row % seq_len */
+  CDK_EPI_SWIGLU = 4,     /* B = [gate; up] (2*half_n rows, K-major); out = silu(g)*u bf16,
+                             out2 = [g | u] bf16 (up at column offset half_n)      */
+  CDK_EPI_DSWIGLU = 5,    /* acc = d(silu(g)*u); aux = [g | u] bf16; out = [dg | du] bf16 */
+  CDK_EPI_ATOMIC_F32 = 6, /* out f32 += acc with atomics (split-K allowed)          */
+  CDK_EPI_ACCUM_F32 = 7   /* out f32 += acc (plain read-modify-write, no split-K)   */
+};
+
+typedef struct CdkGemmEpilogue {
+  int32_t kind;
+  int32_t seq_len;   /* ROPE: rows are (sequence, position) with position = row % seq_len */
+  int32_t rope_cols; /* ROPE: columns [0, rope_cols) are rotated in interleaved pairs     */
+  int32_t reserved;
+  void* out;
+  int64_t ldo;
+  const float* bias; /* optional per-column bias [N]                                     */
+  const float* resid;
+  int64_t ldr;
+  void* out2;
+  int64_t ldo2;
+  const void* aux;
+  int64_t ldaux;
+  int64_t half_n;    /* SWIGLU / DSWIGLU: column offset of the "up" half                 */
+  const float* rope; /* ROPE: table [seq_len][32][2] = (cos, sin) per position and pair  */
+} CdkGemmEpilogue;
+
+/* split_k: 0 = automatic (ATOMIC_F32 only), 1 = none, >1 = forced (ATOMIC_F32 only). */
+int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, int64_t M, int64_t N,
+                  int64_t K, const CdkGemmEpilogue* epi, int split_k, void* stream);
+
+/* ---- attention -----------------------------------------------------------
+ * Replaces torchtune MultiHeadAttention's SDPA call as used by
+ * chessdecoder/models/model.py:158-171 (pass 1: is_causal; pass 2: bool mask
+ * tril | block_id[i]==block_id[j]).  head_dim is fixed at 64.
+ *
+ * qkv: bf16 [nseq*S, 3*E] rows = tokens, columns [q | k | v], heads of 64.
+ * Sequences [0, n_causal) use the causal mask; sequences [n_causal, nseq) use
+ * the prefix mask with block ids bid[(s - n_causal)*S + i] (int32).
+ * meta: int32 workspace from cdk_attn_prefix_meta (NULL if n_causal == nseq).
+ */
+int cdk_attn_prefix_meta(const int32_t* bid, int64_t nseq_prefix, int64_t S, int32_t* meta, void* stream);
+int64_t cdk_attn_meta_elems(int64_t nseq_prefix, int64_t S);
+int cdk_attn_fwd(const void* qkv, void* out, float* lse, int64_t nseq, int64_t n_causal, int64_t S, int64_t H,
+                 const int32_t* bid, const int32_t* meta, void* stream);
+/* Backward.  dqkv receives [dq | dk | dv] for the pre-RoPE q/k (the inverse
+ * rotation with table `rope` [S][32][2] is applied in the epilogue; rope may
+ * be NULL when q/k were not rotated).  dsum: f32 scratch [nseq*H*S]. */
+int cdk_attn_bwd(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum, void* dqkv,
+                 int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid, const int32_t* meta,
+                 const float* rope, void* stream);
+
+/* ---- RMSNorm (torchtune RMSNorm, eps 1e-6; reference restatement at
+ *      chessdecoder/export/backbone_causal.py:61-64) ------------------------ */
+int cdk_rmsnorm_fwd(const float* x, const float* scale, void* y_bf16, float* y_f32, float* rstd, int64_t rows,
+                    int64_t dim, float eps, void* stream);
+/* dx = dres + rmsnorm'(dy); dx_bf16 optional; dscale accumulated (+=).  dy bf16 or f32 (dy_is_f32). */
+int cdk_rmsnorm_bwd(const void* dy, int dy_is_f32, const float* x, const float* scale, const float* rstd,
+                    const float* dres, float* dx, void* dx_bf16, float* dscale, int64_t rows, int64_t dim,
+                    void* stream);
+
+/* ---- embedding + Fourier value injection (model.py:24-36, 174-180) and the
+ *      bucket snapping of utils/training.py:114-133 / model.py:189-194 ------ */
+int cdk_fourier_features(const float* wl_t, const float* d_t, const uint8_t* wl_pos, const uint8_t* d_pos,
+                         const float* wl_centers, const float* d_centers, int32_t n_buckets, const float* freqs,
+                         int32_t n_freq, const int32_t* rows, int64_t n_rows, float* values_out, float* feat_out,
+                         void* stream);
+int cdk_embed_fwd(const int64_t* ids, int64_t n_tok, int64_t vocab, const float* emb, int64_t dim,
+                  const int32_t* slot, const float* fourier_rows, float* out, int64_t n_copies, void* stream);
+int cdk_embed_bwd(const int64_t* ids, int64_t n_tok, int64_t vocab, const float* dh, int64_t dim, int64_t n_copies,
+                  const int32_t* slot, float* demb, float* dfourier_rows, void* stream);
+int cdk_fourier_bwd(const float* values, const float* freqs, int32_t n_freq, const float* dfeat, int64_t n_rows,
+                    float* dfreqs, void* stream);
+
+/* ---- heads: fused softmax cross-entropy (train/train.py:180-207) and the
+ *      value-head tail + soft two-bucket loss (utils/training.py:24-50) -----
+ * softmax_ce: per row r, ce_r = logsumexp(logits_r) - logits_r[target_r]
+ * (target outside [0, ncls) contributes nothing); *loss_out += sum_r w_r*ce_r*norm;
+ * dlogits (bf16, optional) = (softmax - onehot) * w_r * norm * loss_weight;
+ * dbias (optional) += column sums of dlogits; argmax_out (optional) first max. */
+int cdk_softmax_ce(const float* logits, int64_t ldl, int64_t rows, int64_t ncls, const int32_t* target,
+                   const float* row_weight, const float* norm, float loss_weight, void* dlogits_bf16, int64_t ldd,
+                   float* dbias, float* loss_out, int32_t* argmax_out, void* stream);
+/* value_tail: z1 = first Linear output (bias included) [rows, hidden];
+ * a = mish(z1) -> act_out; logits = a W2^T + b2 [rows, nb]; soft two-bucket CE
+ * against `target` using bucket `centers`, masked by `valid` (1/0), scaled by
+ * *norm; dlogits_out f32 [rows, nb] (for dW2 / db2), dz1 bf16 [rows, ldd]
+ * (for dX / dW1), db1 += column sums of dz1. */
+int cdk_value_tail(const float* z1, int64_t rows, int64_t hidden, const float* w2, const float* b2, int64_t nb,
+                   const float* target, const float* valid, const float* centers, const float* norm,
+                   float loss_weight, float* act_out, float* dlogits_out, void* dz1_bf16, int64_t ldd, float* db1,
+                   float* loss_out, int32_t* argmax_out, void* stream);
+
+/* ---- gathers / scatters / casts around the heads ------------------------ */
+int cdk_gather_rows_bf16(const void* src, int64_t ld_src, const int32_t* rows, int64_t n, int64_t dim, void* dst,
+                         int64_t ld_dst, void* stream);
+int cdk_scatter_add_rows_f32(const float* src, int64_t ld_src, const int32_t* rows, int64_t n, int64_t dim,
+                             float* dst, int64_t ld_dst, void* stream);
+int cdk_cast_f32_bf16(const float* src, void* dst, int64_t n, void* stream);
+int cdk_add_f32(const float* a, const float* b, float* out, int64_t n, void* stream);
+int cdk_scale_f32(float* x, int64_t n, float s, void* stream);
+/* fp32 SIMT GEMM for small / precision-sensitive contractions (Fourier
+ * projection, value-head second Linear): C = (accumulate ? C : 0) + op(A) op(B)^T + bias,
+ * A(m,k) = a_t ? A[k*lda+m] : A[m*lda+k],  B(n,k) = b_t ? B[k*ldb+n] : B[n*ldb+k]. */
+int cdk_gemm_f32(const float* a, int64_t lda, int a_t, const float* b, int64_t ldb, int b_t, float* c, int64_t ldc,
+                 int64_t M, int64_t N, int64_t K, const float* bias, int accumulate, void* stream);
+
+/* ---- optimizer: global grad-norm clip + AdamW (train/train.py:64-68,248-253)
+ *      with the 1/world_size mean of utils/distributed.py:55-67 folded in --- */
+/* partial[i] = sum of squares of a grid-stride slice of x; n_partial <= 4096. */
+int cdk_sumsq(const float* x, int64_t n, float* partial, int64_t n_partial, void* stream);
+/* One AdamW step over a flat buffer; `partial` (from cdk_sumsq over the same
+ * gradients, may be NULL = no clipping) gives the global norm; p_bf16 (optional)
+ * receives bf16(p) after the update. */
+int cdk_adamw(float* p, const float* g, float* m, float* v, void* p_bf16, int64_t n, const float* partial,
+              int64_t n_partial, float max_norm, float lr, float beta1, float beta2, float eps, float wd,
+              int64_t step, float grad_scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CDK_H_ */
