@@ -1,0 +1,327 @@
+"""Benchmark: ChessDecoder training step (pass-1 causal + pass-2 prefix
+forward, backward, clip + AdamW) in bf16 on B200, train tokens/s.
+
+Workload: the ~114M-parameter default pretraining model (E=1024, 16 heads, 12
+layers, d_ff=1536, S=256), per-GPU batch 64 sequences of seeded synthetic
+random-playout games (8-120 plies, truncated), AdamW lr 3e-4 / wd 0.1, clip 10.
+With --gpus N (torchrun, one rank per GPU) each rank has its own game stream
+and the gradients are averaged with bucketed NCCL all-reduces overlapped with
+the backward (weak scaling: per-GPU batch fixed).
+
+  value : tokens/s over all ranks, batch already in HBM, device time (CUDA
+          events around K steps, max over ranks)
+  e2e   : the same step through the public API (TrainStep.step /
+          DataParallelStep.step) from pinned host batches, host index
+          preparation + host-to-device copies + the loss read-back inside the
+          timed region
+  --impl reference : the reference step on the host CPU (fp32 oracle port of
+          chessdecoder/train/train.py:157-253), bounded sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "train tokens/s"
+UNIT = "tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--seq", type=int, default=256)
+    ap.add_argument("--layers", type=int, default=12)
+    ap.add_argument("--pool", type=int, default=4, help="distinct synthetic batches per rank")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-steps", type=int, default=3)
+    return ap.parse_args()
+
+
+def step_flops(cfg, db_list, S):
+    """Algorithmic FLOPs of one step (6 * MACs-per-token * tokens for every
+    linear that the loss needs, + attention over the allowed (q,k) pairs of both
+    passes), averaged over the batch pool."""
+    import numpy as np
+    E, F, L = cfg.embed_dim, cfg.ff, cfg.num_layers
+    p_bb = L * (4 * E * E + 3 * E * F)
+    out = []
+    for b in db_list:
+        B = b["input_ids"].shape[0]
+        T = B * S
+        bid = b["block_id"].numpy()
+        pairs = B * S * (S + 1) // 2  # causal pass
+        for r in range(B):
+            ids = bid[r]
+            same = ids[:, None] == ids[None, :]
+            tri = np.tril(np.ones((S, S), dtype=bool))
+            pairs += int((same | tri).sum())
+        nm = int(b["move_mask"].sum())
+        nd = int(b["wl_positions"].sum())
+        pv = E * cfg.value_hidden_size + cfg.value_hidden_size * cfg.n_buckets
+        f = 6 * T * (2 * p_bb + 41 * E) + 6 * nm * (1924 * E + pv) + 6 * nd * pv + 3 * 4 * E * L * pairs
+        out.append(f)
+    return sum(out) / len(out)
+
+
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.samples = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops_sustained", 1392.1), d.get("bf16_tflops", 1648.1), "measured"
+    return 1400.0, 1590.0, "fallback"
+
+
+def cpu_baseline(batch, cfg_kw, steps, threads=None):
+    """The oracle (fp32 port of the reference step) on the host CPU, bounded sample."""
+    from oracle.model import OracleChessDecoder
+    from oracle.step import train_step
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    torch.manual_seed(0)
+    model = OracleChessDecoder(1968, **cfg_kw)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.1)
+    sample = {k: v[:4] for k, v in batch.items()}
+    train_step(model, opt, sample)  # warm-up
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        train_step(model, opt, sample)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    ntok = sample["input_ids"].numel()
+    return {"value": ntok / t, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"one full fp32 step (both passes, backward, clip, AdamW) on 4 of the batch's sequences "
+                      f"x S={sample['input_ids'].shape[1]}, median of {steps} after 1 warm-up",
+            "step_s": t}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference step on the host CPU (oracle port), rank 0 only."""
+    if rank != 0:
+        return
+    from chessdecoder_b200 import data
+    cfg_kw = dict(embed_dim=1024, num_heads=16, num_layers=args.layers, max_seq_len=args.seq, d_ff=1536)
+    batch = data.synthetic_batches(1, 4, args.seq, seed=0)[0]
+    from oracle.model import OracleChessDecoder
+    from oracle.step import train_step
+    threads = os.cpu_count()
+    torch.set_num_threads(threads)
+    torch.manual_seed(0)
+    model = OracleChessDecoder(1968, **cfg_kw)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.1)
+    for _ in range(args.warmup):
+        train_step(model, opt, batch)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        train_step(model, opt, batch)
+    dt = (time.perf_counter() - t0) / args.steps
+    ntok = batch["input_ids"].numel()
+    v = ntok / dt
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt * 1000, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "ChessDecoder pretraining step, default model (E=1024, 16 heads, 12 layers, "
+                                   f"d_ff=1536), S={args.seq}, bounded CPU sample of 4 sequences per step",
+                       "global_batch": 4, "seq_len": args.seq, "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": "4 sequences per step (fp32 oracle port of train.py:157-253; the "
+                                       "reference model needs torchtune, absent here)"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    from chessdecoder_b200.distributed import setup_distributed, cleanup_distributed
+    rank, local_rank, world = setup_distributed() if args.gpus > 1 or "RANK" in os.environ else (0, 0, 1)
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        cleanup_distributed()
+        return
+    import torch.distributed as dist
+    from chessdecoder_b200 import data, kernels as K
+    from chessdecoder_b200.engine import ModelConfig, TrainStep, prepare_batch
+    from chessdecoder_b200.distributed import DataParallelStep
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = ModelConfig(num_layers=args.layers, max_seq_len=args.seq)
+    step = TrainStep(cfg, device=dev, seed=0)
+    dp = DataParallelStep(step)
+    pool = data.synthetic_batches(args.pool, args.batch, args.seq, seed=1234, rank=rank)
+    dbs = [prepare_batch(b, dev) for b in pool]
+    torch.cuda.synchronize()
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- value: device-resident batches ---------------------------------------
+    for i in range(args.warmup):
+        dp.forward_backward(dbs[i % len(dbs)])
+        dp.optimizer_step()
+    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
+                           else local_rank)
+    K.LAUNCHES[0] = 0
+    gemm_timer = K.GemmTimer()
+    K.GEMM_TIMER = gemm_timer
+    sync_all()
+    sampler.start()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(args.steps):
+        dp.forward_backward(dbs[i % len(dbs)])
+        dp.optimizer_step()
+    ev1.record()
+    sync_all()
+    clocks = sampler.stop()
+    K.GEMM_TIMER = None
+    launches = K.LAUNCHES[0] // args.steps
+    dev_ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    tokens_step = args.batch * args.seq * world
+    value = tokens_step / (dev_ms / 1000.0)
+    gemm_stats = gemm_timer.summary()
+
+    # ---- e2e: public API from host batches -------------------------------------
+    host_pool = []
+    for b in pool:
+        host_pool.append({k: (v.pin_memory() if torch.cuda.is_available() else v) for k, v in b.items()})
+    for i in range(2):
+        dp.step(host_pool[i % len(host_pool)])
+    sync_all()
+    h2d = 0
+    d2h = 0
+    t0 = time.perf_counter()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        losses = dp.step(host_pool[i % len(host_pool)])
+        lv = losses.cpu()  # device -> host read of the step's loss
+        d2h += lv.numel() * lv.element_size()
+    e1.record()
+    sync_all()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    db_tmp = prepare_batch(host_pool[0], dev)
+    h2d = db_tmp.h2d_bytes
+    e2e_value = tokens_step / (e2e_ms / 1000.0)
+
+    # ---- roofline of the dominant kernel (the tcgen05 GEMM) ---------------------
+    peak_sust, peak_burst, peak_kind = measured_peaks()
+    achieved = gemm_stats["tflops"]
+    roofline = {"bound": "tensor", "kernel": "gemm_bf16_kernel (tcgen05)", "achieved": achieved,
+                "peak": peak_sust, "unit": "TFLOP/s", "frac": achieved / peak_sust,
+                "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)",
+                "traffic": None, "launches_per_step": gemm_stats["launches"] // max(args.steps, 1),
+                "share_of_step": gemm_stats["ms"] / args.steps / dev_ms}
+    prof = ROOT / "profiles" / "gemm_traffic.json"
+    if prof.exists():
+        roofline["traffic"] = json.loads(prof.read_text()).get("bytes_per_launch")
+
+    flops = step_flops(cfg, pool, args.seq)
+    mfu_spec = flops / (dev_ms / 1000.0) / 2.25e15
+    mfu_meas = flops / (dev_ms / 1000.0) / (peak_burst * 1e12)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(pool[0], dict(embed_dim=1024, num_heads=16, num_layers=args.layers,
+                                         max_seq_len=args.seq, d_ff=1536), args.cpu_steps)
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "ChessDecoder pretraining step (pass-1 causal + pass-2 prefix fwd, bwd, "
+                                       "clip, AdamW), default model E=1024 H=16 L=%d d_ff=1536" % args.layers,
+                           "global_batch": args.batch * world, "seq_len": args.seq,
+                           "parallelism": f"dp{world}", "per_gpu_batch": args.batch,
+                           "l2": "working set (activations ~11 GB) far larger than L2; no flush needed",
+                           "params": int(step.store.numel)},
+                "mfu": {"vs_spec_2250": mfu_spec, "vs_measured_burst": mfu_meas, "flops_per_step": flops},
+                "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step":
+                        d2h // args.steps, "ms_per_step": e2e_ms},
+                "gpu_launches": launches,
+                "roofline": roofline,
+                "clocks": clocks,
+                "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+    cleanup_distributed()
+
+
+if __name__ == "__main__":
+    main()

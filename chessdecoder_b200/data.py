@@ -1,0 +1,171 @@
+"""Batch producer: seeded synthetic games -> the reference loader's 10 tensors.
+
+Restates, for synthetic games, the tokenisation of
+chessdecoder/dataloader/data.py:51-97 (``game_to_token_ids``) and the
+windowing / tensorisation of chessdecoder/dataloader/loader.py:69-184
+(``ChessIterableDataset.__iter__``):
+
+* per ply: the 68-token board block (always for the first ply, otherwise kept
+  with probability 1 - skip_board_prob), the move token, then ``wl_value`` and
+  ``d_value`` placeholders;
+* a random start among ``[0] + [d_pos + 1 ...]`` (every ply boundary except
+  after the last ply), truncation to ``max_seq_len`` dropping plies whose
+  WL/D placeholders were cut, padding with ``pad``;
+* board targets = next token mapped to the 41-token board sub-vocabulary
+  (-100 elsewhere), overridden at each kept move's stm position by
+  ``generic_move``; move targets (1924 sub-vocabulary) at the stm position;
+  WL/D targets at the placeholders and copied to the stm position;
+* ``block_id`` = board-block index inside blocks, unique ids elsewhere.
+
+Game content replaces the missing lc0 parquet files: uniform-random legal
+playouts (see chessgen.random_game).  Each rank gets its own stream seeded with
+``seed + rank * 7919`` (the rank term of loader.py:36).
+"""
+from __future__ import annotations
+
+import random
+
+import numpy as np
+import torch
+
+from . import vocab as V
+from .chessgen import random_game
+
+IGNORE_INDEX = -100
+KEYS = ("input_ids", "board_target_ids", "move_target_ids", "move_mask", "wl_positions", "d_positions",
+        "wl_targets", "d_targets", "wdl_valid", "block_id")
+
+_FULL_TO_BOARD = np.array(V.full_to_board_table(), dtype=np.int64)
+
+
+def game_to_token_ids(plies, rng: random.Random, skip_board_prob: float = 0.0):
+    """Token ids, move targets, board-block boundaries and value data of one game.
+
+    ``plies`` = [(position_tokens, played_move, best_move, played_q, played_d)].
+    Follows chessdecoder/dataloader/data.py:51-97: one ``rng.random()`` draw per
+    ply after the first decides whether the board block is emitted.
+    """
+    seq, move_targets, blocks, values = [], [], [], []
+    for i, (pos_tokens, played, best, q, d) in enumerate(plies):
+        include_board = (i == 0) or (rng.random() > skip_board_prob)
+        if include_board:
+            block_start = len(seq)
+            seq.extend(pos_tokens)
+        move_idx = len(seq)
+        seq.append(played)
+        if include_board:
+            blocks.append((block_start, move_idx))
+        move_targets.append((move_idx, best))
+        wl_pos = len(seq)
+        seq.append("wl_value")
+        d_pos = len(seq)
+        seq.append("d_value")
+        values.append((wl_pos, d_pos, float(q), float(d), True))
+    ids = [V.token_to_idx[t] for t in seq]
+    return ids, move_targets, blocks, values
+
+
+def tensorize(ids, move_targets, blocks, values, rng: random.Random, max_seq_len: int):
+    """One training row (dict of 10 numpy arrays), as loader.py:69-184 builds it."""
+    valid_starts = [0] + [vd[1] + 1 for vd in values[:-1]]
+    start = rng.choice(valid_starts)
+    ids = ids[start:]
+    move_targets = [(m - start, b) for m, b in move_targets if m >= start]
+    values = [(w - start, d - start, wl, dd, ok) for w, d, wl, dd, ok in values if d >= start]
+    adj = []
+    for b0, b1 in blocks:
+        a0, a1 = b0 - start, b1 - start
+        if a1 > 0 and a0 < len(ids):
+            adj.append((max(0, a0), min(len(ids), a1)))
+    if len(ids) > max_seq_len:
+        ids = ids[:max_seq_len]
+        move_targets = [m for m in move_targets if m[0] < max_seq_len]
+        values = [v for v in values if v[1] < max_seq_len]
+        adj = [(b0, min(b1, max_seq_len)) for b0, b1 in adj if b0 < max_seq_len]
+    values = [v for v in values if v[0] < max_seq_len and v[1] < max_seq_len]
+    valid_moves = {v[0] - 1 for v in values}
+    move_targets = [m for m in move_targets if m[0] in valid_moves]
+
+    S = max_seq_len
+    n = len(ids)
+    input_ids = np.full(S, V.token_to_idx["pad"], dtype=np.int64)
+    input_ids[:n] = ids
+    board_t = np.full(S, IGNORE_INDEX, dtype=np.int64)
+    if n > 1:
+        board_t[: n - 1] = _FULL_TO_BOARD[input_ids[1:n]]
+    move_t = np.full(S, IGNORE_INDEX, dtype=np.int64)
+    move_mask = np.zeros(S, dtype=bool)
+    wl_pos = np.zeros(S, dtype=bool)
+    d_pos = np.zeros(S, dtype=bool)
+    wl_t = np.zeros(S, dtype=np.float32)
+    d_t = np.zeros(S, dtype=np.float32)
+    wdl_valid = np.zeros(S, dtype=bool)
+    generic = V.board_token_to_idx["generic_move"]
+    for m_idx, best in move_targets:
+        stm = m_idx - 1
+        if 0 <= stm < S:
+            board_t[stm] = generic
+            move_t[stm] = V.full_idx_to_move_idx[V.token_to_idx[best]]
+            move_mask[stm] = True
+    for w, d, wl, dd, ok in values:
+        if w < S:
+            wl_pos[w] = True
+            wl_t[w] = wl
+            wdl_valid[w] = ok
+        if d < S:
+            d_pos[d] = True
+            d_t[d] = dd
+            wdl_valid[d] = ok
+        stm = w - 2
+        if 0 <= stm < S:
+            wl_t[stm] = wl
+            d_t[stm] = dd
+            wdl_valid[stm] = ok
+    block_id = np.arange(S, dtype=np.int64) + len(adj)
+    for k, (b0, b1) in enumerate(adj):
+        block_id[b0:b1] = k
+    return {"input_ids": input_ids, "board_target_ids": board_t, "move_target_ids": move_t, "move_mask": move_mask,
+            "wl_positions": wl_pos, "d_positions": d_pos, "wl_targets": wl_t, "d_targets": d_t,
+            "wdl_valid": wdl_valid, "block_id": block_id}
+
+
+class SyntheticGames:
+    """Endless seeded stream of training rows from random-playout games.
+
+    ``min_plies``/``max_plies`` bound the game length (uniform).  Only the
+    plies that can land in the window are generated: the start ply is drawn
+    first (uniform over the game's ply boundaries, as the loader does), and
+    play stops once the window is certainly full.
+    """
+
+    def __init__(self, max_seq_len=256, skip_board_prob=0.2, min_plies=8, max_plies=120, seed=0, rank=0):
+        self.S = max_seq_len
+        self.skip = skip_board_prob
+        self.lo, self.hi = min_plies, max_plies
+        self.rng = random.Random(seed + rank * 7919)
+
+    def row(self):
+        rng = self.rng
+        n_plies = rng.randint(self.lo, self.hi)
+        # a ply costs >= 3 tokens, so no window reaches past start + S/3 + 1 plies
+        plies = random_game(rng, n_plies)
+        ids, mt, blocks, values = game_to_token_ids(plies, rng, self.skip)
+        return tensorize(ids, mt, blocks, values, rng, self.S)
+
+    def batch(self, batch_size: int) -> dict:
+        rows = [self.row() for _ in range(batch_size)]
+        return collate(rows)
+
+
+def collate(rows) -> dict:
+    out = {}
+    for k in KEYS:
+        arr = np.stack([r[k] for r in rows])
+        out[k] = torch.from_numpy(arr)
+    return out
+
+
+def synthetic_batches(n_batches: int, batch_size: int, max_seq_len: int = 256, seed: int = 0, rank: int = 0,
+                      min_plies: int = 8, max_plies: int = 120, skip_board_prob: float = 0.2):
+    src = SyntheticGames(max_seq_len, skip_board_prob, min_plies, max_plies, seed, rank)
+    return [src.batch(batch_size) for _ in range(n_batches)]

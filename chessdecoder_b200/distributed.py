@@ -1,0 +1,231 @@
+"""Data parallelism for the ChessDecoder step: the API of
+chessdecoder/utils/distributed.py (setup_distributed, cleanup_distributed,
+is_main_process, get_device, average_gradients, barrier, print_rank0) plus the
+bucketed, backward-overlapped gradient all-reduce used by the fused step.
+
+The reference averages gradients with one blocking ``all_reduce`` per
+parameter after the backward (utils/distributed.py:55-67).  Here gradients
+live in one flat buffer ordered by when the backward finishes them, so a
+bucket is a contiguous slice: as soon as the backward reports a layer done,
+its slice is all-reduced (SUM) on a dedicated communication stream while the
+next layer is differentiated.  The 1/world_size mean is folded into the
+optimizer kernel (``grad_scale``), so no division pass runs.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+from typing import List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+def setup_distributed(timeout_s: float = 120.0):
+    """torchrun env -> (rank, local_rank, world_size); (0, 0, 1) without torchrun.
+
+    Same contract as utils/distributed.py:18-34, with a finite process-group
+    timeout so that a rank that dies ends its peers' collectives with an error.
+    """
+    if "RANK" not in os.environ:
+        return 0, 0, 1
+    rank = int(os.environ["RANK"])
+    local_rank = int(os.environ.get("LOCAL_RANK", rank))
+    world = int(os.environ["WORLD_SIZE"])
+    if not dist.is_initialized():
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s),
+                                    device_id=torch.device(f"cuda:{local_rank}"))
+        else:
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=timeout_s))
+    return rank, local_rank, world
+
+
+def cleanup_distributed():
+    if dist.is_initialized():
+        dist.destroy_process_group()
+
+
+def is_main_process():
+    return not dist.is_initialized() or dist.get_rank() == 0
+
+
+def get_device(local_rank):
+    return torch.device(f"cuda:{local_rank}")
+
+
+def barrier():
+    if dist.is_initialized():
+        dist.barrier()
+
+
+def print_rank0(*args, **kwargs):
+    if is_main_process():
+        print(*args, **kwargs)
+
+
+def _flat_grad_buffers(model) -> List[torch.Tensor]:
+    """If every gradient is a view into one flat buffer, that buffer (once)."""
+    store = getattr(model, "_store", None)
+    if store is not None:
+        return [store.grad]
+    return []
+
+
+def average_gradients(model, bucket_bytes: int = 25 * 1024 * 1024):
+    """After return every ``p.grad`` holds the mean over ranks (utils/distributed.py:55-67).
+
+    Gradients are reduced in ~25 MB contiguous buckets (the flat store of a
+    chessdecoder_b200 model, otherwise coalesced per bucket) instead of one
+    collective per parameter.  No-op when not distributed.
+    """
+    if not dist.is_initialized():
+        return
+    world = dist.get_world_size()
+    flats = _flat_grad_buffers(model)
+    if flats:
+        for buf in flats:
+            n = bucket_bytes // buf.element_size()
+            for s in range(0, buf.numel(), n):
+                _all_reduce_mean(buf[s:s + n], world)
+        return
+    grads = [p.grad for p in model.parameters() if p.grad is not None]
+    bucket, size = [], 0
+    for g in grads:
+        bucket.append(g)
+        size += g.numel() * g.element_size()
+        if size >= bucket_bytes:
+            _reduce_coalesced(bucket, world)
+            bucket, size = [], 0
+    if bucket:
+        _reduce_coalesced(bucket, world)
+
+
+def _all_reduce_mean(t: torch.Tensor, world: int):
+    if t.is_cuda:
+        dist.all_reduce(t, op=dist.ReduceOp.AVG)
+    else:  # gloo has no AVG
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        t.div_(world)
+
+
+def _reduce_coalesced(grads: List[torch.Tensor], world: int):
+    flat = torch.cat([g.reshape(-1) for g in grads])
+    _all_reduce_mean(flat, world)
+    off = 0
+    for g in grads:
+        n = g.numel()
+        g.copy_(flat[off:off + n].view_as(g))
+        off += n
+
+
+class BucketedAllReduce:
+    """Overlapped SUM all-reduce of a flat gradient buffer.
+
+    ``spans`` maps a backward milestone key to a [start, end) slice of
+    ``flat``; ``ready(key)`` launches that slice's all-reduce on the comm
+    stream after the work already queued on the compute stream.  Adjacent
+    small slices are merged up to ``bucket_bytes``.  ``wait()`` makes the
+    compute stream wait for every launched all-reduce.  Every rank must call
+    ``ready`` with the same keys in the same order (the backward is identical
+    on all ranks), so the collectives match up.
+    """
+
+    def __init__(self, flat: torch.Tensor, spans: List[Tuple[object, int, int]], group=None,
+                 bucket_bytes: int = 25 * 1024 * 1024):
+        self.flat = flat
+        self.group = group
+        self.span_of = {k: (s, e) for k, s, e in spans}
+        self.order = [k for k, _, _ in spans]
+        self.bucket_elems = bucket_bytes // flat.element_size()
+        self.pending_start: Optional[int] = None
+        self.pending_end = 0
+        self.cuda = flat.is_cuda
+        self.stream = torch.cuda.Stream(device=flat.device) if self.cuda else None
+        self.works = []
+        self.launched = 0
+
+    def ready(self, key):
+        s, e = self.span_of[key]
+        if self.pending_start is None:
+            self.pending_start, self.pending_end = s, e
+        else:
+            if s != self.pending_end:
+                self._flush()
+                self.pending_start = s
+            self.pending_end = e
+        if self.pending_end - self.pending_start >= self.bucket_elems or key == self.order[-1]:
+            self._flush()
+
+    def _flush(self):
+        if self.pending_start is None:
+            return
+        s, e = self.pending_start, self.pending_end
+        self.pending_start = None
+        view = self.flat[s:e]
+        if self.cuda:
+            ev = torch.cuda.current_stream(self.flat.device).record_event()
+            self.stream.wait_event(ev)
+            with torch.cuda.stream(self.stream):
+                w = dist.all_reduce(view, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+        else:
+            w = dist.all_reduce(view, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+        self.works.append(w)
+        self.launched += 1
+
+    def wait(self):
+        self._flush()
+        for w in self.works:
+            w.wait()
+        self.works = []
+        if self.cuda:
+            torch.cuda.current_stream(self.flat.device).wait_stream(self.stream)
+
+
+def step_spans(store) -> List[Tuple[object, int, int]]:
+    """Backward milestones of the fused step and the flat slices they finish:
+    key L (heads + final norm), then L-1 .. 0 (layers), then -1 (Fourier +
+    embedding).  Slices tile the whole flat buffer."""
+    L = store.cfg.num_layers
+    spans = []
+    first_layer_start = store.layer_grad_span(L - 1)[0]
+    spans.append((L, 0, first_layer_start))
+    prev_end = first_layer_start
+    for i in reversed(range(L)):
+        s, e = store.layer_grad_span(i)
+        assert s == prev_end, "layer slices must be contiguous in backward order"
+        spans.append((i, s, e))
+        prev_end = e
+    spans.append((-1, prev_end, store.numel))
+    return spans
+
+
+class DataParallelStep:
+    """Wraps engine.TrainStep for N ranks: bucketed overlapped all-reduce during
+    the backward, then clip + AdamW with the 1/world mean folded in."""
+
+    def __init__(self, step, group=None, bucket_bytes: int = 25 * 1024 * 1024):
+        self.step_obj = step
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.reducer = None
+        if self.world > 1:
+            self.reducer = BucketedAllReduce(step.store.grad, step_spans(step.store), group, bucket_bytes)
+            step.grad_hook = self.reducer.ready
+            step.grad_scale = 1.0 / self.world
+
+    def forward_backward(self, db, metrics=None):
+        losses = self.step_obj.forward_backward(db, metrics)
+        if self.reducer is not None:
+            self.reducer.wait()
+        return losses
+
+    def optimizer_step(self):
+        self.step_obj.optimizer_step()
+
+    def step(self, batch, metrics=None):
+        from .engine import prepare_batch
+        db = prepare_batch(batch, self.step_obj.device)
+        losses = self.forward_backward(db, metrics)
+        self.optimizer_step()
+        return losses

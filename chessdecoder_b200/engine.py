@@ -1,0 +1,649 @@
+"""The B200 training step for ChessDecoder: parameter store, fused two-pass
+forward, fused heads and losses, explicit backward and the optimizer step.
+
+This replaces the body of the reference loop, chessdecoder/train/train.py:157-253:
+
+* both passes run as ONE batch of 2B sequences (rows [0, B*S) causal = pass 1,
+  rows [B*S, 2B*S) prefix = pass 2).  They share weights and inputs, so every
+  GEMM is twice as tall and every weight is read once per step instead of
+  twice; the attention kernel applies the causal or the block-prefix mask per
+  sequence;
+* heads run only where the loss looks: the board head on pass-1 rows, the
+  policy head on the gathered move rows, the value heads on gathered WL / D
+  rows (the reference computes policy logits at every position);
+* the backward is written out by hand (no autograd): weight gradients land in
+  one flat fp32 buffer laid out in the order the backward finishes them, so a
+  data-parallel all-reduce can start on a finished layer while the next one is
+  still being differentiated;
+* AdamW, the global-norm clip and the bf16 shadow weights are one kernel over
+  the flat buffers.
+
+Tensors named *_16 are bf16, everything else fp32 unless stated.
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+from typing import Callable, Optional
+
+import numpy as np
+import torch
+
+from . import kernels as K
+from . import vocab as V
+
+IGNORE_INDEX = -100
+
+
+@dataclasses.dataclass
+class ModelConfig:
+    """The ``model:`` section of chessdecoder/train/config.yaml (plus vocab size)."""
+    vocab_size: int = V.vocab_size
+    embed_dim: int = 1024
+    num_heads: int = 16
+    num_layers: int = 12
+    max_seq_len: int = 256
+    d_ff: Optional[int] = 1536
+    n_buckets: int = 100
+    value_hidden_size: int = 256
+    num_fourier_freq: int = 128
+    wl_sigma: float = 0.4
+
+    @property
+    def head_dim(self):
+        return self.embed_dim // self.num_heads
+
+    @property
+    def ff(self):
+        return self.d_ff if self.d_ff is not None else 4 * self.embed_dim
+
+
+def make_wl_buckets(n_buckets=100, sigma=0.4):
+    """chessdecoder/models/model.py:12-16."""
+    t = torch.linspace(0.5 / n_buckets, 1 - 0.5 / n_buckets, n_buckets)
+    return (sigma * math.sqrt(2) * torch.erfinv(2 * t - 1)).clamp(-1.0, 1.0)
+
+
+def make_d_buckets(n_buckets=100):
+    """chessdecoder/models/model.py:19-21."""
+    return torch.linspace(0.5 / n_buckets, 1 - 0.5 / n_buckets, n_buckets)
+
+
+def rope_table(max_seq_len: int, dim: int, base: float = 10000.0) -> torch.Tensor:
+    """RoPE cache [max_seq_len, dim/2, 2] = (cos, sin) of p * base^(-2i/dim)
+    (torchtune RotaryPositionalEmbeddings, used at chessdecoder/models/model.py:87)."""
+    theta = 1.0 / (base ** (torch.arange(0, dim, 2)[: dim // 2].float() / dim))
+    ang = torch.einsum("i,j->ij", torch.arange(max_seq_len, dtype=theta.dtype), theta).float()
+    return torch.stack([torch.cos(ang), torch.sin(ang)], dim=-1).contiguous()
+
+
+# ---------------------------------------------------------------------------
+# Parameter store
+# ---------------------------------------------------------------------------
+def param_specs(cfg: ModelConfig):
+    """(name, shape) of every trainable parameter, in flat-buffer order: the
+    order in which the backward produces final gradients (heads, final norm,
+    layers last to first, Fourier encoder, embedding)."""
+    E, F, L = cfg.embed_dim, cfg.ff, cfg.num_layers
+    hv, nb, nf = cfg.value_hidden_size, cfg.n_buckets, cfg.num_fourier_freq
+    specs = [("board_head.weight", (V.board_vocab_size, E)), ("board_head.bias", (V.board_vocab_size,)),
+             ("policy_head.weight", (V.move_vocab_size, E)), ("policy_head.bias", (V.move_vocab_size,))]
+    for h in ("wl_head", "d_head"):
+        specs += [(f"{h}.mlp.0.weight", (hv, E)), (f"{h}.mlp.0.bias", (hv,)), (f"{h}.mlp.2.weight", (nb, hv)),
+                  (f"{h}.mlp.2.bias", (nb,))]
+    specs.append(("norm.scale", (E,)))
+    for i in reversed(range(L)):
+        p = f"layers.{i}."
+        specs += [(p + "attn.q_proj.weight", (E, E)), (p + "attn.k_proj.weight", (E, E)),
+                  (p + "attn.v_proj.weight", (E, E)), (p + "attn.output_proj.weight", (E, E)),
+                  (p + "mlp.w1.weight", (F, E)), (p + "mlp.w3.weight", (F, E)), (p + "mlp.w2.weight", (E, F)),
+                  (p + "sa_norm.scale", (E,)), (p + "mlp_norm.scale", (E,))]
+    specs += [("fourier_encoder.frequencies", (1, nf)), ("fourier_encoder.proj.weight", (E, 2 * nf)),
+              ("fourier_encoder.proj.bias", (E,)), ("tok_embedding.weight", (cfg.vocab_size, E))]
+    return specs
+
+
+# Tensors that must stay adjacent (fused GEMM operands): q|k|v and w1|w3.
+_ALIGN = 64  # elements: every parameter starts on a 256-byte boundary
+
+
+class ParamStore:
+    """All trainable parameters in one flat fp32 buffer, with matching flat
+    gradient, AdamW moment and bf16 shadow buffers.  ``param(name)`` returns a
+    view shaped like the reference parameter."""
+
+    def __init__(self, cfg: ModelConfig, device):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.offsets = {}
+        off = 0
+        for name, shape in param_specs(cfg):
+            n = int(np.prod(shape))
+            self.offsets[name] = (off, shape, n)
+            # q/k/v and w1/w3 are packed back to back (no padding) so that the
+            # fused projections read one [3E,E] / [2F,E] matrix.
+            pad = 0 if name.endswith(("q_proj.weight", "k_proj.weight", "mlp.w1.weight")) else _ALIGN
+            off += n if pad == 0 else (n + _ALIGN - 1) // _ALIGN * _ALIGN
+        self.numel = off
+        self.flat = torch.zeros(off, dtype=torch.float32, device=self.device)
+        self.grad = torch.zeros(off, dtype=torch.float32, device=self.device)
+        self.exp_avg = torch.zeros(off, dtype=torch.float32, device=self.device)
+        self.exp_avg_sq = torch.zeros(off, dtype=torch.float32, device=self.device)
+        self.flat16 = torch.zeros(off, dtype=torch.bfloat16, device=self.device)
+        self.step = 0
+        # the thinking head gets no gradient in pretraining (train.py never calls it)
+        E = cfg.embed_dim
+        self.thinking_weight = torch.zeros(V.move_vocab_size, E, device=self.device)
+        self.thinking_bias = torch.zeros(V.move_vocab_size, device=self.device)
+
+    def names(self):
+        return list(self.offsets)
+
+    def _view(self, buf, name):
+        off, shape, n = self.offsets[name]
+        return buf[off:off + n].view(shape)
+
+    def param(self, name):
+        return self._view(self.flat, name)
+
+    def grad_of(self, name):
+        return self._view(self.grad, name)
+
+    def bf16(self, name):
+        return self._view(self.flat16, name)
+
+    def span(self, first: str, last: str, buf=None):
+        """Contiguous view from the start of `first` through the end of `last`."""
+        buf = self.flat16 if buf is None else buf
+        o0 = self.offsets[first][0]
+        o1, _, n1 = self.offsets[last]
+        return buf[o0:o1 + n1]
+
+    def refresh_bf16(self):
+        K.cast_bf16(self.flat, self.flat16)
+
+    # -- state dict in the reference layout ---------------------------------
+    def load_state_dict(self, sd: dict):
+        with torch.no_grad():
+            for name in self.offsets:
+                self.param(name).copy_(sd[name].reshape(self.offsets[name][1]))
+            if "thinking_policy_head.weight" in sd:
+                self.thinking_weight.copy_(sd["thinking_policy_head.weight"])
+                self.thinking_bias.copy_(sd["thinking_policy_head.bias"])
+        self.refresh_bf16()
+
+    def state_dict(self) -> dict:
+        sd = {name: self.param(name).detach().clone() for name in self.offsets}
+        sd["thinking_policy_head.weight"] = self.thinking_weight.clone()
+        sd["thinking_policy_head.bias"] = self.thinking_bias.clone()
+        return sd
+
+    def layer_grad_span(self, i: int):
+        """[start, end) of layer i's gradients in the flat buffer."""
+        p = f"layers.{i}."
+        s = self.offsets[p + "attn.q_proj.weight"][0]
+        o, _, n = self.offsets[p + "mlp_norm.scale"]
+        return s, (o + n + _ALIGN - 1) // _ALIGN * _ALIGN
+
+
+def init_reference_weights(cfg: ModelConfig, seed: int = 0) -> dict:
+    """Initial weights exactly as ``torch.manual_seed(seed); ChessDecoder(...)``
+    draws them (construction order of chessdecoder/models/model.py:84-132:
+    embedding N(0,1); per layer q,k,v,o then gate,down,up with nn.Linear's
+    kaiming-uniform init; norms = 1; board, policy, thinking heads; WL / D value
+    heads; Fourier frequencies N(0,1) then projection)."""
+    import torch.nn as nn
+    g = torch.random.fork_rng()
+    with g:
+        torch.manual_seed(seed)
+        E, F, L = cfg.embed_dim, cfg.ff, cfg.num_layers
+        sd = {}
+        sd["tok_embedding.weight"] = nn.Embedding(cfg.vocab_size, E).weight.data
+        for i in range(L):
+            p = f"layers.{i}."
+            for n in ("q_proj", "k_proj", "v_proj", "output_proj"):
+                sd[p + f"attn.{n}.weight"] = nn.Linear(E, E, bias=False).weight.data
+            sd[p + "mlp.w1.weight"] = nn.Linear(E, F, bias=False).weight.data
+            sd[p + "mlp.w2.weight"] = nn.Linear(F, E, bias=False).weight.data
+            sd[p + "mlp.w3.weight"] = nn.Linear(E, F, bias=False).weight.data
+            sd[p + "sa_norm.scale"] = torch.ones(E)
+            sd[p + "mlp_norm.scale"] = torch.ones(E)
+        sd["norm.scale"] = torch.ones(E)
+        for name, n in (("board_head", V.board_vocab_size), ("policy_head", V.move_vocab_size),
+                        ("thinking_policy_head", V.move_vocab_size)):
+            lin = nn.Linear(E, n)
+            sd[name + ".weight"], sd[name + ".bias"] = lin.weight.data, lin.bias.data
+        for h in ("wl_head", "d_head"):
+            l0 = nn.Linear(E, cfg.value_hidden_size)
+            l2 = nn.Linear(cfg.value_hidden_size, cfg.n_buckets)
+            sd[h + ".mlp.0.weight"], sd[h + ".mlp.0.bias"] = l0.weight.data, l0.bias.data
+            sd[h + ".mlp.2.weight"], sd[h + ".mlp.2.bias"] = l2.weight.data, l2.bias.data
+        sd["fourier_encoder.frequencies"] = torch.randn(1, cfg.num_fourier_freq)
+        lp = nn.Linear(2 * cfg.num_fourier_freq, E)
+        sd["fourier_encoder.proj.weight"], sd["fourier_encoder.proj.bias"] = lp.weight.data, lp.bias.data
+    return sd
+
+
+# ---------------------------------------------------------------------------
+# Batch preparation (host side: index lists, loss normalisers)
+# ---------------------------------------------------------------------------
+@dataclasses.dataclass
+class DeviceBatch:
+    B: int
+    S: int
+    ids: torch.Tensor            # int64 [B*S]
+    wl_t: torch.Tensor           # f32 [B*S]
+    d_t: torch.Tensor            # f32 [B*S]
+    wl_pos: torch.Tensor         # u8 [B*S]
+    d_pos: torch.Tensor          # u8 [B*S]
+    slot: torch.Tensor           # i32 [B*S]   Fourier slot or -1
+    frows: torch.Tensor          # i32 [Nf]    token rows of the Fourier slots
+    bid: torch.Tensor            # i32 [B, S]
+    board_t: torch.Tensor        # i32 [B*S]
+    board_w: torch.Tensor        # f32 [B*S]
+    prow: torch.Tensor           # i32 [Nm]    merged-batch rows of the policy head (pass 2)
+    pt: torch.Tensor             # i32 [Nm]
+    wrow: torch.Tensor           # i32 [Nw]
+    wtgt: torch.Tensor           # f32 [Nw]
+    wvalid: torch.Tensor         # f32 [Nw]
+    drow: torch.Tensor           # i32 [Nd]
+    dtgt: torch.Tensor           # f32 [Nd]
+    dvalid: torch.Tensor         # f32 [Nd]
+    norms: torch.Tensor          # f32 [4] = 1/(count+1e-8) for move, board, wl, d (0 when the loss is 0)
+    h2d_bytes: int = 0
+
+
+def _host_index_lists(b: dict):
+    """Numpy restatement of the index bookkeeping of train.py:180-233."""
+    ids = b["input_ids"].numpy()
+    Bn, S = ids.shape
+    move_mask = b["move_mask"].numpy()
+    wl_pos = b["wl_positions"].numpy()
+    d_pos = b["d_positions"].numpy()
+    board_t = b["board_target_ids"].numpy()
+    move_t = b["move_target_ids"].numpy()
+    wl_t = b["wl_targets"].numpy().astype(np.float32)
+    d_t = b["d_targets"].numpy().astype(np.float32)
+    valid = b["wdl_valid"].numpy()
+    BS = Bn * S
+    # board mask: target != -100 and position >= first move (train.py:183-191)
+    has = move_mask.any(1)
+    first = np.where(has, move_mask.argmax(1), S)
+    board_mask = (board_t != IGNORE_INDEX) & (np.arange(S)[None, :] >= first[:, None])
+    # Fourier slots: every WL or D placeholder
+    fmask = (wl_pos | d_pos).reshape(-1)
+    frows = np.nonzero(fmask)[0].astype(np.int32)
+    slot = np.full(BS, -1, dtype=np.int32)
+    slot[frows] = np.arange(frows.size, dtype=np.int32)
+    # policy rows (pass 2 = second half of the merged batch)
+    mflat = np.nonzero(move_mask.reshape(-1))[0]
+    prow = (BS + mflat).astype(np.int32)
+    pt = move_t.reshape(-1)[mflat].astype(np.int32)
+    # WL rows at stm + 1 (clamped), targets copied to stm by the loader
+    bb, ss = np.nonzero(move_mask)
+    wrow = (BS + bb * S + np.minimum(ss + 1, S - 1)).astype(np.int32)
+    wtgt = wl_t[bb, ss]
+    wvalid = valid[bb, ss].astype(np.float32)
+    # D rows at WL positions, targets at D positions (zipped in row-major order)
+    wpf = np.nonzero(wl_pos.reshape(-1))[0]
+    dpf = np.nonzero(d_pos.reshape(-1))[0]
+    if wpf.size != dpf.size:
+        raise ValueError("wl_positions and d_positions must pair up one to one (train.py:225-230)")
+    drow = (BS + wpf).astype(np.int32)
+    dtgt = d_t.reshape(-1)[dpf]
+    dvalid = valid.reshape(-1)[dpf].astype(np.float32)
+    nb = board_mask.sum()
+    norms = np.array([
+        1.0 / (mflat.size + 1e-8),
+        1.0 / (nb + 1e-8),
+        (1.0 / (wvalid.sum() + 1e-8)) if (wvalid.size and wvalid.sum() > 0) else 0.0,
+        (1.0 / (dvalid.sum() + 1e-8)) if (dvalid.size and dvalid.sum() > 0) else 0.0,
+    ], dtype=np.float32)
+    board_t32 = np.where(board_mask, board_t, IGNORE_INDEX).reshape(-1).astype(np.int32)
+    return dict(ids=ids.reshape(-1).astype(np.int64), wl_t=wl_t.reshape(-1), d_t=d_t.reshape(-1),
+                wl_pos=wl_pos.reshape(-1).astype(np.uint8), d_pos=d_pos.reshape(-1).astype(np.uint8), slot=slot,
+                frows=frows, bid=b["block_id"].numpy().astype(np.int32), board_t=board_t32,
+                board_w=board_mask.reshape(-1).astype(np.float32), prow=prow, pt=pt, wrow=wrow,
+                wtgt=wtgt.astype(np.float32), wvalid=wvalid, drow=drow, dtgt=dtgt.astype(np.float32), dvalid=dvalid,
+                norms=norms), Bn, S
+
+
+def prepare_batch(batch: dict, device) -> DeviceBatch:
+    """Builds the device batch: index lists on the host (numpy), then one
+    pinned host buffer per dtype and one host-to-device copy each."""
+    host = {k: (v.cpu() if torch.is_tensor(v) else torch.as_tensor(v)) for k, v in batch.items()}
+    lists, Bn, S = _host_index_lists(host)
+    groups = {"i64": ["ids"], "f32": ["wl_t", "d_t", "board_w", "wtgt", "wvalid", "dtgt", "dvalid", "norms"],
+              "i32": ["slot", "frows", "bid", "board_t", "prow", "pt", "wrow", "drow"],
+              "u8": ["wl_pos", "d_pos"]}
+    dt = {"i64": torch.int64, "f32": torch.float32, "i32": torch.int32, "u8": torch.uint8}
+    out = {}
+    total = 0
+    for g, names in groups.items():
+        sizes = [lists[n].size for n in names]
+        # 16-byte aligned segments
+        align = 16 // torch.empty(0, dtype=dt[g]).element_size()
+        offs, o = [], 0
+        for s in sizes:
+            offs.append(o)
+            o += (s + align - 1) // align * align
+        hbuf = torch.empty(max(o, 1), dtype=dt[g], pin_memory=torch.cuda.is_available())
+        hv = hbuf.numpy()
+        for n, off, s in zip(names, offs, sizes):
+            hv[off:off + s] = lists[n].reshape(-1)
+        dbuf = hbuf.to(device, non_blocking=True)
+        total += hbuf.numel() * hbuf.element_size()
+        for n, off, s in zip(names, offs, sizes):
+            out[n] = dbuf[off:off + s]
+    out["bid"] = out["bid"].view(Bn, S)
+    return DeviceBatch(B=Bn, S=S, h2d_bytes=total, **out)
+
+
+# ---------------------------------------------------------------------------
+# Backbone (embedding output -> final RMSNorm), forward and backward
+# ---------------------------------------------------------------------------
+class LayerSaved:
+    __slots__ = ("x", "n1", "r1", "qkv", "ao", "lse", "h1", "n2", "r2", "gu", "u")
+
+
+class Backbone:
+    """The 12 transformer layers + final norm over a batch of sequences where
+    the first ``n_causal`` use the causal mask and the rest the prefix mask."""
+
+    def __init__(self, store: ParamStore, cfg: ModelConfig):
+        self.st = store
+        self.cfg = cfg
+        self.rope = rope_table(cfg.max_seq_len, cfg.head_dim).to(store.device)
+
+    def _w(self, i):
+        st, p = self.st, f"layers.{i}."
+        wqkv = st.span(p + "attn.q_proj.weight", p + "attn.v_proj.weight").view(3 * self.cfg.embed_dim,
+                                                                                 self.cfg.embed_dim)
+        w13 = st.span(p + "mlp.w1.weight", p + "mlp.w3.weight").view(2 * self.cfg.ff, self.cfg.embed_dim)
+        return dict(wqkv=wqkv, wo=st.bf16(p + "attn.output_proj.weight"), w13=w13, w2=st.bf16(p + "mlp.w2.weight"),
+                    s1=st.param(p + "sa_norm.scale"), s2=st.param(p + "mlp_norm.scale"))
+
+    def _g(self, i):
+        st, p = self.st, f"layers.{i}."
+        E, F = self.cfg.embed_dim, self.cfg.ff
+        gqkv = st.span(p + "attn.q_proj.weight", p + "attn.v_proj.weight", st.grad).view(3 * E, E)
+        g13 = st.span(p + "mlp.w1.weight", p + "mlp.w3.weight", st.grad).view(2 * F, E)
+        return dict(wqkv=gqkv, wo=st.grad_of(p + "attn.output_proj.weight"), w13=g13,
+                    w2=st.grad_of(p + "mlp.w2.weight"), s1=st.grad_of(p + "sa_norm.scale"),
+                    s2=st.grad_of(p + "mlp_norm.scale"))
+
+    def forward(self, h, nseq, n_causal, S, bid32=None, meta=None, want_f32=False):
+        cfg = self.cfg
+        E, F, H = cfg.embed_dim, cfg.ff, cfg.num_heads
+        T = h.shape[0]
+        dev = h.device
+        saved = []
+        x = h
+        for i in range(cfg.num_layers):
+            w = self._w(i)
+            s = LayerSaved()
+            s.x = x
+            s.n1 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+            s.r1 = torch.empty(T, device=dev)
+            K.rmsnorm_fwd(x, w["s1"], y16=s.n1, rstd=s.r1)
+            s.qkv = torch.empty(T, 3 * E, device=dev, dtype=torch.bfloat16)
+            K.gemm(s.n1, w["wqkv"], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=self.rope, seq_len=S, rope_cols=2 * E)
+            s.ao = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+            s.lse = torch.empty(nseq * H * S, device=dev)
+            K.attn_fwd(s.qkv, s.ao, s.lse, nseq, n_causal, S, H, bid32, meta)
+            s.h1 = torch.empty(T, E, device=dev)
+            K.gemm(s.ao, w["wo"], kind=K.EPI_RESID_F32, out=s.h1, resid=x)
+            s.n2 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+            s.r2 = torch.empty(T, device=dev)
+            K.rmsnorm_fwd(s.h1, w["s2"], y16=s.n2, rstd=s.r2)
+            s.gu = torch.empty(T, 2 * F, device=dev, dtype=torch.bfloat16)
+            s.u = torch.empty(T, F, device=dev, dtype=torch.bfloat16)
+            K.gemm(s.n2, w["w13"], kind=K.EPI_SWIGLU, out=s.u, out2=s.gu, half_n=F)
+            out = torch.empty(T, E, device=dev)
+            K.gemm(s.u, w["w2"], kind=K.EPI_RESID_F32, out=out, resid=s.h1)
+            saved.append(s)
+            x = out
+        hN16 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+        hN32 = torch.empty(T, E, device=dev) if want_f32 else None
+        rN = torch.empty(T, device=dev)
+        K.rmsnorm_fwd(x, self.st.param("norm.scale"), y16=hN16, y32=hN32, rstd=rN)
+        return hN16, hN32, (saved, x, rN, nseq, n_causal, S, bid32, meta)
+
+    def backward(self, dhN, ctx, on_layer_done: Optional[Callable[[int], None]] = None):
+        """dhN: f32 [T,E] gradient of the final-norm output.  Accumulates every
+        backbone weight gradient into the store; returns d(embedding output)."""
+        saved, xL, rN, nseq, n_causal, S, bid32, meta = ctx
+        cfg, st = self.cfg, self.st
+        E, F, H = cfg.embed_dim, cfg.ff, cfg.num_heads
+        T = dhN.shape[0]
+        dev = dhN.device
+        dh = torch.empty(T, E, device=dev)
+        dh16 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+        K.rmsnorm_bwd(dhN, xL, st.param("norm.scale"), rN, dx=dh, dx16=dh16, dscale=st.grad_of("norm.scale"))
+        if on_layer_done is not None:
+            on_layer_done(cfg.num_layers)  # heads + final norm done
+        dgu = torch.empty(T, 2 * F, device=dev, dtype=torch.bfloat16)
+        dn = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+        dh1 = torch.empty(T, E, device=dev)
+        dh1_16 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+        dao = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+        dqkv = torch.empty(T, 3 * E, device=dev, dtype=torch.bfloat16)
+        dsum = torch.empty(nseq * H * S, device=dev)
+        for i in reversed(range(cfg.num_layers)):
+            s = saved[i]
+            w, g = self._w(i), self._g(i)
+            # MLP block
+            K.gemm(dh16, w["w2"], b_mn=True, kind=K.EPI_DSWIGLU, out=dgu, aux=s.gu, half_n=F, N=F)
+            K.gemm(dh16, s.u, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w2"])
+            K.gemm(dgu, w["w13"], b_mn=True, kind=K.EPI_STORE_BF16, out=dn)
+            K.gemm(dgu, s.n2, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w13"])
+            K.rmsnorm_bwd(dn, s.h1, w["s2"], s.r2, dx=dh1, dx16=dh1_16, dscale=g["s2"], dres=dh)
+            # attention block
+            K.gemm(dh1_16, w["wo"], b_mn=True, kind=K.EPI_STORE_BF16, out=dao)
+            K.gemm(dh1_16, s.ao, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wo"])
+            K.attn_bwd(s.qkv, s.ao, dao, s.lse, dsum, dqkv, nseq, n_causal, S, H, bid32, meta, rope=self.rope)
+            K.gemm(dqkv, w["wqkv"], b_mn=True, kind=K.EPI_STORE_BF16, out=dn)
+            K.gemm(dqkv, s.n1, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wqkv"])
+            K.rmsnorm_bwd(dn, s.x, w["s1"], s.r1, dx=dh, dx16=dh16, dscale=g["s1"], dres=dh1)
+            if on_layer_done is not None:
+                on_layer_done(i)
+        return dh
+
+
+# ---------------------------------------------------------------------------
+# Embedding + Fourier front end
+# ---------------------------------------------------------------------------
+class FrontEnd:
+    def __init__(self, store: ParamStore, cfg: ModelConfig):
+        self.st = store
+        self.cfg = cfg
+        self.wl_c = make_wl_buckets(cfg.n_buckets, cfg.wl_sigma).to(store.device)
+        self.d_c = make_d_buckets(cfg.n_buckets).to(store.device)
+
+    def forward(self, db: DeviceBatch, n_copies: int):
+        cfg, st = self.cfg, self.st
+        E, nf = cfg.embed_dim, cfg.num_fourier_freq
+        dev = db.ids.device
+        Nf = db.frows.numel()
+        fvals = torch.empty(max(Nf, 1), device=dev)
+        feat = torch.empty(max(Nf, 1), 2 * nf, device=dev)
+        frows_out = torch.empty(max(Nf, 1), E, device=dev)
+        if Nf:
+            K.fourier_features(db.wl_t, db.d_t, db.wl_pos, db.d_pos, self.wl_c, self.d_c,
+                               st.param("fourier_encoder.frequencies"), db.frows, fvals, feat)
+            K.gemm_f32(feat, st.param("fourier_encoder.proj.weight"), frows_out,
+                       bias=st.param("fourier_encoder.proj.bias"), M=Nf)
+        h0 = torch.empty(n_copies * db.ids.numel(), E, device=dev)
+        K.embed_fwd(db.ids, st.param("tok_embedding.weight"), db.slot, frows_out, h0, n_copies=n_copies)
+        return h0, (fvals, feat, Nf)
+
+    def backward(self, db: DeviceBatch, dh0, ctx, n_copies: int):
+        fvals, feat, Nf = ctx
+        st, cfg = self.st, self.cfg
+        E = cfg.embed_dim
+        dev = dh0.device
+        dfr = torch.empty(max(Nf, 1), E, device=dev)
+        K.embed_bwd(db.ids, dh0, db.slot, st.grad_of("tok_embedding.weight"), dfr, n_copies=n_copies)
+        if Nf:
+            # d proj.weight [E, 2F] += dfr^T feat ; d proj.bias += colsum(dfr) ; dfeat = dfr W
+            K.gemm_f32(dfr, feat, st.grad_of("fourier_encoder.proj.weight"), a_t=True, b_t=True, accumulate=True,
+                       M=E, N=feat.shape[1], K=Nf)
+            ones = torch.ones(1, Nf, device=dev)
+            K.gemm_f32(ones, dfr, st.grad_of("fourier_encoder.proj.bias").view(1, E), b_t=True, accumulate=True,
+                       M=1, N=E, K=Nf)
+            dfeat = torch.empty(Nf, feat.shape[1], device=dev)
+            K.gemm_f32(dfr, st.param("fourier_encoder.proj.weight"), dfeat, b_t=True, M=Nf, N=feat.shape[1], K=E)
+            K.fourier_bwd(fvals[:Nf], st.param("fourier_encoder.frequencies"), dfeat,
+                          st.grad_of("fourier_encoder.frequencies"))
+
+
+# ---------------------------------------------------------------------------
+# Heads + losses (forward and backward in one pass over the gathered rows)
+# ---------------------------------------------------------------------------
+class Heads:
+    """Board head on pass-1 rows, policy head on move rows, WL / D value heads,
+    each with its loss and its gradient; accumulates dL/dhN."""
+
+    def __init__(self, store: ParamStore, cfg: ModelConfig, loss_weights=(5.0, 1.0, 1.0, 1.0)):
+        self.st = store
+        self.cfg = cfg
+        self.w_move, self.w_board, self.w_wl, self.w_d = loss_weights
+        self.wl_c = make_wl_buckets(cfg.n_buckets, cfg.wl_sigma).to(store.device)
+        self.d_c = make_d_buckets(cfg.n_buckets).to(store.device)
+
+    def run(self, db: DeviceBatch, hN16, losses, metrics=None):
+        """losses: f32 [4] (move, board, wl, d), accumulated.  Returns dhN f32 [2*B*S, E]."""
+        st, cfg = self.st, self.cfg
+        E = cfg.embed_dim
+        BS = db.B * db.S
+        dev = hN16.device
+        T = hN16.shape[0]
+        dhN = torch.empty(T, E, device=dev)
+        dhN[BS:].zero_()
+        norms = db.norms
+        # ---- board head over pass-1 rows -----------------------------------
+        nbv = V.board_vocab_size
+        logits = torch.empty(BS, 44, device=dev)
+        K.gemm(hN16[:BS], st.bf16("board_head.weight"), kind=K.EPI_STORE_F32, out=logits,
+               bias=st.param("board_head.bias"), N=nbv)
+        dl = torch.empty(BS, 48, device=dev, dtype=torch.bfloat16)
+        bam = metrics.get("board_argmax") if metrics is not None else None
+        K.softmax_ce(logits, db.board_t, db.board_w, norms[1:2], self.w_board, dlogits=dl,
+                     dbias=st.grad_of("board_head.bias"), loss_out=losses[1:2], argmax=bam, ncls=nbv)
+        K.gemm(dl, st.bf16("board_head.weight"), b_mn=True, kind=K.EPI_STORE_F32, out=dhN[:BS], K=nbv)
+        K.gemm(dl, hN16[:BS], a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=st.grad_of("board_head.weight"),
+               M=nbv, K=BS)
+        # ---- policy head over gathered move rows ----------------------------
+        Nm = db.prow.numel()
+        if Nm:
+            nmv = V.move_vocab_size
+            hp = torch.empty(Nm, E, device=dev, dtype=torch.bfloat16)
+            K.gather_rows_bf16(hN16, db.prow, hp)
+            lp = torch.empty(Nm, nmv, device=dev)
+            K.gemm(hp, st.bf16("policy_head.weight"), kind=K.EPI_STORE_F32, out=lp, bias=st.param("policy_head.bias"))
+            dlp = torch.empty(Nm, 1928, device=dev, dtype=torch.bfloat16)
+            pam = metrics.get("move_argmax") if metrics is not None else None
+            K.softmax_ce(lp, db.pt, None, norms[0:1], self.w_move, dlogits=dlp, dbias=st.grad_of("policy_head.bias"),
+                         loss_out=losses[0:1], argmax=pam, ncls=nmv)
+            dhp = torch.empty(Nm, E, device=dev)
+            K.gemm(dlp, st.bf16("policy_head.weight"), b_mn=True, kind=K.EPI_STORE_F32, out=dhp, K=nmv)
+            K.scatter_add_rows(dhp, db.prow, dhN)
+            K.gemm(dlp, hp, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=st.grad_of("policy_head.weight"),
+                   M=nmv, K=Nm)
+        # ---- value heads ------------------------------------------------------
+        self._value("wl_head", db.wrow, db.wtgt, db.wvalid, self.wl_c, norms[2:3], self.w_wl, hN16, dhN,
+                    losses[2:3])
+        self._value("d_head", db.drow, db.dtgt, db.dvalid, self.d_c, norms[3:4], self.w_d, hN16, dhN, losses[3:4])
+        return dhN
+
+    def _value(self, name, rows, tgt, valid, centers, norm, weight, hN16, dhN, loss):
+        n = rows.numel()
+        if n == 0:
+            return
+        st, cfg = self.st, self.cfg
+        E, hv, nb = cfg.embed_dim, cfg.value_hidden_size, cfg.n_buckets
+        dev = hN16.device
+        x = torch.empty(n, E, device=dev, dtype=torch.bfloat16)
+        K.gather_rows_bf16(hN16, rows, x)
+        z1 = torch.empty(n, hv, device=dev)
+        K.gemm(x, st.bf16(f"{name}.mlp.0.weight"), kind=K.EPI_STORE_F32, out=z1, bias=st.param(f"{name}.mlp.0.bias"))
+        act = torch.empty(n, hv, device=dev)
+        dlog = torch.empty(n, nb, device=dev)
+        dz = torch.empty(n, hv, device=dev, dtype=torch.bfloat16)
+        K.value_tail(z1, st.param(f"{name}.mlp.2.weight"), st.param(f"{name}.mlp.2.bias"), tgt, valid, centers, norm,
+                     weight, act, dlog, dz, db1=st.grad_of(f"{name}.mlp.0.bias"), loss_out=loss)
+        # second Linear: dW2 += dlog^T act, db2 += colsum(dlog)
+        K.gemm_f32(dlog, act, st.grad_of(f"{name}.mlp.2.weight"), a_t=True, b_t=True, accumulate=True, M=nb, N=hv, K=n)
+        ones = torch.ones(1, n, device=dev)
+        K.gemm_f32(ones, dlog, st.grad_of(f"{name}.mlp.2.bias").view(1, nb), b_t=True, accumulate=True, M=1, N=nb,
+                   K=n)
+        # first Linear: dX = dz W1, dW1 += dz^T X
+        dx = torch.empty(n, E, device=dev)
+        K.gemm(dz, st.bf16(f"{name}.mlp.0.weight"), b_mn=True, kind=K.EPI_STORE_F32, out=dx)
+        K.scatter_add_rows(dx, rows, dhN)
+        K.gemm(dz, x, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=st.grad_of(f"{name}.mlp.0.weight"), M=hv,
+               K=n)
+
+
+# ---------------------------------------------------------------------------
+# The training step
+# ---------------------------------------------------------------------------
+class TrainStep:
+    """One optimizer step of ChessDecoder pretraining on B200.
+
+    ``step(batch)`` = prepare_batch + forward_backward + (all-reduce) +
+    clip + AdamW.  ``grad_hook(layer_index)`` (optional) is called as soon as
+    the gradients of a layer are final; the data-parallel wrapper uses it to
+    start bucket all-reduces during the backward.
+    """
+
+    def __init__(self, cfg: ModelConfig, device="cuda", seed=0, lr=3e-4, weight_decay=0.1, betas=(0.9, 0.999),
+                 eps=1e-8, max_norm=10.0, loss_weights=(5.0, 1.0, 1.0, 1.0), state_dict=None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.store = ParamStore(cfg, self.device)
+        sd = state_dict if state_dict is not None else init_reference_weights(cfg, seed)
+        self.store.load_state_dict({k: v.to(self.device) for k, v in sd.items()})
+        self.backbone = Backbone(self.store, cfg)
+        self.front = FrontEnd(self.store, cfg)
+        self.heads = Heads(self.store, cfg, loss_weights)
+        self.lr, self.wd, self.betas, self.eps, self.max_norm = lr, weight_decay, betas, eps, max_norm
+        self.grad_hook: Optional[Callable[[int], None]] = None
+        self.grad_scale = 1.0
+        self.partial = torch.empty(1024, device=self.device)
+        self.loss_weights = loss_weights
+
+    def forward_backward(self, db: DeviceBatch, metrics=None):
+        """Loss forward + full backward into store.grad (zeroed here).  Returns
+        losses f32 [4] = (move, board, wl, d) on the device."""
+        st = self.store
+        st.grad.zero_()
+        B, S = db.B, db.S
+        losses = torch.zeros(4, device=self.device)
+        meta = K.attn_meta(db.bid, S)
+        h0, fctx = self.front.forward(db, n_copies=2)
+        hN16, _, bctx = self.backbone.forward(h0, 2 * B, B, S, db.bid, meta)
+        dhN = self.heads.run(db, hN16, losses, metrics)
+        dh0 = self.backbone.backward(dhN, bctx, self.grad_hook)
+        self.front.backward(db, dh0, fctx, n_copies=2)
+        if self.grad_hook is not None:
+            self.grad_hook(-1)
+        return losses
+
+    def optimizer_step(self):
+        st = self.store
+        st.step += 1
+        K.sumsq(st.grad, self.partial)
+        K.adamw(st.flat, st.grad, st.exp_avg, st.exp_avg_sq, st.flat16, self.partial, max_norm=self.max_norm,
+                lr=self.lr, beta1=self.betas[0], beta2=self.betas[1], eps=self.eps, wd=self.wd, step=st.step,
+                grad_scale=self.grad_scale)
+
+    def step(self, batch: dict, metrics=None):
+        db = prepare_batch(batch, self.device)
+        losses = self.forward_backward(db, metrics)
+        self.optimizer_step()
+        return losses
+
+    @staticmethod
+    def total(losses, weights=(5.0, 1.0, 1.0, 1.0)):
+        return sum(w * losses[i] for i, w in enumerate(weights))

@@ -23,6 +23,35 @@ EPI_ATOMIC_F32 = 6
 EPI_ACCUM_F32 = 7
 
 
+# Number of CUDA kernels this module has launched (bench.py reports it per step).
+LAUNCHES = [0]
+
+
+def _count(n=1):
+    LAUNCHES[0] += n
+
+
+class GemmTimer:
+    """Per-launch CUDA-event timing of the tcgen05 GEMM (events recorded on the
+    launching stream around each launch); FLOPs are the algorithmic 2*M*N*K."""
+
+    def __init__(self):
+        self.records = []
+
+    def add(self, flops, e0, e1):
+        self.records.append((flops, e0, e1))
+
+    def summary(self):
+        torch.cuda.synchronize()
+        ms = sum(e0.elapsed_time(e1) for _, e0, e1 in self.records)
+        fl = sum(f for f, _, _ in self.records)
+        return {"launches": len(self.records), "ms": ms, "flops": fl,
+                "tflops": (fl / (ms * 1e-3) / 1e12) if ms > 0 else 0.0}
+
+
+GEMM_TIMER = None
+
+
 def _p(t):
     return None if t is None else C.c_void_p(t.data_ptr())
 
@@ -98,9 +127,18 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
         ep.ldaux = aux.stride(0)
     ep.half_n = half_n
     ep.rope = rope.data_ptr() if rope is not None else None
+    timer = GEMM_TIMER
+    if timer is not None:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
     rc = lib().cdk_gemm_bf16(_p(a), _ld(a), int(a_mn), _p(b), _ld(b), int(b_mn), M, N, K, C.byref(ep), split_k,
                              _stream())
     _check(rc, f"gemm_bf16(kind={kind}, M={M}, N={N}, K={K}, a_mn={a_mn}, b_mn={b_mn})")
+    _count()
+    if timer is not None:
+        e1.record()
+        timer.add(2.0 * M * N * K * (2 if kind == EPI_SWIGLU else 1), e0, e1)
     return out
 
 
@@ -116,6 +154,7 @@ def gemm_f32(a, b, c, *, a_t=False, b_t=False, bias=None, accumulate=False, M=No
     rc = lib().cdk_gemm_f32(_p(a), a.stride(0), int(a_t), _p(b), b.stride(0), int(b_t), _p(c), c.stride(0), M, N, K,
                             _p(bias), int(accumulate), _stream())
     _check(rc, "gemm_f32")
+    _count(1)
     return c
 
 
@@ -128,6 +167,7 @@ def attn_meta(bid32: torch.Tensor, S: int) -> torch.Tensor:
     n = lib().cdk_attn_meta_elems(nseq, S)
     meta = torch.empty(max(int(n), 1), dtype=torch.int32, device=bid32.device)
     _check(lib().cdk_attn_prefix_meta(_p(bid32), nseq, S, _p(meta), _stream()), "attn_prefix_meta")
+    _count(1)
     return meta
 
 
@@ -135,6 +175,7 @@ def attn_fwd(qkv, out, lse, nseq, n_causal, S, H, bid32=None, meta=None):
     _need_cuda(qkv, out, lse)
     rc = lib().cdk_attn_fwd(_p(qkv), _p(out), _p(lse), nseq, n_causal, S, H, _p(bid32), _p(meta), _stream())
     _check(rc, "attn_fwd")
+    _count(1)
 
 
 def attn_bwd(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid32=None, meta=None, rope=None):
@@ -142,6 +183,7 @@ def attn_bwd(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid32=None, 
     rc = lib().cdk_attn_bwd(_p(qkv), _p(out), _p(dout), _p(lse), _p(dsum), _p(dqkv), nseq, n_causal, S, H,
                             _p(bid32), _p(meta), _p(rope), _stream())
     _check(rc, "attn_bwd")
+    _count(2)
 
 
 # ---------------------------------------------------------------------------
@@ -152,6 +194,7 @@ def rmsnorm_fwd(x, scale, y16=None, y32=None, rstd=None, eps=1e-6):
     rows, dim = x.shape
     rc = lib().cdk_rmsnorm_fwd(_p(x), _p(scale), _p(y16), _p(y32), _p(rstd), rows, dim, eps, _stream())
     _check(rc, "rmsnorm_fwd")
+    _count(1)
 
 
 def rmsnorm_bwd(dy, x, scale, rstd, dx=None, dx16=None, dscale=None, dres=None):
@@ -160,6 +203,7 @@ def rmsnorm_bwd(dy, x, scale, rstd, dx=None, dx16=None, dscale=None, dres=None):
     rc = lib().cdk_rmsnorm_bwd(_p(dy), int(dy.dtype == torch.float32), _p(x), _p(scale), _p(rstd), _p(dres), _p(dx),
                                _p(dx16), _p(dscale), rows, dim, _stream())
     _check(rc, "rmsnorm_bwd")
+    _count(1)
 
 
 # ---------------------------------------------------------------------------
@@ -170,6 +214,7 @@ def fourier_features(wl_t, d_t, wl_pos_u8, d_pos_u8, wl_c, d_c, freqs, rows32, v
     rc = lib().cdk_fourier_features(_p(wl_t), _p(d_t), _p(wl_pos_u8), _p(d_pos_u8), _p(wl_c), _p(d_c), wl_c.numel(),
                                     _p(freqs), freqs.numel(), _p(rows32), n, _p(values_out), _p(feat_out), _stream())
     _check(rc, "fourier_features")
+    _count(1)
 
 
 def embed_fwd(ids, emb, slot32, frows, out, n_copies=1):
@@ -177,6 +222,7 @@ def embed_fwd(ids, emb, slot32, frows, out, n_copies=1):
     rc = lib().cdk_embed_fwd(_p(ids), n_tok, emb.shape[0], _p(emb), emb.shape[1], _p(slot32), _p(frows), _p(out),
                              n_copies, _stream())
     _check(rc, "embed_fwd")
+    _count(1)
 
 
 def embed_bwd(ids, dh, slot32, demb, dfrows, n_copies=1):
@@ -184,12 +230,14 @@ def embed_bwd(ids, dh, slot32, demb, dfrows, n_copies=1):
     rc = lib().cdk_embed_bwd(_p(ids), n_tok, demb.shape[0], _p(dh), demb.shape[1], n_copies, _p(slot32), _p(demb),
                              _p(dfrows), _stream())
     _check(rc, "embed_bwd")
+    _count(1)
 
 
 def fourier_bwd(values, freqs, dfeat, dfreqs):
     rc = lib().cdk_fourier_bwd(_p(values), _p(freqs), freqs.numel(), _p(dfeat), values.numel(), _p(dfreqs),
                                _stream())
     _check(rc, "fourier_bwd")
+    _count(1)
 
 
 # ---------------------------------------------------------------------------
@@ -203,6 +251,7 @@ def softmax_ce(logits, target32, row_w, norm, loss_weight, dlogits=None, dbias=N
                               float(loss_weight), _p(dlogits), dlogits.stride(0) if dlogits is not None else 0,
                               _p(dbias), _p(loss_out), _p(argmax), _stream())
     _check(rc, "softmax_ce")
+    _count(1)
 
 
 def value_tail(z1, w2, b2, target, valid, centers, norm, loss_weight, act_out, dlogits_out, dz1, db1=None,
@@ -212,30 +261,36 @@ def value_tail(z1, w2, b2, target, valid, centers, norm, loss_weight, act_out, d
                               _p(norm), float(loss_weight), _p(act_out), _p(dlogits_out), _p(dz1), dz1.stride(0),
                               _p(db1), _p(loss_out), _p(argmax), _stream())
     _check(rc, "value_tail")
+    _count(1)
 
 
 def gather_rows_bf16(src, rows32, dst):
     rc = lib().cdk_gather_rows_bf16(_p(src), src.stride(0), _p(rows32), rows32.numel(), src.shape[1], _p(dst),
                                     dst.stride(0), _stream())
     _check(rc, "gather_rows_bf16")
+    _count(1)
 
 
 def scatter_add_rows(src, rows32, dst):
     rc = lib().cdk_scatter_add_rows_f32(_p(src), src.stride(0), _p(rows32), rows32.numel(), dst.shape[1], _p(dst),
                                         dst.stride(0), _stream())
     _check(rc, "scatter_add_rows_f32")
+    _count(1)
 
 
 def cast_bf16(src, dst):
     _check(lib().cdk_cast_f32_bf16(_p(src), _p(dst), src.numel(), _stream()), "cast_f32_bf16")
+    _count(1)
 
 
 def add_f32(a, b, out):
     _check(lib().cdk_add_f32(_p(a), _p(b), _p(out), a.numel(), _stream()), "add_f32")
+    _count(1)
 
 
 def scale_f32(x, s):
     _check(lib().cdk_scale_f32(_p(x), x.numel(), float(s), _stream()), "scale_f32")
+    _count(1)
 
 
 # ---------------------------------------------------------------------------
@@ -243,6 +298,7 @@ def scale_f32(x, s):
 # ---------------------------------------------------------------------------
 def sumsq(x, partial):
     _check(lib().cdk_sumsq(_p(x), x.numel(), _p(partial), partial.numel(), _stream()), "sumsq")
+    _count(1)
 
 
 def adamw(p, g, m, v, p_bf16, partial, *, max_norm, lr, beta1, beta2, eps, wd, step, grad_scale=1.0):
@@ -250,3 +306,4 @@ def adamw(p, g, m, v, p_bf16, partial, *, max_norm, lr, beta1, beta2, eps, wd, s
                          partial.numel() if partial is not None else 0, float(max_norm), float(lr), float(beta1),
                          float(beta2), float(eps), float(wd), int(step), float(grad_scale), _stream())
     _check(rc, "adamw")
+    _count(1)

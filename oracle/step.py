@@ -1,0 +1,107 @@
+"""ORACLE (test infrastructure only): the reference training step restated in fp32.
+
+Follows chessdecoder/train/train.py:157-253 with use_amp disabled:
+prepare_fourier_inputs (utils/training.py:114-133) -> pass 1 (causal) ->
+board head + masked CE (:180-194) -> pass 2 (prefix) -> policy head + masked
+CE (:204-207) -> WL head at stm+1 (:210-222) -> D head at WL positions
+(:225-233) -> total loss (:236-241) -> backward -> clip_grad_norm_(10) ->
+AdamW step (:248-253).  ``soft_bucket_loss`` restates utils/training.py:24-50.
+Both helpers are pinned against the reference's own functions by
+tests/golden/utils_reference.pt.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+IGNORE_INDEX = -100
+
+
+def soft_bucket_loss(logits, target_values, bucket_centers, valid_mask):
+    N = target_values.shape[0]
+    nb = bucket_centers.shape[0]
+    if N == 0 or valid_mask.sum() == 0:
+        return torch.tensor(0.0, device=logits.device)
+    diffs = target_values.unsqueeze(-1) - bucket_centers
+    lower = ((diffs >= 0).long().sum(dim=-1) - 1).clamp(0, nb - 2)
+    upper = lower + 1
+    lc, uc = bucket_centers[lower], bucket_centers[upper]
+    w_up = ((target_values - lc) / (uc - lc).clamp(min=1e-8)).clamp(0.0, 1.0)
+    soft = torch.zeros(N, nb, device=logits.device)
+    soft.scatter_(1, lower.unsqueeze(1), (1 - w_up).unsqueeze(1))
+    soft.scatter_(1, upper.unsqueeze(1), w_up.unsqueeze(1))
+    loss = -(soft * F.log_softmax(logits, dim=-1)).sum(dim=-1)
+    return (loss * valid_mask.float()).sum() / (valid_mask.sum() + 1e-8)
+
+
+def prepare_fourier_inputs(model, wl_targets, d_targets, wl_positions, d_positions):
+    wl_in = torch.zeros_like(wl_targets)
+    d_in = torch.zeros_like(d_targets)
+    if wl_positions.any():
+        wl_in[wl_positions] = model.discretize_to_bucket(wl_targets[wl_positions], model.wl_bucket_centers)
+    if d_positions.any():
+        d_in[d_positions] = model.discretize_to_bucket(d_targets[d_positions], model.d_bucket_centers)
+    return wl_in, d_in
+
+
+def step_losses(model, batch, weights=(5.0, 1.0, 1.0, 1.0)):
+    """Forward of one training step; returns a dict of losses and argmax predictions."""
+    move_w, board_w, wl_w, d_w = weights
+    dev = next(model.parameters()).device
+    b = {k: v.to(dev) for k, v in batch.items()}
+    input_ids, board_t, move_t = b["input_ids"], b["board_target_ids"], b["move_target_ids"]
+    move_mask, wl_pos, d_pos = b["move_mask"], b["wl_positions"], b["d_positions"]
+    wl_t, d_t, wdl_valid, block_id = b["wl_targets"], b["d_targets"], b["wdl_valid"], b["block_id"]
+    ce = nn.CrossEntropyLoss(ignore_index=IGNORE_INDEX, reduction="none")
+
+    wl_in, d_in = prepare_fourier_inputs(model, wl_t, d_t, wl_pos, d_pos)
+    h_causal = model(input_ids, mask_type="causal", wl_values=wl_in, d_values=d_in, wl_positions=wl_pos,
+                     d_positions=d_pos)
+    board_logits = model.board_head(h_causal)
+    board_mask = board_t != IGNORE_INDEX
+    first_move = move_mask.int().argmax(dim=1)
+    has_moves = move_mask.any(dim=1)
+    first_move[~has_moves] = move_mask.size(1)
+    idx = torch.arange(move_mask.size(1), device=dev).unsqueeze(0)
+    board_mask = board_mask & ~(idx < first_move.unsqueeze(1))
+    ce_board = ce(board_logits.view(-1, board_logits.shape[-1]), board_t.view(-1)).view(board_t.shape)
+    board_loss = (ce_board * board_mask.float()).sum() / (board_mask.sum() + 1e-8)
+
+    h_prefix = model(input_ids, mask_type="prefix", block_id=block_id, wl_values=wl_in, d_values=d_in,
+                     wl_positions=wl_pos, d_positions=d_pos)
+    move_logits = model.policy_head(h_prefix)
+    ce_move = ce(move_logits.view(-1, move_logits.shape[-1]), move_t.view(-1)).view(move_t.shape)
+    move_loss = (ce_move * move_mask.float()).sum() / (move_mask.sum() + 1e-8)
+
+    nz = move_mask.nonzero(as_tuple=False)
+    wl_logits = d_logits = None
+    if nz.shape[0] > 0:
+        seq = (nz[:, 1] + 1).clamp(max=h_prefix.shape[1] - 1)
+        wl_logits = model.wl_head(h_prefix[nz[:, 0], seq])
+        wl_loss = soft_bucket_loss(wl_logits, wl_t[move_mask], model.wl_bucket_centers, wdl_valid[move_mask])
+    else:
+        wl_loss = torch.tensor(0.0, device=dev)
+    if wl_pos.any():
+        d_logits = model.d_head(h_prefix[wl_pos])
+        d_loss = soft_bucket_loss(d_logits, d_t[d_pos], model.d_bucket_centers, wdl_valid[d_pos])
+    else:
+        d_loss = torch.tensor(0.0, device=dev)
+    total = move_w * move_loss + board_w * board_loss + wl_w * wl_loss + d_w * d_loss
+    return {
+        "total": total, "move": move_loss, "board": board_loss, "wl": wl_loss, "d": d_loss,
+        "board_argmax": board_logits.argmax(-1), "board_mask": board_mask,
+        "move_argmax": move_logits.argmax(-1), "move_mask": move_mask,
+        "wl_argmax": None if wl_logits is None else wl_logits.argmax(-1),
+        "d_argmax": None if d_logits is None else d_logits.argmax(-1),
+    }
+
+
+def train_step(model, optimizer, batch, max_norm=10.0, weights=(5.0, 1.0, 1.0, 1.0)):
+    """One full optimizer step (grad_accum 1); returns the forward's loss dict."""
+    optimizer.zero_grad(set_to_none=True)
+    out = step_losses(model, batch, weights)
+    out["total"].backward()
+    torch.nn.utils.clip_grad_norm_(model.parameters(), max_norm=max_norm)
+    optimizer.step()
+    return out
