@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--pool", type=int, default=4, help="distinct synthetic batches per rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--detail", action="store_true", help="add a per-shape GEMM breakdown to the JSON line")
     return ap.parse_args()
 
 
@@ -254,7 +255,7 @@ def main():
     dev_ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
     tokens_step = args.batch * args.seq * world
     value = tokens_step / (dev_ms / 1000.0)
-    gemm_stats = gemm_timer.summary()
+    gemm_stats = gemm_timer.summary(detail=args.detail)
 
     # ---- e2e: public API from host batches -------------------------------------
     host_pool = []
@@ -317,6 +318,8 @@ def main():
                 "roofline": roofline,
                 "clocks": clocks,
                 "cpu_baseline": cpu}
+        if args.detail:
+            line["gemm_by_shape"] = gemm_stats.get("by_shape")
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -38,15 +38,29 @@ class GemmTimer:
     def __init__(self):
         self.records = []
 
-    def add(self, flops, e0, e1):
-        self.records.append((flops, e0, e1))
+    def add(self, flops, e0, e1, key=None):
+        self.records.append((flops, e0, e1, key))
 
-    def summary(self):
+    def summary(self, detail=False):
         torch.cuda.synchronize()
-        ms = sum(e0.elapsed_time(e1) for _, e0, e1 in self.records)
-        fl = sum(f for f, _, _ in self.records)
-        return {"launches": len(self.records), "ms": ms, "flops": fl,
-                "tflops": (fl / (ms * 1e-3) / 1e12) if ms > 0 else 0.0}
+        ms = 0.0
+        fl = 0.0
+        per = {}
+        for f, e0, e1, key in self.records:
+            t = e0.elapsed_time(e1)
+            ms += t
+            fl += f
+            d = per.setdefault(key, [0, 0.0, 0.0])
+            d[0] += 1
+            d[1] += t
+            d[2] += f
+        out = {"launches": len(self.records), "ms": ms, "flops": fl,
+               "tflops": (fl / (ms * 1e-3) / 1e12) if ms > 0 else 0.0}
+        if detail:
+            out["by_shape"] = sorted(
+                [{"shape": k, "n": v[0], "ms": v[1], "tflops": v[2] / (v[1] * 1e-3) / 1e12 if v[1] else 0.0}
+                 for k, v in per.items()], key=lambda r: -r["ms"])
+        return out
 
 
 GEMM_TIMER = None
@@ -138,7 +152,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
     _count()
     if timer is not None:
         e1.record()
-        timer.add(2.0 * M * N * K * (2 if kind == EPI_SWIGLU else 1), e0, e1)
+        timer.add(2.0 * M * N * K * (2 if kind == EPI_SWIGLU else 1), e0, e1,
+                  f"M{M} N{N} K{K} kind{kind} mn{int(a_mn)}{int(b_mn)}")
     return out
 
 

@@ -90,8 +90,8 @@ def step_losses(model, batch, weights=(5.0, 1.0, 1.0, 1.0)):
     total = move_w * move_loss + board_w * board_loss + wl_w * wl_loss + d_w * d_loss
     return {
         "total": total, "move": move_loss, "board": board_loss, "wl": wl_loss, "d": d_loss,
-        "board_argmax": board_logits.argmax(-1), "board_mask": board_mask,
-        "move_argmax": move_logits.argmax(-1), "move_mask": move_mask,
+        "board_argmax": board_logits.argmax(-1), "board_mask": board_mask, "board_logits": board_logits,
+        "move_argmax": move_logits.argmax(-1), "move_mask": move_mask, "move_logits": move_logits,
         "wl_argmax": None if wl_logits is None else wl_logits.argmax(-1),
         "d_argmax": None if d_logits is None else d_logits.argmax(-1),
     }
