@@ -237,6 +237,8 @@ def main():
     sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
                            else local_rank)
     K.LAUNCHES[0] = 0
+    if args.detail:
+        K.OP_TIMER = {}
     gemm_timer = K.GemmTimer()
     K.GEMM_TIMER = gemm_timer
     sync_all()
@@ -244,13 +246,17 @@ def main():
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record()
+    host_t0 = time.perf_counter()
     for i in range(args.steps):
         dp.forward_backward(dbs[i % len(dbs)])
         dp.optimizer_step()
+    host_enqueue_ms = (time.perf_counter() - host_t0) * 1000 / args.steps
     ev1.record()
     sync_all()
     clocks = sampler.stop()
     K.GEMM_TIMER = None
+    op_stats = K.op_timer_summary(K.OP_TIMER) if K.OP_TIMER is not None else None
+    K.OP_TIMER = None
     launches = K.LAUNCHES[0] // args.steps
     dev_ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
     tokens_step = args.batch * args.seq * world
@@ -320,6 +326,8 @@ def main():
                 "cpu_baseline": cpu}
         if args.detail:
             line["gemm_by_shape"] = gemm_stats.get("by_shape")
+            line["host_enqueue_ms_per_step"] = host_enqueue_ms
+            line["ops_ms_per_step"] = {k: [n // args.steps, ms / args.steps] for k, (n, ms) in op_stats.items()}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

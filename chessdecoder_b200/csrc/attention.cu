@@ -16,6 +16,8 @@
 #include "../../include/cdk.h"
 #include "cdk_common.cuh"
 
+#include <cstdlib>
+
 namespace cdk {
 
 constexpr int kHd = 64;
@@ -159,18 +161,24 @@ struct AttnArgs {
   const int32_t* bid;   // [nseq - n_causal, S]
   const int32_t* meta;  // per prefix sequence: kv_hi[nt], q_lo[nt]
   const float* rope;
-  int S, H, n_causal, nt;
+  int S, H, n_causal, nt, nseq;
 };
 
-// Per-sequence prefix-mask metadata: for query tile qt the exclusive upper key
-// bound kv_hi, and for key tile kt the lowest query row q_lo that may see it.
-__global__ void attn_meta_kernel(const int32_t* __restrict__ bid, int S, int nt, int32_t* __restrict__ meta) {
+// Per-sequence prefix-mask metadata, laid out as
+//   [nseq][2*nt]  per tile: kv_hi[qt] (exclusive key bound of query tile qt),
+//                           q_lo[kt] (lowest query row that may see key tile kt)
+//   [nseq][S]     first[i] = lowest  j with bid[j] == bid[i]
+//   [nseq][S]     last[i]  = highest j with bid[j] == bid[i]
+__global__ void attn_meta_kernel(const int32_t* __restrict__ bid, int S, int nt, int nseq,
+                                 int32_t* __restrict__ meta) {
   extern __shared__ int32_t sm_meta[];
   int32_t* sb = sm_meta;           // S block ids
   int32_t* skv = sm_meta + S;      // nt
   int32_t* sql = skv + nt;         // nt
   const int seq = blockIdx.x;
   const int32_t* b = bid + (long long)seq * S;
+  int32_t* first_out = meta + (long long)nseq * 2 * nt + (long long)seq * S;
+  int32_t* last_out = meta + (long long)nseq * 2 * nt + (long long)nseq * S + (long long)seq * S;
   for (int i = threadIdx.x; i < S; i += blockDim.x) sb[i] = b[i];
   for (int i = threadIdx.x; i < nt; i += blockDim.x) {
     skv[i] = 0;
@@ -186,6 +194,8 @@ __global__ void attn_meta_kernel(const int32_t* __restrict__ bid, int S, int nt,
         last = max(last, j);
       }
     }
+    first_out[i] = first;
+    last_out[i] = last;
     atomicMax(&skv[i / kTile], last + 1);
     atomicMin(&sql[i / kTile], first);
   }
@@ -620,13 +630,467 @@ __global__ void __launch_bounds__(128) attn_bwd_dkv_kernel(const AttnArgs a) {
   store_tile(sV, dbase, ld, k0, S, 2 * E + h * kHd);
 }
 
+// ===========================================================================
+// Sequence-resident kernels for S <= 256 (the pretraining length): one CTA per
+// (head, sequence) holds the whole sequence's Q/K/V (and dO) tiles in shared
+// memory, fetched by TMA with one mbarrier per 64-row tile, so each tile is read
+// from HBM once per head instead of once per query tile.  Eight warps own
+// 16-row slices, paired (w, 15 - w) so that every warp does the same amount of
+// causal work.
+// ===========================================================================
+constexpr int kSeqTiles = 4;
+constexpr int kSeqMax = kSeqTiles * kTile;
+
+// acc += A * T^T over output chunks [c0, c1) (16 columns each); T stored [n][k].
+__device__ __forceinline__ void mma_a_bt_r(float (&acc)[8][4], const uint32_t (&a)[4][4], uint32_t s_tile, int c0,
+                                           int c1) {
+  const int lane = threadIdx.x & 31;
+  const int m = lane >> 3;
+  #pragma unroll
+  for (int np = 0; np < 4; ++np) {
+    if (np < c0 || np >= c1) continue;
+    #pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const int n = np * 16 + (m >> 1) * 8 + (lane & 7);
+      const int k = kk * 16 + (m & 1) * 8;
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(s_tile + swz(n, k), b0, b1, b2, b3);
+      mma_bf16_16816(acc[2 * np], a[kk], b0, b1);
+      mma_bf16_16816(acc[2 * np + 1], a[kk], b2, b3);
+    }
+  }
+}
+
+// acc += A * T over reduction chunks [c0, c1) of A's columns; T stored [k][n].
+__device__ __forceinline__ void mma_a_b_r(float (&acc)[8][4], const uint32_t (&a)[4][4], uint32_t s_tile, int c0,
+                                          int c1) {
+  const int lane = threadIdx.x & 31;
+  const int m = lane >> 3;
+  #pragma unroll
+  for (int dp = 0; dp < 4; ++dp) {
+    #pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      if (kk < c0 || kk >= c1) continue;
+      const int k = kk * 16 + (m & 1) * 8 + (lane & 7);
+      const int n = dp * 16 + (m >> 1) * 8;
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(s_tile + swz(k, n), b0, b1, b2, b3);
+      mma_bf16_16816(acc[2 * dp], a[kk], b0, b1);
+      mma_bf16_16816(acc[2 * dp + 1], a[kk], b2, b3);
+    }
+  }
+}
+
+// Store a warp's 16 staged rows (swizzled, 128 B each) to global rows row0.. (rows < nrows).
+__device__ __forceinline__ void store_rows16(const uint8_t* stage, __nv_bfloat16* g, long long ld, int row0,
+                                             int nrows, int col0) {
+  const int lane = threadIdx.x & 31;
+  #pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int idx = lane + 32 * j;
+    const int r = idx >> 3, ch = idx & 7;
+    if (row0 + r < nrows)
+      *reinterpret_cast<uint4*>(g + (long long)(row0 + r) * ld + col0 + ch * 8) =
+          *reinterpret_cast<const uint4*>(stage + swz(r, ch * 8));
+  }
+}
+
+struct SeqFwdSmem {
+  uint8_t Q[kSeqTiles][kTile * 128];
+  uint8_t K[kSeqTiles][kTile * 128];
+  uint8_t V[kSeqTiles][kTile * 128];
+  uint64_t bar[kSeqTiles];
+  int32_t bid[kSeqMax];
+  int32_t last[kSeqMax];
+  int abort;
+};
+
+struct SeqBwdSmem {
+  uint8_t Q[kSeqTiles][kTile * 128];
+  uint8_t K[kSeqTiles][kTile * 128];
+  uint8_t V[kSeqTiles][kTile * 128];
+  uint8_t dO[kSeqTiles][kTile * 128];
+  uint8_t stage[8][16 * 128];
+  uint64_t bar[kSeqTiles];
+  float D[kSeqMax];
+  float L[kSeqMax];
+  int32_t bid[kSeqMax];
+  int32_t first[kSeqMax];
+  int32_t last[kSeqMax];
+  int abort;
+};
+
+template <class T>
+__device__ __forceinline__ T& align_smem(uint8_t* raw) {
+  return *reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+}
+
+// Per-row block bounds of prefix sequence `pseq` inside the metadata buffer.
+__device__ __forceinline__ const int32_t* meta_first(const AttnArgs& a, int pseq) {
+  const long long np = a.nseq - a.n_causal;
+  return a.meta + np * 2 * a.nt + (long long)pseq * a.S;
+}
+__device__ __forceinline__ const int32_t* meta_last(const AttnArgs& a, int pseq) {
+  const long long np = a.nseq - a.n_causal;
+  return a.meta + np * 2 * a.nt + np * a.S + (long long)pseq * a.S;
+}
+
+__global__ void __launch_bounds__(256, 1)
+    attn_fwd_seq_kernel(const __grid_constant__ CUtensorMap tqkv, const AttnArgs a) {
+  extern __shared__ uint8_t dsm_raw[];
+  SeqFwdSmem& sm = align_smem<SeqFwdSmem>(dsm_raw);
+  const int h = blockIdx.x, seq = blockIdx.y;
+  const int S = a.S, E = a.H * kHd;
+  const int nt = (S + kTile - 1) / kTile;
+  const bool prefix = seq >= a.n_causal;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int row_base = seq * S;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < nt; ++i) mbar_init(&sm.bar[i], 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tqkv);
+    for (int i = 0; i < nt; ++i) {
+      mbar_arrive_expect_tx(&sm.bar[i], 3 * kTile * 128);
+      tma_load_2d(sm.Q[i], &tqkv, &sm.bar[i], h * kHd, row_base + i * kTile);
+      tma_load_2d(sm.K[i], &tqkv, &sm.bar[i], E + h * kHd, row_base + i * kTile);
+      tma_load_2d(sm.V[i], &tqkv, &sm.bar[i], 2 * E + h * kHd, row_base + i * kTile);
+    }
+  }
+  const int pseq = seq - a.n_causal;
+  const int32_t* bidg = prefix ? a.bid + (long long)pseq * S : nullptr;
+  const int32_t* lastg = prefix ? meta_last(a, pseq) : nullptr;
+  for (int i = threadIdx.x; i < kSeqMax; i += blockDim.x) {
+    sm.bid[i] = i < S ? (prefix ? bidg[i] : i) : -1;
+    sm.last[i] = i < S ? (prefix ? lastg[i] : i) : i;
+  }
+  __syncthreads();
+
+  const float sl2 = 0.125f * kLog2e;
+  const int nslices = (S + 15) / 16;
+  volatile int* abort_flag = &sm.abort;
+  for (int which = 0; which < 2; ++which) {
+    const int slice = which == 0 ? warp : 15 - warp;
+    if (slice >= nslices) continue;
+    const int r0 = slice * 16;
+    int kv_end = 0;
+    {
+      int v = 0;
+      if (lane < 16 && r0 + lane < S) v = max(r0 + lane + 1, sm.last[r0 + lane] + 1);
+      #pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+      kv_end = min(v, S);
+    }
+    const int qt = r0 / kTile, rl = r0 % kTile;
+    mbar_wait(&sm.bar[qt], 0, abort_flag);
+    uint32_t qa[4][4];
+    load_a_frags(smem_u32(sm.Q[qt]), rl, qa);
+    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+    float o[8][4];
+    zero_acc(o);
+    const int i_lo = r0 + g;
+    const int n_kv = (kv_end + kTile - 1) / kTile;
+    for (int kt = 0; kt < n_kv; ++kt) {
+      mbar_wait(&sm.bar[kt], 0, abort_flag);
+      const int k0 = kt * kTile;
+      const int nk = min(4, (kv_end - k0 + 15) / 16);
+      float s[8][4];
+      zero_acc(s);
+      mma_a_bt_r(s, qa, smem_u32(sm.K[kt]), 0, nk);
+      const bool full = k0 + kTile <= r0;
+      #pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float v = s[n][e] * sl2;
+          if (!full) {
+            const int i = i_lo + (e >> 1) * 8;
+            const int j = k0 + n * 8 + 2 * t + (e & 1);
+            const bool ok = (n >> 1) < nk && j < S && i < S && (j <= i || sm.bid[i] == sm.bid[j]);
+            if (!ok) v = -INFINITY;
+          }
+          s[n][e] = v;
+        }
+      }
+      #pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        float mx = -INFINITY;
+        #pragma unroll
+        for (int n = 0; n < 8; ++n) mx = fmaxf(mx, fmaxf(s[n][2 * hr], s[n][2 * hr + 1]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_r[hr], mx);
+        const float corr = m_new == -INFINITY ? 1.f : exp2f(m_r[hr] - m_new);
+        float sum = 0.f;
+        #pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          const float p0 = m_new == -INFINITY ? 0.f : exp2f(s[n][2 * hr] - m_new);
+          const float p1 = m_new == -INFINITY ? 0.f : exp2f(s[n][2 * hr + 1] - m_new);
+          s[n][2 * hr] = p0;
+          s[n][2 * hr + 1] = p1;
+          sum += p0 + p1;
+        }
+        l_r[hr] = l_r[hr] * corr + sum;
+        m_r[hr] = m_new;
+        #pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          o[n][2 * hr] *= corr;
+          o[n][2 * hr + 1] *= corr;
+        }
+      }
+      uint32_t pa[4][4];
+      c_to_a(s, pa);
+      mma_a_b_r(o, pa, smem_u32(sm.V[kt]), 0, nk);
+    }
+    #pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      float l = l_r[hr];
+      l += __shfl_xor_sync(0xffffffffu, l, 1);
+      l += __shfl_xor_sync(0xffffffffu, l, 2);
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      #pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        o[n][2 * hr] *= inv;
+        o[n][2 * hr + 1] *= inv;
+      }
+      const int i = i_lo + hr * 8;
+      if (t == 0 && i < S) a.lse[((long long)seq * a.H + h) * S + i] = m_r[hr] + log2f(l);
+    }
+    // the slice's Q rows belong to this warp alone: reuse them as output staging
+    __syncwarp();
+    c_to_smem(o, sm.Q[qt], rl);
+    __syncwarp();
+    {
+      #pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int idx = lane + 32 * j;
+        const int r = idx >> 3, ch = idx & 7;
+        if (r0 + r < S)
+          *reinterpret_cast<uint4*>(a.out + (long long)(row_base + r0 + r) * E + h * kHd + ch * 8) =
+              *reinterpret_cast<const uint4*>(sm.Q[qt] + swz(rl + r, ch * 8));
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256, 1)
+    attn_bwd_seq_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo,
+                        const AttnArgs a) {
+  extern __shared__ uint8_t dsm_raw[];
+  SeqBwdSmem& sm = align_smem<SeqBwdSmem>(dsm_raw);
+  const int h = blockIdx.x, seq = blockIdx.y;
+  const int S = a.S, E = a.H * kHd;
+  const long long ld = 3ll * E;
+  const int nt = (S + kTile - 1) / kTile;
+  const bool prefix = seq >= a.n_causal;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int row_base = seq * S;
+  const long long lrow = ((long long)seq * a.H + h) * S;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < nt; ++i) mbar_init(&sm.bar[i], 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tqkv);
+    prefetch_tmap(&tdo);
+    for (int i = 0; i < nt; ++i) {
+      mbar_arrive_expect_tx(&sm.bar[i], 4 * kTile * 128);
+      tma_load_2d(sm.Q[i], &tqkv, &sm.bar[i], h * kHd, row_base + i * kTile);
+      tma_load_2d(sm.K[i], &tqkv, &sm.bar[i], E + h * kHd, row_base + i * kTile);
+      tma_load_2d(sm.V[i], &tqkv, &sm.bar[i], 2 * E + h * kHd, row_base + i * kTile);
+      tma_load_2d(sm.dO[i], &tdo, &sm.bar[i], h * kHd, row_base + i * kTile);
+    }
+  }
+  const int pseq = seq - a.n_causal;
+  const int32_t* bidg = prefix ? a.bid + (long long)pseq * S : nullptr;
+  const int32_t* firstg = prefix ? meta_first(a, pseq) : nullptr;
+  const int32_t* lastg = prefix ? meta_last(a, pseq) : nullptr;
+  for (int i = threadIdx.x; i < kSeqMax; i += blockDim.x) {
+    sm.bid[i] = i < S ? (prefix ? bidg[i] : i) : -1;
+    sm.first[i] = i < S ? (prefix ? firstg[i] : i) : i;
+    sm.last[i] = i < S ? (prefix ? lastg[i] : i) : i;
+    float d = 0.f, l = 0.f;
+    if (i < S) {
+      // D_i = sum_d dO[i,d] * O[i,d]
+      const uint4* po = reinterpret_cast<const uint4*>(a.out + (long long)(row_base + i) * E + h * kHd);
+      const uint4* pd = reinterpret_cast<const uint4*>(a.dout + (long long)(row_base + i) * E + h * kHd);
+      #pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint4 wo = po[q], wd = pd[q];
+        const __nv_bfloat162* ho = reinterpret_cast<const __nv_bfloat162*>(&wo);
+        const __nv_bfloat162* hd = reinterpret_cast<const __nv_bfloat162*>(&wd);
+        #pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 fo = __bfloat1622float2(ho[j]), fd = __bfloat1622float2(hd[j]);
+          d += fo.x * fd.x + fo.y * fd.y;
+        }
+      }
+      l = a.lse[lrow + i];
+    }
+    sm.D[i] = d;
+    sm.L[i] = l;
+  }
+  __syncthreads();
+
+  const float sl2 = 0.125f * kLog2e;
+  const int nslices = (S + 15) / 16;
+  volatile int* abort_flag = &sm.abort;
+  uint8_t* stage = sm.stage[warp];
+
+  // ---- dQ for this warp's query slices ---------------------------------------
+  for (int which = 0; which < 2; ++which) {
+    const int slice = which == 0 ? warp : 15 - warp;
+    if (slice >= nslices) continue;
+    const int r0 = slice * 16;
+    int kv_end;
+    {
+      int v = 0;
+      if (lane < 16 && r0 + lane < S) v = max(r0 + lane + 1, sm.last[r0 + lane] + 1);
+      #pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+      kv_end = min(v, S);
+    }
+    const int qt = r0 / kTile, rl = r0 % kTile;
+    mbar_wait(&sm.bar[qt], 0, abort_flag);
+    uint32_t qa[4][4], doa[4][4];
+    load_a_frags(smem_u32(sm.Q[qt]), rl, qa);
+    load_a_frags(smem_u32(sm.dO[qt]), rl, doa);
+    float dq[8][4];
+    zero_acc(dq);
+    const int i_lo = r0 + g;
+    const int n_kv = (kv_end + kTile - 1) / kTile;
+    for (int kt = 0; kt < n_kv; ++kt) {
+      mbar_wait(&sm.bar[kt], 0, abort_flag);
+      const int k0 = kt * kTile;
+      const int nk = min(4, (kv_end - k0 + 15) / 16);
+      float s[8][4], dp[8][4];
+      zero_acc(s);
+      zero_acc(dp);
+      mma_a_bt_r(s, qa, smem_u32(sm.K[kt]), 0, nk);
+      mma_a_bt_r(dp, doa, smem_u32(sm.V[kt]), 0, nk);
+      const bool full = k0 + kTile <= r0;
+      #pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = i_lo + (e >> 1) * 8;
+          bool ok = true;
+          if (!full) {
+            const int j = k0 + n * 8 + 2 * t + (e & 1);
+            ok = (n >> 1) < nk && j < S && i < S && (j <= i || sm.bid[i] == sm.bid[j]);
+          }
+          const float p = ok ? exp2f(s[n][e] * sl2 - sm.L[i]) : 0.f;
+          s[n][e] = p * (dp[n][e] - sm.D[i]);
+        }
+      }
+      uint32_t dsa[4][4];
+      c_to_a(s, dsa);
+      mma_a_b_r(dq, dsa, smem_u32(sm.K[kt]), 0, nk);
+    }
+    #pragma unroll
+    for (int n = 0; n < 8; ++n)
+      #pragma unroll
+      for (int e = 0; e < 4; ++e) dq[n][e] *= 0.125f;
+    unrope_c(dq, a.rope, min(i_lo, S - 1), min(i_lo + 8, S - 1));
+    __syncwarp();
+    c_to_smem(dq, stage, 0);
+    __syncwarp();
+    store_rows16(stage, a.dqkv + (long long)row_base * ld, ld, r0, S, h * kHd);
+    __syncwarp();
+  }
+
+  // ---- dK, dV for this warp's key slices -------------------------------------
+  for (int which = 0; which < 2; ++which) {
+    const int slice = which == 0 ? warp : 15 - warp;
+    if (slice >= nslices) continue;
+    const int k0 = slice * 16;
+    int q_lo;
+    {
+      int v = 1 << 30;
+      if (lane < 16 && k0 + lane < S) v = min(k0 + lane, sm.first[k0 + lane]);
+      #pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+      q_lo = v;
+    }
+    const int kt = k0 / kTile, kl = k0 % kTile;
+    mbar_wait(&sm.bar[kt], 0, abort_flag);
+    uint32_t ka[4][4], va[4][4];
+    load_a_frags(smem_u32(sm.K[kt]), kl, ka);
+    load_a_frags(smem_u32(sm.V[kt]), kl, va);
+    float dk[8][4], dv[8][4];
+    zero_acc(dk);
+    zero_acc(dv);
+    const int j_lo = k0 + g;
+    const int qt0 = q_lo / kTile;
+    for (int qt = qt0; qt < nt; ++qt) {
+      mbar_wait(&sm.bar[qt], 0, abort_flag);
+      const int qb = qt * kTile;
+      const int c0 = qt == qt0 ? (q_lo - qb) / 16 : 0;
+      const int c1 = min(4, (S - qb + 15) / 16);
+      float st[8][4], dpt[8][4];
+      zero_acc(st);
+      zero_acc(dpt);
+      mma_a_bt_r(st, ka, smem_u32(sm.Q[qt]), c0, c1);
+      mma_a_bt_r(dpt, va, smem_u32(sm.dO[qt]), c0, c1);
+      const bool full = (qb >= k0 + 16) && (qb + kTile <= S);
+      float pt[8][4];
+      #pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int il = n * 8 + 2 * t + (e & 1);
+          const int i = qb + il;
+          bool ok = true;
+          if (!full) {
+            const int j = j_lo + (e >> 1) * 8;
+            const int chunk = n >> 1;
+            ok = chunk >= c0 && chunk < c1 && i < S && j < S && (j <= i || sm.bid[i] == sm.bid[j]);
+          }
+          const float p = ok ? exp2f(st[n][e] * sl2 - sm.L[i]) : 0.f;
+          pt[n][e] = p;
+          st[n][e] = p * (dpt[n][e] - sm.D[i]);
+        }
+      }
+      uint32_t pa[4][4], dsa[4][4];
+      c_to_a(pt, pa);
+      c_to_a(st, dsa);
+      mma_a_b_r(dv, pa, smem_u32(sm.dO[qt]), c0, c1);
+      mma_a_b_r(dk, dsa, smem_u32(sm.Q[qt]), c0, c1);
+    }
+    #pragma unroll
+    for (int n = 0; n < 8; ++n)
+      #pragma unroll
+      for (int e = 0; e < 4; ++e) dk[n][e] *= 0.125f;
+    unrope_c(dk, a.rope, min(j_lo, S - 1), min(j_lo + 8, S - 1));
+    __nv_bfloat16* dbase = a.dqkv + (long long)row_base * ld;
+    __syncwarp();
+    c_to_smem(dk, stage, 0);
+    __syncwarp();
+    store_rows16(stage, dbase, ld, k0, S, E + h * kHd);
+    __syncwarp();
+    c_to_smem(dv, stage, 0);
+    __syncwarp();
+    store_rows16(stage, dbase, ld, k0, S, 2 * E + h * kHd);
+    __syncwarp();
+  }
+}
+
 }  // namespace cdk
 
 using namespace cdk;
 
 extern "C" int64_t cdk_attn_meta_elems(int64_t nseq_prefix, int64_t S) {
   const int64_t nt = (S + kTile - 1) / kTile;
-  return nseq_prefix * 2 * nt;
+  return nseq_prefix * (2 * nt + 2 * S);
 }
 
 extern "C" int cdk_attn_prefix_meta(const int32_t* bid, int64_t nseq_prefix, int64_t S, int32_t* meta,
@@ -635,11 +1099,28 @@ extern "C" int cdk_attn_prefix_meta(const int32_t* bid, int64_t nseq_prefix, int
   if (!bid || !meta || S <= 0 || S > 8192 || nseq_prefix < 0) return -1;
   const int nt = (int)((S + kTile - 1) / kTile);
   const size_t smem = (size_t)(S + 2 * nt) * sizeof(int32_t);
-  attn_meta_kernel<<<(unsigned)nseq_prefix, 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(bid, (int)S, nt,
-                                                                                                  meta);
+  attn_meta_kernel<<<(unsigned)nseq_prefix, 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      bid, (int)S, nt, (int)nseq_prefix, meta);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
 }
+
+// Path selection for S <= 256: the tcgen05 kernels (attention_tc.cu) by
+// default; CDK_ATTN_PATH=seq selects the mma.sync sequence-resident kernels and
+// CDK_ATTN_PATH=tiled the tiled kernels (the tests cover all three).  S > 256
+// always takes the tiled kernels.
+static int attn_path() {
+  const char* v = getenv("CDK_ATTN_PATH");
+  if (v && v[0] == 't' && v[1] == 'i') return 2;  // tiled
+  if (v && v[0] == 's') return 1;                  // seq (mma.sync)
+  return 0;                                        // tcgen05
+}
+static bool seq_path_enabled() { return attn_path() != 2; }
+
+namespace cdk {
+int launch_attn_fwd_tc(const void* qkv, void* out, float* lse, int64_t nseq, int64_t n_causal, int64_t S, int64_t H,
+                       const int32_t* bid, const int32_t* meta, cudaStream_t stream);
+}  // namespace cdk
 
 static int attn_check(const void* qkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* meta) {
   if (!qkv || nseq <= 0 || S <= 0 || H <= 0 || H > 64) return -1;
@@ -666,8 +1147,27 @@ extern "C" int cdk_attn_fwd(const void* qkv, void* out, float* lse, int64_t nseq
   a.H = (int)H;
   a.n_causal = (int)n_causal;
   a.nt = (int)((S + kTile - 1) / kTile);
-  dim3 grid((unsigned)a.nt, (unsigned)H, (unsigned)nseq);
-  attn_fwd_kernel<<<grid, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  a.nseq = (int)nseq;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (S <= kSeqMax && attn_path() == 0) {
+    return launch_attn_fwd_tc(qkv, out, lse, nseq, n_causal, S, H, bid, meta, s);
+  }
+  if (S <= kSeqMax && seq_path_enabled()) {
+    CUtensorMap tq;
+    if (!make_tmap(&tq, qkv, 3 * H * kHd, nseq * S, 3 * H * kHd, 64, 64)) return -10;
+    const size_t smem = sizeof(SeqFwdSmem) + 1024;
+    static bool attr_done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+      cudaFuncSetAttribute(attn_fwd_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr_done[dev] = true;
+    }
+    attn_fwd_seq_kernel<<<dim3((unsigned)H, (unsigned)nseq), 256, smem, s>>>(tq, a);
+  } else {
+    dim3 grid((unsigned)a.nt, (unsigned)H, (unsigned)nseq);
+    attn_fwd_kernel<<<grid, 128, 0, s>>>(a);
+  }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
 }
@@ -696,8 +1196,25 @@ extern "C" int cdk_attn_bwd(const void* qkv, const void* out, const void* dout, 
   a.H = (int)H;
   a.n_causal = (int)n_causal;
   a.nt = (int)((S + kTile - 1) / kTile);
+  a.nseq = (int)nseq;
   dim3 grid((unsigned)a.nt, (unsigned)H, (unsigned)nseq);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (S <= kSeqMax && seq_path_enabled()) {
+    CUtensorMap tq, tdo;
+    if (!make_tmap(&tq, qkv, 3 * H * kHd, nseq * S, 3 * H * kHd, 64, 64)) return -10;
+    if (!make_tmap(&tdo, dout, H * kHd, nseq * S, H * kHd, 64, 64)) return -11;
+    const size_t smem = sizeof(SeqBwdSmem) + 1024;
+    static bool seq_attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !seq_attr[dev]) {
+      cudaFuncSetAttribute(attn_bwd_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      seq_attr[dev] = true;
+    }
+    attn_bwd_seq_kernel<<<dim3((unsigned)H, (unsigned)nseq), 256, smem, s>>>(tq, tdo, a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : (int)e;
+  }
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);

@@ -131,6 +131,111 @@ __device__ __forceinline__ void atomic_row_f32(float* dst, const float (&v)[32],
   }
 }
 
+// ---- epilogue tile routines (one thread = one accumulator row) --------------
+// Global operands of a chunk (residual, gate/up, RoPE table) are requested
+// before the chunk's TMEM load so that their latency overlaps it.
+template <int BN>
+__device__ __forceinline__ void epi_swiglu(const EpiDev& e, const GemmParams& p, uint32_t tbase, int row,
+                                           bool row_ok, int n0) {
+  // TMEM columns [0, BN/2) = gate, [BN/2, BN) = up, for output columns n0 ...
+  __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(e.out2) + (long long)row * e.ldo2;
+  __nv_bfloat16* uo = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo;
+  #pragma unroll 1
+  for (int c = 0; c < BN / 64; ++c) {
+    const int col = n0 + c * 32;
+    if (col >= p.N) break;
+    float g[32], up[32];
+    tmem_ld_32x32b_x32(tbase + c * 32, g);
+    tmem_ld_32x32b_x32(tbase + BN / 2 + c * 32, up);
+    if (row_ok) {
+      const int nc = min(32, p.N - col);
+      store_row_bf16(gu + col, g, nc);
+      store_row_bf16(gu + e.half_n + col, up, nc);
+      float h[32];
+      #pragma unroll
+      for (int i = 0; i < 32; ++i) h[i] = silu_f(g[i]) * up[i];
+      store_row_bf16(uo + col, h, nc);
+    }
+  }
+}
+
+template <int BN, int KIND>
+__device__ __forceinline__ void epi_tile(const EpiDev& e, const GemmParams& p, uint32_t tbase, int row, bool row_ok,
+                                         int n0) {
+  const long long orow = (long long)row * e.ldo;
+  const int pos = KIND == CDK_EPI_ROPE_BF16 ? row % e.seq_len : 0;
+  #pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    const int col = n0 + c * 32;
+    if (col >= p.N) break;
+    const int nc = min(32, p.N - col);
+    // prefetch this chunk's global operand
+    float r[32];
+    float a2[32];
+    if (row_ok) {
+      if constexpr (KIND == CDK_EPI_RESID_F32) load_row_f32(e.resid + (long long)row * e.ldr + col, r, nc);
+      if constexpr (KIND == CDK_EPI_ACCUM_F32) load_row_f32(reinterpret_cast<float*>(e.out) + orow + col, r, nc);
+      if constexpr (KIND == CDK_EPI_DSWIGLU) {
+        const __nv_bfloat16* gsrc = e.aux + (long long)row * e.ldaux;
+        load_row_bf16(gsrc + col, r);
+        load_row_bf16(gsrc + e.half_n + col, a2);
+      }
+      if constexpr (KIND == CDK_EPI_ROPE_BF16) {
+        if (col < e.rope_cols) {
+          const float4* cs = reinterpret_cast<const float4*>(e.rope + ((long long)pos * 32 + ((col & 63) >> 1)) * 2);
+          #pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 t = __ldg(cs + q);
+            r[4 * q] = t.x; r[4 * q + 1] = t.y; r[4 * q + 2] = t.z; r[4 * q + 3] = t.w;
+          }
+        }
+      }
+    }
+    float v[32];
+    tmem_ld_32x32b_x32(tbase + c * 32, v);
+    if (!row_ok) continue;
+    if (e.bias != nullptr) {
+      #pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < nc) v[i] += __ldg(e.bias + col + i);
+    }
+    if constexpr (KIND == CDK_EPI_STORE_BF16) {
+      store_row_bf16(reinterpret_cast<__nv_bfloat16*>(e.out) + orow + col, v, nc);
+    } else if constexpr (KIND == CDK_EPI_STORE_F32) {
+      store_row_f32(reinterpret_cast<float*>(e.out) + orow + col, v, nc);
+    } else if constexpr (KIND == CDK_EPI_RESID_F32 || KIND == CDK_EPI_ACCUM_F32) {
+      #pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += r[i];
+      store_row_f32(reinterpret_cast<float*>(e.out) + orow + col, v, nc);
+    } else if constexpr (KIND == CDK_EPI_ATOMIC_F32) {
+      atomic_row_f32(reinterpret_cast<float*>(e.out) + orow + col, v, nc);
+    } else if constexpr (KIND == CDK_EPI_ROPE_BF16) {
+      if (col < e.rope_cols) {
+        #pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float c0 = r[2 * i], s0 = r[2 * i + 1];
+          const float x0 = v[2 * i], x1 = v[2 * i + 1];
+          v[2 * i] = x0 * c0 - x1 * s0;
+          v[2 * i + 1] = x1 * c0 + x0 * s0;
+        }
+      }
+      store_row_bf16(reinterpret_cast<__nv_bfloat16*>(e.out) + orow + col, v, nc);
+    } else if constexpr (KIND == CDK_EPI_DSWIGLU) {
+      float dg[32], du[32];
+      #pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float g = r[i], up = a2[i];
+        const float sg = 1.f / (1.f + __expf(-g));
+        du[i] = v[i] * g * sg;
+        dg[i] = v[i] * up * (sg * (1.f + g * (1.f - sg)));
+      }
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(e.out) + orow;
+      store_row_bf16(o + col, dg, nc);
+      store_row_bf16(o + e.half_n + col, du, nc);
+    }
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
@@ -276,106 +381,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < p.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
 
-      if (e.kind == CDK_EPI_SWIGLU) {
-        // TMEM columns [0, BN/2) = gate, [BN/2, BN) = up, for u-columns n0 ...
-        const int n0 = nt * (BN / 2);
-        #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
-          const int col = n0 + c * 32;
-          if (col >= p.N) break;
-          float g[32], up[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, g);
-          tmem_ld_32x32b_x32(tbase + BN / 2 + c * 32, up);
-          if (row_ok) {
-            const int nc = min(32, p.N - col);
-            __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(e.out2) + (long long)row * e.ldo2;
-            store_row_bf16(gu + col, g, nc);
-            store_row_bf16(gu + e.half_n + col, up, nc);
-            float h[32];
-            #pragma unroll
-            for (int i = 0; i < 32; ++i) h[i] = silu_f(g[i]) * up[i];
-            store_row_bf16(reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo + col, h, nc);
-          }
-        }
-      } else {
-        const int n0 = nt * BN;
-        #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          const int col = n0 + c * 32;
-          if (col >= p.N) break;
-          float v[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, v);
-          if (!row_ok) continue;
-          const int nc = min(32, p.N - col);
-          if (e.bias != nullptr) {
-            #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i < nc) v[i] += e.bias[col + i];
-          }
-          switch (e.kind) {
-            case CDK_EPI_STORE_BF16:
-              store_row_bf16(reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo + col, v, nc);
-              break;
-            case CDK_EPI_STORE_F32:
-              store_row_f32(reinterpret_cast<float*>(e.out) + (long long)row * e.ldo + col, v, nc);
-              break;
-            case CDK_EPI_RESID_F32: {
-              float r[32];
-              load_row_f32(e.resid + (long long)row * e.ldr + col, r, nc);
-              #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] += r[i];
-              store_row_f32(reinterpret_cast<float*>(e.out) + (long long)row * e.ldo + col, v, nc);
-              break;
-            }
-            case CDK_EPI_ACCUM_F32: {
-              float* dst = reinterpret_cast<float*>(e.out) + (long long)row * e.ldo + col;
-              float r[32];
-              load_row_f32(dst, r, nc);
-              #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] += r[i];
-              store_row_f32(dst, v, nc);
-              break;
-            }
-            case CDK_EPI_ATOMIC_F32:
-              atomic_row_f32(reinterpret_cast<float*>(e.out) + (long long)row * e.ldo + col, v, nc);
-              break;
-            case CDK_EPI_ROPE_BF16: {
-              if (col < e.rope_cols) {
-                const int pos = row % e.seq_len;
-                const float* cs = e.rope + ((long long)pos * 32 + ((col & 63) >> 1)) * 2;
-                #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                  const float c0 = cs[2 * i], s0 = cs[2 * i + 1];
-                  const float x0 = v[2 * i], x1 = v[2 * i + 1];
-                  v[2 * i] = x0 * c0 - x1 * s0;
-                  v[2 * i + 1] = x1 * c0 + x0 * s0;
-                }
-              }
-              store_row_bf16(reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo + col, v, nc);
-              break;
-            }
-            case CDK_EPI_DSWIGLU: {
-              float g[32], up[32];
-              const __nv_bfloat16* gu = e.aux + (long long)row * e.ldaux;
-              load_row_bf16(gu + col, g);
-              load_row_bf16(gu + e.half_n + col, up);
-              float dg[32], du[32];
-              #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const float sg = 1.f / (1.f + __expf(-g[i]));
-                const float sl = g[i] * sg;
-                du[i] = v[i] * sl;
-                dg[i] = v[i] * up[i] * (sg * (1.f + g[i] * (1.f - sg)));
-              }
-              __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo;
-              store_row_bf16(o + col, dg, nc);
-              store_row_bf16(o + e.half_n + col, du, nc);
-              break;
-            }
-            default:
-              break;
-          }
-        }
+      switch (e.kind) {
+        case CDK_EPI_SWIGLU: epi_swiglu<BN>(e, p, tbase, row, row_ok, nt * (BN / 2)); break;
+        case CDK_EPI_STORE_BF16: epi_tile<BN, CDK_EPI_STORE_BF16>(e, p, tbase, row, row_ok, nt * BN); break;
+        case CDK_EPI_STORE_F32: epi_tile<BN, CDK_EPI_STORE_F32>(e, p, tbase, row, row_ok, nt * BN); break;
+        case CDK_EPI_RESID_F32: epi_tile<BN, CDK_EPI_RESID_F32>(e, p, tbase, row, row_ok, nt * BN); break;
+        case CDK_EPI_ACCUM_F32: epi_tile<BN, CDK_EPI_ACCUM_F32>(e, p, tbase, row, row_ok, nt * BN); break;
+        case CDK_EPI_ATOMIC_F32: epi_tile<BN, CDK_EPI_ATOMIC_F32>(e, p, tbase, row, row_ok, nt * BN); break;
+        case CDK_EPI_ROPE_BF16: epi_tile<BN, CDK_EPI_ROPE_BF16>(e, p, tbase, row, row_ok, nt * BN); break;
+        case CDK_EPI_DSWIGLU: epi_tile<BN, CDK_EPI_DSWIGLU>(e, p, tbase, row, row_ok, nt * BN); break;
+        default: break;
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -412,8 +427,8 @@ static EncodeTiledFn encode_fn() {
 }
 
 // 2-D bf16 tensor map, 128-byte swizzle: dims {inner, outer}, row pitch in elements.
-static bool make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
-                      uint32_t box_inner, uint32_t box_outer) {
+bool make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
+               uint32_t box_inner, uint32_t box_outer) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {inner, outer};
@@ -448,6 +463,11 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   if (dev < 64 && !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return (int)e;
+    // tcgen05.alloc blocks until columns are free: co-resident CTAs must fit in 512 columns
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kThreads, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return (int)e;
+    if (per_sm * Cfg::kTmemCols > 512) return -12;
     attr_set[dev] = true;
   }
   kfn<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);

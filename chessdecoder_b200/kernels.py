@@ -65,6 +65,34 @@ class GemmTimer:
 
 GEMM_TIMER = None
 
+# Optional per-op CUDA-event timer (bench.py --detail): op name -> [(e0, e1)].
+OP_TIMER = None
+
+
+def _timed(name):
+    def deco(fn):
+        def wrapper(*args, **kwargs):
+            t = OP_TIMER
+            if t is None:
+                return fn(*args, **kwargs)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            r = fn(*args, **kwargs)
+            e1.record()
+            t.setdefault(name, []).append((e0, e1))
+            return r
+        wrapper.__name__ = fn.__name__
+        wrapper.__doc__ = fn.__doc__
+        return wrapper
+    return deco
+
+
+def op_timer_summary(t):
+    torch.cuda.synchronize()
+    out = {k: (len(v), sum(a.elapsed_time(b) for a, b in v)) for k, v in t.items()}
+    return dict(sorted(out.items(), key=lambda kv: -kv[1][1]))
+
 
 def _p(t):
     return None if t is None else C.c_void_p(t.data_ptr())
@@ -157,6 +185,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
     return out
 
 
+@_timed("gemm_f32")
 def gemm_f32(a, b, c, *, a_t=False, b_t=False, bias=None, accumulate=False, M=None, N=None, K=None):
     """C (+)= op(A) op(B)^T + bias in fp32 (small contractions)."""
     _need_cuda(a, b, c)
@@ -176,6 +205,7 @@ def gemm_f32(a, b, c, *, a_t=False, b_t=False, bias=None, accumulate=False, M=No
 # ---------------------------------------------------------------------------
 # Attention
 # ---------------------------------------------------------------------------
+@_timed("attn_meta")
 def attn_meta(bid32: torch.Tensor, S: int) -> torch.Tensor:
     """Per-tile bounds for the prefix mask; bid32 int32 [nseq_prefix, S]."""
     nseq = bid32.shape[0]
@@ -186,6 +216,7 @@ def attn_meta(bid32: torch.Tensor, S: int) -> torch.Tensor:
     return meta
 
 
+@_timed("attn_fwd")
 def attn_fwd(qkv, out, lse, nseq, n_causal, S, H, bid32=None, meta=None):
     _need_cuda(qkv, out, lse)
     rc = lib().cdk_attn_fwd(_p(qkv), _p(out), _p(lse), nseq, n_causal, S, H, _p(bid32), _p(meta), _stream())
@@ -193,6 +224,7 @@ def attn_fwd(qkv, out, lse, nseq, n_causal, S, H, bid32=None, meta=None):
     _count(1)
 
 
+@_timed("attn_bwd")
 def attn_bwd(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid32=None, meta=None, rope=None):
     _need_cuda(qkv, out, dout, lse, dsum, dqkv)
     rc = lib().cdk_attn_bwd(_p(qkv), _p(out), _p(dout), _p(lse), _p(dsum), _p(dqkv), nseq, n_causal, S, H,
@@ -204,6 +236,7 @@ def attn_bwd(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid32=None, 
 # ---------------------------------------------------------------------------
 # RMSNorm
 # ---------------------------------------------------------------------------
+@_timed("rmsnorm_fwd")
 def rmsnorm_fwd(x, scale, y16=None, y32=None, rstd=None, eps=1e-6):
     _need_cuda(x, scale)
     rows, dim = x.shape
@@ -212,6 +245,7 @@ def rmsnorm_fwd(x, scale, y16=None, y32=None, rstd=None, eps=1e-6):
     _count(1)
 
 
+@_timed("rmsnorm_bwd")
 def rmsnorm_bwd(dy, x, scale, rstd, dx=None, dx16=None, dscale=None, dres=None):
     _need_cuda(dy, x, scale, rstd)
     rows, dim = x.shape
@@ -224,6 +258,7 @@ def rmsnorm_bwd(dy, x, scale, rstd, dx=None, dx16=None, dscale=None, dres=None):
 # ---------------------------------------------------------------------------
 # Embedding / Fourier
 # ---------------------------------------------------------------------------
+@_timed("fourier_features")
 def fourier_features(wl_t, d_t, wl_pos_u8, d_pos_u8, wl_c, d_c, freqs, rows32, values_out, feat_out):
     n = rows32.numel()
     rc = lib().cdk_fourier_features(_p(wl_t), _p(d_t), _p(wl_pos_u8), _p(d_pos_u8), _p(wl_c), _p(d_c), wl_c.numel(),
@@ -232,6 +267,7 @@ def fourier_features(wl_t, d_t, wl_pos_u8, d_pos_u8, wl_c, d_c, freqs, rows32, v
     _count(1)
 
 
+@_timed("embed_fwd")
 def embed_fwd(ids, emb, slot32, frows, out, n_copies=1):
     n_tok = ids.numel()
     rc = lib().cdk_embed_fwd(_p(ids), n_tok, emb.shape[0], _p(emb), emb.shape[1], _p(slot32), _p(frows), _p(out),
@@ -240,6 +276,7 @@ def embed_fwd(ids, emb, slot32, frows, out, n_copies=1):
     _count(1)
 
 
+@_timed("embed_bwd")
 def embed_bwd(ids, dh, slot32, demb, dfrows, n_copies=1):
     n_tok = ids.numel()
     rc = lib().cdk_embed_bwd(_p(ids), n_tok, demb.shape[0], _p(dh), demb.shape[1], n_copies, _p(slot32), _p(demb),
@@ -248,6 +285,7 @@ def embed_bwd(ids, dh, slot32, demb, dfrows, n_copies=1):
     _count(1)
 
 
+@_timed("fourier_bwd")
 def fourier_bwd(values, freqs, dfeat, dfreqs):
     rc = lib().cdk_fourier_bwd(_p(values), _p(freqs), freqs.numel(), _p(dfeat), values.numel(), _p(dfreqs),
                                _stream())
@@ -258,6 +296,7 @@ def fourier_bwd(values, freqs, dfeat, dfreqs):
 # ---------------------------------------------------------------------------
 # Heads
 # ---------------------------------------------------------------------------
+@_timed("softmax_ce")
 def softmax_ce(logits, target32, row_w, norm, loss_weight, dlogits=None, dbias=None, loss_out=None, argmax=None,
                ncls=None):
     rows = logits.shape[0]
@@ -269,6 +308,7 @@ def softmax_ce(logits, target32, row_w, norm, loss_weight, dlogits=None, dbias=N
     _count(1)
 
 
+@_timed("value_tail")
 def value_tail(z1, w2, b2, target, valid, centers, norm, loss_weight, act_out, dlogits_out, dz1, db1=None,
                loss_out=None, argmax=None):
     rows, hidden = z1.shape
@@ -279,6 +319,7 @@ def value_tail(z1, w2, b2, target, valid, centers, norm, loss_weight, act_out, d
     _count(1)
 
 
+@_timed("gather_rows_bf16")
 def gather_rows_bf16(src, rows32, dst):
     rc = lib().cdk_gather_rows_bf16(_p(src), src.stride(0), _p(rows32), rows32.numel(), src.shape[1], _p(dst),
                                     dst.stride(0), _stream())
@@ -286,6 +327,7 @@ def gather_rows_bf16(src, rows32, dst):
     _count(1)
 
 
+@_timed("scatter_add_rows")
 def scatter_add_rows(src, rows32, dst):
     rc = lib().cdk_scatter_add_rows_f32(_p(src), src.stride(0), _p(rows32), rows32.numel(), dst.shape[1], _p(dst),
                                         dst.stride(0), _stream())
@@ -293,16 +335,19 @@ def scatter_add_rows(src, rows32, dst):
     _count(1)
 
 
+@_timed("cast_bf16")
 def cast_bf16(src, dst):
     _check(lib().cdk_cast_f32_bf16(_p(src), _p(dst), src.numel(), _stream()), "cast_f32_bf16")
     _count(1)
 
 
+@_timed("add_f32")
 def add_f32(a, b, out):
     _check(lib().cdk_add_f32(_p(a), _p(b), _p(out), a.numel(), _stream()), "add_f32")
     _count(1)
 
 
+@_timed("scale_f32")
 def scale_f32(x, s):
     _check(lib().cdk_scale_f32(_p(x), x.numel(), float(s), _stream()), "scale_f32")
     _count(1)
@@ -311,11 +356,13 @@ def scale_f32(x, s):
 # ---------------------------------------------------------------------------
 # Optimizer
 # ---------------------------------------------------------------------------
+@_timed("sumsq")
 def sumsq(x, partial):
     _check(lib().cdk_sumsq(_p(x), x.numel(), _p(partial), partial.numel(), _stream()), "sumsq")
     _count(1)
 
 
+@_timed("adamw")
 def adamw(p, g, m, v, p_bf16, partial, *, max_norm, lr, beta1, beta2, eps, wd, step, grad_scale=1.0):
     rc = lib().cdk_adamw(_p(p), _p(g), _p(m), _p(v), _p(p_bf16), p.numel(), _p(partial),
                          partial.numel() if partial is not None else 0, float(max_norm), float(lr), float(beta1),

@@ -184,8 +184,17 @@ def ref_attention(qkv, nseq, n_causal, S, H, bid):
     return o.transpose(1, 2).reshape(nseq * S, H * 64)
 
 
-@pytest.mark.parametrize("S,nseq,n_causal", [(256, 4, 2), (100, 3, 1), (256, 2, 2), (320, 2, 0)])
-def test_attention_fwd_bwd(K, S, nseq, n_causal):
+@pytest.fixture(params=["tc", "seq", "tiled"])
+def attn_path(request, monkeypatch):
+    """Every attention implementation: tcgen05 (S <= 256), mma.sync
+    sequence-resident (S <= 256) and mma.sync tiled (any S)."""
+    monkeypatch.setenv("CDK_ATTN_PATH", request.param)
+    return request.param
+
+
+@pytest.mark.parametrize("S,nseq,n_causal", [(256, 4, 2), (100, 3, 1), (256, 2, 2), (320, 2, 0), (68, 3, 1),
+                                             (136, 2, 0)])
+def test_attention_fwd_bwd(K, attn_path, S, nseq, n_causal):
     H = 4
     E = H * 64
     gen = torch.Generator().manual_seed(S + nseq)
@@ -214,7 +223,7 @@ def test_attention_fwd_bwd(K, S, nseq, n_causal):
     assert K.get_error() == 0
 
 
-def test_attention_bwd_unrope(K):
+def test_attention_bwd_unrope(K, attn_path):
     S, nseq, H = 128, 2, 2
     E = H * 64
     gen = torch.Generator().manual_seed(5)
