@@ -1120,6 +1120,9 @@ static bool seq_path_enabled() { return attn_path() != 2; }
 namespace cdk {
 int launch_attn_fwd_tc(const void* qkv, void* out, float* lse, int64_t nseq, int64_t n_causal, int64_t S, int64_t H,
                        const int32_t* bid, const int32_t* meta, cudaStream_t stream);
+int launch_attn_bwd_tc(const void* qkv, const void* out, const void* dout, const float* lse, void* dqkv,
+                       int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,
+                       const int32_t* meta, const float* rope, cudaStream_t stream);
 }  // namespace cdk
 
 static int attn_check(const void* qkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* meta) {
@@ -1199,6 +1202,8 @@ extern "C" int cdk_attn_bwd(const void* qkv, const void* out, const void* dout, 
   a.nseq = (int)nseq;
   dim3 grid((unsigned)a.nt, (unsigned)H, (unsigned)nseq);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (S <= kSeqMax && attn_path() == 0)
+    return launch_attn_bwd_tc(qkv, out, dout, lse, dqkv, nseq, n_causal, S, H, bid, meta, rope, s);
   if (S <= kSeqMax && seq_path_enabled()) {
     CUtensorMap tq, tdo;
     if (!make_tmap(&tq, qkv, 3 * H * kHd, nseq * S, 3 * H * kHd, 64, 64)) return -10;
