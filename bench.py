@@ -321,6 +321,7 @@ def main():
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step":
                         d2h // args.steps, "ms_per_step": e2e_ms},
                 "gpu_launches": launches,
+                "host_enqueue_ms_per_step": host_enqueue_ms,
                 "roofline": roofline,
                 "clocks": clocks,
                 "cpu_baseline": cpu}

@@ -60,6 +60,7 @@ SIGNATURES = {
     "cdk_cast_f32_bf16": (_int, [_vp, _vp, _i64, _vp]),
     "cdk_add_f32": (_int, [_vp, _vp, _vp, _i64, _vp]),
     "cdk_scale_f32": (_int, [_vp, _i64, _f32, _vp]),
+    "cdk_swiglu_bwd": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _vp]),
     "cdk_gemm_f32": (_int, [_vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "cdk_sumsq": (_int, [_vp, _i64, _vp, _i64, _vp]),
     "cdk_adamw": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _f32, _f32, _f32, _f32, _f32, _f32, _i64, _f32,

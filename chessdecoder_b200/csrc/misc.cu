@@ -49,6 +49,39 @@ __global__ void scale_f32_kernel(float* __restrict__ x, long long n, float s) {
     x[i] *= s;
 }
 
+// SwiGLU backward (the w2(silu(w1 x) * w3 x) product of
+// chessdecoder/models/model.py:104-108):  given du = dL/d(silu(g) * u) and the
+// stored pre-activations gu = [g | u] (row pitch ldgu, u at column offset F),
+//   dg = du * u * silu'(g),  du_up = du * silu(g)   -> dgu = [dg | du_up].
+// Eight columns per thread, 16-byte loads and stores, fp32 math.
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ du, long long lddu,
+                                  const __nv_bfloat16* __restrict__ gu, long long ldgu,
+                                  __nv_bfloat16* __restrict__ dgu, long long lddgu, long long rows, int F) {
+  const int f8 = F / 8;
+  const long long total = rows * f8;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long r = idx / f8;
+    const int c = (int)(idx - r * f8) * 8;
+    const uint4 wd = *reinterpret_cast<const uint4*>(du + r * lddu + c);
+    const uint4 wg = *reinterpret_cast<const uint4*>(gu + r * ldgu + c);
+    const uint4 wu = *reinterpret_cast<const uint4*>(gu + r * ldgu + F + c);
+    const __nv_bfloat162* hd = reinterpret_cast<const __nv_bfloat162*>(&wd);
+    const __nv_bfloat162* hg = reinterpret_cast<const __nv_bfloat162*>(&wg);
+    const __nv_bfloat162* hu = reinterpret_cast<const __nv_bfloat162*>(&wu);
+    uint32_t og[4], ou[4];
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 d = __bfloat1622float2(hd[j]), g = __bfloat1622float2(hg[j]), u = __bfloat1622float2(hu[j]);
+      const float s0 = 1.f / (1.f + __expf(-g.x)), s1 = 1.f / (1.f + __expf(-g.y));
+      og[j] = pack_bf16(d.x * u.x * (s0 * (1.f + g.x * (1.f - s0))), d.y * u.y * (s1 * (1.f + g.y * (1.f - s1))));
+      ou[j] = pack_bf16(d.x * g.x * s0, d.y * g.y * s1);
+    }
+    *reinterpret_cast<uint4*>(dgu + r * lddgu + c) = make_uint4(og[0], og[1], og[2], og[3]);
+    *reinterpret_cast<uint4*>(dgu + r * lddgu + F + c) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+  }
+}
+
 // C[M,N] = beta*C + sum_k A(m,k) B(n,k) + bias[n]
 //   A(m,k) = a_t ? A[k*lda + m] : A[m*lda + k];  B(n,k) = b_t ? B[k*ldb + n] : B[n*ldb + k]
 // 64x64 tile, 16-deep k slices, 256 threads with a 4x4 micro-tile each.
@@ -176,6 +209,20 @@ extern "C" int cdk_scale_f32(float* x, int64_t n, float s, void* stream) {
   if (n == 0) return 0;
   if (!x) return -1;
   scale_f32_kernel<<<grid_for(n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, n, s);
+  return finish();
+}
+
+extern "C" int cdk_swiglu_bwd(const void* du, int64_t lddu, const void* gu, int64_t ldgu, void* dgu, int64_t lddgu,
+                              int64_t rows, int64_t F, void* stream) {
+  if (rows == 0) return 0;
+  if (!du || !gu || !dgu || F % 8 || lddu % 8 || ldgu % 8 || lddgu % 8 || rows < 0) return -1;
+  if ((reinterpret_cast<uintptr_t>(du) | reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(dgu)) & 15)
+    return -2;
+  long long blocks = (rows * (F / 8) + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  swiglu_bwd_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(du), lddu, reinterpret_cast<const __nv_bfloat16*>(gu), ldgu,
+      reinterpret_cast<__nv_bfloat16*>(dgu), lddgu, rows, (int)F);
   return finish();
 }
 

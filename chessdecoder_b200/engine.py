@@ -423,6 +423,7 @@ class Backbone:
         if on_layer_done is not None:
             on_layer_done(cfg.num_layers)  # heads + final norm done
         dgu = torch.empty(T, 2 * F, device=dev, dtype=torch.bfloat16)
+        du = torch.empty(T, F, device=dev, dtype=torch.bfloat16)
         dn = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
         dh1 = torch.empty(T, E, device=dev)
         dh1_16 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
@@ -432,8 +433,9 @@ class Backbone:
         for i in reversed(range(cfg.num_layers)):
             s = saved[i]
             w, g = self._w(i), self._g(i)
-            # MLP block
-            K.gemm(dh16, w["w2"], b_mn=True, kind=K.EPI_DSWIGLU, out=dgu, aux=s.gu, half_n=F, N=F)
+            # MLP block: du = dh W2 (plain GEMM), then the coalesced SwiGLU backward
+            K.gemm(dh16, w["w2"], b_mn=True, kind=K.EPI_STORE_BF16, out=du)
+            K.swiglu_bwd(du, s.gu, dgu)
             K.gemm(dh16, s.u, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w2"])
             K.gemm(dgu, w["w13"], b_mn=True, kind=K.EPI_STORE_BF16, out=dn)
             K.gemm(dgu, s.n2, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w13"])

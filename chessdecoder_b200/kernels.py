@@ -347,6 +347,16 @@ def add_f32(a, b, out):
     _count(1)
 
 
+@_timed("swiglu_bwd")
+def swiglu_bwd(du, gu, dgu):
+    """dgu = [du*u*silu'(g) | du*silu(g)] from du [T,F] and gu = [g | u] [T,2F] (all bf16)."""
+    _need_cuda(du, gu, dgu)
+    rows, F = du.shape
+    rc = lib().cdk_swiglu_bwd(_p(du), du.stride(0), _p(gu), gu.stride(0), _p(dgu), dgu.stride(0), rows, F, _stream())
+    _check(rc, "swiglu_bwd")
+    _count(1)
+
+
 @_timed("scale_f32")
 def scale_f32(x, s):
     _check(lib().cdk_scale_f32(_p(x), x.numel(), float(s), _stream()), "scale_f32")

@@ -145,6 +145,10 @@ int cdk_scatter_add_rows_f32(const float* src, int64_t ld_src, const int32_t* ro
 int cdk_cast_f32_bf16(const float* src, void* dst, int64_t n, void* stream);
 int cdk_add_f32(const float* a, const float* b, float* out, int64_t n, void* stream);
 int cdk_scale_f32(float* x, int64_t n, float s, void* stream);
+/* SwiGLU backward (FeedForward of model.py:104-108): du = dL/d(silu(g)*u) bf16
+ * [rows, F]; gu = [g | u] bf16 [rows, 2F]; dgu = [du*u*silu'(g) | du*silu(g)] bf16. */
+int cdk_swiglu_bwd(const void* du, int64_t lddu, const void* gu, int64_t ldgu, void* dgu, int64_t lddgu,
+                   int64_t rows, int64_t F, void* stream);
 /* fp32 SIMT GEMM for small / precision-sensitive contractions (Fourier
  * projection, value-head second Linear): C = (accumulate ? C : 0) + op(A) op(B)^T + bias,
  * A(m,k) = a_t ? A[k*lda+m] : A[m*lda+k],  B(n,k) = b_t ? B[k*ldb+n] : B[n*ldb+k]. */

@@ -155,6 +155,13 @@ def test_gemm_swiglu_and_back(K):
     torch.cuda.synchronize()
     assert rel_err(dgu[:, :F], ref_dg) < 1e-2
     assert rel_err(dgu[:, F:], ref_dup) < 1e-2
+    # the unfused form used by the step: bf16 du, then the elementwise SwiGLU backward
+    du16 = du.to(torch.bfloat16)
+    dgu2 = torch.empty(T, 2 * F, device=DEV, dtype=torch.bfloat16)
+    K.swiglu_bwd(du16, gu, dgu2)
+    torch.cuda.synchronize()
+    assert rel_err(dgu2[:, :F], ref_dg) < 1e-2
+    assert rel_err(dgu2[:, F:], ref_dup) < 1e-2
 
 
 def make_bid(nseq, S, gen):
