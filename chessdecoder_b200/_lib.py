@@ -65,6 +65,8 @@ SIGNATURES = {
     "cdk_sumsq": (_int, [_vp, _i64, _vp, _i64, _vp]),
     "cdk_adamw": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _f32, _f32, _f32, _f32, _f32, _f32, _i64, _f32,
                          _vp]),
+    "cdk_adamw_clip_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _f32, _f32, _f32, _f32, _f32, _i64,
+                                      _f32, _vp]),
 }
 
 _lib = None

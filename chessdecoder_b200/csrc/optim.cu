@@ -17,6 +17,8 @@
 #include "../../include/cdk.h"
 #include "cdk_common.cuh"
 
+#include <mutex>
+
 namespace cdk {
 
 __global__ void sumsq_kernel(const float* __restrict__ x, long long n, float* __restrict__ partial) {
@@ -112,6 +114,78 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
 }  // namespace cdk
 
 using namespace cdk;
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the clip + AdamW step.
+//
+// cdk_sumsq + cdk_adamw need a caller-provided scratch buffer for the
+// per-block partial sums of the gradient norm.  Some callers cannot provide
+// one: they hold only the parameter / gradient / moment buffers and have no
+// way to get more device memory -- a host runtime that passes raw device
+// pointers but has no CUDA allocator of its own, or a training loop running
+// inside a fixed, fully pre-reserved memory pool where a new allocation would
+// fail.  For them the partial sums live in the array below, which is part of
+// the library image: every GPU that loads libcdk.so holds these 16 KB until
+// the process exits.
+//
+// The array is shared by every call on a device and keeps the last call's
+// contents; each call overwrites exactly the entries it then reads, so
+// nothing has to be cleared first.  Calls whose kernels overlap on the GPU
+// (issued on different streams of one device) race on the array: issue them
+// one after another.
+// ---------------------------------------------------------------------------
+namespace cdk {
+
+constexpr int kNoAllocMaxPartial = 4096;
+static __device__ __align__(256) float g_noalloc_partial[kNoAllocMaxPartial];
+
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[64] = {nullptr};
+
+// Device address of g_noalloc_partial on the current device.  In host code
+// the symbol names a host-side stand-in, not device memory, so the address is
+// looked up once per device (with that device current) and cached.  This
+// lookup happens inside the first call on each device, so that first call
+// should be made before any stream capture begins.
+static int noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= 64) return -30;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_partial);
+    if (e != cudaSuccess || ptr == nullptr) return e != cudaSuccess ? (int)e : -31;
+    g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+}  // namespace cdk
+
+extern "C" int cdk_adamw_clip_noalloc(float* p, const float* g, float* m, float* v, void* p_bf16, int64_t n,
+                                      int64_t n_partial, float max_norm, float lr, float beta1, float beta2,
+                                      float eps, float wd, int64_t step, float grad_scale, void* stream) {
+  using namespace cdk;
+  if (n_partial <= 0 || n_partial > kNoAllocMaxPartial) return -32;  // scratch holds at most 4096 partial sums
+  if (n == 0) return 0;
+  if (!p || !g || !m || !v || n < 0 || step < 1) return -1;
+  if (((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(m) |
+        reinterpret_cast<uintptr_t>(v)) & 15) ||
+      (p_bf16 && (reinterpret_cast<uintptr_t>(p_bf16) & 7)))
+    return -2;
+  float* partial = nullptr;
+  int rc = noalloc_scratch(&partial);
+  if (rc != 0) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  sumsq_kernel<<<(unsigned)n_partial, 512, 0, s>>>(g, n, partial);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return (int)e;
+  return cdk_adamw(p, g, m, v, p_bf16, n, partial, n_partial, max_norm, lr, beta1, beta2, eps, wd, step, grad_scale,
+                   stream);
+}
 
 extern "C" int cdk_sumsq(const float* x, int64_t n, float* partial, int64_t n_partial, void* stream) {
   if (!x || !partial || n < 0 || n_partial <= 0 || n_partial > 4096) return -1;

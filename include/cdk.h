@@ -166,6 +166,21 @@ int cdk_adamw(float* p, const float* g, float* m, float* v, void* p_bf16, int64_
               int64_t n_partial, float max_norm, float lr, float beta1, float beta2, float eps, float wd,
               int64_t step, float grad_scale, void* stream);
 
+/* The same clip + AdamW step for callers that cannot allocate device memory
+ * (they hold only the parameter, gradient and moment buffers -- e.g. a host
+ * runtime passing raw device pointers without a CUDA allocator of its own, or
+ * a loop inside a fully pre-reserved memory pool).  No counterpart in the
+ * reference.  The n_partial (1..4096) gradient-norm partial sums go to a
+ * 16 KB array inside libcdk.so, one per device; nothing is allocated.  Sizes
+ * beyond 4096 partial sums are rejected (status -32).  Every call on a device
+ * shares that array (each call overwrites what it reads, so nothing needs
+ * clearing); calls that overlap on the GPU race and must be serialised.  The
+ * first call on a device looks up the array's device address, so make it
+ * before any stream capture. */
+int cdk_adamw_clip_noalloc(float* p, const float* g, float* m, float* v, void* p_bf16, int64_t n, int64_t n_partial,
+                           float max_norm, float lr, float beta1, float beta2, float eps, float wd, int64_t step,
+                           float grad_scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
