@@ -1,7 +1,7 @@
 // Shared device helpers for the chessdecoder_b200 kernel library (sm_100a only).
 //
 // Everything here is plain inline PTX or CUDA intrinsics: mbarrier waits with a
-// bounded spin, TMA tile loads (no cluster multicast anywhere in this library),
+// bounded spin, TMA tile loads (each CTA loads only into its own shared memory),
 // tcgen05 / TMEM helpers, mma.sync fragments for the attention kernels, and the
 // device-side error flag that every bounded wait reports into.
 #pragma once
@@ -96,8 +96,8 @@ __device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ---------------------------------------------------------------------------
-// TMA (bulk tensor) loads.  2-D tiled, completion on an mbarrier.  No
-// .multicast::cluster form exists in this library.
+// TMA (bulk tensor) loads.  2-D tiled, completion on an mbarrier, always
+// into the issuing CTA's own shared memory from this GPU's memory.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
   asm volatile(
