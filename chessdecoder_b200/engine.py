@@ -253,8 +253,13 @@ class DeviceBatch:
     h2d_bytes: int = 0
 
 
-def _host_index_lists(b: dict):
-    """Numpy restatement of the index bookkeeping of train.py:180-233."""
+def _host_index_lists(b: dict, require_pairing: bool = True):
+    """Numpy restatement of the index bookkeeping of train.py:180-233.
+
+    The D head reads rows at wl_positions with targets at d_positions, zipped
+    in order (train.py:225-230); unequal counts are an error there, and here
+    unless ``require_pairing`` is False (forward-only use), in which case the
+    D rows are cut to the shorter list."""
     ids = b["input_ids"].numpy()
     Bn, S = ids.shape
     move_mask = b["move_mask"].numpy()
@@ -288,7 +293,10 @@ def _host_index_lists(b: dict):
     wpf = np.nonzero(wl_pos.reshape(-1))[0]
     dpf = np.nonzero(d_pos.reshape(-1))[0]
     if wpf.size != dpf.size:
-        raise ValueError("wl_positions and d_positions must pair up one to one (train.py:225-230)")
+        if require_pairing:
+            raise ValueError("wl_positions and d_positions must pair up one to one (train.py:225-230)")
+        k = min(wpf.size, dpf.size)
+        wpf, dpf = wpf[:k], dpf[:k]
     drow = (BS + wpf).astype(np.int32)
     dtgt = d_t.reshape(-1)[dpf]
     dvalid = valid.reshape(-1)[dpf].astype(np.float32)
@@ -308,11 +316,11 @@ def _host_index_lists(b: dict):
                 norms=norms), Bn, S
 
 
-def prepare_batch(batch: dict, device) -> DeviceBatch:
+def prepare_batch(batch: dict, device, require_pairing: bool = True) -> DeviceBatch:
     """Builds the device batch: index lists on the host (numpy), then one
     pinned host buffer per dtype and one host-to-device copy each."""
     host = {k: (v.cpu() if torch.is_tensor(v) else torch.as_tensor(v)) for k, v in batch.items()}
-    lists, Bn, S = _host_index_lists(host)
+    lists, Bn, S = _host_index_lists(host, require_pairing)
     groups = {"i64": ["ids"], "f32": ["wl_t", "d_t", "board_w", "wtgt", "wvalid", "dtgt", "dvalid", "norms"],
               "i32": ["slot", "frows", "bid", "board_t", "prow", "pt", "wrow", "drow"],
               "u8": ["wl_pos", "d_pos"]}

@@ -150,7 +150,7 @@ def test_cuda_backbone_matches_reference_backbone():
              "wl_positions": g["override_mask"], "d_positions": torch.zeros(B, S, dtype=torch.bool),
              "wl_targets": g["override_values"], "d_targets": torch.zeros(B, S),
              "wdl_valid": torch.zeros(B, S, dtype=torch.bool), "block_id": g["block_id"]}
-    db = prepare_batch(batch, "cuda")
+    db = prepare_batch(batch, "cuda", require_pairing=False)
     meta = K.attn_meta(db.bid, S)
     h0, _ = step.front.forward(db, n_copies=2)
     _, h32, _ = step.backbone.forward(h0, 2 * B, B, S, db.bid, meta, want_f32=True)
