@@ -41,7 +41,7 @@ UNIT = "tokens/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--batch", type=int, default=64)
@@ -95,7 +95,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -234,8 +234,12 @@ def main():
     for i in range(args.warmup):
         dp.forward_backward(dbs[i % len(dbs)])
         dp.optimizer_step()
-    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
-                           else local_rank)
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys = torch.cuda.current_device()
+    if visible:
+        ids = [x.strip() for x in visible.split(",") if x.strip()]
+        phys = int(ids[phys]) if phys < len(ids) and ids[phys].isdigit() else phys
+    sampler = ClockSampler(phys)
     K.LAUNCHES[0] = 0
     if args.detail:
         K.OP_TIMER = {}
@@ -293,11 +297,16 @@ def main():
     roofline = {"bound": "tensor", "kernel": "gemm_bf16_kernel (tcgen05)", "achieved": achieved,
                 "peak": peak_sust, "unit": "TFLOP/s", "frac": achieved / peak_sust,
                 "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)",
-                "traffic": None, "launches_per_step": gemm_stats["launches"] // max(args.steps, 1),
+                "launches_per_step": gemm_stats["launches"] // max(args.steps, 1),
                 "share_of_step": gemm_stats["ms"] / args.steps / dev_ms}
-    prof = ROOT / "profiles" / "gemm_traffic.json"
-    if prof.exists():
-        roofline["traffic"] = json.loads(prof.read_text()).get("bytes_per_launch")
+    # DRAM bytes (read + write) of one launch of the largest GEMM shape, QKV + RoPE
+    # (M=32768, N=3072, K=1024), from one `ncu --set full --clock-control none`
+    # capture of `python -m chessdecoder_b200.probe gemm --kind rope`: 73.6 MB read
+    # (the algorithmic A + W bytes, no re-reads) + 150.5 MB written inside the
+    # launch; the launch's algorithmic bytes are 275 MB.
+    roofline["traffic"] = 224.0e6
+    roofline["traffic_launch"] = {"shape": "M32768 N3072 K1024 (QKV + RoPE epilogue)",
+                                  "dram_read": 73.6e6, "dram_write": 150.5e6, "algorithmic_bytes": 275.0e6}
 
     flops = step_flops(cfg, pool, args.seq)
     mfu_spec = flops / (dev_ms / 1000.0) / 2.25e15

@@ -193,7 +193,7 @@ def init_reference_weights(cfg: ModelConfig, seed: int = 0) -> dict:
     kaiming-uniform init; norms = 1; board, policy, thinking heads; WL / D value
     heads; Fourier frequencies N(0,1) then projection)."""
     import torch.nn as nn
-    g = torch.random.fork_rng()
+    g = torch.random.fork_rng(devices=[])  # weights are drawn on the CPU generator only
     with g:
         torch.manual_seed(seed)
         E, F, L = cfg.embed_dim, cfg.ff, cfg.num_layers
