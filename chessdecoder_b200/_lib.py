@@ -53,6 +53,7 @@ SIGNATURES = {
     "cdk_embed_bwd": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp]),
     "cdk_fourier_bwd": (_int, [_vp, _vp, _i32, _vp, _i64, _vp, _vp]),
     "cdk_softmax_ce": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _f32, _vp, _i64, _vp, _vp, _vp, _vp]),
+    "cdk_soft_bucket_ce": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _f32, _vp, _i64, _vp, _vp]),
     "cdk_value_tail": (_int, [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _f32, _vp, _vp, _vp, _i64, _vp,
                               _vp, _vp, _vp]),
     "cdk_gather_rows_bf16": (_int, [_vp, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),

@@ -41,9 +41,11 @@ __global__ void fourier_features_kernel(const float* __restrict__ wl_t, const fl
   const int t = rows[k];
   if (threadIdx.x == 0) {
     // d positions take precedence, matching the reference's overwrite order.
+    // nb == 0: the values are used as given (the model forward of
+    // model.py:177-180, whose inputs were snapped by the caller).
     float v = 0.f;
-    if (d_pos[t]) v = snap_to_bucket(d_t[t], d_c, nb);
-    else if (wl_pos[t]) v = snap_to_bucket(wl_t[t], wl_c, nb);
+    if (d_pos[t]) v = nb > 0 ? snap_to_bucket(d_t[t], d_c, nb) : d_t[t];
+    else if (wl_pos[t]) v = nb > 0 ? snap_to_bucket(wl_t[t], wl_c, nb) : wl_t[t];
     sval = v;
     values_out[k] = v;
   }
@@ -140,9 +142,10 @@ extern "C" int cdk_fourier_features(const float* wl_t, const float* d_t, const u
                                     const float* freqs, int32_t n_freq, const int32_t* rows, int64_t n_rows,
                                     float* values_out, float* feat_out, void* stream) {
   if (n_rows == 0) return 0;
-  if (!wl_t || !d_t || !wl_pos || !d_pos || !wl_centers || !d_centers || !freqs || !rows || !values_out ||
-      !feat_out || n_buckets <= 0 || n_freq <= 0 || n_rows < 0)
+  if (!wl_t || !d_t || !wl_pos || !d_pos || !freqs || !rows || !values_out || !feat_out || n_buckets < 0 ||
+      n_freq <= 0 || n_rows < 0)
     return -1;
+  if (n_buckets > 0 && (!wl_centers || !d_centers)) return -1;
   fourier_features_kernel<<<(unsigned)n_rows, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       wl_t, d_t, wl_pos, d_pos, wl_centers, d_centers, n_buckets, freqs, n_freq, rows, values_out, feat_out);
   cudaError_t e = cudaGetLastError();

@@ -176,6 +176,59 @@ __global__ void value_tail_kernel(const float* __restrict__ z1, long long rows, 
   }
 }
 
+// Soft two-bucket cross-entropy on given logits (utils/training.py:24-50),
+// one warp per row: lower = clamp(#{c <= t} - 1, 0, nb-2), upper = lower + 1,
+// w_up = clamp((t - c_lo) / max(c_up - c_lo, 1e-8), 0, 1);
+// loss += valid_r * -(sum soft * log_softmax) * norm;
+// dlogits (f32, optional) = (softmax - soft) * valid_r * norm * loss_weight.
+__global__ void soft_bucket_ce_kernel(const float* __restrict__ logits, long long ldl, long long rows, int nb,
+                                      const float* __restrict__ target, const float* __restrict__ valid,
+                                      const float* __restrict__ centers, const float* __restrict__ norm,
+                                      float loss_weight, float* __restrict__ dl, long long ldd,
+                                      float* __restrict__ loss_out) {
+  const int lane = threadIdx.x & 31;
+  const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const float* x = logits + r * ldl;
+  const float t = target[r];
+  float mx = -INFINITY;
+  int cnt = 0;
+  for (int c = lane; c < nb; c += 32) {
+    mx = fmaxf(mx, x[c]);
+    cnt += (t - centers[c] >= 0.f) ? 1 : 0;
+  }
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  }
+  float se = 0.f;
+  for (int c = lane; c < nb; c += 32) se += __expf(x[c] - mx);
+  se = warp_sum(se);
+  const float lse = mx + __logf(se);
+  int lo = cnt - 1;
+  lo = lo < 0 ? 0 : (lo > nb - 2 ? nb - 2 : lo);
+  const int up = lo + 1;
+  const float span = fmaxf(centers[up] - centers[lo], 1e-8f);
+  const float wup = fminf(fmaxf((t - centers[lo]) / span, 0.f), 1.f);
+  const float vw = valid ? valid[r] : 1.f;
+  const float nrm = norm ? *norm : 1.f;
+  if (lane == 0 && loss_out && vw != 0.f) {
+    const float ll = -((1.f - wup) * (x[lo] - lse) + wup * (x[up] - lse));
+    atomicAdd(loss_out, ll * vw * nrm);
+  }
+  if (dl) {
+    const float coef = vw * nrm * loss_weight;
+    const float inv = 1.f / se;
+    for (int c = lane; c < nb; c += 32) {
+      float g = __expf(x[c] - mx) * inv;
+      if (c == lo) g -= 1.f - wup;
+      if (c == up) g -= wup;
+      dl[r * ldd + c] = g * coef;
+    }
+  }
+}
+
 }  // namespace cdk
 
 using namespace cdk;
@@ -206,6 +259,18 @@ extern "C" int cdk_value_tail(const float* z1, int64_t rows, int64_t hidden, con
   value_tail_kernel<<<(unsigned)rows, 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
       z1, rows, (int)hidden, w2, b2, (int)nb, target, valid, centers, norm, loss_weight, act_out, dlogits_out,
       reinterpret_cast<__nv_bfloat16*>(dz1_bf16), ldd, db1, loss_out, argmax_out);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+extern "C" int cdk_soft_bucket_ce(const float* logits, int64_t ldl, int64_t rows, int64_t nb, const float* target,
+                                  const float* valid, const float* centers, const float* norm, float loss_weight,
+                                  float* dlogits, int64_t ldd, float* loss_out, void* stream) {
+  if (rows == 0) return 0;
+  if (!logits || !target || !centers || rows < 0 || nb < 2 || ldl < nb) return -1;
+  if (dlogits && ldd < nb) return -2;
+  soft_bucket_ce_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      logits, ldl, rows, (int)nb, target, valid, centers, norm, loss_weight, dlogits, ldd, loss_out);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
 }

@@ -65,32 +65,27 @@ def print_rank0(*args, **kwargs):
         print(*args, **kwargs)
 
 
-def _flat_grad_buffers(model) -> List[torch.Tensor]:
-    """If every gradient is a view into one flat buffer, that buffer (once)."""
-    store = getattr(model, "_store", None)
-    if store is not None:
-        return [store.grad]
-    return []
-
-
 def average_gradients(model, bucket_bytes: int = 25 * 1024 * 1024):
     """After return every ``p.grad`` holds the mean over ranks (utils/distributed.py:55-67).
 
-    Gradients are reduced in ~25 MB contiguous buckets (the flat store of a
-    chessdecoder_b200 model, otherwise coalesced per bucket) instead of one
-    collective per parameter.  No-op when not distributed.
+    Gradients are reduced in ~25 MB buckets instead of one collective per
+    parameter: the backbone gradients of a chessdecoder_b200 ``ChessDecoder``
+    are views of one flat buffer, reduced in place slice by slice; all other
+    gradients are coalesced per bucket.  No-op when not distributed.
     """
     if not dist.is_initialized():
         return
     world = dist.get_world_size()
-    flats = _flat_grad_buffers(model)
-    if flats:
-        for buf in flats:
-            n = bucket_bytes // buf.element_size()
-            for s in range(0, buf.numel(), n):
-                _all_reduce_mean(buf[s:s + n], world)
-        return
-    grads = [p.grad for p in model.parameters() if p.grad is not None]
+    done = set()
+    core = getattr(model, "_core", None)
+    if core is not None:
+        flat = core.flat_grad_of(model)
+        if flat is not None:
+            n = bucket_bytes // flat.element_size()
+            for s in range(0, flat.numel(), n):
+                _all_reduce_mean(flat[s:s + n], world)
+            done = {id(core.params[i]) for i in core.backbone_idx}
+    grads = [p.grad for p in model.parameters() if p.grad is not None and id(p) not in done]
     bucket, size = [], 0
     for g in grads:
         bucket.append(g)

@@ -112,7 +112,7 @@ class ParamStore:
     gradient, AdamW moment and bf16 shadow buffers.  ``param(name)`` returns a
     view shaped like the reference parameter."""
 
-    def __init__(self, cfg: ModelConfig, device):
+    def __init__(self, cfg: ModelConfig, device, optimizer_state: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         self.offsets = {}
@@ -126,10 +126,13 @@ class ParamStore:
             off += n if pad == 0 else (n + _ALIGN - 1) // _ALIGN * _ALIGN
         self.numel = off
         self.flat = torch.zeros(off, dtype=torch.float32, device=self.device)
-        self.grad = torch.zeros(off, dtype=torch.float32, device=self.device)
-        self.exp_avg = torch.zeros(off, dtype=torch.float32, device=self.device)
-        self.exp_avg_sq = torch.zeros(off, dtype=torch.float32, device=self.device)
         self.flat16 = torch.zeros(off, dtype=torch.bfloat16, device=self.device)
+        if optimizer_state:
+            self.grad = torch.zeros(off, dtype=torch.float32, device=self.device)
+            self.exp_avg = torch.zeros(off, dtype=torch.float32, device=self.device)
+            self.exp_avg_sq = torch.zeros(off, dtype=torch.float32, device=self.device)
+        else:  # the nn.Module front end: gradients are allocated per backward, moments by the optimizer
+            self.grad = self.exp_avg = self.exp_avg_sq = None
         self.step = 0
         # the thinking head gets no gradient in pretraining (train.py never calls it)
         E = cfg.embed_dim
@@ -470,7 +473,9 @@ class FrontEnd:
         self.wl_c = make_wl_buckets(cfg.n_buckets, cfg.wl_sigma).to(store.device)
         self.d_c = make_d_buckets(cfg.n_buckets).to(store.device)
 
-    def forward(self, db: DeviceBatch, n_copies: int):
+    def forward(self, db: DeviceBatch, n_copies: int, snap: bool = True):
+        """snap=False: the placeholder values are used as given (the module
+        forward, whose caller snapped them with prepare_fourier_inputs)."""
         cfg, st = self.cfg, self.st
         E, nf = cfg.embed_dim, cfg.num_fourier_freq
         dev = db.ids.device
@@ -479,7 +484,8 @@ class FrontEnd:
         feat = torch.empty(max(Nf, 1), 2 * nf, device=dev)
         frows_out = torch.empty(max(Nf, 1), E, device=dev)
         if Nf:
-            K.fourier_features(db.wl_t, db.d_t, db.wl_pos, db.d_pos, self.wl_c, self.d_c,
+            K.fourier_features(db.wl_t, db.d_t, db.wl_pos, db.d_pos, self.wl_c if snap else None,
+                               self.d_c if snap else None,
                                st.param("fourier_encoder.frequencies"), db.frows, fvals, feat)
             K.gemm_f32(feat, st.param("fourier_encoder.proj.weight"), frows_out,
                        bias=st.param("fourier_encoder.proj.bias"), M=Nf)

@@ -260,8 +260,10 @@ def rmsnorm_bwd(dy, x, scale, rstd, dx=None, dx16=None, dscale=None, dres=None):
 # ---------------------------------------------------------------------------
 @_timed("fourier_features")
 def fourier_features(wl_t, d_t, wl_pos_u8, d_pos_u8, wl_c, d_c, freqs, rows32, values_out, feat_out):
+    """wl_c / d_c = None: use the values as given (no bucket snapping)."""
     n = rows32.numel()
-    rc = lib().cdk_fourier_features(_p(wl_t), _p(d_t), _p(wl_pos_u8), _p(d_pos_u8), _p(wl_c), _p(d_c), wl_c.numel(),
+    nb = 0 if wl_c is None else wl_c.numel()
+    rc = lib().cdk_fourier_features(_p(wl_t), _p(d_t), _p(wl_pos_u8), _p(d_pos_u8), _p(wl_c), _p(d_c), nb,
                                     _p(freqs), freqs.numel(), _p(rows32), n, _p(values_out), _p(feat_out), _stream())
     _check(rc, "fourier_features")
     _count(1)
@@ -305,6 +307,16 @@ def softmax_ce(logits, target32, row_w, norm, loss_weight, dlogits=None, dbias=N
                               float(loss_weight), _p(dlogits), dlogits.stride(0) if dlogits is not None else 0,
                               _p(dbias), _p(loss_out), _p(argmax), _stream())
     _check(rc, "softmax_ce")
+    _count(1)
+
+
+@_timed("soft_bucket_ce")
+def soft_bucket_ce(logits, target, valid, centers, norm, loss_weight, dlogits=None, loss_out=None):
+    rows, nb = logits.shape
+    rc = lib().cdk_soft_bucket_ce(_p(logits), logits.stride(0), rows, nb, _p(target), _p(valid), _p(centers), _p(norm),
+                                  float(loss_weight), _p(dlogits), dlogits.stride(0) if dlogits is not None else 0,
+                                  _p(loss_out), _stream())
+    _check(rc, "soft_bucket_ce")
     _count(1)
 
 

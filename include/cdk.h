@@ -107,6 +107,10 @@ int cdk_rmsnorm_bwd(const void* dy, int dy_is_f32, const float* x, const float* 
 
 /* ---- embedding + Fourier value injection (model.py:24-36, 174-180) and the
  *      bucket snapping of utils/training.py:114-133 / model.py:189-194 ------ */
+/* values_out[k] = the value at placeholder row rows[k] (d_pos wins over wl_pos),
+ * snapped to the nearest bucket centre when n_buckets > 0 and taken as given
+ * when n_buckets == 0 (centre pointers may then be NULL); feat_out[k] =
+ * [cos(2 pi v f) | sin(2 pi v f)]. */
 int cdk_fourier_features(const float* wl_t, const float* d_t, const uint8_t* wl_pos, const uint8_t* d_pos,
                          const float* wl_centers, const float* d_centers, int32_t n_buckets, const float* freqs,
                          int32_t n_freq, const int32_t* rows, int64_t n_rows, float* values_out, float* feat_out,
@@ -136,6 +140,13 @@ int cdk_value_tail(const float* z1, int64_t rows, int64_t hidden, const float* w
                    const float* target, const float* valid, const float* centers, const float* norm,
                    float loss_weight, float* act_out, float* dlogits_out, void* dz1_bf16, int64_t ldd, float* db1,
                    float* loss_out, int32_t* argmax_out, void* stream);
+/* soft_bucket_ce: the soft two-bucket cross-entropy of utils/training.py:24-50
+ * on given logits [rows, nb] (row stride ldl): *loss_out += sum_r valid_r *
+ * ce_r * (*norm); dlogits f32 [rows, ldd] (optional) = (softmax - soft labels)
+ * * valid_r * (*norm) * loss_weight.  valid / norm may be NULL (= 1). */
+int cdk_soft_bucket_ce(const float* logits, int64_t ldl, int64_t rows, int64_t nb, const float* target,
+                       const float* valid, const float* centers, const float* norm, float loss_weight,
+                       float* dlogits, int64_t ldd, float* loss_out, void* stream);
 
 /* ---- gathers / scatters / casts around the heads ------------------------ */
 int cdk_gather_rows_bf16(const void* src, int64_t ld_src, const int32_t* rows, int64_t n, int64_t dim, void* dst,
