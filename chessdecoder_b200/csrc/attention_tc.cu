@@ -9,17 +9,19 @@
 // into shared memory.  Then:
 //   1. one thread issues S = Q K^T as tcgen05.mma (M=128, N=keys<=256, K=64)
 //      into TMEM;
-//   2. four softmax warps (one TMEM lane = one query row per thread) read the
-//      whole score row back with tcgen05.ld, apply the causal / block-prefix
-//      mask and a single-pass softmax (the full row is resident, so no online
-//      rescaling), and write P in bf16 into a 128-byte-swizzled K-major
-//      shared-memory operand;
+//   2. eight softmax warps (two threads per query row: the TMEM lane is the
+//      row, the even / odd 32-key chunks are split between warps w and w+4)
+//      read the score row back with tcgen05.ld, apply the causal /
+//      block-prefix mask and a single-pass softmax (the full row is
+//      resident, so no online rescaling; the two halves exchange their row
+//      max and sum through shared memory), and write P in bf16 into a
+//      128-byte-swizzled K-major shared-memory operand;
 //   3. O = P V is issued as tcgen05.mma (M=128, N=64, K=keys, V read
 //      MN-major straight from its TMA tile) into a second TMEM region;
 //   4. the same warps scale O by 1/rowsum and store it, plus the base-2
 //      log-sum-exp that the backward needs.
-// Warp roles (192 threads): thread 0 = barriers + TMA, warp 1 = TMEM
-// allocation + MMA issue, warps 2-5 = softmax / epilogue.  All waits are
+// Warp roles (320 threads): thread 0 = barriers + TMA, warp 1 = TMEM
+// allocation + MMA issue, warps 2-9 = softmax / epilogue.  All waits are
 // bounded (cdk_common).
 #include "../../include/cdk.h"
 #include "cdk_common.cuh"
@@ -57,6 +59,8 @@ struct FwdSmem {
   int n_keys;                      // keys (multiple of 32) this query tile may see
   int32_t bid[kMaxS];
   int32_t hi[kMaxS];               // max(i, last[i]): no key beyond it is visible to row i
+  float red_max[2][128];           // per-half row maxima / sums of the two softmax threads of a row
+  float red_sum[2][128];
 };
 constexpr int kQOff = 0;
 constexpr int kKOff = 16384;
@@ -76,7 +80,7 @@ __device__ __forceinline__ bool visible(int i, int j, int S, int hi, int my_bid,
   return j < S && (j <= i || (j <= hi && bid[j] == my_bid));
 }
 
-constexpr int kFwdThreads = 192;  // warp 0 TMA, warp 1 TMEM + MMA, warps 2-5 softmax / epilogue
+constexpr int kFwdThreads = 320;  // warp 0 TMA, warp 1 TMEM + MMA, warps 2-9 softmax / epilogue
 
 __global__ void __launch_bounds__(kFwdThreads, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tqkv, const Args a) {
@@ -96,7 +100,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     mbar_init(&sm.bar_k, 1);
     mbar_init(&sm.bar_v, 1);
     mbar_init(&sm.bar_s, 1);
-    mbar_init(&sm.bar_p, 128);
+    mbar_init(&sm.bar_p, 256);
     mbar_init(&sm.bar_o, 1);
     sm.abort = 0;
     fence_mbar_init();
@@ -163,7 +167,10 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
       tc_commit(&sm.bar_o);
     }
   } else if (warp >= 2) {
+    // Two threads per query row: warps w and w+4 share TMEM lane quadrant
+    // (w & 3); half 0 takes the even 32-key chunks, half 1 the odd ones.
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     const float sl2 = 0.125f * kLog2e;
@@ -183,99 +190,89 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     // pass 1: max of the raw scores of keys [0, hi] (exact for contiguous
     // blocks, an upper bound otherwise -- either keeps exp2 <= 1)
     float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    for (int c = 0; c < nch; c += 2) {
-      if (c * 32 > hi_w) break;
-      uint32_t u0[32], u1[32];
-      tmem_ld_x32_nowait(trow + c * 32, u0);
-      if (c + 1 < nch) tmem_ld_x32_nowait(trow + (c + 1) * 32, u1);
+    for (int c = half; c < nch; c += 2) {
+      const int base = c * 32;
+      if (base > hi_w) break;
+      uint32_t u[32];
+      tmem_ld_x32_nowait(trow + base, u);
       tmem_wait_ld();
-      #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int base = (c + half) * 32;
-        if (c + half >= nch || base > hi) break;
-        const uint32_t* u = half ? u1 : u0;
-        if (base + 31 <= hi) {
-          #pragma unroll
-          for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(u[e]));
-        } else {
-          #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (base + e <= hi) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(u[e]));
-        }
+      if (base + 31 <= hi) {
+        #pragma unroll
+        for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(u[e]));
+      } else if (base <= hi) {
+        #pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (base + e <= hi) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(u[e]));
       }
     }
-    const float ms = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
-    // pass 2: probabilities -> bf16 P operand (overwrites Q/K), row sum
+    sm.red_max[half][r] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    const float ms = fmaxf(sm.red_max[0][r], sm.red_max[1][r]) * sl2;
+    // pass 2: probabilities -> bf16 P operand (overwrites Q/K), partial row sum
     float l4[4] = {0.f, 0.f, 0.f, 0.f};
     uint8_t* P = sm.qkp;
-    for (int c = 0; c < nch; c += 2) {
-      uint32_t u0[32], u1[32];
-      const bool any0 = c * 32 <= hi_w;                      // warp-uniform
-      const bool any1 = c + 1 < nch && (c + 1) * 32 <= hi_w;  // warp-uniform
-      if (any0) tmem_ld_x32_nowait(trow + c * 32, u0);
-      if (any1) tmem_ld_x32_nowait(trow + (c + 1) * 32, u1);
-      tmem_wait_ld();
-      #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int cc = c + half;
-        if (cc >= nch) break;
-        const uint32_t* u = half ? u1 : u0;
-        const int base = cc * 32;
-        uint32_t pk[16];
-        if (base + 31 <= i_eff) {
-          #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float p0 = exp2f(fmaf(__uint_as_float(u[e]), sl2, -ms));
-            const float p1 = exp2f(fmaf(__uint_as_float(u[e + 1]), sl2, -ms));
-            l4[(e >> 1) & 3] += p0 + p1;
-            pk[e >> 1] = pack_bf16(p0, p1);
-          }
-        } else if (base <= hi) {
-          #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const bool v0 = visible(i, base + e, S, hi, my_bid, sm.bid);
-            const bool v1 = visible(i, base + e + 1, S, hi, my_bid, sm.bid);
-            const float p0 = v0 ? exp2f(fmaf(__uint_as_float(u[e]), sl2, -ms)) : 0.f;
-            const float p1 = v1 ? exp2f(fmaf(__uint_as_float(u[e + 1]), sl2, -ms)) : 0.f;
-            l4[(e >> 1) & 3] += p0 + p1;
-            pk[e >> 1] = pack_bf16(p0, p1);
-          }
-        } else {
-          #pragma unroll
-          for (int e = 0; e < 16; ++e) pk[e] = 0u;
-        }
-        uint8_t* blk = P + (cc >> 1) * (128 * 128);
-        const int cbase = (cc & 1) * 32;
-        #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4*>(blk + sw128(r, cbase + q * 8)) =
-              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+    for (int cc = half; cc < nch; cc += 2) {
+      const int base = cc * 32;
+      uint32_t u[32];
+      const bool any = base <= hi_w;  // warp-uniform
+      if (any) {
+        tmem_ld_x32_nowait(trow + base, u);
+        tmem_wait_ld();
       }
+      uint32_t pk[16];
+      if (base + 31 <= i_eff) {
+        #pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float p0 = exp2f(fmaf(__uint_as_float(u[e]), sl2, -ms));
+          const float p1 = exp2f(fmaf(__uint_as_float(u[e + 1]), sl2, -ms));
+          l4[(e >> 1) & 3] += p0 + p1;
+          pk[e >> 1] = pack_bf16(p0, p1);
+        }
+      } else if (base <= hi) {
+        #pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const bool v0 = visible(i, base + e, S, hi, my_bid, sm.bid);
+          const bool v1 = visible(i, base + e + 1, S, hi, my_bid, sm.bid);
+          const float p0 = v0 ? exp2f(fmaf(__uint_as_float(u[e]), sl2, -ms)) : 0.f;
+          const float p1 = v1 ? exp2f(fmaf(__uint_as_float(u[e + 1]), sl2, -ms)) : 0.f;
+          l4[(e >> 1) & 3] += p0 + p1;
+          pk[e >> 1] = pack_bf16(p0, p1);
+        }
+      } else {
+        #pragma unroll
+        for (int e = 0; e < 16; ++e) pk[e] = 0u;
+      }
+      uint8_t* blk = P + (cc >> 1) * (128 * 128);
+      const int cbase = (cc & 1) * 32;
+      #pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(blk + sw128(r, cbase + q * 8)) =
+            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
     }
-    const float l = (l4[0] + l4[1]) + (l4[2] + l4[3]);
+    sm.red_sum[half][r] = (l4[0] + l4[1]) + (l4[2] + l4[3]);
     fence_proxy_async();
     tc_fence_before();
     mbar_arrive(&sm.bar_p);
-    // epilogue: O / l
+    // epilogue: O / l, half h stores dims [32h, 32h + 32)
     mbar_wait(&sm.bar_o, 0, abort_flag);
+    asm volatile("bar.sync 1, 256;" ::: "memory");
     tc_fence_after();
+    const float l = sm.red_sum[0][r] + sm.red_sum[1][r];
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    uint32_t o0[32], o1[32];
-    tmem_ld_x32_nowait(trow, o0);
-    tmem_ld_x32_nowait(trow + 32, o1);
+    uint32_t o[32];
+    tmem_ld_x32_nowait(trow + half * 32, o);
     tmem_wait_ld();
     if (row_ok) {
-      uint4* dst = reinterpret_cast<uint4*>(a.out + (long long)(row_base + i) * E + h * kHd);
+      uint4* dst = reinterpret_cast<uint4*>(a.out + (long long)(row_base + i) * E + h * kHd + half * 32);
       #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const uint32_t* o = q < 4 ? o0 : o1;
-        const int b = (q & 3) * 8;
+      for (int q = 0; q < 4; ++q) {
+        const int b = q * 8;
         dst[q] = make_uint4(pack_bf16(__uint_as_float(o[b]) * inv, __uint_as_float(o[b + 1]) * inv),
                             pack_bf16(__uint_as_float(o[b + 2]) * inv, __uint_as_float(o[b + 3]) * inv),
                             pack_bf16(__uint_as_float(o[b + 4]) * inv, __uint_as_float(o[b + 5]) * inv),
                             pack_bf16(__uint_as_float(o[b + 6]) * inv, __uint_as_float(o[b + 7]) * inv));
       }
-      a.lse[((long long)seq * a.H + h) * S + i] = ms + log2f(l);
+      if (half == 0) a.lse[((long long)seq * a.H + h) * S + i] = ms + log2f(l);
     }
   }
   tc_fence_before();
@@ -320,20 +317,25 @@ struct BwdSmem {
   uint8_t dO[kTiles][kTileBytes];
   uint8_t PT[2][128 * 128];   // [query block][128 key rows x 64 queries]
   uint8_t dST[2][128 * 128];
-  uint64_t bar_load, bar_sa, bar_ew, bar_mb, bar_epi;
+  uint64_t bar_load, bar_o, bar_sa, bar_ew, bar_mb, bar_epi;
   uint32_t tmem_base;
   int abort;
-  float D[kMaxS];
-  float L[kMaxS];
+  alignas(16) float D[kMaxS];  // read as float4
+  alignas(16) float L[kMaxS];
+  float Dpart[2][kMaxS];
   int32_t bid[kMaxS];
   int32_t first[kMaxS];
 };
 
-constexpr int kBwdThreads = 320;
+static_assert(offsetof(BwdSmem, D) % 16 == 0 && offsetof(BwdSmem, L) % 16 == 0, "D / L are read as float4");
+static_assert(offsetof(BwdSmem, PT) % 1024 == 0 && offsetof(BwdSmem, dST) % 1024 == 0,
+              "TMA / UMMA operands with the 128-byte swizzle need 1024-byte alignment");
+
+constexpr int kBwdThreads = 576;  // warp 0 TMA, warp 1 TMEM + MMA, warps 2-17 elementwise / epilogue
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo,
-                       const BwdArgs a) {
+                       const __grid_constant__ CUtensorMap tout, const BwdArgs a) {
   extern __shared__ uint8_t raw[];
   BwdSmem& sm = *reinterpret_cast<BwdSmem*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   const int h = blockIdx.x, seq = blockIdx.y;
@@ -348,14 +350,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.bar_load, 1);
+    mbar_init(&sm.bar_o, 1);
     mbar_init(&sm.bar_sa, 1);
-    mbar_init(&sm.bar_ew, 256);
+    mbar_init(&sm.bar_ew, 512);
     mbar_init(&sm.bar_mb, 1);
-    mbar_init(&sm.bar_epi, 256);
+    mbar_init(&sm.bar_epi, 512);
     sm.abort = 0;
     fence_mbar_init();
     prefetch_tmap(&tqkv);
     prefetch_tmap(&tdo);
+    prefetch_tmap(&tout);
+    // O (for D = rowsum(dO * O)) goes into the P^T buffer, which is free
+    // until the first elementwise phase
+    mbar_arrive_expect_tx(&sm.bar_o, kTiles * kTileBytes);
+    for (int t = 0; t < kTiles; ++t)
+      tma_load_2d(sm.PT[0] + t * kTileBytes, &tout, &sm.bar_o, h * kHd, row_base + t * kTileRows);
     // all four 64-row tiles of every operand: rows past this sequence are the
     // next sequence's (finite) values or TMA zero fill, never stale memory
     mbar_arrive_expect_tx(&sm.bar_load, 4 * kTiles * kTileBytes);
@@ -371,25 +380,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const bool ok = i < S;
     sm.bid[i] = ok ? (prefix ? a.bid[(long long)pseq * S + i] : i) : -1;
     sm.first[i] = ok ? (prefix ? a.first[(long long)pseq * S + i] : i) : S;
-    float d = 0.f, l = 0.f;
-    if (ok) {
-      const uint4* po = reinterpret_cast<const uint4*>(a.out + (long long)(row_base + i) * E + h * kHd);
-      const uint4* pd = reinterpret_cast<const uint4*>(a.dout + (long long)(row_base + i) * E + h * kHd);
-      #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const uint4 wo = po[q], wd = pd[q];
-        const __nv_bfloat162* ho = reinterpret_cast<const __nv_bfloat162*>(&wo);
-        const __nv_bfloat162* hd = reinterpret_cast<const __nv_bfloat162*>(&wd);
-        #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 fo = __bfloat1622float2(ho[j]), fd = __bfloat1622float2(hd[j]);
-          d += fo.x * fd.x + fo.y * fd.y;
-        }
-      }
-      l = a.lse[lrow + i];
-    }
-    sm.D[i] = d;
-    sm.L[i] = l;
+    sm.L[i] = ok ? a.lse[lrow + i] : 0.f;
   }
   if (warp == 1) {
     tmem_alloc(&sm.tmem_base, 512);
@@ -467,11 +458,47 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   } else if (warp >= 2) {
-    const int g = (warp - 2) >> 2;
+    // 16 elementwise warps: group g = (warp - 2) / 4 owns query columns
+    // [32g, 32g + 32) of the 128-query half; the TMEM lane quadrant (warp & 3)
+    // is the key row block.
+    const int ew = warp - 2;
+    const int g = ew >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const float sl2 = 0.125f * kLog2e;
+    {
+      // D[i] = rowsum(dO_i * O_i) from the swizzled O (in PT) and dO tiles:
+      // two threads per row, 32 dims each; rows >= S get 0
+      const int t = ew * 32 + lane;  // 0..511
+      const int i = t & 255, part = t >> 8;
+      mbar_wait(&sm.bar_load, 0, abort_flag);
+      mbar_wait(&sm.bar_o, 0, abort_flag);
+      float dsum = 0.f;
+      if (i < S) {
+        const uint8_t* ot = sm.PT[0] + (i >> 6) * kTileBytes;
+        const uint8_t* dt = sm.dO[i >> 6];
+        const int rr = i & 63;
+        #pragma unroll
+        for (int c = part * 4; c < part * 4 + 4; ++c) {
+          const uint32_t off = (uint32_t)(rr * 128 + (((c ^ (rr & 7)) & 7) << 4));
+          const uint4 wo = *reinterpret_cast<const uint4*>(ot + off);
+          const uint4 wd = *reinterpret_cast<const uint4*>(dt + off);
+          const __nv_bfloat162* ho = reinterpret_cast<const __nv_bfloat162*>(&wo);
+          const __nv_bfloat162* hd = reinterpret_cast<const __nv_bfloat162*>(&wd);
+          #pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 fo = __bfloat1622float2(ho[e]), fd = __bfloat1622float2(hd[e]);
+            dsum = fmaf(fo.x, fd.x, fmaf(fo.y, fd.y, dsum));
+          }
+        }
+      }
+      sm.Dpart[part][i] = dsum;
+      asm volatile("bar.sync 1, 512;" ::: "memory");
+      if (t < 256) sm.D[t] = sm.Dpart[0][t] + sm.Dpart[1][t];
+      // all D written and all O reads done before P^T overwrites the buffer
+      asm volatile("bar.sync 1, 512;" ::: "memory");
+    }
     for (int it = 0; it < nit; ++it) {
       const int code = (codes >> (2 * it)) & 3;
       const int kt = code >> 1, qh = code & 1;
@@ -480,95 +507,107 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const bool jok = j < S;
       const int fj = jok ? sm.first[j] : S;
       const int bj = jok ? sm.bid[j] : -2;
+      const int qb = qh * 128 + g * 32;
+      // per-thread classification of this 32-query chunk, and its warp-uniform form
+      const bool full = jok && qb >= j && qb + 31 < S;
+      const bool none = !jok || qb + 31 < fj || qb >= S;
+      const bool none_w = __all_sync(0xffffffffu, none);
       mbar_wait(&sm.bar_sa, it & 1, abort_flag);
       if (it > 0) mbar_wait(&sm.bar_mb, (it - 1) & 1, abort_flag);
       tc_fence_after();
-      uint32_t s0[32], s1[32], d0[32], d1[32];
-      tmem_ld_x32_nowait(tmem + lane_off + g * 64, s0);
-      tmem_ld_x32_nowait(tmem + lane_off + g * 64 + 32, s1);
-      tmem_ld_x32_nowait(tmem + lane_off + 128 + g * 64, d0);
-      tmem_ld_x32_nowait(tmem + lane_off + 128 + g * 64 + 32, d1);
-      tmem_wait_ld();
+      uint8_t* pt = sm.PT[g >> 1];
+      uint8_t* dst = sm.dST[g >> 1];
+      const int cbase = (g & 1) * 32;
       #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const uint32_t* su = cc ? s1 : s0;
-        const uint32_t* du = cc ? d1 : d0;
-        const int qb = qh * 128 + g * 64 + cc * 32;
-        const bool full = jok && qb >= j && qb + 31 < S;
-        const bool none = !jok || qb + 31 < fj || qb >= S;
-        uint32_t pk[16], dk[16];
-        if (none) {
+      for (int sc = 0; sc < 2; ++sc) {
+        uint32_t pk[8], dk[8];
+        if (none_w || none) {
           #pragma unroll
-          for (int e = 0; e < 16; ++e) pk[e] = dk[e] = 0u;
-        } else {
-          // L and D of these 32 queries: the same addresses in every lane (broadcast)
-          const float4* L4 = reinterpret_cast<const float4*>(sm.L + qb);
-          const float4* D4 = reinterpret_cast<const float4*>(sm.D + qb);
-          #pragma unroll
-          for (int e4 = 0; e4 < 8; ++e4) {
-            const float4 l4 = L4[e4], dd4 = D4[e4];
-            const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-            const float dv4[4] = {dd4.x, dd4.y, dd4.z, dd4.w};
-            float pv[4], dsv[4];
+          for (int e = 0; e < 8; ++e) pk[e] = dk[e] = 0u;
+        }
+        if (!none_w) {
+          uint32_t su[16], du[16];
+          tmem_ld_x16_nowait(tmem + lane_off + g * 32 + sc * 16, su);
+          tmem_ld_x16_nowait(tmem + lane_off + 128 + g * 32 + sc * 16, du);
+          tmem_wait_ld();
+          if (!none) {
+            // L and D of these 16 queries: the same addresses in every lane (broadcast)
+            const int q0 = qb + sc * 16;
+            const float4* L4 = reinterpret_cast<const float4*>(sm.L + q0);
+            const float4* D4 = reinterpret_cast<const float4*>(sm.D + q0);
             #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int e = e4 * 4 + k;
-              const float p = exp2f(fmaf(__uint_as_float(su[e]), sl2, -lv[k]));
-              pv[k] = p;
-              dsv[k] = p * (__uint_as_float(du[e]) - dv4[k]);
-            }
-            if (!full) {
+            for (int e4 = 0; e4 < 4; ++e4) {
+              const float4 l4 = L4[e4], dd4 = D4[e4];
+              const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+              const float dv4[4] = {dd4.x, dd4.y, dd4.z, dd4.w};
+              float pv[4], dsv[4];
               #pragma unroll
               for (int k = 0; k < 4; ++k) {
-                const int i = qb + e4 * 4 + k;
-                const bool vis = i < S && (i >= j || (i >= fj && sm.bid[i] == bj));
-                pv[k] = vis ? pv[k] : 0.f;
-                dsv[k] = vis ? dsv[k] : 0.f;
+                const int e = e4 * 4 + k;
+                const float p = exp2f(fmaf(__uint_as_float(su[e]), sl2, -lv[k]));
+                pv[k] = p;
+                dsv[k] = p * (__uint_as_float(du[e]) - dv4[k]);
               }
+              if (!full) {
+                #pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const int i = q0 + e4 * 4 + k;
+                  const bool vis = i < S && (i >= j || (i >= fj && sm.bid[i] == bj));
+                  pv[k] = vis ? pv[k] : 0.f;
+                  dsv[k] = vis ? dsv[k] : 0.f;
+                }
+              }
+              pk[e4 * 2] = pack_bf16(pv[0], pv[1]);
+              pk[e4 * 2 + 1] = pack_bf16(pv[2], pv[3]);
+              dk[e4 * 2] = pack_bf16(dsv[0], dsv[1]);
+              dk[e4 * 2 + 1] = pack_bf16(dsv[2], dsv[3]);
             }
-            pk[e4 * 2] = pack_bf16(pv[0], pv[1]);
-            pk[e4 * 2 + 1] = pack_bf16(pv[2], pv[3]);
-            dk[e4 * 2] = pack_bf16(dsv[0], dsv[1]);
-            dk[e4 * 2 + 1] = pack_bf16(dsv[2], dsv[3]);
           }
         }
         #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t off = sw128(r, cc * 32 + q * 8);
-          *reinterpret_cast<uint4*>(sm.PT[g] + off) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          *reinterpret_cast<uint4*>(sm.dST[g] + off) = make_uint4(dk[4 * q], dk[4 * q + 1], dk[4 * q + 2], dk[4 * q + 3]);
+        for (int q = 0; q < 2; ++q) {
+          const uint32_t off = sw128(r, cbase + sc * 16 + q * 8);
+          *reinterpret_cast<uint4*>(pt + off) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          *reinterpret_cast<uint4*>(dst + off) = make_uint4(dk[4 * q], dk[4 * q + 1], dk[4 * q + 2], dk[4 * q + 3]);
         }
       }
       fence_proxy_async();
       tc_fence_before();
       mbar_arrive(&sm.bar_ew);
       if (last_of_kt) {
-        // dV_kt, dK_kt complete: group g stores dims [32g, 32g+32)
+        // dV_kt, dK_kt complete: group g stores dims [16g, 16g + 16).  The TMEM
+        // columns are released (bar_epi) as soon as they are in registers.
         mbar_wait(&sm.bar_mb, it & 1, abort_flag);
         tc_fence_after();
-        uint32_t vv[32], kv[32];
-        tmem_ld_x32_nowait(tmem + lane_off + 256 + g * 32, vv);
-        tmem_ld_x32_nowait(tmem + lane_off + 320 + g * 32, kv);
+        uint32_t vv[16], kv[16];
+        tmem_ld_x16_nowait(tmem + lane_off + 256 + g * 16, vv);
+        tmem_ld_x16_nowait(tmem + lane_off + 320 + g * 16, kv);
         tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&sm.bar_epi);
         if (jok) {
-          float dkf[32];
+          float dkf[16];
           #pragma unroll
-          for (int e = 0; e < 32; ++e) dkf[e] = __uint_as_float(kv[e]) * 0.125f;
+          for (int e = 0; e < 16; ++e) dkf[e] = __uint_as_float(kv[e]) * 0.125f;
           if (a.rope != nullptr) {
-            const float2* cs = reinterpret_cast<const float2*>(a.rope + ((long long)j * 32 + g * 16) * 2);
+            const float4* cs = reinterpret_cast<const float4*>(a.rope + ((long long)j * 32 + g * 8) * 2);
             #pragma unroll
-            for (int p = 0; p < 16; ++p) {
-              const float2 t = cs[p];
-              const float x0 = dkf[2 * p], x1 = dkf[2 * p + 1];
-              dkf[2 * p] = x0 * t.x + x1 * t.y;
-              dkf[2 * p + 1] = x1 * t.x - x0 * t.y;
+            for (int p = 0; p < 4; ++p) {
+              const float4 t = cs[p];  // (cos, sin) of two consecutive pairs
+              float x0 = dkf[4 * p], x1 = dkf[4 * p + 1];
+              dkf[4 * p] = x0 * t.x + x1 * t.y;
+              dkf[4 * p + 1] = x1 * t.x - x0 * t.y;
+              x0 = dkf[4 * p + 2];
+              x1 = dkf[4 * p + 3];
+              dkf[4 * p + 2] = x0 * t.z + x1 * t.w;
+              dkf[4 * p + 3] = x1 * t.z - x0 * t.w;
             }
           }
           __nv_bfloat16* rowp = a.dqkv + (long long)(row_base + j) * ld;
-          uint4* dkp = reinterpret_cast<uint4*>(rowp + E + h * kHd + g * 32);
-          uint4* dvp = reinterpret_cast<uint4*>(rowp + 2 * E + h * kHd + g * 32);
+          uint4* dkp = reinterpret_cast<uint4*>(rowp + E + h * kHd + g * 16);
+          uint4* dvp = reinterpret_cast<uint4*>(rowp + 2 * E + h * kHd + g * 16);
           #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < 2; ++q) {
             dkp[q] = make_uint4(pack_bf16(dkf[8 * q], dkf[8 * q + 1]), pack_bf16(dkf[8 * q + 2], dkf[8 * q + 3]),
                                 pack_bf16(dkf[8 * q + 4], dkf[8 * q + 5]), pack_bf16(dkf[8 * q + 6], dkf[8 * q + 7]));
             dvp[q] = make_uint4(pack_bf16(__uint_as_float(vv[8 * q]), __uint_as_float(vv[8 * q + 1])),
@@ -577,35 +616,43 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                 pack_bf16(__uint_as_float(vv[8 * q + 6]), __uint_as_float(vv[8 * q + 7])));
           }
         }
-        tc_fence_before();
-        mbar_arrive(&sm.bar_epi);
       }
     }
-    // dQ for both query halves (lane = query row within the half)
+    // dQ for both query halves (lane = query row within the half); group g
+    // stores dims [16g, 16g + 16)
     mbar_wait(&sm.bar_mb, (nit - 1) & 1, abort_flag);
     tc_fence_after();
     for (int qh = 0; qh < n_kt; ++qh) {
-      uint32_t qv[32];
-      tmem_ld_x32_nowait(tmem + lane_off + 384 + qh * kHd + g * 32, qv);
-      tmem_wait_ld();
       const int i = qh * 128 + r;
-      if (i < S) {
-        float dqf[32];
+      float4 cs[4];
+      if (a.rope != nullptr && i < S) {
+        const float4* rp = reinterpret_cast<const float4*>(a.rope + ((long long)i * 32 + g * 8) * 2);
         #pragma unroll
-        for (int e = 0; e < 32; ++e) dqf[e] = __uint_as_float(qv[e]) * 0.125f;
+        for (int p = 0; p < 4; ++p) cs[p] = rp[p];
+      }
+      uint32_t qv[16];
+      tmem_ld_x16_nowait(tmem + lane_off + 384 + qh * kHd + g * 16, qv);
+      tmem_wait_ld();
+      if (i < S) {
+        float dqf[16];
+        #pragma unroll
+        for (int e = 0; e < 16; ++e) dqf[e] = __uint_as_float(qv[e]) * 0.125f;
         if (a.rope != nullptr) {
-          const float2* cs = reinterpret_cast<const float2*>(a.rope + ((long long)i * 32 + g * 16) * 2);
           #pragma unroll
-          for (int p = 0; p < 16; ++p) {
-            const float2 t = cs[p];
-            const float x0 = dqf[2 * p], x1 = dqf[2 * p + 1];
-            dqf[2 * p] = x0 * t.x + x1 * t.y;
-            dqf[2 * p + 1] = x1 * t.x - x0 * t.y;
+          for (int p = 0; p < 4; ++p) {
+            const float4 t = cs[p];
+            float x0 = dqf[4 * p], x1 = dqf[4 * p + 1];
+            dqf[4 * p] = x0 * t.x + x1 * t.y;
+            dqf[4 * p + 1] = x1 * t.x - x0 * t.y;
+            x0 = dqf[4 * p + 2];
+            x1 = dqf[4 * p + 3];
+            dqf[4 * p + 2] = x0 * t.z + x1 * t.w;
+            dqf[4 * p + 3] = x1 * t.z - x0 * t.w;
           }
         }
-        uint4* dqp = reinterpret_cast<uint4*>(a.dqkv + (long long)(row_base + i) * ld + h * kHd + g * 32);
+        uint4* dqp = reinterpret_cast<uint4*>(a.dqkv + (long long)(row_base + i) * ld + h * kHd + g * 16);
         #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int q = 0; q < 2; ++q)
           dqp[q] = make_uint4(pack_bf16(dqf[8 * q], dqf[8 * q + 1]), pack_bf16(dqf[8 * q + 2], dqf[8 * q + 3]),
                               pack_bf16(dqf[8 * q + 4], dqf[8 * q + 5]), pack_bf16(dqf[8 * q + 6], dqf[8 * q + 7]));
       }
@@ -631,6 +678,8 @@ int launch_attn_bwd_tc(const void* qkv, const void* out, const void* dout, const
   CUtensorMap tq, tdo;
   if (!make_tmap(&tq, qkv, 3 * H * kHd, nseq * S, 3 * H * kHd, 64, 64)) return -21;
   if (!make_tmap(&tdo, dout, H * kHd, nseq * S, H * kHd, 64, 64)) return -21;
+  CUtensorMap tout;
+  if (!make_tmap(&tout, out, H * kHd, nseq * S, H * kHd, 64, 64)) return -21;
   BwdArgs a;
   a.out = reinterpret_cast<const __nv_bfloat16*>(out);
   a.dout = reinterpret_cast<const __nv_bfloat16*>(dout);
@@ -657,7 +706,7 @@ int launch_attn_bwd_tc(const void* qkv, const void* out, const void* dout, const
     if (per_sm * 512 > 512) return -22;
     attr_done[dev] = true;
   }
-  attn_bwd_tc_kernel<<<dim3((unsigned)H, (unsigned)nseq), kBwdThreads, smem, stream>>>(tq, tdo, a);
+  attn_bwd_tc_kernel<<<dim3((unsigned)H, (unsigned)nseq), kBwdThreads, smem, stream>>>(tq, tdo, tout, a);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
 }

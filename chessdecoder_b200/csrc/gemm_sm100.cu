@@ -1,14 +1,15 @@
 // Warp-specialised persistent bf16 GEMM for sm_100a: TMA -> shared-memory ring
 // -> tcgen05.mma (one elected thread) -> double-buffered TMEM accumulators ->
-// four epilogue warps with fused epilogues (RoPE, SwiGLU, residual add,
+// eight epilogue warps with fused epilogues (RoPE, SwiGLU, residual add,
 // split-K atomic accumulation).
 //
 // Replaces the nn.Linear forward/backward calls of the reference model
 // (chessdecoder/models/model.py:96-108, 119-136) that PyTorch dispatches to
-// cuBLAS.  Roles inside one CTA (192 threads, one CTA per SM):
+// cuBLAS.  Roles inside one CTA (320 threads, one CTA per SM):
 //   warp 0      TMA producer (lane 0)
 //   warp 1      TMEM allocator + MMA issuer (lane 0)
-//   warps 2..5  epilogue; warp w owns TMEM lanes 32*(w%4) .. +31
+//   warps 2..9  epilogue; warp w owns TMEM lanes 32*(w%4) .. +31, warps w and
+//               w+4 split the columns of those rows
 #include "../../include/cdk.h"
 #include "cdk_common.cuh"
 
@@ -18,7 +19,7 @@ namespace cdk {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = 128 B = one swizzle row
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 
 template <int BN>
 struct GemmCfg {
@@ -58,12 +59,14 @@ struct GemmParams {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
 
-// ---- epilogue store helpers (one thread = one row, 32 consecutive columns) --
-__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float (&v)[32], int ncols) {
-  if (ncols >= 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+// ---- epilogue store helpers (one thread = one row, kC consecutive columns) --
+constexpr int kC = 16;  // columns per epilogue chunk (one tcgen05.ld.32x32b.x16)
+
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float (&v)[kC], int ncols) {
+  if (ncols >= kC && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
     uint4* d4 = reinterpret_cast<uint4*>(dst);
     #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < kC / 8; ++q) {
       uint4 w;
       w.x = pack_bf16(v[8 * q + 0], v[8 * q + 1]);
       w.y = pack_bf16(v[8 * q + 2], v[8 * q + 3]);
@@ -73,41 +76,41 @@ __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float (
     }
   } else {
     #pragma unroll
-    for (int i = 0; i < 32; ++i)
+    for (int i = 0; i < kC; ++i)
       if (i < ncols) dst[i] = __float2bfloat16_rn(v[i]);
   }
 }
 
-__device__ __forceinline__ void store_row_f32(float* dst, const float (&v)[32], int ncols) {
-  if (ncols >= 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+__device__ __forceinline__ void store_row_f32(float* dst, const float (&v)[kC], int ncols) {
+  if (ncols >= kC && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
     float4* d4 = reinterpret_cast<float4*>(dst);
     #pragma unroll
-    for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    for (int q = 0; q < kC / 4; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
   } else {
     #pragma unroll
-    for (int i = 0; i < 32; ++i)
+    for (int i = 0; i < kC; ++i)
       if (i < ncols) dst[i] = v[i];
   }
 }
 
-__device__ __forceinline__ void load_row_f32(const float* src, float (&v)[32], int ncols) {
-  if (ncols >= 32 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+__device__ __forceinline__ void load_row_f32(const float* src, float (&v)[kC], int ncols) {
+  if (ncols >= kC && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
     const float4* s4 = reinterpret_cast<const float4*>(src);
     #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 0; q < kC / 4; ++q) {
       float4 t = s4[q];
       v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
     }
   } else {
     #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = i < ncols ? src[i] : 0.f;
+    for (int i = 0; i < kC; ++i) v[i] = i < ncols ? src[i] : 0.f;
   }
 }
 
-__device__ __forceinline__ void load_row_bf16(const __nv_bfloat16* src, float (&v)[32]) {
+__device__ __forceinline__ void load_row_bf16(const __nv_bfloat16* src, float (&v)[kC]) {
   const uint4* s4 = reinterpret_cast<const uint4*>(src);
   #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < kC / 8; ++q) {
     uint4 w = s4[q];
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
     #pragma unroll
@@ -119,41 +122,52 @@ __device__ __forceinline__ void load_row_bf16(const __nv_bfloat16* src, float (&
   }
 }
 
-__device__ __forceinline__ void atomic_row_f32(float* dst, const float (&v)[32], int ncols) {
-  if (ncols >= 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+__device__ __forceinline__ void atomic_row_f32(float* dst, const float (&v)[kC], int ncols) {
+  if (ncols >= kC && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
     float4* d4 = reinterpret_cast<float4*>(dst);
     #pragma unroll
-    for (int q = 0; q < 8; ++q) atomicAdd(d4 + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+    for (int q = 0; q < kC / 4; ++q) atomicAdd(d4 + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
   } else {
     #pragma unroll
-    for (int i = 0; i < 32; ++i)
+    for (int i = 0; i < kC; ++i)
       if (i < ncols) atomicAdd(dst + i, v[i]);
   }
 }
 
-// ---- epilogue tile routines (one thread = one accumulator row) --------------
+__device__ __forceinline__ void tmem_ld_f16cols(uint32_t taddr, float (&v)[kC]) {
+  uint32_t u[kC];
+  tmem_ld_x16_nowait(taddr, u);
+  tmem_wait_ld();
+  #pragma unroll
+  for (int i = 0; i < kC; ++i) v[i] = __uint_as_float(u[i]);
+}
+
+// ---- epilogue tile routines ---------------------------------------------------
+// One thread = one accumulator row; the two epilogue warps of a TMEM lane
+// quadrant split each 32-column block: half h takes columns [32c + 16h, +16).
 // Global operands of a chunk (residual, gate/up, RoPE table) are requested
 // before the chunk's TMEM load so that their latency overlaps it.
 template <int BN>
 __device__ __forceinline__ void epi_swiglu(const EpiDev& e, const GemmParams& p, uint32_t tbase, int row,
-                                           bool row_ok, int n0) {
+                                           bool row_ok, int n0, int half) {
   // TMEM columns [0, BN/2) = gate, [BN/2, BN) = up, for output columns n0 ...
   __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(e.out2) + (long long)row * e.ldo2;
   __nv_bfloat16* uo = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo;
   #pragma unroll 1
   for (int c = 0; c < BN / 64; ++c) {
-    const int col = n0 + c * 32;
+    const int tc = c * 32 + half * kC;
+    const int col = n0 + tc;
     if (col >= p.N) break;
-    float g[32], up[32];
-    tmem_ld_32x32b_x32(tbase + c * 32, g);
-    tmem_ld_32x32b_x32(tbase + BN / 2 + c * 32, up);
+    float g[kC], up[kC];
+    tmem_ld_f16cols(tbase + tc, g);
+    tmem_ld_f16cols(tbase + BN / 2 + tc, up);
     if (row_ok) {
-      const int nc = min(32, p.N - col);
+      const int nc = min(kC, p.N - col);
       store_row_bf16(gu + col, g, nc);
       store_row_bf16(gu + e.half_n + col, up, nc);
-      float h[32];
+      float h[kC];
       #pragma unroll
-      for (int i = 0; i < 32; ++i) h[i] = silu_f(g[i]) * up[i];
+      for (int i = 0; i < kC; ++i) h[i] = silu_f(g[i]) * up[i];
       store_row_bf16(uo + col, h, nc);
     }
   }
@@ -161,17 +175,18 @@ __device__ __forceinline__ void epi_swiglu(const EpiDev& e, const GemmParams& p,
 
 template <int BN, int KIND>
 __device__ __forceinline__ void epi_tile(const EpiDev& e, const GemmParams& p, uint32_t tbase, int row, bool row_ok,
-                                         int n0) {
+                                         int n0, int half) {
   const long long orow = (long long)row * e.ldo;
   const int pos = KIND == CDK_EPI_ROPE_BF16 ? row % e.seq_len : 0;
   #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
-    const int col = n0 + c * 32;
+    const int tc = c * 32 + half * kC;
+    const int col = n0 + tc;
     if (col >= p.N) break;
-    const int nc = min(32, p.N - col);
+    const int nc = min(kC, p.N - col);
     // prefetch this chunk's global operand
-    float r[32];
-    float a2[32];
+    float r[kC];
+    float a2[kC];
     if (row_ok) {
       if constexpr (KIND == CDK_EPI_RESID_F32) load_row_f32(e.resid + (long long)row * e.ldr + col, r, nc);
       if constexpr (KIND == CDK_EPI_ACCUM_F32) load_row_f32(reinterpret_cast<float*>(e.out) + orow + col, r, nc);
@@ -184,19 +199,19 @@ __device__ __forceinline__ void epi_tile(const EpiDev& e, const GemmParams& p, u
         if (col < e.rope_cols) {
           const float4* cs = reinterpret_cast<const float4*>(e.rope + ((long long)pos * 32 + ((col & 63) >> 1)) * 2);
           #pragma unroll
-          for (int q = 0; q < 8; ++q) {
+          for (int q = 0; q < kC / 4; ++q) {
             const float4 t = __ldg(cs + q);
             r[4 * q] = t.x; r[4 * q + 1] = t.y; r[4 * q + 2] = t.z; r[4 * q + 3] = t.w;
           }
         }
       }
     }
-    float v[32];
-    tmem_ld_32x32b_x32(tbase + c * 32, v);
+    float v[kC];
+    tmem_ld_f16cols(tbase + tc, v);
     if (!row_ok) continue;
     if (e.bias != nullptr) {
       #pragma unroll
-      for (int i = 0; i < 32; ++i)
+      for (int i = 0; i < kC; ++i)
         if (i < nc) v[i] += __ldg(e.bias + col + i);
     }
     if constexpr (KIND == CDK_EPI_STORE_BF16) {
@@ -205,14 +220,14 @@ __device__ __forceinline__ void epi_tile(const EpiDev& e, const GemmParams& p, u
       store_row_f32(reinterpret_cast<float*>(e.out) + orow + col, v, nc);
     } else if constexpr (KIND == CDK_EPI_RESID_F32 || KIND == CDK_EPI_ACCUM_F32) {
       #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] += r[i];
+      for (int i = 0; i < kC; ++i) v[i] += r[i];
       store_row_f32(reinterpret_cast<float*>(e.out) + orow + col, v, nc);
     } else if constexpr (KIND == CDK_EPI_ATOMIC_F32) {
       atomic_row_f32(reinterpret_cast<float*>(e.out) + orow + col, v, nc);
     } else if constexpr (KIND == CDK_EPI_ROPE_BF16) {
       if (col < e.rope_cols) {
         #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < kC / 2; ++i) {
           const float c0 = r[2 * i], s0 = r[2 * i + 1];
           const float x0 = v[2 * i], x1 = v[2 * i + 1];
           v[2 * i] = x0 * c0 - x1 * s0;
@@ -221,9 +236,9 @@ __device__ __forceinline__ void epi_tile(const EpiDev& e, const GemmParams& p, u
       }
       store_row_bf16(reinterpret_cast<__nv_bfloat16*>(e.out) + orow + col, v, nc);
     } else if constexpr (KIND == CDK_EPI_DSWIGLU) {
-      float dg[32], du[32];
+      float dg[kC], du[kC];
       #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < kC; ++i) {
         const float g = r[i], up = a2[i];
         const float sg = 1.f / (1.f + __expf(-g));
         du[i] = v[i] * g * sg;
@@ -263,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 256);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -367,6 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue warps ----------------
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const EpiDev& e = p.epi;
     int local = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
@@ -382,14 +398,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
 
       switch (e.kind) {
-        case CDK_EPI_SWIGLU: epi_swiglu<BN>(e, p, tbase, row, row_ok, nt * (BN / 2)); break;
-        case CDK_EPI_STORE_BF16: epi_tile<BN, CDK_EPI_STORE_BF16>(e, p, tbase, row, row_ok, nt * BN); break;
-        case CDK_EPI_STORE_F32: epi_tile<BN, CDK_EPI_STORE_F32>(e, p, tbase, row, row_ok, nt * BN); break;
-        case CDK_EPI_RESID_F32: epi_tile<BN, CDK_EPI_RESID_F32>(e, p, tbase, row, row_ok, nt * BN); break;
-        case CDK_EPI_ACCUM_F32: epi_tile<BN, CDK_EPI_ACCUM_F32>(e, p, tbase, row, row_ok, nt * BN); break;
-        case CDK_EPI_ATOMIC_F32: epi_tile<BN, CDK_EPI_ATOMIC_F32>(e, p, tbase, row, row_ok, nt * BN); break;
-        case CDK_EPI_ROPE_BF16: epi_tile<BN, CDK_EPI_ROPE_BF16>(e, p, tbase, row, row_ok, nt * BN); break;
-        case CDK_EPI_DSWIGLU: epi_tile<BN, CDK_EPI_DSWIGLU>(e, p, tbase, row, row_ok, nt * BN); break;
+        case CDK_EPI_SWIGLU: epi_swiglu<BN>(e, p, tbase, row, row_ok, nt * (BN / 2), half); break;
+        case CDK_EPI_STORE_BF16: epi_tile<BN, CDK_EPI_STORE_BF16>(e, p, tbase, row, row_ok, nt * BN, half); break;
+        case CDK_EPI_STORE_F32: epi_tile<BN, CDK_EPI_STORE_F32>(e, p, tbase, row, row_ok, nt * BN, half); break;
+        case CDK_EPI_RESID_F32: epi_tile<BN, CDK_EPI_RESID_F32>(e, p, tbase, row, row_ok, nt * BN, half); break;
+        case CDK_EPI_ACCUM_F32: epi_tile<BN, CDK_EPI_ACCUM_F32>(e, p, tbase, row, row_ok, nt * BN, half); break;
+        case CDK_EPI_ATOMIC_F32: epi_tile<BN, CDK_EPI_ATOMIC_F32>(e, p, tbase, row, row_ok, nt * BN, half); break;
+        case CDK_EPI_ROPE_BF16: epi_tile<BN, CDK_EPI_ROPE_BF16>(e, p, tbase, row, row_ok, nt * BN, half); break;
+        case CDK_EPI_DSWIGLU: epi_tile<BN, CDK_EPI_DSWIGLU>(e, p, tbase, row, row_ok, nt * BN, half); break;
         default: break;
       }
       tc_fence_before();
