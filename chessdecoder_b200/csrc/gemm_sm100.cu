@@ -29,13 +29,15 @@ struct GemmCfg {
   static constexpr int kStages = BN == 256 ? 4 : 6;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
+  static constexpr int kStagingBytes = 8 * 2560;  // per epilogue warp: 32 rows x 80 B transpose buffer
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes + kStagingBytes;
 };
 
 struct EpiDev {
   int kind;
   int seq_len;
   int rope_cols;
+  int vec;  // 1: full 16-column chunks with 16-byte aligned rows -> warp-cooperative (coalesced) path
   void* out;
   long long ldo;
   const float* bias;
@@ -140,6 +142,185 @@ __device__ __forceinline__ void tmem_ld_f16cols(uint32_t taddr, float (&v)[kC]) 
   tmem_wait_ld();
   #pragma unroll
   for (int i = 0; i < kC; ++i) v[i] = __uint_as_float(u[i]);
+}
+
+// L2 prefetch of the global operand an epilogue tile will read (residual /
+// accumulator rows, or the gate|up rows of the SwiGLU backward): one prefetch
+// per 128-byte line of this thread's row segment, issued a tile ahead so that
+// the DRAM latency overlaps the mainloop instead of the epilogue.
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
+template <int BN>
+__device__ __forceinline__ void epi_prefetch(const EpiDev& e, const GemmParams& p, int row, int n0, int half) {
+  if (row >= p.M) return;
+  if (e.kind == CDK_EPI_RESID_F32 || e.kind == CDK_EPI_ACCUM_F32) {
+    const float* base = e.kind == CDK_EPI_RESID_F32 ? e.resid + (long long)row * e.ldr
+                                                    : reinterpret_cast<const float*>(e.out) + (long long)row * e.ldo;
+    #pragma unroll
+    for (int c = half; c < BN / 32; c += 2)
+      if (n0 + c * 32 < p.N) prefetch_l2(base + n0 + c * 32);
+  } else if (e.kind == CDK_EPI_DSWIGLU) {
+    const __nv_bfloat16* base = e.aux + (long long)row * e.ldaux;
+    #pragma unroll
+    for (int c = half; c < BN / 64; c += 2)
+      if (n0 + c * 64 < p.N) {
+        prefetch_l2(base + n0 + c * 64);
+        prefetch_l2(base + e.half_n + n0 + c * 64);
+      }
+  }
+}
+
+// ---- warp-cooperative row transfers ------------------------------------------
+// A warp's 32 epilogue rows (lane = row) x 16 columns go through a per-warp
+// shared-memory buffer so that global accesses are row-contiguous: a store
+// instruction writes 8 rows x 64 B (fp32) or 16 rows x 32 B (bf16) instead of
+// 32 scattered 16-byte pieces.  Row strides of 20 / 12 words make both the
+// row-wise and the transposed 16-byte accesses conflict-free.
+constexpr int kStgF32 = 20;
+constexpr int kStgB16 = 12;
+constexpr int kStgWords = 32 * kStgF32;
+
+__device__ __forceinline__ void warp_store_f32(uint32_t* stg, const float (&v)[kC], float* g, long long ld,
+                                               int nvalid, int lane) {
+  float4* my = reinterpret_cast<float4*>(stg + lane * kStgF32);
+  #pragma unroll
+  for (int q = 0; q < 4; ++q) my[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  __syncwarp();
+  const int c = lane & 3;
+  #pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = k * 8 + (lane >> 2);
+    const float4 t = *reinterpret_cast<const float4*>(stg + r * kStgF32 + c * 4);
+    if (r < nvalid) *reinterpret_cast<float4*>(g + (long long)r * ld + c * 4) = t;
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ void warp_store_bf16(uint32_t* stg, const float (&v)[kC], __nv_bfloat16* g, long long ld,
+                                                int nvalid, int lane) {
+  uint4* my = reinterpret_cast<uint4*>(stg + lane * kStgB16);
+  my[0] = make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+  my[1] = make_uint4(pack_bf16(v[8], v[9]), pack_bf16(v[10], v[11]), pack_bf16(v[12], v[13]),
+                     pack_bf16(v[14], v[15]));
+  __syncwarp();
+  const int c = lane & 1;
+  #pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int r = k * 16 + (lane >> 1);
+    const uint4 t = *reinterpret_cast<const uint4*>(stg + r * kStgB16 + c * 4);
+    if (r < nvalid) *reinterpret_cast<uint4*>(g + (long long)r * ld + c * 8) = t;
+  }
+  __syncwarp();
+}
+
+// Row-contiguous fp32 loads of 32 rows x 16 columns: issue() starts them,
+// finish() transposes through shared memory so that lane = row again.
+__device__ __forceinline__ void warp_load_f32_issue(float4 (&t)[4], const float* g, long long ld, int nvalid,
+                                                    int lane) {
+  const int c = lane & 3;
+  #pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = k * 8 + (lane >> 2);
+    t[k] = r < nvalid ? __ldg(reinterpret_cast<const float4*>(g + (long long)r * ld + c * 4))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+__device__ __forceinline__ void warp_load_f32_finish(uint32_t* stg, const float4 (&t)[4], float (&v)[kC], int lane) {
+  const int c = lane & 3;
+  #pragma unroll
+  for (int k = 0; k < 4; ++k) *reinterpret_cast<float4*>(stg + (k * 8 + (lane >> 2)) * kStgF32 + c * 4) = t[k];
+  __syncwarp();
+  const float4* my = reinterpret_cast<const float4*>(stg + lane * kStgF32);
+  #pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 x = my[q];
+    v[4 * q] = x.x; v[4 * q + 1] = x.y; v[4 * q + 2] = x.z; v[4 * q + 3] = x.w;
+  }
+  __syncwarp();
+}
+
+// Coalesced variants of the forward epilogues (row0 = the warp's first row).
+template <int BN>
+__device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, uint32_t tbase, int row0, int n0,
+                                        int half, uint32_t* stg, int lane) {
+  const int nvalid = min(32, p.M - row0);
+  const int row = row0 + lane;
+  if (e.kind == CDK_EPI_SWIGLU) {
+    __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(e.out2) + (long long)row0 * e.ldo2;
+    __nv_bfloat16* uo = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row0 * e.ldo;
+    #pragma unroll 1
+    for (int c = 0; c < BN / 64; ++c) {
+      const int tc = c * 32 + half * kC;
+      const int col = n0 + tc;
+      if (col >= p.N) break;
+      float g[kC], up[kC], h[kC];
+      tmem_ld_f16cols(tbase + tc, g);
+      tmem_ld_f16cols(tbase + BN / 2 + tc, up);
+      #pragma unroll
+      for (int i = 0; i < kC; ++i) h[i] = silu_f(g[i]) * up[i];
+      warp_store_bf16(stg, g, gu + col, e.ldo2, nvalid, lane);
+      warp_store_bf16(stg, up, gu + e.half_n + col, e.ldo2, nvalid, lane);
+      warp_store_bf16(stg, h, uo + col, e.ldo, nvalid, lane);
+    }
+    return;
+  }
+  if (e.kind == CDK_EPI_RESID_F32) {
+    const float* rbase = e.resid + (long long)row0 * e.ldr;
+    float* obase = reinterpret_cast<float*>(e.out) + (long long)row0 * e.ldo;
+    float4 pre[4];
+    warp_load_f32_issue(pre, rbase + n0 + half * kC, e.ldr, nvalid, lane);
+    #pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int tc = c * 32 + half * kC;
+      const int col = n0 + tc;
+      if (col >= p.N) break;
+      float r[kC], v[kC];
+      warp_load_f32_finish(stg, pre, r, lane);
+      if (c + 1 < BN / 32 && col + 32 < p.N) warp_load_f32_issue(pre, rbase + col + 32, e.ldr, nvalid, lane);
+      tmem_ld_f16cols(tbase + tc, v);
+      #pragma unroll
+      for (int i = 0; i < kC; ++i) v[i] += r[i] + (e.bias != nullptr ? __ldg(e.bias + col + i) : 0.f);
+      warp_store_f32(stg, v, obase + col, e.ldo, nvalid, lane);
+    }
+    return;
+  }
+  // CDK_EPI_STORE_BF16 / CDK_EPI_ROPE_BF16
+  __nv_bfloat16* obase = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row0 * e.ldo;
+  const int pos = row % max(e.seq_len, 1);
+  #pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    const int tc = c * 32 + half * kC;
+    const int col = n0 + tc;
+    if (col >= p.N) break;
+    float r[kC];
+    const bool rope = e.kind == CDK_EPI_ROPE_BF16 && col < e.rope_cols;
+    if (rope && lane < nvalid) {
+      const float4* cs = reinterpret_cast<const float4*>(e.rope + ((long long)pos * 32 + ((col & 63) >> 1)) * 2);
+      #pragma unroll
+      for (int q = 0; q < kC / 4; ++q) {
+        const float4 t = __ldg(cs + q);
+        r[4 * q] = t.x; r[4 * q + 1] = t.y; r[4 * q + 2] = t.z; r[4 * q + 3] = t.w;
+      }
+    }
+    float v[kC];
+    tmem_ld_f16cols(tbase + tc, v);
+    if (e.bias != nullptr) {
+      #pragma unroll
+      for (int i = 0; i < kC; ++i) v[i] += __ldg(e.bias + col + i);
+    }
+    if (rope && lane < nvalid) {
+      #pragma unroll
+      for (int i = 0; i < kC / 2; ++i) {
+        const float c0 = r[2 * i], s0 = r[2 * i + 1];
+        const float x0 = v[2 * i], x1 = v[2 * i + 1];
+        v[2 * i] = x0 * c0 - x1 * s0;
+        v[2 * i + 1] = x1 * c0 + x0 * s0;
+      }
+    }
+    warp_store_bf16(stg, v, obase + col, e.ldo, nvalid, lane);
+  }
 }
 
 // ---- epilogue tile routines ---------------------------------------------------
@@ -251,7 +432,7 @@ __device__ __forceinline__ void epi_tile(const EpiDev& e, const GemmParams& p, u
   }
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, bool VEC>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                      const GemmParams p) {
@@ -384,6 +565,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const EpiDev& e = p.epi;
+    uint32_t* stg = reinterpret_cast<uint32_t*>(smem + kStages * Cfg::kStageBytes + Cfg::kBarrierBytes) +
+                    (warp - 2) * kStgWords;
     int local = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
       const int rem = u % tiles_mn;
@@ -391,13 +574,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nt = rem - mt * p.n_tiles;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      if (e.kind == CDK_EPI_RESID_F32 || e.kind == CDK_EPI_ACCUM_F32 || e.kind == CDK_EPI_DSWIGLU) {
+        if (local == 0) epi_prefetch<BN>(e, p, mt * kBM + quad * 32 + lane, nt * BN, half);
+        const int un = u + gridDim.x;
+        if (un < units) {
+          const int rn = un % tiles_mn;
+          const int mtn = rn / p.n_tiles;
+          epi_prefetch<BN>(e, p, mtn * kBM + quad * 32 + lane, (rn - mtn * p.n_tiles) * BN, half);
+        }
+      }
       mbar_wait(&tfull[acc], acc_phase, abort_flag);
       tc_fence_after();
       const int row = mt * kBM + quad * 32 + lane;
       const bool row_ok = row < p.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
 
-      switch (e.kind) {
+      if constexpr (VEC) {
+        const int row0 = mt * kBM + quad * 32;
+        if (row0 < p.M)
+          epi_vec<BN>(e, p, tbase, row0, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN, half, stg, lane);
+      } else switch (e.kind) {
         case CDK_EPI_SWIGLU: epi_swiglu<BN>(e, p, tbase, row, row_ok, nt * (BN / 2), half); break;
         case CDK_EPI_STORE_BF16: epi_tile<BN, CDK_EPI_STORE_BF16>(e, p, tbase, row, row_ok, nt * BN, half); break;
         case CDK_EPI_STORE_F32: epi_tile<BN, CDK_EPI_STORE_F32>(e, p, tbase, row, row_ok, nt * BN, half); break;
@@ -468,14 +664,14 @@ static int num_sms(int dev) {
   return cache[dev];
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, bool VEC>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
                        cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  auto kfn = gemm_bf16_kernel<BN, A_MN, B_MN>;
+  auto kfn = gemm_bf16_kernel<BN, A_MN, B_MN, VEC>;
   if (dev < 64 && !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return (int)e;
@@ -494,10 +690,13 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
 template <int BN>
 static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
                           int grid, cudaStream_t s) {
-  if (!a_mn && !b_mn) return launch_gemm<BN, false, false>(ta, tb, p, grid, s);
-  if (!a_mn && b_mn) return launch_gemm<BN, false, true>(ta, tb, p, grid, s);
-  if (a_mn && !b_mn) return launch_gemm<BN, true, false>(ta, tb, p, grid, s);
-  return launch_gemm<BN, true, true>(ta, tb, p, grid, s);
+  // the coalesced epilogues (forward kinds and bf16 stores) have their own instantiations
+  if (p.epi.vec && !a_mn && !b_mn) return launch_gemm<BN, false, false, true>(ta, tb, p, grid, s);
+  if (p.epi.vec && !a_mn && b_mn) return launch_gemm<BN, false, true, true>(ta, tb, p, grid, s);
+  if (!a_mn && !b_mn) return launch_gemm<BN, false, false, false>(ta, tb, p, grid, s);
+  if (!a_mn && b_mn) return launch_gemm<BN, false, true, false>(ta, tb, p, grid, s);
+  if (a_mn && !b_mn) return launch_gemm<BN, true, false, false>(ta, tb, p, grid, s);
+  return launch_gemm<BN, true, true, false>(ta, tb, p, grid, s);
 }
 
 static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -601,6 +800,16 @@ extern "C" int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b
   p.epi.ldaux = epi->ldaux;
   p.epi.half_n = epi->half_n;
   p.epi.rope = epi->rope;
+  {
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    bool v = N % 16 == 0 && al16(epi->out);
+    if (kind == CDK_EPI_RESID_F32) v = v && epi->ldo % 4 == 0 && epi->ldr % 4 == 0 && al16(epi->resid);
+    else if (kind == CDK_EPI_STORE_BF16 || kind == CDK_EPI_ROPE_BF16) v = v && epi->ldo % 8 == 0;
+    else if (kind == CDK_EPI_SWIGLU) v = v && epi->ldo % 8 == 0 && epi->ldo2 % 8 == 0 && epi->half_n % 8 == 0 && al16(epi->out2);
+    else v = false;
+    if (kind == CDK_EPI_ROPE_BF16) v = v && epi->seq_len > 0;
+    p.epi.vec = v && !a_mn ? 1 : 0;
+  }
 
   const long long units = m_tiles * n_tiles * splits;
   const int grid = (int)(units < sms ? units : sms);
