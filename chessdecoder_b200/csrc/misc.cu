@@ -85,28 +85,33 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ du, long lon
 // C[M,N] = beta*C + sum_k A(m,k) B(n,k) + bias[n]
 //   A(m,k) = a_t ? A[k*lda + m] : A[m*lda + k];  B(n,k) = b_t ? B[k*ldb + n] : B[n*ldb + k]
 // 64x64 tile, 16-deep k slices, 256 threads with a 4x4 micro-tile each.
+// Split-K over blockIdx.z (k_per columns of K each): with more than one split
+// the partial sums are atomically added (C zeroed beforehand unless
+// accumulating) and split 0 adds the bias.
 __global__ void __launch_bounds__(256) sgemm_kernel(const float* __restrict__ A, long long lda, int a_t,
                                                     const float* __restrict__ B, long long ldb, int b_t,
                                                     float* __restrict__ C, long long ldc, int M, int N, int K,
-                                                    const float* __restrict__ bias, int accumulate) {
+                                                    const float* __restrict__ bias, int accumulate, int k_per) {
   __shared__ float sA[16][64 + 4];
   __shared__ float sB[16][64 + 4];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  const int kb = blockIdx.z * k_per, ke = min(K, kb + k_per);
+  const bool split = gridDim.z > 1;
   float acc[4][4] = {};
-  for (int k0 = 0; k0 < K; k0 += 16) {
+  for (int k0 = kb; k0 < ke; k0 += 16) {
     for (int i = threadIdx.x; i < 16 * 64; i += 256) {
       int kk, mm;
       if (a_t) { kk = i / 64; mm = i % 64; } else { mm = i / 16; kk = i % 16; }
       const int gm = m0 + mm, gk = k0 + kk;
       float va = 0.f;
-      if (gm < M && gk < K) va = a_t ? A[(long long)gk * lda + gm] : A[(long long)gm * lda + gk];
+      if (gm < M && gk < ke) va = a_t ? A[(long long)gk * lda + gm] : A[(long long)gm * lda + gk];
       sA[kk][mm] = va;
       int nn;
       if (b_t) { kk = i / 64; nn = i % 64; } else { nn = i / 16; kk = i % 16; }
       const int gn = n0 + nn, gk2 = k0 + kk;
       float vb = 0.f;
-      if (gn < N && gk2 < K) vb = b_t ? B[(long long)gk2 * ldb + gn] : B[(long long)gn * ldb + gk2];
+      if (gn < N && gk2 < ke) vb = b_t ? B[(long long)gk2 * ldb + gn] : B[(long long)gn * ldb + gk2];
       sB[kk][nn] = vb;
     }
     __syncthreads();
@@ -132,9 +137,10 @@ __global__ void __launch_bounds__(256) sgemm_kernel(const float* __restrict__ A,
     for (int j = 0; j < 4; ++j) {
       const int gn = n0 + tx * 4 + j;
       if (gn >= N) continue;
-      float v = acc[i][j] + (bias ? bias[gn] : 0.f);
+      float v = acc[i][j] + (bias && blockIdx.z == 0 ? bias[gn] : 0.f);
       float* c = C + (long long)gm * ldc + gn;
-      *c = accumulate ? *c + v : v;
+      if (split) atomicAdd(c, v);
+      else *c = accumulate ? *c + v : v;
     }
   }
 }
@@ -232,8 +238,19 @@ extern "C" int cdk_gemm_f32(const float* a, int64_t lda, int a_t, const float* b
   if (M == 0 || N == 0) return 0;
   if (!a || !b || !c || M < 0 || N < 0 || K < 0) return -1;
   if (M > (1 << 24) || N > (1 << 24)) return -2;
-  dim3 grid((unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64));
-  sgemm_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a, lda, a_t, b, ldb, b_t, c, ldc, (int)M,
-                                                                         (int)N, (int)K, bias, accumulate);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const long long tiles = ((N + 63) / 64) * ((M + 63) / 64);
+  // split K until about two blocks per SM, keeping >= 64 of K per split
+  long long splits = 1;
+  while (tiles * splits * 2 <= 2 * 148 && K / (splits * 2) >= 64) splits *= 2;
+  const int k_per = (int)(((K + splits - 1) / splits + 15) / 16 * 16);
+  splits = K > 0 ? (K + k_per - 1) / k_per : 1;
+  if (splits > 1 && !accumulate) {
+    cudaError_t e = cudaMemset2DAsync(c, (size_t)ldc * sizeof(float), 0, (size_t)N * sizeof(float), (size_t)M, st);
+    if (e != cudaSuccess) return (int)e;
+  }
+  dim3 grid((unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64), (unsigned)splits);
+  sgemm_kernel<<<grid, 256, 0, st>>>(a, lda, a_t, b, ldb, b_t, c, ldc, (int)M, (int)N, (int)K, bias, accumulate,
+                                     k_per > 0 ? k_per : 16);
   return finish();
 }
