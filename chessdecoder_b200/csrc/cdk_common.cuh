@@ -148,6 +148,19 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
       : "memory");
 }
 
+// 8-bit operands (kind::f8f6f4; A and B formats in the instruction
+// descriptor, which may differ: e4m3 x e5m2).  K = 32 per instruction, i.e.
+// the same 32 bytes of a 128-byte swizzle row as the bf16 form.
+__device__ __forceinline__ void umma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // 32 lanes x 32 columns of 32-bit: thread i of the warp receives lane (base+i),
 // columns [col, col+32).
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32]) {
@@ -209,6 +222,15 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool a_mn, 
          | (1u << 10)                    // B format BF16
          | ((a_mn ? 1u : 0u) << 15)      // A major
          | ((b_mn ? 1u : 0u) << 16)      // B major
+         | ((uint32_t)(N >> 3) << 17)    // N / 8
+         | ((uint32_t)(M >> 4) << 24);   // M / 16
+}
+
+// kind::f8f6f4 descriptor for K-major 8-bit operands; fmt 0 = e4m3, 1 = e5m2.
+__host__ __device__ constexpr uint32_t make_idesc_f8(int M, int N, int a_fmt, int b_fmt) {
+  return (1u << 4)                       // D format F32
+         | ((uint32_t)(a_fmt & 7) << 7)  // A format
+         | ((uint32_t)(b_fmt & 7) << 10) // B format
          | ((uint32_t)(N >> 3) << 17)    // N / 8
          | ((uint32_t)(M >> 4) << 24);   // M / 16
 }

@@ -18,7 +18,7 @@
 namespace cdk {
 
 constexpr int kBM = 128;
-constexpr int kBK = 64;  // 64 bf16 = 128 B = one swizzle row
+constexpr int kBK = 64;  // 64 bf16 = 128 B = one swizzle row (128 fp8 elements in the fp8 instantiations)
 constexpr int kThreads = 320;
 
 template <int BN>
@@ -56,6 +56,9 @@ struct GemmParams {
   int m_tiles, n_tiles, splits, k_tiles, k_per_split;
   int dual;      // SWIGLU: B tile = rows [n0, n0+BN/2) and [n0+b_off, ...)
   int b_off;
+  uint32_t idesc_f8;           // fp8 instantiations: kind::f8f6f4 descriptor (operand formats)
+  const float* scale_inv_a;    // fp8: dequantisation factors (device scalars), else null
+  const float* scale_inv_b;
   EpiDev epi;
 };
 
@@ -136,12 +139,14 @@ __device__ __forceinline__ void atomic_row_f32(float* dst, const float (&v)[kC],
   }
 }
 
-__device__ __forceinline__ void tmem_ld_f16cols(uint32_t taddr, float (&v)[kC]) {
+// 16 accumulator columns of this thread's row, times the dequantisation
+// factor `sc` (1 for bf16 operands; 1/(scale_a * scale_b) for fp8 operands).
+__device__ __forceinline__ void tmem_ld_f16cols(uint32_t taddr, float (&v)[kC], float sc) {
   uint32_t u[kC];
   tmem_ld_x16_nowait(taddr, u);
   tmem_wait_ld();
   #pragma unroll
-  for (int i = 0; i < kC; ++i) v[i] = __uint_as_float(u[i]);
+  for (int i = 0; i < kC; ++i) v[i] = __uint_as_float(u[i]) * sc;
 }
 
 // L2 prefetch of the global operand an epilogue tile will read (residual /
@@ -244,7 +249,7 @@ __device__ __forceinline__ void warp_load_f32_finish(uint32_t* stg, const float4
 // Coalesced variants of the forward epilogues (row0 = the warp's first row).
 template <int BN>
 __device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, uint32_t tbase, int row0, int n0,
-                                        int half, uint32_t* stg, int lane) {
+                                        int half, uint32_t* stg, int lane, float sc) {
   const int nvalid = min(32, p.M - row0);
   const int row = row0 + lane;
   if (e.kind == CDK_EPI_SWIGLU) {
@@ -256,8 +261,8 @@ __device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, ui
       const int col = n0 + tc;
       if (col >= p.N) break;
       float g[kC], up[kC], h[kC];
-      tmem_ld_f16cols(tbase + tc, g);
-      tmem_ld_f16cols(tbase + BN / 2 + tc, up);
+      tmem_ld_f16cols(tbase + tc, g, sc);
+      tmem_ld_f16cols(tbase + BN / 2 + tc, up, sc);
       #pragma unroll
       for (int i = 0; i < kC; ++i) h[i] = silu_f(g[i]) * up[i];
       warp_store_bf16(stg, g, gu + col, e.ldo2, nvalid, lane);
@@ -279,7 +284,7 @@ __device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, ui
       float r[kC], v[kC];
       warp_load_f32_finish(stg, pre, r, lane);
       if (c + 1 < BN / 32 && col + 32 < p.N) warp_load_f32_issue(pre, rbase + col + 32, e.ldr, nvalid, lane);
-      tmem_ld_f16cols(tbase + tc, v);
+      tmem_ld_f16cols(tbase + tc, v, sc);
       #pragma unroll
       for (int i = 0; i < kC; ++i) v[i] += r[i] + (e.bias != nullptr ? __ldg(e.bias + col + i) : 0.f);
       warp_store_f32(stg, v, obase + col, e.ldo, nvalid, lane);
@@ -305,7 +310,7 @@ __device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, ui
       }
     }
     float v[kC];
-    tmem_ld_f16cols(tbase + tc, v);
+    tmem_ld_f16cols(tbase + tc, v, sc);
     if (e.bias != nullptr) {
       #pragma unroll
       for (int i = 0; i < kC; ++i) v[i] += __ldg(e.bias + col + i);
@@ -330,7 +335,7 @@ __device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, ui
 // before the chunk's TMEM load so that their latency overlaps it.
 template <int BN>
 __device__ __forceinline__ void epi_swiglu(const EpiDev& e, const GemmParams& p, uint32_t tbase, int row,
-                                           bool row_ok, int n0, int half) {
+                                           bool row_ok, int n0, int half, float sc) {
   // TMEM columns [0, BN/2) = gate, [BN/2, BN) = up, for output columns n0 ...
   __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(e.out2) + (long long)row * e.ldo2;
   __nv_bfloat16* uo = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo;
@@ -340,8 +345,8 @@ __device__ __forceinline__ void epi_swiglu(const EpiDev& e, const GemmParams& p,
     const int col = n0 + tc;
     if (col >= p.N) break;
     float g[kC], up[kC];
-    tmem_ld_f16cols(tbase + tc, g);
-    tmem_ld_f16cols(tbase + BN / 2 + tc, up);
+    tmem_ld_f16cols(tbase + tc, g, sc);
+    tmem_ld_f16cols(tbase + BN / 2 + tc, up, sc);
     if (row_ok) {
       const int nc = min(kC, p.N - col);
       store_row_bf16(gu + col, g, nc);
@@ -356,7 +361,7 @@ __device__ __forceinline__ void epi_swiglu(const EpiDev& e, const GemmParams& p,
 
 template <int BN, int KIND>
 __device__ __forceinline__ void epi_tile(const EpiDev& e, const GemmParams& p, uint32_t tbase, int row, bool row_ok,
-                                         int n0, int half) {
+                                         int n0, int half, float sc) {
   const long long orow = (long long)row * e.ldo;
   const int pos = KIND == CDK_EPI_ROPE_BF16 ? row % e.seq_len : 0;
   #pragma unroll 1
@@ -388,7 +393,7 @@ __device__ __forceinline__ void epi_tile(const EpiDev& e, const GemmParams& p, u
       }
     }
     float v[kC];
-    tmem_ld_f16cols(tbase + tc, v);
+    tmem_ld_f16cols(tbase + tc, v, sc);
     if (!row_ok) continue;
     if (e.bias != nullptr) {
       #pragma unroll
@@ -432,7 +437,7 @@ __device__ __forceinline__ void epi_tile(const EpiDev& e, const GemmParams& p, u
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, bool VEC>
+template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                      const GemmParams p) {
@@ -498,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
           uint8_t* a_dst = sA + stage * Cfg::kBytesA;
           uint8_t* b_dst = sB + stage * Cfg::kBytesB;
-          const int k0 = kt * kBK;
+          const int k0 = kt * (F8 ? 2 * kBK : kBK);  // element coordinate of this 128-byte k block
           if (!A_MN) {
             tma_load_2d(a_dst, &tma_a, &full[stage], k0, m0);
           } else {
@@ -549,7 +554,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 A_MN ? make_sdesc(a_base + kk * 2048, 8192, 1024) : make_sdesc(a_base + kk * 32, 16, 1024);
             const uint64_t bd =
                 B_MN ? make_sdesc(b_base + kk * 2048, 8192, 1024) : make_sdesc(b_base + kk * 32, 16, 1024);
-            umma_f16(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+            if constexpr (F8) umma_f8(d_tmem, ad, bd, p.idesc_f8, (kt > kt0 || kk > 0) ? 1u : 0u);
+            else umma_f16(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
           if (++stage == kStages) {
@@ -567,6 +573,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const EpiDev& e = p.epi;
     uint32_t* stg = reinterpret_cast<uint32_t*>(smem + kStages * Cfg::kStageBytes + Cfg::kBarrierBytes) +
                     (warp - 2) * kStgWords;
+    float sc = 1.f;
+    if constexpr (F8) sc = *p.scale_inv_a * *p.scale_inv_b;
     int local = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
       const int rem = u % tiles_mn;
@@ -592,16 +600,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (VEC) {
         const int row0 = mt * kBM + quad * 32;
         if (row0 < p.M)
-          epi_vec<BN>(e, p, tbase, row0, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN, half, stg, lane);
+          epi_vec<BN>(e, p, tbase, row0, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN, half, stg, lane, sc);
       } else switch (e.kind) {
-        case CDK_EPI_SWIGLU: epi_swiglu<BN>(e, p, tbase, row, row_ok, nt * (BN / 2), half); break;
-        case CDK_EPI_STORE_BF16: epi_tile<BN, CDK_EPI_STORE_BF16>(e, p, tbase, row, row_ok, nt * BN, half); break;
-        case CDK_EPI_STORE_F32: epi_tile<BN, CDK_EPI_STORE_F32>(e, p, tbase, row, row_ok, nt * BN, half); break;
-        case CDK_EPI_RESID_F32: epi_tile<BN, CDK_EPI_RESID_F32>(e, p, tbase, row, row_ok, nt * BN, half); break;
-        case CDK_EPI_ACCUM_F32: epi_tile<BN, CDK_EPI_ACCUM_F32>(e, p, tbase, row, row_ok, nt * BN, half); break;
-        case CDK_EPI_ATOMIC_F32: epi_tile<BN, CDK_EPI_ATOMIC_F32>(e, p, tbase, row, row_ok, nt * BN, half); break;
-        case CDK_EPI_ROPE_BF16: epi_tile<BN, CDK_EPI_ROPE_BF16>(e, p, tbase, row, row_ok, nt * BN, half); break;
-        case CDK_EPI_DSWIGLU: epi_tile<BN, CDK_EPI_DSWIGLU>(e, p, tbase, row, row_ok, nt * BN, half); break;
+        case CDK_EPI_SWIGLU: epi_swiglu<BN>(e, p, tbase, row, row_ok, nt * (BN / 2), half, sc); break;
+        case CDK_EPI_STORE_BF16: epi_tile<BN, CDK_EPI_STORE_BF16>(e, p, tbase, row, row_ok, nt * BN, half, sc); break;
+        case CDK_EPI_STORE_F32: epi_tile<BN, CDK_EPI_STORE_F32>(e, p, tbase, row, row_ok, nt * BN, half, sc); break;
+        case CDK_EPI_RESID_F32: epi_tile<BN, CDK_EPI_RESID_F32>(e, p, tbase, row, row_ok, nt * BN, half, sc); break;
+        case CDK_EPI_ACCUM_F32: epi_tile<BN, CDK_EPI_ACCUM_F32>(e, p, tbase, row, row_ok, nt * BN, half, sc); break;
+        case CDK_EPI_ATOMIC_F32: epi_tile<BN, CDK_EPI_ATOMIC_F32>(e, p, tbase, row, row_ok, nt * BN, half, sc); break;
+        case CDK_EPI_ROPE_BF16: epi_tile<BN, CDK_EPI_ROPE_BF16>(e, p, tbase, row, row_ok, nt * BN, half, sc); break;
+        case CDK_EPI_DSWIGLU: epi_tile<BN, CDK_EPI_DSWIGLU>(e, p, tbase, row, row_ok, nt * BN, half, sc); break;
         default: break;
       }
       tc_fence_before();
@@ -653,6 +661,21 @@ bool make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
   return r == CUDA_SUCCESS;
 }
 
+// 2-D uint8 (fp8 payload) tensor map, 128-byte swizzle; pitch in bytes.
+static bool make_tmap_u8(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
+                         uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 static int num_sms(int dev) {
   static int cache[64] = {0};
   if (dev < 0 || dev >= 64) return 148;
@@ -664,14 +687,14 @@ static int num_sms(int dev) {
   return cache[dev];
 }
 
-template <int BN, bool A_MN, bool B_MN, bool VEC>
+template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
                        cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  auto kfn = gemm_bf16_kernel<BN, A_MN, B_MN, VEC>;
+  auto kfn = gemm_bf16_kernel<BN, A_MN, B_MN, VEC, F8>;
   if (dev < 64 && !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return (int)e;
@@ -691,6 +714,10 @@ template <int BN>
 static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
                           int grid, cudaStream_t s) {
   // the coalesced epilogues (forward kinds and bf16 stores) have their own instantiations
+  if (p.scale_inv_a != nullptr) {  // fp8 operands: K-major only
+    if (p.epi.vec) return launch_gemm<BN, false, false, true, true>(ta, tb, p, grid, s);
+    return launch_gemm<BN, false, false, false, true>(ta, tb, p, grid, s);
+  }
   if (p.epi.vec && !a_mn && !b_mn) return launch_gemm<BN, false, false, true>(ta, tb, p, grid, s);
   if (p.epi.vec && !a_mn && b_mn) return launch_gemm<BN, false, true, true>(ta, tb, p, grid, s);
   if (!a_mn && !b_mn) return launch_gemm<BN, false, false, false>(ta, tb, p, grid, s);
@@ -703,13 +730,18 @@ static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t
 
 }  // namespace cdk
 
-extern "C" int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, int64_t M,
-                             int64_t N, int64_t K, const CdkGemmEpilogue* epi, int split_k, void* stream) {
-  using namespace cdk;
+namespace cdk {
+// Shared host path of cdk_gemm_bf16 and cdk_gemm_fp8 (f8: 8-bit K-major operands
+// with formats a_fmt / b_fmt and device dequantisation scalars sa / sb).
+static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, int64_t M,
+                     int64_t N, int64_t K, const CdkGemmEpilogue* epi, int split_k, void* stream, bool f8, int a_fmt,
+                     int b_fmt, const float* sa, const float* sb) {
   if (!a || !b || !epi || !epi->out) return -1;
   if (M <= 0 || N <= 0 || K <= 0) return -2;
   if (M > (1ll << 31) || N > (1ll << 31) || K > (1ll << 31)) return -2;
-  if (!aligned16(a) || !aligned16(b) || (lda % 8) || (ldb % 8)) return -3;
+  if (!aligned16(a) || !aligned16(b)) return -3;
+  if (f8 ? ((lda % 16) || (ldb % 16)) : ((lda % 8) || (ldb % 8))) return -3;
+  if (f8 && (a_mn || b_mn || !sa || !sb || a_fmt < 0 || a_fmt > 1 || b_fmt < 0 || b_fmt > 1)) return -13;
   const int kind = epi->kind;
   if (kind < CDK_EPI_STORE_BF16 || kind > CDK_EPI_ACCUM_F32) return -4;
   const bool dual = kind == CDK_EPI_SWIGLU;
@@ -740,7 +772,8 @@ extern "C" int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b
   }
   const int n_step = dual ? BN / 2 : BN;
   const long long n_tiles = (N + n_step - 1) / n_step;
-  const long long k_tiles = (K + kBK - 1) / kBK;
+  const int bk = f8 ? 2 * kBK : kBK;  // elements per 128-byte k block
+  const long long k_tiles = (K + bk - 1) / bk;
 
   int splits = 1;
   if (kind == CDK_EPI_ATOMIC_F32) {
@@ -768,10 +801,12 @@ extern "C" int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b
 
   CUtensorMap ta, tb;
   bool ok;
-  if (!a_mn) ok = make_tmap(&ta, a, K, M, lda, kBK, kBM);
+  if (f8) ok = make_tmap_u8(&ta, a, K, M, lda, bk, kBM);
+  else if (!a_mn) ok = make_tmap(&ta, a, K, M, lda, kBK, kBM);
   else ok = make_tmap(&ta, a, M, K, lda, 64, kBK);
   if (!ok) return -10;
-  if (!b_mn) ok = make_tmap(&tb, b, K, dual ? 2 * N : N, ldb, kBK, dual ? BN / 2 : BN);
+  if (f8) ok = make_tmap_u8(&tb, b, K, dual ? 2 * N : N, ldb, bk, dual ? BN / 2 : BN);
+  else if (!b_mn) ok = make_tmap(&tb, b, K, dual ? 2 * N : N, ldb, kBK, dual ? BN / 2 : BN);
   else ok = make_tmap(&tb, b, N, K, ldb, 64, kBK);
   if (!ok) return -11;
 
@@ -786,6 +821,9 @@ extern "C" int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b
   p.k_per_split = (int)k_per;
   p.dual = dual ? 1 : 0;
   p.b_off = dual ? (int)N : 0;
+  p.idesc_f8 = f8 ? make_idesc_f8(kBM, BN, a_fmt, b_fmt) : 0u;
+  p.scale_inv_a = f8 ? sa : nullptr;
+  p.scale_inv_b = f8 ? sb : nullptr;
   p.epi.kind = kind;
   p.epi.seq_len = epi->seq_len;
   p.epi.rope_cols = epi->rope_cols;
@@ -816,4 +854,17 @@ extern "C" int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (BN == 256) return dispatch_major<256>(a_mn, b_mn, ta, tb, p, grid, s);
   return dispatch_major<128>(a_mn, b_mn, ta, tb, p, grid, s);
+}
+}  // namespace cdk
+
+extern "C" int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, int64_t M,
+                             int64_t N, int64_t K, const CdkGemmEpilogue* epi, int split_k, void* stream) {
+  return cdk::gemm_impl(a, lda, a_mn, b, ldb, b_mn, M, N, K, epi, split_k, stream, false, 0, 0, nullptr, nullptr);
+}
+
+extern "C" int cdk_gemm_fp8(const void* a, int64_t lda, int a_fmt, const void* b, int64_t ldb, int b_fmt, int64_t M,
+                            int64_t N, int64_t K, const float* scale_inv_a, const float* scale_inv_b,
+                            const CdkGemmEpilogue* epi, int split_k, void* stream) {
+  return cdk::gemm_impl(a, lda, 0, b, ldb, 0, M, N, K, epi, split_k, stream, true, a_fmt, b_fmt, scale_inv_a,
+                        scale_inv_b);
 }

@@ -132,17 +132,28 @@ def _ld(t: torch.Tensor) -> int:
     return t.stride(0)
 
 
+_FP8_DTYPES = (torch.uint8, torch.float8_e4m3fn, torch.float8_e5m2)
+FP8_E4M3, FP8_E5M2 = 0, 1
+FP8_MAX = {FP8_E4M3: 448.0, FP8_E5M2: 57344.0}
+
+
 def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False, kind: int = EPI_STORE_BF16,
          out: torch.Tensor, bias=None, resid=None, out2=None, aux=None, half_n: int = 0, rope=None,
-         seq_len: int = 0, rope_cols: int = 0, split_k: int = 0, M=None, N=None, K=None) -> torch.Tensor:
+         seq_len: int = 0, rope_cols: int = 0, split_k: int = 0, M=None, N=None, K=None, fp8=None) -> torch.Tensor:
     """D = A @ B^T with a fused epilogue (see include/cdk.h for the kinds).
 
     a: [M,K] (a_mn False) or [K,M] (a_mn True); b: [N,K] (b_mn False) or [K,N].
     For SWIGLU, b is [2N, K] = [gate; up] and N is the number of output columns.
+    fp8 = (a_fmt, b_fmt, scale_inv_a, scale_inv_b): 8-bit K-major operands
+    (FP8_E4M3 / FP8_E5M2) dequantised by the two device scalars.
     """
     _need_cuda(a, b, out)
-    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
-        raise RuntimeError("GEMM inputs must be bf16")
+    if fp8 is None:
+        if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+            raise RuntimeError("GEMM inputs must be bf16")
+    else:
+        if a.dtype not in _FP8_DTYPES or b.dtype not in _FP8_DTYPES or a_mn or b_mn:
+            raise RuntimeError("fp8 GEMM inputs must be 8-bit and K-major")
     if M is None:
         M = a.shape[1] if a_mn else a.shape[0]
     if K is None:
@@ -174,15 +185,55 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-    rc = lib().cdk_gemm_bf16(_p(a), _ld(a), int(a_mn), _p(b), _ld(b), int(b_mn), M, N, K, C.byref(ep), split_k,
-                             _stream())
-    _check(rc, f"gemm_bf16(kind={kind}, M={M}, N={N}, K={K}, a_mn={a_mn}, b_mn={b_mn})")
+    if fp8 is None:
+        rc = lib().cdk_gemm_bf16(_p(a), _ld(a), int(a_mn), _p(b), _ld(b), int(b_mn), M, N, K, C.byref(ep), split_k,
+                                 _stream())
+        _check(rc, f"gemm_bf16(kind={kind}, M={M}, N={N}, K={K}, a_mn={a_mn}, b_mn={b_mn})")
+    else:
+        af, bf, sa, sb = fp8
+        rc = lib().cdk_gemm_fp8(_p(a), a.stride(0), af, _p(b), b.stride(0), bf, M, N, K, _p(sa), _p(sb), C.byref(ep),
+                                split_k, _stream())
+        _check(rc, f"gemm_fp8(kind={kind}, M={M}, N={N}, K={K}, fmt={af}{bf})")
     _count()
     if timer is not None:
         e1.record()
         timer.add(2.0 * M * N * K * (2 if kind == EPI_SWIGLU else 1), e0, e1,
-                  f"M{M} N{N} K{K} kind{kind} mn{int(a_mn)}{int(b_mn)}")
+                  f"M{M} N{N} K{K} kind{kind} mn{int(a_mn)}{int(b_mn)}" + ("" if fp8 is None else " fp8"))
     return out
+
+
+@_timed("fp8_cast")
+def fp8_cast(x, scale, fmt, out=None, out_t=None, amax=None, rows=None, cols=None):
+    """out = sat_fmt(x * scale) (8-bit), out_t its transpose, amax = max(amax, max|x|)."""
+    _need_cuda(x)
+    rows = x.shape[0] if rows is None else rows
+    cols = x.shape[1] if cols is None else cols
+    dt = 0 if x.dtype == torch.float32 else 1 if x.dtype == torch.bfloat16 else None
+    if dt is None:
+        raise RuntimeError("fp8_cast input must be fp32 or bf16")
+    rc = lib().cdk_fp8_cast(_p(x), dt, rows, cols, x.stride(0), _p(scale), fmt, _p(out),
+                            out.stride(0) if out is not None else 0, _p(out_t),
+                            out_t.stride(0) if out_t is not None else 0, _p(amax), _stream())
+    _check(rc, "fp8_cast")
+    _count(1)
+
+
+@_timed("fp8_amax")
+def fp8_amax(x, amax, rows=None, cols=None):
+    rows = x.shape[0] if rows is None else rows
+    cols = x.shape[1] if cols is None else cols
+    dt = 0 if x.dtype == torch.float32 else 1
+    _check(lib().cdk_fp8_amax(_p(x), dt, rows, cols, x.stride(0), _p(amax), _stream()), "fp8_amax")
+    _count(1)
+
+
+@_timed("fp8_scales")
+def fp8_scales(amax_cur, history, scale, scale_inv, fmax, mode=0):
+    n = amax_cur.numel()
+    hist_len = history.shape[1] if history is not None else 0
+    _check(lib().cdk_fp8_scales(_p(amax_cur), _p(history), _p(scale), _p(scale_inv), _p(fmax), n, hist_len, mode,
+                                _stream()), "fp8_scales")
+    _count(1)
 
 
 @_timed("gemm_f32")

@@ -75,6 +75,33 @@ typedef struct CdkGemmEpilogue {
 int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, int64_t M, int64_t N,
                   int64_t K, const CdkGemmEpilogue* epi, int split_k, void* stream);
 
+/* ---- fp8 (the fp8 training variant: e4m3 weights / activations, e5m2
+ *      gradients, per-tensor delayed scaling; no counterpart in the reference,
+ *      whose GEMMs run through torch.autocast fp16) ----------------------------
+ * cdk_gemm_fp8: C = epilogue((A B^T) * (*scale_inv_a) * (*scale_inv_b)) with A
+ * [M, K] and B [N, K] 8-bit, both K-major (row pitch lda / ldb in bytes, a
+ * multiple of 16); a_fmt / b_fmt: 0 = e4m3, 1 = e5m2 (they may differ).  Same
+ * epilogue kinds and split-K rules as cdk_gemm_bf16. */
+int cdk_gemm_fp8(const void* a, int64_t lda, int a_fmt, const void* b, int64_t ldb, int b_fmt, int64_t M, int64_t N,
+                 int64_t K, const float* scale_inv_a, const float* scale_inv_b, const CdkGemmEpilogue* epi,
+                 int split_k, void* stream);
+/* cdk_fp8_cast: out[r, c] = sat_fmt(x[r, c] * (*scale)) (round to nearest even,
+ * saturating to the format's largest finite value); out_t (optional) [cols,
+ * rows] receives the transpose (row pitch ldt bytes); amax (optional) is
+ * raised to max |x| (atomic, non-negative float bits).  x_dtype: 0 = f32,
+ * 1 = bf16; ldx in elements, ldo / ldt in bytes. */
+int cdk_fp8_cast(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx, const float* scale, int fmt,
+                 void* out, int64_t ldo, void* out_t, int64_t ldt, float* amax, void* stream);
+/* cdk_fp8_amax: *amax = max(*amax, max |x|). */
+int cdk_fp8_amax(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx, float* amax, void* stream);
+/* cdk_fp8_scales: per-tensor delayed scaling for n tensors.  mode 0 (end of a
+ * step): history[i] shifts by one and takes amax_cur[i] in slot 0, then
+ * scale[i] = fmax[i] / max(history[i]) (1 when that max is 0), scale_inv[i] =
+ * 1 / scale[i], amax_cur[i] = 0.  mode 1 (first use, empty history): scale
+ * from amax_cur[i] alone, history untouched. */
+int cdk_fp8_scales(float* amax_cur, float* history, float* scale, float* scale_inv, const float* fmax, int32_t n,
+                   int32_t hist_len, int32_t mode, void* stream);
+
 /* ---- attention -----------------------------------------------------------
  * Replaces torchtune MultiHeadAttention's SDPA call as used by
  * chessdecoder/models/model.py:158-171 (pass 1: is_causal; pass 2: bool mask

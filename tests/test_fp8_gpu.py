@@ -1,0 +1,147 @@
+"""fp8 kernels on the GPU: the saturating casts (bit-exact against PyTorch's
+float8 conversion of the clamped, scaled input), their transposed copies and
+amax, the delayed-scaling bookkeeping, and the kind::f8f6f4 GEMM against an
+fp32 matmul of the same 8-bit operands (the products of 8-bit values are
+exact in fp32, so the only difference is the summation order: relative error
+<= 1e-5 for fp32 outputs, bf16 rounding for bf16 outputs).
+"""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+TD = {0: torch.float8_e4m3fn, 1: torch.float8_e5m2}
+FMAX = {0: 448.0, 1: 57344.0}
+
+
+@pytest.fixture(scope="module")
+def K():
+    from chessdecoder_b200 import kernels
+    kernels.lib()
+    return kernels
+
+
+def rel_err(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
+
+
+def ref_cast(x, s, fmt):
+    return (x.float() * s).clamp(-FMAX[fmt], FMAX[fmt]).to(TD[fmt])
+
+
+@pytest.mark.parametrize("rows,cols", [(256, 512), (300, 1000), (1, 7), (65, 129)])
+@pytest.mark.parametrize("fmt", [0, 1])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fp8_cast_transpose_amax(K, rows, cols, fmt, dtype):
+    g = torch.Generator(device=DEV).manual_seed(rows + cols + fmt)
+    x = (torch.randn(rows, cols, generator=g, device=DEV) * 3).to(dtype)
+    x[0, 0] = 40.0  # saturates at scale 20 for e4m3
+    s = torch.tensor([20.0 if fmt == 0 else 300.0], device=DEV)
+    ldo = (cols + 15) // 16 * 16
+    ldt = (rows + 15) // 16 * 16
+    out = torch.zeros(rows, ldo, device=DEV, dtype=torch.uint8)
+    out_t = torch.zeros(cols, ldt, device=DEV, dtype=torch.uint8)
+    amax = torch.zeros(1, device=DEV)
+    K.fp8_cast(x, s, fmt, out=out, out_t=out_t, amax=amax)
+    torch.cuda.synchronize()
+    ref = ref_cast(x, s, fmt).view(torch.uint8)
+    assert torch.equal(out[:, :cols], ref)
+    assert torch.equal(out_t[:, :rows], ref.t())
+    assert float(amax) == float(x.float().abs().max())
+    assert K.get_error() == 0
+
+
+def test_fp8_scales(K):
+    n, hl = 5, 4
+    amax = torch.tensor([1.0, 0.0, 10.0, 0.5, 2.0], device=DEV)
+    hist = torch.zeros(n, hl, device=DEV)
+    hist[:, 1] = torch.tensor([3.0, 0.0, 1.0, 0.25, 2.0], device=DEV)
+    scale = torch.zeros(n, device=DEV)
+    sinv = torch.zeros(n, device=DEV)
+    fmax = torch.tensor([448.0, 448.0, 57344.0, 448.0, 448.0], device=DEV)
+    K.fp8_scales(amax.clone(), hist.clone(), scale, sinv, fmax, mode=1)
+    exp1 = torch.where(amax > 0, fmax / amax.clamp_min(1e-30), torch.ones_like(amax))
+    assert torch.allclose(scale, exp1)
+    a2, h2 = amax.clone(), hist.clone()
+    K.fp8_scales(a2, h2, scale, sinv, fmax, mode=0)
+    torch.cuda.synchronize()
+    exp_h = torch.cat([amax[:, None], hist[:, :-1]], 1)
+    assert torch.equal(h2, exp_h)
+    m = exp_h.max(1).values
+    exp = torch.where(m > 0, fmax / m.clamp_min(1e-30), torch.ones_like(m))
+    assert torch.allclose(scale, exp) and torch.allclose(sinv, 1 / exp)
+    assert float(a2.abs().sum()) == 0.0
+
+
+def _q(shape, fmt, gen, scale=1.0):
+    x = torch.randn(*shape, generator=gen, device=DEV) * scale
+    return x.clamp(-FMAX[fmt], FMAX[fmt]).to(TD[fmt])
+
+
+@pytest.mark.parametrize("M,N,K_", [(300, 384, 512), (1024, 1024, 1024), (77, 41, 256), (128, 1924, 1024)])
+@pytest.mark.parametrize("fa,fb", [(0, 0), (1, 0)])
+def test_fp8_gemm_store(K, M, N, K_, fa, fb):
+    g = torch.Generator(device=DEV).manual_seed(M + N + K_ + fa)
+    A = _q((M, K_), fa, g, 2.0)
+    B = _q((N, K_), fb, g, 2.0)
+    sa = torch.tensor([0.5], device=DEV)
+    sb = torch.tensor([0.125], device=DEV)
+    ref = (A.float() @ B.float().t()) * 0.5 * 0.125
+    out = torch.empty(M, N, device=DEV)
+    K.gemm(A, B, kind=K.EPI_STORE_F32, out=out, fp8=(fa, fb, sa, sb))
+    torch.cuda.synchronize()
+    assert rel_err(out, ref) < 1e-5
+    if N % 16 == 0:
+        o16 = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+        K.gemm(A, B, kind=K.EPI_STORE_BF16, out=o16, fp8=(fa, fb, sa, sb))
+        torch.cuda.synchronize()
+        assert rel_err(o16, ref) < 5e-3
+    assert K.get_error() == 0
+
+
+def test_fp8_gemm_epilogues(K):
+    from chessdecoder_b200.engine import rope_table
+    g = torch.Generator(device=DEV).manual_seed(7)
+    S, E, F = 256, 512, 768
+    T = 2 * S
+    X = _q((T, E), 0, g)
+    W = _q((3 * E, E), 0, g, 0.5)
+    sa = torch.tensor([0.25], device=DEV)
+    sb = torch.tensor([0.5], device=DEV)
+    f8 = (0, 0, sa, sb)
+    y = (X.float() @ W.float().t()) * 0.125
+    # residual
+    resid = torch.randn(T, E, device=DEV)
+    out = torch.empty(T, E, device=DEV)
+    K.gemm(X, W[:E], kind=K.EPI_RESID_F32, out=out, resid=resid, fp8=f8)
+    assert rel_err(out, resid + y[:, :E]) < 1e-5
+    # RoPE on q|k columns
+    rope = rope_table(S, 64).to(DEV)
+    qkv = torch.empty(T, 3 * E, device=DEV, dtype=torch.bfloat16)
+    K.gemm(X, W, kind=K.EPI_ROPE_BF16, out=qkv, rope=rope, seq_len=S, rope_cols=2 * E, fp8=f8)
+    yr = y.view(T, 3 * E // 64, 32, 2).clone()
+    pos = torch.arange(T, device=DEV) % S
+    c, s_ = rope[pos][:, None, :, 0], rope[pos][:, None, :, 1]
+    qk = yr[:, : 2 * E // 64]
+    r0 = qk[..., 0] * c - qk[..., 1] * s_
+    r1 = qk[..., 1] * c + qk[..., 0] * s_
+    yr[:, : 2 * E // 64] = torch.stack([r0, r1], -1)
+    assert rel_err(qkv, yr.view(T, 3 * E)) < 5e-3
+    # SwiGLU (dual B = [gate; up])
+    W13 = _q((2 * F, E), 0, g, 0.5)
+    h = (X.float() @ W13.float().t()) * 0.125
+    gte, up = h[:, :F], h[:, F:]
+    u = torch.empty(T, F, device=DEV, dtype=torch.bfloat16)
+    gu = torch.empty(T, 2 * F, device=DEV, dtype=torch.bfloat16)
+    K.gemm(X, W13, kind=K.EPI_SWIGLU, out=u, out2=gu, half_n=F, fp8=f8)
+    assert rel_err(gu, h) < 5e-3
+    assert rel_err(u, torch.nn.functional.silu(gte) * up) < 5e-3
+    # split-K atomic accumulation (weight-gradient shape, e5m2 x e4m3)
+    dYt = _q((1024, 4096), 1, g, 1.0)
+    Xt = _q((E, 4096), 0, g, 1.0)
+    dw = torch.zeros(1024, E, device=DEV)
+    K.gemm(dYt, Xt, kind=K.EPI_ATOMIC_F32, out=dw, fp8=(1, 0, sa, sb))
+    torch.cuda.synchronize()
+    assert rel_err(dw, (dYt.float() @ Xt.float().t()) * 0.125) < 1e-5
+    assert K.get_error() == 0
