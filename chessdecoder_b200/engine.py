@@ -354,17 +354,33 @@ def prepare_batch(batch: dict, device, require_pairing: bool = True) -> DeviceBa
 # Backbone (embedding output -> final RMSNorm), forward and backward
 # ---------------------------------------------------------------------------
 class LayerSaved:
-    __slots__ = ("x", "n1", "r1", "qkv", "ao", "lse", "h1", "n2", "r2", "gu", "u")
+    __slots__ = ("x", "n1", "r1", "qkv", "ao", "lse", "h1", "n2", "r2", "gu", "u", "n1T", "aoT", "n2T", "uT")
 
 
 class Backbone:
     """The 12 transformer layers + final norm over a batch of sequences where
     the first ``n_causal`` use the causal mask and the rest the prefix mask."""
 
-    def __init__(self, store: ParamStore, cfg: ModelConfig):
+    def __init__(self, store: ParamStore, cfg: ModelConfig, fp8=None):
         self.st = store
         self.cfg = cfg
         self.rope = rope_table(cfg.max_seq_len, cfg.head_dim).to(store.device)
+        self.fp8 = fp8  # Fp8Recipe: the backbone linears run in fp8 (chessdecoder_b200/fp8.py)
+
+    def cast_fp8_weights(self):
+        """e4m3 copies (and their transposes) of this step's backbone weights."""
+        st, E, F = self.st, self.cfg.embed_dim, self.cfg.ff
+        for i in range(self.cfg.num_layers):
+            p = f"layers.{i}."
+            self.fp8.cast_weights(i, {
+                "qkv": st.span(p + "attn.q_proj.weight", p + "attn.v_proj.weight", st.flat).view(3 * E, E),
+                "o": st.param(p + "attn.output_proj.weight"),
+                "13": st.span(p + "mlp.w1.weight", p + "mlp.w3.weight", st.flat).view(2 * F, E),
+                "2": st.param(p + "mlp.w2.weight")})
+
+    def _f8(self, i, lin, a_kind, a_fmt, b_kind, b_fmt):
+        f = self.fp8
+        return (a_fmt, b_fmt, f.sinv(f.site(i, lin, a_kind)), f.sinv(f.site(i, lin, b_kind)))
 
     def _w(self, i):
         st, p = self.st, f"layers.{i}."
@@ -390,6 +406,8 @@ class Backbone:
         dev = h.device
         saved = []
         x = h
+        f8 = self.fp8
+        E4, E5 = K.FP8_E4M3, K.FP8_E5M2
         for i in range(cfg.num_layers):
             w = self._w(i)
             s = LayerSaved()
@@ -398,20 +416,41 @@ class Backbone:
             s.r1 = torch.empty(T, device=dev)
             K.rmsnorm_fwd(x, w["s1"], y16=s.n1, rstd=s.r1)
             s.qkv = torch.empty(T, 3 * E, device=dev, dtype=torch.bfloat16)
-            K.gemm(s.n1, w["wqkv"], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=self.rope, seq_len=S, rope_cols=2 * E)
+            if f8 is None:
+                K.gemm(s.n1, w["wqkv"], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=self.rope, seq_len=S, rope_cols=2 * E)
+            else:
+                x8, s.n1T = f8.cast(s.n1, f8.site(i, "qkv", "x"), E4)
+                s.n1 = None
+                K.gemm(x8, f8.weights[(i, "qkv")][0], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=self.rope, seq_len=S,
+                       rope_cols=2 * E, fp8=self._f8(i, "qkv", "x", E4, "w", E4))
             s.ao = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
             s.lse = torch.empty(nseq * H * S, device=dev)
             K.attn_fwd(s.qkv, s.ao, s.lse, nseq, n_causal, S, H, bid32, meta)
             s.h1 = torch.empty(T, E, device=dev)
-            K.gemm(s.ao, w["wo"], kind=K.EPI_RESID_F32, out=s.h1, resid=x)
+            if f8 is None:
+                K.gemm(s.ao, w["wo"], kind=K.EPI_RESID_F32, out=s.h1, resid=x)
+            else:
+                a8, s.aoT = f8.cast(s.ao, f8.site(i, "o", "x"), E4)
+                K.gemm(a8, f8.weights[(i, "o")][0], kind=K.EPI_RESID_F32, out=s.h1, resid=x,
+                       fp8=self._f8(i, "o", "x", E4, "w", E4))
             s.n2 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
             s.r2 = torch.empty(T, device=dev)
             K.rmsnorm_fwd(s.h1, w["s2"], y16=s.n2, rstd=s.r2)
             s.gu = torch.empty(T, 2 * F, device=dev, dtype=torch.bfloat16)
             s.u = torch.empty(T, F, device=dev, dtype=torch.bfloat16)
-            K.gemm(s.n2, w["w13"], kind=K.EPI_SWIGLU, out=s.u, out2=s.gu, half_n=F)
             out = torch.empty(T, E, device=dev)
-            K.gemm(s.u, w["w2"], kind=K.EPI_RESID_F32, out=out, resid=s.h1)
+            if f8 is None:
+                K.gemm(s.n2, w["w13"], kind=K.EPI_SWIGLU, out=s.u, out2=s.gu, half_n=F)
+                K.gemm(s.u, w["w2"], kind=K.EPI_RESID_F32, out=out, resid=s.h1)
+            else:
+                n8, s.n2T = f8.cast(s.n2, f8.site(i, "13", "x"), E4)
+                s.n2 = None
+                K.gemm(n8, f8.weights[(i, "13")][0], kind=K.EPI_SWIGLU, out=s.u, out2=s.gu, half_n=F,
+                       fp8=self._f8(i, "13", "x", E4, "w", E4))
+                u8, s.uT = f8.cast(s.u, f8.site(i, "2", "x"), E4)
+                s.u = None
+                K.gemm(u8, f8.weights[(i, "2")][0], kind=K.EPI_RESID_F32, out=out, resid=s.h1,
+                       fp8=self._f8(i, "2", "x", E4, "w", E4))
             saved.append(s)
             x = out
         hN16 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
@@ -441,22 +480,47 @@ class Backbone:
         dao = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
         dqkv = torch.empty(T, 3 * E, device=dev, dtype=torch.bfloat16)
         dsum = torch.empty(nseq * H * S, device=dev)
+        f8 = self.fp8
+        E4, E5 = K.FP8_E4M3, K.FP8_E5M2
         for i in reversed(range(cfg.num_layers)):
             s = saved[i]
             w, g = self._w(i), self._g(i)
-            # MLP block: du = dh W2 (plain GEMM), then the coalesced SwiGLU backward
-            K.gemm(dh16, w["w2"], b_mn=True, kind=K.EPI_STORE_BF16, out=du)
-            K.swiglu_bwd(du, s.gu, dgu)
-            K.gemm(dh16, s.u, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w2"])
-            K.gemm(dgu, w["w13"], b_mn=True, kind=K.EPI_STORE_BF16, out=dn)
-            K.gemm(dgu, s.n2, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w13"])
+            if f8 is None:
+                # MLP block: du = dh W2 (plain GEMM), then the coalesced SwiGLU backward
+                K.gemm(dh16, w["w2"], b_mn=True, kind=K.EPI_STORE_BF16, out=du)
+                K.swiglu_bwd(du, s.gu, dgu)
+                K.gemm(dh16, s.u, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w2"])
+                K.gemm(dgu, w["w13"], b_mn=True, kind=K.EPI_STORE_BF16, out=dn)
+                K.gemm(dgu, s.n2, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w13"])
+            else:
+                g8, gT = f8.cast(dh16, f8.site(i, "2", "g"), E5)
+                K.gemm(g8, f8.weights[(i, "2")][1], kind=K.EPI_STORE_BF16, out=du,
+                       fp8=self._f8(i, "2", "g", E5, "w", E4))
+                K.swiglu_bwd(du, s.gu, dgu)
+                K.gemm(gT, s.uT, kind=K.EPI_ATOMIC_F32, out=g["w2"], fp8=self._f8(i, "2", "g", E5, "x", E4))
+                g8, gT = f8.cast(dgu, f8.site(i, "13", "g"), E5)
+                K.gemm(g8, f8.weights[(i, "13")][1], kind=K.EPI_STORE_BF16, out=dn,
+                       fp8=self._f8(i, "13", "g", E5, "w", E4))
+                K.gemm(gT, s.n2T, kind=K.EPI_ATOMIC_F32, out=g["w13"], fp8=self._f8(i, "13", "g", E5, "x", E4))
             K.rmsnorm_bwd(dn, s.h1, w["s2"], s.r2, dx=dh1, dx16=dh1_16, dscale=g["s2"], dres=dh)
             # attention block
-            K.gemm(dh1_16, w["wo"], b_mn=True, kind=K.EPI_STORE_BF16, out=dao)
-            K.gemm(dh1_16, s.ao, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wo"])
+            if f8 is None:
+                K.gemm(dh1_16, w["wo"], b_mn=True, kind=K.EPI_STORE_BF16, out=dao)
+                K.gemm(dh1_16, s.ao, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wo"])
+            else:
+                g8, gT = f8.cast(dh1_16, f8.site(i, "o", "g"), E5)
+                K.gemm(g8, f8.weights[(i, "o")][1], kind=K.EPI_STORE_BF16, out=dao,
+                       fp8=self._f8(i, "o", "g", E5, "w", E4))
+                K.gemm(gT, s.aoT, kind=K.EPI_ATOMIC_F32, out=g["wo"], fp8=self._f8(i, "o", "g", E5, "x", E4))
             K.attn_bwd(s.qkv, s.ao, dao, s.lse, dsum, dqkv, nseq, n_causal, S, H, bid32, meta, rope=self.rope)
-            K.gemm(dqkv, w["wqkv"], b_mn=True, kind=K.EPI_STORE_BF16, out=dn)
-            K.gemm(dqkv, s.n1, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wqkv"])
+            if f8 is None:
+                K.gemm(dqkv, w["wqkv"], b_mn=True, kind=K.EPI_STORE_BF16, out=dn)
+                K.gemm(dqkv, s.n1, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wqkv"])
+            else:
+                g8, gT = f8.cast(dqkv, f8.site(i, "qkv", "g"), E5)
+                K.gemm(g8, f8.weights[(i, "qkv")][1], kind=K.EPI_STORE_BF16, out=dn,
+                       fp8=self._f8(i, "qkv", "g", E5, "w", E4))
+                K.gemm(gT, s.n1T, kind=K.EPI_ATOMIC_F32, out=g["wqkv"], fp8=self._f8(i, "qkv", "g", E5, "x", E4))
             K.rmsnorm_bwd(dn, s.x, w["s1"], s.r1, dx=dh, dx16=dh16, dscale=g["s1"], dres=dh1)
             if on_layer_done is not None:
                 on_layer_done(i)
@@ -614,13 +678,17 @@ class TrainStep:
     """
 
     def __init__(self, cfg: ModelConfig, device="cuda", seed=0, lr=3e-4, weight_decay=0.1, betas=(0.9, 0.999),
-                 eps=1e-8, max_norm=10.0, loss_weights=(5.0, 1.0, 1.0, 1.0), state_dict=None):
+                 eps=1e-8, max_norm=10.0, loss_weights=(5.0, 1.0, 1.0, 1.0), state_dict=None, fp8: bool = False):
         self.cfg = cfg
         self.device = torch.device(device)
         self.store = ParamStore(cfg, self.device)
         sd = state_dict if state_dict is not None else init_reference_weights(cfg, seed)
         self.store.load_state_dict({k: v.to(self.device) for k, v in sd.items()})
-        self.backbone = Backbone(self.store, cfg)
+        self.fp8 = None
+        if fp8:
+            from .fp8 import Fp8Recipe
+            self.fp8 = Fp8Recipe(cfg.num_layers, self.device)
+        self.backbone = Backbone(self.store, cfg, self.fp8)
         self.front = FrontEnd(self.store, cfg)
         self.heads = Heads(self.store, cfg, loss_weights)
         self.lr, self.wd, self.betas, self.eps, self.max_norm = lr, weight_decay, betas, eps, max_norm
@@ -637,11 +705,15 @@ class TrainStep:
         B, S = db.B, db.S
         losses = torch.zeros(4, device=self.device)
         meta = K.attn_meta(db.bid, S)
+        if self.fp8 is not None:
+            self.backbone.cast_fp8_weights()
         h0, fctx = self.front.forward(db, n_copies=2)
         hN16, _, bctx = self.backbone.forward(h0, 2 * B, B, S, db.bid, meta)
         dhN = self.heads.run(db, hN16, losses, metrics)
         dh0 = self.backbone.backward(dhN, bctx, self.grad_hook)
         self.front.backward(db, dh0, fctx, n_copies=2)
+        if self.fp8 is not None:
+            self.fp8.end_step()
         if self.grad_hook is not None:
             self.grad_hook(-1)
         return losses

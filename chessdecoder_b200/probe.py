@@ -72,17 +72,56 @@ def gemm_case(kind: str, T: int = 32768, E: int = 1024, F: int = 1536):
     return fn, 2.0 * M * N * Kd, nbytes, f"M{M} N{N} K{Kd} {kind}"
 
 
+def gemm_case_fp8(kind: str, T: int = 32768, E: int = 1024, F: int = 1536):
+    """The same shapes with 8-bit K-major operands (the dX / dW shapes use the
+    transposed copies the fp8 recipe makes)."""
+    dev = "cuda"
+    q = lambda *s: (torch.randn(*s, device=dev) * 0.5).to(torch.float8_e4m3fn)  # noqa: E731
+    sc = torch.ones(1, device=dev)
+    f8 = (0, 0, sc, sc)
+    if kind == "rope":
+        X, W = q(T, E), q(3 * E, E)
+        out = torch.empty(T, 3 * E, device=dev, dtype=torch.bfloat16)
+        rope = rope_table(256, 64).to(dev)
+        fn = lambda: K.gemm(X, W, kind=K.EPI_ROPE_BF16, out=out, rope=rope, seq_len=256, rope_cols=2 * E, fp8=f8)  # noqa
+        M, N, Kd, nbytes = T, 3 * E, E, T * E + 3 * E * E + T * 3 * E * 2
+    elif kind == "swiglu":
+        X, W = q(T, E), q(2 * F, E)
+        u = torch.empty(T, F, device=dev, dtype=torch.bfloat16)
+        gu = torch.empty(T, 2 * F, device=dev, dtype=torch.bfloat16)
+        fn = lambda: K.gemm(X, W, kind=K.EPI_SWIGLU, out=u, out2=gu, half_n=F, fp8=f8)  # noqa
+        M, N, Kd, nbytes = T, 2 * F, E, T * E + 2 * F * E + T * 3 * F * 2
+    elif kind == "resid":
+        X, W = q(T, E), q(E, E)
+        h = torch.randn(T, E, device=dev)
+        out = torch.empty(T, E, device=dev)
+        fn = lambda: K.gemm(X, W, kind=K.EPI_RESID_F32, out=out, resid=h, fp8=f8)  # noqa
+        M, N, Kd, nbytes = T, E, E, T * E + E * E + 2 * T * E * 4
+    elif kind == "dx":
+        dY, Wt = q(T, 3 * E), q(E, 3 * E)
+        out = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+        fn = lambda: K.gemm(dY, Wt, kind=K.EPI_STORE_BF16, out=out, fp8=f8)  # noqa
+        M, N, Kd, nbytes = T, E, 3 * E, T * 3 * E + 3 * E * E + T * E * 2
+    else:
+        dYt, Xt = q(3 * E, T), q(E, T)
+        out = torch.zeros(3 * E, E, device=dev)
+        fn = lambda: K.gemm(dYt, Xt, kind=K.EPI_ATOMIC_F32, out=out, fp8=f8)  # noqa
+        M, N, Kd, nbytes = 3 * E, E, T, T * 3 * E + T * E + 3 * E * E * 4
+    return fn, 2.0 * M * N * Kd, nbytes, f"M{M} N{N} K{Kd} {kind} fp8"
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("mode", choices=["gemm", "attn", "adamw"])
     ap.add_argument("--kind", default="rope", choices=["rope", "swiglu", "resid", "dx", "dw"])
+    ap.add_argument("--fp8", action="store_true", help="8-bit operands (e4m3; e5m2 x e4m3 for dx / dw)")
     ap.add_argument("--nseq", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     a = ap.parse_args()
     K.lib()
     if a.mode == "gemm":
-        fn, flops, nbytes, name = gemm_case(a.kind)
+        fn, flops, nbytes, name = (gemm_case_fp8 if a.fp8 else gemm_case)(a.kind)
         ms = _time(fn, a.warmup, a.iters)
         print(json.dumps({"probe": name, "ms": ms, "tflops": flops / ms / 1e9, "alg_bytes": nbytes,
                           "alg_gbs": nbytes / ms / 1e6}))
