@@ -226,11 +226,14 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool a_mn, 
          | ((uint32_t)(M >> 4) << 24);   // M / 16
 }
 
-// kind::f8f6f4 descriptor for K-major 8-bit operands; fmt 0 = e4m3, 1 = e5m2.
-__host__ __device__ constexpr uint32_t make_idesc_f8(int M, int N, int a_fmt, int b_fmt) {
+// kind::f8f6f4 descriptor for 8-bit operands; fmt 0 = e4m3, 1 = e5m2 (the
+// MN-major bits are valid for these two formats).
+__host__ __device__ constexpr uint32_t make_idesc_f8(int M, int N, int a_fmt, int b_fmt, bool a_mn, bool b_mn) {
   return (1u << 4)                       // D format F32
          | ((uint32_t)(a_fmt & 7) << 7)  // A format
          | ((uint32_t)(b_fmt & 7) << 10) // B format
+         | ((a_mn ? 1u : 0u) << 15)      // A major
+         | ((b_mn ? 1u : 0u) << 16)      // B major
          | ((uint32_t)(N >> 3) << 17)    // N / 8
          | ((uint32_t)(M >> 4) << 24);   // M / 16
 }

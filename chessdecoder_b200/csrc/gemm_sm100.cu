@@ -504,11 +504,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* a_dst = sA + stage * Cfg::kBytesA;
           uint8_t* b_dst = sB + stage * Cfg::kBytesB;
           const int k0 = kt * (F8 ? 2 * kBK : kBK);  // element coordinate of this 128-byte k block
+          // MN-major operands arrive as 128-byte-wide MN groups (64 bf16 / 128 fp8
+          // elements) of kRowsK k rows each
+          constexpr int kGrpE = F8 ? 128 : 64;
+          constexpr int kGrpB = F8 ? 16384 : 8192;
           if (!A_MN) {
             tma_load_2d(a_dst, &tma_a, &full[stage], k0, m0);
           } else {
-            tma_load_2d(a_dst, &tma_a, &full[stage], m0, k0);
-            tma_load_2d(a_dst + 8192, &tma_a, &full[stage], m0 + 64, k0);
+            #pragma unroll
+            for (int g = 0; g < kBM / kGrpE; ++g) tma_load_2d(a_dst + g * kGrpB, &tma_a, &full[stage], m0 + g * kGrpE, k0);
           }
           if (!B_MN) {
             if (p.dual) {
@@ -519,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else {
             #pragma unroll
-            for (int i = 0; i < BN / 64; ++i) tma_load_2d(b_dst + i * 8192, &tma_b, &full[stage], n0 + 64 * i, k0);
+            for (int i = 0; i < BN / kGrpE; ++i) tma_load_2d(b_dst + i * kGrpB, &tma_b, &full[stage], n0 + kGrpE * i, k0);
           }
           if (++stage == kStages) {
             stage = 0;
@@ -550,10 +554,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_base = smem_u32(sB + stage * Cfg::kBytesB);
           #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
+            // MN-major: one MMA consumes 16 (bf16) / 32 (fp8) k rows of 128 B
+            constexpr uint32_t kKStep = F8 ? 4096 : 2048, kLbo = F8 ? 16384 : 8192;
             const uint64_t ad =
-                A_MN ? make_sdesc(a_base + kk * 2048, 8192, 1024) : make_sdesc(a_base + kk * 32, 16, 1024);
+                A_MN ? make_sdesc(a_base + kk * kKStep, kLbo, 1024) : make_sdesc(a_base + kk * 32, 16, 1024);
             const uint64_t bd =
-                B_MN ? make_sdesc(b_base + kk * 2048, 8192, 1024) : make_sdesc(b_base + kk * 32, 16, 1024);
+                B_MN ? make_sdesc(b_base + kk * kKStep, kLbo, 1024) : make_sdesc(b_base + kk * 32, 16, 1024);
             if constexpr (F8) umma_f8(d_tmem, ad, bd, p.idesc_f8, (kt > kt0 || kk > 0) ? 1u : 0u);
             else umma_f16(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
           }
@@ -714,9 +720,13 @@ template <int BN>
 static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
                           int grid, cudaStream_t s) {
   // the coalesced epilogues (forward kinds and bf16 stores) have their own instantiations
-  if (p.scale_inv_a != nullptr) {  // fp8 operands: K-major only
-    if (p.epi.vec) return launch_gemm<BN, false, false, true, true>(ta, tb, p, grid, s);
-    return launch_gemm<BN, false, false, false, true>(ta, tb, p, grid, s);
+  if (p.scale_inv_a != nullptr) {  // fp8 operands
+    if (p.epi.vec && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, true>(ta, tb, p, grid, s);
+    if (p.epi.vec && !a_mn && b_mn) return launch_gemm<BN, false, true, true, true>(ta, tb, p, grid, s);
+    if (!a_mn && !b_mn) return launch_gemm<BN, false, false, false, true>(ta, tb, p, grid, s);
+    if (!a_mn && b_mn) return launch_gemm<BN, false, true, false, true>(ta, tb, p, grid, s);
+    if (a_mn && !b_mn) return launch_gemm<BN, true, false, false, true>(ta, tb, p, grid, s);
+    return launch_gemm<BN, true, true, false, true>(ta, tb, p, grid, s);
   }
   if (p.epi.vec && !a_mn && !b_mn) return launch_gemm<BN, false, false, true>(ta, tb, p, grid, s);
   if (p.epi.vec && !a_mn && b_mn) return launch_gemm<BN, false, true, true>(ta, tb, p, grid, s);
@@ -741,7 +751,8 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   if (M > (1ll << 31) || N > (1ll << 31) || K > (1ll << 31)) return -2;
   if (!aligned16(a) || !aligned16(b)) return -3;
   if (f8 ? ((lda % 16) || (ldb % 16)) : ((lda % 8) || (ldb % 8))) return -3;
-  if (f8 && (a_mn || b_mn || !sa || !sb || a_fmt < 0 || a_fmt > 1 || b_fmt < 0 || b_fmt > 1)) return -13;
+  if (f8 && (!sa || !sb || a_fmt < 0 || a_fmt > 1 || b_fmt < 0 || b_fmt > 1)) return -13;
+  if (f8 && ((a_mn && M % 16) || (b_mn && N % 16))) return -13;  // MN-major pitch: 16-byte rows
   const int kind = epi->kind;
   if (kind < CDK_EPI_STORE_BF16 || kind > CDK_EPI_ACCUM_F32) return -4;
   const bool dual = kind == CDK_EPI_SWIGLU;
@@ -801,11 +812,13 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
 
   CUtensorMap ta, tb;
   bool ok;
-  if (f8) ok = make_tmap_u8(&ta, a, K, M, lda, bk, kBM);
+  if (f8 && !a_mn) ok = make_tmap_u8(&ta, a, K, M, lda, bk, kBM);
+  else if (f8) ok = make_tmap_u8(&ta, a, M, K, lda, 128, bk);
   else if (!a_mn) ok = make_tmap(&ta, a, K, M, lda, kBK, kBM);
   else ok = make_tmap(&ta, a, M, K, lda, 64, kBK);
   if (!ok) return -10;
-  if (f8) ok = make_tmap_u8(&tb, b, K, dual ? 2 * N : N, ldb, bk, dual ? BN / 2 : BN);
+  if (f8 && !b_mn) ok = make_tmap_u8(&tb, b, K, dual ? 2 * N : N, ldb, bk, dual ? BN / 2 : BN);
+  else if (f8) ok = make_tmap_u8(&tb, b, N, K, ldb, 128, bk);
   else if (!b_mn) ok = make_tmap(&tb, b, K, dual ? 2 * N : N, ldb, kBK, dual ? BN / 2 : BN);
   else ok = make_tmap(&tb, b, N, K, ldb, 64, kBK);
   if (!ok) return -11;
@@ -821,7 +834,7 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   p.k_per_split = (int)k_per;
   p.dual = dual ? 1 : 0;
   p.b_off = dual ? (int)N : 0;
-  p.idesc_f8 = f8 ? make_idesc_f8(kBM, BN, a_fmt, b_fmt) : 0u;
+  p.idesc_f8 = f8 ? make_idesc_f8(kBM, BN, a_fmt, b_fmt, a_mn != 0, b_mn != 0) : 0u;
   p.scale_inv_a = f8 ? sa : nullptr;
   p.scale_inv_b = f8 ? sb : nullptr;
   p.epi.kind = kind;
@@ -862,9 +875,9 @@ extern "C" int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b
   return cdk::gemm_impl(a, lda, a_mn, b, ldb, b_mn, M, N, K, epi, split_k, stream, false, 0, 0, nullptr, nullptr);
 }
 
-extern "C" int cdk_gemm_fp8(const void* a, int64_t lda, int a_fmt, const void* b, int64_t ldb, int b_fmt, int64_t M,
-                            int64_t N, int64_t K, const float* scale_inv_a, const float* scale_inv_b,
-                            const CdkGemmEpilogue* epi, int split_k, void* stream) {
-  return cdk::gemm_impl(a, lda, 0, b, ldb, 0, M, N, K, epi, split_k, stream, true, a_fmt, b_fmt, scale_inv_a,
+extern "C" int cdk_gemm_fp8(const void* a, int64_t lda, int a_mn, int a_fmt, const void* b, int64_t ldb, int b_mn,
+                            int b_fmt, int64_t M, int64_t N, int64_t K, const float* scale_inv_a,
+                            const float* scale_inv_b, const CdkGemmEpilogue* epi, int split_k, void* stream) {
+  return cdk::gemm_impl(a, lda, a_mn, b, ldb, b_mn, M, N, K, epi, split_k, stream, true, a_fmt, b_fmt, scale_inv_a,
                         scale_inv_b);
 }

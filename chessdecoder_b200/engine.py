@@ -354,7 +354,7 @@ def prepare_batch(batch: dict, device, require_pairing: bool = True) -> DeviceBa
 # Backbone (embedding output -> final RMSNorm), forward and backward
 # ---------------------------------------------------------------------------
 class LayerSaved:
-    __slots__ = ("x", "n1", "r1", "qkv", "ao", "lse", "h1", "n2", "r2", "gu", "u", "n1T", "aoT", "n2T", "uT")
+    __slots__ = ("x", "n1", "r1", "qkv", "ao", "lse", "h1", "n2", "r2", "gu", "u", "n1T", "aoT", "n2T", "uT")  # *T: fp8 copies
 
 
 class Backbone:
@@ -419,9 +419,9 @@ class Backbone:
             if f8 is None:
                 K.gemm(s.n1, w["wqkv"], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=self.rope, seq_len=S, rope_cols=2 * E)
             else:
-                x8, s.n1T = f8.cast(s.n1, f8.site(i, "qkv", "x"), E4)
+                x8 = s.n1T = f8.cast(s.n1, f8.site(i, "qkv", "x"), E4)
                 s.n1 = None
-                K.gemm(x8, f8.weights[(i, "qkv")][0], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=self.rope, seq_len=S,
+                K.gemm(x8, f8.weights[(i, "qkv")], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=self.rope, seq_len=S,
                        rope_cols=2 * E, fp8=self._f8(i, "qkv", "x", E4, "w", E4))
             s.ao = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
             s.lse = torch.empty(nseq * H * S, device=dev)
@@ -430,8 +430,8 @@ class Backbone:
             if f8 is None:
                 K.gemm(s.ao, w["wo"], kind=K.EPI_RESID_F32, out=s.h1, resid=x)
             else:
-                a8, s.aoT = f8.cast(s.ao, f8.site(i, "o", "x"), E4)
-                K.gemm(a8, f8.weights[(i, "o")][0], kind=K.EPI_RESID_F32, out=s.h1, resid=x,
+                a8 = s.aoT = f8.cast(s.ao, f8.site(i, "o", "x"), E4)
+                K.gemm(a8, f8.weights[(i, "o")], kind=K.EPI_RESID_F32, out=s.h1, resid=x,
                        fp8=self._f8(i, "o", "x", E4, "w", E4))
             s.n2 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
             s.r2 = torch.empty(T, device=dev)
@@ -443,13 +443,13 @@ class Backbone:
                 K.gemm(s.n2, w["w13"], kind=K.EPI_SWIGLU, out=s.u, out2=s.gu, half_n=F)
                 K.gemm(s.u, w["w2"], kind=K.EPI_RESID_F32, out=out, resid=s.h1)
             else:
-                n8, s.n2T = f8.cast(s.n2, f8.site(i, "13", "x"), E4)
+                n8 = s.n2T = f8.cast(s.n2, f8.site(i, "13", "x"), E4)
                 s.n2 = None
-                K.gemm(n8, f8.weights[(i, "13")][0], kind=K.EPI_SWIGLU, out=s.u, out2=s.gu, half_n=F,
+                K.gemm(n8, f8.weights[(i, "13")], kind=K.EPI_SWIGLU, out=s.u, out2=s.gu, half_n=F,
                        fp8=self._f8(i, "13", "x", E4, "w", E4))
-                u8, s.uT = f8.cast(s.u, f8.site(i, "2", "x"), E4)
+                u8 = s.uT = f8.cast(s.u, f8.site(i, "2", "x"), E4)
                 s.u = None
-                K.gemm(u8, f8.weights[(i, "2")][0], kind=K.EPI_RESID_F32, out=out, resid=s.h1,
+                K.gemm(u8, f8.weights[(i, "2")], kind=K.EPI_RESID_F32, out=out, resid=s.h1,
                        fp8=self._f8(i, "2", "x", E4, "w", E4))
             saved.append(s)
             x = out
@@ -493,34 +493,38 @@ class Backbone:
                 K.gemm(dgu, w["w13"], b_mn=True, kind=K.EPI_STORE_BF16, out=dn)
                 K.gemm(dgu, s.n2, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w13"])
             else:
-                g8, gT = f8.cast(dh16, f8.site(i, "2", "g"), E5)
-                K.gemm(g8, f8.weights[(i, "2")][1], kind=K.EPI_STORE_BF16, out=du,
+                g8 = f8.cast(dh16, f8.site(i, "2", "g"), E5)
+                K.gemm(g8, f8.weights[(i, "2")], b_mn=True, kind=K.EPI_STORE_BF16, out=du,
                        fp8=self._f8(i, "2", "g", E5, "w", E4))
                 K.swiglu_bwd(du, s.gu, dgu)
-                K.gemm(gT, s.uT, kind=K.EPI_ATOMIC_F32, out=g["w2"], fp8=self._f8(i, "2", "g", E5, "x", E4))
-                g8, gT = f8.cast(dgu, f8.site(i, "13", "g"), E5)
-                K.gemm(g8, f8.weights[(i, "13")][1], kind=K.EPI_STORE_BF16, out=dn,
+                K.gemm(g8, s.uT, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w2"],
+                       fp8=self._f8(i, "2", "g", E5, "x", E4))
+                g8 = f8.cast(dgu, f8.site(i, "13", "g"), E5)
+                K.gemm(g8, f8.weights[(i, "13")], b_mn=True, kind=K.EPI_STORE_BF16, out=dn,
                        fp8=self._f8(i, "13", "g", E5, "w", E4))
-                K.gemm(gT, s.n2T, kind=K.EPI_ATOMIC_F32, out=g["w13"], fp8=self._f8(i, "13", "g", E5, "x", E4))
+                K.gemm(g8, s.n2T, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w13"],
+                       fp8=self._f8(i, "13", "g", E5, "x", E4))
             K.rmsnorm_bwd(dn, s.h1, w["s2"], s.r2, dx=dh1, dx16=dh1_16, dscale=g["s2"], dres=dh)
             # attention block
             if f8 is None:
                 K.gemm(dh1_16, w["wo"], b_mn=True, kind=K.EPI_STORE_BF16, out=dao)
                 K.gemm(dh1_16, s.ao, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wo"])
             else:
-                g8, gT = f8.cast(dh1_16, f8.site(i, "o", "g"), E5)
-                K.gemm(g8, f8.weights[(i, "o")][1], kind=K.EPI_STORE_BF16, out=dao,
+                g8 = f8.cast(dh1_16, f8.site(i, "o", "g"), E5)
+                K.gemm(g8, f8.weights[(i, "o")], b_mn=True, kind=K.EPI_STORE_BF16, out=dao,
                        fp8=self._f8(i, "o", "g", E5, "w", E4))
-                K.gemm(gT, s.aoT, kind=K.EPI_ATOMIC_F32, out=g["wo"], fp8=self._f8(i, "o", "g", E5, "x", E4))
+                K.gemm(g8, s.aoT, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wo"],
+                       fp8=self._f8(i, "o", "g", E5, "x", E4))
             K.attn_bwd(s.qkv, s.ao, dao, s.lse, dsum, dqkv, nseq, n_causal, S, H, bid32, meta, rope=self.rope)
             if f8 is None:
                 K.gemm(dqkv, w["wqkv"], b_mn=True, kind=K.EPI_STORE_BF16, out=dn)
                 K.gemm(dqkv, s.n1, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wqkv"])
             else:
-                g8, gT = f8.cast(dqkv, f8.site(i, "qkv", "g"), E5)
-                K.gemm(g8, f8.weights[(i, "qkv")][1], kind=K.EPI_STORE_BF16, out=dn,
+                g8 = f8.cast(dqkv, f8.site(i, "qkv", "g"), E5)
+                K.gemm(g8, f8.weights[(i, "qkv")], b_mn=True, kind=K.EPI_STORE_BF16, out=dn,
                        fp8=self._f8(i, "qkv", "g", E5, "w", E4))
-                K.gemm(gT, s.n1T, kind=K.EPI_ATOMIC_F32, out=g["wqkv"], fp8=self._f8(i, "qkv", "g", E5, "x", E4))
+                K.gemm(g8, s.n1T, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wqkv"],
+                       fp8=self._f8(i, "qkv", "g", E5, "x", E4))
             K.rmsnorm_bwd(dn, s.x, w["s1"], s.r1, dx=dh, dx16=dh16, dscale=g["s1"], dres=dh1)
             if on_layer_done is not None:
                 on_layer_done(i)

@@ -3,17 +3,19 @@
 Every backbone linear (q|k|v, output projection, gate|up, down) runs its three
 GEMMs on the kind::f8f6f4 tensor cores:
 
-    forward   Y  = X  W^T        X, W in e4m3
-    backward  dX = dY W          dY in e5m2, W^T in e4m3
-              dW = dY^T X        dY^T in e5m2, X^T in e4m3
+    forward   Y  = X  W^T        X, W in e4m3 (K-major)
+    backward  dX = dY W          dY in e5m2, W in e4m3 read MN-major
+              dW = dY^T X        dY in e5m2, X in e4m3, both read MN-major
+
+so one row-major 8-bit copy of each tensor serves all three products (the
+tcgen05 MN-major operand layout is valid for e4m3 / e5m2).
 
 Each quantised tensor is a *site* with per-tensor delayed scaling: the scale
 used in step t is fmax / max(amax history of steps < t) (fmax 448 for e4m3,
 57344 for e5m2, history of 16 steps); the cast that quantises the tensor
 records its amax, and ``end_step`` pushes those into the histories.  In the
 first step (empty histories) each cast first measures its own tensor's amax
-("just in time").  Casts are saturating, round-to-nearest-even.  The K-major
-transposed copies (X^T, dY^T, W^T) come from the same cast kernel.
+("just in time").  Casts are saturating, round-to-nearest-even.
 
 The reference has no fp8 path: its linears run in fp16 under torch.autocast
 (chessdecoder/train/train.py:168).  Heads, norms, attention, softmax and the
@@ -51,7 +53,7 @@ class Fp8Recipe:
         self.scale = torch.ones(n, device=self.device)
         self.scale_inv = torch.ones(n, device=self.device)
         self.steps = 0  # completed end_step calls
-        self.weights = {}  # (layer, linear) -> (w8 [N, K], w8T [K, N])
+        self.weights = {}  # (layer, linear) -> w8 [N, K]
 
     def site(self, layer: int, lin: str, kind: str) -> int:
         return self.index[(layer, lin, kind)]
@@ -59,8 +61,9 @@ class Fp8Recipe:
     def sinv(self, i: int) -> torch.Tensor:
         return self.scale_inv[i:i + 1]
 
-    def cast(self, x: torch.Tensor, i: int, fmt: int, transpose: bool = True, row_major: bool = True):
-        """(x8 [rows, cols] or None, x8T [cols, rows] or None) of a 2-D fp32 / bf16 tensor."""
+    def cast(self, x: torch.Tensor, i: int, fmt: int, transpose: bool = False):
+        """8-bit copy [rows, cols] of a 2-D fp32 / bf16 tensor (and, with
+        transpose=True, also its [cols, rows] transpose: returns (x8, x8T))."""
         rows, cols = x.shape
         if self.steps == 0:
             K.fp8_amax(x, self.amax[i:i + 1])
@@ -70,10 +73,10 @@ class Fp8Recipe:
         else:
             amax = self.amax[i:i + 1]
         dt = torch.float8_e4m3fn if fmt == K.FP8_E4M3 else torch.float8_e5m2
-        x8 = _empty8(rows, cols, dt, self.device) if row_major else None
+        x8 = _empty8(rows, cols, dt, self.device)
         xt = _empty8(cols, rows, dt, self.device) if transpose else None
         K.fp8_cast(x, self.scale[i:i + 1], fmt, out=x8, out_t=xt, amax=amax)
-        return x8, xt
+        return (x8, xt) if transpose else x8
 
     def cast_weights(self, layer: int, ws: dict):
         """ws: linear name -> fp32 weight [N, K] (views of the master store)."""

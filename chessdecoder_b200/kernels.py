@@ -144,16 +144,16 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
 
     a: [M,K] (a_mn False) or [K,M] (a_mn True); b: [N,K] (b_mn False) or [K,N].
     For SWIGLU, b is [2N, K] = [gate; up] and N is the number of output columns.
-    fp8 = (a_fmt, b_fmt, scale_inv_a, scale_inv_b): 8-bit K-major operands
-    (FP8_E4M3 / FP8_E5M2) dequantised by the two device scalars.
+    fp8 = (a_fmt, b_fmt, scale_inv_a, scale_inv_b): 8-bit operands (FP8_E4M3 /
+    FP8_E5M2, same layouts as bf16) dequantised by the two device scalars.
     """
     _need_cuda(a, b, out)
     if fp8 is None:
         if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
             raise RuntimeError("GEMM inputs must be bf16")
     else:
-        if a.dtype not in _FP8_DTYPES or b.dtype not in _FP8_DTYPES or a_mn or b_mn:
-            raise RuntimeError("fp8 GEMM inputs must be 8-bit and K-major")
+        if a.dtype not in _FP8_DTYPES or b.dtype not in _FP8_DTYPES:
+            raise RuntimeError("fp8 GEMM inputs must be 8-bit")
     if M is None:
         M = a.shape[1] if a_mn else a.shape[0]
     if K is None:
@@ -191,8 +191,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
         _check(rc, f"gemm_bf16(kind={kind}, M={M}, N={N}, K={K}, a_mn={a_mn}, b_mn={b_mn})")
     else:
         af, bf, sa, sb = fp8
-        rc = lib().cdk_gemm_fp8(_p(a), a.stride(0), af, _p(b), b.stride(0), bf, M, N, K, _p(sa), _p(sb), C.byref(ep),
-                                split_k, _stream())
+        rc = lib().cdk_gemm_fp8(_p(a), a.stride(0), int(a_mn), af, _p(b), b.stride(0), int(b_mn), bf, M, N, K, _p(sa),
+                                _p(sb), C.byref(ep), split_k, _stream())
         _check(rc, f"gemm_fp8(kind={kind}, M={M}, N={N}, K={K}, fmt={af}{bf})")
     _count()
     if timer is not None:

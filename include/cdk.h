@@ -78,13 +78,14 @@ int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b, int64_t l
 /* ---- fp8 (the fp8 training variant: e4m3 weights / activations, e5m2
  *      gradients, per-tensor delayed scaling; no counterpart in the reference,
  *      whose GEMMs run through torch.autocast fp16) ----------------------------
- * cdk_gemm_fp8: C = epilogue((A B^T) * (*scale_inv_a) * (*scale_inv_b)) with A
- * [M, K] and B [N, K] 8-bit, both K-major (row pitch lda / ldb in bytes, a
- * multiple of 16); a_fmt / b_fmt: 0 = e4m3, 1 = e5m2 (they may differ).  Same
- * epilogue kinds and split-K rules as cdk_gemm_bf16. */
-int cdk_gemm_fp8(const void* a, int64_t lda, int a_fmt, const void* b, int64_t ldb, int b_fmt, int64_t M, int64_t N,
-                 int64_t K, const float* scale_inv_a, const float* scale_inv_b, const CdkGemmEpilogue* epi,
-                 int split_k, void* stream);
+ * cdk_gemm_fp8: C = epilogue((A B^T) * (*scale_inv_a) * (*scale_inv_b)) with
+ * 8-bit A and B laid out as in cdk_gemm_bf16 (a_mn / b_mn: MN-major, M / N a
+ * multiple of 16 then; row pitch lda / ldb in bytes, a multiple of 16); a_fmt /
+ * b_fmt: 0 = e4m3, 1 = e5m2 (they may differ).  Same epilogue kinds and
+ * split-K rules as cdk_gemm_bf16. */
+int cdk_gemm_fp8(const void* a, int64_t lda, int a_mn, int a_fmt, const void* b, int64_t ldb, int b_mn, int b_fmt,
+                 int64_t M, int64_t N, int64_t K, const float* scale_inv_a, const float* scale_inv_b,
+                 const CdkGemmEpilogue* epi, int split_k, void* stream);
 /* cdk_fp8_cast: out[r, c] = sat_fmt(x[r, c] * (*scale)) (round to nearest even,
  * saturating to the format's largest finite value); out_t (optional) [cols,
  * rows] receives the transpose (row pitch ldt bytes); amax (optional) is

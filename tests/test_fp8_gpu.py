@@ -52,6 +52,22 @@ def test_fp8_cast_transpose_amax(K, rows, cols, fmt, dtype):
     assert K.get_error() == 0
 
 
+@pytest.mark.parametrize("rows,cols", [(256, 512), (300, 1008), (3, 16)])
+@pytest.mark.parametrize("fmt", [0, 1])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fp8_cast_rows(K, rows, cols, fmt, dtype):
+    """Row-major cast without the transposed copy (the vectorised path)."""
+    g = torch.Generator(device=DEV).manual_seed(rows * cols + fmt)
+    x = (torch.randn(rows, cols, generator=g, device=DEV) * 5).to(dtype)
+    s = torch.tensor([30.0 if fmt == 0 else 500.0], device=DEV)
+    out = torch.zeros(rows, cols, device=DEV, dtype=torch.uint8)
+    amax = torch.zeros(1, device=DEV)
+    K.fp8_cast(x, s, fmt, out=out, amax=amax)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_cast(x, s, fmt).view(torch.uint8))
+    assert float(amax) == float(x.float().abs().max())
+
+
 def test_fp8_scales(K):
     n, hl = 5, 4
     amax = torch.tensor([1.0, 0.0, 10.0, 0.5, 2.0], device=DEV)
@@ -144,4 +160,33 @@ def test_fp8_gemm_epilogues(K):
     K.gemm(dYt, Xt, kind=K.EPI_ATOMIC_F32, out=dw, fp8=(1, 0, sa, sb))
     torch.cuda.synchronize()
     assert rel_err(dw, (dYt.float() @ Xt.float().t()) * 0.125) < 1e-5
+    assert K.get_error() == 0
+
+
+def _t8(x):
+    """Transposed contiguous copy of an 8-bit tensor (through its byte view)."""
+    return x.view(torch.uint8).t().contiguous().view(x.dtype)
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("M,N,K_", [(256, 384, 512), (1024, 1024, 4096), (128, 128, 256)])
+def test_fp8_gemm_mn_major(K, a_mn, b_mn, M, N, K_):
+    g = torch.Generator(device=DEV).manual_seed(M + 3 * N + K_ + int(a_mn) * 2 + int(b_mn))
+    A = _q((M, K_), 1, g, 1.0)
+    B = _q((N, K_), 0, g, 2.0)
+    sa = torch.tensor([0.25], device=DEV)
+    sb = torch.tensor([2.0], device=DEV)
+    a_arg = _t8(A) if a_mn else A
+    b_arg = _t8(B) if b_mn else B
+    ref = (A.float() @ B.float().t()) * 0.5
+    out = torch.empty(M, N, device=DEV)
+    K.gemm(a_arg, b_arg, a_mn=a_mn, b_mn=b_mn, kind=K.EPI_STORE_F32, out=out, M=M, N=N, K=K_, fp8=(1, 0, sa, sb))
+    torch.cuda.synchronize()
+    assert rel_err(out, ref) < 1e-5
+    if a_mn and b_mn:  # the weight-gradient form: split-K atomics into a zeroed fp32 buffer
+        acc = torch.zeros(M, N, device=DEV)
+        K.gemm(a_arg, b_arg, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=acc, M=M, N=N, K=K_,
+               fp8=(1, 0, sa, sb))
+        torch.cuda.synchronize()
+        assert rel_err(acc, ref) < 1e-5
     assert K.get_error() == 0
