@@ -47,6 +47,13 @@ SIGNATURES = {
     "cdk_fp8_cast": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _int, _vp, _i64, _vp, _i64, _vp, _vp]),
     "cdk_fp8_amax": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp]),
     "cdk_fp8_scales": (_int, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
+    "cdk_moe_route_workspace": (_i64, [_i64, _i32, _i32]),
+    "cdk_moe_route": (_int, [_vp, _i64, _i32, _i32, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "cdk_moe_dispatch": (_int, [_vp, _i64, _vp, _i64, _i64, _vp, _vp]),
+    "cdk_moe_combine": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "cdk_moe_combine_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _vp]),
+    "cdk_moe_route_bwd": (_int, [_vp, _vp, _vp, _i64, _i32, _vp, _i64, _vp]),
+    "cdk_moe_gather_sum": (_int, [_vp, _vp, _vp, _i64, _i64, _int, _vp]),
     "cdk_attn_prefix_meta": (_int, [_vp, _i64, _i64, _vp, _vp]),
     "cdk_attn_meta_elems": (_i64, [_i64, _i64]),
     "cdk_attn_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),

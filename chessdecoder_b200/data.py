@@ -65,10 +65,11 @@ def game_to_token_ids(plies, rng: random.Random, skip_board_prob: float = 0.0):
     return ids, move_targets, blocks, values
 
 
-def tensorize(ids, move_targets, blocks, values, rng: random.Random, max_seq_len: int):
-    """One training row (dict of 10 numpy arrays), as loader.py:69-184 builds it."""
+def tensorize(ids, move_targets, blocks, values, rng: random.Random, max_seq_len: int, random_start: bool = True):
+    """One training row (dict of 10 numpy arrays), as loader.py:69-184 builds it
+    (random_start=False keeps the sequence start, as the thinking rows need)."""
     valid_starts = [0] + [vd[1] + 1 for vd in values[:-1]]
-    start = rng.choice(valid_starts)
+    start = rng.choice(valid_starts) if random_start else 0
     ids = ids[start:]
     move_targets = [(m - start, b) for m, b in move_targets if m >= start]
     values = [(w - start, d - start, wl, dd, ok) for w, d, wl, dd, ok in values if d >= start]
@@ -169,3 +170,81 @@ def synthetic_batches(n_batches: int, batch_size: int, max_seq_len: int = 256, s
                       min_plies: int = 8, max_plies: int = 120, skip_board_prob: float = 0.2):
     src = SyntheticGames(max_seq_len, skip_board_prob, min_plies, max_plies, seed, rank)
     return [src.batch(batch_size) for _ in range(n_batches)]
+
+
+# ---------------------------------------------------------------------------
+# Thinking-variation rows (the MoE variant's long sequences)
+# ---------------------------------------------------------------------------
+def _wdl(rng: random.Random):
+    w, d = rng.random(), rng.random()
+    if w + d > 1.0:
+        w, d = 1.0 - w, 1.0 - d
+    return w - (1.0 - w - d), d
+
+
+def thinking_game_to_token_ids(rng: random.Random, min_lines=3, max_lines=6, min_depth=2, max_depth=8,
+                               max_opening=40):
+    """One thinking-variation sequence in the layout of
+    chessdecoder/finetune/data.py:144-247: root board block, ``start_think``,
+    then 3-6 candidate lines, each 2-8 plies of [move][wl_value][d_value]
+    [board68] and an ``end_var``, then ``end_think``, the final move and its
+    wl / d placeholders.  Positions come from a seeded random opening; lines
+    are seeded uniform-random legal continuations; WL / D targets are uniform
+    on the simplex.  Every board is its own block; each move is predicted from
+    the token before it (stm, ``start_think`` or ``end_var``, ``end_think``).
+    Returns (ids, move_targets, blocks, values) as ``game_to_token_ids``."""
+    from .chessgen import Position
+    while True:
+        pos = Position()
+        for _ in range(rng.randint(0, max_opening)):
+            moves = pos.legal_moves()
+            if not moves:
+                break
+            pos = pos.apply(moves[rng.randrange(len(moves))])
+        root_moves = pos.legal_moves()
+        if root_moves:
+            break
+    seq, move_targets, blocks, values = [], [], [], []
+    b0 = len(seq)
+    seq.extend(pos.position_tokens())
+    blocks.append((b0, len(seq)))
+    seq.append("start_think")
+    for _ in range(rng.randint(min_lines, max_lines)):
+        p = pos
+        for _ in range(rng.randint(min_depth, max_depth)):
+            moves = p.legal_moves()
+            if not moves:
+                break
+            chosen = moves[rng.randrange(len(moves))]
+            mv = Position.move_token(chosen)
+            move_targets.append((len(seq), mv))
+            seq.append(mv)
+            p = p.apply(chosen)
+            wl, dd = _wdl(rng)
+            values.append((len(seq), len(seq) + 1, wl, dd, True))
+            seq += ["wl_value", "d_value"]
+            b0 = len(seq)
+            seq.extend(p.position_tokens())
+            blocks.append((b0, len(seq)))
+        seq.append("end_var")
+    seq.append("end_think")
+    mv = Position.move_token(root_moves[rng.randrange(len(root_moves))])
+    move_targets.append((len(seq), mv))
+    seq.append(mv)
+    wl, dd = _wdl(rng)
+    values.append((len(seq), len(seq) + 1, wl, dd, True))
+    seq += ["wl_value", "d_value"]
+    return [V.token_to_idx[t] for t in seq], move_targets, blocks, values
+
+
+def thinking_batches(n_batches: int, batch_size: int, max_seq_len: int = 4096, seed: int = 0, rank: int = 0):
+    """Seeded batches of thinking-variation rows, padded / truncated to max_seq_len."""
+    rng = random.Random(seed + rank * 7919)
+    out = []
+    for _ in range(n_batches):
+        rows = []
+        for _ in range(batch_size):
+            ids, mt, blocks, values = thinking_game_to_token_ids(rng)
+            rows.append(tensorize(ids, mt, blocks, values, rng, max_seq_len, random_start=False))
+        out.append(collate(rows))
+    return out

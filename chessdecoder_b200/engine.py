@@ -48,6 +48,8 @@ class ModelConfig:
     value_hidden_size: int = 256
     num_fourier_freq: int = 128
     wl_sigma: float = 0.4
+    moe_experts: int = 0        # MoE variant: experts per layer (0 = the dense SwiGLU MLP)
+    moe_capacity: float = 1.25  # capacity factor (slots per expert = ceil(cf * 2 * tokens / experts))
 
     @property
     def head_dim(self):
@@ -92,12 +94,17 @@ def param_specs(cfg: ModelConfig):
         specs += [(f"{h}.mlp.0.weight", (hv, E)), (f"{h}.mlp.0.bias", (hv,)), (f"{h}.mlp.2.weight", (nb, hv)),
                   (f"{h}.mlp.2.bias", (nb,))]
     specs.append(("norm.scale", (E,)))
+    X = cfg.moe_experts
     for i in reversed(range(L)):
         p = f"layers.{i}."
         specs += [(p + "attn.q_proj.weight", (E, E)), (p + "attn.k_proj.weight", (E, E)),
-                  (p + "attn.v_proj.weight", (E, E)), (p + "attn.output_proj.weight", (E, E)),
-                  (p + "mlp.w1.weight", (F, E)), (p + "mlp.w3.weight", (F, E)), (p + "mlp.w2.weight", (E, F)),
-                  (p + "sa_norm.scale", (E,)), (p + "mlp_norm.scale", (E,))]
+                  (p + "attn.v_proj.weight", (E, E)), (p + "attn.output_proj.weight", (E, E))]
+        if X:
+            specs += [(p + "mlp.router.weight", (X, E)), (p + "mlp.experts.w13", (X, 2 * F, E)),
+                      (p + "mlp.experts.w2", (X, E, F))]
+        else:
+            specs += [(p + "mlp.w1.weight", (F, E)), (p + "mlp.w3.weight", (F, E)), (p + "mlp.w2.weight", (E, F))]
+        specs += [(p + "sa_norm.scale", (E,)), (p + "mlp_norm.scale", (E,))]
     specs += [("fourier_encoder.frequencies", (1, nf)), ("fourier_encoder.proj.weight", (E, 2 * nf)),
               ("fourier_encoder.proj.bias", (E,)), ("tok_embedding.weight", (cfg.vocab_size, E))]
     return specs
@@ -206,9 +213,22 @@ def init_reference_weights(cfg: ModelConfig, seed: int = 0) -> dict:
             p = f"layers.{i}."
             for n in ("q_proj", "k_proj", "v_proj", "output_proj"):
                 sd[p + f"attn.{n}.weight"] = nn.Linear(E, E, bias=False).weight.data
-            sd[p + "mlp.w1.weight"] = nn.Linear(E, F, bias=False).weight.data
-            sd[p + "mlp.w2.weight"] = nn.Linear(F, E, bias=False).weight.data
-            sd[p + "mlp.w3.weight"] = nn.Linear(E, F, bias=False).weight.data
+            if cfg.moe_experts:
+                # router, then per expert gate / down / up (oracle/moe.py construction order)
+                sd[p + "mlp.router.weight"] = nn.Linear(E, cfg.moe_experts, bias=False).weight.data
+                w13, w2 = [], []
+                for _ in range(cfg.moe_experts):
+                    gate = nn.Linear(E, F, bias=False).weight.data
+                    down = nn.Linear(F, E, bias=False).weight.data
+                    up = nn.Linear(E, F, bias=False).weight.data
+                    w13.append(torch.cat([gate, up], 0))
+                    w2.append(down)
+                sd[p + "mlp.experts.w13"] = torch.stack(w13)
+                sd[p + "mlp.experts.w2"] = torch.stack(w2)
+            else:
+                sd[p + "mlp.w1.weight"] = nn.Linear(E, F, bias=False).weight.data
+                sd[p + "mlp.w2.weight"] = nn.Linear(F, E, bias=False).weight.data
+                sd[p + "mlp.w3.weight"] = nn.Linear(E, F, bias=False).weight.data
             sd[p + "sa_norm.scale"] = torch.ones(E)
             sd[p + "mlp_norm.scale"] = torch.ones(E)
         sd["norm.scale"] = torch.ones(E)
@@ -354,7 +374,8 @@ def prepare_batch(batch: dict, device, require_pairing: bool = True) -> DeviceBa
 # Backbone (embedding output -> final RMSNorm), forward and backward
 # ---------------------------------------------------------------------------
 class LayerSaved:
-    __slots__ = ("x", "n1", "r1", "qkv", "ao", "lse", "h1", "n2", "r2", "gu", "u", "n1T", "aoT", "n2T", "uT")  # *T: fp8 copies
+    __slots__ = ("x", "n1", "r1", "qkv", "ao", "lse", "h1", "n2", "r2", "gu", "u", "n1T", "aoT", "n2T", "uT",
+                 "moe")  # *T: fp8 copies; moe: saved routing / expert buffers
 
 
 class Backbone:
@@ -378,6 +399,75 @@ class Backbone:
                 "13": st.span(p + "mlp.w1.weight", p + "mlp.w3.weight", st.flat).view(2 * F, E),
                 "2": st.param(p + "mlp.w2.weight")})
 
+    # -- MoE MLP (csrc/moe.cu; semantics restated by oracle/moe.py) ------------
+    def _moe_fwd(self, i, w, h1, n_seg, T, dev):
+        """Router -> top-2 / capacity slots -> per-expert SwiGLU GEMMs on the
+        expert-major rows -> weighted combine into the fp32 residual stream.
+        The router runs in fp32 (fp32 normalised input and weights) so that the
+        discrete top-2 / capacity decisions see fp32 logits."""
+        cfg = self.cfg
+        E, F, X = cfg.embed_dim, cfg.ff, cfg.moe_experts
+        cap = math.ceil(cfg.moe_capacity * 2 * (T // n_seg) / X)
+        rows_e = n_seg * cap
+        R = X * rows_e
+        n2 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+        n2_32 = torch.empty(T, E, device=dev)
+        r2 = torch.empty(T, device=dev)
+        K.rmsnorm_fwd(h1, w["s2"], y16=n2, y32=n2_32, rstd=r2)
+        logits = torch.empty(T, X, device=dev)
+        K.gemm_f32(n2_32, self.st.param(f"layers.{i}.mlp.router.weight"), logits)
+        del n2_32
+        m = {"n2": n2, "r2": r2, "rows_e": rows_e,
+             "expert": torch.empty(T, 2, dtype=torch.int32, device=dev), "weight": torch.empty(T, 2, device=dev),
+             "probs": torch.empty(T, X, device=dev), "slot": torch.empty(T, 2, dtype=torch.int32, device=dev)}
+        src = torch.empty(R, dtype=torch.int32, device=dev)
+        ws = torch.empty(K.moe_route_workspace(T, n_seg, X), dtype=torch.uint8, device=dev)
+        K.moe_route(logits, n_seg, cap, m["expert"], m["weight"], m["probs"], m["slot"], src, ws)
+        xe = torch.empty(R, E, device=dev, dtype=torch.bfloat16)
+        K.moe_dispatch(n2, src, xe)
+        gu = torch.empty(R, 2 * F, device=dev, dtype=torch.bfloat16)
+        u = torch.empty(R, F, device=dev, dtype=torch.bfloat16)
+        ye = torch.empty(R, E, device=dev, dtype=torch.bfloat16)
+        for e in range(X):
+            r = slice(e * rows_e, (e + 1) * rows_e)
+            K.gemm(xe[r], w["w13"][e], kind=K.EPI_SWIGLU, out=u[r], out2=gu[r], half_n=F)
+            K.gemm(u[r], w["w2"][e], kind=K.EPI_STORE_BF16, out=ye[r])
+        out = torch.empty(T, E, device=dev)
+        K.moe_combine(ye, m["slot"], m["weight"], h1, out)
+        m.update(xe=xe, gu=gu, u=u, ye=ye)
+        return out, m
+
+    def _moe_bwd(self, w, g, m, dh):
+        """Gradient of the MoE MLP: returns d(mlp_norm output) [T, E] fp32 and
+        accumulates the router / expert weight gradients."""
+        cfg = self.cfg
+        E, F, X = cfg.embed_dim, cfg.ff, cfg.moe_experts
+        T = dh.shape[0]
+        dev = dh.device
+        rows_e = m["rows_e"]
+        R = X * rows_e
+        dye = torch.empty(R, E, device=dev, dtype=torch.bfloat16)
+        dweight = torch.empty(T, 2, device=dev)
+        K.moe_combine_bwd(dh, m["ye"], m["slot"], m["weight"], dye, dweight)
+        du = torch.empty(R, F, device=dev, dtype=torch.bfloat16)
+        dgu = torch.empty(R, 2 * F, device=dev, dtype=torch.bfloat16)
+        dxe = torch.empty(R, E, device=dev, dtype=torch.bfloat16)
+        for e in range(X):
+            r = slice(e * rows_e, (e + 1) * rows_e)
+            K.gemm(dye[r], w["w2"][e], b_mn=True, kind=K.EPI_STORE_BF16, out=du[r])
+            K.gemm(dye[r], m["u"][r], a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w2"][e])
+            K.swiglu_bwd(du[r], m["gu"][r], dgu[r])
+            K.gemm(dgu[r], w["w13"][e], b_mn=True, kind=K.EPI_STORE_BF16, out=dxe[r])
+            K.gemm(dgu[r], m["xe"][r], a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w13"][e])
+        ldd = (X + 7) // 8 * 8
+        dlog = torch.empty(T, ldd, device=dev, dtype=torch.bfloat16)
+        K.moe_route_bwd(m["probs"], m["expert"], dweight, dlog)
+        dn = torch.empty(T, E, device=dev)
+        K.moe_gather_sum(dxe, m["slot"], dn)
+        K.gemm(dlog, w["router"], b_mn=True, kind=K.EPI_ACCUM_F32, out=dn, K=X)
+        K.gemm(dlog, m["n2"], a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["router"], M=X)
+        return dn
+
     def _f8(self, i, lin, a_kind, a_fmt, b_kind, b_fmt):
         f = self.fp8
         return (a_fmt, b_fmt, f.sinv(f.site(i, lin, a_kind)), f.sinv(f.site(i, lin, b_kind)))
@@ -386,18 +476,29 @@ class Backbone:
         st, p = self.st, f"layers.{i}."
         wqkv = st.span(p + "attn.q_proj.weight", p + "attn.v_proj.weight").view(3 * self.cfg.embed_dim,
                                                                                  self.cfg.embed_dim)
-        w13 = st.span(p + "mlp.w1.weight", p + "mlp.w3.weight").view(2 * self.cfg.ff, self.cfg.embed_dim)
-        return dict(wqkv=wqkv, wo=st.bf16(p + "attn.output_proj.weight"), w13=w13, w2=st.bf16(p + "mlp.w2.weight"),
-                    s1=st.param(p + "sa_norm.scale"), s2=st.param(p + "mlp_norm.scale"))
+        d = dict(wqkv=wqkv, wo=st.bf16(p + "attn.output_proj.weight"), s1=st.param(p + "sa_norm.scale"),
+                 s2=st.param(p + "mlp_norm.scale"))
+        if self.cfg.moe_experts:
+            d.update(router=st.bf16(p + "mlp.router.weight"), w13=st.bf16(p + "mlp.experts.w13"),
+                     w2=st.bf16(p + "mlp.experts.w2"))
+        else:
+            d.update(w13=st.span(p + "mlp.w1.weight", p + "mlp.w3.weight").view(2 * self.cfg.ff, self.cfg.embed_dim),
+                     w2=st.bf16(p + "mlp.w2.weight"))
+        return d
 
     def _g(self, i):
         st, p = self.st, f"layers.{i}."
         E, F = self.cfg.embed_dim, self.cfg.ff
         gqkv = st.span(p + "attn.q_proj.weight", p + "attn.v_proj.weight", st.grad).view(3 * E, E)
-        g13 = st.span(p + "mlp.w1.weight", p + "mlp.w3.weight", st.grad).view(2 * F, E)
-        return dict(wqkv=gqkv, wo=st.grad_of(p + "attn.output_proj.weight"), w13=g13,
-                    w2=st.grad_of(p + "mlp.w2.weight"), s1=st.grad_of(p + "sa_norm.scale"),
-                    s2=st.grad_of(p + "mlp_norm.scale"))
+        d = dict(wqkv=gqkv, wo=st.grad_of(p + "attn.output_proj.weight"), s1=st.grad_of(p + "sa_norm.scale"),
+                 s2=st.grad_of(p + "mlp_norm.scale"))
+        if self.cfg.moe_experts:
+            d.update(router=st.grad_of(p + "mlp.router.weight"), w13=st.grad_of(p + "mlp.experts.w13"),
+                     w2=st.grad_of(p + "mlp.experts.w2"))
+        else:
+            d.update(w13=st.span(p + "mlp.w1.weight", p + "mlp.w3.weight", st.grad).view(2 * F, E),
+                     w2=st.grad_of(p + "mlp.w2.weight"))
+        return d
 
     def forward(self, h, nseq, n_causal, S, bid32=None, meta=None, want_f32=False):
         cfg = self.cfg
@@ -408,6 +509,8 @@ class Backbone:
         x = h
         f8 = self.fp8
         E4, E5 = K.FP8_E4M3, K.FP8_E5M2
+        # MoE capacity is per forward pass: the merged batch routes its two halves separately
+        n_seg = 2 if 0 < n_causal < nseq and 2 * n_causal == nseq else 1
         for i in range(cfg.num_layers):
             w = self._w(i)
             s = LayerSaved()
@@ -433,6 +536,12 @@ class Backbone:
                 a8 = s.aoT = f8.cast(s.ao, f8.site(i, "o", "x"), E4)
                 K.gemm(a8, f8.weights[(i, "o")], kind=K.EPI_RESID_F32, out=s.h1, resid=x,
                        fp8=self._f8(i, "o", "x", E4, "w", E4))
+            if cfg.moe_experts:
+                out, s.moe = self._moe_fwd(i, w, s.h1, n_seg, T, dev)
+                s.n2, s.r2 = s.moe["n2"], s.moe["r2"]
+                saved.append(s)
+                x = out
+                continue
             s.n2 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
             s.r2 = torch.empty(T, device=dev)
             K.rmsnorm_fwd(s.h1, w["s2"], y16=s.n2, rstd=s.r2)
@@ -485,7 +594,10 @@ class Backbone:
         for i in reversed(range(cfg.num_layers)):
             s = saved[i]
             w, g = self._w(i), self._g(i)
-            if f8 is None:
+            if cfg.moe_experts:
+                dn_moe = self._moe_bwd(w, g, s.moe, dh)
+                K.rmsnorm_bwd(dn_moe, s.h1, w["s2"], s.r2, dx=dh1, dx16=dh1_16, dscale=g["s2"], dres=dh)
+            elif f8 is None:
                 # MLP block: du = dh W2 (plain GEMM), then the coalesced SwiGLU backward
                 K.gemm(dh16, w["w2"], b_mn=True, kind=K.EPI_STORE_BF16, out=du)
                 K.swiglu_bwd(du, s.gu, dgu)
@@ -504,7 +616,8 @@ class Backbone:
                        fp8=self._f8(i, "13", "g", E5, "w", E4))
                 K.gemm(g8, s.n2T, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w13"],
                        fp8=self._f8(i, "13", "g", E5, "x", E4))
-            K.rmsnorm_bwd(dn, s.h1, w["s2"], s.r2, dx=dh1, dx16=dh1_16, dscale=g["s2"], dres=dh)
+            if not cfg.moe_experts:
+                K.rmsnorm_bwd(dn, s.h1, w["s2"], s.r2, dx=dh1, dx16=dh1_16, dscale=g["s2"], dres=dh)
             # attention block
             if f8 is None:
                 K.gemm(dh1_16, w["wo"], b_mn=True, kind=K.EPI_STORE_BF16, out=dao)
@@ -689,6 +802,8 @@ class TrainStep:
         sd = state_dict if state_dict is not None else init_reference_weights(cfg, seed)
         self.store.load_state_dict({k: v.to(self.device) for k, v in sd.items()})
         self.fp8 = None
+        if fp8 and cfg.moe_experts:
+            raise ValueError("the fp8 recipe covers the dense MLP only; the MoE variant runs in bf16")
         if fp8:
             from .fp8 import Fp8Recipe
             self.fp8 = Fp8Recipe(cfg.num_layers, self.device)

@@ -442,3 +442,58 @@ def adamw(p, g, m, v, p_bf16, partial, *, max_norm, lr, beta1, beta2, eps, wd, s
                          float(beta2), float(eps), float(wd), int(step), float(grad_scale), _stream())
     _check(rc, "adamw")
     _count(1)
+
+
+# ---------------------------------------------------------------------------
+# Mixture of experts
+# ---------------------------------------------------------------------------
+@_timed("moe_route")
+def moe_route(logits, n_seg, cap, expert, weight, probs, slot, src, workspace):
+    T, X = logits.shape
+    _check(lib().cdk_moe_route(_p(logits), T, X, n_seg, cap, _p(expert), _p(weight), _p(probs), _p(slot), _p(src),
+                               _p(workspace), _stream()), "moe_route")
+    _count(4)
+
+
+def moe_route_workspace(T, n_seg, X):
+    n = int(lib().cdk_moe_route_workspace(T, n_seg, X))
+    if n < 0:
+        raise RuntimeError("moe_route_workspace: token count must split into equal segments")
+    return n
+
+
+@_timed("moe_dispatch")
+def moe_dispatch(x, src, xe):
+    _check(lib().cdk_moe_dispatch(_p(x), x.stride(0), _p(src), xe.shape[0], xe.shape[1], _p(xe), _stream()),
+           "moe_dispatch")
+    _count(1)
+
+
+@_timed("moe_combine")
+def moe_combine(ye, slot, weight, resid, out):
+    T, dim = out.shape
+    _check(lib().cdk_moe_combine(_p(ye), _p(slot), _p(weight), _p(resid), _p(out), T, dim, _stream()), "moe_combine")
+    _count(1)
+
+
+@_timed("moe_combine_bwd")
+def moe_combine_bwd(dout, ye, slot, weight, dye, dweight):
+    T, dim = dout.shape
+    _check(lib().cdk_moe_combine_bwd(_p(dout), _p(ye), _p(slot), _p(weight), _p(dye), dye.shape[0], _p(dweight), T,
+                                     dim, _stream()), "moe_combine_bwd")
+    _count(1)
+
+
+@_timed("moe_route_bwd")
+def moe_route_bwd(probs, expert, dweight, dlogits):
+    T, X = probs.shape
+    _check(lib().cdk_moe_route_bwd(_p(probs), _p(expert), _p(dweight), T, X, _p(dlogits), dlogits.stride(0),
+                                   _stream()), "moe_route_bwd")
+    _count(1)
+
+
+@_timed("moe_gather_sum")
+def moe_gather_sum(dxe, slot, out, accumulate=False):
+    T, dim = out.shape
+    _check(lib().cdk_moe_gather_sum(_p(dxe), _p(slot), _p(out), T, dim, int(accumulate), _stream()), "moe_gather_sum")
+    _count(1)

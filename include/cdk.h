@@ -103,6 +103,38 @@ int cdk_fp8_amax(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t
 int cdk_fp8_scales(float* amax_cur, float* history, float* scale, float* scale_inv, const float* fmax, int32_t n,
                    int32_t hist_len, int32_t mode, void* stream);
 
+/* ---- mixture of experts (the MoE variant: X experts, top-2 routing,
+ *      capacity-limited; no counterpart in the reference, whose MLP is one
+ *      dense SwiGLU per layer, chessdecoder/models/model.py:104-108) ---------
+ * cdk_moe_route: from router logits [T, X] (fp32): probs = softmax [T, X],
+ * expert / weight [T, 2] = top-2 (lower index on ties) with weights
+ * renormalised over the two; then, inside each of n_seg equal token segments,
+ * every expert gets `cap` slots filled by the first choices in token order and
+ * then the second choices in token order; slot [T, 2] = row of the
+ * expert-major buffers (e * n_seg * cap + seg * cap + position) or -1 when the
+ * expert was full; src [X * n_seg * cap] = token of each row or -1.
+ * workspace: cdk_moe_route_workspace(T, n_seg, X) bytes. */
+int64_t cdk_moe_route_workspace(int64_t T, int32_t n_seg, int32_t X);
+int cdk_moe_route(const float* logits, int64_t T, int32_t X, int32_t n_seg, int64_t cap, int32_t* expert,
+                  float* weight, float* probs, int32_t* slot, int32_t* src, void* workspace, void* stream);
+/* xe[r] = x[src[r]] (bf16 rows, zero when src[r] < 0). */
+int cdk_moe_dispatch(const void* x, int64_t ldx, const int32_t* src, int64_t rows, int64_t dim, void* xe,
+                     void* stream);
+/* out[t] = resid[t] + sum_k weight[t,k] * ye[slot[t,k]] (ye bf16, out / resid fp32; dropped slots skipped). */
+int cdk_moe_combine(const void* ye, const int32_t* slot, const float* weight, const float* resid, float* out,
+                    int64_t T, int64_t dim, void* stream);
+/* dye (bf16, dye_rows rows, zeroed first)[slot[t,k]] = weight[t,k] * dout[t];
+ * dweight[t,k] = dout[t] . ye[slot[t,k]] (0 when dropped). */
+int cdk_moe_combine_bwd(const float* dout, const void* ye, const int32_t* slot, const float* weight, void* dye,
+                        int64_t dye_rows, float* dweight, int64_t T, int64_t dim, void* stream);
+/* dlogits (bf16 [T, ldd], ldd in [X, 32]) = d(loss)/d(router logits) through the
+ * renormalised top-2 weights and the softmax. */
+int cdk_moe_route_bwd(const float* probs, const int32_t* expert, const float* dweight, int64_t T, int32_t X,
+                      void* dlogits, int64_t ldd, void* stream);
+/* out[t] (accumulate ? += : =) sum_k dxe[slot[t,k]] (dxe bf16, out fp32). */
+int cdk_moe_gather_sum(const void* dxe, const int32_t* slot, float* out, int64_t T, int64_t dim, int accumulate,
+                       void* stream);
+
 /* ---- attention -----------------------------------------------------------
  * Replaces torchtune MultiHeadAttention's SDPA call as used by
  * chessdecoder/models/model.py:158-171 (pass 1: is_causal; pass 2: bool mask

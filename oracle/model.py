@@ -121,7 +121,8 @@ class ValueHead(nn.Module):
 
 class OracleChessDecoder(nn.Module):
     def __init__(self, vocab_size, embed_dim=768, num_heads=12, num_layers=12, max_seq_len=2048, d_ff=None,
-                 n_buckets=100, value_hidden_size=256, num_fourier_freq=128, wl_sigma=0.4):
+                 n_buckets=100, value_hidden_size=256, num_fourier_freq=128, wl_sigma=0.4, moe_experts=0,
+                 moe_capacity=1.25):
         super().__init__()
         head_dim = embed_dim // num_heads
         d_ff = d_ff if d_ff is not None else 4 * embed_dim
@@ -134,11 +135,17 @@ class OracleChessDecoder(nn.Module):
             k = nn.Linear(embed_dim, embed_dim, bias=False)
             v = nn.Linear(embed_dim, embed_dim, bias=False)
             o = nn.Linear(embed_dim, embed_dim, bias=False)
-            gate = nn.Linear(embed_dim, d_ff, bias=False)
-            down = nn.Linear(d_ff, embed_dim, bias=False)
-            up = nn.Linear(embed_dim, d_ff, bias=False)
-            self.layers.append(Layer(Attention(q, k, v, o, num_heads, head_dim), FeedForward(gate, down, up),
-                                     RMSNorm(embed_dim), RMSNorm(embed_dim)))
+            if moe_experts:
+                # the MoE variant (oracle/moe.py): router + experts replace the dense FFN
+                from .moe import OracleMoE
+                mlp = OracleMoE(embed_dim, d_ff, moe_experts, moe_capacity)
+            else:
+                gate = nn.Linear(embed_dim, d_ff, bias=False)
+                down = nn.Linear(d_ff, embed_dim, bias=False)
+                up = nn.Linear(embed_dim, d_ff, bias=False)
+                mlp = FeedForward(gate, down, up)
+            self.layers.append(Layer(Attention(q, k, v, o, num_heads, head_dim), mlp, RMSNorm(embed_dim),
+                                     RMSNorm(embed_dim)))
         self.norm = RMSNorm(embed_dim)
         self.board_head = nn.Linear(embed_dim, BOARD_VOCAB_SIZE)
         self.policy_head = nn.Linear(embed_dim, MOVE_VOCAB_SIZE)
