@@ -47,7 +47,10 @@ def parse():
     ap.add_argument("--batch", type=int, default=None, help="per-GPU sequences (default 64; 128 with --fp8)")
     ap.add_argument("--fp8", action="store_true",
                     help="fp8 variant: backbone linears on e4m3 / e5m2 GEMMs with delayed scaling (per-GPU batch 128)")
-    ap.add_argument("--seq", type=int, default=256)
+    ap.add_argument("--moe", action="store_true",
+                    help="MoE variant: 8 experts, top-2, capacity 1.25, thinking-variation rows, S=4096, "
+                         "per-GPU batch 16")
+    ap.add_argument("--seq", type=int, default=None, help="sequence length (default 256; 4096 with --moe)")
     ap.add_argument("--layers", type=int, default=12)
     ap.add_argument("--pool", type=int, default=4, help="distinct synthetic batches per rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -59,10 +62,12 @@ def parse():
 def step_flops(cfg, db_list, S):
     """Algorithmic FLOPs of one step (6 * MACs-per-token * tokens for every
     linear that the loss needs, + attention over the allowed (q,k) pairs of both
-    passes), averaged over the batch pool."""
+    passes), averaged over the batch pool.  MoE: each token's MLP counts twice
+    (top-2 experts, no credit for dropped choices' padding) plus the router."""
     import numpy as np
     E, F, L = cfg.embed_dim, cfg.ff, cfg.num_layers
-    p_bb = L * (4 * E * E + 3 * E * F)
+    mlp = 3 * E * F * (2 if cfg.moe_experts else 1) + E * cfg.moe_experts
+    p_bb = L * (4 * E * E + mlp)
     out = []
     for b in db_list:
         B = b["input_ids"].shape[0]
@@ -71,9 +76,9 @@ def step_flops(cfg, db_list, S):
         pairs = B * S * (S + 1) // 2  # causal pass
         for r in range(B):
             ids = bid[r]
-            same = ids[:, None] == ids[None, :]
-            tri = np.tril(np.ones((S, S), dtype=bool))
-            pairs += int((same | tri).sum())
+            # causal pairs + the extra (future, same-block) pairs of each block
+            _, counts = np.unique(ids, return_counts=True)
+            pairs += S * (S + 1) // 2 + int((counts * (counts - 1) // 2).sum())
         nm = int(b["move_mask"].sum())
         nd = int(b["wl_positions"].sum())
         pv = E * cfg.value_hidden_size + cfg.value_hidden_size * cfg.n_buckets
@@ -200,7 +205,11 @@ def run_reference(args, rank, world):
 def main():
     args = parse()
     if args.batch is None:
-        args.batch = 128 if args.fp8 else 64
+        args.batch = 128 if args.fp8 else 16 if args.moe else 64
+    if args.seq is None:
+        args.seq = 4096 if args.moe else 256
+    if args.moe and args.fp8:
+        raise SystemExit("--moe and --fp8 are separate variants")
     from chessdecoder_b200.distributed import setup_distributed, cleanup_distributed
     rank, local_rank, world = setup_distributed() if args.gpus > 1 or "RANK" in os.environ else (0, 0, 1)
     if args.impl == "reference":
@@ -214,10 +223,13 @@ def main():
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    cfg = ModelConfig(num_layers=args.layers, max_seq_len=args.seq)
+    cfg = ModelConfig(num_layers=args.layers, max_seq_len=args.seq, moe_experts=8 if args.moe else 0)
     step = TrainStep(cfg, device=dev, seed=0, fp8=args.fp8)
     dp = DataParallelStep(step)
-    pool = data.synthetic_batches(args.pool, args.batch, args.seq, seed=1234, rank=rank)
+    if args.moe:
+        pool = data.thinking_batches(args.pool, args.batch, args.seq, seed=1234, rank=rank)
+    else:
+        pool = data.synthetic_batches(args.pool, args.batch, args.seq, seed=1234, rank=rank)
     dbs = [prepare_batch(b, dev) for b in pool]
     torch.cuda.synchronize()
 
@@ -321,7 +333,7 @@ def main():
                             "pool; the dense fp8 spec is 4.5 PFLOP/s)")
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.moe:
         cpu = cpu_baseline(pool[0], dict(embed_dim=1024, num_heads=16, num_layers=args.layers,
                                          max_seq_len=args.seq, d_ff=1536), args.cpu_steps)
     if rank == 0:
@@ -329,10 +341,11 @@ def main():
                 "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None,
                 "dtype": "fp8 (e4m3 activations/weights, e5m2 grads) backbone linears; bf16 attention and heads"
-                if args.fp8 else "bf16", "data": "synthetic",
+                if args.fp8 else "bf16", "data": "synthetic thinking-variation rows" if args.moe else "synthetic",
                 "config": {"workload": ("ChessDecoder pretraining step (pass-1 causal + pass-2 prefix fwd, bwd, "
                                         "clip, AdamW), default model E=1024 H=16 L=%d d_ff=1536" % args.layers)
-                           + (", fp8 variant (per-tensor delayed scaling, amax history 16)" if args.fp8 else ""),
+                           + (", fp8 variant (per-tensor delayed scaling, amax history 16)" if args.fp8 else "")
+                           + (", MoE variant (8 experts, top-2, capacity 1.25)" if args.moe else ""),
                            "global_batch": args.batch * world, "seq_len": args.seq,
                            "parallelism": f"dp{world}", "per_gpu_batch": args.batch,
                            "l2": "working set (activations ~11 GB) far larger than L2; no flush needed",
