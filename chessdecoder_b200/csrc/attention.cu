@@ -1105,10 +1105,11 @@ extern "C" int cdk_attn_prefix_meta(const int32_t* bid, int64_t nseq_prefix, int
   return e == cudaSuccess ? 0 : (int)e;
 }
 
-// Path selection for S <= 256: the tcgen05 kernels (attention_tc.cu) by
+// Path selection.  S <= 256: the tcgen05 kernels (attention_tc.cu) by
 // default; CDK_ATTN_PATH=seq selects the mma.sync sequence-resident kernels and
-// CDK_ATTN_PATH=tiled the tiled kernels (the tests cover all three).  S > 256
-// always takes the tiled kernels.
+// CDK_ATTN_PATH=tiled the tiled kernels (the tests cover all three).  S > 256:
+// the tcgen05 online-softmax forward (attention_long.cu) by default, the tiled
+// kernels with CDK_ATTN_PATH=tiled or seq; the backward uses the tiled kernels.
 static int attn_path() {
   const char* v = getenv("CDK_ATTN_PATH");
   if (v && v[0] == 't' && v[1] == 'i') return 2;  // tiled
@@ -1120,6 +1121,8 @@ static bool seq_path_enabled() { return attn_path() != 2; }
 namespace cdk {
 int launch_attn_fwd_tc(const void* qkv, void* out, float* lse, int64_t nseq, int64_t n_causal, int64_t S, int64_t H,
                        const int32_t* bid, const int32_t* meta, cudaStream_t stream);
+int launch_attn_fwd_long(const void* qkv, void* out, float* lse, int64_t nseq, int64_t n_causal, int64_t S,
+                         int64_t H, const int32_t* bid, const int32_t* meta, cudaStream_t stream);
 int launch_attn_bwd_tc(const void* qkv, const void* out, const void* dout, const float* lse, void* dqkv,
                        int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,
                        const int32_t* meta, const float* rope, cudaStream_t stream);
@@ -1154,6 +1157,9 @@ extern "C" int cdk_attn_fwd(const void* qkv, void* out, float* lse, int64_t nseq
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (S <= kSeqMax && attn_path() == 0) {
     return launch_attn_fwd_tc(qkv, out, lse, nseq, n_causal, S, H, bid, meta, s);
+  }
+  if (S > kSeqMax && attn_path() == 0) {
+    return launch_attn_fwd_long(qkv, out, lse, nseq, n_causal, S, H, bid, meta, s);
   }
   if (S <= kSeqMax && seq_path_enabled()) {
     CUtensorMap tq;

@@ -116,6 +116,7 @@ def main():
     ap.add_argument("--kind", default="rope", choices=["rope", "swiglu", "resid", "dx", "dw"])
     ap.add_argument("--fp8", action="store_true", help="8-bit operands (e4m3; e5m2 x e4m3 for dx / dw)")
     ap.add_argument("--nseq", type=int, default=128)
+    ap.add_argument("--seq", type=int, default=256, help="attention sequence length (> 256: thinking-row blocks)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     a = ap.parse_args()
@@ -126,16 +127,20 @@ def main():
         print(json.dumps({"probe": name, "ms": ms, "tflops": flops / ms / 1e9, "alg_bytes": nbytes,
                           "alg_gbs": nbytes / ms / 1e6}))
     elif a.mode == "attn":
-        S, H = 256, 16
+        S, H = a.seq, 16
         E = H * 64
         nseq, ncaus = a.nseq, a.nseq // 2
         g = torch.Generator().manual_seed(0)
         qkv = (torch.randn(nseq * S, 3 * E, generator=g) * 0.8).to("cuda").to(torch.bfloat16)
-        bid = (torch.arange(S) + 1000).repeat(nseq - ncaus, 1)
-        for r in range(nseq - ncaus):  # three 68-token board blocks per sequence
-            bid[r, 10:78] = 0
-            bid[r, 81:149] = 1
-            bid[r, 152:220] = 2
+        if S > 256:  # thinking-variation rows: a board block every 71 tokens
+            from .data import thinking_batches
+            bid = thinking_batches(1, nseq - ncaus, S, seed=0)[0]["block_id"]
+        else:
+            bid = (torch.arange(S) + 1000).repeat(nseq - ncaus, 1)
+            for r in range(nseq - ncaus):  # three 68-token board blocks per sequence
+                bid[r, 10:78] = 0
+                bid[r, 81:149] = 1
+                bid[r, 152:220] = 2
         bid32 = bid.to(torch.int32).cuda().contiguous()
         meta = K.attn_meta(bid32, S)
         out = torch.empty(nseq * S, E, device="cuda", dtype=torch.bfloat16)
@@ -150,7 +155,14 @@ def main():
         ms_b = _time(bwd, a.warmup, a.iters)
         bytes_f = qkv.numel() * 2 + out.numel() * 2
         bytes_b = qkv.numel() * 2 * 2 + out.numel() * 2 * 2
+        # allowed (query, key) pairs -> FLOPs (fwd 4*hd per pair, bwd 10*hd)
+        pairs = ncaus * S * (S + 1) // 2
+        for r in range(nseq - ncaus):
+            _, cnt = torch.unique(bid[r], return_counts=True)
+            pairs += S * (S + 1) // 2 + int((cnt * (cnt - 1) // 2).sum())
+        pairs *= H
         print(json.dumps({"probe": f"attention nseq={nseq} S={S} H={H}", "fwd_ms": ms_f, "bwd_ms": ms_b,
+                          "fwd_tflops": 4 * 64 * pairs / ms_f / 1e9, "bwd_tflops": 10 * 64 * pairs / ms_b / 1e9,
                           "fwd_alg_gbs": bytes_f / ms_f / 1e6, "bwd_alg_gbs": bytes_b / ms_b / 1e6,
                           "err": K.get_error()}))
     else:
