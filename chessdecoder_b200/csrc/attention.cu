@@ -1108,8 +1108,9 @@ extern "C" int cdk_attn_prefix_meta(const int32_t* bid, int64_t nseq_prefix, int
 // Path selection.  S <= 256: the tcgen05 kernels (attention_tc.cu) by
 // default; CDK_ATTN_PATH=seq selects the mma.sync sequence-resident kernels and
 // CDK_ATTN_PATH=tiled the tiled kernels (the tests cover all three).  S > 256:
-// the tcgen05 online-softmax forward (attention_long.cu) by default, the tiled
-// kernels with CDK_ATTN_PATH=tiled or seq; the backward uses the tiled kernels.
+// the tcgen05 kernels of attention_long.cu by default (the backward needs the
+// caller's fp32 dQ workspace, cdk_attn_bwd_ws), the tiled kernels with
+// CDK_ATTN_PATH=tiled or seq or without a workspace.
 static int attn_path() {
   const char* v = getenv("CDK_ATTN_PATH");
   if (v && v[0] == 't' && v[1] == 'i') return 2;  // tiled
@@ -1181,9 +1182,27 @@ extern "C" int cdk_attn_fwd(const void* qkv, void* out, float* lse, int64_t nseq
   return e == cudaSuccess ? 0 : (int)e;
 }
 
+namespace cdk {
+int launch_attn_bwd_long(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,
+                         void* dqkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,
+                         const int32_t* meta, const float* rope, void* workspace, cudaStream_t stream);
+}  // namespace cdk
+
+extern "C" int64_t cdk_attn_bwd_workspace(int64_t nseq, int64_t S, int64_t H) {
+  if (nseq < 0 || S <= 0 || H <= 0) return -1;
+  return S > kSeqMax ? nseq * S * H * kHd * (int64_t)sizeof(float) : 0;
+}
+
 extern "C" int cdk_attn_bwd(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,
                             void* dqkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,
                             const int32_t* meta, const float* rope, void* stream) {
+  return cdk_attn_bwd_ws(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid, meta, rope, nullptr, 0, stream);
+}
+
+extern "C" int cdk_attn_bwd_ws(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,
+                               void* dqkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,
+                               const int32_t* meta, const float* rope, void* workspace, int64_t workspace_bytes,
+                               void* stream) {
   int rc = attn_check(qkv, nseq, n_causal, S, H, meta);
   if (rc) return rc;
   if (!out || !dout || !lse || !dsum || !dqkv) return -1;
@@ -1210,6 +1229,12 @@ extern "C" int cdk_attn_bwd(const void* qkv, const void* out, const void* dout, 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (S <= kSeqMax && attn_path() == 0)
     return launch_attn_bwd_tc(qkv, out, dout, lse, dqkv, nseq, n_causal, S, H, bid, meta, rope, s);
+  if (S > kSeqMax && attn_path() == 0 && workspace != nullptr) {
+    if (workspace_bytes < cdk_attn_bwd_workspace(nseq, S, H) || (reinterpret_cast<uintptr_t>(workspace) & 15))
+      return -5;
+    return launch_attn_bwd_long(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid, meta, rope, workspace,
+                                s);
+  }
   if (S <= kSeqMax && seq_path_enabled()) {
     CUtensorMap tq, tdo;
     if (!make_tmap(&tq, qkv, 3 * H * kHd, nseq * S, 3 * H * kHd, 64, 64)) return -10;

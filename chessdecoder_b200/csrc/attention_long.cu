@@ -292,6 +292,377 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
 }
 
+
+// ===========================================================================
+// Backward for S > 256.  One CTA per (128-key tile, head, sequence) walks the
+// 128-query tiles that can see the key tile:
+//   MMA-A  S^T = K Q_t^T, dP^T = V dO_t^T                  (TMEM, 128 cols each)
+//   EW     P^T = exp2(S^T c - L), dS^T = P^T (dP^T - D)    (bf16 operands in smem)
+//   MMA-B  dV += P^T dO_t, dK += dS^T Q_t                  (TMEM, accumulated)
+//          dQ_t = dS K                                      (TMEM, per query tile)
+// and the elementwise warps add dQ_t into an fp32 [tokens, E] accumulator with
+// vector atomics while the next tile's products run.  D = rowsum(dO * O) comes
+// from a pass before; a pass after scales dQ by 1/8, undoes RoPE and writes it
+// into dqkv.  TMEM: S^T | dP^T | dV | dK | dQ = 448 of 512 columns.
+// ===========================================================================
+constexpr int kQStages = 3;
+constexpr int kBwdThreads = 576;  // warp 0 TMA, warp 1 MMA, warps 2-17 elementwise
+
+struct BwdSmem {
+  uint8_t K[2 * kTileBytes];
+  uint8_t V[2 * kTileBytes];
+  uint8_t Q[kQStages][2 * kTileBytes];
+  uint8_t dO[kQStages][2 * kTileBytes];
+  uint8_t PT[2][128 * 128];   // [64-query block][128 key rows x 64 queries]
+  uint8_t dST[2][128 * 128];
+  uint64_t bar_kv, bar_full[kQStages], bar_empty[kQStages], bar_sa, bar_ew, bar_mb, bar_dq;
+  uint32_t tmem_base;
+  int abort;
+  int q_first, n_q;
+};
+static_assert(offsetof(BwdSmem, V) % 1024 == 0 && offsetof(BwdSmem, Q) % 1024 == 0 &&
+                  offsetof(BwdSmem, dO) % 1024 == 0 && offsetof(BwdSmem, PT) % 1024 == 0 &&
+                  offsetof(BwdSmem, dST) % 1024 == 0,
+              "TMA / UMMA operands with the 128-byte swizzle need 1024-byte alignment");
+
+struct LongBwdArgs {
+  const float* lse;           // [nseq, H, S]
+  const float* dsum;          // [nseq, H, S]  D = rowsum(dO * O)
+  float* dq;                  // [nseq * S, E] fp32 accumulator (zeroed)
+  __nv_bfloat16* dqkv;
+  const int32_t* bid;         // [nseq - n_causal, S]
+  const int32_t* first;       // [nseq - n_causal, S]
+  const int32_t* q_lo;        // [nseq - n_causal][2 * nt64] (+ nt64 within a sequence's slice)
+  const float* rope;
+  int S, H, n_causal, nt64;
+};
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_long_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo,
+                         const LongBwdArgs a) {
+  extern __shared__ uint8_t raw[];
+  BwdSmem& sm = *reinterpret_cast<BwdSmem*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  const int kt = blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
+  const int S = a.S, E = a.H * kHd;
+  const long long ld = 3ll * E;
+  const bool prefix = seq >= a.n_causal;
+  const int pseq = seq - a.n_causal;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row_base = seq * S;
+  const long long lrow = ((long long)seq * a.H + h) * S;
+  volatile int* abort_flag = &sm.abort;
+  const int nqt = (S + kBQ - 1) / kBQ;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.bar_kv, 1);
+    for (int b = 0; b < kQStages; ++b) {
+      mbar_init(&sm.bar_full[b], 1);
+      mbar_init(&sm.bar_empty[b], 1);
+    }
+    mbar_init(&sm.bar_sa, 1);
+    mbar_init(&sm.bar_ew, 512);
+    mbar_init(&sm.bar_mb, 1);
+    mbar_init(&sm.bar_dq, 512);
+    sm.abort = 0;
+    // first query tile that can see this key tile: causal -> the diagonal one;
+    // prefix -> the lowest query row of the key rows' blocks (metadata)
+    int q0 = kt * kBQ;
+    if (prefix) {
+      const int* ql = a.q_lo + (long long)pseq * 2 * a.nt64 + a.nt64;
+      for (int t = 2 * kt; t < min(2 * kt + 2, a.nt64); ++t) q0 = min(q0, ql[t]);
+    }
+    sm.q_first = q0 / kBQ;
+    sm.n_q = nqt - q0 / kBQ;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const int q_first = sm.q_first, n_q = sm.n_q;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tqkv);
+      prefetch_tmap(&tdo);
+      mbar_arrive_expect_tx(&sm.bar_kv, 4 * kTileBytes);
+      for (int t = 0; t < 2; ++t) {
+        const int r0 = row_base + kt * kBK + t * 64;
+        tma_load_2d(sm.K + t * kTileBytes, &tqkv, &sm.bar_kv, E + h * kHd, r0);
+        tma_load_2d(sm.V + t * kTileBytes, &tqkv, &sm.bar_kv, 2 * E + h * kHd, r0);
+      }
+      for (int it = 0; it < n_q; ++it) {
+        const int st = it % kQStages;
+        mbar_wait(&sm.bar_empty[st], ((it / kQStages) & 1) ^ 1u, abort_flag);
+        mbar_arrive_expect_tx(&sm.bar_full[st], 4 * kTileBytes);
+        for (int t = 0; t < 2; ++t) {
+          const int r0 = row_base + (q_first + it) * kBQ + t * 64;
+          tma_load_2d(sm.Q[st] + t * kTileBytes, &tqkv, &sm.bar_full[st], h * kHd, r0);
+          tma_load_2d(sm.dO[st] + t * kTileBytes, &tdo, &sm.bar_full[st], h * kHd, r0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t kb = smem_u32(sm.K), vb = smem_u32(sm.V);
+      const uint32_t ptb = smem_u32(sm.PT[0]), dsb = smem_u32(sm.dST[0]);
+      const uint32_t id_s = make_idesc_bf16(128, 128, false, false);
+      const uint32_t id_kn = make_idesc_bf16(128, kHd, false, true);
+      const uint32_t id_nn = make_idesc_bf16(128, kHd, true, true);
+      mbar_wait(&sm.bar_kv, 0, abort_flag);
+      auto issue_a = [&](int it) {
+        const int st = it % kQStages;
+        mbar_wait(&sm.bar_full[st], (it / kQStages) & 1, abort_flag);
+        tc_fence_after();
+        const uint32_t qb = smem_u32(sm.Q[st]), ob = smem_u32(sm.dO[st]);
+        #pragma unroll
+        for (int kk = 0; kk < kHd / 16; ++kk) {
+          umma_f16(tmem, make_sdesc(kb + kk * 32, 16, 1024), make_sdesc(qb + kk * 32, 16, 1024), id_s,
+                   kk > 0 ? 1u : 0u);
+          umma_f16(tmem + 128, make_sdesc(vb + kk * 32, 16, 1024), make_sdesc(ob + kk * 32, 16, 1024), id_s,
+                   kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&sm.bar_sa);
+      };
+      if (n_q > 0) issue_a(0);
+      for (int it = 0; it < n_q; ++it) {
+        const int st = it % kQStages;
+        const uint32_t qb = smem_u32(sm.Q[st]), ob = smem_u32(sm.dO[st]);
+        mbar_wait(&sm.bar_ew, it & 1, abort_flag);
+        if (it > 0) mbar_wait(&sm.bar_dq, (it - 1) & 1, abort_flag);
+        tc_fence_after();
+        #pragma unroll 1
+        for (int kk = 0; kk < 8; ++kk) {  // 128 queries
+          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+          const uint64_t a_pt = make_sdesc(ptb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+          const uint64_t a_ds = make_sdesc(dsb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+          umma_f16(tmem + 256, a_pt, make_sdesc(ob + kk * 2048, 8192, 1024), id_kn, acc);
+          umma_f16(tmem + 320, a_ds, make_sdesc(qb + kk * 2048, 8192, 1024), id_kn, acc);
+        }
+        #pragma unroll 1
+        for (int kk = 0; kk < 8; ++kk)  // 128 keys
+          umma_f16(tmem + 384, make_sdesc(dsb + kk * 2048, 16384, 1024), make_sdesc(kb + kk * 2048, 8192, 1024),
+                   id_nn, kk > 0 ? 1u : 0u);
+        tc_commit(&sm.bar_mb);
+        tc_commit(&sm.bar_empty[st]);
+        if (it + 1 < n_q) issue_a(it + 1);
+      }
+    }
+  } else {
+    const int ew = warp - 2;
+    const int g = ew >> 2;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const float sl2 = 0.125f * kLog2e;
+    const int j = kt * kBK + r;  // this thread's key
+    const bool jok = j < S;
+    const int32_t* bidrow = prefix ? a.bid + (long long)pseq * S : nullptr;
+    const int fj = jok ? (prefix ? a.first[(long long)pseq * S + j] : j) : S;
+    const int bj = (jok && prefix) ? bidrow[j] : -2;
+    auto dq_atomics = [&](int qt_prev, const uint32_t (&dqv)[16]) {
+      const int qi = qt_prev * kBQ + r;  // lane = query row for dQ
+      if (qi < S) {
+        float4* dst = reinterpret_cast<float4*>(a.dq + (long long)(row_base + qi) * E + h * kHd + g * 16);
+        #pragma unroll
+        for (int q = 0; q < 4; ++q)
+          atomicAdd(dst + q, make_float4(__uint_as_float(dqv[4 * q]), __uint_as_float(dqv[4 * q + 1]),
+                                         __uint_as_float(dqv[4 * q + 2]), __uint_as_float(dqv[4 * q + 3])));
+      }
+    };
+    for (int it = 0; it < n_q; ++it) {
+      const int qt = q_first + it;
+      const int qb = qt * kBQ + g * 32;
+      const bool full = jok && qb >= j && qb + 31 < S;
+      const bool none = !jok || qb + 31 < fj || qb >= S;
+      const bool none_w = __all_sync(0xffffffffu, none);
+      mbar_wait(&sm.bar_sa, it & 1, abort_flag);
+      tc_fence_after();
+      if (it > 0) {  // dQ of the previous query tile (its products retired before this S^T)
+        uint32_t dqv[16];
+        tmem_ld_x16_nowait(tmem + lane_off + 384 + g * 16, dqv);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&sm.bar_dq);
+        dq_atomics(qt - 1, dqv);
+      }
+      uint8_t* pt = sm.PT[g >> 1];
+      uint8_t* dst = sm.dST[g >> 1];
+      const int cbase = (g & 1) * 32;
+      #pragma unroll
+      for (int sc = 0; sc < 2; ++sc) {
+        uint32_t pk[8], dk[8];
+        if (none_w || none) {
+          #pragma unroll
+          for (int e = 0; e < 8; ++e) pk[e] = dk[e] = 0u;
+        }
+        if (!none_w) {
+          uint32_t su[16], du[16];
+          tmem_ld_x16_nowait(tmem + lane_off + g * 32 + sc * 16, su);
+          tmem_ld_x16_nowait(tmem + lane_off + 128 + g * 32 + sc * 16, du);
+          tmem_wait_ld();
+          if (!none) {
+            // L and D of these 16 queries (the same addresses in every lane)
+            float Lv[16], Dv[16];
+            #pragma unroll
+            for (int e4 = 0; e4 < 4; ++e4) {
+              const int q = qb + sc * 16 + e4 * 4;
+              float4 l4, d4;
+              if (q + 3 < S && (S & 3) == 0) {
+                l4 = *reinterpret_cast<const float4*>(a.lse + lrow + q);
+                d4 = *reinterpret_cast<const float4*>(a.dsum + lrow + q);
+              } else {
+                l4.x = q < S ? a.lse[lrow + q] : 0.f;
+                l4.y = q + 1 < S ? a.lse[lrow + q + 1] : 0.f;
+                l4.z = q + 2 < S ? a.lse[lrow + q + 2] : 0.f;
+                l4.w = q + 3 < S ? a.lse[lrow + q + 3] : 0.f;
+                d4.x = q < S ? a.dsum[lrow + q] : 0.f;
+                d4.y = q + 1 < S ? a.dsum[lrow + q + 1] : 0.f;
+                d4.z = q + 2 < S ? a.dsum[lrow + q + 2] : 0.f;
+                d4.w = q + 3 < S ? a.dsum[lrow + q + 3] : 0.f;
+              }
+              Lv[e4 * 4] = l4.x; Lv[e4 * 4 + 1] = l4.y; Lv[e4 * 4 + 2] = l4.z; Lv[e4 * 4 + 3] = l4.w;
+              Dv[e4 * 4] = d4.x; Dv[e4 * 4 + 1] = d4.y; Dv[e4 * 4 + 2] = d4.z; Dv[e4 * 4 + 3] = d4.w;
+            }
+            #pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              float pv[2], dsv[2];
+              #pragma unroll
+              for (int k = 0; k < 2; ++k) {
+                const int ee = sc * 16 + e + k;
+                const float p = ex2_approx(fmaf(__uint_as_float(su[e + k]), sl2, -Lv[e + k]));
+                pv[k] = p;
+                dsv[k] = p * (__uint_as_float(du[e + k]) - Dv[e + k]);
+                if (!full) {
+                  const int i = qb + ee;
+                  bool vis = i < S && (i >= j || (i >= fj && bidrow != nullptr && bidrow[i] == bj));
+                  pv[k] = vis ? pv[k] : 0.f;
+                  dsv[k] = vis ? dsv[k] : 0.f;
+                }
+              }
+              pk[e >> 1] = pack_bf16(pv[0], pv[1]);
+              dk[e >> 1] = pack_bf16(dsv[0], dsv[1]);
+            }
+          }
+        }
+        #pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const uint32_t off = sw128(r, cbase + sc * 16 + q * 8);
+          *reinterpret_cast<uint4*>(pt + off) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          *reinterpret_cast<uint4*>(dst + off) = make_uint4(dk[4 * q], dk[4 * q + 1], dk[4 * q + 2], dk[4 * q + 3]);
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(&sm.bar_ew);
+    }
+    if (n_q > 0) {
+      mbar_wait(&sm.bar_mb, (n_q - 1) & 1, abort_flag);
+      tc_fence_after();
+      uint32_t dqv[16], vv[16], kv[16];
+      tmem_ld_x16_nowait(tmem + lane_off + 384 + g * 16, dqv);
+      tmem_ld_x16_nowait(tmem + lane_off + 256 + g * 16, vv);
+      tmem_ld_x16_nowait(tmem + lane_off + 320 + g * 16, kv);
+      tmem_wait_ld();
+      dq_atomics(q_first + n_q - 1, dqv);
+      if (jok) {
+        float dkf[16];
+        #pragma unroll
+        for (int e = 0; e < 16; ++e) dkf[e] = __uint_as_float(kv[e]) * 0.125f;
+        if (a.rope != nullptr) {
+          const float4* cs = reinterpret_cast<const float4*>(a.rope + ((long long)j * 32 + g * 8) * 2);
+          #pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const float4 t = cs[p];
+            float x0 = dkf[4 * p], x1 = dkf[4 * p + 1];
+            dkf[4 * p] = x0 * t.x + x1 * t.y;
+            dkf[4 * p + 1] = x1 * t.x - x0 * t.y;
+            x0 = dkf[4 * p + 2];
+            x1 = dkf[4 * p + 3];
+            dkf[4 * p + 2] = x0 * t.z + x1 * t.w;
+            dkf[4 * p + 3] = x1 * t.z - x0 * t.w;
+          }
+        }
+        __nv_bfloat16* rowp = a.dqkv + (long long)(row_base + j) * ld;
+        uint4* dkp = reinterpret_cast<uint4*>(rowp + E + h * kHd + g * 16);
+        uint4* dvp = reinterpret_cast<uint4*>(rowp + 2 * E + h * kHd + g * 16);
+        #pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          dkp[q] = make_uint4(pack_bf16(dkf[8 * q], dkf[8 * q + 1]), pack_bf16(dkf[8 * q + 2], dkf[8 * q + 3]),
+                              pack_bf16(dkf[8 * q + 4], dkf[8 * q + 5]), pack_bf16(dkf[8 * q + 6], dkf[8 * q + 7]));
+          dvp[q] = make_uint4(pack_bf16(__uint_as_float(vv[8 * q]), __uint_as_float(vv[8 * q + 1])),
+                              pack_bf16(__uint_as_float(vv[8 * q + 2]), __uint_as_float(vv[8 * q + 3])),
+                              pack_bf16(__uint_as_float(vv[8 * q + 4]), __uint_as_float(vv[8 * q + 5])),
+                              pack_bf16(__uint_as_float(vv[8 * q + 6]), __uint_as_float(vv[8 * q + 7])));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// D[seq, h, i] = sum_d O[row, h*64+d] * dO[row, h*64+d]; one warp per row, a
+// lane covers half a head (32 dims).
+__global__ void attn_dsum_kernel(const __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ dout,
+                                 float* __restrict__ dsum, long long T, int S, int H) {
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= T) return;
+  const int E = H * kHd;
+  for (int c0 = lane * 32; c0 < E; c0 += 32 * 32) {
+    const uint4* po = reinterpret_cast<const uint4*>(out + row * E + c0);
+    const uint4* pd = reinterpret_cast<const uint4*>(dout + row * E + c0);
+    float d = 0.f;
+    #pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 wo = po[q], wd = pd[q];
+      const __nv_bfloat162* ho = reinterpret_cast<const __nv_bfloat162*>(&wo);
+      const __nv_bfloat162* hd = reinterpret_cast<const __nv_bfloat162*>(&wd);
+      #pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fo = __bfloat1622float2(ho[e]), fd = __bfloat1622float2(hd[e]);
+        d = fmaf(fo.x, fd.x, fmaf(fo.y, fd.y, d));
+      }
+    }
+    d += __shfl_xor_sync(0xffffffffu, d, 1);
+    if ((lane & 1) == 0) {
+      const int hh = c0 / kHd;
+      const long long seq = row / S, i = row - seq * S;
+      dsum[(seq * H + hh) * S + i] = d;
+    }
+  }
+}
+
+// dqkv[row, h*64 + d] (q part) = unrope(dq[row, ...] / 8), pairs of dims per thread.
+__global__ void attn_dq_finish_kernel(const float* __restrict__ dq, __nv_bfloat16* __restrict__ dqkv,
+                                      const float* __restrict__ rope, long long T, int S, int E) {
+  const long long n = T * (E / 2);
+  for (long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x; p < n; p += (long long)gridDim.x * blockDim.x) {
+    const long long row = p / (E / 2);
+    const int c = (int)(p - row * (E / 2)) * 2;
+    const float2 v = *reinterpret_cast<const float2*>(dq + row * E + c);
+    float x0 = v.x * 0.125f, x1 = v.y * 0.125f;
+    if (rope != nullptr) {
+      const int pos = (int)(row % S);
+      const float2 t = *reinterpret_cast<const float2*>(rope + ((long long)pos * 32 + ((c & 63) >> 1)) * 2);
+      const float y0 = x0 * t.x + x1 * t.y, y1 = x1 * t.x - x0 * t.y;
+      x0 = y0;
+      x1 = y1;
+    }
+    *reinterpret_cast<uint32_t*>(dqkv + row * 3ll * E + c) = pack_bf16(x0, x1);
+  }
+}
+
 }  // namespace tclong
 
 // Host launcher used by cdk_attn_fwd for S > 256.
@@ -332,4 +703,60 @@ int launch_attn_fwd_long(const void* qkv, void* out, float* lse, int64_t nseq, i
   return e == cudaSuccess ? 0 : (int)e;
 }
 
+}  // namespace cdk
+
+namespace cdk {
+// Host launcher used by cdk_attn_bwd for S > 256 (workspace: fp32 [nseq*S, E]).
+int launch_attn_bwd_long(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,
+                         void* dqkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,
+                         const int32_t* meta, const float* rope, void* workspace, cudaStream_t stream) {
+  using namespace tclong;
+  if (S <= 0 || !workspace) return -20;
+  const int64_t E = H * kHd, T = nseq * S;
+  CUtensorMap tq, tdo;
+  if (!make_tmap(&tq, qkv, 3 * E, T, 3 * E, 64, 64)) return -21;
+  if (!make_tmap(&tdo, dout, E, T, E, 64, 64)) return -21;
+  cudaError_t e = cudaMemsetAsync(workspace, 0, (size_t)T * E * sizeof(float), stream);
+  if (e != cudaSuccess) return (int)e;
+  attn_dsum_kernel<<<(unsigned)((T + 7) / 8), 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(out),
+                                                                  reinterpret_cast<const __nv_bfloat16*>(dout),
+                                                                  dsum, T, (int)S, (int)H);
+  LongBwdArgs a;
+  a.lse = lse;
+  a.dsum = dsum;
+  a.dq = reinterpret_cast<float*>(workspace);
+  a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv);
+  const int64_t np = nseq - n_causal;
+  const int nt64 = (int)((S + 63) / 64);
+  a.bid = bid;
+  a.q_lo = meta;
+  a.first = np > 0 ? meta + np * 2 * nt64 : nullptr;
+  a.rope = rope;
+  a.S = (int)S;
+  a.H = (int)H;
+  a.n_causal = (int)n_causal;
+  a.nt64 = nt64;
+  const size_t smem = sizeof(BwdSmem) + 1024;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    e = cudaFuncSetAttribute(attn_bwd_long_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_bwd_long_kernel, kBwdThreads, smem);
+    if (e != cudaSuccess) return (int)e;
+    if (per_sm * 512 > 512) return -22;
+    attr_done[dev] = true;
+  }
+  attn_bwd_long_kernel<<<dim3((unsigned)((S + kBK - 1) / kBK), (unsigned)H, (unsigned)nseq), kBwdThreads, smem,
+                         stream>>>(tq, tdo, a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return (int)e;
+  long long blocks = (T * (E / 2) + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  attn_dq_finish_kernel<<<(unsigned)blocks, 256, 0, stream>>>(a.dq, a.dqkv, rope, T, (int)S, (int)E);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
 }  // namespace cdk

@@ -278,8 +278,10 @@ def attn_fwd(qkv, out, lse, nseq, n_causal, S, H, bid32=None, meta=None):
 @_timed("attn_bwd")
 def attn_bwd(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid32=None, meta=None, rope=None):
     _need_cuda(qkv, out, dout, lse, dsum, dqkv)
-    rc = lib().cdk_attn_bwd(_p(qkv), _p(out), _p(dout), _p(lse), _p(dsum), _p(dqkv), nseq, n_causal, S, H,
-                            _p(bid32), _p(meta), _p(rope), _stream())
+    nb = int(lib().cdk_attn_bwd_workspace(nseq, S, H))
+    ws = torch.empty(max(nb, 16) // 4, dtype=torch.float32, device=qkv.device) if nb > 0 else None
+    rc = lib().cdk_attn_bwd_ws(_p(qkv), _p(out), _p(dout), _p(lse), _p(dsum), _p(dqkv), nseq, n_causal, S, H,
+                               _p(bid32), _p(meta), _p(rope), _p(ws), max(nb, 0), _stream())
     _check(rc, "attn_bwd")
     _count(2)
 

@@ -139,7 +139,7 @@ def test_moe_dispatch_combine_and_backward(K):
     assert K.get_error() == 0
 
 
-@pytest.mark.parametrize("S,nseq,n_causal", [(1024, 2, 1), (4096, 2, 1)])
+@pytest.mark.parametrize("S,nseq,n_causal", [(301, 3, 1), (1024, 2, 1), (4096, 2, 1)])
 def test_attention_long_sequences(K, S, nseq, n_causal):
     """The tiled kernels (S > 256) on thinking-row block structure."""
     from chessdecoder_b200 import data
