@@ -1229,7 +1229,7 @@ extern "C" int cdk_attn_bwd_ws(const void* qkv, const void* out, const void* dou
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (S <= kSeqMax && attn_path() == 0)
     return launch_attn_bwd_tc(qkv, out, dout, lse, dqkv, nseq, n_causal, S, H, bid, meta, rope, s);
-  if (S > kSeqMax && attn_path() == 0 && workspace != nullptr) {
+  if (S > kSeqMax && attn_path() == 0 && workspace != nullptr && S % 4 == 0) {
     if (workspace_bytes < cdk_attn_bwd_workspace(nseq, S, H) || (reinterpret_cast<uintptr_t>(workspace) & 15))
       return -5;
     return launch_attn_bwd_long(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid, meta, rope, workspace,

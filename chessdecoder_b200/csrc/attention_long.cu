@@ -300,12 +300,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 //   EW     P^T = exp2(S^T c - L), dS^T = P^T (dP^T - D)    (bf16 operands in smem)
 //   MMA-B  dV += P^T dO_t, dK += dS^T Q_t                  (TMEM, accumulated)
 //          dQ_t = dS K                                      (TMEM, per query tile)
-// and the elementwise warps add dQ_t into an fp32 [tokens, E] accumulator with
-// vector atomics while the next tile's products run.  D = rowsum(dO * O) comes
+// and the elementwise warps stage dQ_t in shared memory for a bulk reduce-add
+// (cp.reduce.async.bulk.tensor) into an fp32 [tokens, E] accumulator while the
+// next tile's products run.  L and D arrive with each query tile by bulk copy.  D = rowsum(dO * O) comes
 // from a pass before; a pass after scales dQ by 1/8, undoes RoPE and writes it
 // into dqkv.  TMEM: S^T | dP^T | dV | dK | dQ = 448 of 512 columns.
 // ===========================================================================
-constexpr int kQStages = 3;
+constexpr int kQStages = 2;
 constexpr int kBwdThreads = 576;  // warp 0 TMA, warp 1 MMA, warps 2-17 elementwise
 
 struct BwdSmem {
@@ -315,6 +316,9 @@ struct BwdSmem {
   uint8_t dO[kQStages][2 * kTileBytes];
   uint8_t PT[2][128 * 128];   // [64-query block][128 key rows x 64 queries]
   uint8_t dST[2][128 * 128];
+  float dq_stage[2][128 * 32];   // dQ tile for the bulk reduce: two [128 rows x 32 dims] swizzled boxes
+  float Lq[kQStages][kBQ];       // L and D of the staged query tile
+  float Dq[kQStages][kBQ];
   uint64_t bar_kv, bar_full[kQStages], bar_empty[kQStages], bar_sa, bar_ew, bar_mb, bar_dq;
   uint32_t tmem_base;
   int abort;
@@ -322,7 +326,8 @@ struct BwdSmem {
 };
 static_assert(offsetof(BwdSmem, V) % 1024 == 0 && offsetof(BwdSmem, Q) % 1024 == 0 &&
                   offsetof(BwdSmem, dO) % 1024 == 0 && offsetof(BwdSmem, PT) % 1024 == 0 &&
-                  offsetof(BwdSmem, dST) % 1024 == 0,
+                  offsetof(BwdSmem, dST) % 1024 == 0 && offsetof(BwdSmem, dq_stage) % 1024 == 0 &&
+                  offsetof(BwdSmem, Lq) % 16 == 0 && offsetof(BwdSmem, Dq) % 16 == 0,
               "TMA / UMMA operands with the 128-byte swizzle need 1024-byte alignment");
 
 struct LongBwdArgs {
@@ -339,7 +344,7 @@ struct LongBwdArgs {
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_long_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo,
-                         const LongBwdArgs a) {
+                         const __grid_constant__ CUtensorMap tdq, const LongBwdArgs a) {
   extern __shared__ uint8_t raw[];
   BwdSmem& sm = *reinterpret_cast<BwdSmem*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   const int kt = blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
@@ -397,13 +402,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       for (int it = 0; it < n_q; ++it) {
         const int st = it % kQStages;
+        const int qt = q_first + it;
+        const uint32_t ld_bytes = (uint32_t)min(kBQ, S - qt * kBQ) * 4u;  // S % 4 == 0: a multiple of 16
         mbar_wait(&sm.bar_empty[st], ((it / kQStages) & 1) ^ 1u, abort_flag);
-        mbar_arrive_expect_tx(&sm.bar_full[st], 4 * kTileBytes);
+        mbar_arrive_expect_tx(&sm.bar_full[st], 4 * kTileBytes + 2 * ld_bytes);
         for (int t = 0; t < 2; ++t) {
-          const int r0 = row_base + (q_first + it) * kBQ + t * 64;
+          const int r0 = row_base + qt * kBQ + t * 64;
           tma_load_2d(sm.Q[st] + t * kTileBytes, &tqkv, &sm.bar_full[st], h * kHd, r0);
           tma_load_2d(sm.dO[st] + t * kTileBytes, &tdo, &sm.bar_full[st], h * kHd, r0);
         }
+        bulk_load_1d(sm.Lq[st], a.lse + lrow + qt * kBQ, ld_bytes, &sm.bar_full[st]);
+        bulk_load_1d(sm.Dq[st], a.dsum + lrow + qt * kBQ, ld_bytes, &sm.bar_full[st]);
       }
     }
   } else if (warp == 1) {
@@ -464,14 +473,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int32_t* bidrow = prefix ? a.bid + (long long)pseq * S : nullptr;
     const int fj = jok ? (prefix ? a.first[(long long)pseq * S + j] : j) : S;
     const int bj = (jok && prefix) ? bidrow[j] : -2;
-    auto dq_atomics = [&](int qt_prev, const uint32_t (&dqv)[16]) {
-      const int qi = qt_prev * kBQ + r;  // lane = query row for dQ
-      if (qi < S) {
-        float4* dst = reinterpret_cast<float4*>(a.dq + (long long)(row_base + qi) * E + h * kHd + g * 16);
-        #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          atomicAdd(dst + q, make_float4(__uint_as_float(dqv[4 * q]), __uint_as_float(dqv[4 * q + 1]),
-                                         __uint_as_float(dqv[4 * q + 2]), __uint_as_float(dqv[4 * q + 3])));
+    // dQ of a query tile: TMEM (lane = query row) -> swizzled staging boxes ->
+    // one bulk reduce-add per box into the fp32 accumulator (rows past S are 0)
+    const bool leader = threadIdx.x == 64;
+    auto dq_flush = [&](int qt_prev, const uint32_t (&dqv)[16]) {
+      if (leader) bulk_wait_read0();  // the previous tile's reduce has read the staging boxes
+      asm volatile("bar.sync 1, 512;" ::: "memory");
+      uint8_t* box = reinterpret_cast<uint8_t*>(sm.dq_stage[g >> 1]);
+      #pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int chunk = (g & 1) * 4 + q;  // 16-byte chunk of the 128-byte row
+        *reinterpret_cast<uint4*>(box + r * 128 + ((chunk ^ (r & 7)) << 4)) =
+            make_uint4(dqv[4 * q], dqv[4 * q + 1], dqv[4 * q + 2], dqv[4 * q + 3]);
+      }
+      fence_proxy_async();
+      asm volatile("bar.sync 1, 512;" ::: "memory");
+      if (leader) {
+        tma_reduce_add_2d(&tdq, sm.dq_stage[0], h * kHd, row_base + qt_prev * kBQ);
+        tma_reduce_add_2d(&tdq, sm.dq_stage[1], h * kHd + 32, row_base + qt_prev * kBQ);
+        bulk_commit();
       }
     };
     for (int it = 0; it < n_q; ++it) {
@@ -488,8 +508,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&sm.bar_dq);
-        dq_atomics(qt - 1, dqv);
+        dq_flush(qt - 1, dqv);
       }
+      const int st = it % kQStages;
       uint8_t* pt = sm.PT[g >> 1];
       uint8_t* dst = sm.dST[g >> 1];
       const int cbase = (g & 1) * 32;
@@ -506,25 +527,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tmem_ld_x16_nowait(tmem + lane_off + 128 + g * 32 + sc * 16, du);
           tmem_wait_ld();
           if (!none) {
-            // L and D of these 16 queries (the same addresses in every lane)
+            // L and D of these 16 queries from the staged tile (broadcast reads;
+            // entries past S are stale but their elements are masked)
             float Lv[16], Dv[16];
+            const float4* L4 = reinterpret_cast<const float4*>(sm.Lq[st] + g * 32 + sc * 16);
+            const float4* D4 = reinterpret_cast<const float4*>(sm.Dq[st] + g * 32 + sc * 16);
             #pragma unroll
             for (int e4 = 0; e4 < 4; ++e4) {
-              const int q = qb + sc * 16 + e4 * 4;
-              float4 l4, d4;
-              if (q + 3 < S && (S & 3) == 0) {
-                l4 = *reinterpret_cast<const float4*>(a.lse + lrow + q);
-                d4 = *reinterpret_cast<const float4*>(a.dsum + lrow + q);
-              } else {
-                l4.x = q < S ? a.lse[lrow + q] : 0.f;
-                l4.y = q + 1 < S ? a.lse[lrow + q + 1] : 0.f;
-                l4.z = q + 2 < S ? a.lse[lrow + q + 2] : 0.f;
-                l4.w = q + 3 < S ? a.lse[lrow + q + 3] : 0.f;
-                d4.x = q < S ? a.dsum[lrow + q] : 0.f;
-                d4.y = q + 1 < S ? a.dsum[lrow + q + 1] : 0.f;
-                d4.z = q + 2 < S ? a.dsum[lrow + q + 2] : 0.f;
-                d4.w = q + 3 < S ? a.dsum[lrow + q + 3] : 0.f;
-              }
+              const float4 l4 = L4[e4], d4 = D4[e4];
               Lv[e4 * 4] = l4.x; Lv[e4 * 4 + 1] = l4.y; Lv[e4 * 4 + 2] = l4.z; Lv[e4 * 4 + 3] = l4.w;
               Dv[e4 * 4] = d4.x; Dv[e4 * 4 + 1] = d4.y; Dv[e4 * 4 + 2] = d4.z; Dv[e4 * 4 + 3] = d4.w;
             }
@@ -568,7 +578,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_ld_x16_nowait(tmem + lane_off + 256 + g * 16, vv);
       tmem_ld_x16_nowait(tmem + lane_off + 320 + g * 16, kv);
       tmem_wait_ld();
-      dq_atomics(q_first + n_q - 1, dqv);
+      dq_flush(q_first + n_q - 1, dqv);
+      if (leader) bulk_wait0();
       if (jok) {
         float dkf[16];
         #pragma unroll
@@ -713,9 +724,11 @@ int launch_attn_bwd_long(const void* qkv, const void* out, const void* dout, con
   using namespace tclong;
   if (S <= 0 || !workspace) return -20;
   const int64_t E = H * kHd, T = nseq * S;
-  CUtensorMap tq, tdo;
+  if (S % 4) return -23;  // the L / D tiles are bulk-copied in 16-byte units
+  CUtensorMap tq, tdo, tdq;
   if (!make_tmap(&tq, qkv, 3 * E, T, 3 * E, 64, 64)) return -21;
   if (!make_tmap(&tdo, dout, E, T, E, 64, 64)) return -21;
+  if (!make_tmap_f32(&tdq, workspace, E, T, E, 32, 128)) return -21;
   cudaError_t e = cudaMemsetAsync(workspace, 0, (size_t)T * E * sizeof(float), stream);
   if (e != cudaSuccess) return (int)e;
   attn_dsum_kernel<<<(unsigned)((T + 7) / 8), 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(out),
@@ -750,7 +763,7 @@ int launch_attn_bwd_long(const void* qkv, const void* out, const void* dout, con
     attr_done[dev] = true;
   }
   attn_bwd_long_kernel<<<dim3((unsigned)((S + kBK - 1) / kBK), (unsigned)H, (unsigned)nseq), kBwdThreads, smem,
-                         stream>>>(tq, tdo, a);
+                         stream>>>(tq, tdo, tdq, a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return (int)e;
   long long blocks = (T * (E / 2) + 255) / 256;

@@ -667,6 +667,21 @@ bool make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
   return r == CUDA_SUCCESS;
 }
 
+// 2-D fp32 tensor map, 128-byte swizzle; pitch in elements.
+bool make_tmap_f32(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
+                   uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch * 4};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // 2-D uint8 (fp8 payload) tensor map, 128-byte swizzle; pitch in bytes.
 static bool make_tmap_u8(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
                          uint32_t box_inner, uint32_t box_outer) {

@@ -158,7 +158,8 @@ int cdk_attn_bwd(const void* qkv, const void* out, const void* dout, const float
 /* cdk_attn_bwd_ws: cdk_attn_bwd with a caller workspace; for S > 256 the
  * tcgen05 backward accumulates dQ in fp32 there (cdk_attn_bwd_workspace bytes,
  * 16-byte aligned; 0 bytes for S <= 256) and writes D = rowsum(dO * O) into
- * dsum.  Without a workspace S > 256 takes the mma.sync tiled kernels. */
+ * dsum.  Without a workspace, or when S is not a multiple of 4, S > 256 takes
+ * the mma.sync tiled kernels. */
 int64_t cdk_attn_bwd_workspace(int64_t nseq, int64_t S, int64_t H);
 int cdk_attn_bwd_ws(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum, void* dqkv,
                     int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid, const int32_t* meta,
