@@ -1110,13 +1110,16 @@ extern "C" int cdk_attn_prefix_meta(const int32_t* bid, int64_t nseq_prefix, int
 // CDK_ATTN_PATH=tiled the tiled kernels (the tests cover all three).  S > 256:
 // the tcgen05 kernels of attention_long.cu by default (the backward needs the
 // caller's fp32 dQ workspace, cdk_attn_bwd_ws), the tiled kernels with
-// CDK_ATTN_PATH=tiled or seq or without a workspace.
+// CDK_ATTN_PATH=tiled or seq or without a workspace.  CDK_ATTN_PATH=long takes
+// the attention_long.cu kernels at every S.
 static int attn_path() {
   const char* v = getenv("CDK_ATTN_PATH");
   if (v && v[0] == 't' && v[1] == 'i') return 2;  // tiled
   if (v && v[0] == 's') return 1;                  // seq (mma.sync)
+  if (v && v[0] == 'l') return 3;                  // tcgen05 long-sequence kernels at any S
   return 0;                                        // tcgen05
 }
+static bool long_path(int64_t S) { return (S > kSeqMax && attn_path() == 0) || attn_path() == 3; }
 static bool seq_path_enabled() { return attn_path() != 2; }
 
 namespace cdk {
@@ -1159,7 +1162,7 @@ extern "C" int cdk_attn_fwd(const void* qkv, void* out, float* lse, int64_t nseq
   if (S <= kSeqMax && attn_path() == 0) {
     return launch_attn_fwd_tc(qkv, out, lse, nseq, n_causal, S, H, bid, meta, s);
   }
-  if (S > kSeqMax && attn_path() == 0) {
+  if (long_path(S)) {
     return launch_attn_fwd_long(qkv, out, lse, nseq, n_causal, S, H, bid, meta, s);
   }
   if (S <= kSeqMax && seq_path_enabled()) {
@@ -1190,7 +1193,7 @@ int launch_attn_bwd_long(const void* qkv, const void* out, const void* dout, con
 
 extern "C" int64_t cdk_attn_bwd_workspace(int64_t nseq, int64_t S, int64_t H) {
   if (nseq < 0 || S <= 0 || H <= 0) return -1;
-  return S > kSeqMax ? nseq * S * H * kHd * (int64_t)sizeof(float) : 0;
+  return long_path(S) ? nseq * S * H * kHd * (int64_t)sizeof(float) : 0;
 }
 
 extern "C" int cdk_attn_bwd(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,
@@ -1229,7 +1232,7 @@ extern "C" int cdk_attn_bwd_ws(const void* qkv, const void* out, const void* dou
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (S <= kSeqMax && attn_path() == 0)
     return launch_attn_bwd_tc(qkv, out, dout, lse, dqkv, nseq, n_causal, S, H, bid, meta, rope, s);
-  if (S > kSeqMax && attn_path() == 0 && workspace != nullptr && S % 4 == 0) {
+  if (long_path(S) && workspace != nullptr && S % 4 == 0) {
     if (workspace_bytes < cdk_attn_bwd_workspace(nseq, S, H) || (reinterpret_cast<uintptr_t>(workspace) & 15))
       return -5;
     return launch_attn_bwd_long(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid, meta, rope, workspace,

@@ -295,39 +295,46 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
 // ===========================================================================
 // Backward for S > 256.  One CTA per (128-key tile, head, sequence) walks the
-// 128-query tiles that can see the key tile:
-//   MMA-A  S^T = K Q_t^T, dP^T = V dO_t^T                  (TMEM, 128 cols each)
-//   EW     P^T = exp2(S^T c - L), dS^T = P^T (dP^T - D)    (bf16 operands in smem)
-//   MMA-B  dV += P^T dO_t, dK += dS^T Q_t                  (TMEM, accumulated)
-//          dQ_t = dS K                                      (TMEM, per query tile)
-// and the elementwise warps stage dQ_t in shared memory for a bulk reduce-add
-// (cp.reduce.async.bulk.tensor) into an fp32 [tokens, E] accumulator while the
-// next tile's products run.  L and D arrive with each query tile by bulk copy.  D = rowsum(dO * O) comes
-// from a pass before; a pass after scales dQ by 1/8, undoes RoPE and writes it
-// into dqkv.  TMEM: S^T | dP^T | dV | dK | dQ = 448 of 512 columns.
+// 64-query sub-tiles s that can see the key tile (two per 128-query tile t):
+//   MMA-A(s)  S^T = K Q_s^T, dP^T = V dO_s^T            (TMEM, 64 columns each)
+//   EW(s)     P^T = exp2(S^T c - L), dS^T = P^T (dP^T - D)  (bf16 operands in smem)
+//   MMA-B(s)  dV += P^T dO_s, dK += dS^T Q_s             (TMEM, accumulated;
+//             P^T and dS^T are read from TMEM, where EW(s) stores them in bf16)
+//   MMA-Q(t)  dQ_t = dS K over both sub-tiles of t       (TMEM; dS read from smem)
+// S^T | dP^T are double-buffered, so the tensor core runs A(s+2), B(s) and
+// Q(t) while the elementwise warps work on sub-tile s+1: a tcgen05.mma of
+// M=128, K=16 costs about the same for N=64 as for N=128, which makes the
+// 40 instructions of a 128 x 128 (key, query) tile as long as its elementwise
+// work, and only overlapping the two keeps both busy; taking the A operand of
+// the dV / dK products from TMEM keeps their shared-memory reads to the B
+// tiles.  The elementwise warps
+// also move dQ_t from TMEM into shared memory (the tile's dS^T pair, free
+// once Q(t) has retired) for a bulk reduce-add (cp.reduce.async.bulk.tensor)
+// into an fp32 [tokens, E] accumulator.  Q, dO, L and D arrive per sub-tile
+// in a 4-deep ring.  D = rowsum(dO * O) comes from a pass before; a pass after
+// scales dQ by 1/8, undoes RoPE and writes it into dqkv.
+// TMEM: S^T|dP^T x 2 (256) | dV (64) | dK (64) | dQ (64) | P^T|dS^T bf16 (64) = 512.
 // ===========================================================================
-constexpr int kQStages = 2;
+constexpr int kQStages = 4;       // sub-tile ring (Q, dO, L, D of 64 queries)
 constexpr int kBwdThreads = 576;  // warp 0 TMA, warp 1 MMA, warps 2-17 elementwise
 
 struct BwdSmem {
   uint8_t K[2 * kTileBytes];
   uint8_t V[2 * kTileBytes];
-  uint8_t Q[kQStages][2 * kTileBytes];
-  uint8_t dO[kQStages][2 * kTileBytes];
-  uint8_t PT[2][128 * 128];   // [64-query block][128 key rows x 64 queries]
-  uint8_t dST[2][128 * 128];
-  float dq_stage[2][128 * 32];   // dQ tile for the bulk reduce: two [128 rows x 32 dims] swizzled boxes
-  float Lq[kQStages][kBQ];       // L and D of the staged query tile
-  float Dq[kQStages][kBQ];
-  uint64_t bar_kv, bar_full[kQStages], bar_empty[kQStages], bar_sa, bar_ew, bar_mb, bar_dq;
+  uint8_t Q[kQStages][kTileBytes];
+  uint8_t dO[kQStages][kTileBytes];
+  uint8_t dST[2][2][128 * 128];   // [tile parity][sub-tile]: 128 key rows x 64 queries; after Q(t) the pair stages dQ_t
+  float Lq[kQStages][64];
+  float Dq[kQStages][64];
+  uint64_t bar_kv, bar_full[kQStages], bar_empty[kQStages];
+  uint64_t bar_sa[2], bar_ew[2], bar_b[2], bar_dq, bar_dqfree;
   uint32_t tmem_base;
   int abort;
   int q_first, n_q;
 };
 static_assert(offsetof(BwdSmem, V) % 1024 == 0 && offsetof(BwdSmem, Q) % 1024 == 0 &&
-                  offsetof(BwdSmem, dO) % 1024 == 0 && offsetof(BwdSmem, PT) % 1024 == 0 &&
-                  offsetof(BwdSmem, dST) % 1024 == 0 && offsetof(BwdSmem, dq_stage) % 1024 == 0 &&
-                  offsetof(BwdSmem, Lq) % 16 == 0 && offsetof(BwdSmem, Dq) % 16 == 0,
+                  offsetof(BwdSmem, dO) % 1024 == 0 && offsetof(BwdSmem, dST) % 1024 == 0 && offsetof(BwdSmem, Lq) % 16 == 0 &&
+                  offsetof(BwdSmem, Dq) % 16 == 0,
               "TMA / UMMA operands with the 128-byte swizzle need 1024-byte alignment");
 
 struct LongBwdArgs {
@@ -364,10 +371,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&sm.bar_full[b], 1);
       mbar_init(&sm.bar_empty[b], 1);
     }
-    mbar_init(&sm.bar_sa, 1);
-    mbar_init(&sm.bar_ew, 512);
-    mbar_init(&sm.bar_mb, 1);
-    mbar_init(&sm.bar_dq, 512);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.bar_sa[b], 1);
+      mbar_init(&sm.bar_ew[b], 512);
+      mbar_init(&sm.bar_b[b], 1);
+    }
+    mbar_init(&sm.bar_dq, 1);
+    mbar_init(&sm.bar_dqfree, 512);
     sm.abort = 0;
     // first query tile that can see this key tile: causal -> the diagonal one;
     // prefix -> the lowest query row of the key rows' blocks (metadata)
@@ -389,81 +399,88 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
   const int q_first = sm.q_first, n_q = sm.n_q;
+  const int ns = 2 * n_q;  // 64-query sub-tiles
 
   if (warp == 0) {
     if (lane == 0) {
       prefetch_tmap(&tqkv);
       prefetch_tmap(&tdo);
+      prefetch_tmap(&tdq);
       mbar_arrive_expect_tx(&sm.bar_kv, 4 * kTileBytes);
       for (int t = 0; t < 2; ++t) {
         const int r0 = row_base + kt * kBK + t * 64;
         tma_load_2d(sm.K + t * kTileBytes, &tqkv, &sm.bar_kv, E + h * kHd, r0);
         tma_load_2d(sm.V + t * kTileBytes, &tqkv, &sm.bar_kv, 2 * E + h * kHd, r0);
       }
-      for (int it = 0; it < n_q; ++it) {
-        const int st = it % kQStages;
-        const int qt = q_first + it;
-        const uint32_t ld_bytes = (uint32_t)min(kBQ, S - qt * kBQ) * 4u;  // S % 4 == 0: a multiple of 16
-        mbar_wait(&sm.bar_empty[st], ((it / kQStages) & 1) ^ 1u, abort_flag);
-        mbar_arrive_expect_tx(&sm.bar_full[st], 4 * kTileBytes + 2 * ld_bytes);
-        for (int t = 0; t < 2; ++t) {
-          const int r0 = row_base + qt * kBQ + t * 64;
-          tma_load_2d(sm.Q[st] + t * kTileBytes, &tqkv, &sm.bar_full[st], h * kHd, r0);
-          tma_load_2d(sm.dO[st] + t * kTileBytes, &tdo, &sm.bar_full[st], h * kHd, r0);
+      for (int s = 0; s < ns; ++s) {
+        const int st = s % kQStages;
+        const int q64 = 2 * q_first + s;  // 64-query block within the sequence
+        // L / D entries of the sub-tile inside the sequence (S % 4 == 0: a multiple of 16 bytes)
+        const int nld = max(0, min(64, S - q64 * 64));
+        const uint32_t ld_bytes = (uint32_t)nld * 4u;
+        mbar_wait(&sm.bar_empty[st], ((s / kQStages) & 1) ^ 1u, abort_flag);
+        mbar_arrive_expect_tx(&sm.bar_full[st], 2 * kTileBytes + 2 * ld_bytes);
+        tma_load_2d(sm.Q[st], &tqkv, &sm.bar_full[st], h * kHd, row_base + q64 * 64);
+        tma_load_2d(sm.dO[st], &tdo, &sm.bar_full[st], h * kHd, row_base + q64 * 64);
+        if (nld > 0) {
+          bulk_load_1d(sm.Lq[st], a.lse + lrow + q64 * 64, ld_bytes, &sm.bar_full[st]);
+          bulk_load_1d(sm.Dq[st], a.dsum + lrow + q64 * 64, ld_bytes, &sm.bar_full[st]);
         }
-        bulk_load_1d(sm.Lq[st], a.lse + lrow + qt * kBQ, ld_bytes, &sm.bar_full[st]);
-        bulk_load_1d(sm.Dq[st], a.dsum + lrow + qt * kBQ, ld_bytes, &sm.bar_full[st]);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t kb = smem_u32(sm.K), vb = smem_u32(sm.V);
-      const uint32_t ptb = smem_u32(sm.PT[0]), dsb = smem_u32(sm.dST[0]);
-      const uint32_t id_s = make_idesc_bf16(128, 128, false, false);
-      const uint32_t id_kn = make_idesc_bf16(128, kHd, false, true);
-      const uint32_t id_nn = make_idesc_bf16(128, kHd, true, true);
+      const uint32_t id_s = make_idesc_bf16(128, 64, false, false);   // N = 64 queries
+      const uint32_t id_kn = make_idesc_bf16(128, kHd, false, true);  // dV, dK: B read MN-major
+      const uint32_t id_nn = make_idesc_bf16(128, kHd, true, true);   // dQ: A (dS) and B (K) MN-major
       mbar_wait(&sm.bar_kv, 0, abort_flag);
-      auto issue_a = [&](int it) {
-        const int st = it % kQStages;
-        mbar_wait(&sm.bar_full[st], (it / kQStages) & 1, abort_flag);
+      auto issue_a = [&](int s) {
+        const int st = s % kQStages, b = s & 1;
+        mbar_wait(&sm.bar_full[st], (s / kQStages) & 1, abort_flag);
         tc_fence_after();
         const uint32_t qb = smem_u32(sm.Q[st]), ob = smem_u32(sm.dO[st]);
         #pragma unroll
         for (int kk = 0; kk < kHd / 16; ++kk) {
-          umma_f16(tmem, make_sdesc(kb + kk * 32, 16, 1024), make_sdesc(qb + kk * 32, 16, 1024), id_s,
+          umma_f16(tmem + b * 128, make_sdesc(kb + kk * 32, 16, 1024), make_sdesc(qb + kk * 32, 16, 1024), id_s,
                    kk > 0 ? 1u : 0u);
-          umma_f16(tmem + 128, make_sdesc(vb + kk * 32, 16, 1024), make_sdesc(ob + kk * 32, 16, 1024), id_s,
-                   kk > 0 ? 1u : 0u);
+          umma_f16(tmem + b * 128 + 64, make_sdesc(vb + kk * 32, 16, 1024), make_sdesc(ob + kk * 32, 16, 1024),
+                   id_s, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&sm.bar_sa);
+        tc_commit(&sm.bar_sa[b]);
       };
-      if (n_q > 0) issue_a(0);
-      for (int it = 0; it < n_q; ++it) {
-        const int st = it % kQStages;
-        const uint32_t qb = smem_u32(sm.Q[st]), ob = smem_u32(sm.dO[st]);
-        mbar_wait(&sm.bar_ew, it & 1, abort_flag);
-        if (it > 0) mbar_wait(&sm.bar_dq, (it - 1) & 1, abort_flag);
+      if (ns > 0) issue_a(0);
+      if (ns > 1) issue_a(1);
+      for (int s = 0; s < ns; ++s) {
+        const int t = s >> 1, hh = s & 1, b = s & 1, st = s % kQStages;
+        mbar_wait(&sm.bar_ew[b], (s >> 1) & 1, abort_flag);
         tc_fence_after();
-        #pragma unroll 1
-        for (int kk = 0; kk < 8; ++kk) {  // 128 queries
-          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-          const uint64_t a_pt = make_sdesc(ptb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-          const uint64_t a_ds = make_sdesc(dsb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-          umma_f16(tmem + 256, a_pt, make_sdesc(ob + kk * 2048, 8192, 1024), id_kn, acc);
-          umma_f16(tmem + 320, a_ds, make_sdesc(qb + kk * 2048, 8192, 1024), id_kn, acc);
+        const uint32_t qb = smem_u32(sm.Q[st]), ob = smem_u32(sm.dO[st]);
+        #pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {  // 64 queries: A = P^T / dS^T columns of 16 queries in TMEM
+          const uint32_t acc = (s > 0 || kk > 0) ? 1u : 0u;
+          umma_f16_ts(tmem + 256, tmem + 448 + kk * 8, make_sdesc(ob + kk * 2048, 8192, 1024), id_kn, acc);
+          umma_f16_ts(tmem + 320, tmem + 480 + kk * 8, make_sdesc(qb + kk * 2048, 8192, 1024), id_kn, acc);
         }
-        #pragma unroll 1
-        for (int kk = 0; kk < 8; ++kk)  // 128 keys
-          umma_f16(tmem + 384, make_sdesc(dsb + kk * 2048, 16384, 1024), make_sdesc(kb + kk * 2048, 8192, 1024),
-                   id_nn, kk > 0 ? 1u : 0u);
-        tc_commit(&sm.bar_mb);
+        tc_commit(&sm.bar_b[b]);
         tc_commit(&sm.bar_empty[st]);
-        if (it + 1 < n_q) issue_a(it + 1);
+        if (hh == 1) {
+          // dQ_t = dS K: A = the tile's dS^T pair read MN-major (queries 0-63 | 64-127)
+          if (t >= 1) mbar_wait(&sm.bar_dqfree, (t - 1) & 1, abort_flag);
+          tc_fence_after();
+          const uint32_t pair = smem_u32(sm.dST[t & 1][0]);
+          #pragma unroll 1
+          for (int kk = 0; kk < 8; ++kk)  // 128 keys
+            umma_f16(tmem + 384, make_sdesc(pair + kk * 2048, 16384, 1024), make_sdesc(kb + kk * 2048, 8192, 1024),
+                     id_nn, kk > 0 ? 1u : 0u);
+          tc_commit(&sm.bar_dq);
+        }
+        if (s + 2 < ns) issue_a(s + 2);
       }
     }
   } else {
     const int ew = warp - 2;
-    const int g = ew >> 2;
+    const int g = ew >> 2;  // 16-query column group of a sub-tile
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
@@ -473,13 +490,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int32_t* bidrow = prefix ? a.bid + (long long)pseq * S : nullptr;
     const int fj = jok ? (prefix ? a.first[(long long)pseq * S + j] : j) : S;
     const int bj = (jok && prefix) ? bidrow[j] : -2;
-    // dQ of a query tile: TMEM (lane = query row) -> swizzled staging boxes ->
-    // one bulk reduce-add per box into the fp32 accumulator (rows past S are 0)
     const bool leader = threadIdx.x == 64;
-    auto dq_flush = [&](int qt_prev, const uint32_t (&dqv)[16]) {
-      if (leader) bulk_wait_read0();  // the previous tile's reduce has read the staging boxes
-      asm volatile("bar.sync 1, 512;" ::: "memory");
-      uint8_t* box = reinterpret_cast<uint8_t*>(sm.dq_stage[g >> 1]);
+    // dQ of query tile t: TMEM (lane = query row) -> the tile's dS^T pair as two
+    // swizzled [128 rows x 32 dims] fp32 boxes -> bulk reduce-add (rows past S
+    // are 0: their dS columns are masked)
+    auto dq_flush = [&](int t) {
+      mbar_wait(&sm.bar_dq, t & 1, abort_flag);
+      tc_fence_after();
+      uint32_t dqv[16];
+      tmem_ld_x16_nowait(tmem + lane_off + 384 + g * 16, dqv);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&sm.bar_dqfree);
+      uint8_t* box = sm.dST[t & 1][g >> 1];
       #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int chunk = (g & 1) * 4 + q;  // 16-byte chunk of the 128-byte row
@@ -489,96 +512,91 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       fence_proxy_async();
       asm volatile("bar.sync 1, 512;" ::: "memory");
       if (leader) {
-        tma_reduce_add_2d(&tdq, sm.dq_stage[0], h * kHd, row_base + qt_prev * kBQ);
-        tma_reduce_add_2d(&tdq, sm.dq_stage[1], h * kHd + 32, row_base + qt_prev * kBQ);
+        const int y = row_base + (q_first + t) * kBQ;
+        tma_reduce_add_2d(&tdq, sm.dST[t & 1][0], h * kHd, y);
+        tma_reduce_add_2d(&tdq, sm.dST[t & 1][1], h * kHd + 32, y);
         bulk_commit();
       }
     };
-    for (int it = 0; it < n_q; ++it) {
-      const int qt = q_first + it;
-      const int qb = qt * kBQ + g * 32;
-      const bool full = jok && qb >= j && qb + 31 < S;
-      const bool none = !jok || qb + 31 < fj || qb >= S;
+    for (int s = 0; s < ns; ++s) {
+      const int t = s >> 1, hh = s & 1, b = s & 1, st = s % kQStages;
+      const int qb = (q_first + t) * kBQ + hh * 64 + g * 16;  // this thread's 16 queries
+      const bool full = jok && qb >= j && qb + 15 < S;
+      const bool none = !jok || qb + 15 < fj || qb >= S;
       const bool none_w = __all_sync(0xffffffffu, none);
-      mbar_wait(&sm.bar_sa, it & 1, abort_flag);
-      tc_fence_after();
-      if (it > 0) {  // dQ of the previous query tile (its products retired before this S^T)
-        uint32_t dqv[16];
-        tmem_ld_x16_nowait(tmem + lane_off + 384 + g * 16, dqv);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&sm.bar_dq);
-        dq_flush(qt - 1, dqv);
+      if (hh == 0 && t >= 2) {
+        // the dS^T pair of this tile parity staged dQ_{t-2}: its reduce must have read it
+        if (leader) bulk_wait_read0();
+        asm volatile("bar.sync 1, 512;" ::: "memory");
       }
-      const int st = it % kQStages;
-      uint8_t* pt = sm.PT[g >> 1];
-      uint8_t* dst = sm.dST[g >> 1];
-      const int cbase = (g & 1) * 32;
-      #pragma unroll
-      for (int sc = 0; sc < 2; ++sc) {
-        uint32_t pk[8], dk[8];
-        if (none_w || none) {
+      mbar_wait(&sm.bar_sa[b], (s >> 1) & 1, abort_flag);
+      tc_fence_after();
+      uint32_t pk[8], dk[8];
+      if (none_w || none) {
+        #pragma unroll
+        for (int e = 0; e < 8; ++e) pk[e] = dk[e] = 0u;
+      }
+      if (!none_w) {
+        uint32_t su[16], du[16];
+        tmem_ld_x16_nowait(tmem + lane_off + b * 128 + g * 16, su);
+        tmem_ld_x16_nowait(tmem + lane_off + b * 128 + 64 + g * 16, du);
+        tmem_wait_ld();
+        if (!none) {
+          // L and D of these 16 queries from the staged sub-tile (broadcast reads;
+          // entries past S are stale but their elements are masked)
+          float Lv[16], Dv[16];
+          const float4* L4 = reinterpret_cast<const float4*>(sm.Lq[st] + g * 16);
+          const float4* D4 = reinterpret_cast<const float4*>(sm.Dq[st] + g * 16);
           #pragma unroll
-          for (int e = 0; e < 8; ++e) pk[e] = dk[e] = 0u;
-        }
-        if (!none_w) {
-          uint32_t su[16], du[16];
-          tmem_ld_x16_nowait(tmem + lane_off + g * 32 + sc * 16, su);
-          tmem_ld_x16_nowait(tmem + lane_off + 128 + g * 32 + sc * 16, du);
-          tmem_wait_ld();
-          if (!none) {
-            // L and D of these 16 queries from the staged tile (broadcast reads;
-            // entries past S are stale but their elements are masked)
-            float Lv[16], Dv[16];
-            const float4* L4 = reinterpret_cast<const float4*>(sm.Lq[st] + g * 32 + sc * 16);
-            const float4* D4 = reinterpret_cast<const float4*>(sm.Dq[st] + g * 32 + sc * 16);
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const float4 l4 = L4[e4], d4 = D4[e4];
+            Lv[e4 * 4] = l4.x; Lv[e4 * 4 + 1] = l4.y; Lv[e4 * 4 + 2] = l4.z; Lv[e4 * 4 + 3] = l4.w;
+            Dv[e4 * 4] = d4.x; Dv[e4 * 4 + 1] = d4.y; Dv[e4 * 4 + 2] = d4.z; Dv[e4 * 4 + 3] = d4.w;
+          }
+          #pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            float pv[2], dsv[2];
             #pragma unroll
-            for (int e4 = 0; e4 < 4; ++e4) {
-              const float4 l4 = L4[e4], d4 = D4[e4];
-              Lv[e4 * 4] = l4.x; Lv[e4 * 4 + 1] = l4.y; Lv[e4 * 4 + 2] = l4.z; Lv[e4 * 4 + 3] = l4.w;
-              Dv[e4 * 4] = d4.x; Dv[e4 * 4 + 1] = d4.y; Dv[e4 * 4 + 2] = d4.z; Dv[e4 * 4 + 3] = d4.w;
-            }
-            #pragma unroll
-            for (int e = 0; e < 16; e += 2) {
-              float pv[2], dsv[2];
-              #pragma unroll
-              for (int k = 0; k < 2; ++k) {
-                const int ee = sc * 16 + e + k;
-                const float p = ex2_approx(fmaf(__uint_as_float(su[e + k]), sl2, -Lv[e + k]));
-                pv[k] = p;
-                dsv[k] = p * (__uint_as_float(du[e + k]) - Dv[e + k]);
-                if (!full) {
-                  const int i = qb + ee;
-                  bool vis = i < S && (i >= j || (i >= fj && bidrow != nullptr && bidrow[i] == bj));
-                  pv[k] = vis ? pv[k] : 0.f;
-                  dsv[k] = vis ? dsv[k] : 0.f;
-                }
+            for (int k = 0; k < 2; ++k) {
+              const float p = ex2_approx(fmaf(__uint_as_float(su[e + k]), sl2, -Lv[e + k]));
+              pv[k] = p;
+              dsv[k] = p * (__uint_as_float(du[e + k]) - Dv[e + k]);
+              if (!full) {
+                const int i = qb + e + k;
+                const bool vis = i < S && (i >= j || (i >= fj && bidrow != nullptr && bidrow[i] == bj));
+                pv[k] = vis ? pv[k] : 0.f;
+                dsv[k] = vis ? dsv[k] : 0.f;
               }
-              pk[e >> 1] = pack_bf16(pv[0], pv[1]);
-              dk[e >> 1] = pack_bf16(dsv[0], dsv[1]);
             }
+            pk[e >> 1] = pack_bf16(pv[0], pv[1]);
+            dk[e >> 1] = pack_bf16(dsv[0], dsv[1]);
           }
         }
-        #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const uint32_t off = sw128(r, cbase + sc * 16 + q * 8);
-          *reinterpret_cast<uint4*>(pt + off) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          *reinterpret_cast<uint4*>(dst + off) = make_uint4(dk[4 * q], dk[4 * q + 1], dk[4 * q + 2], dk[4 * q + 3]);
-        }
       }
+      uint8_t* dst = sm.dST[t & 1][hh];
+      #pragma unroll
+      for (int q = 0; q < 2; ++q)
+        *reinterpret_cast<uint4*>(dst + sw128(r, g * 16 + q * 8)) =
+            make_uint4(dk[4 * q], dk[4 * q + 1], dk[4 * q + 2], dk[4 * q + 3]);
+      // P^T, dS^T (bf16 pairs) into TMEM once B(s-1) has read the previous ones
+      if (s >= 1) mbar_wait(&sm.bar_b[(s - 1) & 1], ((s - 1) >> 1) & 1, abort_flag);
+      tc_fence_after();
+      tmem_st_x8(tmem + lane_off + 448 + g * 8, pk);
+      tmem_st_x8(tmem + lane_off + 480 + g * 8, dk);
+      tmem_wait_st();
       fence_proxy_async();
       tc_fence_before();
-      mbar_arrive(&sm.bar_ew);
+      mbar_arrive(&sm.bar_ew[b]);
+      if (hh == 0 && t >= 1) dq_flush(t - 1);
     }
     if (n_q > 0) {
-      mbar_wait(&sm.bar_mb, (n_q - 1) & 1, abort_flag);
+      dq_flush(n_q - 1);
+      mbar_wait(&sm.bar_b[(ns - 1) & 1], ((ns - 1) >> 1) & 1, abort_flag);  // dV, dK complete
       tc_fence_after();
-      uint32_t dqv[16], vv[16], kv[16];
-      tmem_ld_x16_nowait(tmem + lane_off + 384 + g * 16, dqv);
+      uint32_t vv[16], kv[16];
       tmem_ld_x16_nowait(tmem + lane_off + 256 + g * 16, vv);
       tmem_ld_x16_nowait(tmem + lane_off + 320 + g * 16, kv);
       tmem_wait_ld();
-      dq_flush(q_first + n_q - 1, dqv);
       if (leader) bulk_wait0();
       if (jok) {
         float dkf[16];

@@ -191,10 +191,11 @@ def ref_attention(qkv, nseq, n_causal, S, H, bid):
     return o.transpose(1, 2).reshape(nseq * S, H * 64)
 
 
-@pytest.fixture(params=["tc", "seq", "tiled"])
+@pytest.fixture(params=["tc", "seq", "tiled", "long"])
 def attn_path(request, monkeypatch):
     """Every attention implementation: tcgen05 (S <= 256), mma.sync
-    sequence-resident (S <= 256) and mma.sync tiled (any S)."""
+    sequence-resident (S <= 256), mma.sync tiled (any S) and the tcgen05
+    long-sequence kernels forced at short S."""
     monkeypatch.setenv("CDK_ATTN_PATH", request.param)
     return request.param
 
