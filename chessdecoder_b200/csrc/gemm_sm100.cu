@@ -247,6 +247,13 @@ __device__ __forceinline__ void warp_load_f32_finish(uint32_t* stg, const float4
 }
 
 // Coalesced variants of the forward epilogues (row0 = the warp's first row).
+// Software-pipelined: the TMEM load of chunk c+1 is in flight while chunk c is
+// converted and stored, and the residual rows arrive two chunks ahead.
+__device__ __forceinline__ void unpack_scaled(const uint32_t (&u)[kC], float (&v)[kC], float sc) {
+  #pragma unroll
+  for (int i = 0; i < kC; ++i) v[i] = __uint_as_float(u[i]) * sc;
+}
+
 template <int BN>
 __device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, uint32_t tbase, int row0, int n0,
                                         int half, uint32_t* stg, int lane, float sc) {
@@ -255,14 +262,23 @@ __device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, ui
   if (e.kind == CDK_EPI_SWIGLU) {
     __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(e.out2) + (long long)row0 * e.ldo2;
     __nv_bfloat16* uo = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row0 * e.ldo;
+    const int nch = min(BN / 64, (p.N - n0 - half * kC + 31) / 32);
+    uint32_t ug[kC], uu[kC];
+    if (nch > 0) {
+      tmem_ld_x16_nowait(tbase + half * kC, ug);
+      tmem_ld_x16_nowait(tbase + BN / 2 + half * kC, uu);
+    }
     #pragma unroll 1
-    for (int c = 0; c < BN / 64; ++c) {
-      const int tc = c * 32 + half * kC;
-      const int col = n0 + tc;
-      if (col >= p.N) break;
+    for (int c = 0; c < nch; ++c) {
+      const int col = n0 + c * 32 + half * kC;
       float g[kC], up[kC], h[kC];
-      tmem_ld_f16cols(tbase + tc, g, sc);
-      tmem_ld_f16cols(tbase + BN / 2 + tc, up, sc);
+      tmem_wait_ld();
+      unpack_scaled(ug, g, sc);
+      unpack_scaled(uu, up, sc);
+      if (c + 1 < nch) {
+        tmem_ld_x16_nowait(tbase + (c + 1) * 32 + half * kC, ug);
+        tmem_ld_x16_nowait(tbase + BN / 2 + (c + 1) * 32 + half * kC, uu);
+      }
       #pragma unroll
       for (int i = 0; i < kC; ++i) h[i] = silu_f(g[i]) * up[i];
       warp_store_bf16(stg, g, gu + col, e.ldo2, nvalid, lane);
@@ -271,20 +287,27 @@ __device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, ui
     }
     return;
   }
+  const int nch = min(BN / 32, (p.N - n0 - half * kC + 31) / 32);
+  if (nch <= 0) return;
+  uint32_t ua[kC];
+  tmem_ld_x16_nowait(tbase + half * kC, ua);
   if (e.kind == CDK_EPI_RESID_F32) {
     const float* rbase = e.resid + (long long)row0 * e.ldr;
     float* obase = reinterpret_cast<float*>(e.out) + (long long)row0 * e.ldo;
-    float4 pre[4];
-    warp_load_f32_issue(pre, rbase + n0 + half * kC, e.ldr, nvalid, lane);
+    float4 pre0[4], pre1[4];
+    warp_load_f32_issue(pre0, rbase + n0 + half * kC, e.ldr, nvalid, lane);
+    if (nch > 1) warp_load_f32_issue(pre1, rbase + n0 + 32 + half * kC, e.ldr, nvalid, lane);
     #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      const int tc = c * 32 + half * kC;
-      const int col = n0 + tc;
-      if (col >= p.N) break;
+    for (int c = 0; c < nch; ++c) {
+      const int col = n0 + c * 32 + half * kC;
       float r[kC], v[kC];
-      warp_load_f32_finish(stg, pre, r, lane);
-      if (c + 1 < BN / 32 && col + 32 < p.N) warp_load_f32_issue(pre, rbase + col + 32, e.ldr, nvalid, lane);
-      tmem_ld_f16cols(tbase + tc, v, sc);
+      warp_load_f32_finish(stg, pre0, r, lane);
+      #pragma unroll
+      for (int q = 0; q < 4; ++q) pre0[q] = pre1[q];
+      if (c + 2 < nch) warp_load_f32_issue(pre1, rbase + col + 64, e.ldr, nvalid, lane);
+      tmem_wait_ld();
+      unpack_scaled(ua, v, sc);
+      if (c + 1 < nch) tmem_ld_x16_nowait(tbase + (c + 1) * 32 + half * kC, ua);
       #pragma unroll
       for (int i = 0; i < kC; ++i) v[i] += r[i] + (e.bias != nullptr ? __ldg(e.bias + col + i) : 0.f);
       warp_store_f32(stg, v, obase + col, e.ldo, nvalid, lane);
@@ -295,10 +318,8 @@ __device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, ui
   __nv_bfloat16* obase = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row0 * e.ldo;
   const int pos = row % max(e.seq_len, 1);
   #pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
-    const int tc = c * 32 + half * kC;
-    const int col = n0 + tc;
-    if (col >= p.N) break;
+  for (int c = 0; c < nch; ++c) {
+    const int col = n0 + c * 32 + half * kC;
     float r[kC];
     const bool rope = e.kind == CDK_EPI_ROPE_BF16 && col < e.rope_cols;
     if (rope && lane < nvalid) {
@@ -310,7 +331,9 @@ __device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, ui
       }
     }
     float v[kC];
-    tmem_ld_f16cols(tbase + tc, v, sc);
+    tmem_wait_ld();
+    unpack_scaled(ua, v, sc);
+    if (c + 1 < nch) tmem_ld_x16_nowait(tbase + (c + 1) * 32 + half * kC, ua);
     if (e.bias != nullptr) {
       #pragma unroll
       for (int i = 0; i < kC; ++i) v[i] += __ldg(e.bias + col + i);
