@@ -50,7 +50,10 @@ def parse():
     ap.add_argument("--moe", action="store_true",
                     help="MoE variant: 8 experts, top-2, capacity 1.25, thinking-variation rows, S=4096, "
                          "per-GPU batch 16")
-    ap.add_argument("--seq", type=int, default=None, help="sequence length (default 256; 4096 with --moe)")
+    ap.add_argument("--finetune", action="store_true",
+                    help="finetune step (chessdecoder/finetune/train.py): thinking head + 5-term loss on "
+                         "thinking-variation rows, S=4096, per-GPU batch 4")
+    ap.add_argument("--seq", type=int, default=None, help="sequence length (default 256; 4096 with --moe / --finetune)")
     ap.add_argument("--layers", type=int, default=12)
     ap.add_argument("--pool", type=int, default=4, help="distinct synthetic batches per rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -80,9 +83,11 @@ def step_flops(cfg, db_list, S):
             _, counts = np.unique(ids, return_counts=True)
             pairs += S * (S + 1) // 2 + int((counts * (counts - 1) // 2).sum())
         nm = int(b["move_mask"].sum())
+        nt = int(b["thinking_move_mask"].sum()) if "thinking_move_mask" in b else 0  # thinking head + WL rows
         nd = int(b["wl_positions"].sum())
         pv = E * cfg.value_hidden_size + cfg.value_hidden_size * cfg.n_buckets
-        f = 6 * T * (2 * p_bb + 41 * E) + 6 * nm * (1924 * E + pv) + 6 * nd * pv + 3 * 4 * E * L * pairs
+        f = (6 * T * (2 * p_bb + 41 * E) + 6 * (nm + nt) * (1924 * E + pv) + 6 * nd * pv
+             + 3 * 4 * E * L * pairs)
         out.append(f)
     return sum(out) / len(out)
 
@@ -205,11 +210,11 @@ def run_reference(args, rank, world):
 def main():
     args = parse()
     if args.batch is None:
-        args.batch = 128 if args.fp8 else 16 if args.moe else 64
+        args.batch = 128 if args.fp8 else 16 if args.moe else 4 if args.finetune else 64
     if args.seq is None:
-        args.seq = 4096 if args.moe else 256
-    if args.moe and args.fp8:
-        raise SystemExit("--moe and --fp8 are separate variants")
+        args.seq = 4096 if (args.moe or args.finetune) else 256
+    if args.moe + args.fp8 + args.finetune > 1:
+        raise SystemExit("--moe, --fp8 and --finetune are separate variants")
     from chessdecoder_b200.distributed import setup_distributed, cleanup_distributed
     rank, local_rank, world = setup_distributed() if args.gpus > 1 or "RANK" in os.environ else (0, 0, 1)
     if args.impl == "reference":
@@ -218,16 +223,22 @@ def main():
         return
     import torch.distributed as dist
     from chessdecoder_b200 import data, kernels as K
-    from chessdecoder_b200.engine import ModelConfig, TrainStep, prepare_batch
+    from chessdecoder_b200.engine import FINETUNE_LOSS_WEIGHTS, ModelConfig, TrainStep, prepare_batch
     from chessdecoder_b200.distributed import DataParallelStep
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    cfg = ModelConfig(num_layers=args.layers, max_seq_len=args.seq, moe_experts=8 if args.moe else 0)
-    step = TrainStep(cfg, device=dev, seed=0, fp8=args.fp8)
+    cfg = ModelConfig(num_layers=args.layers, max_seq_len=args.seq, moe_experts=8 if args.moe else 0,
+                      finetune=args.finetune)
+    if args.finetune:  # chessdecoder/finetune/config.yaml: lr 3e-5, loss weights 3/1/3/3/3
+        step = TrainStep(cfg, device=dev, seed=0, lr=3e-5, loss_weights=FINETUNE_LOSS_WEIGHTS)
+    else:
+        step = TrainStep(cfg, device=dev, seed=0, fp8=args.fp8)
     dp = DataParallelStep(step)
     if args.moe:
         pool = data.thinking_batches(args.pool, args.batch, args.seq, seed=1234, rank=rank)
+    elif args.finetune:
+        pool = data.finetune_batches(args.pool, args.batch, args.seq, seed=1234, rank=rank)
     else:
         pool = data.synthetic_batches(args.pool, args.batch, args.seq, seed=1234, rank=rank)
     dbs = [prepare_batch(b, dev) for b in pool]
@@ -333,7 +344,7 @@ def main():
                             "pool; the dense fp8 spec is 4.5 PFLOP/s)")
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.moe:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.moe and not args.finetune:
         cpu = cpu_baseline(pool[0], dict(embed_dim=1024, num_heads=16, num_layers=args.layers,
                                          max_seq_len=args.seq, d_ff=1536), args.cpu_steps)
     if rank == 0:
@@ -341,11 +352,14 @@ def main():
                 "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None,
                 "dtype": "fp8 (e4m3 activations/weights, e5m2 grads) backbone linears; bf16 attention and heads"
-                if args.fp8 else "bf16", "data": "synthetic thinking-variation rows" if args.moe else "synthetic",
-                "config": {"workload": ("ChessDecoder pretraining step (pass-1 causal + pass-2 prefix fwd, bwd, "
-                                        "clip, AdamW), default model E=1024 H=16 L=%d d_ff=1536" % args.layers)
+                if args.fp8 else "bf16", "data": "synthetic thinking-variation rows" if (args.moe or args.finetune)
+                else "synthetic",
+                "config": {"workload": ("ChessDecoder %s step (pass-1 causal + pass-2 prefix fwd, bwd, "
+                                        "clip, AdamW), default model E=1024 H=16 L=%d d_ff=1536"
+                                        % ("finetune" if args.finetune else "pretraining", args.layers))
                            + (", fp8 variant (per-tensor delayed scaling, amax history 16)" if args.fp8 else "")
-                           + (", MoE variant (8 experts, top-2, capacity 1.25)" if args.moe else ""),
+                           + (", MoE variant (8 experts, top-2, capacity 1.25)" if args.moe else "")
+                           + (", finetune step (thinking head, 5-term loss)" if args.finetune else ""),
                            "global_batch": args.batch * world, "seq_len": args.seq,
                            "parallelism": f"dp{world}", "per_gpu_batch": args.batch,
                            "l2": "working set (activations ~11 GB) far larger than L2; no flush needed",

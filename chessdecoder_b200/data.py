@@ -248,3 +248,85 @@ def thinking_batches(n_batches: int, batch_size: int, max_seq_len: int = 4096, s
             rows.append(tensorize(ids, mt, blocks, values, rng, max_seq_len, random_start=False))
         out.append(collate(rows))
     return out
+
+
+# ---------------------------------------------------------------------------
+# Finetune rows (thinking head + final move): chessdecoder/finetune/loader.py
+# ---------------------------------------------------------------------------
+FINETUNE_KEYS = KEYS + ("thinking_move_mask",)
+
+
+def tensorize_variation(ids, thinking, final, values, blocks, max_seq_len: int):
+    """One finetune row as ``_build_variation_tensors`` builds it
+    (chessdecoder/finetune/loader.py:337-440): shifted board targets; at every
+    thinking prediction position the move target, ``thinking_move_mask`` and a
+    board target of ``generic_move`` (after ``start_think``), ``new_variation``
+    (after ``end_var``) or ``continue_var`` (a board's stm); at the final
+    prediction position (``end_think``) the move target, ``move_mask`` and
+    ``generic_move``; WL / D targets at their placeholders and copied to the
+    prediction position two tokens before the WL placeholder; a block id per
+    board, unique ids elsewhere.
+
+    thinking: [(predict_pos, move_token)], final: (predict_pos, move_token) or None,
+    values: [(wl_pos, d_pos, wl, d, valid)], blocks: [(start, end)]."""
+    S = max_seq_len
+    n = min(len(ids), S)
+    input_ids = np.full(S, V.token_to_idx["pad"], dtype=np.int64)
+    input_ids[:n] = ids[:n]
+    board_t = np.full(S, IGNORE_INDEX, dtype=np.int64)
+    if n > 1:
+        board_t[: n - 1] = _FULL_TO_BOARD[input_ids[1:n]]
+    move_t = np.full(S, IGNORE_INDEX, dtype=np.int64)
+    move_mask = np.zeros(S, dtype=bool)
+    think_mask = np.zeros(S, dtype=bool)
+    start_think, end_var = V.token_to_idx["start_think"], V.token_to_idx["end_var"]
+    bt = V.board_token_to_idx
+    for pos, mv in thinking:
+        if not 0 <= pos < S:
+            continue
+        move_t[pos] = V.full_idx_to_move_idx[V.token_to_idx[mv]]
+        think_mask[pos] = True
+        tok = ids[pos]
+        board_t[pos] = (bt["generic_move"] if tok == start_think else
+                        bt["new_variation"] if tok == end_var else bt["continue_var"])
+    if final is not None and 0 <= final[0] < S:
+        move_t[final[0]] = V.full_idx_to_move_idx[V.token_to_idx[final[1]]]
+        move_mask[final[0]] = True
+        board_t[final[0]] = bt["generic_move"]
+    wl_pos = np.zeros(S, dtype=bool)
+    d_pos = np.zeros(S, dtype=bool)
+    wl_t = np.zeros(S, dtype=np.float32)
+    d_t = np.zeros(S, dtype=np.float32)
+    valid = np.zeros(S, dtype=bool)
+    for w, d, wl, dd, ok in values:
+        if w < S:
+            wl_pos[w], wl_t[w], valid[w] = True, wl, ok
+        if d < S:
+            d_pos[d], d_t[d], valid[d] = True, dd, ok
+        p = w - 2
+        if 0 <= p < S:
+            wl_t[p], d_t[p], valid[p] = wl, dd, ok
+    block_id = np.arange(S, dtype=np.int64) + len(blocks)
+    for k, (b0, b1) in enumerate(blocks):
+        block_id[b0:b1] = k
+    return {"input_ids": input_ids, "board_target_ids": board_t, "move_target_ids": move_t, "move_mask": move_mask,
+            "wl_positions": wl_pos, "d_positions": d_pos, "wl_targets": wl_t, "d_targets": d_t,
+            "wdl_valid": valid, "block_id": block_id, "thinking_move_mask": think_mask}
+
+
+def finetune_batches(n_batches: int, batch_size: int, max_seq_len: int = 4096, seed: int = 0, rank: int = 0,
+                     min_lines: int = 3, max_lines: int = 6, min_depth: int = 2, max_depth: int = 8):
+    """Seeded finetune batches: thinking-variation sequences (the layout of
+    chessdecoder/finetune/data.py:144-247) in which every variation move is a
+    thinking-head target and the move after ``end_think`` the policy-head
+    target."""
+    rng = random.Random(seed + rank * 7919)
+    out = []
+    for _ in range(n_batches):
+        rows = []
+        for _ in range(batch_size):
+            ids, mt, blocks, values = thinking_game_to_token_ids(rng, min_lines, max_lines, min_depth, max_depth)
+            preds = [(m - 1, mv) for m, mv in mt]  # each move is predicted from the token before it
+            rows.append(tensorize_variation(ids, preds[:-1], preds[-1], values, blocks, max_seq_len))
+        out.append({k: torch.from_numpy(np.stack([r[k] for r in rows])) for k in FINETUNE_KEYS})
+    return out

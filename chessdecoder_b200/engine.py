@@ -50,6 +50,7 @@ class ModelConfig:
     wl_sigma: float = 0.4
     moe_experts: int = 0        # MoE variant: experts per layer (0 = the dense SwiGLU MLP)
     moe_capacity: float = 1.25  # capacity factor (slots per expert = ceil(cf * 2 * tokens / experts))
+    finetune: bool = False      # finetune step: the thinking head is trained (chessdecoder/finetune/train.py)
 
     @property
     def head_dim(self):
@@ -90,6 +91,9 @@ def param_specs(cfg: ModelConfig):
     hv, nb, nf = cfg.value_hidden_size, cfg.n_buckets, cfg.num_fourier_freq
     specs = [("board_head.weight", (V.board_vocab_size, E)), ("board_head.bias", (V.board_vocab_size,)),
              ("policy_head.weight", (V.move_vocab_size, E)), ("policy_head.bias", (V.move_vocab_size,))]
+    if cfg.finetune:  # trained only by the finetune step; pretraining leaves it out of AdamW
+        specs += [("thinking_policy_head.weight", (V.move_vocab_size, E)),
+                  ("thinking_policy_head.bias", (V.move_vocab_size,))]
     for h in ("wl_head", "d_head"):
         specs += [(f"{h}.mlp.0.weight", (hv, E)), (f"{h}.mlp.0.bias", (hv,)), (f"{h}.mlp.2.weight", (nb, hv)),
                   (f"{h}.mlp.2.bias", (nb,))]
@@ -141,7 +145,8 @@ class ParamStore:
         else:  # the nn.Module front end: gradients are allocated per backward, moments by the optimizer
             self.grad = self.exp_avg = self.exp_avg_sq = None
         self.step = 0
-        # the thinking head gets no gradient in pretraining (train.py never calls it)
+        # the thinking head gets no gradient in pretraining (train.py never calls
+        # it): kept outside the flat buffers unless the finetune step trains it
         E = cfg.embed_dim
         self.thinking_weight = torch.zeros(V.move_vocab_size, E, device=self.device)
         self.thinking_bias = torch.zeros(V.move_vocab_size, device=self.device)
@@ -177,15 +182,16 @@ class ParamStore:
         with torch.no_grad():
             for name in self.offsets:
                 self.param(name).copy_(sd[name].reshape(self.offsets[name][1]))
-            if "thinking_policy_head.weight" in sd:
+            if "thinking_policy_head.weight" in sd and "thinking_policy_head.weight" not in self.offsets:
                 self.thinking_weight.copy_(sd["thinking_policy_head.weight"])
                 self.thinking_bias.copy_(sd["thinking_policy_head.bias"])
         self.refresh_bf16()
 
     def state_dict(self) -> dict:
         sd = {name: self.param(name).detach().clone() for name in self.offsets}
-        sd["thinking_policy_head.weight"] = self.thinking_weight.clone()
-        sd["thinking_policy_head.bias"] = self.thinking_bias.clone()
+        if "thinking_policy_head.weight" not in self.offsets:
+            sd["thinking_policy_head.weight"] = self.thinking_weight.clone()
+            sd["thinking_policy_head.bias"] = self.thinking_bias.clone()
         return sd
 
     def layer_grad_span(self, i: int):
@@ -272,7 +278,9 @@ class DeviceBatch:
     drow: torch.Tensor           # i32 [Nd]
     dtgt: torch.Tensor           # f32 [Nd]
     dvalid: torch.Tensor         # f32 [Nd]
-    norms: torch.Tensor          # f32 [4] = 1/(count+1e-8) for move, board, wl, d (0 when the loss is 0)
+    norms: torch.Tensor          # f32 [5] = 1/(count+1e-8) for move, board, wl, d, thinking move (0 when the loss is 0)
+    trow: Optional[torch.Tensor] = None  # i32 [Nt]  merged-batch rows of the thinking head (finetune)
+    tt: Optional[torch.Tensor] = None    # i32 [Nt]
     h2d_bytes: int = 0
 
 
@@ -282,7 +290,12 @@ def _host_index_lists(b: dict, require_pairing: bool = True):
     The D head reads rows at wl_positions with targets at d_positions, zipped
     in order (train.py:225-230); unequal counts are an error there, and here
     unless ``require_pairing`` is False (forward-only use), in which case the
-    D rows are cut to the shorter list."""
+    D rows are cut to the shorter list.
+
+    A batch with ``thinking_move_mask`` is a finetune batch
+    (chessdecoder/finetune/train.py:287-346): the board mask starts at the
+    first move of either kind, the thinking head reads the thinking rows, and
+    the WL head reads stm+1 of every move row of either kind."""
     ids = b["input_ids"].numpy()
     Bn, S = ids.shape
     move_mask = b["move_mask"].numpy()
@@ -295,8 +308,10 @@ def _host_index_lists(b: dict, require_pairing: bool = True):
     valid = b["wdl_valid"].numpy()
     BS = Bn * S
     # board mask: target != -100 and position >= first move (train.py:183-191)
-    has = move_mask.any(1)
-    first = np.where(has, move_mask.argmax(1), S)
+    think = b["thinking_move_mask"].numpy() if "thinking_move_mask" in b else np.zeros_like(move_mask)
+    any_move = move_mask | think
+    has = any_move.any(1)
+    first = np.where(has, any_move.argmax(1), S)
     board_mask = (board_t != IGNORE_INDEX) & (np.arange(S)[None, :] >= first[:, None])
     # Fourier slots: every WL or D placeholder
     fmask = (wl_pos | d_pos).reshape(-1)
@@ -307,8 +322,12 @@ def _host_index_lists(b: dict, require_pairing: bool = True):
     mflat = np.nonzero(move_mask.reshape(-1))[0]
     prow = (BS + mflat).astype(np.int32)
     pt = move_t.reshape(-1)[mflat].astype(np.int32)
+    # thinking-head rows (finetune) in the same merged-batch layout
+    tflat = np.nonzero(think.reshape(-1))[0]
+    trow = (BS + tflat).astype(np.int32)
+    tt = move_t.reshape(-1)[tflat].astype(np.int32)
     # WL rows at stm + 1 (clamped), targets copied to stm by the loader
-    bb, ss = np.nonzero(move_mask)
+    bb, ss = np.nonzero(any_move)
     wrow = (BS + bb * S + np.minimum(ss + 1, S - 1)).astype(np.int32)
     wtgt = wl_t[bb, ss]
     wvalid = valid[bb, ss].astype(np.float32)
@@ -329,12 +348,13 @@ def _host_index_lists(b: dict, require_pairing: bool = True):
         1.0 / (nb + 1e-8),
         (1.0 / (wvalid.sum() + 1e-8)) if (wvalid.size and wvalid.sum() > 0) else 0.0,
         (1.0 / (dvalid.sum() + 1e-8)) if (dvalid.size and dvalid.sum() > 0) else 0.0,
+        1.0 / (tflat.size + 1e-8),
     ], dtype=np.float32)
     board_t32 = np.where(board_mask, board_t, IGNORE_INDEX).reshape(-1).astype(np.int32)
     return dict(ids=ids.reshape(-1).astype(np.int64), wl_t=wl_t.reshape(-1), d_t=d_t.reshape(-1),
                 wl_pos=wl_pos.reshape(-1).astype(np.uint8), d_pos=d_pos.reshape(-1).astype(np.uint8), slot=slot,
                 frows=frows, bid=b["block_id"].numpy().astype(np.int32), board_t=board_t32,
-                board_w=board_mask.reshape(-1).astype(np.float32), prow=prow, pt=pt, wrow=wrow,
+                board_w=board_mask.reshape(-1).astype(np.float32), prow=prow, pt=pt, trow=trow, tt=tt, wrow=wrow,
                 wtgt=wtgt.astype(np.float32), wvalid=wvalid, drow=drow, dtgt=dtgt.astype(np.float32), dvalid=dvalid,
                 norms=norms), Bn, S
 
@@ -345,7 +365,7 @@ def prepare_batch(batch: dict, device, require_pairing: bool = True) -> DeviceBa
     host = {k: (v.cpu() if torch.is_tensor(v) else torch.as_tensor(v)) for k, v in batch.items()}
     lists, Bn, S = _host_index_lists(host, require_pairing)
     groups = {"i64": ["ids"], "f32": ["wl_t", "d_t", "board_w", "wtgt", "wvalid", "dtgt", "dvalid", "norms"],
-              "i32": ["slot", "frows", "bid", "board_t", "prow", "pt", "wrow", "drow"],
+              "i32": ["slot", "frows", "bid", "board_t", "prow", "pt", "trow", "tt", "wrow", "drow"],
               "u8": ["wl_pos", "d_pos"]}
     dt = {"i64": torch.int64, "f32": torch.float32, "i32": torch.int32, "u8": torch.uint8}
     out = {}
@@ -704,12 +724,15 @@ class Heads:
     def __init__(self, store: ParamStore, cfg: ModelConfig, loss_weights=(5.0, 1.0, 1.0, 1.0)):
         self.st = store
         self.cfg = cfg
-        self.w_move, self.w_board, self.w_wl, self.w_d = loss_weights
+        self.w_move, self.w_board, self.w_wl, self.w_d = loss_weights[:4]
+        self.w_think = loss_weights[4] if len(loss_weights) > 4 else 0.0
+        if self.w_think and not cfg.finetune:
+            raise ValueError("a thinking-move loss weight needs ModelConfig(finetune=True)")
         self.wl_c = make_wl_buckets(cfg.n_buckets, cfg.wl_sigma).to(store.device)
         self.d_c = make_d_buckets(cfg.n_buckets).to(store.device)
 
     def run(self, db: DeviceBatch, hN16, losses, metrics=None):
-        """losses: f32 [4] (move, board, wl, d), accumulated.  Returns dhN f32 [2*B*S, E]."""
+        """losses: f32 [5] (move, board, wl, d, thinking move), accumulated.  Returns dhN f32 [2*B*S, E]."""
         st, cfg = self.st, self.cfg
         E = cfg.embed_dim
         BS = db.B * db.S
@@ -730,28 +753,39 @@ class Heads:
         K.gemm(dl, st.bf16("board_head.weight"), b_mn=True, kind=K.EPI_STORE_F32, out=dhN[:BS], K=nbv)
         K.gemm(dl, hN16[:BS], a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=st.grad_of("board_head.weight"),
                M=nbv, K=BS)
-        # ---- policy head over gathered move rows ----------------------------
-        Nm = db.prow.numel()
-        if Nm:
-            nmv = V.move_vocab_size
-            hp = torch.empty(Nm, E, device=dev, dtype=torch.bfloat16)
-            K.gather_rows_bf16(hN16, db.prow, hp)
-            lp = torch.empty(Nm, nmv, device=dev)
-            K.gemm(hp, st.bf16("policy_head.weight"), kind=K.EPI_STORE_F32, out=lp, bias=st.param("policy_head.bias"))
-            dlp = torch.empty(Nm, 1928, device=dev, dtype=torch.bfloat16)
-            pam = metrics.get("move_argmax") if metrics is not None else None
-            K.softmax_ce(lp, db.pt, None, norms[0:1], self.w_move, dlogits=dlp, dbias=st.grad_of("policy_head.bias"),
-                         loss_out=losses[0:1], argmax=pam, ncls=nmv)
-            dhp = torch.empty(Nm, E, device=dev)
-            K.gemm(dlp, st.bf16("policy_head.weight"), b_mn=True, kind=K.EPI_STORE_F32, out=dhp, K=nmv)
-            K.scatter_add_rows(dhp, db.prow, dhN)
-            K.gemm(dlp, hp, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=st.grad_of("policy_head.weight"),
-                   M=nmv, K=Nm)
+        # ---- policy head over gathered move rows; thinking head (finetune) ----
+        pam = metrics.get("move_argmax") if metrics is not None else None
+        self._move_head("policy_head", db.prow, db.pt, norms[0:1], self.w_move, hN16, dhN, losses[0:1], pam)
+        if db.trow is not None and db.trow.numel():
+            tam = metrics.get("thinking_argmax") if metrics is not None else None
+            self._move_head("thinking_policy_head", db.trow, db.tt, norms[4:5], self.w_think, hN16, dhN,
+                            losses[4:5], tam)
         # ---- value heads ------------------------------------------------------
         self._value("wl_head", db.wrow, db.wtgt, db.wvalid, self.wl_c, norms[2:3], self.w_wl, hN16, dhN,
                     losses[2:3])
         self._value("d_head", db.drow, db.dtgt, db.dvalid, self.d_c, norms[3:4], self.w_d, hN16, dhN, losses[3:4])
         return dhN
+
+    def _move_head(self, name, rows, tgt, norm, weight, hN16, dhN, loss, argmax=None):
+        """Move-vocabulary head + masked CE on gathered rows (train.py:204-207;
+        the thinking head of chessdecoder/finetune/train.py:315-318 is the
+        same statement)."""
+        n = rows.numel()
+        if n == 0:
+            return
+        st, E, dev = self.st, self.cfg.embed_dim, hN16.device
+        nmv = V.move_vocab_size
+        hp = torch.empty(n, E, device=dev, dtype=torch.bfloat16)
+        K.gather_rows_bf16(hN16, rows, hp)
+        lp = torch.empty(n, nmv, device=dev)
+        K.gemm(hp, st.bf16(f"{name}.weight"), kind=K.EPI_STORE_F32, out=lp, bias=st.param(f"{name}.bias"))
+        dlp = torch.empty(n, 1928, device=dev, dtype=torch.bfloat16)
+        K.softmax_ce(lp, tgt, None, norm, weight, dlogits=dlp, dbias=st.grad_of(f"{name}.bias"), loss_out=loss,
+                     argmax=argmax, ncls=nmv)
+        dhp = torch.empty(n, E, device=dev)
+        K.gemm(dlp, st.bf16(f"{name}.weight"), b_mn=True, kind=K.EPI_STORE_F32, out=dhp, K=nmv)
+        K.scatter_add_rows(dhp, rows, dhN)
+        K.gemm(dlp, hp, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=st.grad_of(f"{name}.weight"), M=nmv, K=n)
 
     def _value(self, name, rows, tgt, valid, centers, norm, weight, hN16, dhN, loss):
         n = rows.numel()
@@ -818,11 +852,12 @@ class TrainStep:
 
     def forward_backward(self, db: DeviceBatch, metrics=None):
         """Loss forward + full backward into store.grad (zeroed here).  Returns
-        losses f32 [4] = (move, board, wl, d) on the device."""
+        losses f32 [5] = (move, board, wl, d, thinking move) on the device
+        (the last is 0 outside the finetune step)."""
         st = self.store
         st.grad.zero_()
         B, S = db.B, db.S
-        losses = torch.zeros(4, device=self.device)
+        losses = torch.zeros(5, device=self.device)
         meta = K.attn_meta(db.bid, S)
         if self.fp8 is not None:
             self.backbone.cast_fp8_weights()
@@ -854,3 +889,7 @@ class TrainStep:
     @staticmethod
     def total(losses, weights=(5.0, 1.0, 1.0, 1.0)):
         return sum(w * losses[i] for i, w in enumerate(weights))
+
+
+# Loss weights of chessdecoder/finetune/config.yaml (final move, board, wl, d, thinking move).
+FINETUNE_LOSS_WEIGHTS = (3.0, 1.0, 3.0, 3.0, 3.0)
