@@ -12,6 +12,8 @@
 #include "../../include/cdk.h"
 #include "cdk_common.cuh"
 
+#include <type_traits>
+
 namespace cdk {
 
 template <int VPT>  // float4 per lane; dim = 128 * VPT
@@ -79,53 +81,69 @@ __device__ __forceinline__ float4 load_dy4(const void* dy, long long idx4) {
 
 // dx = dres + r * (g - xhat * mean(g * xhat)),  g = dy * scale, xhat = x * r
 // dscale[c] += sum_rows dy[c] * xhat[c]
+// A warp issues all of a row's loads (x, dy, dres) before its first use, so
+// each warp keeps three streams in flight; the scale lives in shared memory.
 template <int VPT, bool DY_F32>
-__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const void* __restrict__ dy, const float* __restrict__ x,
-                                                          const float* __restrict__ scale,
-                                                          const float* __restrict__ rstd,
-                                                          const float* __restrict__ dres, float* __restrict__ dx,
-                                                          __nv_bfloat16* __restrict__ dx16,
-                                                          float* __restrict__ dscale, long long rows) {
+__global__ void __launch_bounds__(256, 2) rmsnorm_bwd_kernel(const void* __restrict__ dy, const float* __restrict__ x,
+                                                             const float* __restrict__ scale,
+                                                             const float* __restrict__ rstd,
+                                                             const float* __restrict__ dres, float* __restrict__ dx,
+                                                             __nv_bfloat16* __restrict__ dx16,
+                                                             float* __restrict__ dscale, long long rows) {
   constexpr int dim = 128 * VPT;
-  extern __shared__ float red[];  // [8][dim]
+  extern __shared__ float red[];  // [8][dim] per-warp column partials of dscale, then [dim] scale
+  float* ssc = red + 8 * dim;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float4 ds[VPT];
+  for (int c = threadIdx.x; c < dim; c += blockDim.x) ssc[c] = scale[c];
+  float4* myds = reinterpret_cast<float4*>(red + warp * dim);
   #pragma unroll
-  for (int i = 0; i < VPT; ++i) ds[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 sc[VPT];
-  #pragma unroll
-  for (int i = 0; i < VPT; ++i) sc[i] = reinterpret_cast<const float4*>(scale)[lane + 32 * i];
+  for (int i = 0; i < VPT; ++i) myds[lane + 32 * i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncthreads();
+  const float4* sc4 = reinterpret_cast<const float4*>(ssc);
 
   for (long long row = (long long)blockIdx.x * 8 + warp; row < rows; row += (long long)gridDim.x * 8) {
-    const float r = rstd[row];
-    float4 xv[VPT], gv[VPT];
-    float dot = 0.f;
+    float4 xv[VPT], qv[VPT];
+    typename std::conditional<DY_F32, float4, uint2>::type draw[VPT];
     #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const long long idx4 = row * (dim / 4) + lane + 32 * i;
       xv[i] = reinterpret_cast<const float4*>(x)[idx4];
-      const float4 d = load_dy4<DY_F32>(dy, idx4);
+      if constexpr (DY_F32) draw[i] = reinterpret_cast<const float4*>(dy)[idx4];
+      else draw[i] = reinterpret_cast<const uint2*>(dy)[idx4];
+      qv[i] = dres ? reinterpret_cast<const float4*>(dres)[idx4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    auto dyv = [&](int i) -> float4 {
+      if constexpr (DY_F32) {
+        return draw[i];
+      } else {
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&draw[i].x));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&draw[i].y));
+        return make_float4(a.x, a.y, b.x, b.y);
+      }
+    };
+    const float r = rstd[row];
+    float dot = 0.f;
+    #pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const float4 s = sc4[lane + 32 * i];
+      const float4 d = dyv(i);
       xv[i] = make_float4(xv[i].x * r, xv[i].y * r, xv[i].z * r, xv[i].w * r);  // xhat
-      gv[i] = make_float4(d.x * sc[i].x, d.y * sc[i].y, d.z * sc[i].z, d.w * sc[i].w);
-      dot += gv[i].x * xv[i].x + gv[i].y * xv[i].y + gv[i].z * xv[i].z + gv[i].w * xv[i].w;
-      ds[i].x += d.x * xv[i].x;
-      ds[i].y += d.y * xv[i].y;
-      ds[i].z += d.z * xv[i].z;
-      ds[i].w += d.w * xv[i].w;
+      dot += d.x * s.x * xv[i].x + d.y * s.y * xv[i].y + d.z * s.z * xv[i].z + d.w * s.w * xv[i].w;
+      float4 a = myds[lane + 32 * i];
+      a.x += d.x * xv[i].x;
+      a.y += d.y * xv[i].y;
+      a.z += d.z * xv[i].z;
+      a.w += d.w * xv[i].w;
+      myds[lane + 32 * i] = a;
     }
     dot = warp_sum(dot) / (float)dim;
     #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const long long idx4 = row * (dim / 4) + lane + 32 * i;
-      float4 o = make_float4(r * (gv[i].x - xv[i].x * dot), r * (gv[i].y - xv[i].y * dot),
-                             r * (gv[i].z - xv[i].z * dot), r * (gv[i].w - xv[i].w * dot));
-      if (dres) {
-        const float4 q = reinterpret_cast<const float4*>(dres)[idx4];
-        o.x += q.x;
-        o.y += q.y;
-        o.z += q.z;
-        o.w += q.w;
-      }
+      const float4 s = sc4[lane + 32 * i];
+      const float4 d = dyv(i);
+      const float4 o = make_float4(qv[i].x + r * (d.x * s.x - xv[i].x * dot), qv[i].y + r * (d.y * s.y - xv[i].y * dot),
+                                   qv[i].z + r * (d.z * s.z - xv[i].z * dot), qv[i].w + r * (d.w * s.w - xv[i].w * dot));
       if (dx) reinterpret_cast<float4*>(dx)[idx4] = o;
       if (dx16) {
         uint2 w;
@@ -136,8 +154,6 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const void* __restrict
     }
   }
   if (dscale) {
-    #pragma unroll
-    for (int i = 0; i < VPT; ++i) reinterpret_cast<float4*>(red + warp * dim)[lane + 32 * i] = ds[i];
     __syncthreads();
     for (int c = threadIdx.x; c < dim; c += blockDim.x) {
       float s = 0.f;
@@ -158,9 +174,9 @@ static int num_sms_dev() {
 template <int VPT>
 static int launch_bwd(const void* dy, int dy_f32, const float* x, const float* scale, const float* rstd,
                       const float* dres, float* dx, void* dx16, float* dscale, long long rows, cudaStream_t s) {
-  const size_t smem = (size_t)8 * 128 * VPT * sizeof(float);
+  const size_t smem = (size_t)9 * 128 * VPT * sizeof(float);
   long long blocks = (rows + 7) / 8;
-  const long long cap = (long long)num_sms_dev() * 4;
+  const long long cap = (long long)num_sms_dev() * 2;
   if (blocks > cap) blocks = cap;
   if (dy_f32) {
     auto k = rmsnorm_bwd_kernel<VPT, true>;
