@@ -246,6 +246,36 @@ __device__ __forceinline__ void warp_load_f32_finish(uint32_t* stg, const float4
   __syncwarp();
 }
 
+// Row-contiguous bf16 loads of 32 rows x 16 columns (two lanes per row),
+// transposed through shared memory so that lane = row.
+__device__ __forceinline__ void warp_load_bf16_issue(uint4 (&t)[2], const __nv_bfloat16* g, long long ld, int nvalid,
+                                                     int lane) {
+  const int c = lane & 1;
+  #pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int r = k * 16 + (lane >> 1);
+    t[k] = r < nvalid ? __ldg(reinterpret_cast<const uint4*>(g + (long long)r * ld + c * 8)) : make_uint4(0, 0, 0, 0);
+  }
+}
+__device__ __forceinline__ void warp_load_bf16_finish(uint32_t* stg, const uint4 (&t)[2], float (&v)[kC], int lane) {
+  const int c = lane & 1;
+  #pragma unroll
+  for (int k = 0; k < 2; ++k) *reinterpret_cast<uint4*>(stg + (k * 16 + (lane >> 1)) * kStgB16 + c * 4) = t[k];
+  __syncwarp();
+  #pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const uint4 w = *reinterpret_cast<const uint4*>(stg + lane * kStgB16 + q * 4);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      v[8 * q + 2 * j] = f.x;
+      v[8 * q + 2 * j + 1] = f.y;
+    }
+  }
+  __syncwarp();
+}
+
 // Coalesced variants of the forward epilogues (row0 = the warp's first row).
 // Software-pipelined: the TMEM load of chunk c+1 is in flight while chunk c is
 // converted and stored, and the residual rows arrive two chunks ahead.
@@ -254,7 +284,7 @@ __device__ __forceinline__ void unpack_scaled(const uint32_t (&u)[kC], float (&v
   for (int i = 0; i < kC; ++i) v[i] = __uint_as_float(u[i]) * sc;
 }
 
-template <int BN>
+template <int BN, bool F8>
 __device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, uint32_t tbase, int row0, int n0,
                                         int half, uint32_t* stg, int lane, float sc) {
   const int nvalid = min(32, p.M - row0);
@@ -291,6 +321,38 @@ __device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, ui
   if (nch <= 0) return;
   uint32_t ua[kC];
   tmem_ld_x16_nowait(tbase + half * kC, ua);
+  if (!F8 && e.kind == CDK_EPI_DSWIGLU) {  // (the host keeps fp8 DSWIGLU launches off this path)
+    // acc = d(silu(g) * u) for columns n0..; aux = [g | u]; out = [dg | du]
+    const __nv_bfloat16* abase = e.aux + (long long)row0 * e.ldaux;
+    __nv_bfloat16* obase = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row0 * e.ldo;
+    uint4 g0[2], u0[2];
+    warp_load_bf16_issue(g0, abase + n0 + half * kC, e.ldaux, nvalid, lane);
+    warp_load_bf16_issue(u0, abase + e.half_n + n0 + half * kC, e.ldaux, nvalid, lane);
+    #pragma unroll 1
+    for (int c = 0; c < nch; ++c) {
+      const int col = n0 + c * 32 + half * kC;
+      float g[kC], up[kC], v[kC];
+      warp_load_bf16_finish(stg, g0, g, lane);
+      warp_load_bf16_finish(stg, u0, up, lane);
+      if (c + 1 < nch) {  // the next chunk's gate / up rows (L2-prefetched a tile ahead)
+        warp_load_bf16_issue(g0, abase + col + 32, e.ldaux, nvalid, lane);
+        warp_load_bf16_issue(u0, abase + e.half_n + col + 32, e.ldaux, nvalid, lane);
+      }
+      tmem_wait_ld();
+      unpack_scaled(ua, v, sc);
+      if (c + 1 < nch) tmem_ld_x16_nowait(tbase + (c + 1) * 32 + half * kC, ua);
+      float dg[kC], du[kC];
+      #pragma unroll
+      for (int i = 0; i < kC; ++i) {
+        const float sg = 1.f / (1.f + __expf(-g[i]));
+        du[i] = v[i] * g[i] * sg;
+        dg[i] = v[i] * up[i] * (sg * (1.f + g[i] * (1.f - sg)));
+      }
+      warp_store_bf16(stg, dg, obase + col, e.ldo, nvalid, lane);
+      warp_store_bf16(stg, du, obase + e.half_n + col, e.ldo, nvalid, lane);
+    }
+    return;
+  }
   if (e.kind == CDK_EPI_RESID_F32) {
     const float* rbase = e.resid + (long long)row0 * e.ldr;
     float* obase = reinterpret_cast<float*>(e.out) + (long long)row0 * e.ldo;
@@ -629,7 +691,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (VEC) {
         const int row0 = mt * kBM + quad * 32;
         if (row0 < p.M)
-          epi_vec<BN>(e, p, tbase, row0, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN, half, stg, lane, sc);
+          epi_vec<BN, F8>(e, p, tbase, row0, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN, half, stg, lane,
+                          sc);
       } else switch (e.kind) {
         case CDK_EPI_SWIGLU: epi_swiglu<BN>(e, p, tbase, row, row_ok, nt * (BN / 2), half, sc); break;
         case CDK_EPI_STORE_BF16: epi_tile<BN, CDK_EPI_STORE_BF16>(e, p, tbase, row, row_ok, nt * BN, half, sc); break;
@@ -895,6 +958,7 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
     if (kind == CDK_EPI_RESID_F32) v = v && epi->ldo % 4 == 0 && epi->ldr % 4 == 0 && al16(epi->resid);
     else if (kind == CDK_EPI_STORE_BF16 || kind == CDK_EPI_ROPE_BF16) v = v && epi->ldo % 8 == 0;
     else if (kind == CDK_EPI_SWIGLU) v = v && epi->ldo % 8 == 0 && epi->ldo2 % 8 == 0 && epi->half_n % 8 == 0 && al16(epi->out2);
+    else if (kind == CDK_EPI_DSWIGLU) v = v && !f8 && epi->ldo % 8 == 0 && epi->ldaux % 8 == 0 && epi->half_n % 8 == 0 && al16(epi->aux);
     else v = false;
     if (kind == CDK_EPI_ROPE_BF16) v = v && epi->seq_len > 0;
     p.epi.vec = v && !a_mn ? 1 : 0;

@@ -130,8 +130,9 @@ def test_gemm_rope(K):
     assert rel_err(out, ref) < 1e-2
 
 
-def test_gemm_swiglu_and_back(K):
-    T, E, F = 1024, 512, 768
+@pytest.mark.parametrize("T", [1024, 1000])
+def test_gemm_swiglu_and_back(K, T):
+    E, F = 512, 768
     X, W13 = _bf(T, E), _bf(2 * F, E, scale=0.05)
     u = torch.empty(T, F, device=DEV, dtype=torch.bfloat16)
     gu = torch.empty(T, 2 * F, device=DEV, dtype=torch.bfloat16)
