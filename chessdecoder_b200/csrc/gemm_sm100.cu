@@ -13,6 +13,8 @@
 #include "../../include/cdk.h"
 #include "cdk_common.cuh"
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 namespace cdk {
@@ -20,6 +22,13 @@ namespace cdk {
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = 128 B = one swizzle row (128 fp8 elements in the fp8 instantiations)
 constexpr int kThreads = 320;
+// TMA-fed epilogue (residual add, SwiGLU backward): an 11th warp streams the
+// epilogue's global operand through a ring of 8 x 8 KB shared-memory slots
+// (16 columns x 128 rows per slot) and writes the results back by TMA store;
+// the mainloop ring gives up one (BN=256) stage for it.
+constexpr int kThreadsTE = 352;
+constexpr int kTeSlots = 8;
+constexpr int kTeSlotBytes = 8192;
 
 template <int BN>
 struct GemmCfg {
@@ -31,6 +40,8 @@ struct GemmCfg {
   static constexpr int kBarrierBytes = 256;
   static constexpr int kStagingBytes = 8 * 2560;  // per epilogue warp: 32 rows x 80 B transpose buffer
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes + kStagingBytes;
+  static constexpr int kStagesTE = BN == 256 ? 3 : 5;
+  static constexpr int kSmemBytesTE = kStagesTE * kStageBytes + 1024 + kTeSlots * kTeSlotBytes + kBarrierBytes;
 };
 
 struct EpiDev {
@@ -522,21 +533,171 @@ __device__ __forceinline__ void epi_tile(const EpiDev& e, const GemmParams& p, u
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false>
-__global__ void __launch_bounds__(kThreads, 1)
+// ---- TMA-fed epilogue (residual add, SwiGLU backward) ----------------------
+// Every role walks the CTA's tiles in the same order, each tile as 16-column
+// chunks; the k-th chunk of the walk uses slot k % 4 of the ring.
+struct TeCursor {
+  int u, j, nch, m0, n0;
+};
+template <int BN>
+__device__ __forceinline__ void te_tile(TeCursor& c, const GemmParams& p) {
+  const int units = p.m_tiles * p.n_tiles;
+  while (c.u < units) {
+    const int mt = c.u / p.n_tiles, nt = c.u - mt * p.n_tiles;
+    c.m0 = mt * kBM;
+    c.n0 = nt * BN;
+    c.nch = min(BN, p.N - c.n0) / 16;
+    c.j = 0;
+    if (c.nch > 0) return;
+    c.u += gridDim.x;
+  }
+}
+template <int BN>
+__device__ __forceinline__ void te_next(TeCursor& c, const GemmParams& p) {
+  if (++c.j == c.nch) {
+    c.u += gridDim.x;
+    te_tile<BN>(c, p);
+  }
+}
+__device__ __forceinline__ void te_fence_proxy() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// The streaming warp (one thread): loads chunk k into slot k % 4 once the TMA
+// store of chunk k - 4 has left the slot, and stores chunk k once the epilogue
+// warps have written it (a 2-D box of 16 columns x 128 rows; for the SwiGLU
+// backward two boxes: gate | up columns in, dg | du columns out).
+template <int BN>
+__device__ void te_stream(const CUtensorMap* te_in, const CUtensorMap* te_out, const GemmParams& p, uint8_t* slots,
+                          uint64_t* sfull, uint64_t* sdone, volatile int* abort_flag) {
+  const bool dsw = p.epi.kind == CDK_EPI_DSWIGLU;
+  const int hn = (int)p.epi.half_n;
+  const int units = p.m_tiles * p.n_tiles;
+  TeCursor L{(int)blockIdx.x, 0, 0, 0, 0};
+  te_tile<BN>(L, p);
+  TeCursor S = L;
+  int kl = 0, ks = 0;
+  while (S.u < units) {
+    while (L.u < units && kl < ks + kTeSlots) {
+      const int slot = kl & (kTeSlots - 1);
+      if (kl >= kTeSlots) {
+        // bulk groups committed after the store of chunk kl - 8: ks - 1 - (kl - 8)
+        switch (ks - kl + kTeSlots - 1) {
+          case 0: bulk_wait_read<0>(); break;
+          case 1: bulk_wait_read<1>(); break;
+          case 2: bulk_wait_read<2>(); break;
+          case 3: bulk_wait_read<3>(); break;
+          case 4: bulk_wait_read<4>(); break;
+          case 5: bulk_wait_read<5>(); break;
+          case 6: bulk_wait_read<6>(); break;
+          default: bulk_wait_read<7>(); break;
+        }
+      }
+      uint8_t* dst = slots + slot * kTeSlotBytes;
+      const int x = L.n0 + L.j * 16;
+      mbar_arrive_expect_tx(&sfull[slot], kTeSlotBytes);
+      tma_load_2d(dst, te_in, &sfull[slot], x, L.m0);
+      if (dsw) tma_load_2d(dst + kTeSlotBytes / 2, te_in, &sfull[slot], hn + x, L.m0);
+      te_next<BN>(L, p);
+      ++kl;
+    }
+    const int slot = ks & (kTeSlots - 1);
+    mbar_wait(&sdone[slot], (ks / kTeSlots) & 1, abort_flag);
+    const uint8_t* src = slots + slot * kTeSlotBytes;
+    const int x = S.n0 + S.j * 16;
+    tma_store_2d(te_out, src, x, S.m0);
+    if (dsw) tma_store_2d(te_out, src + kTeSlotBytes / 2, hn + x, S.m0);
+    bulk_commit();
+    te_next<BN>(S, p);
+    ++ks;
+  }
+  bulk_wait0();
+}
+
+// Epilogue warps: half h takes chunks j = h, h + 2, ... of the tile; thread
+// row r of the tile.  Residual: fp32 rows of 64 B in the slot (64-byte
+// swizzle: 16-byte piece q at q ^ ((r >> 1) & 3)); SwiGLU backward: gate and
+// up as bf16 rows of 32 B (32-byte swizzle: piece q at q ^ ((r >> 2) & 1)).
+// Results are written back in place for the TMA store.
+__device__ __forceinline__ void epi_te_tile(const EpiDev& e, uint32_t tbase, int r, int n0, int nch, int half,
+                                            int kbase, uint8_t* slots, uint64_t* sfull, uint64_t* sdone,
+                                            volatile int* abort_flag) {
+  if (half >= nch) return;
+  uint32_t ua[kC];
+  tmem_ld_x16_nowait(tbase + half * kC, ua);
+  #pragma unroll 1
+  for (int j = half; j < nch; j += 2) {
+    const int k = kbase + j, slot = k & (kTeSlots - 1);
+    float v[kC];
+    tmem_wait_ld();
+    unpack_scaled(ua, v, 1.f);
+    if (j + 2 < nch) tmem_ld_x16_nowait(tbase + (j + 2) * kC, ua);
+    mbar_wait(&sfull[slot], (k / kTeSlots) & 1, abort_flag);
+    uint8_t* sl = slots + slot * kTeSlotBytes;
+    if (e.kind == CDK_EPI_RESID_F32) {
+      float4* row = reinterpret_cast<float4*>(sl + r * 64);
+      const int sw = (r >> 1) & 3;
+      const int col = n0 + j * kC;
+      #pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float4 t = row[q ^ sw];
+        t.x += v[4 * q];
+        t.y += v[4 * q + 1];
+        t.z += v[4 * q + 2];
+        t.w += v[4 * q + 3];
+        if (e.bias != nullptr) {
+          t.x += __ldg(e.bias + col + 4 * q);
+          t.y += __ldg(e.bias + col + 4 * q + 1);
+          t.z += __ldg(e.bias + col + 4 * q + 2);
+          t.w += __ldg(e.bias + col + 4 * q + 3);
+        }
+        row[q ^ sw] = t;
+      }
+    } else {
+      uint4* gr = reinterpret_cast<uint4*>(sl + r * 32);
+      uint4* ur = reinterpret_cast<uint4*>(sl + kTeSlotBytes / 2 + r * 32);
+      const int sw = (r >> 2) & 1;
+      #pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const uint4 gw = gr[q ^ sw], uw = ur[q ^ sw];
+        const __nv_bfloat162* hg = reinterpret_cast<const __nv_bfloat162*>(&gw);
+        const __nv_bfloat162* hu = reinterpret_cast<const __nv_bfloat162*>(&uw);
+        uint32_t og[4], ou[4];
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 g = __bfloat1622float2(hg[i]), u = __bfloat1622float2(hu[i]);
+          const float d0 = v[8 * q + 2 * i], d1 = v[8 * q + 2 * i + 1];
+          const float s0 = 1.f / (1.f + __expf(-g.x)), s1 = 1.f / (1.f + __expf(-g.y));
+          og[i] = pack_bf16(d0 * u.x * (s0 * (1.f + g.x * (1.f - s0))), d1 * u.y * (s1 * (1.f + g.y * (1.f - s1))));
+          ou[i] = pack_bf16(d0 * g.x * s0, d1 * g.y * s1);
+        }
+        gr[q ^ sw] = make_uint4(og[0], og[1], og[2], og[3]);
+        ur[q ^ sw] = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+      }
+    }
+    te_fence_proxy();
+    mbar_arrive(&sdone[slot]);
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, bool TE = false>
+__global__ void __launch_bounds__(TE ? kThreadsTE : kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                     const __grid_constant__ CUtensorMap te_in, const __grid_constant__ CUtensorMap te_out,
                      const GemmParams p) {
   using Cfg = GemmCfg<BN>;
-  constexpr int kStages = Cfg::kStages;
+  constexpr int kStages = TE ? Cfg::kStagesTE : Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * Cfg::kBytesA;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * Cfg::kStageBytes);
+  uint8_t* te_slots = smem + kStages * Cfg::kStageBytes;  // TE: 8 x 8 KB, 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * Cfg::kStageBytes + (TE ? kTeSlots * kTeSlotBytes : 0));
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* sfull = tempty + 2;      // TE only
+  uint64_t* sdone = sfull + kTeSlots;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(TE ? sdone + kTeSlots : tempty + 2);
+  static_assert((2 * kStages + 4 + (TE ? 2 * kTeSlots : 0)) * 8 + 8 <= Cfg::kBarrierBytes, "barrier area");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -550,6 +711,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 256);
+    }
+    if constexpr (TE) {
+      for (int a = 0; a < kTeSlots; ++a) {
+        mbar_init(&sfull[a], 1);
+        mbar_init(&sdone[a], 128);
+      }
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -657,6 +824,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_commit(&tfull[acc]);
       }
     }
+  } else if (TE && warp == 10) {
+    // ---------------- epilogue operand streaming (TE) ----------------
+    if (lane == 0) {
+      prefetch_tmap(&te_in);
+      prefetch_tmap(&te_out);
+      te_stream<BN>(&te_in, &te_out, p, te_slots, sfull, sdone, abort_flag);
+    }
   } else {
     // ---------------- epilogue warps ----------------
     const int quad = warp & 3;
@@ -667,6 +841,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float sc = 1.f;
     if constexpr (F8) sc = *p.scale_inv_a * *p.scale_inv_b;
     int local = 0;
+    int te_k = 0;  // TE: chunks of the CTA's earlier tiles
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
       const int rem = u % tiles_mn;
       const int mt = rem / p.n_tiles;
@@ -688,7 +863,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < p.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
 
-      if constexpr (VEC) {
+      if constexpr (TE) {
+        const int nch = min(BN, p.N - nt * BN) / 16;
+        epi_te_tile(e, tbase, quad * 32 + lane, nt * BN, nch, half, te_k, te_slots, sfull, sdone, abort_flag);
+        te_k += nch;
+      } else if constexpr (VEC) {
         const int row0 = mt * kBM + quad * 32;
         if (row0 < p.M)
           epi_vec<BN, F8>(e, p, tbase, row0, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN, half, stg, lane,
@@ -783,6 +962,30 @@ static bool make_tmap_u8(CUtensorMap* m, const void* base, uint64_t inner, uint6
   return r == CUDA_SUCCESS;
 }
 
+// 2-D tensor map with a chosen element type and swizzle (TMA-fed epilogue boxes).
+static bool make_tmap_sw(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                         uint64_t outer, uint64_t pitch, uint32_t box_inner, uint32_t box_outer,
+                         CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || base == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// CDK_GEMM_TE=0 turns the TMA-fed epilogue off (the register-staged epilogue runs instead).
+static bool te_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("CDK_GEMM_TE");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 static int num_sms(int dev) {
   static int cache[64] = {0};
   if (dev < 0 || dev >= 64) return 148;
@@ -794,47 +997,55 @@ static int num_sms(int dev) {
   return cache[dev];
 }
 
-template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false>
-static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
-                       cudaStream_t stream) {
+template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, bool TE = false>
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& te_in,
+                       const CUtensorMap& te_out, const GemmParams& p, int grid, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
+  constexpr int threads = TE ? kThreadsTE : kThreads;
+  constexpr int smem = TE ? Cfg::kSmemBytesTE : Cfg::kSmemBytes;
+  static_assert(smem <= 232448, "shared memory");
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  auto kfn = gemm_bf16_kernel<BN, A_MN, B_MN, VEC, F8>;
+  auto kfn = gemm_bf16_kernel<BN, A_MN, B_MN, VEC, F8, TE>;
   if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
     // tcgen05.alloc blocks until columns are free: co-resident CTAs must fit in 512 columns
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kThreads, Cfg::kSmemBytes);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, threads, smem);
     if (e != cudaSuccess) return (int)e;
     if (per_sm * Cfg::kTmemCols > 512) return -12;
     attr_set[dev] = true;
   }
-  kfn<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  kfn<<<grid, threads, smem, stream>>>(ta, tb, te_in, te_out, p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
 }
 
 template <int BN>
-static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-                          int grid, cudaStream_t s) {
+static int dispatch_major(bool a_mn, bool b_mn, bool te, const CUtensorMap& ta, const CUtensorMap& tb,
+                          const CUtensorMap& te_in, const CUtensorMap& te_out, const GemmParams& p, int grid,
+                          cudaStream_t s) {
+  const CUtensorMap &ti = te_in, &to = te_out;
   // the coalesced epilogues (forward kinds and bf16 stores) have their own instantiations
   if (p.scale_inv_a != nullptr) {  // fp8 operands
-    if (p.epi.vec && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, true>(ta, tb, p, grid, s);
-    if (p.epi.vec && !a_mn && b_mn) return launch_gemm<BN, false, true, true, true>(ta, tb, p, grid, s);
-    if (!a_mn && !b_mn) return launch_gemm<BN, false, false, false, true>(ta, tb, p, grid, s);
-    if (!a_mn && b_mn) return launch_gemm<BN, false, true, false, true>(ta, tb, p, grid, s);
-    if (a_mn && !b_mn) return launch_gemm<BN, true, false, false, true>(ta, tb, p, grid, s);
-    return launch_gemm<BN, true, true, false, true>(ta, tb, p, grid, s);
+    if (p.epi.vec && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, true>(ta, tb, ti, to, p, grid, s);
+    if (p.epi.vec && !a_mn && b_mn) return launch_gemm<BN, false, true, true, true>(ta, tb, ti, to, p, grid, s);
+    if (!a_mn && !b_mn) return launch_gemm<BN, false, false, false, true>(ta, tb, ti, to, p, grid, s);
+    if (!a_mn && b_mn) return launch_gemm<BN, false, true, false, true>(ta, tb, ti, to, p, grid, s);
+    if (a_mn && !b_mn) return launch_gemm<BN, true, false, false, true>(ta, tb, ti, to, p, grid, s);
+    return launch_gemm<BN, true, true, false, true>(ta, tb, ti, to, p, grid, s);
   }
-  if (p.epi.vec && !a_mn && !b_mn) return launch_gemm<BN, false, false, true>(ta, tb, p, grid, s);
-  if (p.epi.vec && !a_mn && b_mn) return launch_gemm<BN, false, true, true>(ta, tb, p, grid, s);
-  if (!a_mn && !b_mn) return launch_gemm<BN, false, false, false>(ta, tb, p, grid, s);
-  if (!a_mn && b_mn) return launch_gemm<BN, false, true, false>(ta, tb, p, grid, s);
-  if (a_mn && !b_mn) return launch_gemm<BN, true, false, false>(ta, tb, p, grid, s);
-  return launch_gemm<BN, true, true, false>(ta, tb, p, grid, s);
+  // TMA-fed epilogue (residual add / SwiGLU backward; K-major A)
+  if (te && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, false, true>(ta, tb, ti, to, p, grid, s);
+  if (te && !a_mn && b_mn) return launch_gemm<BN, false, true, true, false, true>(ta, tb, ti, to, p, grid, s);
+  if (p.epi.vec && !a_mn && !b_mn) return launch_gemm<BN, false, false, true>(ta, tb, ti, to, p, grid, s);
+  if (p.epi.vec && !a_mn && b_mn) return launch_gemm<BN, false, true, true>(ta, tb, ti, to, p, grid, s);
+  if (!a_mn && !b_mn) return launch_gemm<BN, false, false, false>(ta, tb, ti, to, p, grid, s);
+  if (!a_mn && b_mn) return launch_gemm<BN, false, true, false>(ta, tb, ti, to, p, grid, s);
+  if (a_mn && !b_mn) return launch_gemm<BN, true, false, false>(ta, tb, ti, to, p, grid, s);
+  return launch_gemm<BN, true, true, false>(ta, tb, ti, to, p, grid, s);
 }
 
 static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -964,11 +1175,30 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
     p.epi.vec = v && !a_mn ? 1 : 0;
   }
 
+  // TMA-fed epilogue for the residual add and the SwiGLU backward: 16-column x
+  // 128-row boxes of the epilogue operand in and of the result out
+  CUtensorMap te_in, te_out;
+  std::memset(&te_in, 0, sizeof(te_in));
+  std::memset(&te_out, 0, sizeof(te_out));
+  bool te = !f8 && p.epi.vec && splits == 1 && !dual && N % 16 == 0 && te_enabled() &&
+            (kind == CDK_EPI_RESID_F32 || kind == CDK_EPI_DSWIGLU);
+  if (te && kind == CDK_EPI_RESID_F32) {
+    te = make_tmap_sw(&te_in, epi->resid, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, epi->ldr, 16, kBM,
+                      CU_TENSOR_MAP_SWIZZLE_64B) &&
+         make_tmap_sw(&te_out, epi->out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, epi->ldo, 16, kBM,
+                      CU_TENSOR_MAP_SWIZZLE_64B);
+  } else if (te) {
+    te = make_tmap_sw(&te_in, epi->aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, epi->half_n + N, M, epi->ldaux, 16,
+                      kBM, CU_TENSOR_MAP_SWIZZLE_32B) &&
+         make_tmap_sw(&te_out, epi->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, epi->half_n + N, M, epi->ldo, 16, kBM,
+                      CU_TENSOR_MAP_SWIZZLE_32B);
+  }
+
   const long long units = m_tiles * n_tiles * splits;
   const int grid = (int)(units < sms ? units : sms);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (BN == 256) return dispatch_major<256>(a_mn, b_mn, ta, tb, p, grid, s);
-  return dispatch_major<128>(a_mn, b_mn, ta, tb, p, grid, s);
+  if (BN == 256) return dispatch_major<256>(a_mn, b_mn, te, ta, tb, te_in, te_out, p, grid, s);
+  return dispatch_major<128>(a_mn, b_mn, te, ta, tb, te_in, te_out, p, grid, s);
 }
 }  // namespace cdk
 

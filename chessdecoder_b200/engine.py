@@ -618,10 +618,8 @@ class Backbone:
                 dn_moe = self._moe_bwd(w, g, s.moe, dh)
                 K.rmsnorm_bwd(dn_moe, s.h1, w["s2"], s.r2, dx=dh1, dx16=dh1_16, dscale=g["s2"], dres=dh)
             elif f8 is None:
-                # MLP block: du = dh W2 (plain GEMM), then the coalesced SwiGLU backward (the fused
-                # EPI_DSWIGLU epilogue is slower at this shape: its gate / up loads stall the epilogue)
-                K.gemm(dh16, w["w2"], b_mn=True, kind=K.EPI_STORE_BF16, out=du)
-                K.swiglu_bwd(du, s.gu, dgu)
+                # MLP block: [dg | du] = SwiGLU backward of dh W2, fused into that GEMM's (TMA-fed) epilogue
+                K.gemm(dh16, w["w2"], b_mn=True, kind=K.EPI_DSWIGLU, out=dgu, aux=s.gu, half_n=F, N=F)
                 K.gemm(dh16, s.u, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w2"])
                 K.gemm(dgu, w["w13"], b_mn=True, kind=K.EPI_STORE_BF16, out=dn)
                 K.gemm(dgu, s.n2, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w13"])

@@ -57,6 +57,18 @@ def gemm_case(kind: str, T: int = 32768, E: int = 1024, F: int = 1536):
         out = torch.empty(T, E, device=dev)
         fn = lambda: K.gemm(X, W, kind=K.EPI_RESID_F32, out=out, resid=h)  # noqa
         M, N, Kd, nbytes = T, E, E, (T * E + E * E) * 2 + 2 * T * E * 4
+    elif kind == "resid2":  # the down projection: K = d_ff
+        X, W = bf(T, F), bf(E, F)
+        h = torch.randn(T, E, device=dev)
+        out = torch.empty(T, E, device=dev)
+        fn = lambda: K.gemm(X, W, kind=K.EPI_RESID_F32, out=out, resid=h)  # noqa
+        M, N, Kd, nbytes = T, E, F, (T * F + E * F) * 2 + 2 * T * E * 4
+    elif kind == "dswiglu":  # [dg | du] = SwiGLU backward of dh W2, fused into the GEMM epilogue
+        dH, W2 = bf(T, E), bf(E, F)
+        gu = bf(T, 2 * F)
+        dgu = torch.empty(T, 2 * F, device=dev, dtype=torch.bfloat16)
+        fn = lambda: K.gemm(dH, W2, b_mn=True, kind=K.EPI_DSWIGLU, out=dgu, aux=gu, half_n=F, N=F)  # noqa
+        M, N, Kd, nbytes = T, F, E, (T * E + E * F + 4 * T * F) * 2
     elif kind == "dx":
         dY, W = bf(T, 3 * E), bf(3 * E, E)
         out = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
@@ -113,7 +125,7 @@ def gemm_case_fp8(kind: str, T: int = 32768, E: int = 1024, F: int = 1536):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("mode", choices=["gemm", "attn", "adamw"])
-    ap.add_argument("--kind", default="rope", choices=["rope", "swiglu", "resid", "dx", "dw"])
+    ap.add_argument("--kind", default="rope", choices=["rope", "swiglu", "resid", "resid2", "dswiglu", "dx", "dw"])
     ap.add_argument("--fp8", action="store_true", help="8-bit operands (e4m3; e5m2 x e4m3 for dx / dw)")
     ap.add_argument("--nseq", type=int, default=128)
     ap.add_argument("--seq", type=int, default=256, help="attention sequence length (> 256: thinking-row blocks)")

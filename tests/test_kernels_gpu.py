@@ -85,6 +85,24 @@ def test_gemm_bias_resid_accum(K):
     assert K.get_error() == 0
 
 
+@pytest.mark.parametrize("M,N,K_", [(1000, 1040, 512), (4096, 1024, 1536), (130, 96, 256)])
+def test_gemm_resid_tma_epilogue(K, M, N, K_):
+    """Residual epilogue (TMA-fed when the shapes allow): ragged rows, a
+    partial last column tile, bias, in-place and out-of-place."""
+    A, B = _bf(M, K_), _bf(N, K_)
+    bias = torch.randn(N, device=DEV)
+    resid = torch.randn(M, N, device=DEV)
+    ref = A.float() @ B.float().t() + bias
+    out = torch.full((M, N), float("nan"), device=DEV)
+    K.gemm(A, B, kind=K.EPI_RESID_F32, out=out, resid=resid, bias=bias)
+    r2 = resid.clone()
+    K.gemm(A, B, kind=K.EPI_RESID_F32, out=r2, resid=r2, bias=bias)
+    torch.cuda.synchronize()
+    assert rel_err(out, resid + ref) < 2e-3
+    assert rel_err(r2, resid + ref) < 2e-3
+    assert K.get_error() == 0
+
+
 @pytest.mark.parametrize("split", [0, 1, 3])
 def test_gemm_atomic_splitk(K, split):
     M, N, K_ = 3072, 1024, 8192  # dW shape: [out, in] over K = tokens
