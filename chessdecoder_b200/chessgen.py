@@ -94,6 +94,23 @@ class Position:
         ep = -1 if len(parts) < 4 or parts[3] == "-" else (int(parts[3][1]) - 1) * 8 + FILES.index(parts[3][0])
         return cls(board, white, castling, ep)
 
+    def fen(self, halfmove: int = 0, fullmove: int = 1) -> str:
+        """FEN of the position (the form the reference's parquet rows carry)."""
+        rows = []
+        for rank in range(7, -1, -1):
+            row, run = "", 0
+            for f in range(8):
+                p = self.board[rank * 8 + f]
+                if p == EMPTY:
+                    run += 1
+                else:
+                    row += (str(run) if run else "") + p
+                    run = 0
+            rows.append(row + (str(run) if run else ""))
+        ep = "-" if self.ep < 0 else sq_name(self.ep)
+        cast = "".join(c for c in "KQkq" if c in self.castling) or "-"
+        return f"{'/'.join(rows)} {'w' if self.white else 'b'} {cast} {ep} {halfmove} {fullmove}"
+
     def copy(self) -> "Position":
         return Position(self.board[:], self.white, self.castling, self.ep)
 
@@ -286,6 +303,30 @@ def perft(pos: Position, depth: int) -> int:
     if depth == 0:
         return 1
     return sum(perft(pos.apply(m), depth - 1) for m in pos.legal_moves()) if depth > 1 else len(pos.legal_moves())
+
+
+def random_game_rows(rng: random.Random, n_plies: int) -> dict:
+    """A uniform-random legal game as parquet-style columns (one entry per ply):
+    ``fen``, ``played_move``, ``best_move``, ``played_q``, ``played_d`` --
+    the per-ply fields chessdecoder/dataloader/data.py:50-97 reads."""
+    pos = Position()
+    cols = {"fen": [], "played_move": [], "best_move": [], "played_q": [], "played_d": []}
+    for ply in range(n_plies):
+        moves = pos.legal_moves()
+        if not moves:
+            break
+        played = moves[rng.randrange(len(moves))]
+        best = moves[rng.randrange(len(moves))]
+        w, d = rng.random(), rng.random()
+        if w + d > 1.0:
+            w, d = 1.0 - w, 1.0 - d
+        cols["fen"].append(pos.fen(0, ply // 2 + 1))
+        cols["played_move"].append(Position.move_token(played))
+        cols["best_move"].append(Position.move_token(best))
+        cols["played_q"].append(w - (1.0 - w - d))
+        cols["played_d"].append(d)
+        pos = pos.apply(played)
+    return cols
 
 
 def random_game(rng: random.Random, n_plies: int):

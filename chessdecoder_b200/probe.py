@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
 
 import torch
 
@@ -124,7 +125,7 @@ def gemm_case_fp8(kind: str, T: int = 32768, E: int = 1024, F: int = 1536):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("mode", choices=["gemm", "attn", "adamw"])
+    ap.add_argument("mode", choices=["gemm", "attn", "adamw", "tokenize"])
     ap.add_argument("--kind", default="rope", choices=["rope", "swiglu", "resid", "resid2", "dswiglu", "dx", "dw"])
     ap.add_argument("--fp8", action="store_true", help="8-bit operands (e4m3; e5m2 x e4m3 for dx / dw)")
     ap.add_argument("--nseq", type=int, default=128)
@@ -177,6 +178,29 @@ def main():
                           "fwd_tflops": 4 * 64 * pairs / ms_f / 1e9, "bwd_tflops": 10 * 64 * pairs / ms_b / 1e9,
                           "fwd_alg_gbs": bytes_f / ms_f / 1e6, "bwd_alg_gbs": bytes_b / ms_b / 1e6,
                           "err": K.get_error()}))
+    elif a.mode == "tokenize":
+        # host batch producer: 256 random games (8-120 plies) -> [256, S] rows, skip_board_prob 0.2
+        import random
+        import time
+        import numpy as np
+        from .chessgen import random_game_rows
+        from .loader import GameTokenizer
+        rng = random.Random(0)
+        S = a.seq
+        games = [random_game_rows(rng, rng.randint(8, 120)) for _ in range(256)]
+        res = {"probe": f"batch producer: 256 games -> [256, {S}] rows", "host_threads": os.cpu_count()}
+        for th in (1, 0):
+            tok = GameTokenizer(S, n_threads=th)
+            drng = random.Random(1)
+            draws = [tok.draw_decisions(g, drng, 0.2) for g in games]
+            tok(games, draws)
+            t0 = time.perf_counter()
+            for _ in range(a.iters):
+                tok(games, draws)
+            dt = (time.perf_counter() - t0) / a.iters
+            res[f"seq_per_s_threads_{th or 'all'}"] = len(games) / dt
+            res[f"tokens_per_s_threads_{th or 'all'}"] = len(games) * S / dt
+        print(json.dumps(res))
     else:
         n = 111_849_344
         p, gr, m, v = (torch.randn(n, device="cuda") for _ in range(4))

@@ -261,6 +261,38 @@ int cdk_adamw_clip_noalloc(float* p, const float* g, float* m, float* v, void* p
                            float max_norm, float lr, float beta1, float beta2, float eps, float wd, int64_t step,
                            float grad_scale, void* stream);
 
+/* ---- batch producer (host memory; no GPU involved) ------------------------
+ * Tokenisation + tensorisation of pretraining games: the native counterpart of
+ * chessdecoder/dataloader/data.py:7-97 (fen_to_position_tokens,
+ * game_to_token_ids) and the per-game body of
+ * chessdecoder/dataloader/loader.py:69-184.
+ *
+ * cdk_vocab_create: token strings (concatenated, offsets[n_tokens + 1]) and
+ * the full -> board / full -> move sub-vocabulary maps (-1 where absent);
+ * returns NULL if a structural token is missing.  The handle is immutable and
+ * may be shared by threads.
+ *
+ * cdk_tokenize_games: n_games games, game g = plies [game_offsets[g],
+ * game_offsets[g+1]) in ply order.  Per ply: FEN, played move and best move
+ * (vocabulary tokens; an empty played move adds nothing, as `if played_move:`),
+ * played Q and D (NaN = invalid), include_board (the reference's
+ * `random.random() > skip_board_prob`; ignored for a game's first ply).  Per
+ * game: start_choice = the index that `random.choice(valid_starts)` drew.
+ * Outputs are [n_games, max_seq_len] row-major (bool tensors as uint8).
+ * n_threads <= 0: all hardware threads.  Status: 0 ok, -1 bad argument,
+ * -2 unknown move token, -3 malformed FEN, -4 start_choice out of range,
+ * -5 a game without plies. */
+void* cdk_vocab_create(const char* chars, const int64_t* offsets, int64_t n_tokens, const int32_t* full_to_board,
+                       const int32_t* full_to_move);
+void cdk_vocab_destroy(void* vocab);
+int cdk_tokenize_games(const void* vocab, int64_t n_games, const int64_t* game_offsets, const char* fen_chars,
+                       const int64_t* fen_offsets, const char* played_chars, const int64_t* played_offsets,
+                       const char* best_chars, const int64_t* best_offsets, const double* played_q,
+                       const double* played_d, const uint8_t* include_board, const int64_t* start_choice,
+                       int64_t max_seq_len, int32_t n_threads, int64_t* input_ids, int64_t* board_target_ids,
+                       int64_t* move_target_ids, uint8_t* move_mask, uint8_t* wl_positions, uint8_t* d_positions,
+                       float* wl_targets, float* d_targets, uint8_t* wdl_valid, int64_t* block_id);
+
 #ifdef __cplusplus
 }
 #endif
