@@ -29,6 +29,12 @@ constexpr int kThreads = 320;
 constexpr int kThreadsTE = 352;
 constexpr int kTeSlots = 8;
 constexpr int kTeSlotBytes = 8192;
+// Store-only form for the bf16 epilogues (plain store, RoPE, SwiGLU forward):
+// the epilogue warps write 64-column x 128-row bf16 boxes (128-byte swizzle)
+// into 2 x 16 KB slots and the 11th warp stores them with TMA, so the output
+// leaves as full 128-byte row segments.
+constexpr int kTe2Slots = 2;
+constexpr int kTe2SlotBytes = 16384;
 
 template <int BN>
 struct GemmCfg {
@@ -42,6 +48,7 @@ struct GemmCfg {
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes + kStagingBytes;
   static constexpr int kStagesTE = BN == 256 ? 3 : 5;
   static constexpr int kSmemBytesTE = kStagesTE * kStageBytes + 1024 + kTeSlots * kTeSlotBytes + kBarrierBytes;
+  static constexpr int kSmemBytesTE2 = kStages * kStageBytes + 1024 + kTe2Slots * kTe2SlotBytes + kBarrierBytes;
 };
 
 struct EpiDev {
@@ -678,26 +685,154 @@ __device__ __forceinline__ void epi_te_tile(const EpiDev& e, uint32_t tbase, int
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, bool TE = false>
-__global__ void __launch_bounds__(TE ? kThreadsTE : kThreads, 1)
+// ---- TMA-stored bf16 epilogue (store-only form) ------------------------------
+// Output boxes of 64 columns: plain store / RoPE: one box per 64 output columns;
+// SwiGLU forward: per 64 output columns three boxes, g and u into out2 (gate |
+// up halves), silu(g) * u into out.  The k-th box of the CTA's walk uses slot
+// k % 2; the epilogue warps wait until the TMA store of box k - 2 has left the
+// slot (sfree), write their rows, and arrive on sdone; the streaming thread
+// stores the box and frees the slot once the store has read it.
+template <int BN>
+__device__ void te2_stream(const CUtensorMap* map_a, const CUtensorMap* map_b, const GemmParams& p, uint8_t* slots,
+                           uint64_t* sdone, uint64_t* sfree, volatile int* abort_flag) {
+  const bool sw = p.epi.kind == CDK_EPI_SWIGLU;
+  const int hn = (int)p.epi.half_n;
+  const int units = p.m_tiles * p.n_tiles;
+  const int n_step = sw ? BN / 2 : BN;
+  int k = 0;
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
+    const int m0 = mt * kBM, n0 = nt * n_step;
+    const int nq = min(n_step, p.N - n0) / 64;
+    for (int j = 0; j < nq; ++j) {
+      for (int o = 0; o < (sw ? 3 : 1); ++o, ++k) {
+        const int slot = k & (kTe2Slots - 1);
+        mbar_wait(&sdone[slot], (k / kTe2Slots) & 1, abort_flag);
+        const uint8_t* src = slots + slot * kTe2SlotBytes;
+        const int x = n0 + j * 64;
+        if (!sw || o == 2) tma_store_2d(map_b, src, x, m0);
+        else tma_store_2d(map_a, src, o == 0 ? x : hn + x, m0);
+        bulk_commit();
+        bulk_wait_read<0>();
+        mbar_arrive(&sfree[slot]);
+      }
+    }
+  }
+  bulk_wait0();
+}
+
+// One thread's 32 bf16 (64 bytes) of row r into box k: half h owns 16-byte
+// pieces 4h .. 4h+3 of the 128-byte row (128-byte swizzle: piece q at q ^ (r & 7)).
+__device__ __forceinline__ void te2_put(uint8_t* slots, uint64_t* sdone, uint64_t* sfree, int k, int r, int half,
+                                        const uint32_t (&w)[16], volatile int* abort_flag) {
+  const int slot = k & (kTe2Slots - 1);
+  if (k >= kTe2Slots) mbar_wait(&sfree[slot], ((k / kTe2Slots) - 1) & 1, abort_flag);
+  uint4* row = reinterpret_cast<uint4*>(slots + slot * kTe2SlotBytes + r * 128);
+  #pragma unroll
+  for (int q = 0; q < 4; ++q) row[(half * 4 + q) ^ (r & 7)] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  te_fence_proxy();
+  mbar_arrive(&sdone[slot]);
+}
+
+template <int BN>
+__device__ __forceinline__ void epi_te2_tile(const EpiDev& e, const GemmParams& p, uint32_t tbase, int r, int row,
+                                             int n0, int half, int& k, uint8_t* slots, uint64_t* sdone,
+                                             uint64_t* sfree, volatile int* abort_flag) {
+  const bool sw = e.kind == CDK_EPI_SWIGLU;
+  const int n_step = sw ? BN / 2 : BN;
+  const int nq = min(n_step, p.N - n0) / 64;
+  // RoPE: the (cos, sin) pairs of this thread's 32 columns within a head are
+  // the same for every head of the tile: load them once
+  float cs[32];
+  const bool rope_tile = e.kind == CDK_EPI_ROPE_BF16 && n0 < e.rope_cols;
+  if (rope_tile) {
+    const int pos = (row < p.M ? row : 0) % max(e.seq_len, 1);
+    const float4* t = reinterpret_cast<const float4*>(e.rope + ((long long)pos * 32 + half * 16) * 2);
+    #pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 x = __ldg(t + q);
+      cs[4 * q] = x.x; cs[4 * q + 1] = x.y; cs[4 * q + 2] = x.z; cs[4 * q + 3] = x.w;
+    }
+  }
+  #pragma unroll 1
+  for (int j = 0; j < nq; ++j) {
+    const int c0 = j * 64 + half * 32;  // first TMEM / output column of this thread's 32
+    uint32_t a0[kC], a1[kC];
+    tmem_ld_x16_nowait(tbase + c0, a0);
+    tmem_ld_x16_nowait(tbase + c0 + kC, a1);
+    if (!sw) {
+      tmem_wait_ld();
+      float v[32];
+      #pragma unroll
+      for (int i = 0; i < kC; ++i) {
+        v[i] = __uint_as_float(a0[i]);
+        v[kC + i] = __uint_as_float(a1[i]);
+      }
+      const int col = n0 + c0;
+      if (e.bias != nullptr) {
+        #pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += __ldg(e.bias + col + i);
+      }
+      if (rope_tile && col < e.rope_cols) {
+        #pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float c = cs[2 * i], s_ = cs[2 * i + 1];
+          const float x0 = v[2 * i], x1 = v[2 * i + 1];
+          v[2 * i] = x0 * c - x1 * s_;
+          v[2 * i + 1] = x1 * c + x0 * s_;
+        }
+      }
+      uint32_t w[16];
+      #pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+      te2_put(slots, sdone, sfree, k++, r, half, w, abort_flag);
+    } else {
+      uint32_t b0[kC], b1[kC];
+      tmem_ld_x16_nowait(tbase + BN / 2 + c0, b0);
+      tmem_ld_x16_nowait(tbase + BN / 2 + c0 + kC, b1);
+      tmem_wait_ld();
+      uint32_t wg[16], wu[16], wh[16];
+      #pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t* ga = i < 8 ? a0 : a1;
+        const uint32_t* ua = i < 8 ? b0 : b1;
+        const int ii = (i & 7) * 2;
+        const float g0 = __uint_as_float(ga[ii]), g1 = __uint_as_float(ga[ii + 1]);
+        const float u0 = __uint_as_float(ua[ii]), u1 = __uint_as_float(ua[ii + 1]);
+        wg[i] = pack_bf16(g0, g1);
+        wu[i] = pack_bf16(u0, u1);
+        wh[i] = pack_bf16(silu_f(g0) * u0, silu_f(g1) * u1);
+      }
+      te2_put(slots, sdone, sfree, k++, r, half, wg, abort_flag);
+      te2_put(slots, sdone, sfree, k++, r, half, wu, abort_flag);
+      te2_put(slots, sdone, sfree, k++, r, half, wh, abort_flag);
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, int TEM = 0>
+__global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap te_in, const __grid_constant__ CUtensorMap te_out,
                      const GemmParams p) {
   using Cfg = GemmCfg<BN>;
+  constexpr bool TE = TEM == 1;
   constexpr int kStages = TE ? Cfg::kStagesTE : Cfg::kStages;
+  constexpr int kSlotArea = TEM == 1 ? kTeSlots * kTeSlotBytes : TEM == 2 ? kTe2Slots * kTe2SlotBytes : 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * Cfg::kBytesA;
-  uint8_t* te_slots = smem + kStages * Cfg::kStageBytes;  // TE: 8 x 8 KB, 1024-aligned
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * Cfg::kStageBytes + (TE ? kTeSlots * kTeSlotBytes : 0));
+  uint8_t* te_slots = smem + kStages * Cfg::kStageBytes;  // TE: 8 x 8 KB / store-only: 2 x 16 KB, 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * Cfg::kStageBytes + kSlotArea);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
-  uint64_t* sfull = tempty + 2;      // TE only
-  uint64_t* sdone = sfull + kTeSlots;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(TE ? sdone + kTeSlots : tempty + 2);
-  static_assert((2 * kStages + 4 + (TE ? 2 * kTeSlots : 0)) * 8 + 8 <= Cfg::kBarrierBytes, "barrier area");
+  constexpr int kSlotBars = TEM == 1 ? kTeSlots : TEM == 2 ? kTe2Slots : 0;
+  uint64_t* sfull = tempty + 2;      // TE / store-only forms
+  uint64_t* sdone = sfull + kSlotBars;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sdone + kSlotBars);
+  static_assert((2 * kStages + 4 + 2 * kSlotBars) * 8 + 8 <= Cfg::kBarrierBytes, "barrier area");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -716,6 +851,12 @@ __global__ void __launch_bounds__(TE ? kThreadsTE : kThreads, 1)
       for (int a = 0; a < kTeSlots; ++a) {
         mbar_init(&sfull[a], 1);
         mbar_init(&sdone[a], 128);
+      }
+    }
+    if constexpr (TEM == 2) {  // sfull = slot freed by the store (streaming thread), sdone = box written (256)
+      for (int a = 0; a < kTe2Slots; ++a) {
+        mbar_init(&sfull[a], 1);
+        mbar_init(&sdone[a], 256);
       }
     }
     *abort_flag = 0;
@@ -824,12 +965,13 @@ __global__ void __launch_bounds__(TE ? kThreadsTE : kThreads, 1)
         tc_commit(&tfull[acc]);
       }
     }
-  } else if (TE && warp == 10) {
-    // ---------------- epilogue operand streaming (TE) ----------------
+  } else if (TEM && warp == 10) {
+    // ---------------- epilogue operand streaming (TE) / output stores ----------------
     if (lane == 0) {
       prefetch_tmap(&te_in);
       prefetch_tmap(&te_out);
-      te_stream<BN>(&te_in, &te_out, p, te_slots, sfull, sdone, abort_flag);
+      if constexpr (TEM == 1) te_stream<BN>(&te_in, &te_out, p, te_slots, sfull, sdone, abort_flag);
+      else te2_stream<BN>(&te_in, &te_out, p, te_slots, sdone, sfull, abort_flag);
     }
   } else {
     // ---------------- epilogue warps ----------------
@@ -867,6 +1009,9 @@ __global__ void __launch_bounds__(TE ? kThreadsTE : kThreads, 1)
         const int nch = min(BN, p.N - nt * BN) / 16;
         epi_te_tile(e, tbase, quad * 32 + lane, nt * BN, nch, half, te_k, te_slots, sfull, sdone, abort_flag);
         te_k += nch;
+      } else if constexpr (TEM == 2) {
+        epi_te2_tile<BN>(e, p, tbase, quad * 32 + lane, row, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN,
+                         half, te_k, te_slots, sdone, sfull, abort_flag);
       } else if constexpr (VEC) {
         const int row0 = mt * kBM + quad * 32;
         if (row0 < p.M)
@@ -997,12 +1142,12 @@ static int num_sms(int dev) {
   return cache[dev];
 }
 
-template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, bool TE = false>
+template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, int TE = 0>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& te_in,
                        const CUtensorMap& te_out, const GemmParams& p, int grid, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   constexpr int threads = TE ? kThreadsTE : kThreads;
-  constexpr int smem = TE ? Cfg::kSmemBytesTE : Cfg::kSmemBytes;
+  constexpr int smem = TE == 1 ? Cfg::kSmemBytesTE : TE == 2 ? Cfg::kSmemBytesTE2 : Cfg::kSmemBytes;
   static_assert(smem <= 232448, "shared memory");
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -1024,7 +1169,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
 }
 
 template <int BN>
-static int dispatch_major(bool a_mn, bool b_mn, bool te, const CUtensorMap& ta, const CUtensorMap& tb,
+static int dispatch_major(bool a_mn, bool b_mn, int te, const CUtensorMap& ta, const CUtensorMap& tb,
                           const CUtensorMap& te_in, const CUtensorMap& te_out, const GemmParams& p, int grid,
                           cudaStream_t s) {
   const CUtensorMap &ti = te_in, &to = te_out;
@@ -1038,8 +1183,10 @@ static int dispatch_major(bool a_mn, bool b_mn, bool te, const CUtensorMap& ta, 
     return launch_gemm<BN, true, true, false, true>(ta, tb, ti, to, p, grid, s);
   }
   // TMA-fed epilogue (residual add / SwiGLU backward; K-major A)
-  if (te && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, false, true>(ta, tb, ti, to, p, grid, s);
-  if (te && !a_mn && b_mn) return launch_gemm<BN, false, true, true, false, true>(ta, tb, ti, to, p, grid, s);
+  if (te == 1 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, false, 1>(ta, tb, ti, to, p, grid, s);
+  if (te == 1 && !a_mn && b_mn) return launch_gemm<BN, false, true, true, false, 1>(ta, tb, ti, to, p, grid, s);
+  if (te == 2 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, false, 2>(ta, tb, ti, to, p, grid, s);
+  if (te == 2 && !a_mn && b_mn) return launch_gemm<BN, false, true, true, false, 2>(ta, tb, ti, to, p, grid, s);
   if (p.epi.vec && !a_mn && !b_mn) return launch_gemm<BN, false, false, true>(ta, tb, ti, to, p, grid, s);
   if (p.epi.vec && !a_mn && b_mn) return launch_gemm<BN, false, true, true>(ta, tb, ti, to, p, grid, s);
   if (!a_mn && !b_mn) return launch_gemm<BN, false, false, false>(ta, tb, ti, to, p, grid, s);
@@ -1182,6 +1329,19 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   std::memset(&te_out, 0, sizeof(te_out));
   bool te = !f8 && p.epi.vec && splits == 1 && !dual && N % 16 == 0 && te_enabled() &&
             (kind == CDK_EPI_RESID_F32 || kind == CDK_EPI_DSWIGLU);
+  // store-only form: 64-column bf16 boxes (N a multiple of 64)
+  bool te2 = !f8 && p.epi.vec && splits == 1 && N % 64 == 0 && te_enabled() &&
+             (kind == CDK_EPI_STORE_BF16 || kind == CDK_EPI_ROPE_BF16 || kind == CDK_EPI_SWIGLU);
+  if (te2 && kind == CDK_EPI_SWIGLU) {
+    te2 = make_tmap_sw(&te_in, epi->out2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 2 * epi->half_n, M, epi->ldo2, 64, kBM,
+                       CU_TENSOR_MAP_SWIZZLE_128B) &&
+          make_tmap_sw(&te_out, epi->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, epi->ldo, 64, kBM,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+  } else if (te2) {
+    te2 = make_tmap_sw(&te_out, epi->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, epi->ldo, 64, kBM,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+    te_in = te_out;
+  }
   if (te && kind == CDK_EPI_RESID_F32) {
     te = make_tmap_sw(&te_in, epi->resid, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, epi->ldr, 16, kBM,
                       CU_TENSOR_MAP_SWIZZLE_64B) &&
@@ -1197,8 +1357,9 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   const long long units = m_tiles * n_tiles * splits;
   const int grid = (int)(units < sms ? units : sms);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (BN == 256) return dispatch_major<256>(a_mn, b_mn, te, ta, tb, te_in, te_out, p, grid, s);
-  return dispatch_major<128>(a_mn, b_mn, te, ta, tb, te_in, te_out, p, grid, s);
+  const int tem = te ? 1 : te2 ? 2 : 0;
+  if (BN == 256) return dispatch_major<256>(a_mn, b_mn, tem, ta, tb, te_in, te_out, p, grid, s);
+  return dispatch_major<128>(a_mn, b_mn, tem, ta, tb, te_in, te_out, p, grid, s);
 }
 }  // namespace cdk
 
