@@ -696,21 +696,26 @@ template <int BN>
 __device__ void te2_stream(const CUtensorMap* map_a, const CUtensorMap* map_b, const GemmParams& p, uint8_t* slots,
                            uint64_t* sdone, uint64_t* sfree, volatile int* abort_flag) {
   const bool sw = p.epi.kind == CDK_EPI_SWIGLU;
+  const bool red = p.epi.kind == CDK_EPI_ATOMIC_F32;  // fp32 boxes of 32 columns, bulk reduce-add (split-K)
   const int hn = (int)p.epi.half_n;
-  const int units = p.m_tiles * p.n_tiles;
+  const int tiles_mn = p.m_tiles * p.n_tiles;
+  const int units = tiles_mn * p.splits;
   const int n_step = sw ? BN / 2 : BN;
+  const int box = red ? 32 : 64;
   int k = 0;
   for (int u = blockIdx.x; u < units; u += gridDim.x) {
-    const int mt = u / p.n_tiles, nt = u - mt * p.n_tiles;
+    const int rem = u % tiles_mn;
+    const int mt = rem / p.n_tiles, nt = rem - mt * p.n_tiles;
     const int m0 = mt * kBM, n0 = nt * n_step;
-    const int nq = min(n_step, p.N - n0) / 64;
+    const int nq = min(n_step, p.N - n0) / box;
     for (int j = 0; j < nq; ++j) {
       for (int o = 0; o < (sw ? 3 : 1); ++o, ++k) {
         const int slot = k & (kTe2Slots - 1);
         mbar_wait(&sdone[slot], (k / kTe2Slots) & 1, abort_flag);
         const uint8_t* src = slots + slot * kTe2SlotBytes;
-        const int x = n0 + j * 64;
-        if (!sw || o == 2) tma_store_2d(map_b, src, x, m0);
+        const int x = n0 + j * box;
+        if (red) tma_reduce_add_2d(map_b, src, x, m0);
+        else if (!sw || o == 2) tma_store_2d(map_b, src, x, m0);
         else tma_store_2d(map_a, src, o == 0 ? x : hn + x, m0);
         bulk_commit();
         bulk_wait_read<0>();
@@ -740,6 +745,22 @@ __device__ __forceinline__ void epi_te2_tile(const EpiDev& e, const GemmParams& 
                                              uint64_t* sfree, volatile int* abort_flag) {
   const bool sw = e.kind == CDK_EPI_SWIGLU;
   const int n_step = sw ? BN / 2 : BN;
+  if (e.kind == CDK_EPI_ATOMIC_F32) {
+    // fp32 partial sums, 32-column boxes (16 columns per half) for the bulk reduce-add
+    const int nb = min(BN, p.N - n0) / 32;
+    uint32_t a[kC];
+    if (nb > 0) tmem_ld_x16_nowait(tbase + half * kC, a);
+    #pragma unroll 1
+    for (int j = 0; j < nb; ++j) {
+      tmem_wait_ld();
+      uint32_t w[16];
+      #pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = a[i];
+      if (j + 1 < nb) tmem_ld_x16_nowait(tbase + (j + 1) * 32 + half * kC, a);
+      te2_put(slots, sdone, sfree, k++, r, half, w, abort_flag);
+    }
+    return;
+  }
   const int nq = min(n_step, p.N - n0) / 64;
   // RoPE: the (cos, sin) pairs of this thread's 32 columns within a head are
   // the same for every head of the tile: load them once
@@ -818,7 +839,8 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   using Cfg = GemmCfg<BN>;
   constexpr bool TE = TEM == 1;
   constexpr int kStages = TE ? Cfg::kStagesTE : Cfg::kStages;
-  constexpr int kSlotArea = TEM == 1 ? kTeSlots * kTeSlotBytes : TEM == 2 ? kTe2Slots * kTe2SlotBytes : 0;
+  constexpr bool TE2 = TEM == 2 || TEM == 3;  // store-only / reduce-add forms share the slots and the stream
+  constexpr int kSlotArea = TEM == 1 ? kTeSlots * kTeSlotBytes : TE2 ? kTe2Slots * kTe2SlotBytes : 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -828,7 +850,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
-  constexpr int kSlotBars = TEM == 1 ? kTeSlots : TEM == 2 ? kTe2Slots : 0;
+  constexpr int kSlotBars = TEM == 1 ? kTeSlots : TE2 ? kTe2Slots : 0;
   uint64_t* sfull = tempty + 2;      // TE / store-only forms
   uint64_t* sdone = sfull + kSlotBars;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sdone + kSlotBars);
@@ -853,7 +875,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
         mbar_init(&sdone[a], 128);
       }
     }
-    if constexpr (TEM == 2) {  // sfull = slot freed by the store (streaming thread), sdone = box written (256)
+    if constexpr (TE2) {  // sfull = slot freed by the store (streaming thread), sdone = box written (256)
       for (int a = 0; a < kTe2Slots; ++a) {
         mbar_init(&sfull[a], 1);
         mbar_init(&sdone[a], 256);
@@ -1009,7 +1031,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
         const int nch = min(BN, p.N - nt * BN) / 16;
         epi_te_tile(e, tbase, quad * 32 + lane, nt * BN, nch, half, te_k, te_slots, sfull, sdone, abort_flag);
         te_k += nch;
-      } else if constexpr (TEM == 2) {
+      } else if constexpr (TE2) {
         epi_te2_tile<BN>(e, p, tbase, quad * 32 + lane, row, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN,
                          half, te_k, te_slots, sdone, sfull, abort_flag);
       } else if constexpr (VEC) {
@@ -1147,7 +1169,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
                        const CUtensorMap& te_out, const GemmParams& p, int grid, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   constexpr int threads = TE ? kThreadsTE : kThreads;
-  constexpr int smem = TE == 1 ? Cfg::kSmemBytesTE : TE == 2 ? Cfg::kSmemBytesTE2 : Cfg::kSmemBytes;
+  constexpr int smem = TE == 1 ? Cfg::kSmemBytesTE : TE >= 2 ? Cfg::kSmemBytesTE2 : Cfg::kSmemBytes;
   static_assert(smem <= 232448, "shared memory");
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -1187,6 +1209,8 @@ static int dispatch_major(bool a_mn, bool b_mn, int te, const CUtensorMap& ta, c
   if (te == 1 && !a_mn && b_mn) return launch_gemm<BN, false, true, true, false, 1>(ta, tb, ti, to, p, grid, s);
   if (te == 2 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, false, 2>(ta, tb, ti, to, p, grid, s);
   if (te == 2 && !a_mn && b_mn) return launch_gemm<BN, false, true, true, false, 2>(ta, tb, ti, to, p, grid, s);
+  if (te == 3 && a_mn && b_mn) return launch_gemm<BN, true, true, false, false, 3>(ta, tb, ti, to, p, grid, s);
+  if (te == 3 && !a_mn && !b_mn) return launch_gemm<BN, false, false, false, false, 3>(ta, tb, ti, to, p, grid, s);
   if (p.epi.vec && !a_mn && !b_mn) return launch_gemm<BN, false, false, true>(ta, tb, ti, to, p, grid, s);
   if (p.epi.vec && !a_mn && b_mn) return launch_gemm<BN, false, true, true>(ta, tb, ti, to, p, grid, s);
   if (!a_mn && !b_mn) return launch_gemm<BN, false, false, false>(ta, tb, ti, to, p, grid, s);
@@ -1329,9 +1353,17 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   std::memset(&te_out, 0, sizeof(te_out));
   bool te = !f8 && p.epi.vec && splits == 1 && !dual && N % 16 == 0 && te_enabled() &&
             (kind == CDK_EPI_RESID_F32 || kind == CDK_EPI_DSWIGLU);
-  // store-only form: 64-column bf16 boxes (N a multiple of 64)
+  // store-only form: 64-column bf16 boxes (N a multiple of 64); split-K fp32
+  // partial sums: 32-column boxes reduce-added by TMA
   bool te2 = !f8 && p.epi.vec && splits == 1 && N % 64 == 0 && te_enabled() &&
              (kind == CDK_EPI_STORE_BF16 || kind == CDK_EPI_ROPE_BF16 || kind == CDK_EPI_SWIGLU);
+  bool te3 = !f8 && kind == CDK_EPI_ATOMIC_F32 && N % 32 == 0 && epi->bias == nullptr && epi->ldo % 4 == 0 &&
+             (reinterpret_cast<uintptr_t>(epi->out) & 15) == 0 && te_enabled();
+  if (te3) {
+    te3 = make_tmap_sw(&te_out, epi->out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, epi->ldo, 32, kBM,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+    te_in = te_out;
+  }
   if (te2 && kind == CDK_EPI_SWIGLU) {
     te2 = make_tmap_sw(&te_in, epi->out2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 2 * epi->half_n, M, epi->ldo2, 64, kBM,
                        CU_TENSOR_MAP_SWIZZLE_128B) &&
@@ -1357,7 +1389,7 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   const long long units = m_tiles * n_tiles * splits;
   const int grid = (int)(units < sms ? units : sms);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int tem = te ? 1 : te2 ? 2 : 0;
+  const int tem = te ? 1 : te2 ? 2 : te3 ? 3 : 0;
   if (BN == 256) return dispatch_major<256>(a_mn, b_mn, tem, ta, tb, te_in, te_out, p, grid, s);
   return dispatch_major<128>(a_mn, b_mn, tem, ta, tb, te_in, te_out, p, grid, s);
 }
