@@ -23,9 +23,9 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = 128 B = one swizzle row (128 fp8 elements in the fp8 instantiations)
 constexpr int kThreads = 320;
 // TMA-fed epilogue (residual add, SwiGLU backward): an 11th warp streams the
-// epilogue's global operand through a ring of 8 x 8 KB shared-memory slots
-// (16 columns x 128 rows per slot) and writes the results back by TMA store;
-// the mainloop ring gives up one (BN=256) stage for it.
+// epilogue's global operand through 64 KB of shared-memory slots (boxes of
+// 128 rows x 128 bytes) and writes the results back by TMA store; the
+// mainloop ring gives up one (BN=256) stage for it.
 constexpr int kThreadsTE = 352;
 constexpr int kTeSlots = 8;
 constexpr int kTeSlotBytes = 8192;
@@ -541,11 +541,16 @@ __device__ __forceinline__ void epi_tile(const EpiDev& e, const GemmParams& p, u
 }
 
 // ---- TMA-fed epilogue (residual add, SwiGLU backward) ----------------------
-// Every role walks the CTA's tiles in the same order, each tile as 16-column
-// chunks; the k-th chunk of the walk uses slot k % 4 of the ring.
+// Boxes of 128 rows with 128-byte rows (128-byte swizzle: 16-byte piece q of
+// row r at q ^ (r & 7)): the residual as fp32 boxes of 32 columns (16 KB, 4
+// slots), the SwiGLU backward as a gate box and an up box of 64 bf16 columns
+// (32 KB, 2 slots).  Every role walks the CTA's tiles in the same order; the
+// k-th box of the walk uses slot k % slots.  Half h of the epilogue warps owns
+// pieces 4h .. 4h+3 of each row; results are written back in place.
 struct TeCursor {
   int u, j, nch, m0, n0;
 };
+__device__ __forceinline__ int te_cols(const GemmParams& p) { return p.epi.kind == CDK_EPI_DSWIGLU ? 64 : 32; }
 template <int BN>
 __device__ __forceinline__ void te_tile(TeCursor& c, const GemmParams& p) {
   const int units = p.m_tiles * p.n_tiles;
@@ -553,7 +558,7 @@ __device__ __forceinline__ void te_tile(TeCursor& c, const GemmParams& p) {
     const int mt = c.u / p.n_tiles, nt = c.u - mt * p.n_tiles;
     c.m0 = mt * kBM;
     c.n0 = nt * BN;
-    c.nch = min(BN, p.N - c.n0) / 16;
+    c.nch = min(BN, p.N - c.n0) / te_cols(p);
     c.j = 0;
     if (c.nch > 0) return;
     c.u += gridDim.x;
@@ -568,50 +573,48 @@ __device__ __forceinline__ void te_next(TeCursor& c, const GemmParams& p) {
 }
 __device__ __forceinline__ void te_fence_proxy() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// The streaming warp (one thread): loads chunk k into slot k % 4 once the TMA
-// store of chunk k - 4 has left the slot, and stores chunk k once the epilogue
-// warps have written it (a 2-D box of 16 columns x 128 rows; for the SwiGLU
-// backward two boxes: gate | up columns in, dg | du columns out).
+// The streaming warp (one thread): loads box k into its slot once the TMA
+// store of box k - slots has left it, and stores box k once the epilogue warps
+// have written it.
 template <int BN>
 __device__ void te_stream(const CUtensorMap* te_in, const CUtensorMap* te_out, const GemmParams& p, uint8_t* slots,
                           uint64_t* sfull, uint64_t* sdone, volatile int* abort_flag) {
   const bool dsw = p.epi.kind == CDK_EPI_DSWIGLU;
   const int hn = (int)p.epi.half_n;
   const int units = p.m_tiles * p.n_tiles;
+  const int nslots = dsw ? 2 : 4;
+  const int sbytes = kTeSlots * kTeSlotBytes / nslots;
+  const int w = te_cols(p);
   TeCursor L{(int)blockIdx.x, 0, 0, 0, 0};
   te_tile<BN>(L, p);
   TeCursor S = L;
   int kl = 0, ks = 0;
   while (S.u < units) {
-    while (L.u < units && kl < ks + kTeSlots) {
-      const int slot = kl & (kTeSlots - 1);
-      if (kl >= kTeSlots) {
-        // bulk groups committed after the store of chunk kl - 8: ks - 1 - (kl - 8)
-        switch (ks - kl + kTeSlots - 1) {
+    while (L.u < units && kl < ks + nslots) {
+      const int slot = kl % nslots;
+      if (kl >= nslots) {
+        // bulk groups committed after the store of box kl - nslots: ks - 1 - (kl - nslots)
+        switch (ks - kl + nslots - 1) {
           case 0: bulk_wait_read<0>(); break;
           case 1: bulk_wait_read<1>(); break;
           case 2: bulk_wait_read<2>(); break;
-          case 3: bulk_wait_read<3>(); break;
-          case 4: bulk_wait_read<4>(); break;
-          case 5: bulk_wait_read<5>(); break;
-          case 6: bulk_wait_read<6>(); break;
-          default: bulk_wait_read<7>(); break;
+          default: bulk_wait_read<3>(); break;
         }
       }
-      uint8_t* dst = slots + slot * kTeSlotBytes;
-      const int x = L.n0 + L.j * 16;
-      mbar_arrive_expect_tx(&sfull[slot], kTeSlotBytes);
+      uint8_t* dst = slots + slot * sbytes;
+      const int x = L.n0 + L.j * w;
+      mbar_arrive_expect_tx(&sfull[slot], sbytes);
       tma_load_2d(dst, te_in, &sfull[slot], x, L.m0);
-      if (dsw) tma_load_2d(dst + kTeSlotBytes / 2, te_in, &sfull[slot], hn + x, L.m0);
+      if (dsw) tma_load_2d(dst + sbytes / 2, te_in, &sfull[slot], hn + x, L.m0);
       te_next<BN>(L, p);
       ++kl;
     }
-    const int slot = ks & (kTeSlots - 1);
-    mbar_wait(&sdone[slot], (ks / kTeSlots) & 1, abort_flag);
-    const uint8_t* src = slots + slot * kTeSlotBytes;
-    const int x = S.n0 + S.j * 16;
+    const int slot = ks % nslots;
+    mbar_wait(&sdone[slot], (ks / nslots) & 1, abort_flag);
+    const uint8_t* src = slots + slot * sbytes;
+    const int x = S.n0 + S.j * w;
     tma_store_2d(te_out, src, x, S.m0);
-    if (dsw) tma_store_2d(te_out, src + kTeSlotBytes / 2, hn + x, S.m0);
+    if (dsw) tma_store_2d(te_out, src + sbytes / 2, hn + x, S.m0);
     bulk_commit();
     te_next<BN>(S, p);
     ++ks;
@@ -619,65 +622,64 @@ __device__ void te_stream(const CUtensorMap* te_in, const CUtensorMap* te_out, c
   bulk_wait0();
 }
 
-// Epilogue warps: half h takes chunks j = h, h + 2, ... of the tile; thread
-// row r of the tile.  Residual: fp32 rows of 64 B in the slot (64-byte
-// swizzle: 16-byte piece q at q ^ ((r >> 1) & 3)); SwiGLU backward: gate and
-// up as bf16 rows of 32 B (32-byte swizzle: piece q at q ^ ((r >> 2) & 1)).
-// Results are written back in place for the TMA store.
 __device__ __forceinline__ void epi_te_tile(const EpiDev& e, uint32_t tbase, int r, int n0, int nch, int half,
                                             int kbase, uint8_t* slots, uint64_t* sfull, uint64_t* sdone,
                                             volatile int* abort_flag) {
-  if (half >= nch) return;
-  uint32_t ua[kC];
-  tmem_ld_x16_nowait(tbase + half * kC, ua);
+  const bool dsw = e.kind == CDK_EPI_DSWIGLU;
+  const int nslots = dsw ? 2 : 4;
+  const int sbytes = kTeSlots * kTeSlotBytes / nslots;
+  const int w = dsw ? 64 : 32;  // box columns; this thread takes w / 2 of them
   #pragma unroll 1
-  for (int j = half; j < nch; j += 2) {
-    const int k = kbase + j, slot = k & (kTeSlots - 1);
-    float v[kC];
+  for (int j = 0; j < nch; ++j) {
+    const int k = kbase + j, slot = k % nslots;
+    const int c0 = j * w + half * (w / 2);
+    uint32_t a0[kC], a1[kC];
+    tmem_ld_x16_nowait(tbase + c0, a0);
+    if (dsw) tmem_ld_x16_nowait(tbase + c0 + kC, a1);
+    mbar_wait(&sfull[slot], (k / nslots) & 1, abort_flag);
     tmem_wait_ld();
-    unpack_scaled(ua, v, 1.f);
-    if (j + 2 < nch) tmem_ld_x16_nowait(tbase + (j + 2) * kC, ua);
-    mbar_wait(&sfull[slot], (k / kTeSlots) & 1, abort_flag);
-    uint8_t* sl = slots + slot * kTeSlotBytes;
-    if (e.kind == CDK_EPI_RESID_F32) {
-      float4* row = reinterpret_cast<float4*>(sl + r * 64);
-      const int sw = (r >> 1) & 3;
-      const int col = n0 + j * kC;
+    uint8_t* sl = slots + slot * sbytes;
+    if (!dsw) {
+      float4* row = reinterpret_cast<float4*>(sl + r * 128);
+      const int col = n0 + c0;
       #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        float4 t = row[q ^ sw];
-        t.x += v[4 * q];
-        t.y += v[4 * q + 1];
-        t.z += v[4 * q + 2];
-        t.w += v[4 * q + 3];
+        const int pc = (half * 4 + q) ^ (r & 7);
+        float4 t = row[pc];
+        t.x += __uint_as_float(a0[4 * q]);
+        t.y += __uint_as_float(a0[4 * q + 1]);
+        t.z += __uint_as_float(a0[4 * q + 2]);
+        t.w += __uint_as_float(a0[4 * q + 3]);
         if (e.bias != nullptr) {
           t.x += __ldg(e.bias + col + 4 * q);
           t.y += __ldg(e.bias + col + 4 * q + 1);
           t.z += __ldg(e.bias + col + 4 * q + 2);
           t.w += __ldg(e.bias + col + 4 * q + 3);
         }
-        row[q ^ sw] = t;
+        row[pc] = t;
       }
     } else {
-      uint4* gr = reinterpret_cast<uint4*>(sl + r * 32);
-      uint4* ur = reinterpret_cast<uint4*>(sl + kTeSlotBytes / 2 + r * 32);
-      const int sw = (r >> 2) & 1;
+      uint4* gr = reinterpret_cast<uint4*>(sl + r * 128);
+      uint4* ur = reinterpret_cast<uint4*>(sl + sbytes / 2 + r * 128);
       #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const uint4 gw = gr[q ^ sw], uw = ur[q ^ sw];
+      for (int q = 0; q < 4; ++q) {
+        const int pc = (half * 4 + q) ^ (r & 7);
+        const uint4 gw = gr[pc], uw = ur[pc];
         const __nv_bfloat162* hg = reinterpret_cast<const __nv_bfloat162*>(&gw);
         const __nv_bfloat162* hu = reinterpret_cast<const __nv_bfloat162*>(&uw);
+        const uint32_t* acc = q < 2 ? a0 : a1;
         uint32_t og[4], ou[4];
         #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 g = __bfloat1622float2(hg[i]), u = __bfloat1622float2(hu[i]);
-          const float d0 = v[8 * q + 2 * i], d1 = v[8 * q + 2 * i + 1];
+          const int ai = (q & 1) * 8 + 2 * i;
+          const float d0 = __uint_as_float(acc[ai]), d1 = __uint_as_float(acc[ai + 1]);
           const float s0 = 1.f / (1.f + __expf(-g.x)), s1 = 1.f / (1.f + __expf(-g.y));
           og[i] = pack_bf16(d0 * u.x * (s0 * (1.f + g.x * (1.f - s0))), d1 * u.y * (s1 * (1.f + g.y * (1.f - s1))));
           ou[i] = pack_bf16(d0 * g.x * s0, d1 * g.y * s1);
         }
-        gr[q ^ sw] = make_uint4(og[0], og[1], og[2], og[3]);
-        ur[q ^ sw] = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+        gr[pc] = make_uint4(og[0], og[1], og[2], og[3]);
+        ur[pc] = make_uint4(ou[0], ou[1], ou[2], ou[3]);
       }
     }
     te_fence_proxy();
@@ -872,7 +874,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
     if constexpr (TE) {
       for (int a = 0; a < kTeSlots; ++a) {
         mbar_init(&sfull[a], 1);
-        mbar_init(&sdone[a], 128);
+        mbar_init(&sdone[a], 256);
       }
     }
     if constexpr (TE2) {  // sfull = slot freed by the store (streaming thread), sdone = box written (256)
@@ -1028,7 +1030,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
 
       if constexpr (TE) {
-        const int nch = min(BN, p.N - nt * BN) / 16;
+        const int nch = min(BN, p.N - nt * BN) / (e.kind == CDK_EPI_DSWIGLU ? 64 : 32);
         epi_te_tile(e, tbase, quad * 32 + lane, nt * BN, nch, half, te_k, te_slots, sfull, sdone, abort_flag);
         te_k += nch;
       } else if constexpr (TE2) {
@@ -1375,15 +1377,17 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
     te_in = te_out;
   }
   if (te && kind == CDK_EPI_RESID_F32) {
-    te = make_tmap_sw(&te_in, epi->resid, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, epi->ldr, 16, kBM,
-                      CU_TENSOR_MAP_SWIZZLE_64B) &&
-         make_tmap_sw(&te_out, epi->out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, epi->ldo, 16, kBM,
-                      CU_TENSOR_MAP_SWIZZLE_64B);
+    te = N % 32 == 0 &&
+         make_tmap_sw(&te_in, epi->resid, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, epi->ldr, 32, kBM,
+                      CU_TENSOR_MAP_SWIZZLE_128B) &&
+         make_tmap_sw(&te_out, epi->out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, epi->ldo, 32, kBM,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
   } else if (te) {
-    te = make_tmap_sw(&te_in, epi->aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, epi->half_n + N, M, epi->ldaux, 16,
-                      kBM, CU_TENSOR_MAP_SWIZZLE_32B) &&
-         make_tmap_sw(&te_out, epi->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, epi->half_n + N, M, epi->ldo, 16, kBM,
-                      CU_TENSOR_MAP_SWIZZLE_32B);
+    te = N % 64 == 0 &&
+         make_tmap_sw(&te_in, epi->aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, epi->half_n + N, M, epi->ldaux, 64,
+                      kBM, CU_TENSOR_MAP_SWIZZLE_128B) &&
+         make_tmap_sw(&te_out, epi->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, epi->half_n + N, M, epi->ldo, 64, kBM,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
   }
 
   const long long units = m_tiles * n_tiles * splits;
