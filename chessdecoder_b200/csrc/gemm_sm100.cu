@@ -624,7 +624,7 @@ __device__ void te_stream(const CUtensorMap* te_in, const CUtensorMap* te_out, c
 
 __device__ __forceinline__ void epi_te_tile(const EpiDev& e, uint32_t tbase, int r, int n0, int nch, int half,
                                             int kbase, uint8_t* slots, uint64_t* sfull, uint64_t* sdone,
-                                            volatile int* abort_flag) {
+                                            volatile int* abort_flag, float sc) {
   const bool dsw = e.kind == CDK_EPI_DSWIGLU;
   const int nslots = dsw ? 2 : 4;
   const int sbytes = kTeSlots * kTeSlotBytes / nslots;
@@ -646,10 +646,10 @@ __device__ __forceinline__ void epi_te_tile(const EpiDev& e, uint32_t tbase, int
       for (int q = 0; q < 4; ++q) {
         const int pc = (half * 4 + q) ^ (r & 7);
         float4 t = row[pc];
-        t.x += __uint_as_float(a0[4 * q]);
-        t.y += __uint_as_float(a0[4 * q + 1]);
-        t.z += __uint_as_float(a0[4 * q + 2]);
-        t.w += __uint_as_float(a0[4 * q + 3]);
+        t.x += __uint_as_float(a0[4 * q]) * sc;
+        t.y += __uint_as_float(a0[4 * q + 1]) * sc;
+        t.z += __uint_as_float(a0[4 * q + 2]) * sc;
+        t.w += __uint_as_float(a0[4 * q + 3]) * sc;
         if (e.bias != nullptr) {
           t.x += __ldg(e.bias + col + 4 * q);
           t.y += __ldg(e.bias + col + 4 * q + 1);
@@ -673,7 +673,7 @@ __device__ __forceinline__ void epi_te_tile(const EpiDev& e, uint32_t tbase, int
         for (int i = 0; i < 4; ++i) {
           const float2 g = __bfloat1622float2(hg[i]), u = __bfloat1622float2(hu[i]);
           const int ai = (q & 1) * 8 + 2 * i;
-          const float d0 = __uint_as_float(acc[ai]), d1 = __uint_as_float(acc[ai + 1]);
+          const float d0 = __uint_as_float(acc[ai]) * sc, d1 = __uint_as_float(acc[ai + 1]) * sc;
           const float s0 = 1.f / (1.f + __expf(-g.x)), s1 = 1.f / (1.f + __expf(-g.y));
           og[i] = pack_bf16(d0 * u.x * (s0 * (1.f + g.x * (1.f - s0))), d1 * u.y * (s1 * (1.f + g.y * (1.f - s1))));
           ou[i] = pack_bf16(d0 * g.x * s0, d1 * g.y * s1);
@@ -742,7 +742,7 @@ __device__ __forceinline__ void te2_put(uint8_t* slots, uint64_t* sdone, uint64_
 }
 
 template <int BN>
-__device__ __forceinline__ void epi_te2_tile(const EpiDev& e, const GemmParams& p, uint32_t tbase, int r, int row,
+__device__ __forceinline__ void epi_te2_tile(const EpiDev& e, const GemmParams& p, uint32_t tbase, int r, int row, float sc,
                                              int n0, int half, int& k, uint8_t* slots, uint64_t* sdone,
                                              uint64_t* sfree, volatile int* abort_flag) {
   const bool sw = e.kind == CDK_EPI_SWIGLU;
@@ -757,7 +757,7 @@ __device__ __forceinline__ void epi_te2_tile(const EpiDev& e, const GemmParams& 
       tmem_wait_ld();
       uint32_t w[16];
       #pragma unroll
-      for (int i = 0; i < 16; ++i) w[i] = a[i];
+      for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(__uint_as_float(a[i]) * sc);
       if (j + 1 < nb) tmem_ld_x16_nowait(tbase + (j + 1) * 32 + half * kC, a);
       te2_put(slots, sdone, sfree, k++, r, half, w, abort_flag);
     }
@@ -788,8 +788,8 @@ __device__ __forceinline__ void epi_te2_tile(const EpiDev& e, const GemmParams& 
       float v[32];
       #pragma unroll
       for (int i = 0; i < kC; ++i) {
-        v[i] = __uint_as_float(a0[i]);
-        v[kC + i] = __uint_as_float(a1[i]);
+        v[i] = __uint_as_float(a0[i]) * sc;
+        v[kC + i] = __uint_as_float(a1[i]) * sc;
       }
       const int col = n0 + c0;
       if (e.bias != nullptr) {
@@ -820,8 +820,8 @@ __device__ __forceinline__ void epi_te2_tile(const EpiDev& e, const GemmParams& 
         const uint32_t* ga = i < 8 ? a0 : a1;
         const uint32_t* ua = i < 8 ? b0 : b1;
         const int ii = (i & 7) * 2;
-        const float g0 = __uint_as_float(ga[ii]), g1 = __uint_as_float(ga[ii + 1]);
-        const float u0 = __uint_as_float(ua[ii]), u1 = __uint_as_float(ua[ii + 1]);
+        const float g0 = __uint_as_float(ga[ii]) * sc, g1 = __uint_as_float(ga[ii + 1]) * sc;
+        const float u0 = __uint_as_float(ua[ii]) * sc, u1 = __uint_as_float(ua[ii + 1]) * sc;
         wg[i] = pack_bf16(g0, g1);
         wu[i] = pack_bf16(u0, u1);
         wh[i] = pack_bf16(silu_f(g0) * u0, silu_f(g1) * u1);
@@ -1031,10 +1031,10 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
 
       if constexpr (TE) {
         const int nch = min(BN, p.N - nt * BN) / (e.kind == CDK_EPI_DSWIGLU ? 64 : 32);
-        epi_te_tile(e, tbase, quad * 32 + lane, nt * BN, nch, half, te_k, te_slots, sfull, sdone, abort_flag);
+        epi_te_tile(e, tbase, quad * 32 + lane, nt * BN, nch, half, te_k, te_slots, sfull, sdone, abort_flag, sc);
         te_k += nch;
       } else if constexpr (TE2) {
-        epi_te2_tile<BN>(e, p, tbase, quad * 32 + lane, row, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN,
+        epi_te2_tile<BN>(e, p, tbase, quad * 32 + lane, row, sc, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN,
                          half, te_k, te_slots, sdone, sfull, abort_flag);
       } else if constexpr (VEC) {
         const int row0 = mt * kBM + quad * 32;
@@ -1199,6 +1199,11 @@ static int dispatch_major(bool a_mn, bool b_mn, int te, const CUtensorMap& ta, c
   const CUtensorMap &ti = te_in, &to = te_out;
   // the coalesced epilogues (forward kinds and bf16 stores) have their own instantiations
   if (p.scale_inv_a != nullptr) {  // fp8 operands
+    if (te == 1 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, true, 1>(ta, tb, ti, to, p, grid, s);
+    if (te == 2 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, true, 2>(ta, tb, ti, to, p, grid, s);
+    if (te == 2 && !a_mn && b_mn) return launch_gemm<BN, false, true, true, true, 2>(ta, tb, ti, to, p, grid, s);
+    if (te == 3 && a_mn && b_mn) return launch_gemm<BN, true, true, false, true, 3>(ta, tb, ti, to, p, grid, s);
+    if (te == 3 && !a_mn && !b_mn) return launch_gemm<BN, false, false, false, true, 3>(ta, tb, ti, to, p, grid, s);
     if (p.epi.vec && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, true>(ta, tb, ti, to, p, grid, s);
     if (p.epi.vec && !a_mn && b_mn) return launch_gemm<BN, false, true, true, true>(ta, tb, ti, to, p, grid, s);
     if (!a_mn && !b_mn) return launch_gemm<BN, false, false, false, true>(ta, tb, ti, to, p, grid, s);
@@ -1353,13 +1358,13 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   CUtensorMap te_in, te_out;
   std::memset(&te_in, 0, sizeof(te_in));
   std::memset(&te_out, 0, sizeof(te_out));
-  bool te = !f8 && p.epi.vec && splits == 1 && !dual && N % 16 == 0 && te_enabled() &&
-            (kind == CDK_EPI_RESID_F32 || kind == CDK_EPI_DSWIGLU);
+  bool te = p.epi.vec && splits == 1 && !dual && N % 16 == 0 && te_enabled() &&
+            (kind == CDK_EPI_RESID_F32 || (kind == CDK_EPI_DSWIGLU && !f8));
   // store-only form: 64-column bf16 boxes (N a multiple of 64); split-K fp32
   // partial sums: 32-column boxes reduce-added by TMA
-  bool te2 = !f8 && p.epi.vec && splits == 1 && N % 64 == 0 && te_enabled() &&
+  bool te2 = p.epi.vec && splits == 1 && N % 64 == 0 && te_enabled() &&
              (kind == CDK_EPI_STORE_BF16 || kind == CDK_EPI_ROPE_BF16 || kind == CDK_EPI_SWIGLU);
-  bool te3 = !f8 && kind == CDK_EPI_ATOMIC_F32 && N % 32 == 0 && epi->bias == nullptr && epi->ldo % 4 == 0 &&
+  bool te3 = kind == CDK_EPI_ATOMIC_F32 && N % 32 == 0 && epi->bias == nullptr && epi->ldo % 4 == 0 &&
              (reinterpret_cast<uintptr_t>(epi->out) & 15) == 0 && te_enabled();
   if (te3) {
     te3 = make_tmap_sw(&te_out, epi->out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, epi->ldo, 32, kBM,
