@@ -53,7 +53,11 @@ def parse():
     ap.add_argument("--finetune", action="store_true",
                     help="finetune step (chessdecoder/finetune/train.py): thinking head + 5-term loss on "
                          "thinking-variation rows, S=4096, per-GPU batch 4")
-    ap.add_argument("--seq", type=int, default=None, help="sequence length (default 256; 4096 with --moe / --finetune)")
+    ap.add_argument("--grpo", action="store_true",
+                    help="GRPO policy-gradient step (chessdecoder/rl): prefix pass, thinking / final move heads, "
+                         "clipped ratio + KL loss, S=4096, mini-batch 4")
+    ap.add_argument("--seq", type=int, default=None,
+                    help="sequence length (default 256; 4096 with --moe / --finetune / --grpo)")
     ap.add_argument("--layers", type=int, default=12)
     ap.add_argument("--pool", type=int, default=4, help="distinct synthetic batches per rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -207,18 +211,69 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_grpo(args, rank, world):
+    """GRPO step (prefix pass, move-action log-probs, clipped-ratio + KL loss,
+    backward, clip, AdamW) on synthetic thinking rows with rollout / reference
+    log-probs perturbed around the current policy; one rank, device time."""
+    from chessdecoder_b200 import data, kernels as K
+    from chessdecoder_b200.engine import ModelConfig
+    from chessdecoder_b200.rl import GRPOStep, prepare_rl_batch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = ModelConfig(num_layers=args.layers, max_seq_len=args.seq, finetune=True)
+    step = GRPOStep(cfg, device=dev)
+    rbs = []
+    for b in data.finetune_batches(args.pool, args.batch, args.seq, seed=1234, rank=rank):
+        rb = {"input_ids": b["input_ids"], "block_id": b["block_id"], "wl_positions": b["wl_positions"],
+              "d_positions": b["d_positions"], "wl_values": b["wl_targets"], "d_values": b["d_targets"],
+              "thinking_move_mask": b["thinking_move_mask"], "final_move_mask": b["move_mask"],
+              "move_token_ids": b["move_target_ids"].clamp_min(0)}
+        lp, _ = step.log_probs(prepare_rl_batch(rb, dev))
+        g = torch.Generator(device="cpu").manual_seed(len(rbs))
+        old = lp.cpu() + torch.randn(lp.shape, generator=g) * 0.1
+        adv = torch.randn(args.batch, generator=g)
+        rbs.append(prepare_rl_batch(rb, dev, old, lp.cpu(), adv))
+    for i in range(args.warmup):
+        step.forward_backward(rbs[i % len(rbs)])
+        step.optimizer_step()
+    torch.cuda.synchronize()
+    K.LAUNCHES[0] = 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        loss, _ = step.forward_backward(rbs[i % len(rbs)])
+        step.optimizer_step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    tokens = args.batch * args.seq
+    print(json.dumps({"metric": METRIC, "value": tokens / (ms / 1000.0), "unit": UNIT, "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                      "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                      "data": "synthetic thinking-variation rows; rollout log-probs = current + N(0, 0.1)",
+                      "config": {"workload": "ChessDecoder GRPO step (prefix pass, thinking / final move log-probs, "
+                                             "clipped ratio + KL loss, bwd, clip, AdamW), default model E=1024 H=16 "
+                                             "L=%d d_ff=1536" % args.layers,
+                                 "global_batch": args.batch, "seq_len": args.seq, "parallelism": "dp1"},
+                      "gpu_launches": K.LAUNCHES[0] // args.steps, "loss": float(loss)}))
+
+
 def main():
     args = parse()
     if args.batch is None:
-        args.batch = 128 if args.fp8 else 16 if args.moe else 4 if args.finetune else 64
+        args.batch = 128 if args.fp8 else 16 if args.moe else 4 if (args.finetune or args.grpo) else 64
     if args.seq is None:
-        args.seq = 4096 if (args.moe or args.finetune) else 256
-    if args.moe + args.fp8 + args.finetune > 1:
-        raise SystemExit("--moe, --fp8 and --finetune are separate variants")
+        args.seq = 4096 if (args.moe or args.finetune or args.grpo) else 256
+    if args.moe + args.fp8 + args.finetune + args.grpo > 1:
+        raise SystemExit("--moe, --fp8, --finetune and --grpo are separate variants")
     from chessdecoder_b200.distributed import setup_distributed, cleanup_distributed
     rank, local_rank, world = setup_distributed() if args.gpus > 1 or "RANK" in os.environ else (0, 0, 1)
     if args.impl == "reference":
         run_reference(args, rank, world)
+        cleanup_distributed()
+        return
+    if args.grpo:
+        run_grpo(args, rank, world)
         cleanup_distributed()
         return
     import torch.distributed as dist

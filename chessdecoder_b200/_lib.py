@@ -82,6 +82,8 @@ SIGNATURES = {
                          _vp]),
     "cdk_adamw_clip_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _f32, _f32, _f32, _f32, _f32, _i64,
                                       _f32, _vp]),
+    "cdk_grpo_token": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _f32, _f32, _f32, _vp, _vp, _i64, _vp,
+                              _vp, _vp]),
     "cdk_vocab_create": (_vp, [_vp, _vp, _i64, _vp, _vp]),
     "cdk_vocab_destroy": (None, [_vp]),
     "cdk_tokenize_games": (_int, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int,

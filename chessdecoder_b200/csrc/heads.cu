@@ -70,6 +70,58 @@ __global__ void softmax_ce_kernel(const float* __restrict__ logits, long long ld
   }
 }
 
+// GRPO per-token policy loss on gathered action rows (one warp per row):
+// lp = log_softmax(logits)[target]; with old / ref log-probs and the row's
+// advantage A: r = exp(lp - old), r_ref = exp(lp - ref),
+// loss = -min(r A, clamp(r, 1-eps_lo, 1+eps_hi) A) + beta ((r_ref - 1) - log(r_ref + 1e-8)),
+// summed times *norm (1 / action tokens); dlogits = dloss/dlp * (onehot - softmax) * *norm.
+// The gradient of min() is the reference's autograd one: r A where the
+// unclipped term is the minimum (or both are equal inside the clip range), 0 where
+// the clipped term is.
+__global__ void grpo_token_kernel(const float* __restrict__ logits, long long ldl, long long rows, int ncls,
+                                  const int32_t* __restrict__ target, const float* __restrict__ old_lp,
+                                  const float* __restrict__ ref_lp, const float* __restrict__ adv,
+                                  const float* __restrict__ norm, float eps_lo, float eps_hi, float beta,
+                                  float* __restrict__ lp_out, __nv_bfloat16* __restrict__ dl, long long ldd,
+                                  float* __restrict__ dbias, float* __restrict__ loss_out) {
+  const int lane = threadIdx.x & 31;
+  const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const float* x = logits + r * ldl;
+  float mx = -INFINITY;
+  for (int c = lane; c < ncls; c += 32) mx = fmaxf(mx, x[c]);
+  mx = warp_max(mx);
+  float se = 0.f;
+  for (int c = lane; c < ncls; c += 32) se += __expf(x[c] - mx);
+  se = warp_sum(se);
+  const int tgt = target[r];
+  const bool ok = tgt >= 0 && tgt < ncls;
+  const float lp = ok ? x[tgt] - mx - __logf(se) : 0.f;
+  if (lane == 0 && lp_out) lp_out[r] = lp;
+  if (!old_lp) return;
+  const float nrm = norm ? *norm : 1.f;
+  const float A = adv[r];
+  const float ratio = __expf(lp - old_lp[r]);
+  const float s1 = ratio * A;
+  const float rc = fminf(fmaxf(ratio, 1.f - eps_lo), 1.f + eps_hi);
+  const float s2 = rc * A;
+  const bool inside = ratio >= 1.f - eps_lo && ratio <= 1.f + eps_hi;
+  const float rr = __expf(lp - ref_lp[r]);
+  const float kl = (rr - 1.f) - __logf(rr + 1e-8f);
+  const float g_obj = (s1 < s2 || (s1 == s2 && inside)) ? s1 : 0.f;
+  const float dlp = ok ? (-g_obj + beta * (rr - rr / (rr + 1e-8f))) * nrm : 0.f;
+  if (lane == 0 && loss_out && ok) atomicAdd(loss_out, (-fminf(s1, s2) + beta * kl) * nrm);
+  if (dl) {
+    const float inv = 1.f / se;
+    for (int c = lane; c < ncls; c += 32) {
+      float p = __expf(x[c] - mx) * inv;
+      const float g = dlp * ((c == tgt ? 1.f : 0.f) - p);
+      dl[r * ldd + c] = __float2bfloat16_rn(g);
+      if (dbias && dlp != 0.f) atomicAdd(dbias + c, g);
+    }
+  }
+}
+
 __device__ __forceinline__ float softplus_t(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 
 // One block (256 threads) per row; hidden <= 1024, nb <= 256.
@@ -271,6 +323,21 @@ extern "C" int cdk_soft_bucket_ce(const float* logits, int64_t ldl, int64_t rows
   if (dlogits && ldd < nb) return -2;
   soft_bucket_ce_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       logits, ldl, rows, (int)nb, target, valid, centers, norm, loss_weight, dlogits, ldd, loss_out);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+extern "C" int cdk_grpo_token(const float* logits, int64_t ldl, int64_t rows, int64_t ncls, const int32_t* target,
+                              const float* old_lp, const float* ref_lp, const float* adv, const float* norm,
+                              float eps_low, float eps_high, float kl_coeff, float* lp_out, void* dlogits_bf16,
+                              int64_t ldd, float* dbias, float* loss_out, void* stream) {
+  if (rows == 0) return 0;
+  if (!logits || !target || rows < 0 || ncls <= 0 || ldl < ncls) return -1;
+  if (old_lp && (!ref_lp || !adv)) return -2;
+  if (dlogits_bf16 && (!old_lp || ldd < ncls)) return -3;
+  grpo_token_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      logits, ldl, rows, (int)ncls, target, old_lp, ref_lp, adv, norm, eps_low, eps_high, kl_coeff, lp_out,
+      reinterpret_cast<__nv_bfloat16*>(dlogits_bf16), ldd, dbias, loss_out);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
 }

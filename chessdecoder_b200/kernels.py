@@ -363,6 +363,21 @@ def softmax_ce(logits, target32, row_w, norm, loss_weight, dlogits=None, dbias=N
     _count(1)
 
 
+@_timed("grpo_token")
+def grpo_token(logits, target32, lp_out, old_lp=None, ref_lp=None, adv=None, norm=None, eps_low=0.2, eps_high=0.2,
+               kl_coeff=0.0, dlogits=None, dbias=None, loss_out=None, ncls=None):
+    """Per-token log-probs of gathered action rows, and with old / ref
+    log-probs and advantages the GRPO loss and its logit gradient."""
+    _need_cuda(logits, target32)
+    rows = logits.shape[0]
+    ncls = logits.shape[1] if ncls is None else ncls
+    rc = lib().cdk_grpo_token(_p(logits), logits.stride(0), rows, ncls, _p(target32), _p(old_lp), _p(ref_lp), _p(adv),
+                              _p(norm), float(eps_low), float(eps_high), float(kl_coeff), _p(lp_out), _p(dlogits),
+                              dlogits.stride(0) if dlogits is not None else 0, _p(dbias), _p(loss_out), _stream())
+    _check(rc, "grpo_token")
+    _count(1)
+
+
 @_timed("soft_bucket_ce")
 def soft_bucket_ce(logits, target, valid, centers, norm, loss_weight, dlogits=None, loss_out=None):
     rows, nb = logits.shape

@@ -261,6 +261,17 @@ int cdk_adamw_clip_noalloc(float* p, const float* g, float* m, float* v, void* p
                            float max_norm, float lr, float beta1, float beta2, float eps, float wd, int64_t step,
                            float grad_scale, void* stream);
 
+/* ---- GRPO policy loss (chessdecoder/rl/log_probs.py:58-128, rl/grpo.py:58-126)
+ * On gathered action rows: lp_out[r] = log_softmax(logits[r])[target[r]].
+ * With old_lp / ref_lp / adv (per row) also the per-token clipped policy loss
+ * + Schulman KL, summed times *norm (1 / action tokens) into *loss_out, its
+ * gradient as bf16 dlogits [rows, ldd] (optional) and dbias += column sums.
+ * old_lp == NULL: log-probs only (the frozen / rollout policy). */
+int cdk_grpo_token(const float* logits, int64_t ldl, int64_t rows, int64_t ncls, const int32_t* target,
+                   const float* old_lp, const float* ref_lp, const float* adv, const float* norm, float eps_low,
+                   float eps_high, float kl_coeff, float* lp_out, void* dlogits_bf16, int64_t ldd, float* dbias,
+                   float* loss_out, void* stream);
+
 /* ---- batch producer (host memory; no GPU involved) ------------------------
  * Tokenisation + tensorisation of pretraining games: the native counterpart of
  * chessdecoder/dataloader/data.py:7-97 (fen_to_position_tokens,
