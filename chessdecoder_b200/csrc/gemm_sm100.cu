@@ -578,12 +578,12 @@ __device__ __forceinline__ void te_fence_proxy() { asm volatile("fence.proxy.asy
 // have written it.
 template <int BN>
 __device__ void te_stream(const CUtensorMap* te_in, const CUtensorMap* te_out, const GemmParams& p, uint8_t* slots,
-                          uint64_t* sfull, uint64_t* sdone, volatile int* abort_flag) {
+                          uint64_t* sfull, uint64_t* sdone, volatile int* abort_flag, int area) {
   const bool dsw = p.epi.kind == CDK_EPI_DSWIGLU;
   const int hn = (int)p.epi.half_n;
   const int units = p.m_tiles * p.n_tiles;
-  const int nslots = dsw ? 2 : 4;
-  const int sbytes = kTeSlots * kTeSlotBytes / nslots;
+  const int sbytes = dsw ? 32768 : 16384;
+  const int nslots = area / sbytes;
   const int w = te_cols(p);
   TeCursor L{(int)blockIdx.x, 0, 0, 0, 0};
   te_tile<BN>(L, p);
@@ -624,10 +624,10 @@ __device__ void te_stream(const CUtensorMap* te_in, const CUtensorMap* te_out, c
 
 __device__ __forceinline__ void epi_te_tile(const EpiDev& e, uint32_t tbase, int r, int n0, int nch, int half,
                                             int kbase, uint8_t* slots, uint64_t* sfull, uint64_t* sdone,
-                                            volatile int* abort_flag, float sc) {
+                                            volatile int* abort_flag, float sc, int area) {
   const bool dsw = e.kind == CDK_EPI_DSWIGLU;
-  const int nslots = dsw ? 2 : 4;
-  const int sbytes = kTeSlots * kTeSlotBytes / nslots;
+  const int sbytes = dsw ? 32768 : 16384;
+  const int nslots = area / sbytes;
   const int w = dsw ? 64 : 32;  // box columns; this thread takes w / 2 of them
   #pragma unroll 1
   for (int j = 0; j < nch; ++j) {
@@ -839,10 +839,13 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
                      const __grid_constant__ CUtensorMap te_in, const __grid_constant__ CUtensorMap te_out,
                      const GemmParams p) {
   using Cfg = GemmCfg<BN>;
-  constexpr bool TE = TEM == 1;
-  constexpr int kStages = TE ? Cfg::kStagesTE : Cfg::kStages;
+  // TEM 1: TMA-fed form with 64 KB of slots (3-stage ring at BN=256); TEM 4: the
+  // same for the residual add with 2 x 16 KB slots and the full ring
+  constexpr bool TE = TEM == 1 || TEM == 4;
+  constexpr int kStages = TEM == 1 ? Cfg::kStagesTE : Cfg::kStages;
   constexpr bool TE2 = TEM == 2 || TEM == 3;  // store-only / reduce-add forms share the slots and the stream
-  constexpr int kSlotArea = TEM == 1 ? kTeSlots * kTeSlotBytes : TE2 ? kTe2Slots * kTe2SlotBytes : 0;
+  constexpr int kSlotArea =
+      TEM == 1 ? kTeSlots * kTeSlotBytes : TEM == 4 ? 32768 : TE2 ? kTe2Slots * kTe2SlotBytes : 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -852,7 +855,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
-  constexpr int kSlotBars = TEM == 1 ? kTeSlots : TE2 ? kTe2Slots : 0;
+  constexpr int kSlotBars = TEM == 1 ? kTeSlots : TEM == 4 ? 2 : TE2 ? kTe2Slots : 0;
   uint64_t* sfull = tempty + 2;      // TE / store-only forms
   uint64_t* sdone = sfull + kSlotBars;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sdone + kSlotBars);
@@ -872,7 +875,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
       mbar_init(&tempty[a], 256);
     }
     if constexpr (TE) {
-      for (int a = 0; a < kTeSlots; ++a) {
+      for (int a = 0; a < kSlotBars; ++a) {
         mbar_init(&sfull[a], 1);
         mbar_init(&sdone[a], 256);
       }
@@ -994,7 +997,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
     if (lane == 0) {
       prefetch_tmap(&te_in);
       prefetch_tmap(&te_out);
-      if constexpr (TEM == 1) te_stream<BN>(&te_in, &te_out, p, te_slots, sfull, sdone, abort_flag);
+      if constexpr (TE) te_stream<BN>(&te_in, &te_out, p, te_slots, sfull, sdone, abort_flag, kSlotArea);
       else te2_stream<BN>(&te_in, &te_out, p, te_slots, sdone, sfull, abort_flag);
     }
   } else {
@@ -1031,7 +1034,8 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
 
       if constexpr (TE) {
         const int nch = min(BN, p.N - nt * BN) / (e.kind == CDK_EPI_DSWIGLU ? 64 : 32);
-        epi_te_tile(e, tbase, quad * 32 + lane, nt * BN, nch, half, te_k, te_slots, sfull, sdone, abort_flag, sc);
+        epi_te_tile(e, tbase, quad * 32 + lane, nt * BN, nch, half, te_k, te_slots, sfull, sdone, abort_flag, sc,
+                    kSlotArea);
         te_k += nch;
       } else if constexpr (TE2) {
         epi_te2_tile<BN>(e, p, tbase, quad * 32 + lane, row, sc, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN,
@@ -1155,6 +1159,14 @@ static bool te_enabled() {
   return on;
 }
 
+static bool te_resid_deep() {
+  static const bool on = [] {
+    const char* v = getenv("CDK_GEMM_TE_RESID_SLOTS");
+    return v && v[0] == '4';
+  }();
+  return on;
+}
+
 static int num_sms(int dev) {
   static int cache[64] = {0};
   if (dev < 0 || dev >= 64) return 148;
@@ -1172,6 +1184,8 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   using Cfg = GemmCfg<BN>;
   constexpr int threads = TE ? kThreadsTE : kThreads;
   constexpr int smem = TE == 1 ? Cfg::kSmemBytesTE : TE >= 2 ? Cfg::kSmemBytesTE2 : Cfg::kSmemBytes;
+  static_assert(TE != 4 || Cfg::kSmemBytesTE2 == Cfg::kStages * Cfg::kStageBytes + 1024 + 32768 + Cfg::kBarrierBytes,
+                "TEM 4 uses the store-only form's layout");
   static_assert(smem <= 232448, "shared memory");
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -1200,6 +1214,7 @@ static int dispatch_major(bool a_mn, bool b_mn, int te, const CUtensorMap& ta, c
   // the coalesced epilogues (forward kinds and bf16 stores) have their own instantiations
   if (p.scale_inv_a != nullptr) {  // fp8 operands
     if (te == 1 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, true, 1>(ta, tb, ti, to, p, grid, s);
+    if (te == 4 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, true, 4>(ta, tb, ti, to, p, grid, s);
     if (te == 2 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, true, 2>(ta, tb, ti, to, p, grid, s);
     if (te == 2 && !a_mn && b_mn) return launch_gemm<BN, false, true, true, true, 2>(ta, tb, ti, to, p, grid, s);
     if (te == 3 && a_mn && b_mn) return launch_gemm<BN, true, true, false, true, 3>(ta, tb, ti, to, p, grid, s);
@@ -1213,6 +1228,7 @@ static int dispatch_major(bool a_mn, bool b_mn, int te, const CUtensorMap& ta, c
   }
   // TMA-fed epilogue (residual add / SwiGLU backward; K-major A)
   if (te == 1 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, false, 1>(ta, tb, ti, to, p, grid, s);
+  if (te == 4 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, false, 4>(ta, tb, ti, to, p, grid, s);
   if (te == 1 && !a_mn && b_mn) return launch_gemm<BN, false, true, true, false, 1>(ta, tb, ti, to, p, grid, s);
   if (te == 2 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, false, 2>(ta, tb, ti, to, p, grid, s);
   if (te == 2 && !a_mn && b_mn) return launch_gemm<BN, false, true, true, false, 2>(ta, tb, ti, to, p, grid, s);
@@ -1398,7 +1414,9 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   const long long units = m_tiles * n_tiles * splits;
   const int grid = (int)(units < sms ? units : sms);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int tem = te ? 1 : te2 ? 2 : te3 ? 3 : 0;
+  // the residual add keeps the full mainloop ring (its mainloop is the slower half)
+  // unless CDK_GEMM_TE_RESID_SLOTS=4 asks for the 4-slot / 3-stage layout
+  const int tem = te ? (kind == CDK_EPI_RESID_F32 && !te_resid_deep() ? 4 : 1) : te2 ? 2 : te3 ? 3 : 0;
   if (BN == 256) return dispatch_major<256>(a_mn, b_mn, tem, ta, tb, te_in, te_out, p, grid, s);
   return dispatch_major<128>(a_mn, b_mn, tem, ta, tb, te_in, te_out, p, grid, s);
 }
