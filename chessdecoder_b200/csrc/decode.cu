@@ -1,0 +1,399 @@
+// KV-cache inference kernels: the batched incremental backbone of
+// chessdecoder/cpp/decoder/batched_backbone.cpp over the exported KV-cache
+// module chessdecoder/export/backbone_causal.py.
+//
+// Cache layout in HBM, per cache (causal or prefix) and layer:
+//   k, v   bf16 [B][H][max_len][64]   (one 128-byte row per key, per head)
+//   valid  u8   [B][max_len]          (key j of sequence b may be attended)
+//   len    int32 on the device        (keys [0, len) are in the cache)
+// The reference keeps an additive fp32 mask [B, 1, 1, max_seq_len] of 0 / -1e9
+// per cache and concatenates fp16 K / V; here the validity is one byte per key
+// and the cache is preallocated, so a step writes only its new rows.
+//
+// Kernels:
+//   kv_append     rotary embedding of q and k at explicit per-token positions
+//                 (backbone_causal.py:68-77) and the new k / v rows into the
+//                 cache at [len, len + S_new) (backbone_causal.py:112-116);
+//   decode_attn   softmax(q k^T / 8 + mask) v for S_new new queries per
+//                 sequence over the cache keys and the new block
+//                 (backbone_causal.py:121-124; masks of batched_backbone.cpp:
+//                 117-150 causalForward, 160-177 causalIncremental, 192-205
+//                 prefixForward, 207-225 prefixIncremental, 227-258
+//                 prefixBlockForward, 264-305 probes);
+//   decode_mark   marks keys valid and advances len (markCausalValid,
+//                 markCausalValidRange, markPrefixValid(Range) and the cache
+//                 length update of forwardImpl).
+// The HBM-bound part is decode_attn: it reads each cache key row once per
+// (sequence, head, 8-query chunk); kv_append and decode_mark are O(new rows).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "cdk.h"
+#include "cdk_common.cuh"
+
+using namespace cdk;
+
+namespace {
+
+constexpr int kHD = 64;      // head dim (embed 1024 / 16 heads)
+constexpr int kQC = 8;       // queries per CTA
+constexpr int kWarps = 8;    // warps per CTA; each walks its own key tiles
+constexpr int kKT = 32;      // keys per warp tile: one key per lane
+
+__device__ __forceinline__ float2 bf2f(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+__device__ __forceinline__ uint32_t f2bf2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// One thread per (token row, head, dim pair): q / k rotated, v copied.
+// qkv_f32: the projection output is fp32 [T, ldq] (q | k | v), not rotated;
+// otherwise it is bf16 with q / k already rotated (a prefill through the
+// training forward) and only the k / v rows are written.
+__global__ void kv_append_kernel(const void* __restrict__ qkv, long long ldq, int qkv_f32,
+                                 const int32_t* __restrict__ pos, const float* __restrict__ rope, int rope_len,
+                                 int S_new, int H, long long max_len, const int32_t* __restrict__ len_dev,
+                                 __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
+                                 __nv_bfloat16* __restrict__ q_out, long long ldo, long long total) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int pair = (int)(idx & 31);
+  const long long th = idx >> 5;
+  const int h = (int)(th % H);
+  const long long t = th / H;
+  const long long b = t / S_new;
+  const int s = (int)(t % S_new);
+  const long long slot = (long long)*len_dev + s;
+  const int E = H * kHD;
+  const int col = h * kHD + 2 * pair;
+  float2 q, k, v;
+  if (qkv_f32) {
+    const float* row = reinterpret_cast<const float*>(qkv) + t * ldq;
+    q = *reinterpret_cast<const float2*>(row + col);
+    k = *reinterpret_cast<const float2*>(row + E + col);
+    v = *reinterpret_cast<const float2*>(row + 2 * E + col);
+    const int p = pos[t];
+    if (p < 0 || p >= rope_len) {
+      if (pair == 0) report_error(kErrIndex);
+      return;
+    }
+    const float2 cs = *reinterpret_cast<const float2*>(rope + ((long long)p * 32 + pair) * 2);
+    q = make_float2(q.x * cs.x - q.y * cs.y, q.y * cs.x + q.x * cs.y);
+    k = make_float2(k.x * cs.x - k.y * cs.y, k.y * cs.x + k.x * cs.y);
+    *reinterpret_cast<uint32_t*>(q_out + t * ldo + col) = f2bf2(q.x, q.y);
+  } else {
+    const __nv_bfloat16* row = reinterpret_cast<const __nv_bfloat16*>(qkv) + t * ldq;
+    k = bf2f(*reinterpret_cast<const uint32_t*>(row + E + col));
+    v = bf2f(*reinterpret_cast<const uint32_t*>(row + 2 * E + col));
+  }
+  if (slot >= max_len) {
+    if (pair == 0) report_error(kErrIndex);
+    return;
+  }
+  const long long off = ((b * H + h) * max_len + slot) * kHD + 2 * pair;
+  *reinterpret_cast<uint32_t*>(kc + off) = f2bf2(k.x, k.y);
+  *reinterpret_cast<uint32_t*>(vc + off) = f2bf2(v.x, v.y);
+}
+
+struct DecodeAttnArgs {
+  const __nv_bfloat16* q;
+  long long ldq;
+  const __nv_bfloat16* kc;
+  const __nv_bfloat16* vc;
+  long long max_len;
+  const int32_t* len_dev;  // cache keys [0, *len_dev) precede the new block
+  int S_new;
+  int H;
+  const uint8_t* valid;    // [B][ldv]
+  long long ldv;
+  int block_mode;          // CDK_BLOCK_*
+  const uint8_t* active;   // [B] or null (all active)
+  const int64_t* num_real; // [B] or null (all real): CAUSAL mode
+  const uint8_t* full;     // [B][S_new][ldf] explicit mask over all keys, or null
+  long long ldf;
+  __nv_bfloat16* out;
+  long long ldo;
+  float scale_log2;        // softmax scale * log2(e)
+};
+
+// Grid (ceil(S_new / kQC), H, B), kWarps warps.  Warp w walks key tiles
+// w, w + kWarps, ...; lane l holds key (tile * 32 + l) in registers for the
+// scores, the tile's V rows sit in shared memory for the weighted sum (lane l
+// owns output dims 2l, 2l + 1).  Online softmax per query and warp, merged
+// across warps at the end.  A query with no valid key writes zeros.
+__global__ void __launch_bounds__(kWarps * 32, 2) decode_attn_kernel(const DecodeAttnArgs a) {
+  __shared__ float qs[kQC][kHD];
+  __shared__ __align__(16) uint32_t vbuf[kWarps][kKT][kHD / 2];  // also the merge area after the loop
+  __shared__ float cm[kWarps][kQC], cl[kWarps][kQC];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int q0 = blockIdx.x * kQC;
+  const int h = blockIdx.y;
+  const long long b = blockIdx.z;
+  const int nq = min(kQC, a.S_new - q0);
+  int n_cache = *a.len_dev;
+  if (n_cache < 0 || (long long)n_cache + a.S_new > a.max_len) {  // host keeps len + S_new <= max_len
+    if (tid == 0) report_error(kErrIndex);
+    n_cache = max(0, min(n_cache, (int)a.max_len - a.S_new));
+  }
+  const int total = n_cache + a.S_new;
+
+  for (int i = tid; i < kQC * kHD; i += blockDim.x) {
+    const int q = i / kHD, d = i % kHD;
+    float v = 0.f;
+    if (q < nq) v = __bfloat162float(a.q[(b * a.S_new + q0 + q) * a.ldq + h * kHD + d]) * a.scale_log2;
+    qs[q][d] = v;
+  }
+  __syncthreads();
+
+  const bool act = a.active == nullptr || a.active[b] != 0;
+  const long long nreal = a.num_real ? a.num_real[b] : (long long)a.S_new;
+  const __nv_bfloat16* kbase = a.kc + (b * a.H + h) * a.max_len * kHD;
+  const __nv_bfloat16* vbase = a.vc + (b * a.H + h) * a.max_len * kHD;
+
+  float m[kQC], l[kQC];
+  float2 acc[kQC];
+#pragma unroll
+  for (int q = 0; q < kQC; ++q) {
+    m[q] = -INFINITY;
+    l[q] = 0.f;
+    acc[q] = make_float2(0.f, 0.f);
+  }
+  uint32_t (*vs)[kHD / 2] = vbuf[warp];
+
+  for (int t0 = warp * kKT; t0 < total; t0 += kWarps * kKT) {
+    const int j = t0 + lane;
+    uint4 kr[8];
+    if (j < total) {
+      const uint4* src = reinterpret_cast<const uint4*>(kbase + (long long)j * kHD);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) kr[c] = src[c];
+    } else {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) kr[c] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    // V tile: 4 rows of 8 x 16 bytes per instruction, coalesced.
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = (lane >> 3) + 4 * i, c = lane & 7;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (t0 + r < total) v = reinterpret_cast<const uint4*>(vbase + (long long)(t0 + r) * kHD)[c];
+      *reinterpret_cast<uint4*>(&vs[r][c * 4]) = v;
+    }
+    // Key validity shared by all queries (cache part) or per query (new block).
+    const bool in_cache = j < n_cache;
+    const bool cache_ok = j < total && (in_cache || a.block_mode == CDK_BLOCK_VALID) && a.valid[b * a.ldv + j] != 0;
+    const int jt = j - n_cache;  // index within the new block
+    __syncwarp();
+
+    float p[kQC];
+#pragma unroll
+    for (int q = 0; q < kQC; ++q) {
+      p[q] = 0.f;
+      if (q < nq) {
+        const float* qq = qs[q];
+        float s = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t w[4] = {kr[c].x, kr[c].y, kr[c].z, kr[c].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 kf = bf2f(w[e]);
+            const float2 qf = *reinterpret_cast<const float2*>(qq + c * 8 + e * 2);
+            s = fmaf(qf.x, kf.x, s);
+            s = fmaf(qf.y, kf.y, s);
+          }
+        }
+        bool ok;
+        if (j >= total) {
+          ok = false;
+        } else if (a.full) {
+          ok = j < a.ldf && a.full[(b * a.S_new + q0 + q) * a.ldf + j] != 0;
+        } else if (in_cache || a.block_mode == CDK_BLOCK_VALID) {
+          ok = cache_ok;
+        } else if (a.block_mode == CDK_BLOCK_CAUSAL) {
+          ok = jt <= q0 + q && jt < nreal;
+        } else if (a.block_mode == CDK_BLOCK_ACTIVE) {
+          ok = act;
+        } else {
+          ok = true;
+        }
+        s = ok ? s : -INFINITY;
+        float tmax = s;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+        const float mnew = fmaxf(m[q], tmax);
+        if (mnew != -INFINITY) {
+          const float pv = ok ? exp2f(s - mnew) : 0.f;
+          float sum = pv;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+          const float alpha = exp2f(m[q] - mnew);
+          l[q] = l[q] * alpha + sum;
+          acc[q].x *= alpha;
+          acc[q].y *= alpha;
+          m[q] = mnew;
+          p[q] = pv;
+        }
+      }
+    }
+#pragma unroll 4
+    for (int jj = 0; jj < kKT; ++jj) {
+      const float2 v = bf2f(vs[jj][lane]);
+#pragma unroll
+      for (int q = 0; q < kQC; ++q) {
+        if (q < nq) {
+          const float pj = __shfl_sync(0xffffffffu, p[q], jj);
+          acc[q].x = fmaf(pj, v.x, acc[q].x);
+          acc[q].y = fmaf(pj, v.y, acc[q].y);
+        }
+      }
+    }
+    __syncwarp();
+  }
+
+  // Merge the warps' partial softmax states.
+  __syncthreads();
+  float2 (*cacc)[kQC][32] = reinterpret_cast<float2 (*)[kQC][32]>(&vbuf[0][0][0]);
+  static_assert(sizeof(float2) * kWarps * kQC * 32 <= sizeof(vbuf), "merge area");
+#pragma unroll
+  for (int q = 0; q < kQC; ++q) {
+    cacc[warp][q][lane] = acc[q];
+    if (lane == 0) {
+      cm[warp][q] = m[q];
+      cl[warp][q] = l[q];
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < kQC * 32; i += blockDim.x) {
+    const int q = i >> 5, d2 = i & 31;
+    if (q >= nq) continue;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, cm[w][q]);
+    float L = 0.f, ox = 0.f, oy = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float f = exp2f(cm[w][q] - M);
+        L += cl[w][q] * f;
+        ox += cacc[w][q][d2].x * f;
+        oy += cacc[w][q][d2].y * f;
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    *reinterpret_cast<uint32_t*>(a.out + (b * a.S_new + q0 + q) * a.ldo + h * kHD + 2 * d2) = f2bf2(ox * inv, oy * inv);
+  }
+}
+
+// One block: keys [base, base + count) of each sequence become valid where the
+// sequence is active and the key's offset is below its real-token count, with
+// base = start (start >= 0) or len; then len += advance (every thread has read
+// len before thread 0 writes it).
+__global__ void decode_mark_kernel(uint8_t* __restrict__ valid, long long ldv, int B, long long start, int count,
+                                   int advance, int32_t* __restrict__ len_dev, const uint8_t* __restrict__ active,
+                                   const int64_t* __restrict__ num_real, long long max_len) {
+  const int len = *len_dev;
+  const long long base = start >= 0 ? start : (long long)len;
+  for (long long i = threadIdx.x; i < (long long)B * count; i += blockDim.x) {
+    const long long b = i / count;
+    const int s = (int)(i % count);
+    const bool on = (active == nullptr || active[b] != 0) && (num_real == nullptr || s < num_real[b]);
+    if (on && base + s < max_len) valid[b * ldv + base + s] = 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (base + count > max_len || (long long)len + advance > max_len) report_error(kErrIndex);
+    *len_dev = len + advance;
+  }
+}
+
+__global__ void decode_slots_kernel(const uint8_t* __restrict__ om, long long n, int32_t* __restrict__ slot) {
+  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t < n) slot[t] = om[t] ? (int32_t)t : -1;
+}
+
+inline bool al(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
+}  // namespace
+
+extern "C" int cdk_kv_append(const void* qkv, int64_t ldq, int qkv_f32, const int32_t* pos, const float* rope,
+                             int64_t rope_len, int64_t B, int64_t S_new, int64_t H, void* k_cache, void* v_cache,
+                             int64_t max_len, const int32_t* len_dev, void* q_out, int64_t ldo, void* stream) {
+  if (B == 0 || S_new == 0) return 0;
+  if (!qkv || !k_cache || !v_cache || !len_dev || B < 0 || S_new < 0 || H <= 0 || max_len <= 0) return -1;
+  if (ldq < 3 * H * kHD || ldq % 2) return -2;
+  if (qkv_f32 && (!pos || !rope || !q_out || rope_len <= 0 || ldo < H * kHD || ldo % 2)) return -3;
+  if (!al(k_cache, 16) || !al(v_cache, 16) || !al(qkv, 8)) return -4;
+  const long long total = B * S_new * H * 32;
+  const unsigned blocks = (unsigned)((total + 255) / 256);
+  kv_append_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      qkv, ldq, qkv_f32, pos, rope, (int)rope_len, (int)S_new, (int)H, max_len, len_dev,
+      reinterpret_cast<__nv_bfloat16*>(k_cache), reinterpret_cast<__nv_bfloat16*>(v_cache),
+      reinterpret_cast<__nv_bfloat16*>(q_out), ldo, total);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+extern "C" int cdk_decode_attn(const void* q, int64_t ldq, const void* k_cache, const void* v_cache,
+                               int64_t max_len, const int32_t* len_dev, int64_t S_new, int64_t B, int64_t H,
+                               const uint8_t* valid, int64_t ldv, int block_mode, const uint8_t* active,
+                               const int64_t* num_real, const uint8_t* full_mask, int64_t ldf, void* out,
+                               int64_t ldo, float scale, void* stream) {
+  if (B == 0 || S_new == 0) return 0;
+  if (!q || !k_cache || !v_cache || !len_dev || !valid || !out || B < 0 || S_new < 0 || H <= 0) return -1;
+  if (B > 65535 || H > 65535 || ldq < H * kHD || ldo < H * kHD || ldo % 2 || ldv < max_len || S_new > max_len)
+    return -2;
+  if (full_mask && ldf < 1) return -3;
+  if (block_mode < CDK_BLOCK_CAUSAL || block_mode > CDK_BLOCK_VALID) return -4;
+  if (!al(k_cache, 16) || !al(v_cache, 16) || !al(out, 4)) return -5;
+  DecodeAttnArgs a;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  a.ldq = ldq;
+  a.kc = reinterpret_cast<const __nv_bfloat16*>(k_cache);
+  a.vc = reinterpret_cast<const __nv_bfloat16*>(v_cache);
+  a.max_len = max_len;
+  a.len_dev = len_dev;
+  a.S_new = (int)S_new;
+  a.H = (int)H;
+  a.valid = valid;
+  a.ldv = ldv;
+  a.block_mode = block_mode;
+  a.active = active;
+  a.num_real = num_real;
+  a.full = full_mask;
+  a.ldf = ldf;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.ldo = ldo;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  dim3 grid((unsigned)((S_new + kQC - 1) / kQC), (unsigned)H, (unsigned)B);
+  decode_attn_kernel<<<grid, kWarps * 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+extern "C" int cdk_decode_mark(void* valid, int64_t ldv, int64_t B, int64_t start, int64_t count, int64_t advance,
+                               int32_t* len_dev, const uint8_t* active, const int64_t* num_real, int64_t max_len,
+                               void* stream) {
+  if (!valid || !len_dev || B < 0 || count < 0 || advance < 0 || ldv < max_len || start >= max_len) return -1;
+  if (B == 0 || (count == 0 && advance == 0)) return 0;
+  decode_mark_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<uint8_t*>(valid), ldv, (int)B, start, (int)count, (int)advance, len_dev, active, num_real,
+      max_len);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+extern "C" int cdk_decode_slots(const uint8_t* override_mask, int64_t n, int32_t* slot, void* stream) {
+  if (n == 0) return 0;
+  if (!override_mask || !slot || n < 0) return -1;
+  decode_slots_kernel<<<(unsigned)((n + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      override_mask, n, slot);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}

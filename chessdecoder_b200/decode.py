@@ -1,0 +1,272 @@
+"""KV-cache inference backbone on the CUDA kernels: the counterpart of
+chessdecoder/cpp/decoder/batched_backbone.{hpp,cpp} (``BatchedBackbone``),
+which runs the exported module chessdecoder/export/backbone_causal.py
+(``BackboneCausal.forward``: embedding with Fourier override, 12 pre-norm
+layers with RoPE at explicit positions, attention over past + new keys under an
+additive mask, SwiGLU MLP, final norm) through TorchScript with fp16 caches.
+
+Here one batch of B sequences keeps two caches (causal and prefix, as the
+reference), each preallocated in HBM:
+
+* ``k`` / ``v``: bf16 [L, B, H, max_len, 64]; a step writes only its new rows;
+* ``valid``: u8 [B, max_len], the reference's 0 / -1e9 mask buffer as one byte
+  per key;
+* ``len_dev``: the cache length as a device int32, read by the kernels, so a
+  fixed-shape step replays from a CUDA graph; ``len`` is its host mirror.
+
+Per layer a step runs RMSNorm -> fused q|k|v GEMM (fp32 out) -> ``kv_append``
+(RoPE at the tokens' positions, q to a bf16 buffer, k / v into the cache) ->
+``decode_attn`` -> output GEMM + residual -> RMSNorm -> SwiGLU GEMM -> down
+GEMM + residual; then the final norm.  Weights are the training parameter
+store's bf16 copies (the same ``state_dict`` layout as ChessDecoder).
+
+The public methods mirror BatchedBackbone (batched_backbone.hpp:17-94) with the
+same argument meaning: ids / pos [B, S] int64, override values [B, S] and mask
+[B, S] bool (Fourier injection), active [B] bool, num_real [B] int64.  They
+return the final-norm hidden state [B, S, E] (fp32; ``last_hidden16`` holds the
+bf16 copy for the heads).
+"""
+from __future__ import annotations
+
+import dataclasses
+from typing import Optional
+
+import torch
+
+from . import kernels as K
+from .engine import ModelConfig, ParamStore, init_reference_weights, rope_table
+
+HEAD_DIM = 64
+
+
+class KVCache:
+    def __init__(self, L, B, H, max_len, device):
+        self.k = torch.zeros(L, B, H, max_len, HEAD_DIM, dtype=torch.bfloat16, device=device)
+        self.v = torch.zeros_like(self.k)
+        self.valid = torch.zeros(B, max_len, dtype=torch.uint8, device=device)
+        self.len_dev = torch.zeros(1, dtype=torch.int32, device=device)
+        self.len = 0
+
+    def reset(self):
+        """resetCausal / resetPrefix (batched_backbone.cpp:110-116, 184-190):
+        empty cache, every key invalid.  Rows past ``len`` are rewritten before
+        they are read, so k / v need no clearing."""
+        self.valid.zero_()
+        self.len_dev.zero_()
+        self.len = 0
+
+
+def _u8(t, device):
+    return None if t is None else t.to(device=device, dtype=torch.bool).contiguous().view(torch.uint8)
+
+
+def _i64(t, device):
+    return None if t is None else t.to(device=device, dtype=torch.int64).contiguous()
+
+
+class BatchedBackbone:
+    """Batched KV-cache backbone (dense ChessDecoder; the exported module has no
+    MoE).  ``max_seq_len``: cache capacity (keys per sequence), default the
+    model's."""
+
+    def __init__(self, cfg: Optional[ModelConfig] = None, batch_size: int = 1, max_seq_len: Optional[int] = None,
+                 state_dict=None, device="cuda", seed: int = 0, store: Optional[ParamStore] = None):
+        cfg = cfg or ModelConfig()
+        if cfg.moe_experts:
+            raise ValueError("the KV-cache backbone covers the dense model")
+        if cfg.head_dim != HEAD_DIM:
+            raise ValueError(f"head_dim must be {HEAD_DIM}")
+        self.cfg = cfg
+        self.B = int(batch_size)
+        self.max_len = int(max_seq_len or cfg.max_seq_len)
+        self.device = torch.device(device)
+        if store is None:
+            store = ParamStore(dataclasses.replace(cfg, finetune=False), self.device, optimizer_state=False)
+            sd = state_dict if state_dict is not None else init_reference_weights(cfg, seed)
+            store.load_state_dict({k: v.to(self.device) for k, v in sd.items()})
+        self.store = store
+        self.rope = rope_table(max(cfg.max_seq_len, self.max_len), cfg.head_dim).to(self.device)
+        L, H = cfg.num_layers, cfg.num_heads
+        self.causal = KVCache(L, self.B, H, self.max_len, self.device)
+        self.prefix = KVCache(L, self.B, H, self.max_len, self.device)
+        st, E, F = store, cfg.embed_dim, cfg.ff
+        self._layers = []
+        for i in range(L):
+            p = f"layers.{i}."
+            self._layers.append(dict(
+                wqkv=st.span(p + "attn.q_proj.weight", p + "attn.v_proj.weight").view(3 * E, E),
+                wo=st.bf16(p + "attn.output_proj.weight"), s1=st.param(p + "sa_norm.scale"),
+                s2=st.param(p + "mlp_norm.scale"),
+                w13=st.span(p + "mlp.w1.weight", p + "mlp.w3.weight").view(2 * F, E), w2=st.bf16(p + "mlp.w2.weight")))
+        self._ar = {}
+        self.last_hidden16 = None
+
+    # -- lengths ------------------------------------------------------------
+    @property
+    def causal_len(self):
+        return self.causal.len
+
+    @property
+    def prefix_len(self):
+        return self.prefix.len
+
+    def reset_causal(self):
+        self.causal.reset()
+
+    def reset_prefix(self):
+        self.prefix.reset()
+
+    # -- mask buffer helpers (batched_backbone.cpp:74-104) ------------------
+    def mark_causal_valid(self, pos: int, active):
+        K.decode_mark(self.causal.valid, self.B, self.causal.len_dev, start=int(pos), count=1,
+                      active=_u8(active, self.device))
+
+    def mark_prefix_valid(self, pos: int, active):
+        K.decode_mark(self.prefix.valid, self.B, self.prefix.len_dev, start=int(pos), count=1,
+                      active=_u8(active, self.device))
+
+    def mark_causal_valid_range(self, start: int, count: int, active):
+        K.decode_mark(self.causal.valid, self.B, self.causal.len_dev, start=int(start), count=int(count),
+                      active=_u8(active, self.device))
+
+    def mark_prefix_valid_range(self, start: int, count: int, active):
+        K.decode_mark(self.prefix.valid, self.B, self.prefix.len_dev, start=int(start), count=int(count),
+                      active=_u8(active, self.device))
+
+    # -- core forward --------------------------------------------------------
+    def _arange32(self, n):
+        t = self._ar.get(n)
+        if t is None:
+            t = self._ar[n] = torch.arange(n, dtype=torch.int32, device=self.device)
+        return t
+
+    def _embed(self, ids, ov, om_u8):
+        """tok_embedding, with the rows under the override mask replaced by the
+        Fourier encoding of their value (backbone_causal.py:100-109: every row
+        is encoded, then blended)."""
+        cfg, st = self.cfg, self.store
+        T, E, nf = ids.numel(), cfg.embed_dim, cfg.num_fourier_freq
+        dev = self.device
+        rows = self._arange32(T)
+        ones = torch.ones(T, dtype=torch.uint8, device=dev)
+        fvals = torch.empty(T, device=dev)
+        feat = torch.empty(T, 2 * nf, device=dev)
+        K.fourier_features(ov, ov, ones, torch.zeros_like(ones), None, None, st.param("fourier_encoder.frequencies"),
+                           rows, fvals, feat)
+        frows = torch.empty(T, E, device=dev)
+        K.gemm_f32(feat, st.param("fourier_encoder.proj.weight"), frows, bias=st.param("fourier_encoder.proj.bias"),
+                   M=T)
+        slot = torch.empty(T, dtype=torch.int32, device=dev)
+        K.decode_slots(om_u8, slot)
+        h0 = torch.empty(T, E, device=dev)
+        K.embed_fwd(ids, st.param("tok_embedding.weight"), slot, frows, h0)
+        return h0
+
+    def _forward(self, cache: KVCache, ids, pos, ov, om, *, block_mode, active=None, num_real=None, full=None):
+        """One pass of S new tokens per sequence over ``cache`` (keys [0, len)
+        plus the new block); writes the new k / v rows at [len, len + S) but
+        leaves len and the validity bytes to the caller."""
+        cfg, dev = self.cfg, self.device
+        B, S = ids.shape
+        if B != self.B:
+            raise ValueError(f"batch {B} != {self.B}")
+        if cache.len + S > self.max_len:
+            raise ValueError(f"cache full: {cache.len} + {S} > {self.max_len}")
+        E, F, H = cfg.embed_dim, cfg.ff, cfg.num_heads
+        T = B * S
+        ids = ids.to(device=dev, dtype=torch.int64).reshape(-1).contiguous()
+        pos32 = pos.to(device=dev, dtype=torch.int32).reshape(-1).contiguous()
+        ov = (torch.zeros(T, device=dev) if ov is None else
+              ov.to(device=dev, dtype=torch.float32).reshape(-1).contiguous())
+        om_u8 = (torch.zeros(T, dtype=torch.uint8, device=dev) if om is None else _u8(om, dev).reshape(-1))
+        x = self._embed(ids, ov, om_u8)
+        n1 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+        qkv = torch.empty(T, 3 * E, device=dev)
+        q16 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+        ao = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+        gu = torch.empty(T, 2 * F, device=dev, dtype=torch.bfloat16)
+        u = torch.empty(T, F, device=dev, dtype=torch.bfloat16)
+        h1 = torch.empty(T, E, device=dev)
+        for i, w in enumerate(self._layers):
+            K.rmsnorm_fwd(x, w["s1"], y16=n1)
+            K.gemm(n1, w["wqkv"], kind=K.EPI_STORE_F32, out=qkv)
+            K.kv_append(qkv, B, S, H, cache.k[i], cache.v[i], cache.len_dev, pos=pos32, rope=self.rope, q_out=q16)
+            K.decode_attn(q16, cache.k[i], cache.v[i], cache.len_dev, S, B, H, cache.valid, ao, block_mode=block_mode,
+                          active=active, num_real=num_real, full_mask=full)
+            K.gemm(ao, w["wo"], kind=K.EPI_RESID_F32, out=h1, resid=x)
+            K.rmsnorm_fwd(h1, w["s2"], y16=n1)
+            K.gemm(n1, w["w13"], kind=K.EPI_SWIGLU, out=u, out2=gu, half_n=F)
+            xn = torch.empty(T, E, device=dev)
+            K.gemm(u, w["w2"], kind=K.EPI_RESID_F32, out=xn, resid=h1)
+            x = xn
+        h16 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+        h32 = torch.empty(T, E, device=dev)
+        K.rmsnorm_fwd(x, self.store.param("norm.scale"), y16=h16, y32=h32)
+        self.last_hidden16 = h16.view(B, S, E)
+        return h32.view(B, S, E)
+
+    # -- causal mode (batched_backbone.cpp:110-177) -------------------------
+    def causal_forward(self, ids, pos, ov, om, active, num_real):
+        """S new tokens, causal among the first num_real[b] of each sequence;
+        those become valid keys and the cache grows by S."""
+        B, S = ids.shape
+        nr = _i64(num_real, self.device)
+        h = self._forward(self.causal, ids, pos, ov, om, block_mode=K.BLOCK_CAUSAL, num_real=nr)
+        K.decode_mark(self.causal.valid, B, self.causal.len_dev, start=-1, count=S, advance=S, num_real=nr)
+        self.causal.len += S
+        return h
+
+    def causal_incremental(self, ids, pos, ov, om, active):
+        """One token: its key is valid where active (marked first, as the
+        reference does); the cache grows by 1."""
+        return self._incremental(self.causal, ids, pos, ov, om, active)
+
+    def causal_probe(self, ids, pos, ov, om):
+        """S tokens over the valid cache and each other; no cache update."""
+        return self._forward(self.causal, ids, pos, ov, om, block_mode=K.BLOCK_ALL)
+
+    # -- prefix mode (batched_backbone.cpp:184-258) -------------------------
+    def prefix_forward(self, ids, pos, mask, ov, om, active):
+        """Full pass with an explicit additive mask [B, 1, S, len + S] (0 =
+        attend); then keys [0, S) become valid where active, as the reference
+        marks them."""
+        B, S = ids.shape
+        total = self.prefix.len + S
+        m = mask.to(self.device)
+        if m.dim() == 4:
+            m = m[:, 0]
+        if tuple(m.shape) != (B, S, total):
+            raise ValueError(f"mask must be [B, 1, {S}, {total}]")
+        full = (m > -1e4).to(torch.uint8).contiguous()
+        act = _u8(active, self.device)
+        h = self._forward(self.prefix, ids, pos, ov, om, block_mode=K.BLOCK_ALL, full=full)
+        K.decode_mark(self.prefix.valid, B, self.prefix.len_dev, start=0, count=S, advance=S, active=act)
+        self.prefix.len += S
+        return h
+
+    def prefix_incremental(self, ids, pos, ov, om, active):
+        return self._incremental(self.prefix, ids, pos, ov, om, active)
+
+    def prefix_block_forward(self, ids, pos, ov, om, active):
+        """S tokens attending to the valid cache and, where active, to the
+        whole block; the block's keys become valid where active."""
+        B, S = ids.shape
+        act = _u8(active, self.device)
+        h = self._forward(self.prefix, ids, pos, ov, om, block_mode=K.BLOCK_ACTIVE, active=act)
+        K.decode_mark(self.prefix.valid, B, self.prefix.len_dev, start=-1, count=S, advance=S, active=act)
+        self.prefix.len += S
+        return h
+
+    def prefix_probe(self, ids, pos, ov, om):
+        return self._forward(self.prefix, ids, pos, ov, om, block_mode=K.BLOCK_ALL)
+
+    def _incremental(self, cache, ids, pos, ov, om, active):
+        B, S = ids.shape
+        if S != 1:
+            raise ValueError("incremental steps take one token per sequence")
+        act = _u8(active, self.device)
+        K.decode_mark(cache.valid, B, cache.len_dev, start=-1, count=1, active=act)
+        h = self._forward(cache, ids, pos, ov, om, block_mode=K.BLOCK_VALID)
+        K.decode_mark(cache.valid, B, cache.len_dev, advance=1)
+        cache.len += 1
+        return h

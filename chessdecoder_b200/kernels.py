@@ -514,3 +514,53 @@ def moe_gather_sum(dxe, slot, out, accumulate=False):
     T, dim = out.shape
     _check(lib().cdk_moe_gather_sum(_p(dxe), _p(slot), _p(out), T, dim, int(accumulate), _stream()), "moe_gather_sum")
     _count(1)
+
+
+# ---------------------------------------------------------------------------
+# KV-cache inference (csrc/decode.cu)
+# ---------------------------------------------------------------------------
+BLOCK_CAUSAL, BLOCK_ACTIVE, BLOCK_ALL, BLOCK_VALID = 0, 1, 2, 3
+
+
+@_timed("kv_append")
+def kv_append(qkv, B, S_new, H, k_cache, v_cache, len_dev, pos=None, rope=None, q_out=None):
+    """qkv fp32 (rotated here at pos) or bf16 (already rotated); k / v rows into
+    the cache at [len, len + S_new)."""
+    _need_cuda(qkv, k_cache, v_cache, len_dev)
+    f32 = qkv.dtype == torch.float32
+    max_len = k_cache.shape[-2]
+    rc = lib().cdk_kv_append(_p(qkv), qkv.stride(0), int(f32), _p(pos), _p(rope), rope.shape[0] if rope is not None
+                             else 0, B, S_new, H, _p(k_cache), _p(v_cache), max_len, _p(len_dev), _p(q_out),
+                             q_out.stride(0) if q_out is not None else 0, _stream())
+    _check(rc, "kv_append")
+    _count(1)
+
+
+@_timed("decode_attn")
+def decode_attn(q, k_cache, v_cache, len_dev, S_new, B, H, valid, out, block_mode=BLOCK_ACTIVE, active=None,
+                num_real=None, full_mask=None, scale=0.125):
+    _need_cuda(q, k_cache, v_cache, valid, out)
+    max_len = k_cache.shape[-2]
+    rc = lib().cdk_decode_attn(_p(q), q.stride(0), _p(k_cache), _p(v_cache), max_len, _p(len_dev), S_new, B, H,
+                               _p(valid), valid.stride(0), block_mode, _p(active), _p(num_real), _p(full_mask),
+                               full_mask.stride(1) if full_mask is not None else 0, _p(out), out.stride(0), scale,
+                               _stream())
+    _check(rc, "decode_attn")
+    _count(1)
+
+
+@_timed("decode_mark")
+def decode_mark(valid, B, len_dev, start=-1, count=0, advance=0, active=None, num_real=None):
+    """Keys [base, base + count) valid where active / real (base = start, or
+    the cache length when start < 0); then the cache length += advance."""
+    rc = lib().cdk_decode_mark(_p(valid), valid.stride(0), B, start, count, advance, _p(len_dev), _p(active),
+                               _p(num_real), valid.shape[1], _stream())
+    _check(rc, "decode_mark")
+    _count(1)
+
+
+@_timed("decode_slots")
+def decode_slots(override_mask_u8, slot32):
+    rc = lib().cdk_decode_slots(_p(override_mask_u8), override_mask_u8.numel(), _p(slot32), _stream())
+    _check(rc, "decode_slots")
+    _count(1)

@@ -304,6 +304,52 @@ int cdk_tokenize_games(const void* vocab, int64_t n_games, const int64_t* game_o
                        int64_t* move_target_ids, uint8_t* move_mask, uint8_t* wl_positions, uint8_t* d_positions,
                        float* wl_targets, float* d_targets, uint8_t* wdl_valid, int64_t* block_id);
 
+/* ---- KV-cache inference (chessdecoder/cpp/decoder/batched_backbone.hpp:17-94,
+ *      over the exported module chessdecoder/export/backbone_causal.py:79-158)
+ * A cache holds, per layer, k and v as bf16 [B][H][max_len][64], a validity
+ * byte per key u8 [B][ldv] (the reference's 0 / -1e9 mask buffer
+ * [B, 1, 1, max_seq_len]) and its length as an int32 on the device (len_dev),
+ * so that a step can be captured in a CUDA graph.  A step with S_new new tokens
+ * per sequence (rows t = b * S_new + s):
+ *
+ * cdk_kv_append: qkv_f32 != 0: qkv fp32 [T, ldq] = q | k | v projections (not
+ * rotated); q and k are rotated at positions pos[t] (rope [rope_len][32][2] =
+ * (cos, sin), the rope_cache of backbone_causal.py:33), q goes to q_out bf16
+ * [T, ldo] and k, v to cache rows len + s.  qkv_f32 == 0: qkv bf16 with q, k
+ * already rotated (a prefill through the training forward): only k, v are
+ * written (pos, rope, q_out unused).
+ *
+ * cdk_decode_attn: out[t, h] = softmax(q k^T * scale + mask) v over keys
+ * [0, len + S_new) of sequence b, head h.  Keys j < len: valid[b][j].  New
+ * keys (j = len + u): block_mode CDK_BLOCK_CAUSAL -> u <= s and u <
+ * num_real[b] (causalForward), CDK_BLOCK_ACTIVE -> active[b]
+ * (prefixBlockForward), CDK_BLOCK_ALL (probes), CDK_BLOCK_VALID -> valid[b][j]
+ * like the cache keys (causal- / prefixIncremental, whose new key the caller
+ * marks first, as the reference does).  full_mask
+ * (u8 [B][S_new][ldf], non-zero = attend) overrides all of it (prefixForward's
+ * explicit mask).  active / num_real may be NULL (all).  A query with no valid
+ * key gets zeros (the reference's all -1e9 row averages every key; such rows
+ * belong to inactive sequences and are never read).  Requires len + S_new <=
+ * max_len; a violation sets the index error bit and clamps.
+ *
+ * cdk_decode_mark: keys [base, base + count) become valid where active[b] and
+ * offset < num_real[b] (NULL = all), base = start (>= 0) or len (start < 0);
+ * then len += advance.  One block, stream-ordered with the step's kernels.
+ *
+ * cdk_decode_slots: slot[t] = override_mask[t] ? t : -1 (the Fourier override
+ * rows for cdk_embed_fwd, backbone_causal.py:105-109). */
+enum { CDK_BLOCK_CAUSAL = 0, CDK_BLOCK_ACTIVE = 1, CDK_BLOCK_ALL = 2, CDK_BLOCK_VALID = 3 };
+int cdk_kv_append(const void* qkv, int64_t ldq, int qkv_f32, const int32_t* pos, const float* rope, int64_t rope_len,
+                  int64_t B, int64_t S_new, int64_t H, void* k_cache, void* v_cache, int64_t max_len,
+                  const int32_t* len_dev, void* q_out, int64_t ldo, void* stream);
+int cdk_decode_attn(const void* q, int64_t ldq, const void* k_cache, const void* v_cache, int64_t max_len,
+                    const int32_t* len_dev, int64_t S_new, int64_t B, int64_t H, const uint8_t* valid, int64_t ldv,
+                    int block_mode, const uint8_t* active, const int64_t* num_real, const uint8_t* full_mask,
+                    int64_t ldf, void* out, int64_t ldo, float scale, void* stream);
+int cdk_decode_mark(void* valid, int64_t ldv, int64_t B, int64_t start, int64_t count, int64_t advance,
+                    int32_t* len_dev, const uint8_t* active, const int64_t* num_real, int64_t max_len, void* stream);
+int cdk_decode_slots(const uint8_t* override_mask, int64_t n, int32_t* slot, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

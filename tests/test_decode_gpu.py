@@ -1,0 +1,140 @@
+"""KV-cache inference on the GPU (chessdecoder_b200.decode.BatchedBackbone,
+csrc/decode.cu) against the reference's exported module (golden fixture) and
+against the oracle at the full model size.
+
+Tolerance: the caches, the GEMM inputs and the attention output are bf16 (the
+reference runs fp16), so hidden states agree to a relative Frobenius error of
+2e-2 (2 layers) / 3e-2 (12 layers) and a per-row cosine of 0.999 / 0.998."""
+import numpy as np
+import pytest
+import torch
+
+from chessdecoder_b200 import decode as D
+from chessdecoder_b200 import kernels as K
+from chessdecoder_b200.engine import ModelConfig, init_reference_weights
+from oracle import decode as OD
+
+from test_decode_cpu import G, golden_weights
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(h, ref, rel_tol, cos_tol, what):
+    h = h.detach().float().cpu().reshape(-1, h.shape[-1])
+    ref = torch.as_tensor(ref).float().reshape(-1, h.shape[-1])
+    rel = ((h - ref).norm() / ref.norm()).item()
+    cos = torch.nn.functional.cosine_similarity(h, ref, dim=1).min().item()
+    assert rel < rel_tol and cos > cos_tol, (what, rel, cos)
+
+
+def _sd(cfg, named, seed=0):
+    sd = init_reference_weights(cfg, seed)
+    for k, v in named.items():
+        sd[k] = torch.as_tensor(np.asarray(v, np.float32)).reshape(sd[k].shape)
+    return sd
+
+
+def test_decode_matches_reference_golden():
+    w, gc = golden_weights()
+    cfg = ModelConfig(vocab_size=gc["vocab_size"], embed_dim=gc["embed_dim"], num_heads=gc["num_heads"],
+                      num_layers=gc["num_layers"], max_seq_len=gc["max_seq_len"], d_ff=gc["d_ff"],
+                      num_fourier_freq=gc["num_fourier_freq"])
+    bb = D.BatchedBackbone(cfg, batch_size=G["batch"], max_seq_len=gc["max_seq_len"], state_dict=_sd(cfg, w))
+    K.get_error()
+    for call in G["calls"]:
+        h = getattr(bb, call["method"])(**call["inputs"])
+        _check(h, call["hidden"], 2e-2, 0.999, call["method"])
+    assert bb.causal_len == 8 + 3 and bb.prefix_len == 10 + 4 + 1
+    assert K.get_error() == 0
+
+
+def _full_scenario(rng, B, V):
+    ids = lambda S: torch.from_numpy(rng.integers(0, V, (B, S)))  # noqa: E731
+    calls = []
+    S0 = 20
+    num_real = torch.tensor([20, 17, 20, 12])
+    om = torch.zeros(B, S0, dtype=torch.bool)
+    om[1, 4] = om[3, 9] = True
+    ov = torch.zeros(B, S0)
+    ov[1, 4], ov[3, 9] = 0.6, -0.3
+    calls.append(("causal_forward", dict(ids=ids(S0), pos=torch.arange(S0).repeat(B, 1), ov=ov, om=om,
+                                         active=torch.ones(B, dtype=torch.bool), num_real=num_real)))
+    pos = num_real.clone()
+    for k in range(12):
+        act = torch.from_numpy(rng.random(B) > 0.25)
+        om1 = torch.zeros(B, 1, dtype=torch.bool)
+        ov1 = torch.zeros(B, 1)
+        if k % 4 == 1:
+            om1[k % B, 0], ov1[k % B, 0] = True, float(rng.uniform(-1, 1))
+        calls.append(("causal_incremental", dict(ids=ids(1), pos=pos[:, None].clone(), ov=ov1, om=om1, active=act)))
+        pos = pos + act.long()
+    calls.append(("causal_probe", dict(ids=ids(3), pos=torch.stack([pos, pos + 1, pos + 2], 1), ov=torch.zeros(B, 3),
+                                       om=torch.zeros(B, 3, dtype=torch.bool))))
+    S1 = 24
+    blk = torch.from_numpy(np.repeat(np.arange(6), 4))
+    m = torch.where(blk[None, :] <= blk[:, None], 0.0, -1e9).expand(B, 1, S1, S1).clone()
+    calls.append(("prefix_forward", dict(ids=ids(S1), pos=torch.arange(S1).repeat(B, 1), mask=m, ov=torch.zeros(B, S1),
+                                         om=torch.zeros(B, S1, dtype=torch.bool),
+                                         active=torch.tensor([True, True, False, True]))))
+    calls.append(("prefix_block_forward", dict(ids=ids(5), pos=torch.arange(S1, S1 + 5).repeat(B, 1),
+                                               ov=torch.zeros(B, 5), om=torch.zeros(B, 5, dtype=torch.bool),
+                                               active=torch.tensor([True, False, True, True]))))
+    for k in range(3):
+        calls.append(("prefix_incremental", dict(ids=ids(1), pos=torch.full((B, 1), S1 + 5 + k), ov=torch.zeros(B, 1),
+                                                 om=torch.zeros(B, 1, dtype=torch.bool),
+                                                 active=torch.tensor([True, True, k != 1, True]))))
+    calls.append(("prefix_probe", dict(ids=ids(2), pos=torch.full((B, 2), S1 + 8), ov=torch.zeros(B, 2),
+                                       om=torch.zeros(B, 2, dtype=torch.bool))))
+    return calls
+
+
+def test_decode_full_size_matches_oracle():
+    """E=1024, 16 heads, 12 layers; q / k weights scaled by 4 so that the
+    attention is far from uniform and the masks matter."""
+    cfg = ModelConfig()
+    B, max_len = 4, 96
+    sd = init_reference_weights(cfg, 5)
+    for i in range(cfg.num_layers):
+        for n in ("q_proj", "k_proj"):
+            sd[f"layers.{i}.attn.{n}.weight"] = sd[f"layers.{i}.attn.{n}.weight"] * 4.0
+    bb = D.BatchedBackbone(cfg, batch_size=B, max_seq_len=max_len, state_dict=sd)
+    w = {k: v.float().numpy() for k, v in sd.items()}
+    ob = OD.Batched(w, dict(num_layers=cfg.num_layers, num_heads=cfg.num_heads, embed_dim=cfg.embed_dim,
+                            max_seq_len=cfg.max_seq_len), B, max_len)
+    K.get_error()
+    for name, kw in _full_scenario(np.random.default_rng(2), B, cfg.vocab_size):
+        h = getattr(bb, name)(**kw)
+        ref = getattr(ob, name)(**{k: v.numpy() for k, v in kw.items()})
+        _check(h, ref, 3e-2, 0.998, name)
+    assert (bb.causal_len, bb.prefix_len) == (ob.causal_len, ob.prefix_len)
+    assert K.get_error() == 0
+
+
+def test_premarked_keys_and_cache_limit():
+    """markCausalValidRange ahead of an incremental step keeps a pre-marked key
+    valid for an inactive sequence (the reference's masked_fill only sets
+    zeros); a step past the cache capacity is rejected on the host."""
+    cfg = ModelConfig(num_layers=2)
+    B, max_len = 2, 8
+    sd = init_reference_weights(cfg, 1)
+    bb = D.BatchedBackbone(cfg, batch_size=B, max_seq_len=max_len, state_dict=sd)
+    w = {k: v.float().numpy() for k, v in sd.items()}
+    ob = OD.Batched(w, dict(num_layers=2, num_heads=cfg.num_heads, embed_dim=cfg.embed_dim,
+                            max_seq_len=cfg.max_seq_len), B, max_len)
+    rng = np.random.default_rng(0)
+    S0 = 6
+    kw = dict(ids=torch.from_numpy(rng.integers(0, cfg.vocab_size, (B, S0))), pos=torch.arange(S0).repeat(B, 1),
+              ov=torch.zeros(B, S0), om=torch.zeros(B, S0, dtype=torch.bool), active=torch.ones(B, dtype=torch.bool),
+              num_real=torch.tensor([6, 6]))
+    _check(bb.causal_forward(**kw), ob.causal_forward(**{k: v.numpy() for k, v in kw.items()}), 3e-2, 0.998, "fwd")
+    both = torch.ones(B, dtype=torch.bool)
+    bb.mark_causal_valid_range(S0, 1, both)
+    ob.cbuf[both.numpy(), S0] = 0.0
+    kw = dict(ids=torch.from_numpy(rng.integers(0, cfg.vocab_size, (B, 1))), pos=torch.full((B, 1), S0),
+              ov=torch.zeros(B, 1), om=torch.zeros(B, 1, dtype=torch.bool), active=torch.tensor([True, False]))
+    _check(bb.causal_incremental(**kw), ob.causal_incremental(**{k: v.numpy() for k, v in kw.items()}), 3e-2, 0.998,
+           "incremental after pre-mark")
+    kw["ids"] = torch.zeros(B, 2, dtype=torch.long)
+    with pytest.raises(ValueError):
+        bb.causal_probe(ids=kw["ids"], pos=torch.zeros(B, 2, dtype=torch.long), ov=None, om=None)
+    assert K.get_error() == 0
