@@ -56,8 +56,12 @@ def parse():
     ap.add_argument("--grpo", action="store_true",
                     help="GRPO policy-gradient step (chessdecoder/rl): prefix pass, thinking / final move heads, "
                          "clipped ratio + KL loss, S=4096, mini-batch 4")
+    ap.add_argument("--decode", action="store_true",
+                    help="KV-cache inference (chessdecoder/cpp/decoder BatchedBackbone): causal prefill of --seq "
+                         "tokens (default 512) for --batch sequences (default 64), then timed incremental steps")
     ap.add_argument("--seq", type=int, default=None,
-                    help="sequence length (default 256; 4096 with --moe / --finetune / --grpo)")
+                    help="sequence length (default 256; 4096 with --moe / --finetune / --grpo; 512 prefill with "
+                         "--decode)")
     ap.add_argument("--layers", type=int, default=12)
     ap.add_argument("--pool", type=int, default=4, help="distinct synthetic batches per rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -258,14 +262,147 @@ def run_grpo(args, rank, world):
                       "gpu_launches": K.LAUNCHES[0] // args.steps, "loss": float(loss)}))
 
 
+def run_decode(args, rank, world):
+    """KV-cache inference: one step = one new token for every sequence of the
+    batch through the 12 layers (causal_incremental, replayed from a CUDA
+    graph).  Device time over the timed steps; e2e adds, per step, the copy of
+    the step's token ids from pinned host memory and the read-back of the final
+    hidden states.  Replicas only: each rank decodes its own batch."""
+    import numpy as np
+    from chessdecoder_b200 import kernels as K
+    from chessdecoder_b200.decode import BatchedBackbone
+    from chessdecoder_b200.engine import ModelConfig
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, ctx = args.batch, args.seq
+    n_new = args.warmup + 2 * args.steps + 2
+    max_len = ctx + n_new
+    cfg = ModelConfig(num_layers=args.layers, max_seq_len=max(256, max_len))
+    bb = BatchedBackbone(cfg, batch_size=B, max_seq_len=max_len, device=dev)
+    g = torch.Generator().manual_seed(7)
+    ids = torch.randint(0, cfg.vocab_size, (B, ctx), generator=g)
+    bb.causal_forward(ids, torch.arange(ctx).repeat(B, 1), None, None, None, torch.full((B,), ctx))
+    toks = torch.randint(0, cfg.vocab_size, (n_new, B, 1), generator=g)
+    toks_dev = toks.to(dev)
+    pos = (ctx + torch.arange(n_new)).view(n_new, 1, 1).expand(n_new, B, 1).contiguous()
+    pos_dev = pos.to(dev)
+    act = torch.ones(B, dtype=torch.bool, device=dev)
+    k = 0
+    for _ in range(args.warmup):
+        bb.causal_incremental(toks_dev[k], pos_dev[k], None, None, act)
+        k += 1
+    torch.cuda.synchronize()
+    clocks = ClockSampler(0)
+    clocks.start()
+    K.LAUNCHES[0] = 0
+    len0 = bb.causal_len
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        bb.causal_incremental(toks_dev[k], pos_dev[k], None, None, act)
+        k += 1
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    launches = K.LAUNCHES[0] // args.steps
+    # e2e: token ids from pinned host memory in, final hidden states out, every step
+    ids_h = toks.pin_memory()
+    pos_h = pos.pin_memory()
+    out_h = torch.empty(B, cfg.embed_dim, pin_memory=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        h = bb.causal_incremental(ids_h[k], pos_h[k], None, None, act)
+        out_h.copy_(h[:, 0], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        k += 1
+    e2e_ms = (time.perf_counter() - t0) * 1000.0 / args.steps
+    clk = clocks.stop()
+    # the dominant kernel alone: decode attention over one layer's cache at the final length
+    q = torch.randn(B, cfg.embed_dim, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    c = bb.causal
+    for _ in range(3):
+        K.decode_attn(q, c.k[0], c.v[0], c.len_dev, 1, B, cfg.num_heads, c.valid, out, block_mode=K.BLOCK_VALID)
+    torch.cuda.synchronize()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    n_a = 50
+    for _ in range(n_a):
+        K.decode_attn(q, c.k[0], c.v[0], c.len_dev, 1, B, cfg.num_heads, c.valid, out, block_mode=K.BLOCK_VALID)
+    a1.record()
+    torch.cuda.synchronize()
+    attn_us = a0.elapsed_time(a1) * 1000.0 / n_a
+    err = K.get_error()
+    if err:
+        raise SystemExit(f"device error flag {err} after the decode run")
+    keys = c.len + 1
+    attn_bytes = B * cfg.num_heads * keys * 64 * 2 * 2
+    hbm = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("hbm_gbs") if (
+        ROOT / "MEASURED_PEAKS.json").exists() else None
+    peak = hbm or 6650.0
+    mid = len0 + args.steps / 2.0
+    E, F, L = cfg.embed_dim, cfg.ff, cfg.num_layers
+    step_bytes = L * (4 * E * E + 3 * E * F) * 2 + L * B * cfg.num_heads * (mid + 1) * 64 * 2 * 2
+    line = {"metric": "decode tokens/s", "value": B / (ms / 1000.0), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic token ids; random-init weights",
+            "config": {"workload": "ChessDecoder KV-cache incremental decode (causal cache, one token per sequence "
+                                   "per step, CUDA-graph replay), E=1024 H=16 L=%d d_ff=1536" % L,
+                       "batch": B, "prefill": ctx, "cache_keys_mid": mid, "parallelism": "replicas",
+                       "l2": "KV cache (%.2f GB) and weights larger than L2" % (L * B * cfg.num_heads * mid * 256
+                                                                             / 1e9)},
+            "e2e": {"value": B / (e2e_ms / 1000.0), "unit": "tokens/s", "h2d_bytes_per_step": B * 8 * 2,
+                    "d2h_bytes_per_step": B * E * 4},
+            "roofline": {"bound": "hbm", "kernel": "decode_attn_1q", "achieved": attn_bytes / attn_us / 1e3,
+                         "peak": peak, "unit": "GB/s", "frac": attn_bytes / attn_us / 1e3 / peak,
+                         "launch_us": attn_us, "bytes_per_launch": attn_bytes, "traffic": None,
+                         "peak_kind": "measured" if hbm else "fallback",
+                         "step_hbm_gbs": step_bytes / (ms / 1000.0) / 1e9},
+            "gpu_launches": launches}
+    if clk:
+        line["clocks"] = clk
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = decode_cpu_baseline(cfg, ctx)
+    print(json.dumps(line))
+
+
+def decode_cpu_baseline(cfg, ctx, reps=5):
+    """The oracle (numpy fp32 restatement of the exported KV-cache module) on
+    the host: one incremental token of one sequence over a ctx-key cache."""
+    import numpy as np
+    from chessdecoder_b200.engine import init_reference_weights
+    from oracle import decode as OD
+    sd = init_reference_weights(cfg, 0)
+    w = {k: v.float().numpy() for k, v in sd.items()}
+    c = dict(num_layers=cfg.num_layers, num_heads=cfg.num_heads, embed_dim=cfg.embed_dim)
+    rng = np.random.default_rng(0)
+    pk = rng.standard_normal((cfg.num_layers, 1, cfg.num_heads, ctx, 64)).astype(np.float32)
+    pv = rng.standard_normal(pk.shape).astype(np.float32)
+    rope = OD.rope_table(ctx + 1, 64)
+    args = (np.array([[5]]), np.array([[ctx]]), np.zeros((1, 1, 1, ctx + 1), np.float32), pk, pv,
+            np.zeros((1, 1), np.float32), np.zeros((1, 1), bool), rope)
+    OD.forward(w, c, *args)
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        OD.forward(w, c, *args)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": 1.0 / t, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"one incremental token of one sequence over a {ctx}-key cache (numpy fp32 oracle of "
+                      f"the exported module), median of {reps}"}
+
+
 def main():
     args = parse()
     if args.batch is None:
         args.batch = 128 if args.fp8 else 16 if args.moe else 4 if (args.finetune or args.grpo) else 64
     if args.seq is None:
-        args.seq = 4096 if (args.moe or args.finetune or args.grpo) else 256
-    if args.moe + args.fp8 + args.finetune + args.grpo > 1:
-        raise SystemExit("--moe, --fp8, --finetune and --grpo are separate variants")
+        args.seq = 4096 if (args.moe or args.finetune or args.grpo) else 512 if args.decode else 256
+    if args.moe + args.fp8 + args.finetune + args.grpo + args.decode > 1:
+        raise SystemExit("--moe, --fp8, --finetune, --grpo and --decode are separate variants")
     from chessdecoder_b200.distributed import setup_distributed, cleanup_distributed
     rank, local_rank, world = setup_distributed() if args.gpus > 1 or "RANK" in os.environ else (0, 0, 1)
     if args.impl == "reference":
@@ -274,6 +411,10 @@ def main():
         return
     if args.grpo:
         run_grpo(args, rank, world)
+        cleanup_distributed()
+        return
+    if args.decode:
+        run_decode(args, rank, world)
         cleanup_distributed()
         return
     import torch.distributed as dist

@@ -39,7 +39,7 @@ namespace {
 
 constexpr int kHD = 64;      // head dim (embed 1024 / 16 heads)
 constexpr int kQC = 8;       // queries per CTA
-constexpr int kWarps = 8;    // warps per CTA; each walks its own key tiles
+constexpr int kWarps = 4;    // warps per CTA; each walks its own key tiles
 constexpr int kKT = 32;      // keys per warp tile: one key per lane
 
 __device__ __forceinline__ float2 bf2f(uint32_t w) {
@@ -103,8 +103,6 @@ __global__ void kv_append_kernel(const void* __restrict__ qkv, long long ldq, in
 struct DecodeAttnArgs {
   const __nv_bfloat16* q;
   long long ldq;
-  const __nv_bfloat16* kc;
-  const __nv_bfloat16* vc;
   long long max_len;
   const int32_t* len_dev;  // cache keys [0, *len_dev) precede the new block
   int S_new;
@@ -121,15 +119,37 @@ struct DecodeAttnArgs {
   float scale_log2;        // softmax scale * log2(e)
 };
 
+constexpr int kStages = 3;                      // per-warp ring of key tiles
+constexpr int kTileBytes = kKT * kHD * 2;       // 4 KB: 32 key rows of 128 bytes
+constexpr int kStageBytes = 2 * kTileBytes;     // K tile + V tile
+constexpr int kRingBytes = kWarps * kStages * kStageBytes;
+constexpr int kQBytes = kQC * kHD * 4;
+constexpr int kSmemBytes = kRingBytes + kQBytes + 4 * kWarps * 32 * 4 + kWarps * kStages * 8 + 16 + 1024;
+static_assert(kWarps * kQC * 32 * 8 <= kRingBytes, "merge area fits in the ring");
+
+// 16-byte chunk c of row r of a 128B-swizzled tile (rows of 128 bytes in a
+// 1024-byte-aligned buffer): the TMA SWIZZLE_128B placement.
+__device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
 // Grid (ceil(S_new / kQC), H, B), kWarps warps.  Warp w walks key tiles
-// w, w + kWarps, ...; lane l holds key (tile * 32 + l) in registers for the
-// scores, the tile's V rows sit in shared memory for the weighted sum (lane l
-// owns output dims 2l, 2l + 1).  Online softmax per query and warp, merged
-// across warps at the end.  A query with no valid key writes zeros.
-__global__ void __launch_bounds__(kWarps * 32, 2) decode_attn_kernel(const DecodeAttnArgs a) {
-  __shared__ float qs[kQC][kHD];
-  __shared__ __align__(16) uint32_t vbuf[kWarps][kKT][kHD / 2];  // also the merge area after the loop
-  __shared__ float cm[kWarps][kQC], cl[kWarps][kQC];
+// w, w + kWarps, ... of 32 keys; its lane 0 keeps kStages - 1 tiles of K and V
+// in flight by TMA (2-D tiles of the cache viewed as [B*H*max_len, 64] bf16,
+// 128-byte swizzle).  Lane l scores key (tile * 32 + l) from its swizzled K row
+// (conflict-free 16-byte reads; the fp32 query row is a broadcast), the
+// weighted sum reads V row by row (lane l owns output dims 2l, 2l + 1).  Online
+// softmax per query and warp, merged across warps at the end.  A query with no
+// valid key writes zeros.
+__global__ void __launch_bounds__(kWarps * 32, 2)
+    decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                       const DecodeAttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  float (*qs)[kHD] = reinterpret_cast<float (*)[kHD]>(smem + kRingBytes);
+  float* cm = reinterpret_cast<float*>(smem + kRingBytes + kQBytes);
+  float* cl = cm + kWarps * kQC;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(cl + kWarps * kQC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kWarps * kStages);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int q0 = blockIdx.x * kQC;
@@ -142,7 +162,22 @@ __global__ void __launch_bounds__(kWarps * 32, 2) decode_attn_kernel(const Decod
     n_cache = max(0, min(n_cache, (int)a.max_len - a.S_new));
   }
   const int total = n_cache + a.S_new;
+  const int row_base = (int)((b * a.H + h) * a.max_len);
+  uint64_t* wbar = bars + warp * kStages;
+  uint8_t* wring = ring + warp * kStages * kStageBytes;
+  const int n_tiles = total > warp * kKT ? (total - warp * kKT + kWarps * kKT - 1) / (kWarps * kKT) : 0;
 
+  if (tid == 0) *abort_flag = 0;
+  if (lane == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&wbar[s], 1);
+    fence_mbar_init();
+    for (int k = 0; k < kStages - 1 && k < n_tiles; ++k) {
+      const int t0 = (warp + k * kWarps) * kKT;
+      mbar_arrive_expect_tx(&wbar[k], kStageBytes);
+      tma_load_2d(wring + k * kStageBytes, &kmap, &wbar[k], 0, row_base + t0);
+      tma_load_2d(wring + k * kStageBytes + kTileBytes, &vmap, &wbar[k], 0, row_base + t0);
+    }
+  }
   for (int i = tid; i < kQC * kHD; i += blockDim.x) {
     const int q = i / kHD, d = i % kHD;
     float v = 0.f;
@@ -153,8 +188,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) decode_attn_kernel(const Decod
 
   const bool act = a.active == nullptr || a.active[b] != 0;
   const long long nreal = a.num_real ? a.num_real[b] : (long long)a.S_new;
-  const __nv_bfloat16* kbase = a.kc + (b * a.H + h) * a.max_len * kHD;
-  const __nv_bfloat16* vbase = a.vc + (b * a.H + h) * a.max_len * kHD;
+  const bool use_valid_new = a.block_mode == CDK_BLOCK_VALID;
 
   float m[kQC], l[kQC];
   float2 acc[kQC];
@@ -164,32 +198,34 @@ __global__ void __launch_bounds__(kWarps * 32, 2) decode_attn_kernel(const Decod
     l[q] = 0.f;
     acc[q] = make_float2(0.f, 0.f);
   }
-  uint32_t (*vs)[kHD / 2] = vbuf[warp];
+  // validity byte of this lane's key, one tile ahead
+  auto valid_of = [&](int j) -> uint8_t {
+    return (j < total && (j < n_cache || use_valid_new)) ? a.valid[b * a.ldv + j] : (uint8_t)0;
+  };
+  uint8_t vcur = n_tiles > 0 ? valid_of(warp * kKT + lane) : 0;
 
-  for (int t0 = warp * kKT; t0 < total; t0 += kWarps * kKT) {
+  for (int k = 0; k < n_tiles; ++k) {
+    const int t0 = (warp + k * kWarps) * kKT;
+    const int st = k % kStages;
+    mbar_wait(&wbar[st], (uint32_t)((k / kStages) & 1), abort_flag);
+    if (lane == 0 && k + kStages - 1 < n_tiles) {
+      // the stage refilled here was read in iteration k - 1 (finished at its __syncwarp)
+      const int kn = k + kStages - 1, sn = kn % kStages;
+      const int tn = (warp + kn * kWarps) * kKT;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive_expect_tx(&wbar[sn], kStageBytes);
+      tma_load_2d(wring + sn * kStageBytes, &kmap, &wbar[sn], 0, row_base + tn);
+      tma_load_2d(wring + sn * kStageBytes + kTileBytes, &vmap, &wbar[sn], 0, row_base + tn);
+    }
+    const uint8_t vnext = k + 1 < n_tiles ? valid_of(t0 + kWarps * kKT + lane) : 0;
+    const uint8_t* kt = wring + st * kStageBytes;
+    const uint8_t* vt = kt + kTileBytes;
     const int j = t0 + lane;
-    uint4 kr[8];
-    if (j < total) {
-      const uint4* src = reinterpret_cast<const uint4*>(kbase + (long long)j * kHD);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) kr[c] = src[c];
-    } else {
-#pragma unroll
-      for (int c = 0; c < 8; ++c) kr[c] = make_uint4(0u, 0u, 0u, 0u);
-    }
-    // V tile: 4 rows of 8 x 16 bytes per instruction, coalesced.
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = (lane >> 3) + 4 * i, c = lane & 7;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (t0 + r < total) v = reinterpret_cast<const uint4*>(vbase + (long long)(t0 + r) * kHD)[c];
-      *reinterpret_cast<uint4*>(&vs[r][c * 4]) = v;
-    }
-    // Key validity shared by all queries (cache part) or per query (new block).
     const bool in_cache = j < n_cache;
-    const bool cache_ok = j < total && (in_cache || a.block_mode == CDK_BLOCK_VALID) && a.valid[b * a.ldv + j] != 0;
     const int jt = j - n_cache;  // index within the new block
-    __syncwarp();
+    uint4 kr[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) kr[c] = *reinterpret_cast<const uint4*>(kt + swz(lane, c));
 
     float p[kQC];
 #pragma unroll
@@ -201,12 +237,14 @@ __global__ void __launch_bounds__(kWarps * 32, 2) decode_attn_kernel(const Decod
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const uint32_t w[4] = {kr[c].x, kr[c].y, kr[c].z, kr[c].w};
+          const float4 qa = *reinterpret_cast<const float4*>(qq + c * 8);
+          const float4 qb = *reinterpret_cast<const float4*>(qq + c * 8 + 4);
+          const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 kf = bf2f(w[e]);
-            const float2 qf = *reinterpret_cast<const float2*>(qq + c * 8 + e * 2);
-            s = fmaf(qf.x, kf.x, s);
-            s = fmaf(qf.y, kf.y, s);
+            s = fmaf(qv[2 * e], kf.x, s);
+            s = fmaf(qv[2 * e + 1], kf.y, s);
           }
         }
         bool ok;
@@ -214,8 +252,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) decode_attn_kernel(const Decod
           ok = false;
         } else if (a.full) {
           ok = j < a.ldf && a.full[(b * a.S_new + q0 + q) * a.ldf + j] != 0;
-        } else if (in_cache || a.block_mode == CDK_BLOCK_VALID) {
-          ok = cache_ok;
+        } else if (in_cache || use_valid_new) {
+          ok = vcur != 0;
         } else if (a.block_mode == CDK_BLOCK_CAUSAL) {
           ok = jt <= q0 + q && jt < nreal;
         } else if (a.block_mode == CDK_BLOCK_ACTIVE) {
@@ -242,31 +280,41 @@ __global__ void __launch_bounds__(kWarps * 32, 2) decode_attn_kernel(const Decod
         }
       }
     }
-#pragma unroll 4
-    for (int jj = 0; jj < kKT; ++jj) {
-      const float2 v = bf2f(vs[jj][lane]);
+    const int nk = min(kKT, total - t0);  // rows past the sequence's keys are never read
+    if (nq == 1) {
+      for (int jj = 0; jj < nk; ++jj) {
+        const float2 v = bf2f(*reinterpret_cast<const uint32_t*>(vt + swz(jj, lane >> 2) + (lane & 3) * 4));
+        const float pj = __shfl_sync(0xffffffffu, p[0], jj);
+        acc[0].x = fmaf(pj, v.x, acc[0].x);
+        acc[0].y = fmaf(pj, v.y, acc[0].y);
+      }
+    } else {
+      for (int jj = 0; jj < nk; ++jj) {
+        const float2 v = bf2f(*reinterpret_cast<const uint32_t*>(vt + swz(jj, lane >> 2) + (lane & 3) * 4));
 #pragma unroll
-      for (int q = 0; q < kQC; ++q) {
-        if (q < nq) {
-          const float pj = __shfl_sync(0xffffffffu, p[q], jj);
-          acc[q].x = fmaf(pj, v.x, acc[q].x);
-          acc[q].y = fmaf(pj, v.y, acc[q].y);
+        for (int q = 0; q < kQC; ++q) {
+          if (q < nq) {
+            const float pj = __shfl_sync(0xffffffffu, p[q], jj);
+            acc[q].x = fmaf(pj, v.x, acc[q].x);
+            acc[q].y = fmaf(pj, v.y, acc[q].y);
+          }
         }
       }
     }
+    vcur = vnext;
     __syncwarp();
   }
 
-  // Merge the warps' partial softmax states.
+  // Merge the warps' partial softmax states (every issued tile was waited for,
+  // so the ring is free).
   __syncthreads();
-  float2 (*cacc)[kQC][32] = reinterpret_cast<float2 (*)[kQC][32]>(&vbuf[0][0][0]);
-  static_assert(sizeof(float2) * kWarps * kQC * 32 <= sizeof(vbuf), "merge area");
+  float2 (*cacc)[kQC][32] = reinterpret_cast<float2 (*)[kQC][32]>(ring);
 #pragma unroll
   for (int q = 0; q < kQC; ++q) {
     cacc[warp][q][lane] = acc[q];
     if (lane == 0) {
-      cm[warp][q] = m[q];
-      cl[warp][q] = l[q];
+      cm[warp * kQC + q] = m[q];
+      cl[warp * kQC + q] = l[q];
     }
   }
   __syncthreads();
@@ -275,19 +323,203 @@ __global__ void __launch_bounds__(kWarps * 32, 2) decode_attn_kernel(const Decod
     if (q >= nq) continue;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, cm[w][q]);
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, cm[w * kQC + q]);
     float L = 0.f, ox = 0.f, oy = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) {
-        const float f = exp2f(cm[w][q] - M);
-        L += cl[w][q] * f;
+        const float f = exp2f(cm[w * kQC + q] - M);
+        L += cl[w * kQC + q] * f;
         ox += cacc[w][q][d2].x * f;
         oy += cacc[w][q][d2].y * f;
       }
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
     *reinterpret_cast<uint32_t*>(a.out + (b * a.S_new + q0 + q) * a.ldo + h * kHD + 2 * d2) = f2bf2(ox * inv, oy * inv);
+  }
+}
+
+// One query per (sequence, head): the incremental step.  Grid (H, B),
+// kWarps warps, the same per-warp TMA ring of K / V tiles as decode_attn_kernel.
+// Lane l owns key (tile * 32 + l): it scores it from its swizzled K row and, if
+// the key is valid, folds it into its own online-softmax state (max, sum and a
+// 64-wide fp32 accumulator from its swizzled V row), so the loop has no
+// cross-lane traffic.  The 32 x kWarps lane states are merged once at the end.
+__global__ void __launch_bounds__(kWarps * 32, 2)
+    decode_attn_1q_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                          const DecodeAttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  float* qs = reinterpret_cast<float*>(smem + kRingBytes);
+  float* cm = reinterpret_cast<float*>(smem + kRingBytes + kQBytes);
+  float* cl = cm + kWarps * 32;  // kWarps * 32 * 3 floats
+  uint64_t* bars = reinterpret_cast<uint64_t*>(cm + 4 * kWarps * 32);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kWarps * kStages);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int h = blockIdx.x;
+  const long long b = blockIdx.y;
+  int n_cache = *a.len_dev;
+  if (n_cache < 0 || (long long)n_cache + 1 > a.max_len) {
+    if (tid == 0) report_error(kErrIndex);
+    n_cache = max(0, min(n_cache, (int)a.max_len - 1));
+  }
+  const int total = n_cache + 1;
+  const int row_base = (int)((b * a.H + h) * a.max_len);
+  uint64_t* wbar = bars + warp * kStages;
+  uint8_t* wring = ring + warp * kStages * kStageBytes;
+  const int n_tiles = total > warp * kKT ? (total - warp * kKT + kWarps * kKT - 1) / (kWarps * kKT) : 0;
+
+  if (tid == 0) *abort_flag = 0;
+  if (lane == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&wbar[s], 1);
+    fence_mbar_init();
+    for (int k = 0; k < kStages - 1 && k < n_tiles; ++k) {
+      const int t0 = (warp + k * kWarps) * kKT;
+      mbar_arrive_expect_tx(&wbar[k], kStageBytes);
+      tma_load_2d(wring + k * kStageBytes, &kmap, &wbar[k], 0, row_base + t0);
+      tma_load_2d(wring + k * kStageBytes + kTileBytes, &vmap, &wbar[k], 0, row_base + t0);
+    }
+  }
+  if (tid < kHD) qs[tid] = __bfloat162float(a.q[b * a.ldq + h * kHD + tid]) * a.scale_log2;
+  __syncthreads();
+
+  const bool act = a.active == nullptr || a.active[b] != 0;
+  const long long nreal = a.num_real ? a.num_real[b] : 1;
+  auto key_ok = [&](int j) -> bool {
+    if (j >= total) return false;
+    if (a.full) return j < a.ldf && a.full[b * a.ldf + j] != 0;
+    if (j < n_cache || a.block_mode == CDK_BLOCK_VALID) return a.valid[b * a.ldv + j] != 0;
+    if (a.block_mode == CDK_BLOCK_CAUSAL) return nreal > 0;
+    if (a.block_mode == CDK_BLOCK_ACTIVE) return act;
+    return true;
+  };
+
+  float m = -INFINITY, l = 0.f;
+  float acc[kHD];
+#pragma unroll
+  for (int d = 0; d < kHD; ++d) acc[d] = 0.f;
+  bool ok_cur = n_tiles > 0 && key_ok(warp * kKT + lane);
+
+  for (int k = 0; k < n_tiles; ++k) {
+    const int t0 = (warp + k * kWarps) * kKT;
+    const int st = k % kStages;
+    mbar_wait(&wbar[st], (uint32_t)((k / kStages) & 1), abort_flag);
+    if (lane == 0 && k + kStages - 1 < n_tiles) {
+      const int kn = k + kStages - 1, sn = kn % kStages;
+      const int tn = (warp + kn * kWarps) * kKT;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive_expect_tx(&wbar[sn], kStageBytes);
+      tma_load_2d(wring + sn * kStageBytes, &kmap, &wbar[sn], 0, row_base + tn);
+      tma_load_2d(wring + sn * kStageBytes + kTileBytes, &vmap, &wbar[sn], 0, row_base + tn);
+    }
+    const bool ok_next = k + 1 < n_tiles && key_ok(t0 + kWarps * kKT + lane);
+    const uint8_t* kt = wring + st * kStageBytes;
+    const uint8_t* vt = kt + kTileBytes;
+    if (ok_cur) {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 kc = *reinterpret_cast<const uint4*>(kt + swz(lane, c));
+        const float4 qa = *reinterpret_cast<const float4*>(qs + c * 8);
+        const float4 qb = *reinterpret_cast<const float4*>(qs + c * 8 + 4);
+        float2 f = bf2f(kc.x);
+        s0 = fmaf(qa.x, f.x, s0);
+        s1 = fmaf(qa.y, f.y, s1);
+        f = bf2f(kc.y);
+        s0 = fmaf(qa.z, f.x, s0);
+        s1 = fmaf(qa.w, f.y, s1);
+        f = bf2f(kc.z);
+        s0 = fmaf(qb.x, f.x, s0);
+        s1 = fmaf(qb.y, f.y, s1);
+        f = bf2f(kc.w);
+        s0 = fmaf(qb.z, f.x, s0);
+        s1 = fmaf(qb.w, f.y, s1);
+      }
+      const float sc = s0 + s1;
+      if (sc > m) {  // new running max for this lane: rescale its state
+        const float alpha = exp2f(m - sc);
+        l *= alpha;
+#pragma unroll
+        for (int d = 0; d < kHD; ++d) acc[d] *= alpha;
+        m = sc;
+      }
+      const float pv = exp2f(sc - m);
+      l += pv;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 vc = *reinterpret_cast<const uint4*>(vt + swz(lane, c));
+        float2 f = bf2f(vc.x);
+        acc[c * 8 + 0] = fmaf(pv, f.x, acc[c * 8 + 0]);
+        acc[c * 8 + 1] = fmaf(pv, f.y, acc[c * 8 + 1]);
+        f = bf2f(vc.y);
+        acc[c * 8 + 2] = fmaf(pv, f.x, acc[c * 8 + 2]);
+        acc[c * 8 + 3] = fmaf(pv, f.y, acc[c * 8 + 3]);
+        f = bf2f(vc.z);
+        acc[c * 8 + 4] = fmaf(pv, f.x, acc[c * 8 + 4]);
+        acc[c * 8 + 5] = fmaf(pv, f.y, acc[c * 8 + 5]);
+        f = bf2f(vc.w);
+        acc[c * 8 + 6] = fmaf(pv, f.x, acc[c * 8 + 6]);
+        acc[c * 8 + 7] = fmaf(pv, f.y, acc[c * 8 + 7]);
+      }
+    }
+    ok_cur = ok_next;
+    __syncwarp();
+  }
+
+  // Merge the kWarps * 32 lane states: every lane rescales its state to the
+  // block-wide max M, stores it row-wise into the (now idle) ring, then thread
+  // (group g, pair d2) sums 32 rows of dims 2 d2, 2 d2 + 1 and group partials
+  // are added up.
+  float wm = m;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+  __syncthreads();  // all warps are done with the ring
+  float* red = cm;  // [kWarps] warp maxima, then [kWarps][32] x (x, y, L) partials
+  if (lane == 0) red[warp] = wm;
+  __syncthreads();
+  float M = red[0];
+#pragma unroll
+  for (int w = 1; w < kWarps; ++w) M = fmaxf(M, red[w]);
+  const float f = (m == -INFINITY) ? 0.f : exp2f(m - M);
+  float* st_acc = reinterpret_cast<float*>(ring);
+  static_assert(kWarps * 32 * (kHD + 1) * 4 <= kRingBytes, "lane states fit in the ring");
+  float* st_l = st_acc + kWarps * 32 * kHD;
+#pragma unroll
+  for (int c = 0; c < kHD / 4; ++c)
+    *reinterpret_cast<float4*>(st_acc + tid * kHD + c * 4) =
+        make_float4(acc[c * 4] * f, acc[c * 4 + 1] * f, acc[c * 4 + 2] * f, acc[c * 4 + 3] * f);
+  st_l[tid] = l * f;
+  __syncthreads();
+  {
+    const int d2 = lane, g = warp;
+    float ox = 0.f, oy = 0.f, L = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < 32; ++i) {
+      const int r = g * 32 + i;
+      const float2 v = *reinterpret_cast<const float2*>(st_acc + r * kHD + 2 * d2);
+      ox += v.x;
+      oy += v.y;
+      L += st_l[r];
+    }
+    __syncthreads();
+    float* part = cl;  // [kWarps][32][3]
+    part[(g * 32 + d2) * 3 + 0] = ox;
+    part[(g * 32 + d2) * 3 + 1] = oy;
+    part[(g * 32 + d2) * 3 + 2] = L;
+  }
+  __syncthreads();
+  if (tid < 32) {
+    float ox = 0.f, oy = 0.f, L = 0.f;
+#pragma unroll
+    for (int g = 0; g < kWarps; ++g) {
+      ox += cl[(g * 32 + tid) * 3 + 0];
+      oy += cl[(g * 32 + tid) * 3 + 1];
+      L += cl[(g * 32 + tid) * 3 + 2];
+    }
+    const float inv = (M != -INFINITY && L > 0.f) ? 1.f / L : 0.f;
+    *reinterpret_cast<uint32_t*>(a.out + b * a.ldo + h * kHD + 2 * tid) = f2bf2(ox * inv, oy * inv);
   }
 }
 
@@ -352,11 +584,14 @@ extern "C" int cdk_decode_attn(const void* q, int64_t ldq, const void* k_cache, 
   if (full_mask && ldf < 1) return -3;
   if (block_mode < CDK_BLOCK_CAUSAL || block_mode > CDK_BLOCK_VALID) return -4;
   if (!al(k_cache, 16) || !al(v_cache, 16) || !al(out, 4)) return -5;
+  if (B * H * max_len >= (1ll << 31)) return -6;
+  CUtensorMap kmap, vmap;
+  const uint64_t rows = (uint64_t)(B * H * max_len);
+  if (!make_tmap(&kmap, k_cache, kHD, rows, kHD, kHD, kKT) || !make_tmap(&vmap, v_cache, kHD, rows, kHD, kHD, kKT))
+    return -7;
   DecodeAttnArgs a;
   a.q = reinterpret_cast<const __nv_bfloat16*>(q);
   a.ldq = ldq;
-  a.kc = reinterpret_cast<const __nv_bfloat16*>(k_cache);
-  a.vc = reinterpret_cast<const __nv_bfloat16*>(v_cache);
   a.max_len = max_len;
   a.len_dev = len_dev;
   a.S_new = (int)S_new;
@@ -371,8 +606,22 @@ extern "C" int cdk_decode_attn(const void* q, int64_t ldq, const void* k_cache, 
   a.out = reinterpret_cast<__nv_bfloat16*>(out);
   a.ldo = ldo;
   a.scale_log2 = scale * 1.4426950408889634f;
-  dim3 grid((unsigned)((S_new + kQC - 1) / kQC), (unsigned)H, (unsigned)B);
-  decode_attn_kernel<<<grid, kWarps * 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return -8;
+  if (!attr_done[dev]) {
+    cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaFuncSetAttribute(decode_attn_1q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    attr_done[dev] = true;
+  }
+  if (S_new == 1) {
+    decode_attn_1q_kernel<<<dim3((unsigned)H, (unsigned)B), kWarps * 32, kSmemBytes,
+                            reinterpret_cast<cudaStream_t>(stream)>>>(kmap, vmap, a);
+  } else {
+    dim3 grid((unsigned)((S_new + kQC - 1) / kQC), (unsigned)H, (unsigned)B);
+    decode_attn_kernel<<<grid, kWarps * 32, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(kmap, vmap, a);
+  }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
 }

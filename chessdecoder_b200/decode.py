@@ -24,7 +24,9 @@ The public methods mirror BatchedBackbone (batched_backbone.hpp:17-94) with the
 same argument meaning: ids / pos [B, S] int64, override values [B, S] and mask
 [B, S] bool (Fourier injection), active [B] bool, num_real [B] int64.  They
 return the final-norm hidden state [B, S, E] (fp32; ``last_hidden16`` holds the
-bf16 copy for the heads).
+bf16 copy for the heads).  The incremental steps run from a CUDA graph after
+their first call; their outputs are then the graph's static buffers, valid
+until the next incremental step of the same cache.
 """
 from __future__ import annotations
 
@@ -40,7 +42,8 @@ HEAD_DIM = 64
 
 
 class KVCache:
-    def __init__(self, L, B, H, max_len, device):
+    def __init__(self, L, B, H, max_len, device, name="cache"):
+        self.name = name
         self.k = torch.zeros(L, B, H, max_len, HEAD_DIM, dtype=torch.bfloat16, device=device)
         self.v = torch.zeros_like(self.k)
         self.valid = torch.zeros(B, max_len, dtype=torch.uint8, device=device)
@@ -70,7 +73,8 @@ class BatchedBackbone:
     model's."""
 
     def __init__(self, cfg: Optional[ModelConfig] = None, batch_size: int = 1, max_seq_len: Optional[int] = None,
-                 state_dict=None, device="cuda", seed: int = 0, store: Optional[ParamStore] = None):
+                 state_dict=None, device="cuda", seed: int = 0, store: Optional[ParamStore] = None,
+                 use_graphs: bool = True):
         cfg = cfg or ModelConfig()
         if cfg.moe_experts:
             raise ValueError("the KV-cache backbone covers the dense model")
@@ -87,8 +91,11 @@ class BatchedBackbone:
         self.store = store
         self.rope = rope_table(max(cfg.max_seq_len, self.max_len), cfg.head_dim).to(self.device)
         L, H = cfg.num_layers, cfg.num_heads
-        self.causal = KVCache(L, self.B, H, self.max_len, self.device)
-        self.prefix = KVCache(L, self.B, H, self.max_len, self.device)
+        self.causal = KVCache(L, self.B, H, self.max_len, self.device, "causal")
+        self.prefix = KVCache(L, self.B, H, self.max_len, self.device, "prefix")
+        # incremental steps replay from CUDA graphs (first call eager, second captures)
+        self.use_graphs = bool(use_graphs) and self.device.type == "cuda"
+        self._graphs = {}
         st, E, F = store, cfg.embed_dim, cfg.ff
         self._layers = []
         for i in range(L):
@@ -264,9 +271,70 @@ class BatchedBackbone:
         B, S = ids.shape
         if S != 1:
             raise ValueError("incremental steps take one token per sequence")
+        if B != self.B:
+            raise ValueError(f"batch {B} != {self.B}")
+        if cache.len + 1 > self.max_len:
+            raise ValueError(f"cache full: {cache.len} + 1 > {self.max_len}")
+        g = self._graphs.get(cache.name) if self.use_graphs else None
+        if g is None or g == "warm":
+            if g == "warm":  # second call: capture, then replay below
+                g = self._graphs[cache.name] = _IncrementalGraph(self, cache)
+            else:
+                if self.use_graphs:  # first call runs eagerly: every lazy set-up happens outside capture
+                    self._graphs[cache.name] = "warm"
+                h = self._incremental_body(cache, ids, pos, ov, om, active)
+                cache.len += 1
+                return h
+        g.load(ids, pos, ov, om, active)
+        g.graph.replay()
+        K.LAUNCHES[0] += g.n_launch
+        cache.len += 1
+        self.last_hidden16 = g.out16
+        return g.out
+
+    def _incremental_body(self, cache, ids, pos, ov, om, active):
+        B = ids.shape[0]
         act = _u8(active, self.device)
         K.decode_mark(cache.valid, B, cache.len_dev, start=-1, count=1, active=act)
         h = self._forward(cache, ids, pos, ov, om, block_mode=K.BLOCK_VALID)
         K.decode_mark(cache.valid, B, cache.len_dev, advance=1)
-        cache.len += 1
         return h
+
+
+class _IncrementalGraph:
+    """One incremental step of a cache captured as a CUDA graph: static input
+    buffers, the whole 12-layer pass and the cache-length update replay as one
+    launch.  The step reads the cache length on the device, so the same graph
+    serves every position."""
+
+    def __init__(self, bb: BatchedBackbone, cache: KVCache):
+        dev, B = bb.device, bb.B
+        self.ids = torch.zeros(B, 1, dtype=torch.int64, device=dev)
+        self.pos = torch.zeros(B, 1, dtype=torch.int64, device=dev)
+        self.ov = torch.zeros(B, 1, device=dev)
+        self.om = torch.zeros(B, 1, dtype=torch.bool, device=dev)
+        self.active = torch.ones(B, dtype=torch.bool, device=dev)
+        self.graph = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize(dev)
+        n0 = K.LAUNCHES[0]
+        with torch.cuda.graph(self.graph):
+            self.out = bb._incremental_body(cache, self.ids, self.pos, self.ov, self.om, self.active)
+        self.n_launch = K.LAUNCHES[0] - n0  # kernels of the library in one replay
+        K.LAUNCHES[0] = n0
+        self.out16 = bb.last_hidden16
+
+    def load(self, ids, pos, ov, om, active):
+        self.ids.copy_(ids.reshape(self.ids.shape), non_blocking=True)
+        self.pos.copy_(pos.reshape(self.pos.shape), non_blocking=True)
+        if ov is None:
+            self.ov.zero_()
+        else:
+            self.ov.copy_(ov.reshape(self.ov.shape), non_blocking=True)
+        if om is None:
+            self.om.zero_()
+        else:
+            self.om.copy_(om.reshape(self.om.shape), non_blocking=True)
+        if active is None:
+            self.active.fill_(True)
+        else:
+            self.active.copy_(active.reshape(self.active.shape), non_blocking=True)
