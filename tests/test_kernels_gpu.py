@@ -250,6 +250,37 @@ def test_attention_fwd_bwd(K, attn_path, S, nseq, n_causal):
     assert K.get_error() == 0
 
 
+@pytest.mark.parametrize("S,nseq,n_causal,H", [(256, 40, 20, 16), (100, 64, 32, 8), (136, 48, 16, 8)])
+def test_attention_bwd_many_items(K, S, nseq, n_causal, H):
+    """The S <= 256 backward over more (head, sequence) items than the GPU has
+    SMs (several waves), mixed causal / block-prefix, full and partial tiles;
+    every output row written (the output starts as NaN)."""
+    E = H * 64
+    gen = torch.Generator().manual_seed(S * 3 + nseq)
+    qkv = (torch.randn(nseq * S, 3 * E, generator=gen) * 0.8).to(DEV).to(torch.bfloat16)
+    bid = make_bid(nseq - n_causal, S, gen)
+    bid32 = bid.to(torch.int32).to(DEV).contiguous()
+    meta = K.attn_meta(bid32, S)
+    out = torch.empty(nseq * S, E, device=DEV, dtype=torch.bfloat16)
+    lse = torch.empty(nseq * H * S, device=DEV)
+    K.attn_fwd(qkv, out, lse, nseq, n_causal, S, H, bid32, meta)
+    qkv_f = qkv.float().requires_grad_(True)
+    ref = ref_attention(qkv_f, nseq, n_causal, S, H, bid)
+    dout = (torch.randn(nseq * S, E, generator=gen) * 0.5).to(DEV).to(torch.bfloat16)
+    ref.backward(dout.float())
+    dqkv = torch.full_like(qkv, float("nan"))
+    dsum = torch.empty(nseq * H * S, device=DEV)
+    K.attn_bwd(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid32, meta)
+    torch.cuda.synchronize()
+    g = qkv_f.grad
+    assert torch.isfinite(dqkv.float()).all()
+    for i, name in enumerate("qkv"):
+        sl = slice(i * E, (i + 1) * E)
+        assert cosine(dqkv[:, sl], g[:, sl]) > 0.999, name
+        assert rel_err(dqkv[:, sl], g[:, sl]) < 3e-2, name
+    assert K.get_error() == 0
+
+
 def test_attention_bwd_unrope(K, attn_path):
     S, nseq, H = 128, 2, 2
     E = H * 64
