@@ -545,6 +545,22 @@ __global__ void decode_mark_kernel(uint8_t* __restrict__ valid, long long ldv, i
   }
 }
 
+// u[t, f] = silu(gu[t, f]) * gu[t, F + f] from fp32 projections (the split-K
+// form of the small-batch SwiGLU), bf16 out.  Two columns per thread.
+__global__ void swiglu_f32_kernel(const float* __restrict__ gu, long long ldg, long long T, int F,
+                                  __nv_bfloat16* __restrict__ u, long long ldu) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int half = F / 2;
+  if (i >= T * half) return;
+  const long long t = i / half;
+  const int f = (int)(i % half) * 2;
+  const float2 g = *reinterpret_cast<const float2*>(gu + t * ldg + f);
+  const float2 v = *reinterpret_cast<const float2*>(gu + t * ldg + F + f);
+  const float a = g.x / (1.f + __expf(-g.x)) * v.x;
+  const float c = g.y / (1.f + __expf(-g.y)) * v.y;
+  *reinterpret_cast<uint32_t*>(u + t * ldu + f) = f2bf2(a, c);
+}
+
 __global__ void decode_slots_kernel(const uint8_t* __restrict__ om, long long n, int32_t* __restrict__ slot) {
   const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (t < n) slot[t] = om[t] ? (int32_t)t : -1;
@@ -634,6 +650,17 @@ extern "C" int cdk_decode_mark(void* valid, int64_t ldv, int64_t B, int64_t star
   decode_mark_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<uint8_t*>(valid), ldv, (int)B, start, (int)count, (int)advance, len_dev, active, num_real,
       max_len);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+extern "C" int cdk_swiglu_f32(const float* gu, int64_t ldg, int64_t T, int64_t F, void* u, int64_t ldu,
+                              void* stream) {
+  if (T == 0) return 0;
+  if (!gu || !u || T < 0 || F <= 0 || F % 2 || ldg < 2 * F || ldg % 2 || ldu < F || ldu % 2) return -1;
+  const long long n = T * (F / 2);
+  swiglu_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      gu, ldg, T, (int)F, reinterpret_cast<__nv_bfloat16*>(u), ldu);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
 }

@@ -59,6 +59,14 @@ class KVCache:
         self.len = 0
 
 
+def _splits(M: int, N: int, K_: int, sms: int = 148) -> int:
+    """K splits for a split-K projection of M rows x N output columns over K_
+    inputs: about one wave of (128 x 256 tile, K slice) units, at least one
+    64-deep k block each."""
+    tiles = ((M + 127) // 128) * ((N + 255) // 256)
+    return max(1, min(K_ // 64, sms // tiles))
+
+
 def _u8(t, device):
     return None if t is None else t.to(device=device, dtype=torch.bool).contiguous().view(torch.uint8)
 
@@ -107,6 +115,8 @@ class BatchedBackbone:
                 w13=st.span(p + "mlp.w1.weight", p + "mlp.w3.weight").view(2 * F, E), w2=st.bf16(p + "mlp.w2.weight")))
         self._ar = {}
         self.last_hidden16 = None
+        self._sms = (torch.cuda.get_device_properties(self.device).multi_processor_count
+                     if self.device.type == "cuda" else 148)
 
     # -- lengths ------------------------------------------------------------
     @property
@@ -191,20 +201,42 @@ class BatchedBackbone:
         qkv = torch.empty(T, 3 * E, device=dev)
         q16 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
         ao = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
-        gu = torch.empty(T, 2 * F, device=dev, dtype=torch.bfloat16)
         u = torch.empty(T, F, device=dev, dtype=torch.bfloat16)
         h1 = torch.empty(T, E, device=dev)
+        # Few rows (incremental steps, small blocks): 128 x 256 output tiles
+        # would leave most SMs idle while the weights stream, so the
+        # projections run split-K, reduce-adding fp32 partial sums into a zeroed
+        # output (or into a copy of the residual); SwiGLU then runs on the sums.
+        small = T <= 512
+        if small:
+            gu32 = torch.empty(T, 2 * F, device=dev)
+        else:
+            gu = torch.empty(T, 2 * F, device=dev, dtype=torch.bfloat16)
         for i, w in enumerate(self._layers):
             K.rmsnorm_fwd(x, w["s1"], y16=n1)
-            K.gemm(n1, w["wqkv"], kind=K.EPI_STORE_F32, out=qkv)
+            if small:
+                qkv.zero_()
+                K.gemm(n1, w["wqkv"], kind=K.EPI_ATOMIC_F32, out=qkv, split_k=_splits(T, 3 * E, E, self._sms))
+            else:
+                K.gemm(n1, w["wqkv"], kind=K.EPI_STORE_F32, out=qkv)
             K.kv_append(qkv, B, S, H, cache.k[i], cache.v[i], cache.len_dev, pos=pos32, rope=self.rope, q_out=q16)
             K.decode_attn(q16, cache.k[i], cache.v[i], cache.len_dev, S, B, H, cache.valid, ao, block_mode=block_mode,
                           active=active, num_real=num_real, full_mask=full)
-            K.gemm(ao, w["wo"], kind=K.EPI_RESID_F32, out=h1, resid=x)
-            K.rmsnorm_fwd(h1, w["s2"], y16=n1)
-            K.gemm(n1, w["w13"], kind=K.EPI_SWIGLU, out=u, out2=gu, half_n=F)
             xn = torch.empty(T, E, device=dev)
-            K.gemm(u, w["w2"], kind=K.EPI_RESID_F32, out=xn, resid=h1)
+            if small:
+                h1.copy_(x)
+                K.gemm(ao, w["wo"], kind=K.EPI_ATOMIC_F32, out=h1, split_k=_splits(T, E, E, self._sms))
+                K.rmsnorm_fwd(h1, w["s2"], y16=n1)
+                gu32.zero_()
+                K.gemm(n1, w["w13"], kind=K.EPI_ATOMIC_F32, out=gu32, split_k=_splits(T, 2 * F, E, self._sms))
+                K.swiglu_f32(gu32, u)
+                xn.copy_(h1)
+                K.gemm(u, w["w2"], kind=K.EPI_ATOMIC_F32, out=xn, split_k=_splits(T, E, F, self._sms))
+            else:
+                K.gemm(ao, w["wo"], kind=K.EPI_RESID_F32, out=h1, resid=x)
+                K.rmsnorm_fwd(h1, w["s2"], y16=n1)
+                K.gemm(n1, w["w13"], kind=K.EPI_SWIGLU, out=u, out2=gu, half_n=F)
+                K.gemm(u, w["w2"], kind=K.EPI_RESID_F32, out=xn, resid=h1)
             x = xn
         h16 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
         h32 = torch.empty(T, E, device=dev)

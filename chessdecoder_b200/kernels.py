@@ -564,3 +564,12 @@ def decode_slots(override_mask_u8, slot32):
     rc = lib().cdk_decode_slots(_p(override_mask_u8), override_mask_u8.numel(), _p(slot32), _stream())
     _check(rc, "decode_slots")
     _count(1)
+
+
+@_timed("swiglu_f32")
+def swiglu_f32(gu32, u):
+    """u = silu(gate) * up from fp32 [T, 2F] (gate | up)."""
+    T, F = u.shape
+    rc = lib().cdk_swiglu_f32(_p(gu32), gu32.stride(0), T, F, _p(u), u.stride(0), _stream())
+    _check(rc, "swiglu_f32")
+    _count(1)

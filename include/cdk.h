@@ -349,6 +349,10 @@ int cdk_decode_attn(const void* q, int64_t ldq, const void* k_cache, const void*
 int cdk_decode_mark(void* valid, int64_t ldv, int64_t B, int64_t start, int64_t count, int64_t advance,
                     int32_t* len_dev, const uint8_t* active, const int64_t* num_real, int64_t max_len, void* stream);
 int cdk_decode_slots(const uint8_t* override_mask, int64_t n, int32_t* slot, void* stream);
+/* u[t, f] = silu(gu[t, f]) * gu[t, F + f], gu fp32 [T, ldg] (gate | up), u bf16
+ * [T, ldu]: the SwiGLU of a small decode batch whose gate / up projection ran as
+ * a split-K fp32 GEMM (backbone_causal.py:141-143). */
+int cdk_swiglu_f32(const float* gu, int64_t ldg, int64_t T, int64_t F, void* u, int64_t ldu, void* stream);
 
 #ifdef __cplusplus
 }

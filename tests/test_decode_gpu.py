@@ -138,3 +138,33 @@ def test_premarked_keys_and_cache_limit():
     with pytest.raises(ValueError):
         bb.causal_probe(ids=kw["ids"], pos=torch.zeros(B, 2, dtype=torch.long), ov=None, om=None)
     assert K.get_error() == 0
+
+
+def test_prefill_rows_above_split_threshold():
+    """A prefill of more than 512 rows (the fused-epilogue GEMM path) followed
+    by incremental steps (the split-K path), against the oracle."""
+    cfg = ModelConfig(num_layers=4)
+    B, max_len, S0 = 12, 64, 48
+    sd = init_reference_weights(cfg, 9)
+    for i in range(cfg.num_layers):
+        for n in ("q_proj", "k_proj"):
+            sd[f"layers.{i}.attn.{n}.weight"] = sd[f"layers.{i}.attn.{n}.weight"] * 4.0
+    bb = D.BatchedBackbone(cfg, batch_size=B, max_seq_len=max_len, state_dict=sd)
+    w = {k: v.float().numpy() for k, v in sd.items()}
+    ob = OD.Batched(w, dict(num_layers=cfg.num_layers, num_heads=cfg.num_heads, embed_dim=cfg.embed_dim,
+                            max_seq_len=cfg.max_seq_len), B, max_len)
+    rng = np.random.default_rng(4)
+    kw = dict(ids=torch.from_numpy(rng.integers(0, cfg.vocab_size, (B, S0))), pos=torch.arange(S0).repeat(B, 1),
+              ov=torch.zeros(B, S0), om=torch.zeros(B, S0, dtype=torch.bool), active=torch.ones(B, dtype=torch.bool),
+              num_real=torch.tensor([48, 40, 48, 33, 47, 48, 48, 21, 48, 48, 44, 48]))
+    K.get_error()
+    _check(bb.causal_forward(**kw), ob.causal_forward(**{k: v.numpy() for k, v in kw.items()}), 3e-2, 0.998,
+           "prefill")
+    pos = kw["num_real"].clone()
+    for step in range(3):
+        kw = dict(ids=torch.from_numpy(rng.integers(0, cfg.vocab_size, (B, 1))), pos=pos[:, None].clone(),
+                  ov=torch.zeros(B, 1), om=torch.zeros(B, 1, dtype=torch.bool), active=torch.ones(B, dtype=torch.bool))
+        _check(bb.causal_incremental(**kw), ob.causal_incremental(**{k: v.numpy() for k, v in kw.items()}), 3e-2,
+               0.998, f"step {step}")
+        pos += 1
+    assert K.get_error() == 0
