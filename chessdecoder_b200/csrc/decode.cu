@@ -161,7 +161,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
     if (tid == 0) report_error(kErrIndex);
     n_cache = max(0, min(n_cache, (int)a.max_len - a.S_new));
   }
-  const int total = n_cache + a.S_new;
+  // causal new block without an explicit mask: keys past the chunk's last
+  // query are visible to none of its queries
+  const int total = (a.block_mode == CDK_BLOCK_CAUSAL && a.full == nullptr) ? n_cache + min(a.S_new, q0 + nq)
+                                                                          : n_cache + a.S_new;
   const int row_base = (int)((b * a.H + h) * a.max_len);
   uint64_t* wbar = bars + warp * kStages;
   uint8_t* wring = ring + warp * kStages * kStageBytes;

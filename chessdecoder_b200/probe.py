@@ -125,7 +125,10 @@ def gemm_case_fp8(kind: str, T: int = 32768, E: int = 1024, F: int = 1536):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("mode", choices=["gemm", "attn", "adamw", "tokenize"])
+    ap.add_argument("mode", choices=["gemm", "attn", "adamw", "tokenize", "decode"])
+    ap.add_argument("--batch", type=int, default=64, help="decode: sequences")
+    ap.add_argument("--keys", type=int, default=542, help="decode: cached keys per sequence")
+    ap.add_argument("--new", type=int, default=1, help="decode: new tokens per sequence")
     ap.add_argument("--kind", default="rope", choices=["rope", "swiglu", "resid", "resid2", "dswiglu", "dx", "dw"])
     ap.add_argument("--fp8", action="store_true", help="8-bit operands (e4m3; e5m2 x e4m3 for dx / dw)")
     ap.add_argument("--nseq", type=int, default=128)
@@ -139,6 +142,24 @@ def main():
         ms = _time(fn, a.warmup, a.iters)
         print(json.dumps({"probe": name, "ms": ms, "tflops": flops / ms / 1e9, "alg_bytes": nbytes,
                           "alg_gbs": nbytes / ms / 1e6}))
+    elif a.mode == "decode":
+        # decode attention over one layer's cache: B sequences x 16 heads x `keys`
+        # cached keys (bf16 K / V rows of 128 B), `new` queries per sequence
+        B, H, L0, S_new = a.batch, 16, a.keys, a.new
+        max_len = L0 + S_new
+        g = torch.Generator(device="cuda").manual_seed(0)
+        kc = torch.randn(B, H, max_len, 64, device="cuda", generator=g).to(torch.bfloat16)
+        vc = torch.randn(B, H, max_len, 64, device="cuda", generator=g).to(torch.bfloat16)
+        valid = torch.ones(B, max_len, dtype=torch.uint8, device="cuda")
+        len_dev = torch.tensor([L0], dtype=torch.int32, device="cuda")
+        q = torch.randn(B * S_new, H * 64, device="cuda", generator=g).to(torch.bfloat16)
+        out = torch.empty_like(q)
+        mode = K.BLOCK_VALID if S_new == 1 else K.BLOCK_ALL
+        fn = lambda: K.decode_attn(q, kc, vc, len_dev, S_new, B, H, valid, out, block_mode=mode)  # noqa: E731
+        ms = _time(fn, a.warmup, a.iters)
+        nbytes = B * H * (L0 + S_new) * 64 * 2 * 2
+        print(json.dumps({"probe": f"decode_attn B={B} H={H} keys={L0} new={S_new}", "us": ms * 1e3,
+                          "alg_bytes": nbytes, "alg_gbs": nbytes / ms / 1e6, "err": K.get_error()}))
     elif a.mode == "attn":
         S, H = a.seq, 16
         E = H * 64
