@@ -333,6 +333,28 @@ def run_decode(args, rank, world):
     a1.record()
     torch.cuda.synchronize()
     attn_us = a0.elapsed_time(a1) * 1000.0 / n_a
+    # greedy board generation of one sequence (the single-sequence engine's
+    # causalBoardStep loop): 80-token prefill, then 68 board tokens through the
+    # board head, each fed back on the device
+    from chessdecoder_b200 import vocab as V
+    gb = BatchedBackbone(cfg, batch_size=1, max_seq_len=80 + 68, device=dev, store=bb.store)
+    first = torch.full((1, 1), V.token_to_idx["start_pos"], dtype=torch.int64, device=dev)
+    gids = torch.randint(0, cfg.vocab_size, (1, 80), generator=g).to(dev)
+    gpos = torch.arange(80, device=dev).view(1, 80)
+    n80 = torch.full((1,), 80, device=dev)
+    gen_ms = []
+    for rep in range(4):
+        gb.reset_causal()
+        gb.causal_forward(gids, gpos, None, None, None, n80)
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        gb.generate(first, torch.full((1, 1), 80, device=dev), 68, head="board_head", lut=V.board_idx_to_full_idx)
+        g1.record()
+        torch.cuda.synchronize()
+        if rep > 0:
+            gen_ms.append(g0.elapsed_time(g1))
+    gen_t = statistics.median(gen_ms)
     err = K.get_error()
     if err:
         raise SystemExit(f"device error flag {err} after the decode run")
@@ -360,7 +382,9 @@ def run_decode(args, rank, world):
                          "launch_us": attn_us, "bytes_per_launch": attn_bytes, "traffic": None,
                          "peak_kind": "measured" if hbm else "fallback",
                          "step_hbm_gbs": step_bytes / (ms / 1000.0) / 1e9},
-            "gpu_launches": launches}
+            "gpu_launches": launches,
+            "generate": {"batch": 1, "prefill": 80, "tokens": 68, "head": "board_head", "ms": gen_t,
+                         "tokens_per_s": 68 / (gen_t / 1000.0), "ms_per_token": gen_t / 68}}
     if clk:
         line["clocks"] = clk
     if not args.no_cpu_baseline:
@@ -473,11 +497,9 @@ def main():
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record()
-    host_t0 = time.perf_counter()
     for i in range(args.steps):
         dp.forward_backward(dbs[i % len(dbs)])
         dp.optimizer_step()
-    host_enqueue_ms = (time.perf_counter() - host_t0) * 1000 / args.steps
     ev1.record()
     sync_all()
     clocks = sampler.stop()
@@ -489,6 +511,14 @@ def main():
     tokens_step = args.batch * args.seq * world
     value = tokens_step / (dev_ms / 1000.0)
     gemm_stats = gemm_timer.summary(detail=args.detail)
+    # host cost of enqueueing one step with the GPU idle (inside the timed loop the
+    # host waits on the full launch queue, so its wall time there is the GPU's)
+    sync_all()
+    host_t0 = time.perf_counter()
+    dp.forward_backward(dbs[0])
+    dp.optimizer_step()
+    host_enqueue_ms = (time.perf_counter() - host_t0) * 1000
+    sync_all()
 
     # ---- e2e: public API from host batches -------------------------------------
     host_pool = []

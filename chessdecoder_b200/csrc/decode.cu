@@ -564,6 +564,50 @@ __global__ void swiglu_f32_kernel(const float* __restrict__ gu, long long ldg, l
   *reinterpret_cast<uint32_t*>(u + t * ldu + f) = f2bf2(a, c);
 }
 
+// Greedy next token per sequence: idx = argmax(logits[r, :ncols]) (lowest
+// index on ties, as torch.argmax), ids[r] = lut ? lut[idx] : idx, and the
+// step's ids appended to hist[*counter][r]; then pos[r] += 1 and *counter += 1.
+// One block: warp w handles rows w, w + 8, ...
+__global__ void head_argmax_kernel(const float* __restrict__ logits, long long ldl, int rows, int ncols,
+                                   const int64_t* __restrict__ lut, int64_t* __restrict__ ids,
+                                   int64_t* __restrict__ pos, int64_t* __restrict__ hist, int32_t* __restrict__ counter,
+                                   int max_steps) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int step = counter ? *counter : 0;
+  for (int r = warp; r < rows; r += blockDim.x >> 5) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = lane; c < ncols; c += 32) {
+      const float v = logits[(long long)r * ldl + c];
+      if (v > best || (v == best && c < bi)) {
+        best = v;
+        bi = c;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      if (bi >= ncols) bi = 0;  // every logit NaN
+      const int64_t id = lut ? lut[bi] : (int64_t)bi;
+      ids[r] = id;
+      if (pos) pos[r] += 1;
+      if (hist) {
+        if (step < max_steps) hist[(long long)step * rows + r] = id;
+        else report_error(kErrIndex);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && counter) *counter = step + 1;
+}
+
 __global__ void decode_slots_kernel(const uint8_t* __restrict__ om, long long n, int32_t* __restrict__ slot) {
   const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (t < n) slot[t] = om[t] ? (int32_t)t : -1;
@@ -664,6 +708,17 @@ extern "C" int cdk_swiglu_f32(const float* gu, int64_t ldg, int64_t T, int64_t F
   const long long n = T * (F / 2);
   swiglu_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       gu, ldg, T, (int)F, reinterpret_cast<__nv_bfloat16*>(u), ldu);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+extern "C" int cdk_head_argmax(const float* logits, int64_t ldl, int64_t rows, int64_t ncols, const int64_t* lut,
+                               int64_t* ids, int64_t* pos, int64_t* hist, int32_t* counter, int64_t max_steps,
+                               void* stream) {
+  if (rows == 0) return 0;
+  if (!logits || !ids || rows < 0 || ncols <= 0 || ldl < ncols || (hist && !counter)) return -1;
+  head_argmax_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      logits, ldl, (int)rows, (int)ncols, lut, ids, pos, hist, counter, (int)max_steps);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
 }

@@ -104,6 +104,7 @@ class BatchedBackbone:
         # incremental steps replay from CUDA graphs (first call eager, second captures)
         self.use_graphs = bool(use_graphs) and self.device.type == "cuda"
         self._graphs = {}
+        self._gen = {}
         st, E, F = store, cfg.embed_dim, cfg.ff
         self._layers = []
         for i in range(L):
@@ -299,6 +300,49 @@ class BatchedBackbone:
     def prefix_probe(self, ids, pos, ov, om):
         return self._forward(self.prefix, ids, pos, ov, om, block_mode=K.BLOCK_ALL)
 
+    # -- greedy generation (causalBoardStep, torch_backbone.hpp:141-152) ---------
+    def generate(self, ids, pos, n_steps: int, head: str = "board_head", lut=None, active=None):
+        """Greedy generation on the causal cache, entirely on the device: step k
+        runs one incremental step, the `head` logits of its hidden state, their
+        argmax mapped to the full vocabulary by `lut` (sub-vocabulary index ->
+        token id; None = identity), and feeds that token back as step k+1's
+        input at position + 1.  The first step runs eagerly, the others replay
+        one CUDA graph (no host synchronisation between steps).  ids / pos
+        [B, 1]: the first input token and its position; active [B] (default
+        all).  Returns the generated token ids [n_steps, B] (device)."""
+        B = self.B
+        cache = self.causal
+        if n_steps <= 0:
+            return torch.empty(0, B, dtype=torch.int64, device=self.device)
+        if cache.len + n_steps > self.max_len:
+            raise ValueError(f"cache full: {cache.len} + {n_steps} > {self.max_len}")
+        key = (head, None if lut is None else tuple(int(x) for x in lut))
+        st = self._gen.get(key)
+        if st is None:
+            st = self._gen[key] = _GenState(self, head, lut)
+        st.ids.copy_(ids.reshape(B, 1))
+        st.pos.copy_(pos.reshape(B, 1))
+        if active is None:
+            st.active.fill_(True)
+        else:
+            st.active.copy_(active.reshape(B))
+        st.counter.zero_()
+        self._gen_body(st)  # eager: every lazy set-up happens outside capture
+        cache.len += 1
+        if n_steps > 1:
+            if st.graph is None:
+                st.capture(self)
+            for _ in range(n_steps - 1):
+                st.graph.replay()
+                K.LAUNCHES[0] += st.n_launch
+                cache.len += 1
+        return st.hist[:n_steps].clone()
+
+    def _gen_body(self, st):
+        self._incremental_body(self.causal, st.ids, st.pos, None, None, st.active)
+        K.gemm(self.last_hidden16.reshape(self.B, -1), st.weight, kind=K.EPI_STORE_F32, out=st.logits, bias=st.bias)
+        K.head_argmax(st.logits, st.ids.view(-1), lut=st.lut, pos=st.pos.view(-1), hist=st.hist, counter=st.counter)
+
     def _incremental(self, cache, ids, pos, ov, om, active):
         B, S = ids.shape
         if S != 1:
@@ -370,3 +414,33 @@ class _IncrementalGraph:
             self.active.fill_(True)
         else:
             self.active.copy_(active.reshape(self.active.shape), non_blocking=True)
+
+
+class _GenState:
+    """Static buffers and the captured step of a greedy generation loop."""
+
+    def __init__(self, bb: BatchedBackbone, head: str, lut):
+        dev, B = bb.device, bb.B
+        self.weight = bb.store.bf16(f"{head}.weight")
+        self.bias = bb.store.param(f"{head}.bias")
+        V = self.weight.shape[0]
+        self.lut = None if lut is None else torch.as_tensor(list(lut), dtype=torch.int64, device=dev)
+        if self.lut is not None and self.lut.numel() != V:
+            raise ValueError(f"lut has {self.lut.numel()} entries, head {head} has {V} outputs")
+        self.ids = torch.zeros(B, 1, dtype=torch.int64, device=dev)
+        self.pos = torch.zeros(B, 1, dtype=torch.int64, device=dev)
+        self.active = torch.ones(B, dtype=torch.bool, device=dev)
+        self.logits = torch.empty(B, V, device=dev)
+        self.hist = torch.zeros(bb.max_len, B, dtype=torch.int64, device=dev)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.graph = None
+        self.n_launch = 0
+
+    def capture(self, bb: BatchedBackbone):
+        self.graph = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize(bb.device)
+        n0 = K.LAUNCHES[0]
+        with torch.cuda.graph(self.graph):
+            bb._gen_body(self)
+        self.n_launch = K.LAUNCHES[0] - n0
+        K.LAUNCHES[0] = n0

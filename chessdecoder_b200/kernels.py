@@ -573,3 +573,14 @@ def swiglu_f32(gu32, u):
     rc = lib().cdk_swiglu_f32(_p(gu32), gu32.stride(0), T, F, _p(u), u.stride(0), _stream())
     _check(rc, "swiglu_f32")
     _count(1)
+
+
+@_timed("head_argmax")
+def head_argmax(logits, ids, lut=None, pos=None, hist=None, counter=None):
+    """ids[r] = lut[argmax(logits[r])]; optionally pos += 1 and the ids appended
+    to hist at row *counter (counter += 1)."""
+    rows, ncols = logits.shape
+    rc = lib().cdk_head_argmax(_p(logits), logits.stride(0), rows, ncols, _p(lut), _p(ids), _p(pos), _p(hist),
+                               _p(counter), hist.shape[0] if hist is not None else 0, _stream())
+    _check(rc, "head_argmax")
+    _count(1)

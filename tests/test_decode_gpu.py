@@ -168,3 +168,49 @@ def test_prefill_rows_above_split_threshold():
                0.998, f"step {step}")
         pos += 1
     assert K.get_error() == 0
+
+
+def test_greedy_generation_matches_oracle():
+    """Device-side greedy generation through the board head (causalBoardStep):
+    each generated token, fed back teacher-forced into the oracle, is the
+    oracle's argmax unless the oracle's top-2 margin is a near-tie."""
+    from chessdecoder_b200 import vocab as V
+    cfg = ModelConfig(num_layers=4)
+    B, max_len, S0, n = 3, 48, 10, 12
+    sd = init_reference_weights(cfg, 13)
+    sd["board_head.weight"] = sd["board_head.weight"] * 30.0
+    for i in range(cfg.num_layers):
+        for nm in ("q_proj", "k_proj"):
+            sd[f"layers.{i}.attn.{nm}.weight"] = sd[f"layers.{i}.attn.{nm}.weight"] * 4.0
+    bb = D.BatchedBackbone(cfg, batch_size=B, max_seq_len=max_len, state_dict=sd)
+    w = {k: v.float().numpy() for k, v in sd.items()}
+    ob = OD.Batched(w, dict(num_layers=cfg.num_layers, num_heads=cfg.num_heads, embed_dim=cfg.embed_dim,
+                            max_seq_len=cfg.max_seq_len), B, max_len)
+    rng = np.random.default_rng(8)
+    kw = dict(ids=torch.from_numpy(rng.integers(0, cfg.vocab_size, (B, S0))), pos=torch.arange(S0).repeat(B, 1),
+              ov=torch.zeros(B, S0), om=torch.zeros(B, S0, dtype=torch.bool), active=torch.ones(B, dtype=torch.bool),
+              num_real=torch.full((B,), S0))
+    bb.causal_forward(**kw)
+    ob.causal_forward(**{k: v.numpy() for k, v in kw.items()})
+    lut = V.board_idx_to_full_idx
+    first = torch.full((B, 1), V.token_to_idx["start_pos"] if "start_pos" in V.token_to_idx else 0)
+    K.get_error()
+    gen = bb.generate(first, torch.full((B, 1), S0), n, head="board_head", lut=lut).cpu()
+    assert gen.shape == (n, B) and bb.causal_len == S0 + n
+    assert K.get_error() == 0
+    inv = {t: i for i, t in enumerate(lut)}
+    ids = first.numpy()
+    near_ties = 0
+    for k in range(n):
+        h = ob.causal_incremental(ids, np.full((B, 1), S0 + k), np.zeros((B, 1), np.float32),
+                                  np.zeros((B, 1), bool), np.ones(B, bool))
+        logits = h[:, 0] @ w["board_head.weight"].T + w["board_head.bias"]
+        for b in range(B):
+            got = inv[int(gen[k, b])]
+            best = int(np.argmax(logits[b]))
+            if got != best:
+                margin = logits[b, best] - logits[b, got]
+                assert margin < 0.02 * logits[b].std(), (k, b, got, best, margin)
+                near_ties += 1
+        ids = gen[k].numpy().reshape(B, 1)
+    assert near_ties <= 2
