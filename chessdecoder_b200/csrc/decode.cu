@@ -25,6 +25,9 @@
 //                 length update of forwardImpl).
 // The HBM-bound part is decode_attn: it reads each cache key row once per
 // (sequence, head, 8-query chunk); kv_append and decode_mark are O(new rows).
+#include <algorithm>
+#include <cstddef>
+
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -342,187 +345,209 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
   }
 }
 
-// One query per (sequence, head): the incremental step.  Grid (H, B),
-// kWarps warps, the same per-warp TMA ring of K / V tiles as decode_attn_kernel.
-// Lane l owns key (tile * 32 + l): it scores it from its swizzled K row and, if
-// the key is valid, folds it into its own online-softmax state (max, sum and a
-// 64-wide fp32 accumulator from its swizzled V row), so the loop has no
-// cross-lane traffic.  The 32 x kWarps lane states are merged once at the end.
+// One query per (sequence, head): the incremental step.  Persistent: each
+// CTA walks (sequence, head) items i = blockIdx.x + n * gridDim.x.  Every
+// sequence has the same number of keys (len + 1), so each of the kWarps warps
+// sees the same tile count per item and its TMA ring runs as one stream of
+// tiles across items: while a warp merges item n, the first tiles of item n+1
+// are already in flight.  Lane l owns key (tile * 32 + l): it scores it from
+// its swizzled K row and, if the key is valid, folds it into its own online-
+// softmax state (max, sum, 64 fp32 accumulators from its swizzled V row), so
+// the key loop has no cross-lane traffic; the lane states are merged by warp
+// shuffles, then across the warps through shared memory.
+struct Dec1qSmem {
+  float q[kWarps][kHD];          // each warp's copy of the item's scaled query
+  float red[kWarps][kHD + 4];    // per-warp merged state: acc[64], max, sum (rows 16-byte aligned)
+  uint64_t bar[kWarps][kStages];
+  int abort;
+};
+static_assert(offsetof(Dec1qSmem, red) % 16 == 0 && ((kHD + 4) * 4) % 16 == 0 && offsetof(Dec1qSmem, bar) % 8 == 0,
+              "float4 rows and mbarriers need their alignment");
+constexpr int kSmem1q = kRingBytes + (int)sizeof(Dec1qSmem) + 1024;
+
 __global__ void __launch_bounds__(kWarps * 32, 2)
     decode_attn_1q_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                          const DecodeAttnArgs a) {
+                          const DecodeAttnArgs a, int n_items) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ring = smem;
-  float* qs = reinterpret_cast<float*>(smem + kRingBytes);
-  float* cm = reinterpret_cast<float*>(smem + kRingBytes + kQBytes);
-  float* cl = cm + kWarps * 32;  // kWarps * 32 * 3 floats
-  uint64_t* bars = reinterpret_cast<uint64_t*>(cm + 4 * kWarps * 32);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kWarps * kStages);
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Dec1qSmem& sm = *reinterpret_cast<Dec1qSmem*>(ring + kRingBytes);
+  volatile int* abort_flag = &sm.abort;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int h = blockIdx.x;
-  const long long b = blockIdx.y;
   int n_cache = *a.len_dev;
   if (n_cache < 0 || (long long)n_cache + 1 > a.max_len) {
     if (tid == 0) report_error(kErrIndex);
     n_cache = max(0, min(n_cache, (int)a.max_len - 1));
   }
   const int total = n_cache + 1;
-  const int row_base = (int)((b * a.H + h) * a.max_len);
-  uint64_t* wbar = bars + warp * kStages;
-  uint8_t* wring = ring + warp * kStages * kStageBytes;
   const int n_tiles = total > warp * kKT ? (total - warp * kKT + kWarps * kKT - 1) / (kWarps * kKT) : 0;
+  const int n_local = n_items > (int)blockIdx.x ? (n_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+  const long long stream_len = (long long)n_local * n_tiles;  // this warp's tiles over all its items
+  uint64_t* wbar = sm.bar[warp];
+  uint8_t* wring = ring + warp * kStages * kStageBytes;
 
+  // tile g of this warp's stream: item blockIdx.x + (g / n_tiles) * gridDim.x, key tile g % n_tiles
+  auto issue = [&](long long g) {
+    const int item = (int)blockIdx.x + (int)(g / n_tiles) * (int)gridDim.x;
+    const int k = (int)(g % n_tiles);
+    const long long bb = item / a.H;
+    const int hh = item % a.H;
+    const int row = (int)((bb * a.H + hh) * a.max_len) + (warp + k * kWarps) * kKT;
+    const int st = (int)(g % kStages);
+    mbar_arrive_expect_tx(&wbar[st], kStageBytes);
+    tma_load_2d(wring + st * kStageBytes, &kmap, &wbar[st], 0, row);
+    tma_load_2d(wring + st * kStageBytes + kTileBytes, &vmap, &wbar[st], 0, row);
+  };
   if (tid == 0) *abort_flag = 0;
   if (lane == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&wbar[s], 1);
     fence_mbar_init();
-    for (int k = 0; k < kStages - 1 && k < n_tiles; ++k) {
-      const int t0 = (warp + k * kWarps) * kKT;
-      mbar_arrive_expect_tx(&wbar[k], kStageBytes);
-      tma_load_2d(wring + k * kStageBytes, &kmap, &wbar[k], 0, row_base + t0);
-      tma_load_2d(wring + k * kStageBytes + kTileBytes, &vmap, &wbar[k], 0, row_base + t0);
-    }
+    for (long long g = 0; g < kStages - 1 && g < stream_len; ++g) issue(g);
   }
-  if (tid < kHD) qs[tid] = __bfloat162float(a.q[b * a.ldq + h * kHD + tid]) * a.scale_log2;
   __syncthreads();
 
-  const bool act = a.active == nullptr || a.active[b] != 0;
-  const long long nreal = a.num_real ? a.num_real[b] : 1;
-  auto key_ok = [&](int j) -> bool {
+  auto key_ok = [&](long long b, int j) -> bool {
     if (j >= total) return false;
     if (a.full) return j < a.ldf && a.full[b * a.ldf + j] != 0;
     if (j < n_cache || a.block_mode == CDK_BLOCK_VALID) return a.valid[b * a.ldv + j] != 0;
-    if (a.block_mode == CDK_BLOCK_CAUSAL) return nreal > 0;
-    if (a.block_mode == CDK_BLOCK_ACTIVE) return act;
+    if (a.block_mode == CDK_BLOCK_CAUSAL) return a.num_real == nullptr || a.num_real[b] > 0;
+    if (a.block_mode == CDK_BLOCK_ACTIVE) return a.active == nullptr || a.active[b] != 0;
     return true;
   };
 
-  float m = -INFINITY, l = 0.f;
-  float acc[kHD];
-#pragma unroll
-  for (int d = 0; d < kHD; ++d) acc[d] = 0.f;
-  bool ok_cur = n_tiles > 0 && key_ok(warp * kKT + lane);
-
-  for (int k = 0; k < n_tiles; ++k) {
-    const int t0 = (warp + k * kWarps) * kKT;
-    const int st = k % kStages;
-    mbar_wait(&wbar[st], (uint32_t)((k / kStages) & 1), abort_flag);
-    if (lane == 0 && k + kStages - 1 < n_tiles) {
-      const int kn = k + kStages - 1, sn = kn % kStages;
-      const int tn = (warp + kn * kWarps) * kKT;
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive_expect_tx(&wbar[sn], kStageBytes);
-      tma_load_2d(wring + sn * kStageBytes, &kmap, &wbar[sn], 0, row_base + tn);
-      tma_load_2d(wring + sn * kStageBytes + kTileBytes, &vmap, &wbar[sn], 0, row_base + tn);
-    }
-    const bool ok_next = k + 1 < n_tiles && key_ok(t0 + kWarps * kKT + lane);
-    const uint8_t* kt = wring + st * kStageBytes;
-    const uint8_t* vt = kt + kTileBytes;
-    if (ok_cur) {
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 kc = *reinterpret_cast<const uint4*>(kt + swz(lane, c));
-        const float4 qa = *reinterpret_cast<const float4*>(qs + c * 8);
-        const float4 qb = *reinterpret_cast<const float4*>(qs + c * 8 + 4);
-        float2 f = bf2f(kc.x);
-        s0 = fmaf(qa.x, f.x, s0);
-        s1 = fmaf(qa.y, f.y, s1);
-        f = bf2f(kc.y);
-        s0 = fmaf(qa.z, f.x, s0);
-        s1 = fmaf(qa.w, f.y, s1);
-        f = bf2f(kc.z);
-        s0 = fmaf(qb.x, f.x, s0);
-        s1 = fmaf(qb.y, f.y, s1);
-        f = bf2f(kc.w);
-        s0 = fmaf(qb.z, f.x, s0);
-        s1 = fmaf(qb.w, f.y, s1);
-      }
-      const float sc = s0 + s1;
-      if (sc > m) {  // new running max for this lane: rescale its state
-        const float alpha = exp2f(m - sc);
-        l *= alpha;
-#pragma unroll
-        for (int d = 0; d < kHD; ++d) acc[d] *= alpha;
-        m = sc;
-      }
-      const float pv = exp2f(sc - m);
-      l += pv;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 vc = *reinterpret_cast<const uint4*>(vt + swz(lane, c));
-        float2 f = bf2f(vc.x);
-        acc[c * 8 + 0] = fmaf(pv, f.x, acc[c * 8 + 0]);
-        acc[c * 8 + 1] = fmaf(pv, f.y, acc[c * 8 + 1]);
-        f = bf2f(vc.y);
-        acc[c * 8 + 2] = fmaf(pv, f.x, acc[c * 8 + 2]);
-        acc[c * 8 + 3] = fmaf(pv, f.y, acc[c * 8 + 3]);
-        f = bf2f(vc.z);
-        acc[c * 8 + 4] = fmaf(pv, f.x, acc[c * 8 + 4]);
-        acc[c * 8 + 5] = fmaf(pv, f.y, acc[c * 8 + 5]);
-        f = bf2f(vc.w);
-        acc[c * 8 + 6] = fmaf(pv, f.x, acc[c * 8 + 6]);
-        acc[c * 8 + 7] = fmaf(pv, f.y, acc[c * 8 + 7]);
-      }
-    }
-    ok_cur = ok_next;
-    __syncwarp();
+  // query of the first item (two bf16 per lane), then prefetched one item ahead
+  uint32_t qnext = 0;
+  if (n_local > 0) {
+    const int item = blockIdx.x;
+    qnext = *reinterpret_cast<const uint32_t*>(a.q + (long long)(item / a.H) * a.ldq + (item % a.H) * kHD + 2 * lane);
   }
+  long long g = 0;
+  // validity of this lane's key in the current tile, loaded one tile ahead
+  bool ok_cur = n_local > 0 && n_tiles > 0 && key_ok((int)blockIdx.x / a.H, warp * kKT + lane);
+  for (int n = 0; n < n_local; ++n) {
+    const int item = (int)blockIdx.x + n * (int)gridDim.x;
+    const long long b = item / a.H;
+    const int h = item % a.H;
+    {
+      const float2 qf = bf2f(qnext);
+      sm.q[warp][2 * lane] = qf.x * a.scale_log2;
+      sm.q[warp][2 * lane + 1] = qf.y * a.scale_log2;
+      if (n + 1 < n_local) {
+        const int nx = item + (int)gridDim.x;
+        qnext = *reinterpret_cast<const uint32_t*>(a.q + (long long)(nx / a.H) * a.ldq + (nx % a.H) * kHD + 2 * lane);
+      }
+      __syncwarp();
+    }
+    const float* qs = sm.q[warp];
+    float m = -INFINITY, l = 0.f;
+    float acc[kHD];
+#pragma unroll
+    for (int d = 0; d < kHD; ++d) acc[d] = 0.f;
+    for (int k = 0; k < n_tiles; ++k, ++g) {
+      const int t0 = (warp + k * kWarps) * kKT;
+      const int st = (int)(g % kStages);
+      mbar_wait(&wbar[st], (uint32_t)((g / kStages) & 1), abort_flag);
+      // refill the stage read in the previous step (its reads finished at that step's __syncwarp)
+      if (lane == 0 && g + kStages - 1 < stream_len) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue(g + kStages - 1);
+      }
+      bool ok_next = false;  // next tile of this item, or the first tile of the next item
+      if (k + 1 < n_tiles) ok_next = key_ok(b, t0 + kWarps * kKT + lane);
+      else if (n + 1 < n_local) ok_next = key_ok((item + (int)gridDim.x) / a.H, warp * kKT + lane);
+      const uint8_t* kt = wring + st * kStageBytes;
+      const uint8_t* vt = kt + kTileBytes;
+      if (ok_cur) {
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 kc = *reinterpret_cast<const uint4*>(kt + swz(lane, c));
+          const float4 qa = *reinterpret_cast<const float4*>(qs + c * 8);
+          const float4 qb = *reinterpret_cast<const float4*>(qs + c * 8 + 4);
+          float2 f = bf2f(kc.x);
+          s0 = fmaf(qa.x, f.x, s0);
+          s1 = fmaf(qa.y, f.y, s1);
+          f = bf2f(kc.y);
+          s0 = fmaf(qa.z, f.x, s0);
+          s1 = fmaf(qa.w, f.y, s1);
+          f = bf2f(kc.z);
+          s0 = fmaf(qb.x, f.x, s0);
+          s1 = fmaf(qb.y, f.y, s1);
+          f = bf2f(kc.w);
+          s0 = fmaf(qb.z, f.x, s0);
+          s1 = fmaf(qb.w, f.y, s1);
+        }
+        const float sc = s0 + s1;
+        if (sc > m) {  // new running max for this lane: rescale its state
+          const float alpha = exp2f(m - sc);
+          l *= alpha;
+#pragma unroll
+          for (int d = 0; d < kHD; ++d) acc[d] *= alpha;
+          m = sc;
+        }
+        const float pv = exp2f(sc - m);
+        l += pv;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 vc = *reinterpret_cast<const uint4*>(vt + swz(lane, c));
+          float2 f = bf2f(vc.x);
+          acc[c * 8 + 0] = fmaf(pv, f.x, acc[c * 8 + 0]);
+          acc[c * 8 + 1] = fmaf(pv, f.y, acc[c * 8 + 1]);
+          f = bf2f(vc.y);
+          acc[c * 8 + 2] = fmaf(pv, f.x, acc[c * 8 + 2]);
+          acc[c * 8 + 3] = fmaf(pv, f.y, acc[c * 8 + 3]);
+          f = bf2f(vc.z);
+          acc[c * 8 + 4] = fmaf(pv, f.x, acc[c * 8 + 4]);
+          acc[c * 8 + 5] = fmaf(pv, f.y, acc[c * 8 + 5]);
+          f = bf2f(vc.w);
+          acc[c * 8 + 6] = fmaf(pv, f.x, acc[c * 8 + 6]);
+          acc[c * 8 + 7] = fmaf(pv, f.y, acc[c * 8 + 7]);
+        }
+      }
+      ok_cur = ok_next;
+      __syncwarp();
+    }
 
-  // Merge the kWarps * 32 lane states: every lane rescales its state to the
-  // block-wide max M, stores it row-wise into the (now idle) ring, then thread
-  // (group g, pair d2) sums 32 rows of dims 2 d2, 2 d2 + 1 and group partials
-  // are added up.
-  float wm = m;
+    // warp merge: rescale every lane to the warp max, then butterfly sums
+    float wm = m;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
-  __syncthreads();  // all warps are done with the ring
-  float* red = cm;  // [kWarps] warp maxima, then [kWarps][32] x (x, y, L) partials
-  if (lane == 0) red[warp] = wm;
-  __syncthreads();
-  float M = red[0];
+    for (int o = 16; o > 0; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+    const float f = (m == -INFINITY) ? 0.f : exp2f(m - wm);
+    l *= f;
 #pragma unroll
-  for (int w = 1; w < kWarps; ++w) M = fmaxf(M, red[w]);
-  const float f = (m == -INFINITY) ? 0.f : exp2f(m - M);
-  float* st_acc = reinterpret_cast<float*>(ring);
-  static_assert(kWarps * 32 * (kHD + 1) * 4 <= kRingBytes, "lane states fit in the ring");
-  float* st_l = st_acc + kWarps * 32 * kHD;
+    for (int d = 0; d < kHD; ++d) acc[d] *= f;
 #pragma unroll
-  for (int c = 0; c < kHD / 4; ++c)
-    *reinterpret_cast<float4*>(st_acc + tid * kHD + c * 4) =
-        make_float4(acc[c * 4] * f, acc[c * 4 + 1] * f, acc[c * 4 + 2] * f, acc[c * 4 + 3] * f);
-  st_l[tid] = l * f;
-  __syncthreads();
-  {
-    const int d2 = lane, g = warp;
-    float ox = 0.f, oy = 0.f, L = 0.f;
-#pragma unroll 8
-    for (int i = 0; i < 32; ++i) {
-      const int r = g * 32 + i;
-      const float2 v = *reinterpret_cast<const float2*>(st_acc + r * kHD + 2 * d2);
-      ox += v.x;
-      oy += v.y;
-      L += st_l[r];
+    for (int o = 16; o > 0; o >>= 1) {
+      l += __shfl_xor_sync(0xffffffffu, l, o);
+#pragma unroll
+      for (int d = 0; d < kHD; ++d) acc[d] += __shfl_xor_sync(0xffffffffu, acc[d], o);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int d = 0; d < kHD; d += 4)
+        *reinterpret_cast<float4*>(&sm.red[warp][d]) = make_float4(acc[d], acc[d + 1], acc[d + 2], acc[d + 3]);
+      sm.red[warp][kHD] = wm;
+      sm.red[warp][kHD + 1] = l;
     }
     __syncthreads();
-    float* part = cl;  // [kWarps][32][3]
-    part[(g * 32 + d2) * 3 + 0] = ox;
-    part[(g * 32 + d2) * 3 + 1] = oy;
-    part[(g * 32 + d2) * 3 + 2] = L;
-  }
-  __syncthreads();
-  if (tid < 32) {
-    float ox = 0.f, oy = 0.f, L = 0.f;
+    if (warp == 0) {
+      float M = -INFINITY;
 #pragma unroll
-    for (int g = 0; g < kWarps; ++g) {
-      ox += cl[(g * 32 + tid) * 3 + 0];
-      oy += cl[(g * 32 + tid) * 3 + 1];
-      L += cl[(g * 32 + tid) * 3 + 2];
+      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm.red[w][kHD]);
+      float L = 0.f, ox = 0.f, oy = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+          const float fw = sm.red[w][kHD] == -INFINITY ? 0.f : exp2f(sm.red[w][kHD] - M);
+          L += sm.red[w][kHD + 1] * fw;
+          ox += sm.red[w][2 * lane] * fw;
+          oy += sm.red[w][2 * lane + 1] * fw;
+        }
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      *reinterpret_cast<uint32_t*>(a.out + b * a.ldo + h * kHD + 2 * lane) = f2bf2(ox * inv, oy * inv);
     }
-    const float inv = (M != -INFINITY && L > 0.f) ? 1.f / L : 0.f;
-    *reinterpret_cast<uint32_t*>(a.out + b * a.ldo + h * kHD + 2 * tid) = f2bf2(ox * inv, oy * inv);
+    __syncthreads();  // sm.red is rewritten by the next item
   }
 }
 
@@ -642,7 +667,8 @@ extern "C" int cdk_decode_attn(const void* q, int64_t ldq, const void* k_cache, 
                                int64_t ldo, float scale, void* stream) {
   if (B == 0 || S_new == 0) return 0;
   if (!q || !k_cache || !v_cache || !len_dev || !valid || !out || B < 0 || S_new < 0 || H <= 0) return -1;
-  if (B > 65535 || H > 65535 || ldq < H * kHD || ldo < H * kHD || ldo % 2 || ldv < max_len || S_new > max_len)
+  if (B > 65535 || H > 65535 || ldq < H * kHD || ldq % 2 || ldo < H * kHD || ldo % 2 || ldv < max_len ||
+      S_new > max_len)
     return -2;
   if (full_mask && ldf < 1) return -3;
   if (block_mode < CDK_BLOCK_CAUSAL || block_mode > CDK_BLOCK_VALID) return -4;
@@ -670,17 +696,21 @@ extern "C" int cdk_decode_attn(const void* q, int64_t ldq, const void* k_cache, 
   a.ldo = ldo;
   a.scale_log2 = scale * 1.4426950408889634f;
   static bool attr_done[64] = {false};
+  static int num_sms[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return -8;
   if (!attr_done[dev]) {
     cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    cudaFuncSetAttribute(decode_attn_1q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaFuncSetAttribute(decode_attn_1q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem1q);
+    cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
     attr_done[dev] = true;
   }
   if (S_new == 1) {
-    decode_attn_1q_kernel<<<dim3((unsigned)H, (unsigned)B), kWarps * 32, kSmemBytes,
-                            reinterpret_cast<cudaStream_t>(stream)>>>(kmap, vmap, a);
+    const long long n_items = B * H;
+    const int grid = (int)std::min<long long>(n_items, 2ll * std::max(num_sms[dev], 1));
+    decode_attn_1q_kernel<<<grid, kWarps * 32, kSmem1q, reinterpret_cast<cudaStream_t>(stream)>>>(kmap, vmap, a,
+                                                                                              (int)n_items);
   } else {
     dim3 grid((unsigned)((S_new + kQC - 1) / kQC), (unsigned)H, (unsigned)B);
     decode_attn_kernel<<<grid, kWarps * 32, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(kmap, vmap, a);
