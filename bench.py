@@ -222,8 +222,7 @@ def run_grpo(args, rank, world):
     from chessdecoder_b200 import data, kernels as K
     from chessdecoder_b200.engine import ModelConfig
     from chessdecoder_b200.rl import GRPOStep, prepare_rl_batch
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
+    dev = torch.device("cuda", torch.cuda.current_device())
     cfg = ModelConfig(num_layers=args.layers, max_seq_len=args.seq, finetune=True)
     step = GRPOStep(cfg, device=dev)
     rbs = []
@@ -272,8 +271,7 @@ def run_decode(args, rank, world):
     from chessdecoder_b200 import kernels as K
     from chessdecoder_b200.decode import BatchedBackbone
     from chessdecoder_b200.engine import ModelConfig
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
+    dev = torch.device("cuda", torch.cuda.current_device())
     B, ctx = args.batch, args.seq
     n_new = args.warmup + 2 * args.steps + 2
     max_len = ctx + n_new
@@ -292,7 +290,7 @@ def run_decode(args, rank, world):
         bb.causal_incremental(toks_dev[k], pos_dev[k], None, None, act)
         k += 1
     torch.cuda.synchronize()
-    clocks = ClockSampler(0)
+    clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
     K.LAUNCHES[0] = 0
     len0 = bb.causal_len
@@ -433,12 +431,12 @@ def main():
         run_reference(args, rank, world)
         cleanup_distributed()
         return
-    if args.grpo:
-        run_grpo(args, rank, world)
-        cleanup_distributed()
-        return
-    if args.decode:
-        run_decode(args, rank, world)
+    if args.grpo or args.decode:
+        # one-GPU variants: under torchrun rank 0 measures on its own GPU, the
+        # other ranks exit without work
+        if rank == 0:
+            torch.cuda.set_device(local_rank)
+            (run_grpo if args.grpo else run_decode)(args, rank, world)
         cleanup_distributed()
         return
     import torch.distributed as dist
