@@ -89,7 +89,7 @@ SIGNATURES = {
     "cdk_tokenize_games": (_int, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int,
                                   _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "cdk_kv_append": (_int, [_vp, _i64, _int, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _i64,
-                             _vp]),
+                             _int, _vp]),
     "cdk_decode_attn": (_int, [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _int, _vp, _vp, _vp,
                                _i64, _vp, _i64, _f32, _vp]),
     "cdk_decode_mark": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp]),

@@ -62,7 +62,7 @@ __global__ void kv_append_kernel(const void* __restrict__ qkv, long long ldq, in
                                  const int32_t* __restrict__ pos, const float* __restrict__ rope, int rope_len,
                                  int S_new, int H, long long max_len, const int32_t* __restrict__ len_dev,
                                  __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
-                                 __nv_bfloat16* __restrict__ q_out, long long ldo, long long total) {
+                                 __nv_bfloat16* __restrict__ q_out, long long ldo, int qkv_out, long long total) {
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total) return;
   const int pair = (int)(idx & 31);
@@ -89,6 +89,10 @@ __global__ void kv_append_kernel(const void* __restrict__ qkv, long long ldq, in
     q = make_float2(q.x * cs.x - q.y * cs.y, q.y * cs.x + q.x * cs.y);
     k = make_float2(k.x * cs.x - k.y * cs.y, k.y * cs.x + k.x * cs.y);
     *reinterpret_cast<uint32_t*>(q_out + t * ldo + col) = f2bf2(q.x, q.y);
+    if (qkv_out) {  // the rotated q | k | v row in the training layout (prefill through attn_fwd)
+      *reinterpret_cast<uint32_t*>(q_out + t * ldo + E + col) = f2bf2(k.x, k.y);
+      *reinterpret_cast<uint32_t*>(q_out + t * ldo + 2 * E + col) = f2bf2(v.x, v.y);
+    }
   } else {
     const __nv_bfloat16* row = reinterpret_cast<const __nv_bfloat16*>(qkv) + t * ldq;
     k = bf2f(*reinterpret_cast<const uint32_t*>(row + E + col));
@@ -644,18 +648,20 @@ inline bool al(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>
 
 extern "C" int cdk_kv_append(const void* qkv, int64_t ldq, int qkv_f32, const int32_t* pos, const float* rope,
                              int64_t rope_len, int64_t B, int64_t S_new, int64_t H, void* k_cache, void* v_cache,
-                             int64_t max_len, const int32_t* len_dev, void* q_out, int64_t ldo, void* stream) {
+                             int64_t max_len, const int32_t* len_dev, void* q_out, int64_t ldo, int qkv_out,
+                             void* stream) {
   if (B == 0 || S_new == 0) return 0;
   if (!qkv || !k_cache || !v_cache || !len_dev || B < 0 || S_new < 0 || H <= 0 || max_len <= 0) return -1;
   if (ldq < 3 * H * kHD || ldq % 2) return -2;
-  if (qkv_f32 && (!pos || !rope || !q_out || rope_len <= 0 || ldo < H * kHD || ldo % 2)) return -3;
+  if (qkv_f32 && (!pos || !rope || !q_out || rope_len <= 0 || ldo < (qkv_out ? 3 : 1) * H * kHD || ldo % 2))
+    return -3;
   if (!al(k_cache, 16) || !al(v_cache, 16) || !al(qkv, 8)) return -4;
   const long long total = B * S_new * H * 32;
   const unsigned blocks = (unsigned)((total + 255) / 256);
   kv_append_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       qkv, ldq, qkv_f32, pos, rope, (int)rope_len, (int)S_new, (int)H, max_len, len_dev,
       reinterpret_cast<__nv_bfloat16*>(k_cache), reinterpret_cast<__nv_bfloat16*>(v_cache),
-      reinterpret_cast<__nv_bfloat16*>(q_out), ldo, total);
+      reinterpret_cast<__nv_bfloat16*>(q_out), ldo, qkv_f32 ? qkv_out : 0, total);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
 }

@@ -198,6 +198,14 @@ class BatchedBackbone:
               ov.to(device=dev, dtype=torch.float32).reshape(-1).contiguous())
         om_u8 = (torch.zeros(T, dtype=torch.uint8, device=dev) if om is None else _u8(om, dev).reshape(-1))
         x = self._embed(ids, ov, om_u8)
+        # A causal block into an empty cache with no padding is the training
+        # forward's causal attention: q | k | v rows go through cdk_attn_fwd
+        # (tensor cores) instead of the cache-attention kernel.
+        fresh = (cache.len == 0 and block_mode == K.BLOCK_CAUSAL and full is None and S >= 16
+                 and (num_real is None or bool((num_real == S).all())))
+        if fresh:
+            qkv16 = torch.empty(T, 3 * E, device=dev, dtype=torch.bfloat16)
+            lse = torch.empty(B * H * S, device=dev)
         n1 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
         qkv = torch.empty(T, 3 * E, device=dev)
         q16 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
@@ -220,9 +228,15 @@ class BatchedBackbone:
                 K.gemm(n1, w["wqkv"], kind=K.EPI_ATOMIC_F32, out=qkv, split_k=_splits(T, 3 * E, E, self._sms))
             else:
                 K.gemm(n1, w["wqkv"], kind=K.EPI_STORE_F32, out=qkv)
-            K.kv_append(qkv, B, S, H, cache.k[i], cache.v[i], cache.len_dev, pos=pos32, rope=self.rope, q_out=q16)
-            K.decode_attn(q16, cache.k[i], cache.v[i], cache.len_dev, S, B, H, cache.valid, ao, block_mode=block_mode,
-                          active=active, num_real=num_real, full_mask=full)
+            if fresh:
+                K.kv_append(qkv, B, S, H, cache.k[i], cache.v[i], cache.len_dev, pos=pos32, rope=self.rope,
+                            q_out=qkv16, qkv_out=True)
+                K.attn_fwd(qkv16, ao, lse, B, B, S, H)
+            else:
+                K.kv_append(qkv, B, S, H, cache.k[i], cache.v[i], cache.len_dev, pos=pos32, rope=self.rope,
+                            q_out=q16)
+                K.decode_attn(q16, cache.k[i], cache.v[i], cache.len_dev, S, B, H, cache.valid, ao,
+                              block_mode=block_mode, active=active, num_real=num_real, full_mask=full)
             xn = torch.empty(T, E, device=dev)
             if small:
                 h1.copy_(x)

@@ -523,15 +523,16 @@ BLOCK_CAUSAL, BLOCK_ACTIVE, BLOCK_ALL, BLOCK_VALID = 0, 1, 2, 3
 
 
 @_timed("kv_append")
-def kv_append(qkv, B, S_new, H, k_cache, v_cache, len_dev, pos=None, rope=None, q_out=None):
+def kv_append(qkv, B, S_new, H, k_cache, v_cache, len_dev, pos=None, rope=None, q_out=None, qkv_out=False):
     """qkv fp32 (rotated here at pos) or bf16 (already rotated); k / v rows into
-    the cache at [len, len + S_new)."""
+    the cache at [len, len + S_new).  qkv_out: q_out receives the rotated
+    q | k | v rows (the training attention's layout)."""
     _need_cuda(qkv, k_cache, v_cache, len_dev)
     f32 = qkv.dtype == torch.float32
     max_len = k_cache.shape[-2]
     rc = lib().cdk_kv_append(_p(qkv), qkv.stride(0), int(f32), _p(pos), _p(rope), rope.shape[0] if rope is not None
                              else 0, B, S_new, H, _p(k_cache), _p(v_cache), max_len, _p(len_dev), _p(q_out),
-                             q_out.stride(0) if q_out is not None else 0, _stream())
+                             q_out.stride(0) if q_out is not None else 0, int(qkv_out), _stream())
     _check(rc, "kv_append")
     _count(1)
 

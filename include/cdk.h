@@ -315,7 +315,9 @@ int cdk_tokenize_games(const void* vocab, int64_t n_games, const int64_t* game_o
  * cdk_kv_append: qkv_f32 != 0: qkv fp32 [T, ldq] = q | k | v projections (not
  * rotated); q and k are rotated at positions pos[t] (rope [rope_len][32][2] =
  * (cos, sin), the rope_cache of backbone_causal.py:33), q goes to q_out bf16
- * [T, ldo] and k, v to cache rows len + s.  qkv_f32 == 0: qkv bf16 with q, k
+ * [T, ldo] and k, v to cache rows len + s; qkv_out != 0: q_out rows receive the
+ * rotated q | k | v (ldo >= 3 * H * 64), the layout cdk_attn_fwd reads (a
+ * prefill from an empty cache runs the training attention).  qkv_f32 == 0: qkv bf16 with q, k
  * already rotated (a prefill through the training forward): only k, v are
  * written (pos, rope, q_out unused).
  *
@@ -341,7 +343,7 @@ int cdk_tokenize_games(const void* vocab, int64_t n_games, const int64_t* game_o
 enum { CDK_BLOCK_CAUSAL = 0, CDK_BLOCK_ACTIVE = 1, CDK_BLOCK_ALL = 2, CDK_BLOCK_VALID = 3 };
 int cdk_kv_append(const void* qkv, int64_t ldq, int qkv_f32, const int32_t* pos, const float* rope, int64_t rope_len,
                   int64_t B, int64_t S_new, int64_t H, void* k_cache, void* v_cache, int64_t max_len,
-                  const int32_t* len_dev, void* q_out, int64_t ldo, void* stream);
+                  const int32_t* len_dev, void* q_out, int64_t ldo, int qkv_out, void* stream);
 int cdk_decode_attn(const void* q, int64_t ldq, const void* k_cache, const void* v_cache, int64_t max_len,
                     const int32_t* len_dev, int64_t S_new, int64_t B, int64_t H, const uint8_t* valid, int64_t ldv,
                     int block_mode, const uint8_t* active, const int64_t* num_real, const uint8_t* full_mask,

@@ -214,3 +214,35 @@ def test_greedy_generation_matches_oracle():
                 near_ties += 1
         ids = gen[k].numpy().reshape(B, 1)
     assert near_ties <= 2
+
+
+@pytest.mark.parametrize("B,S0", [(2, 40), (12, 48), (3, 256)])
+def test_unpadded_prefill_uses_training_attention(B, S0):
+    """A causal prefill without padding into an empty cache (the training
+    attention path), then incremental steps over the cache it wrote."""
+    cfg = ModelConfig(num_layers=3)
+    max_len = S0 + 4
+    sd = init_reference_weights(cfg, 21)
+    for i in range(cfg.num_layers):
+        for nm in ("q_proj", "k_proj"):
+            sd[f"layers.{i}.attn.{nm}.weight"] = sd[f"layers.{i}.attn.{nm}.weight"] * 4.0
+    bb = D.BatchedBackbone(cfg, batch_size=B, max_seq_len=max_len, state_dict=sd)
+    w = {k: v.float().numpy() for k, v in sd.items()}
+    ob = OD.Batched(w, dict(num_layers=cfg.num_layers, num_heads=cfg.num_heads, embed_dim=cfg.embed_dim,
+                            max_seq_len=cfg.max_seq_len), B, max_len)
+    rng = np.random.default_rng(B * 100 + S0)
+    om = torch.zeros(B, S0, dtype=torch.bool)
+    om[0, 5] = True
+    ov = torch.zeros(B, S0)
+    ov[0, 5] = 0.4
+    kw = dict(ids=torch.from_numpy(rng.integers(0, cfg.vocab_size, (B, S0))), pos=torch.arange(S0).repeat(B, 1),
+              ov=ov, om=om, active=torch.ones(B, dtype=torch.bool), num_real=torch.full((B,), S0))
+    K.get_error()
+    _check(bb.causal_forward(**kw), ob.causal_forward(**{k: v.numpy() for k, v in kw.items()}), 3e-2, 0.998,
+           "prefill")
+    for step in range(2):
+        kw = dict(ids=torch.from_numpy(rng.integers(0, cfg.vocab_size, (B, 1))), pos=torch.full((B, 1), S0 + step),
+                  ov=torch.zeros(B, 1), om=torch.zeros(B, 1, dtype=torch.bool), active=torch.ones(B, dtype=torch.bool))
+        _check(bb.causal_incremental(**kw), ob.causal_incremental(**{k: v.numpy() for k, v in kw.items()}), 3e-2,
+               0.998, f"step {step}")
+    assert K.get_error() == 0
