@@ -155,7 +155,8 @@ def test_train_py_loop_matches_oracle(use_amp):
     scaler.unscale_(opt)
     for n in ("move", "board", "wl", "d"):
         r = float(out_ref[n].detach())
-        assert abs(float(out[n]) - r) <= 1e-2 * max(abs(r), 1e-6), (n, float(out[n]), r)
+        got = float(out[n].detach())
+        assert abs(got - r) <= 1e-2 * max(abs(r), 1e-6), (n, got, r)
     rp = dict(ref.named_parameters())
     for name, p in ours.named_parameters():
         if name.startswith("thinking_policy_head"):
