@@ -24,7 +24,7 @@
 //                 markCausalValidRange, markPrefixValid(Range) and the cache
 //                 length update of forwardImpl).
 // The HBM-bound part is decode_attn: it reads each cache key row once per
-// (sequence, head, 8-query chunk); kv_append and decode_mark are O(new rows).
+// (sequence, head, 16-query chunk); kv_append and decode_mark are O(new rows).
 #include <algorithm>
 #include <cstddef>
 
@@ -41,7 +41,6 @@ using namespace cdk;
 namespace {
 
 constexpr int kHD = 64;      // head dim (embed 1024 / 16 heads)
-constexpr int kQC = 8;       // queries per CTA
 constexpr int kWarps = 4;    // warps per CTA; each walks its own key tiles
 constexpr int kKT = 32;      // keys per warp tile: one key per lane
 
@@ -130,39 +129,41 @@ constexpr int kStages = 3;                      // per-warp ring of key tiles
 constexpr int kTileBytes = kKT * kHD * 2;       // 4 KB: 32 key rows of 128 bytes
 constexpr int kStageBytes = 2 * kTileBytes;     // K tile + V tile
 constexpr int kRingBytes = kWarps * kStages * kStageBytes;
-constexpr int kQBytes = kQC * kHD * 4;
-constexpr int kSmemBytes = kRingBytes + kQBytes + 4 * kWarps * 32 * 4 + kWarps * kStages * 8 + 16 + 1024;
-static_assert(kWarps * kQC * 32 * 8 <= kRingBytes, "merge area fits in the ring");
 
 // 16-byte chunk c of row r of a 128B-swizzled tile (rows of 128 bytes in a
 // 1024-byte-aligned buffer): the TMA SWIZZLE_128B placement.
 __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
-// Grid (ceil(S_new / kQC), H, B), kWarps warps.  Warp w walks key tiles
-// w, w + kWarps, ... of 32 keys; its lane 0 keeps kStages - 1 tiles of K and V
-// in flight by TMA (2-D tiles of the cache viewed as [B*H*max_len, 64] bf16,
-// 128-byte swizzle).  Lane l scores key (tile * 32 + l) from its swizzled K row
-// (conflict-free 16-byte reads; the fp32 query row is a broadcast), the
-// weighted sum reads V row by row (lane l owns output dims 2l, 2l + 1).  Online
-// softmax per query and warp, merged across warps at the end.  A query with no
-// valid key writes zeros.
+// Several new tokens per sequence (multi-token causal steps, padded prefills,
+// prefix / block steps, probes).  Grid (ceil(S_new / 16), H, B), kWarps warps.
+// Warp w walks key tiles w, w + kWarps, ... of 32 keys; its lane 0 keeps
+// kStages - 1 tiles of K and V in flight by TMA (2-D tiles of the cache viewed
+// as [B*H*max_len, 64] bf16, 128-byte swizzle).  Per tile the warp computes the
+// 16 x 32 scores S = Q K^T with mma.sync m16n8k16 (K fragments by ldmatrix from
+// the swizzled tile), applies the mask and an online softmax per query row in
+// registers, and accumulates O += P V (P re-packed from the score fragments
+// as the A operand, V fragments by ldmatrix.trans).  The warps' partial states
+// are merged through shared memory at the end.  A query with no valid key
+// writes zeros.
+constexpr int kMQ = 16;  // queries per CTA (one m16 tile)
+constexpr int kSmemMQ = kRingBytes + kMQ * kHD * 2 + kWarps * kStages * 8 + 16 + 1024;
+static_assert(kWarps * (kMQ * kHD + 2 * kMQ) * 4 <= kRingBytes, "merge area fits in the ring");
+
 __global__ void __launch_bounds__(kWarps * 32, 2)
     decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                        const DecodeAttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
-  float (*qs)[kHD] = reinterpret_cast<float (*)[kHD]>(smem + kRingBytes);
-  float* cm = reinterpret_cast<float*>(smem + kRingBytes + kQBytes);
-  float* cl = cm + kWarps * kQC;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(cl + kWarps * kQC);
+  uint8_t* qtile = smem + kRingBytes;  // [16 rows][128 bytes], swizzled like the K / V tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(qtile + kMQ * kHD * 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kWarps * kStages);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int q0 = blockIdx.x * kQC;
+  const int q0 = blockIdx.x * kMQ;
   const int h = blockIdx.y;
   const long long b = blockIdx.z;
-  const int nq = min(kQC, a.S_new - q0);
+  const int nq = min(kMQ, a.S_new - q0);
   int n_cache = *a.len_dev;
   if (n_cache < 0 || (long long)n_cache + a.S_new > a.max_len) {  // host keeps len + S_new <= max_len
     if (tid == 0) report_error(kErrIndex);
@@ -188,31 +189,31 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       tma_load_2d(wring + k * kStageBytes + kTileBytes, &vmap, &wbar[k], 0, row_base + t0);
     }
   }
-  for (int i = tid; i < kQC * kHD; i += blockDim.x) {
-    const int q = i / kHD, d = i % kHD;
-    float v = 0.f;
-    if (q < nq) v = __bfloat162float(a.q[(b * a.S_new + q0 + q) * a.ldq + h * kHD + d]) * a.scale_log2;
-    qs[q][d] = v;
+  {  // query tile: thread t loads 16 bytes (row t / 8, chunk t % 8); rows past the block are zero
+    const int row = tid >> 3, c = tid & 7;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row < nq) v = *reinterpret_cast<const uint4*>(a.q + (b * a.S_new + q0 + row) * a.ldq + h * kHD + c * 8);
+    *reinterpret_cast<uint4*>(qtile + swz(row, c)) = v;
   }
   __syncthreads();
 
   const bool act = a.active == nullptr || a.active[b] != 0;
   const long long nreal = a.num_real ? a.num_real[b] : (long long)a.S_new;
-  const bool use_valid_new = a.block_mode == CDK_BLOCK_VALID;
+  const int r0 = lane >> 2;           // this thread's rows: r0 and r0 + 8
+  const int cq = (lane & 3) * 2;      // and columns cq, cq + 1 of every 8-wide n tile
 
-  float m[kQC], l[kQC];
-  float2 acc[kQC];
+  uint32_t qa[4][4];
+  {
+    const int mi = lane >> 3;
+    const int row = (mi & 1) * 8 + (lane & 7);
 #pragma unroll
-  for (int q = 0; q < kQC; ++q) {
-    m[q] = -INFINITY;
-    l[q] = 0.f;
-    acc[q] = make_float2(0.f, 0.f);
+    for (int kk = 0; kk < 4; ++kk)
+      ldsm_x4(smem_u32(qtile + swz(row, 2 * kk + (mi >> 1))), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
   }
-  // validity byte of this lane's key, one tile ahead
-  auto valid_of = [&](int j) -> uint8_t {
-    return (j < total && (j < n_cache || use_valid_new)) ? a.valid[b * a.ldv + j] : (uint8_t)0;
-  };
-  uint8_t vcur = n_tiles > 0 ? valid_of(warp * kKT + lane) : 0;
+  float o[8][4];
+#pragma unroll
+  for (int nd = 0; nd < 8; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
 
   for (int k = 0; k < n_tiles; ++k) {
     const int t0 = (warp + k * kWarps) * kKT;
@@ -227,125 +228,158 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       tma_load_2d(wring + sn * kStageBytes, &kmap, &wbar[sn], 0, row_base + tn);
       tma_load_2d(wring + sn * kStageBytes + kTileBytes, &vmap, &wbar[sn], 0, row_base + tn);
     }
-    const uint8_t vnext = k + 1 < n_tiles ? valid_of(t0 + kWarps * kKT + lane) : 0;
-    const uint8_t* kt = wring + st * kStageBytes;
-    const uint8_t* vt = kt + kTileBytes;
-    const int j = t0 + lane;
-    const bool in_cache = j < n_cache;
-    const int jt = j - n_cache;  // index within the new block
-    uint4 kr[8];
+    uint8_t* kt = wring + st * kStageBytes;
+    uint8_t* vt = kt + kTileBytes;
+    if (t0 + kKT > total) {  // keys past the sequence's end: zero V rows so that 0 * V stays 0
+      if (t0 + lane >= total) {
 #pragma unroll
-    for (int c = 0; c < 8; ++c) kr[c] = *reinterpret_cast<const uint4*>(kt + swz(lane, c));
-
-    float p[kQC];
+        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vt + swz(lane, c)) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      __syncwarp();
+    }
+    // S = Q K^T: 4 n tiles of 8 keys x 4 k steps of 16 dims
+    float sc[4][4];
 #pragma unroll
-    for (int q = 0; q < kQC; ++q) {
-      p[q] = 0.f;
-      if (q < nq) {
-        const float* qq = qs[q];
-        float s = 0.f;
+    for (int nt = 0; nt < 4; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t w[4] = {kr[c].x, kr[c].y, kr[c].z, kr[c].w};
-          const float4 qa = *reinterpret_cast<const float4*>(qq + c * 8);
-          const float4 qb = *reinterpret_cast<const float4*>(qq + c * 8 + 4);
-          const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 kf = bf2f(w[e]);
-            s = fmaf(qv[2 * e], kf.x, s);
-            s = fmaf(qv[2 * e + 1], kf.y, s);
-          }
-        }
-        bool ok;
-        if (j >= total) {
-          ok = false;
-        } else if (a.full) {
-          ok = j < a.ldf && a.full[(b * a.S_new + q0 + q) * a.ldf + j] != 0;
-        } else if (in_cache || use_valid_new) {
-          ok = vcur != 0;
-        } else if (a.block_mode == CDK_BLOCK_CAUSAL) {
-          ok = jt <= q0 + q && jt < nreal;
-        } else if (a.block_mode == CDK_BLOCK_ACTIVE) {
-          ok = act;
-        } else {
-          ok = true;
-        }
-        s = ok ? s : -INFINITY;
-        float tmax = s;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
-        const float mnew = fmaxf(m[q], tmax);
-        if (mnew != -INFINITY) {
-          const float pv = ok ? exp2f(s - mnew) : 0.f;
-          float sum = pv;
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-          const float alpha = exp2f(m[q] - mnew);
-          l[q] = l[q] * alpha + sum;
-          acc[q].x *= alpha;
-          acc[q].y *= alpha;
-          m[q] = mnew;
-          p[q] = pv;
-        }
+      for (int kk = 0; kk < 4; kk += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(smem_u32(kt + swz(nt * 8 + (lane & 7), 2 * kk + (lane >> 3))), b0, b1, b2, b3);
+        mma_bf16_16816(sc[nt], qa[kk], b0, b1);
+        mma_bf16_16816(sc[nt], qa[kk + 1], b2, b3);
       }
     }
-    const int nk = min(kKT, total - t0);  // rows past the sequence's keys are never read
-    if (nq == 1) {
-      for (int jj = 0; jj < nk; ++jj) {
-        const float2 v = bf2f(*reinterpret_cast<const uint32_t*>(vt + swz(jj, lane >> 2) + (lane & 3) * 4));
-        const float pj = __shfl_sync(0xffffffffu, p[0], jj);
-        acc[0].x = fmaf(pj, v.x, acc[0].x);
-        acc[0].y = fmaf(pj, v.y, acc[0].y);
-      }
-    } else {
-      for (int jj = 0; jj < nk; ++jj) {
-        const float2 v = bf2f(*reinterpret_cast<const uint32_t*>(vt + swz(jj, lane >> 2) + (lane & 3) * 4));
+    // mask: cache keys share one validity byte per column; new keys depend on the row
+    bool cok[4][2];
 #pragma unroll
-        for (int q = 0; q < kQC; ++q) {
-          if (q < nq) {
-            const float pj = __shfl_sync(0xffffffffu, p[q], jj);
-            acc[q].x = fmaf(pj, v.x, acc[q].x);
-            acc[q].y = fmaf(pj, v.y, acc[q].y);
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = t0 + nt * 8 + cq + e;
+        cok[nt][e] = j < total && (j < n_cache || a.block_mode == CDK_BLOCK_VALID) && a.valid[b * a.ldv + j] != 0;
+      }
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const int row = r0 + rr * 8;
+      const int q = q0 + row;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int j = t0 + nt * 8 + cq + e;
+          bool ok;
+          if (row >= nq || j >= total) {
+            ok = false;
+          } else if (a.full) {
+            ok = j < a.ldf && a.full[(b * a.S_new + q) * a.ldf + j] != 0;
+          } else if (j < n_cache || a.block_mode == CDK_BLOCK_VALID) {
+            ok = cok[nt][e];
+          } else if (a.block_mode == CDK_BLOCK_CAUSAL) {
+            const int jt = j - n_cache;
+            ok = jt <= q && jt < nreal;
+          } else if (a.block_mode == CDK_BLOCK_ACTIVE) {
+            ok = act;
+          } else {
+            ok = true;
           }
+          const float v = ok ? sc[nt][rr * 2 + e] * a.scale_log2 : -INFINITY;
+          sc[nt][rr * 2 + e] = v;
+          mx = fmaxf(mx, v);
         }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mnew = fmaxf(m[rr], mx);
+      if (mnew == -INFINITY) {  // nothing visible to this row yet
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) sc[nt][rr * 2] = sc[nt][rr * 2 + 1] = 0.f;
+      } else {
+        const float alpha = exp2f(m[rr] - mnew);
+        float sum = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float pv = exp2f(sc[nt][rr * 2 + e] - mnew);  // exp2(-inf) = 0
+            sc[nt][rr * 2 + e] = pv;
+            sum += pv;
+          }
+        l[rr] = l[rr] * alpha + sum;
+#pragma unroll
+        for (int nd = 0; nd < 8; ++nd) {
+          o[nd][rr * 2] *= alpha;
+          o[nd][rr * 2 + 1] *= alpha;
+        }
+        m[rr] = mnew;
       }
     }
-    vcur = vnext;
+    // O += P V: P (16 x 32) from the score fragments, 2 k steps of 16 keys
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16(sc[2 * ks][0], sc[2 * ks][1]);
+      pa[1] = pack_bf16(sc[2 * ks][2], sc[2 * ks][3]);
+      pa[2] = pack_bf16(sc[2 * ks + 1][0], sc[2 * ks + 1][1]);
+      pa[3] = pack_bf16(sc[2 * ks + 1][2], sc[2 * ks + 1][3]);
+      const int mi = lane >> 3;
+      const int key = ks * 16 + (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+      for (int nd = 0; nd < 8; nd += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(vt + swz(key, nd + (mi >> 1))), b0, b1, b2, b3);
+        mma_bf16_16816(o[nd], pa, b0, b1);
+        mma_bf16_16816(o[nd + 1], pa, b2, b3);
+      }
+    }
     __syncwarp();
   }
 
-  // Merge the warps' partial softmax states (every issued tile was waited for,
-  // so the ring is free).
-  __syncthreads();
-  float2 (*cacc)[kQC][32] = reinterpret_cast<float2 (*)[kQC][32]>(ring);
+  // Merge the warps' partial states (every issued tile was waited for, so the
+  // ring is free): per warp O [16][64], row max [16], row sum [16].
 #pragma unroll
-  for (int q = 0; q < kQC; ++q) {
-    cacc[warp][q][lane] = acc[q];
-    if (lane == 0) {
-      cm[warp * kQC + q] = m[q];
-      cl[warp * kQC + q] = l[q];
+  for (int rr = 0; rr < 2; ++rr) {
+    l[rr] += __shfl_xor_sync(0xffffffffu, l[rr], 1);
+    l[rr] += __shfl_xor_sync(0xffffffffu, l[rr], 2);
+  }
+  __syncthreads();
+  float* wo = reinterpret_cast<float*>(ring) + warp * (kMQ * kHD + 2 * kMQ);
+#pragma unroll
+  for (int nd = 0; nd < 8; ++nd)
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr)
+      *reinterpret_cast<float2*>(wo + (r0 + rr * 8) * kHD + nd * 8 + cq) = make_float2(o[nd][rr * 2], o[nd][rr * 2 + 1]);
+  if ((lane & 3) == 0) {
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      wo[kMQ * kHD + r0 + rr * 8] = m[rr];
+      wo[kMQ * kHD + kMQ + r0 + rr * 8] = l[rr];
     }
   }
   __syncthreads();
-  for (int i = tid; i < kQC * 32; i += blockDim.x) {
-    const int q = i >> 5, d2 = i & 31;
-    if (q >= nq) continue;
+  for (int i = tid; i < kMQ * (kHD / 2); i += blockDim.x) {
+    const int row = i / (kHD / 2), d2 = i % (kHD / 2);
+    if (row >= nq) continue;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, cm[w * kQC + q]);
+    for (int w = 0; w < kWarps; ++w)
+      M = fmaxf(M, reinterpret_cast<const float*>(ring)[w * (kMQ * kHD + 2 * kMQ) + kMQ * kHD + row]);
     float L = 0.f, ox = 0.f, oy = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) {
-        const float f = exp2f(cm[w * kQC + q] - M);
-        L += cl[w * kQC + q] * f;
-        ox += cacc[w][q][d2].x * f;
-        oy += cacc[w][q][d2].y * f;
+        const float* ww = reinterpret_cast<const float*>(ring) + w * (kMQ * kHD + 2 * kMQ);
+        const float mw = ww[kMQ * kHD + row];
+        const float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
+        L += ww[kMQ * kHD + kMQ + row] * f;
+        const float2 v = *reinterpret_cast<const float2*>(ww + row * kHD + 2 * d2);
+        ox += v.x * f;
+        oy += v.y * f;
       }
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
-    *reinterpret_cast<uint32_t*>(a.out + (b * a.S_new + q0 + q) * a.ldo + h * kHD + 2 * d2) = f2bf2(ox * inv, oy * inv);
+    *reinterpret_cast<uint32_t*>(a.out + (b * a.S_new + q0 + row) * a.ldo + h * kHD + 2 * d2) =
+        f2bf2(ox * inv, oy * inv);
   }
 }
 
@@ -707,7 +741,7 @@ extern "C" int cdk_decode_attn(const void* q, int64_t ldq, const void* k_cache, 
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return -8;
   if (!attr_done[dev]) {
-    cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMQ);
     cudaFuncSetAttribute(decode_attn_1q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem1q);
     cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
     attr_done[dev] = true;
@@ -718,8 +752,9 @@ extern "C" int cdk_decode_attn(const void* q, int64_t ldq, const void* k_cache, 
     decode_attn_1q_kernel<<<grid, kWarps * 32, kSmem1q, reinterpret_cast<cudaStream_t>(stream)>>>(kmap, vmap, a,
                                                                                               (int)n_items);
   } else {
-    dim3 grid((unsigned)((S_new + kQC - 1) / kQC), (unsigned)H, (unsigned)B);
-    decode_attn_kernel<<<grid, kWarps * 32, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(kmap, vmap, a);
+    if (ldq % 8) return -9;  // 16-byte query rows
+    dim3 grid((unsigned)((S_new + kMQ - 1) / kMQ), (unsigned)H, (unsigned)B);
+    decode_attn_kernel<<<grid, kWarps * 32, kSmemMQ, reinterpret_cast<cudaStream_t>(stream)>>>(kmap, vmap, a);
   }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
