@@ -439,15 +439,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (first_of_kt && it > 0) mbar_wait(&sm.bar_epi, (epi_waits++) & 1, abort_flag);
         tc_fence_after();
         #pragma unroll 1
-        for (int kk = 0; kk < 8; ++kk) {  // 128 queries
+        for (int kk = 0; kk < 8; ++kk) {
+          // three independent accumulation chains interleaved: dV, dK over the
+          // 128 queries and dQ over the 128 keys, step kk of each
           const uint32_t acc_kv = (!first_of_kt || kk > 0) ? 1u : 0u;
           const uint64_t a_pt = make_sdesc(ptb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
           const uint64_t a_ds = make_sdesc(dsb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
           umma_f16(tmem + 256, a_pt, make_sdesc(ob + qh * 16384 + kk * 2048, 8192, 1024), id_kn, acc_kv);
           umma_f16(tmem + 320, a_ds, make_sdesc(qb + qh * 16384 + kk * 2048, 8192, 1024), id_kn, acc_kv);
-        }
-        #pragma unroll 1
-        for (int kk = 0; kk < 8; ++kk) {  // 128 keys
           const uint32_t acc_q = (((q_seen >> qh) & 1u) || kk > 0) ? 1u : 0u;
           umma_f16(tmem + 384 + qh * kHd, make_sdesc(dsb + kk * 2048, 16384, 1024),
                    make_sdesc(kb + kt * 16384 + kk * 2048, 8192, 1024), id_nn, acc_q);
