@@ -627,23 +627,50 @@ __global__ void swiglu_f32_kernel(const float* __restrict__ gu, long long ldg, l
   *reinterpret_cast<uint32_t*>(u + t * ldu + f) = f2bf2(a, c);
 }
 
-// Greedy next token per sequence: idx = argmax(logits[r, :ncols]) (lowest
-// index on ties, as torch.argmax), ids[r] = lut ? lut[idx] : idx, and the
-// step's ids appended to hist[*counter][r]; then pos[r] += 1 and *counter += 1.
-// One block: warp w handles rows w, w + 8, ...
-__global__ void head_argmax_kernel(const float* __restrict__ logits, long long ldl, int rows, int ncols,
+// splitmix64 finaliser (Steele, Lea and Flood, "Fast splittable pseudorandom
+// number generators", 2014): a counter-based stream keyed by (seed, step,
+// row, column), so a replayed step draws fresh numbers from the step counter.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Next token per sequence.  temperature <= 0: idx = argmax(logits[r, :ncols])
+// (lowest index on ties, as torch.argmax); otherwise a sample of
+// softmax(logits / temperature) by the Gumbel-max rule, argmax(logit / T + g)
+// with g = -log(-log(u)), u uniform in (0, 1) from the counter-based stream.
+// ids[r] = lut ? lut[idx] : idx; lp_out[r] = log_softmax(logits[r])[idx] (the
+// unscaled log-probability, as the reference records it); the step's ids (and
+// log-probs) appended at row *counter of hist (lp_hist); then pos[r] += 1 and
+// *counter += 1.  One block: warp w handles rows w, w + 8, ...
+__global__ void head_select_kernel(const float* __restrict__ logits, long long ldl, int rows, int ncols,
+                                   float temperature, const uint64_t* __restrict__ seed,
                                    const int64_t* __restrict__ lut, int64_t* __restrict__ ids,
-                                   int64_t* __restrict__ pos, int64_t* __restrict__ hist, int32_t* __restrict__ counter,
-                                   int max_steps) {
+                                   float* __restrict__ lp_out, int64_t* __restrict__ pos, int64_t* __restrict__ hist,
+                                   float* __restrict__ lp_hist, int32_t* __restrict__ counter, int max_steps) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int step = counter ? *counter : 0;
+  const bool sample = temperature > 0.f;
+  const float inv_t = sample ? 1.f / temperature : 0.f;
+  const uint64_t key = mix64((seed ? *seed : 0ull) ^ mix64((uint64_t)step));
+  const bool want_lp = lp_out != nullptr || lp_hist != nullptr;
   for (int r = warp; r < rows; r += blockDim.x >> 5) {
-    float best = -INFINITY;
+    const float* row = logits + (long long)r * ldl;
+    const uint64_t rkey = mix64(key ^ (uint64_t)r);
+    float best = -INFINITY, mx = -INFINITY;
     int bi = 0x7fffffff;
     for (int c = lane; c < ncols; c += 32) {
-      const float v = logits[(long long)r * ldl + c];
-      if (v > best || (v == best && c < bi)) {
-        best = v;
+      const float v = row[c];
+      mx = fmaxf(mx, v);
+      float sc = v;
+      if (sample) {
+        const float u = ((float)(mix64(rkey ^ (uint64_t)c) >> 40) + 0.5f) * (1.f / 16777216.f);
+        sc = v * inv_t - logf(-logf(u));
+      }
+      if (sc > best || (sc == best && c < bi)) {
+        best = sc;
         bi = c;
       }
     }
@@ -655,15 +682,29 @@ __global__ void head_argmax_kernel(const float* __restrict__ logits, long long l
         best = ov;
         bi = oi;
       }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    float lp = 0.f;
+    if (want_lp) {
+      float sum = 0.f;
+      for (int c = lane; c < ncols; c += 32) sum += expf(row[c] - mx);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (bi < ncols) lp = row[bi] - mx - logf(sum);
     }
     if (lane == 0) {
       if (bi >= ncols) bi = 0;  // every logit NaN
       const int64_t id = lut ? lut[bi] : (int64_t)bi;
       ids[r] = id;
+      if (lp_out) lp_out[r] = lp;
       if (pos) pos[r] += 1;
-      if (hist) {
-        if (step < max_steps) hist[(long long)step * rows + r] = id;
-        else report_error(kErrIndex);
+      if (hist || lp_hist) {
+        if (step < max_steps) {
+          if (hist) hist[(long long)step * rows + r] = id;
+          if (lp_hist) lp_hist[(long long)step * rows + r] = lp;
+        } else {
+          report_error(kErrIndex);
+        }
       }
     }
   }
@@ -783,13 +824,15 @@ extern "C" int cdk_swiglu_f32(const float* gu, int64_t ldg, int64_t T, int64_t F
   return e == cudaSuccess ? 0 : (int)e;
 }
 
-extern "C" int cdk_head_argmax(const float* logits, int64_t ldl, int64_t rows, int64_t ncols, const int64_t* lut,
-                               int64_t* ids, int64_t* pos, int64_t* hist, int32_t* counter, int64_t max_steps,
-                               void* stream) {
+extern "C" int cdk_head_select(const float* logits, int64_t ldl, int64_t rows, int64_t ncols, float temperature,
+                               const uint64_t* seed, const int64_t* lut, int64_t* ids, float* lp_out, int64_t* pos,
+                               int64_t* hist, float* lp_hist, int32_t* counter, int64_t max_steps, void* stream) {
   if (rows == 0) return 0;
-  if (!logits || !ids || rows < 0 || ncols <= 0 || ldl < ncols || (hist && !counter)) return -1;
-  head_argmax_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      logits, ldl, (int)rows, (int)ncols, lut, ids, pos, hist, counter, (int)max_steps);
+  if (!logits || !ids || rows < 0 || ncols <= 0 || ldl < ncols || ((hist || lp_hist) && !counter)) return -1;
+  if (!(temperature == temperature)) return -2;  // NaN temperature
+  head_select_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      logits, ldl, (int)rows, (int)ncols, temperature, seed, lut, ids, lp_out, pos, hist, lp_hist, counter,
+      (int)max_steps);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
 }

@@ -315,31 +315,39 @@ class BatchedBackbone:
         return self._forward(self.prefix, ids, pos, ov, om, block_mode=K.BLOCK_ALL)
 
     # -- greedy generation (causalBoardStep, torch_backbone.hpp:141-152) ---------
-    def generate(self, ids, pos, n_steps: int, head: str = "board_head", lut=None, active=None):
-        """Greedy generation on the causal cache, entirely on the device: step k
-        runs one incremental step, the `head` logits of its hidden state, their
-        argmax mapped to the full vocabulary by `lut` (sub-vocabulary index ->
-        token id; None = identity), and feeds that token back as step k+1's
-        input at position + 1.  The first step runs eagerly, the others replay
-        one CUDA graph (no host synchronisation between steps).  ids / pos
-        [B, 1]: the first input token and its position; active [B] (default
-        all).  Returns the generated token ids [n_steps, B] (device)."""
+    def generate(self, ids, pos, n_steps: int, head: str = "board_head", lut=None, active=None,
+                 temperature: float = 0.0, seed: int = 0, return_log_probs: bool = False):
+        """Generation on the causal cache, entirely on the device: step k runs
+        one incremental step, the `head` logits of its hidden state, picks a
+        token (argmax at temperature <= 0, as causalBoardStep; otherwise a
+        sample of softmax(logits / temperature), as sampleBatched, from a
+        counter-based stream keyed by `seed`), maps it to the full vocabulary
+        by `lut` (sub-vocabulary index -> token id; None = identity) and feeds
+        it back as step k+1's input at position + 1.  The first step runs
+        eagerly, the others replay one CUDA graph (no host synchronisation
+        between steps).  ids / pos [B, 1]: the first input token and its
+        position; active [B] (default all).  Returns the generated token ids
+        [n_steps, B] (device), and with return_log_probs also their unscaled
+        log-softmax values [n_steps, B] (the log-probabilities the reference
+        records for GRPO)."""
         B = self.B
         cache = self.causal
         if n_steps <= 0:
-            return torch.empty(0, B, dtype=torch.int64, device=self.device)
+            e = torch.empty(0, B, dtype=torch.int64, device=self.device)
+            return (e, e.float()) if return_log_probs else e
         if cache.len + n_steps > self.max_len:
             raise ValueError(f"cache full: {cache.len} + {n_steps} > {self.max_len}")
-        key = (head, None if lut is None else tuple(int(x) for x in lut))
+        key = (head, None if lut is None else tuple(int(x) for x in lut), float(max(temperature, 0.0)))
         st = self._gen.get(key)
         if st is None:
-            st = self._gen[key] = _GenState(self, head, lut)
+            st = self._gen[key] = _GenState(self, head, lut, float(max(temperature, 0.0)))
         st.ids.copy_(ids.reshape(B, 1))
         st.pos.copy_(pos.reshape(B, 1))
         if active is None:
             st.active.fill_(True)
         else:
             st.active.copy_(active.reshape(B))
+        st.seed.fill_(int(seed) & 0x7FFFFFFFFFFFFFFF)
         st.counter.zero_()
         self._gen_body(st)  # eager: every lazy set-up happens outside capture
         cache.len += 1
@@ -350,12 +358,14 @@ class BatchedBackbone:
                 st.graph.replay()
                 K.LAUNCHES[0] += st.n_launch
                 cache.len += 1
-        return st.hist[:n_steps].clone()
+        out = st.hist[:n_steps].clone()
+        return (out, st.lp_hist[:n_steps].clone()) if return_log_probs else out
 
     def _gen_body(self, st):
         self._incremental_body(self.causal, st.ids, st.pos, None, None, st.active)
         K.gemm(self.last_hidden16.reshape(self.B, -1), st.weight, kind=K.EPI_STORE_F32, out=st.logits, bias=st.bias)
-        K.head_argmax(st.logits, st.ids.view(-1), lut=st.lut, pos=st.pos.view(-1), hist=st.hist, counter=st.counter)
+        K.head_select(st.logits, st.ids.view(-1), temperature=st.temperature, seed=st.seed, lut=st.lut,
+                      pos=st.pos.view(-1), hist=st.hist, lp_hist=st.lp_hist, counter=st.counter)
 
     def _incremental(self, cache, ids, pos, ov, om, active):
         B, S = ids.shape
@@ -433,8 +443,9 @@ class _IncrementalGraph:
 class _GenState:
     """Static buffers and the captured step of a greedy generation loop."""
 
-    def __init__(self, bb: BatchedBackbone, head: str, lut):
+    def __init__(self, bb: BatchedBackbone, head: str, lut, temperature: float = 0.0):
         dev, B = bb.device, bb.B
+        self.temperature = temperature
         self.weight = bb.store.bf16(f"{head}.weight")
         self.bias = bb.store.param(f"{head}.bias")
         V = self.weight.shape[0]
@@ -446,6 +457,8 @@ class _GenState:
         self.active = torch.ones(B, dtype=torch.bool, device=dev)
         self.logits = torch.empty(B, V, device=dev)
         self.hist = torch.zeros(bb.max_len, B, dtype=torch.int64, device=dev)
+        self.lp_hist = torch.zeros(bb.max_len, B, device=dev)
+        self.seed = torch.zeros(1, dtype=torch.int64, device=dev)
         self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
         self.graph = None
         self.n_launch = 0

@@ -576,12 +576,16 @@ def swiglu_f32(gu32, u):
     _count(1)
 
 
-@_timed("head_argmax")
-def head_argmax(logits, ids, lut=None, pos=None, hist=None, counter=None):
-    """ids[r] = lut[argmax(logits[r])]; optionally pos += 1 and the ids appended
-    to hist at row *counter (counter += 1)."""
+@_timed("head_select")
+def head_select(logits, ids, temperature=0.0, seed=None, lut=None, lp=None, pos=None, hist=None, lp_hist=None,
+                counter=None):
+    """ids[r] = lut[argmax(logits[r])] (temperature <= 0) or a sample of
+    softmax(logits[r] / temperature) (seed: device int64 [1]); lp[r] = the
+    unscaled log-softmax at the chosen index; optionally pos += 1 and ids / lp
+    appended to hist / lp_hist at row *counter (counter += 1)."""
     rows, ncols = logits.shape
-    rc = lib().cdk_head_argmax(_p(logits), logits.stride(0), rows, ncols, _p(lut), _p(ids), _p(pos), _p(hist),
-                               _p(counter), hist.shape[0] if hist is not None else 0, _stream())
-    _check(rc, "head_argmax")
+    max_steps = hist.shape[0] if hist is not None else (lp_hist.shape[0] if lp_hist is not None else 0)
+    rc = lib().cdk_head_select(_p(logits), logits.stride(0), rows, ncols, float(temperature), _p(seed), _p(lut),
+                               _p(ids), _p(lp), _p(pos), _p(hist), _p(lp_hist), _p(counter), max_steps, _stream())
+    _check(rc, "head_select")
     _count(1)

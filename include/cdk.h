@@ -355,15 +355,21 @@ int cdk_decode_slots(const uint8_t* override_mask, int64_t n, int32_t* slot, voi
  * [T, ldu]: the SwiGLU of a small decode batch whose gate / up projection ran as
  * a split-K fp32 GEMM (backbone_causal.py:141-143). */
 int cdk_swiglu_f32(const float* gu, int64_t ldg, int64_t T, int64_t F, void* u, int64_t ldu, void* stream);
-/* Greedy next token of a generation loop (causalBoardStep of
- * chessdecoder/cpp/decoder/torch_backbone.hpp:141-152, argmax at temperature 0 in
- * batched_engine.cpp:127-137): idx = argmax over logits[r, :ncols] (lowest index
- * on ties), ids[r] = lut ? lut[idx] : idx (sub-vocabulary -> full vocabulary);
- * optional: pos[r] += 1, hist[*counter * rows + r] = ids[r] and *counter += 1
- * (hist has max_steps rows; beyond them the index error bit is set).  One block,
- * stream-ordered, so a captured step can feed the next one without the host. */
-int cdk_head_argmax(const float* logits, int64_t ldl, int64_t rows, int64_t ncols, const int64_t* lut, int64_t* ids,
-                    int64_t* pos, int64_t* hist, int32_t* counter, int64_t max_steps, void* stream);
+/* Next token of a generation loop (causalBoardStep of
+ * chessdecoder/cpp/decoder/torch_backbone.hpp:141-152; sampleBatched and the
+ * recorded log-probabilities of batched_engine.cpp:125-180).  temperature <= 0:
+ * idx = argmax over logits[r, :ncols] (lowest index on ties); temperature > 0: a
+ * sample of softmax(logits / temperature) (Gumbel-max over a counter-based
+ * random stream keyed by *seed, the step counter, the row and the column; seed
+ * NULL = 0).  ids[r] = lut ? lut[idx] : idx (sub-vocabulary -> full vocabulary);
+ * lp_out[r] = log_softmax(logits[r])[idx], unscaled by the temperature.
+ * Optional: pos[r] += 1; ids / log-probs appended at row *counter of hist /
+ * lp_hist (max_steps rows; beyond them the index error bit is set) and
+ * *counter += 1.  One block, stream-ordered, so a captured step can feed the
+ * next one without the host. */
+int cdk_head_select(const float* logits, int64_t ldl, int64_t rows, int64_t ncols, float temperature,
+                    const uint64_t* seed, const int64_t* lut, int64_t* ids, float* lp_out, int64_t* pos,
+                    int64_t* hist, float* lp_hist, int32_t* counter, int64_t max_steps, void* stream);
 
 #ifdef __cplusplus
 }

@@ -246,3 +246,77 @@ def test_unpadded_prefill_uses_training_attention(B, S0):
         _check(bb.causal_incremental(**kw), ob.causal_incremental(**{k: v.numpy() for k, v in kw.items()}), 3e-2,
                0.998, f"step {step}")
     assert K.get_error() == 0
+
+
+def test_head_select_sampling_and_log_probs():
+    """cdk_head_select: greedy = argmax; at a temperature the sample frequencies
+    over 8192 identical rows follow softmax(logits / T) (each within 0.03, about
+    4 standard deviations); the recorded log-probability is the unscaled
+    log-softmax at the chosen index; the same seed repeats, another seed
+    differs."""
+    g = torch.Generator(device="cuda").manual_seed(3)
+    V, R = 12, 8192
+    base = torch.randn(V, device="cuda", generator=g) * 1.5
+    logits = base.repeat(R, 1).contiguous()
+    ids = torch.empty(R, dtype=torch.int64, device="cuda")
+    lp = torch.empty(R, device="cuda")
+    K.get_error()
+    K.head_select(logits, ids, temperature=0.0, lp=lp)
+    assert bool((ids == int(base.argmax())).all())
+    ref_lp = torch.log_softmax(base, 0)
+    assert torch.allclose(lp, ref_lp[ids], atol=1e-5)
+    for T in (1.0, 0.6):
+        seed = torch.tensor([12345], dtype=torch.int64, device="cuda")
+        K.head_select(logits, ids, temperature=T, seed=seed, lp=lp)
+        freq = torch.bincount(ids, minlength=V).float() / R
+        assert (freq - torch.softmax(base / T, 0)).abs().max().item() < 0.03, T
+        assert torch.allclose(lp, ref_lp[ids], atol=1e-5)
+        again = torch.empty_like(ids)
+        K.head_select(logits, again, temperature=T, seed=seed)
+        assert torch.equal(again, ids)
+        K.head_select(logits, again, temperature=T, seed=seed + 1)
+        assert not torch.equal(again, ids)
+    assert K.get_error() == 0
+
+
+def test_generate_with_temperature():
+    """Sampled generation on the device: ids in the board vocabulary, recorded
+    log-probabilities equal the oracle's log-softmax of the board head at the
+    sampled tokens (teacher-forced), reproducible for a seed."""
+    from chessdecoder_b200 import vocab as V
+    cfg = ModelConfig(num_layers=2)
+    B, max_len, S0, n = 3, 64, 8, 10
+    sd = init_reference_weights(cfg, 17)
+    sd["board_head.weight"] = sd["board_head.weight"] * 10.0
+    w = {k: v.float().numpy() for k, v in sd.items()}
+    lut = V.board_idx_to_full_idx
+    inv = {t: i for i, t in enumerate(lut)}
+    rng = np.random.default_rng(5)
+    prompt = torch.from_numpy(rng.integers(0, cfg.vocab_size, (B, S0)))
+    outs = []
+    for rep in range(2):
+        bb = D.BatchedBackbone(cfg, batch_size=B, max_seq_len=max_len, state_dict=sd)
+        kw = dict(ids=prompt, pos=torch.arange(S0).repeat(B, 1), ov=torch.zeros(B, S0),
+                  om=torch.zeros(B, S0, dtype=torch.bool), active=torch.ones(B, dtype=torch.bool),
+                  num_real=torch.full((B,), S0))
+        bb.causal_forward(**kw)
+        first = torch.full((B, 1), V.token_to_idx["start_pos"])
+        ids, lps = bb.generate(first, torch.full((B, 1), S0), n, head="board_head", lut=lut, temperature=1.0,
+                               seed=99, return_log_probs=True)
+        outs.append((ids.cpu(), lps.cpu()))
+    assert torch.equal(outs[0][0], outs[1][0])
+    ids, lps = outs[0]
+    assert all(int(t) in inv for t in ids.flatten())
+    ob = OD.Batched(w, dict(num_layers=cfg.num_layers, num_heads=cfg.num_heads, embed_dim=cfg.embed_dim,
+                            max_seq_len=cfg.max_seq_len), B, max_len)
+    ob.causal_forward(**{k: v.numpy() for k, v in kw.items()})
+    cur = first.numpy()
+    for k in range(n):
+        h = ob.causal_incremental(cur, np.full((B, 1), S0 + k), np.zeros((B, 1), np.float32), np.zeros((B, 1), bool),
+                                  np.ones(B, bool))
+        logits = torch.from_numpy(h[:, 0] @ w["board_head.weight"].T + w["board_head.bias"])
+        ref = torch.log_softmax(logits, 1)
+        for b in range(B):
+            assert abs(float(lps[k, b]) - float(ref[b, inv[int(ids[k, b])]])) < 0.05 + 0.02 * abs(float(lps[k, b]))
+        cur = ids[k].numpy().reshape(B, 1)
+    assert K.get_error() == 0
