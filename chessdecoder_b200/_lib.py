@@ -96,6 +96,7 @@ SIGNATURES = {
     "cdk_decode_slots": (_int, [_vp, _i64, _vp, _vp]),
     "cdk_swiglu_f32": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _vp]),
     "cdk_head_select": (_int, [_vp, _i64, _i64, _i64, _f32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),
+    "cdk_mish_bf16": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _vp]),
 }
 
 _lib = None

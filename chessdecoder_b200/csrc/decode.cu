@@ -712,6 +712,20 @@ __global__ void head_select_kernel(const float* __restrict__ logits, long long l
   if (threadIdx.x == 0 && counter) *counter = step + 1;
 }
 
+// a[r, c] = mish(z[r, c]) = z * tanh(softplus(z)) in bf16: the hidden layer of
+// the value heads (Linear -> Mish -> Linear, model.py:39-52), softplus passing
+// through above 20 as torch's does.
+__global__ void mish_bf16_kernel(const float* __restrict__ z, long long ldz, long long rows, int cols,
+                                 __nv_bfloat16* __restrict__ a, long long lda) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * cols) return;
+  const long long r = i / cols;
+  const int c = (int)(i % cols);
+  const float x = z[r * ldz + c];
+  const float sp = x > 20.f ? x : log1pf(expf(x));
+  a[r * lda + c] = __float2bfloat16_rn(x * tanhf(sp));
+}
+
 __global__ void decode_slots_kernel(const uint8_t* __restrict__ om, long long n, int32_t* __restrict__ slot) {
   const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (t < n) slot[t] = om[t] ? (int32_t)t : -1;
@@ -833,6 +847,17 @@ extern "C" int cdk_head_select(const float* logits, int64_t ldl, int64_t rows, i
   head_select_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       logits, ldl, (int)rows, (int)ncols, temperature, seed, lut, ids, lp_out, pos, hist, lp_hist, counter,
       (int)max_steps);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+extern "C" int cdk_mish_bf16(const float* z, int64_t ldz, int64_t rows, int64_t cols, void* a, int64_t lda,
+                             void* stream) {
+  if (rows == 0 || cols == 0) return 0;
+  if (!z || !a || rows < 0 || cols < 0 || ldz < cols || lda < cols) return -1;
+  const long long n = rows * cols;
+  mish_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      z, ldz, rows, (int)cols, reinterpret_cast<__nv_bfloat16*>(a), lda);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
 }

@@ -36,7 +36,7 @@ from typing import Optional
 import torch
 
 from . import kernels as K
-from .engine import ModelConfig, ParamStore, init_reference_weights, rope_table
+from .engine import ModelConfig, ParamStore, init_reference_weights, make_d_buckets, make_wl_buckets, rope_table
 
 HEAD_DIM = 64
 
@@ -105,6 +105,7 @@ class BatchedBackbone:
         self.use_graphs = bool(use_graphs) and self.device.type == "cuda"
         self._graphs = {}
         self._gen = {}
+        self._centers = {}
         st, E, F = store, cfg.embed_dim, cfg.ff
         self._layers = []
         for i in range(L):
@@ -360,6 +361,36 @@ class BatchedBackbone:
                 cache.len += 1
         out = st.hist[:n_steps].clone()
         return (out, st.lp_hist[:n_steps].clone()) if return_log_probs else out
+
+    # -- value heads (evalWlHead / evalDHead, batched_engine.cpp:151-180) -------
+    def value_head(self, name: str = "wl_head", h16=None, temperature: float = 0.0, seed: int = 0):
+        """WL or D value head on hidden states h16 [B, E] bf16 (default: the
+        last position of the latest call): Linear -> Mish -> Linear to bucket
+        logits, a bucket picked as in cdk_head_select (argmax, or a sample at a
+        temperature), its unscaled log-probability, and its centre value.
+        Returns (bucket [B] int64, value [B] fp32, log_prob [B] fp32, logits)."""
+        if name not in ("wl_head", "d_head"):
+            raise ValueError("value heads are wl_head and d_head")
+        st, cfg, dev = self.store, self.cfg, self.device
+        if h16 is None:
+            h16 = self.last_hidden16[:, -1, :]
+        B = h16.shape[0]
+        hv, nb = cfg.value_hidden_size, cfg.n_buckets
+        z = torch.empty(B, hv, device=dev)
+        K.gemm(h16, st.bf16(f"{name}.mlp.0.weight"), kind=K.EPI_STORE_F32, out=z, bias=st.param(f"{name}.mlp.0.bias"))
+        a16 = torch.empty(B, hv, device=dev, dtype=torch.bfloat16)
+        K.mish_bf16(z, a16)
+        logits = torch.empty(B, nb, device=dev)
+        K.gemm(a16, st.bf16(f"{name}.mlp.2.weight"), kind=K.EPI_STORE_F32, out=logits,
+               bias=st.param(f"{name}.mlp.2.bias"))
+        idx = torch.empty(B, dtype=torch.int64, device=dev)
+        lp = torch.empty(B, device=dev)
+        seed_t = torch.full((1,), int(seed) & 0x7FFFFFFFFFFFFFFF, dtype=torch.int64, device=dev)
+        K.head_select(logits, idx, temperature=temperature, seed=seed_t, lp=lp)
+        if name not in self._centers:
+            self._centers[name] = (make_wl_buckets(cfg.n_buckets, cfg.wl_sigma) if name == "wl_head"
+                                   else make_d_buckets(cfg.n_buckets)).to(dev)
+        return idx, self._centers[name][idx], lp, logits
 
     def _gen_body(self, st):
         self._incremental_body(self.causal, st.ids, st.pos, None, None, st.active)

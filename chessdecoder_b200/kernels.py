@@ -589,3 +589,11 @@ def head_select(logits, ids, temperature=0.0, seed=None, lut=None, lp=None, pos=
                                _p(ids), _p(lp), _p(pos), _p(hist), _p(lp_hist), _p(counter), max_steps, _stream())
     _check(rc, "head_select")
     _count(1)
+
+
+@_timed("mish_bf16")
+def mish_bf16(z, a):
+    """a = mish(z) in bf16 (z fp32 [rows, cols])."""
+    rows, cols = z.shape
+    _check(lib().cdk_mish_bf16(_p(z), z.stride(0), rows, cols, _p(a), a.stride(0), _stream()), "mish_bf16")
+    _count(1)

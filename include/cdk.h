@@ -370,6 +370,10 @@ int cdk_swiglu_f32(const float* gu, int64_t ldg, int64_t T, int64_t F, void* u, 
 int cdk_head_select(const float* logits, int64_t ldl, int64_t rows, int64_t ncols, float temperature,
                     const uint64_t* seed, const int64_t* lut, int64_t* ids, float* lp_out, int64_t* pos,
                     int64_t* hist, float* lp_hist, int32_t* counter, int64_t max_steps, void* stream);
+/* a[r, c] = mish(z[r, c]) (bf16 out): the hidden layer of the WL / D value heads
+ * (chessdecoder/models/model.py:39-52) as the decoder engine evaluates them on a
+ * step's hidden states (evalWlHead / evalDHead, batched_engine.cpp:151-180). */
+int cdk_mish_bf16(const float* z, int64_t ldz, int64_t rows, int64_t cols, void* a, int64_t lda, void* stream);
 
 #ifdef __cplusplus
 }

@@ -320,3 +320,41 @@ def test_generate_with_temperature():
             assert abs(float(lps[k, b]) - float(ref[b, inv[int(ids[k, b])]])) < 0.05 + 0.02 * abs(float(lps[k, b]))
         cur = ids[k].numpy().reshape(B, 1)
     assert K.get_error() == 0
+
+
+def test_value_heads_match_oracle():
+    """WL / D value heads on the last hidden state (evalWlHead / evalDHead):
+    bucket logits against Linear -> Mish -> Linear on the oracle's hidden state,
+    the greedy bucket (unless a near-tie), its log-probability and centre value."""
+    from chessdecoder_b200.engine import make_d_buckets, make_wl_buckets
+    cfg = ModelConfig(num_layers=2)
+    B, S0 = 4, 12
+    sd = init_reference_weights(cfg, 23)
+    for name in ("wl_head", "d_head"):
+        sd[f"{name}.mlp.2.weight"] = sd[f"{name}.mlp.2.weight"] * 8.0
+    bb = D.BatchedBackbone(cfg, batch_size=B, max_seq_len=32, state_dict=sd)
+    w = {k: v.float().numpy() for k, v in sd.items()}
+    ob = OD.Batched(w, dict(num_layers=cfg.num_layers, num_heads=cfg.num_heads, embed_dim=cfg.embed_dim,
+                            max_seq_len=cfg.max_seq_len), B, 32)
+    rng = np.random.default_rng(6)
+    kw = dict(ids=torch.from_numpy(rng.integers(0, cfg.vocab_size, (B, S0))), pos=torch.arange(S0).repeat(B, 1),
+              ov=torch.zeros(B, S0), om=torch.zeros(B, S0, dtype=torch.bool), active=torch.ones(B, dtype=torch.bool),
+              num_real=torch.full((B,), S0))
+    bb.causal_forward(**kw)
+    h = ob.causal_forward(**{k: v.numpy() for k, v in kw.items()})[:, -1]
+    K.get_error()
+    for name, centers in (("wl_head", make_wl_buckets(cfg.n_buckets, cfg.wl_sigma)), ("d_head", make_d_buckets())):
+        idx, val, lp, logits = bb.value_head(name)
+        z = torch.from_numpy(h @ w[f"{name}.mlp.0.weight"].T + w[f"{name}.mlp.0.bias"])
+        a = z * torch.tanh(torch.nn.functional.softplus(z))
+        ref = a @ torch.from_numpy(w[f"{name}.mlp.2.weight"]).T + torch.from_numpy(w[f"{name}.mlp.2.bias"])
+        _check(logits, ref, 3e-2, 0.998, name)
+        ref_lp = torch.log_softmax(ref, 1)
+        idx, val, lp = idx.cpu(), val.cpu(), lp.cpu()
+        for b in range(B):
+            best = int(ref[b].argmax())
+            if int(idx[b]) != best:
+                assert ref[b, best] - ref[b, int(idx[b])] < 0.02 * ref[b].std(), (name, b)
+            assert abs(float(lp[b]) - float(ref_lp[b, int(idx[b])])) < 0.05 + 0.02 * abs(float(lp[b]))
+            assert float(val[b]) == float(centers[int(idx[b])])
+    assert K.get_error() == 0
