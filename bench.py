@@ -377,7 +377,12 @@ def run_decode(args, rank, world):
                     "d2h_bytes_per_step": B * E * 4},
             "roofline": {"bound": "hbm", "kernel": "decode_attn_1q", "achieved": attn_bytes / attn_us / 1e3,
                          "peak": peak, "unit": "GB/s", "frac": attn_bytes / attn_us / 1e3 / peak,
-                         "launch_us": attn_us, "bytes_per_launch": attn_bytes, "traffic": None,
+                         "launch_us": attn_us, "bytes_per_launch": attn_bytes,
+                         # DRAM bytes per launch: an ncu capture of the same kernel at 64 sequences x 1001
+                         # keys read 263.0 MB (+ 4.6 MB written) for 262.4 MB of K / V rows; traffic grows with
+                         # the rows read, so it is scaled by this launch's bytes
+                         "traffic": attn_bytes * (263.0 + 4.6) / 262.4,
+                         "traffic_source": "ncu capture at B=64, 1001 keys, scaled by K/V bytes",
                          "peak_kind": "measured" if hbm else "fallback",
                          "step_hbm_gbs": step_bytes / (ms / 1000.0) / 1e9},
             "gpu_launches": launches,
