@@ -511,6 +511,8 @@ def main():
     K.OP_TIMER = None
     launches = K.LAUNCHES[0] // args.steps
     dev_ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    # a bounded device wait that gave up (or an out-of-range index) invalidates the run
+    device_error = int(max_over_ranks(float(K.get_error())))
     tokens_step = args.batch * args.seq * world
     value = tokens_step / (dev_ms / 1000.0)
     gemm_stats = gemm_timer.summary(detail=args.detail)
@@ -598,6 +600,7 @@ def main():
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step":
                         d2h // args.steps, "ms_per_step": e2e_ms},
                 "gpu_launches": launches,
+                "device_error_flags": device_error,
                 "host_enqueue_ms_per_step": host_enqueue_ms,
                 "roofline": roofline,
                 "clocks": clocks,
