@@ -241,7 +241,8 @@ def test_soft_bucket_loss_kernel_matches_oracle():
     lc = logits.cuda().requires_grad_(True)
     v = soft_bucket_loss(lc, tgt.cuda(), c.cuda(), valid.cuda())
     v.backward()
-    assert abs(float(v) - float(r)) <= 1e-5 * max(1.0, abs(float(r)))
+    vf, rf = float(v.detach()), float(r.detach())
+    assert abs(vf - rf) <= 1e-5 * max(1.0, abs(rf))
     assert torch.allclose(lc.grad.cpu(), lr_.grad, atol=1e-6, rtol=1e-4)
     # no valid rows -> constant 0 without a graph
     z = soft_bucket_loss(lc, tgt.cuda(), c.cuda(), torch.zeros(n, dtype=torch.bool, device="cuda"))
