@@ -91,3 +91,17 @@ def test_ops_refuse_cpu_tensors():
     x = torch.zeros(4, 1024)
     with pytest.raises(RuntimeError):
         kernels.rmsnorm_fwd(x, torch.ones(1024))
+
+
+def test_ctypes_signatures_match_header_arity():
+    """Every C-ABI declaration in include/cdk.h has as many parameters as the
+    ctypes binding in chessdecoder_b200/_lib.py passes (a mismatch would shift
+    every later argument silently)."""
+    from chessdecoder_b200 import _lib
+    header = (ROOT / "include" / "cdk.h").read_text()
+    header = re.sub(r"/\*.*?\*/", "", header, flags=re.S)
+    for m in re.finditer(r"\b(cdk_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", header):
+        name, params = m.group(1), " ".join(m.group(2).split())
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert name in _lib.SIGNATURES, name
+        assert len(_lib.SIGNATURES[name][1]) == n, (name, n, len(_lib.SIGNATURES[name][1]))
