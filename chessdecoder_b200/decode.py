@@ -352,7 +352,11 @@ class BatchedBackbone:
         st.counter.zero_()
         self._gen_body(st)  # eager: every lazy set-up happens outside capture
         cache.len += 1
-        if n_steps > 1:
+        if n_steps > 1 and not self.use_graphs:
+            for _ in range(n_steps - 1):
+                self._gen_body(st)
+                cache.len += 1
+        elif n_steps > 1:
             if st.graph is None:
                 st.capture(self)
             for _ in range(n_steps - 1):

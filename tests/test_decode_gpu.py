@@ -170,10 +170,12 @@ def test_prefill_rows_above_split_threshold():
     assert K.get_error() == 0
 
 
-def test_greedy_generation_matches_oracle():
-    """Device-side greedy generation through the board head (causalBoardStep):
-    each generated token, fed back teacher-forced into the oracle, is the
-    oracle's argmax unless the oracle's top-2 margin is a near-tie."""
+@pytest.mark.parametrize("use_graphs", [True, False])
+def test_greedy_generation_matches_oracle(use_graphs):
+    """Device-side greedy generation through the board head (causalBoardStep),
+    replayed from a CUDA graph or run eagerly: each generated token, fed back
+    teacher-forced into the oracle, is the oracle's argmax unless the oracle's
+    top-2 margin is a near-tie."""
     from chessdecoder_b200 import vocab as V
     cfg = ModelConfig(num_layers=4)
     B, max_len, S0, n = 3, 48, 10, 12
@@ -182,7 +184,7 @@ def test_greedy_generation_matches_oracle():
     for i in range(cfg.num_layers):
         for nm in ("q_proj", "k_proj"):
             sd[f"layers.{i}.attn.{nm}.weight"] = sd[f"layers.{i}.attn.{nm}.weight"] * 4.0
-    bb = D.BatchedBackbone(cfg, batch_size=B, max_seq_len=max_len, state_dict=sd)
+    bb = D.BatchedBackbone(cfg, batch_size=B, max_seq_len=max_len, state_dict=sd, use_graphs=use_graphs)
     w = {k: v.float().numpy() for k, v in sd.items()}
     ob = OD.Batched(w, dict(num_layers=cfg.num_layers, num_heads=cfg.num_heads, embed_dim=cfg.embed_dim,
                             max_seq_len=cfg.max_seq_len), B, max_len)
