@@ -639,8 +639,9 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
 
 // Next token per sequence.  temperature <= 0: idx = argmax(logits[r, :ncols])
 // (lowest index on ties, as torch.argmax); otherwise a sample of
-// softmax(logits / temperature) by the Gumbel-max rule, argmax(logit / T + g)
-// with g = -log(-log(u)), u uniform in (0, 1) from the counter-based stream.
+// softmax(clamp(logits, -1e4, 1e4) / temperature) by the Gumbel-max rule,
+// argmax(logit / T + g) with g = -log(-log(u)), u uniform in (0, 1) from the
+// counter-based stream.
 // ids[r] = lut ? lut[idx] : idx; lp_out[r] = log_softmax(logits[r])[idx] (the
 // unscaled log-probability, as the reference records it); the step's ids (and
 // log-probs) appended at row *counter of hist (lp_hist); then pos[r] += 1 and
@@ -666,8 +667,13 @@ __global__ void head_select_kernel(const float* __restrict__ logits, long long l
       mx = fmaxf(mx, v);
       float sc = v;
       if (sample) {
-        const float u = ((float)(mix64(rkey ^ (uint64_t)c) >> 40) + 0.5f) * (1.f / 16777216.f);
-        sc = v * inv_t - logf(-logf(u));
+        // u = (k + 0.5) / 2^23 for a 23-bit k: exact in fp32 and strictly
+        // inside (0, 1), so -log(-log(u)) is finite for every draw.  The
+        // logit is clamped to [-1e4, 1e4] before the temperature (the
+        // reference's sampler clamps before its softmax); the recorded
+        // log-probability below uses the unclamped logits.
+        const float u = ((float)(mix64(rkey ^ (uint64_t)c) >> 41) + 0.5f) * (1.f / 8388608.f);
+        sc = fminf(fmaxf(v, -1e4f), 1e4f) * inv_t - logf(-logf(u));
       }
       if (sc > best || (sc == best && c < bi)) {
         best = sc;

@@ -216,9 +216,14 @@ extern "C" int cdk_adamw(float* p, const float* g, float* m, float* v, void* p_b
   h.inv_bc2_sqrt = (float)(1.0 / sqrt(bc2));
   h.max_norm = max_norm;
   h.grad_scale = grad_scale;
+  // SM count per device, looked up on the first call on that device
+  static int sm_count[64] = {0};
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (dev >= 0 && dev < 64) {
+    if (sm_count[dev] == 0) cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (sm_count[dev] > 0) sms = sm_count[dev];
+  }
   long long blocks = (n / 4 + 255) / 256;
   if (blocks > (long long)sms * 8) blocks = (long long)sms * 8;
   if (blocks < 1) blocks = 1;

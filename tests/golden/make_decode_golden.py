@@ -1,9 +1,9 @@
 """Generates tests/golden/decode_reference.pt from the reference's exported
 KV-cache module (chessdecoder/export/backbone_causal.py, ``BackboneCausal``,
 which imports only torch).  Run where the ChessDecoder repository is mounted
-(default /root/reference, or REFERENCE_ROOT):
+(its root given by the REFERENCE_ROOT environment variable, required):
 
-    python tests/golden/make_decode_golden.py
+    REFERENCE_ROOT=<ChessDecoder checkout> python tests/golden/make_decode_golden.py
 
 The C++ ``BatchedBackbone`` (chessdecoder/cpp/decoder/batched_backbone.cpp)
 that drives the module cannot run here (it needs libtorch and a TorchScript
@@ -23,7 +23,14 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+
+
+def reference_root() -> Path:
+    """The ChessDecoder checkout named by REFERENCE_ROOT (required)."""
+    if not os.environ.get("REFERENCE_ROOT"):
+        raise SystemExit("set REFERENCE_ROOT to the root of the ChessDecoder repository")
+    return Path(os.environ["REFERENCE_ROOT"])
+
 
 CONFIG = dict(num_layers=2, num_heads=2, head_dim=64, embed_dim=128, d_ff=256, vocab_size=64, max_seq_len=64,
               num_fourier_freq=16)
@@ -180,7 +187,7 @@ def scenario(B, V, seed):
 
 
 def main():
-    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(reference_root()))
     from chessdecoder.export.backbone_causal import BackboneCausal
     cfg = CONFIG
     model = BackboneCausal(cfg["num_layers"], cfg["num_heads"], cfg["head_dim"], cfg["embed_dim"], cfg["d_ff"],

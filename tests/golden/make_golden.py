@@ -1,9 +1,9 @@
 """Generates the golden fixtures in this directory from the reference code.
 
-Run in a container where the ChessDecoder repository is mounted (default
-/root/reference, or the REFERENCE_ROOT environment variable):
+Run where the ChessDecoder repository is mounted, its root given by the
+REFERENCE_ROOT environment variable (required):
 
-    python tests/golden/make_golden.py
+    REFERENCE_ROOT=<ChessDecoder checkout> python tests/golden/make_golden.py
 
 Only reference modules that import without torchtune / python-chess are
 executed:
@@ -36,12 +36,19 @@ from pathlib import Path
 
 import torch
 
-REF = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+
+
+def reference_root() -> Path:
+    """The ChessDecoder checkout named by REFERENCE_ROOT (required)."""
+    if not os.environ.get("REFERENCE_ROOT"):
+        raise SystemExit("set REFERENCE_ROOT to the root of the ChessDecoder repository")
+    return Path(os.environ["REFERENCE_ROOT"])
+
 OUT = Path(__file__).resolve().parent
 
 
 def _extract_model_defs():
-    src = (REF / "chessdecoder/models/model.py").read_text()
+    src = (reference_root() / "chessdecoder/models/model.py").read_text()
     tree = ast.parse(src)
     keep = []
     for node in tree.body:
@@ -55,7 +62,7 @@ def _extract_model_defs():
                     keep.append(item)
     mod = ast.Module(body=keep, type_ignores=[])
     ns = {"torch": torch, "nn": torch.nn, "math": math}
-    exec(compile(mod, str(REF / "chessdecoder/models/model.py"), "exec"), ns)
+    exec(compile(mod, str(reference_root() / "chessdecoder/models/model.py"), "exec"), ns)
     return ns
 
 
@@ -66,7 +73,7 @@ def rope_cache_torchtune(max_seq_len, dim, base=10000.0):
 
 
 def main():
-    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(reference_root()))
     from chessdecoder.models import vocab as V
     from chessdecoder.export.backbone_causal import BackboneCausal
     from chessdecoder.utils import training as T

@@ -1,8 +1,9 @@
 """Generates tests/golden/rl_reference.pt from the reference's GRPO functions
 (chessdecoder/rl/grpo.py imports only torch).  Run where the ChessDecoder
-repository is mounted (default /root/reference, or REFERENCE_ROOT):
+repository is mounted, its root given by the REFERENCE_ROOT environment
+variable (required):
 
-    python tests/golden/make_rl_golden.py
+    REFERENCE_ROOT=<ChessDecoder checkout> python tests/golden/make_rl_golden.py
 """
 from __future__ import annotations
 
@@ -12,11 +13,18 @@ from pathlib import Path
 
 import torch
 
-REF = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+
+
+def reference_root() -> Path:
+    """The ChessDecoder checkout named by REFERENCE_ROOT (required)."""
+    if not os.environ.get("REFERENCE_ROOT"):
+        raise SystemExit("set REFERENCE_ROOT to the root of the ChessDecoder repository")
+    return Path(os.environ["REFERENCE_ROOT"])
+
 
 
 def main():
-    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(reference_root()))
     from chessdecoder.rl import grpo as G
     g = torch.Generator().manual_seed(7)
     N, S = 6, 40

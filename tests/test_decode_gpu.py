@@ -281,6 +281,24 @@ def test_head_select_sampling_and_log_probs():
     assert K.get_error() == 0
 
 
+def test_head_select_never_samples_masked_columns():
+    """Columns masked to -1e9 (illegal moves) are never sampled: about 1e9
+    masked (row, column) draws across 64 seeds, where a uniform that rounded
+    to 1 (a Gumbel term of +inf, probability 2^-24 per draw) would pick one."""
+    R, V, legal = 8192, 1924, 12
+    g = torch.Generator(device="cuda").manual_seed(9)
+    logits = torch.full((R, V), -1e9, device="cuda")
+    cols = torch.randperm(V, generator=g, device="cuda")[:legal]
+    logits[:, cols] = torch.randn(R, legal, device="cuda", generator=g)
+    ok = torch.zeros(V, dtype=torch.bool, device="cuda")
+    ok[cols] = True
+    ids = torch.empty(R, dtype=torch.int64, device="cuda")
+    for s in range(64):
+        K.head_select(logits, ids, temperature=1.0, seed=torch.tensor([1000 + s], dtype=torch.int64, device="cuda"))
+        assert bool(ok[ids].all()), s
+    assert K.get_error() == 0
+
+
 def test_generate_with_temperature():
     """Sampled generation on the device: ids in the board vocabulary, and the
     recorded log-probabilities equal the oracle's log-softmax of the board head

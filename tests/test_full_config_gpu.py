@@ -1,0 +1,111 @@
+"""Training-step parity at the benchmarked model size.
+
+The B200 step against the fp32 oracle step (oracle/step.py, a restatement of
+chessdecoder/train/train.py:157-253) at the reference's default pretraining
+model -- E=1024, 16 heads, 12 layers, d_ff=1536, S=256
+(chessdecoder/train/config.yaml:8-20; chessdecoder/models/model.py:75-136) --
+on the same seeded synthetic batch and the same weights.  The oracle runs in
+fp32 on the GPU (TF32 off), so the full batch is cheap.
+
+Gates:
+* bf16, B=64 (the benchmarked batch): each loss within 1e-2 relative, every
+  parameter gradient cosine >= 0.999, board and move argmax agreement
+  >= 99.9% at a briefly trained checkpoint (30 oracle steps).  At random init
+  the full-size model's logits are nearly flat (top-2 margins of a few 1e-3),
+  so there every disagreement must be an oracle near-tie (margin < 0.02).
+"""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+FULL = dict(embed_dim=1024, num_heads=16, num_layers=12, max_seq_len=256, d_ff=1536)
+
+
+def cosine(a, b):
+    a, b = a.double().flatten(), b.double().flatten()
+    return (a @ b / (a.norm() * b.norm()).clamp_min(1e-30)).item()
+
+
+def _top2_margin(logits):
+    t = logits.detach().float().topk(2, dim=-1).values
+    return t[..., 0] - t[..., 1]
+
+
+def _oracle(kw, seed=0, pretrain_steps=0, pretrain_batch=8, data_seed=3):
+    """fp32 oracle on the GPU, seeded like the reference's constructor; with
+    pretrain_steps > 0 it is first trained on its own synthetic stream."""
+    from chessdecoder_b200 import data
+    from chessdecoder_b200.engine import ModelConfig
+    from oracle.model import OracleChessDecoder
+    from oracle.step import train_step
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    cfg = ModelConfig(**kw)
+    torch.manual_seed(seed)
+    oracle = OracleChessDecoder(cfg.vocab_size, **kw).cuda()
+    if pretrain_steps:
+        opt = torch.optim.AdamW(oracle.parameters(), lr=1e-3, weight_decay=0.1)
+        for b in data.synthetic_batches(pretrain_steps, pretrain_batch, cfg.max_seq_len, seed=data_seed + 100):
+            train_step(oracle, opt, b)
+        del opt
+    oracle.zero_grad(set_to_none=True)
+    return cfg, oracle
+
+
+def compare(step, oracle, batch, loss_tol):
+    """Runs both steps on `batch`; returns (per-loss (got, ref), per-tensor
+    gradient cosines, board / move argmax agreement and the near-tie check)."""
+    from chessdecoder_b200.engine import prepare_batch
+    from oracle.step import step_losses
+    out = step_losses(oracle, batch)
+    out["total"].backward()
+    db = prepare_batch(batch, "cuda")
+    metrics = {"board_argmax": torch.empty(db.B * db.S, dtype=torch.int32, device="cuda"),
+               "move_argmax": torch.empty(max(db.prow.numel(), 1), dtype=torch.int32, device="cuda")}
+    losses = step.forward_backward(db, metrics).cpu()
+    res = {"loss": {}, "cos": {}}
+    for i, n in enumerate(["move", "board", "wl", "d"]):
+        res["loss"][n] = (float(losses[i]), float(out[n].detach()))
+    rp = dict(oracle.named_parameters())
+    for name in step.store.names():
+        rg = rp[name].grad
+        res["cos"][name] = cosine(step.store.grad_of(name), rg) if rg is not None else float("nan")
+    bm = out["board_mask"].reshape(-1)
+    ba = metrics["board_argmax"].long()[bm]
+    bo = out["board_argmax"].reshape(-1)[bm]
+    mm = out["move_mask"].reshape(-1)
+    ma = metrics["move_argmax"][: int(mm.sum())].long()
+    mo = out["move_argmax"].reshape(-1)[mm]
+    res["agree_board"] = (ba == bo).float().mean().item()
+    res["agree_move"] = (ma == mo).float().mean().item()
+    bl = out["board_logits"].reshape(-1, out["board_logits"].shape[-1])[bm]
+    ml = out["move_logits"].reshape(-1, out["move_logits"].shape[-1])[mm]
+    res["board_ties_only"] = bool((_top2_margin(bl)[ba != bo] < 0.02).all())
+    res["move_ties_only"] = bool((_top2_margin(ml)[ma != mo] < 0.02).all())
+    return res
+
+
+def check(res, loss_tol, cos_min):
+    for n, (got, ref) in res["loss"].items():
+        assert abs(got - ref) <= loss_tol * max(abs(ref), 1e-6), (n, got, ref)
+    worst = sorted(res["cos"].items(), key=lambda kv: kv[1])[:5]
+    assert all(c >= cos_min for c in res["cos"].values()), worst
+
+
+@pytest.mark.parametrize("pretrain", [0, 30])
+def test_full_config_bf16_step_matches_oracle(pretrain):
+    from chessdecoder_b200 import data, kernels
+    from chessdecoder_b200.engine import TrainStep
+    cfg, oracle = _oracle(FULL, pretrain_steps=pretrain)
+    sd = {k: v.detach().cpu().clone() for k, v in oracle.state_dict().items()}
+    step = TrainStep(cfg, device="cuda", state_dict=sd)
+    batch = data.synthetic_batches(1, 64, cfg.max_seq_len, seed=3)[0]
+    res = compare(step, oracle, batch, 1e-2)
+    check(res, 1e-2, 0.999)
+    if pretrain:
+        assert res["agree_board"] >= 0.999, res["agree_board"]
+        assert res["agree_move"] >= 0.999, res["agree_move"]
+    else:
+        assert res["board_ties_only"] and res["move_ties_only"], (res["agree_board"], res["agree_move"])
+    assert kernels.get_error() == 0
