@@ -1115,6 +1115,7 @@ extern "C" int cdk_attn_prefix_meta(const int32_t* bid, int64_t nseq_prefix, int
 static int attn_path() {
   const char* v = getenv("CDK_ATTN_PATH");
   if (v && v[0] == 't' && v[1] == 'i') return 2;  // tiled
+  if (v && v[0] == 't' && v[1] == 'c') return 4;  // one CTA per (query tile, head, sequence) tcgen05 kernels
   if (v && v[0] == 's') return 1;                  // seq (mma.sync)
   if (v && v[0] == 'l') return 3;                  // tcgen05 long-sequence kernels at any S
   return 0;                                        // tcgen05
@@ -1123,6 +1124,8 @@ static bool long_path(int64_t S) { return (S > kSeqMax && attn_path() == 0) || a
 static bool seq_path_enabled() { return attn_path() != 2; }
 
 namespace cdk {
+int launch_attn_fwd_pst(const void* qkv, void* out, float* lse, int64_t nseq, int64_t n_causal, int64_t S,
+                        int64_t H, const int32_t* bid, const int32_t* meta, cudaStream_t stream);
 int launch_attn_fwd_tc(const void* qkv, void* out, float* lse, int64_t nseq, int64_t n_causal, int64_t S, int64_t H,
                        const int32_t* bid, const int32_t* meta, cudaStream_t stream);
 int launch_attn_fwd_long(const void* qkv, void* out, float* lse, int64_t nseq, int64_t n_causal, int64_t S,
@@ -1160,6 +1163,9 @@ extern "C" int cdk_attn_fwd(const void* qkv, void* out, float* lse, int64_t nseq
   a.nseq = (int)nseq;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (S <= kSeqMax && attn_path() == 0) {
+    return launch_attn_fwd_pst(qkv, out, lse, nseq, n_causal, S, H, bid, meta, s);
+  }
+  if (S <= kSeqMax && attn_path() == 4) {
     return launch_attn_fwd_tc(qkv, out, lse, nseq, n_causal, S, H, bid, meta, s);
   }
   if (long_path(S)) {
@@ -1230,7 +1236,7 @@ extern "C" int cdk_attn_bwd_ws(const void* qkv, const void* out, const void* dou
   a.nseq = (int)nseq;
   dim3 grid((unsigned)a.nt, (unsigned)H, (unsigned)nseq);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (S <= kSeqMax && attn_path() == 0)
+  if (S <= kSeqMax && (attn_path() == 0 || attn_path() == 4))
     return launch_attn_bwd_tc(qkv, out, dout, lse, dqkv, nseq, n_causal, S, H, bid, meta, rope, s);
   if (long_path(S) && workspace != nullptr && S % 4 == 0) {
     if (workspace_bytes < cdk_attn_bwd_workspace(nseq, S, H) || (reinterpret_cast<uintptr_t>(workspace) & 15))

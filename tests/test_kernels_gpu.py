@@ -210,12 +210,16 @@ def ref_attention(qkv, nseq, n_causal, S, H, bid):
     return o.transpose(1, 2).reshape(nseq * S, H * 64)
 
 
-@pytest.fixture(params=["tc", "seq", "tiled", "long"])
+@pytest.fixture(params=["default", "tc", "seq", "tiled", "long"])
 def attn_path(request, monkeypatch):
-    """Every attention implementation: tcgen05 (S <= 256), mma.sync
+    """Every attention implementation: the default (persistent tcgen05 forward
+    for S <= 256), tcgen05 with one CTA per query tile (S <= 256), mma.sync
     sequence-resident (S <= 256), mma.sync tiled (any S) and the tcgen05
     long-sequence kernels forced at short S."""
-    monkeypatch.setenv("CDK_ATTN_PATH", request.param)
+    if request.param == "default":
+        monkeypatch.delenv("CDK_ATTN_PATH", raising=False)
+    else:
+        monkeypatch.setenv("CDK_ATTN_PATH", request.param)
     return request.param
 
 
@@ -252,20 +256,24 @@ def test_attention_fwd_bwd(K, attn_path, S, nseq, n_causal):
 
 @pytest.mark.parametrize("S,nseq,n_causal,H", [(256, 40, 20, 16), (100, 64, 32, 8), (136, 48, 16, 8)])
 def test_attention_bwd_many_items(K, S, nseq, n_causal, H):
-    """The S <= 256 backward over more (head, sequence) items than the GPU has
-    SMs (several waves), mixed causal / block-prefix, full and partial tiles;
-    every output row written (the output starts as NaN)."""
+    """The S <= 256 forward and backward over more (head, sequence) items than
+    the GPU has SMs (several waves; several items per CTA of the persistent
+    forward), mixed causal / block-prefix, full and partial tiles; every output
+    row and log-sum-exp written (the outputs start as NaN)."""
     E = H * 64
     gen = torch.Generator().manual_seed(S * 3 + nseq)
     qkv = (torch.randn(nseq * S, 3 * E, generator=gen) * 0.8).to(DEV).to(torch.bfloat16)
     bid = make_bid(nseq - n_causal, S, gen)
     bid32 = bid.to(torch.int32).to(DEV).contiguous()
     meta = K.attn_meta(bid32, S)
-    out = torch.empty(nseq * S, E, device=DEV, dtype=torch.bfloat16)
-    lse = torch.empty(nseq * H * S, device=DEV)
+    out = torch.full((nseq * S, E), float("nan"), device=DEV, dtype=torch.bfloat16)
+    lse = torch.full((nseq * H * S,), float("nan"), device=DEV)
     K.attn_fwd(qkv, out, lse, nseq, n_causal, S, H, bid32, meta)
     qkv_f = qkv.float().requires_grad_(True)
     ref = ref_attention(qkv_f, nseq, n_causal, S, H, bid)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all() and torch.isfinite(lse).all()
+    assert rel_err(out, ref) < 1e-2 and cosine(out, ref) > 0.9999
     dout = (torch.randn(nseq * S, E, generator=gen) * 0.5).to(DEV).to(torch.bfloat16)
     ref.backward(dout.float())
     dqkv = torch.full_like(qkv, float("nan"))
