@@ -15,10 +15,12 @@
 //                   S_t = Q_t K^T (M=128, N = keys <= 256) into TMEM region t,
 //                   then O_t = P_t V with P_t read from TMEM (A operand) and V
 //                   MN-major from its TMA tile
-//   warps 4-7 / 8-11  softmax of tile 0 / 1, one thread per query row (the
-//                   TMEM lane), 64 keys per TMEM round trip: row max, exp2,
-//                   bf16 P written back into the score columns it has
-//                   consumed (P for keys 2c, 2c+1 in column c), then
+//   warps 4-11 / 12-19  softmax of tile 0 / 1, two threads per query row
+//                   (the TMEM lane) each taking one half of the keys: row
+//                   max (halves merged in shared memory), exp2, bf16 P
+//                   written back into score columns the same thread has
+//                   already read (P for keys 2c, 2c+1 in consecutive columns;
+//                   the upper half from column keys/2), then
 //                   O_t / rowsum -> bf16 rows in global memory and the base-2
 //                   log-sum-exp for the backward.  With contiguous blocks (the
 //                   loader's rows: a board block is one run of 68 rows, every
@@ -27,8 +29,8 @@
 //                   block layouts compare block ids per key
 //
 // TMEM (512 columns): region t = [256 t, 256 t + 256): scores in [0, keys),
-// P in [0, keys / 2), O in [128, 192) (written only after the row's scores
-// have been read).  Every wait is bounded (cdk_common); a timeout sets the
+// P in [0, keys / 4) and [keys / 2, 3 keys / 4), O in [192, 256) (written
+// only after the row's scores have been read).  Every wait is bounded (cdk_common); a timeout sets the
 // device error word and drains every role to the TMEM release.
 #include "../../include/cdk.h"
 #include "cdk_common.cuh"
@@ -40,7 +42,7 @@ constexpr int kHd = 64;
 constexpr int kMaxS = 256;
 constexpr int kBox = 64 * 128;  // one TMA box: 64 rows x 128 B (64 bf16)
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kThreads = 384;   // warps 0-3 producer / MMA, 4-11 softmax
+constexpr int kThreads = 640;   // warps 0-3 producer / MMA, 4-11 softmax of tile 0, 12-19 of tile 1
 
 struct Slot {
   uint8_t Q[4 * kBox];
@@ -54,6 +56,8 @@ struct FwdSmem {
   int32_t hi[2][kMaxS];    // max(i, last[i]): no key beyond it is visible to row i
   int32_t nk[2][2];        // keys (multiple of 64) of query tile 0 / 1
   int32_t contig[2];       // 1: every block id of the sequence is one contiguous run of rows
+  float red_max[2][2][128];  // [tile][key half][row]: partial row maxima of the two threads of a row
+  float red_sum[2][2][128];  // partial row sums
   uint64_t full[2], empty[2];
   uint64_t sfull[2], pfull[2], ofull[2], oempty[2];
   uint32_t tmem_base;
@@ -176,9 +180,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.sfull[t], 1);
-      mbar_init(&sm.pfull[t], 128);
+      mbar_init(&sm.pfull[t], 256);
       mbar_init(&sm.ofull[t], 1);
-      mbar_init(&sm.oempty[t], 128);
+      mbar_init(&sm.oempty[t], 256);
     }
     sm.abort = 0;
     fence_mbar_init();
@@ -257,22 +261,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&sm.pfull[t], k & 1, abort_flag);
         tc_fence_after();
         const uint32_t vb = smem_u32(sm.slot[s].V);
-        for (int kk = 0; kk < nk / 16; ++kk)
-          umma_f16_ts(treg + 128, treg + kk * 8, make_sdesc(vb + kk * 16 * 128, 8192, 1024), idesc_o,
+        // P of keys [0, nk/2) sits in columns [0, nk/4), P of keys [nk/2, nk)
+        // in columns [nk/2, 3 nk/4): each half written over scores its own
+        // thread has read
+        for (int kk = 0; kk < nk / 16; ++kk) {
+          const uint32_t acol = (uint32_t)(kk * 8 + (kk * 16 >= nk / 2 ? nk / 4 : 0));
+          umma_f16_ts(treg + 192, treg + acol, make_sdesc(vb + kk * 16 * 128, 8192, 1024), idesc_o,
                       kk > 0 ? 1u : 0u);
+        }
         tc_commit(&sm.ofull[t]);
         tc_commit(&sm.empty[s]);
       }
     }
   } else if (warp >= 4) {
     // ---- softmax + epilogue of query tile t ------------------------------
-    const int t = (warp - 4) >> 2;
+    // Two threads per query row: warps 4 + 8t + 4h + q (q = TMEM lane
+    // quadrant) take key half h, keys [h nk/2, (h + 1) nk/2).
+    const int t = (warp - 4) >> 3;
+    const int hf = ((warp - 4) >> 2) & 1;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int i = t * 128 + r;
     const bool row_ok = i < S;
     const uint32_t trow = tmem + (uint32_t)(t * 256) + (static_cast<uint32_t>(quad * 32) << 16);
     const float sl2 = 0.125f * kLog2e;
+    const int bar_id = 1 + t;  // named barrier of the tile's 256 softmax threads
     if (t < n_tiles) {
       for (int k = 0; k < n_local; ++k) {
         const int s = k & 1, u = k >> 1;
@@ -292,76 +305,65 @@ __global__ void __launch_bounds__(kThreads, 1)
         int hi_w = hi;
         #pragma unroll
         for (int o = 16; o > 0; o >>= 1) hi_w = max(hi_w, __shfl_xor_sync(0xffffffffu, hi_w, o));
-        const int nch = nk / 32;
+        const int c0 = hf * (nk / 64), c1 = c0 + nk / 64;  // this thread's 32-key chunks
+        const int c1v = min(c1, hi_w >= 0 ? hi_w / 32 + 1 : 0);  // ... that hold a key <= hi_w
         mbar_wait(&sm.sfull[t], k & 1, abort_flag);
         tc_fence_after();
-        // pass 1: max of the raw scores of keys [0, hi] (an upper bound of the
-        // visible maximum; either keeps exp2 <= 1)
+        // pass 1: max of the raw scores of keys <= hi (an upper bound of the
+        // visible maximum; either keeps exp2 <= 1), halves merged in shared memory
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        const int nch1 = min(nch, hi_w >= 0 ? hi_w / 32 + 1 : 0);  // chunks with a key <= hi_w
-        for (int c = 0; c < nch1; ++c) {
+        for (int c = c0; c < c1v; ++c) {
           uint32_t va[32];
           tmem_ld_x32_nowait(trow + c * 32, va);
           tmem_wait_ld_dep(va);
           row_max_chunk(va, c * 32, hi, mx4);
         }
-        const float ms = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
-        // pass 2: bf16 probabilities into the consumed score columns (keys
-        // 2c, 2c + 1 in column c), row sum; the load of chunk c + 1 is in
-        // flight while chunk c is exponentiated and stored
+        sm.red_max[t][hf][r] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+        asm volatile("bar.sync %0, 256;" ::"r"(bar_id) : "memory");
+        const float ms = fmaxf(sm.red_max[t][0][r], sm.red_max[t][1][r]) * sl2;
+        // pass 2: bf16 probabilities of this thread's keys into score columns
+        // it has already read (P of keys [base_h, ...) from column
+        // hf * nk/4 + (key / 2)), partial row sum
         float l4[4] = {0.f, 0.f, 0.f, 0.f};
-        {
-          uint32_t va[32], vb[32], pk[16];
-          if (nch1 > 0) tmem_ld_x32_nowait(trow, va);
-          for (int c = 0; c < nch; c += 2) {
-            if (c < nch1) {
-              tmem_wait_ld_dep(va);
-              if (c + 1 < nch1) tmem_ld_x32_nowait(trow + (c + 1) * 32, vb);
-              probs_chunk(va, c * 32, sl2, ms, full_hi, hi, my_bid, contig, bid, pk, l4);
-            } else {
-              zero16(pk);
-            }
-            tmem_st_x16(trow + c * 16, pk);
-            if (c + 1 >= nch) break;
-            if (c + 1 < nch1) {
-              tmem_wait_ld_dep(vb);
-              if (c + 2 < nch1) tmem_ld_x32_nowait(trow + (c + 2) * 32, va);
-              probs_chunk(vb, (c + 1) * 32, sl2, ms, full_hi, hi, my_bid, contig, bid, pk, l4);
-            } else {
-              zero16(pk);
-            }
-            tmem_st_x16(trow + (c + 1) * 16, pk);
+        for (int c = c0; c < c1; ++c) {
+          uint32_t pk[16];
+          if (c < c1v) {
+            uint32_t va[32];
+            tmem_ld_x32_nowait(trow + c * 32, va);
+            tmem_wait_ld_dep(va);
+            probs_chunk(va, c * 32, sl2, ms, full_hi, hi, my_bid, contig, bid, pk, l4);
+          } else {
+            zero16(pk);
           }
+          tmem_st_x16(trow + hf * (nk / 4) + c * 16, pk);
         }
-        const float l = (l4[0] + l4[1]) + (l4[2] + l4[3]);
+        sm.red_sum[t][hf][r] = (l4[0] + l4[1]) + (l4[2] + l4[3]);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&sm.pfull[t]);
-        // epilogue: O / l in bf16, and the base-2 log-sum-exp
+        // epilogue: O / l in bf16 (half hf stores dims [32 hf, 32 hf + 32)),
+        // and the base-2 log-sum-exp
         mbar_wait(&sm.ofull[t], k & 1, abort_flag);
         tc_fence_after();
-        uint32_t o0[32], o1[32];
-        tmem_ld_x32_nowait(trow + 128, o0);
-        tmem_ld_x32_nowait(trow + 160, o1);
-        tmem_wait_ld();
+        uint32_t o[32];
+        tmem_ld_x32_nowait(trow + 192 + hf * 32, o);
+        tmem_wait_ld_dep(o);
         tc_fence_before();
         mbar_arrive(&sm.oempty[t]);
+        asm volatile("bar.sync %0, 256;" ::"r"(bar_id) : "memory");  // both partial sums written
+        const float l = sm.red_sum[t][0][r] + sm.red_sum[t][1][r];
         if (row_ok) {
           const float inv = l > 0.f ? 1.f / l : 0.f;
-          uint4* dst = reinterpret_cast<uint4*>(a.out + (long long)(seq * S + i) * E + h * kHd);
+          uint4* dst = reinterpret_cast<uint4*>(a.out + (long long)(seq * S + i) * E + h * kHd + hf * 32);
           #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int b = q * 8;
-            dst[q] = make_uint4(pack_bf16(__uint_as_float(o0[b]) * inv, __uint_as_float(o0[b + 1]) * inv),
-                                pack_bf16(__uint_as_float(o0[b + 2]) * inv, __uint_as_float(o0[b + 3]) * inv),
-                                pack_bf16(__uint_as_float(o0[b + 4]) * inv, __uint_as_float(o0[b + 5]) * inv),
-                                pack_bf16(__uint_as_float(o0[b + 6]) * inv, __uint_as_float(o0[b + 7]) * inv));
-            dst[q + 4] = make_uint4(pack_bf16(__uint_as_float(o1[b]) * inv, __uint_as_float(o1[b + 1]) * inv),
-                                    pack_bf16(__uint_as_float(o1[b + 2]) * inv, __uint_as_float(o1[b + 3]) * inv),
-                                    pack_bf16(__uint_as_float(o1[b + 4]) * inv, __uint_as_float(o1[b + 5]) * inv),
-                                    pack_bf16(__uint_as_float(o1[b + 6]) * inv, __uint_as_float(o1[b + 7]) * inv));
+            dst[q] = make_uint4(pack_bf16(__uint_as_float(o[b]) * inv, __uint_as_float(o[b + 1]) * inv),
+                                pack_bf16(__uint_as_float(o[b + 2]) * inv, __uint_as_float(o[b + 3]) * inv),
+                                pack_bf16(__uint_as_float(o[b + 4]) * inv, __uint_as_float(o[b + 5]) * inv),
+                                pack_bf16(__uint_as_float(o[b + 6]) * inv, __uint_as_float(o[b + 7]) * inv));
           }
-          a.lse[((long long)seq * H + h) * S + i] = ms + log2f(l);
+          if (hf == 0) a.lse[((long long)seq * H + h) * S + i] = ms + log2f(l);
         }
       }
     }
