@@ -407,6 +407,11 @@ class Backbone:
         self.cfg = cfg
         self.rope = rope_table(cfg.max_seq_len, cfg.head_dim).to(store.device)
         self.fp8 = fp8  # Fp8Recipe: the backbone linears run in fp8 (chessdecoder_b200/fp8.py)
+        # MoE variant: with keep_routing set, each forward leaves its per-layer
+        # decisions in `routing` as (expert [T, 2] int32, slot [T, 2] int32,
+        # -1 = dropped) for inspection (load balance, parity checks)
+        self.keep_routing = False
+        self.routing = None
 
     def cast_fp8_weights(self):
         """e4m3 copies (and their transposes) of this step's backbone weights."""
@@ -582,6 +587,8 @@ class Backbone:
                        fp8=self._f8(i, "2", "x", E4, "w", E4))
             saved.append(s)
             x = out
+        if cfg.moe_experts and self.keep_routing:
+            self.routing = [(s.moe["expert"], s.moe["slot"]) for s in saved]
         hN16 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
         hN32 = torch.empty(T, E, device=dev) if want_f32 else None
         rN = torch.empty(T, device=dev)

@@ -47,19 +47,33 @@ class _Experts(nn.Module):
 
 
 class OracleMoE(nn.Module):
+    """``forced``: optional list of (expert [T, 2], keep [T, 2] bool) decisions,
+    one per forward call in call order, that replace the top-2 / capacity
+    choices (the weights are still this module's renormalised probabilities
+    of the given experts): a check of everything downstream of the discrete
+    routing against another implementation's decisions.  ``record``: when a
+    list, each call appends its own (expert, keep)."""
+
     def __init__(self, embed_dim, d_ff, n_experts=8, capacity=1.25):
         super().__init__()
         self.E, self.F, self.X, self.capacity = embed_dim, d_ff, n_experts, capacity
         self.router = _Router(embed_dim, n_experts)
         self.experts = _Experts(embed_dim, d_ff, n_experts)
+        self.forced = None
+        self.record = None
 
     def route(self, xt):
         """(idx [T,2], w [T,2], keep [T,2] bool, cap) for tokens xt [T, E]."""
         T, X = xt.shape[0], self.X
         p = torch.softmax(xt @ self.router.weight.t(), dim=-1)
+        cap = math.ceil(self.capacity * 2 * T / X)
+        if self.forced:
+            idx, keep = self.forced.pop(0)
+            idx, keep = idx.to(xt.device).long(), keep.to(xt.device).bool()
+            v = p.gather(1, idx)
+            return idx, v / v.sum(-1, keepdim=True), keep, cap
         v, idx = torch.topk(p, 2, dim=-1)
         w = v / v.sum(-1, keepdim=True)
-        cap = math.ceil(self.capacity * 2 * T / X)
         keep = torch.zeros(T, 2, dtype=torch.bool, device=xt.device)
         fill = torch.zeros(X, dtype=torch.long, device=xt.device)
         ar = torch.arange(T, device=xt.device)
@@ -69,6 +83,8 @@ class OracleMoE(nn.Module):
             pos = (torch.cumsum(oh, 0) - 1)[ar, e] + fill[e]
             keep[:, k] = pos < cap
             fill = fill + oh.sum(0)
+        if self.record is not None:
+            self.record.append((idx.detach().clone(), keep.clone()))
         return idx, w, keep, cap
 
     def forward(self, x):

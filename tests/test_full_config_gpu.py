@@ -109,3 +109,83 @@ def test_full_config_bf16_step_matches_oracle(pretrain):
     else:
         assert res["board_ties_only"] and res["move_ties_only"], (res["agree_board"], res["agree_move"])
     assert kernels.get_error() == 0
+
+
+def test_full_config_fp8_step_matches_fp8_recipe_oracle():
+    """fp8 variant at B=128.  Against the fp32 oracle each loss is within 3e-2.
+    Gradients are gated against the oracle that applies the same fp8 recipe
+    (oracle/fp8.py: e4m3 inputs / weights, e5m2 output gradients, per-tensor
+    scaling) at cosine >= 0.999: one e5m2 rounding of a gradient alone (2
+    mantissa bits, relative spacing 2^-2) bounds its cosine to the unquantised
+    gradient near 0.998, so the fp32 oracle cannot gate the fp8 gradients at
+    0.999; the recipe oracle can."""
+    from chessdecoder_b200 import data, kernels
+    from chessdecoder_b200.engine import TrainStep
+    from oracle.fp8 import Fp8OracleChessDecoder
+    cfg, oracle = _oracle(FULL)
+    sd = {k: v.detach().cpu().clone() for k, v in oracle.state_dict().items()}
+    batch = data.synthetic_batches(1, 128, cfg.max_seq_len, seed=3)[0]
+    step = TrainStep(cfg, device="cuda", state_dict=sd, fp8=True)
+    res = compare(step, oracle, batch, 3e-2)
+    for n, (got, ref) in res["loss"].items():
+        assert abs(got - ref) <= 3e-2 * max(abs(ref), 1e-6), (n, got, ref)
+    del oracle, step
+    torch.cuda.empty_cache()
+    torch.manual_seed(0)
+    f8o = Fp8OracleChessDecoder(cfg.vocab_size, **FULL).cuda()
+    f8o.load_state_dict({k: v.cuda() for k, v in sd.items()})
+    step8 = TrainStep(cfg, device="cuda", state_dict=sd, fp8=True)
+    res8 = compare(step8, f8o, batch, 3e-2)
+    check(res8, 3e-2, 0.999)
+    assert kernels.get_error() == 0
+
+
+def test_full_config_moe_step_matches_oracle():
+    """MoE variant (8 experts, top-2, capacity 1.25) at S=4096 with a reduced
+    batch of 2 thinking-variation sequences.  The top-2 and capacity choices
+    are discrete: a bf16-vs-fp32 near-tie of two router probabilities sends a
+    token to another expert.  So (1) the CUDA step's choices must agree with
+    the fp32 oracle's own on >= 99% of (token, choice) decisions, and (2) given
+    the CUDA step's choices (oracle/moe.py ``forced``) the oracle's losses are
+    within 1e-2 and every gradient has cosine >= 0.999."""
+    from chessdecoder_b200 import data, kernels
+    from chessdecoder_b200.engine import TrainStep, prepare_batch
+    from oracle.step import step_losses
+    kw = dict(FULL, max_seq_len=4096, moe_experts=8, moe_capacity=1.25)
+    cfg, oracle = _oracle(kw)
+    sd = {k: v.detach().cpu().clone() for k, v in oracle.state_dict().items()}
+    batch = data.thinking_batches(1, 2, cfg.max_seq_len, seed=5)[0]
+    step = TrainStep(cfg, device="cuda", state_dict=sd)
+    step.backbone.keep_routing = True
+    db = prepare_batch(batch, "cuda")
+    losses = step.forward_backward(db).cpu()
+    BS = db.B * db.S
+    routing = step.backbone.routing
+    # (1) the oracle's own decisions, pass 1 then pass 2 of each layer
+    for layer in oracle.layers:
+        layer.mlp.record = []
+    with torch.no_grad():
+        step_losses(oracle, batch)
+    agree = total = 0
+    for i, layer in enumerate(oracle.layers):
+        ex, sl = routing[i]
+        for p, (idx, keep) in enumerate(layer.mlp.record):
+            e = ex[p * BS:(p + 1) * BS].long()
+            k = sl[p * BS:(p + 1) * BS] >= 0
+            agree += int(((e == idx) & (k == keep)).sum())
+            total += idx.numel()
+        layer.mlp.record = None
+    assert agree / total >= 0.99, agree / total
+    # (2) parity given the CUDA step's decisions
+    for i, layer in enumerate(oracle.layers):
+        ex, sl = routing[i]
+        layer.mlp.forced = [(ex[p * BS:(p + 1) * BS], sl[p * BS:(p + 1) * BS] >= 0) for p in range(2)]
+    out = step_losses(oracle, batch)
+    out["total"].backward()
+    for j, n in enumerate(["move", "board", "wl", "d"]):
+        ref = float(out[n].detach())
+        assert abs(float(losses[j]) - ref) <= 1e-2 * max(abs(ref), 1e-6), (n, float(losses[j]), ref)
+    rp = dict(oracle.named_parameters())
+    cos = {name: cosine(step.store.grad_of(name), rp[name].grad) for name in step.store.names()}
+    assert all(c >= 0.999 for c in cos.values()), sorted(cos.items(), key=lambda kv: kv[1])[:5]
+    assert kernels.get_error() == 0
