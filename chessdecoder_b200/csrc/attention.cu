@@ -1116,6 +1116,7 @@ static int attn_path() {
   const char* v = getenv("CDK_ATTN_PATH");
   if (v && v[0] == 't' && v[1] == 'i') return 2;  // tiled
   if (v && v[0] == 't' && v[1] == 'c') return 4;  // one CTA per (query tile, head, sequence) tcgen05 kernels
+  if (v && v[0] == 'p') return 5;                  // persistent tcgen05 backward (S <= 256)
   if (v && v[0] == 's') return 1;                  // seq (mma.sync)
   if (v && v[0] == 'l') return 3;                  // tcgen05 long-sequence kernels at any S
   return 0;                                        // tcgen05
@@ -1162,7 +1163,7 @@ extern "C" int cdk_attn_fwd(const void* qkv, void* out, float* lse, int64_t nseq
   a.nt = (int)((S + kTile - 1) / kTile);
   a.nseq = (int)nseq;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (S <= kSeqMax && attn_path() == 0) {
+  if (S <= kSeqMax && (attn_path() == 0 || attn_path() == 5)) {
     return launch_attn_fwd_pst(qkv, out, lse, nseq, n_causal, S, H, bid, meta, s);
   }
   if (S <= kSeqMax && attn_path() == 4) {
@@ -1192,6 +1193,9 @@ extern "C" int cdk_attn_fwd(const void* qkv, void* out, float* lse, int64_t nseq
 }
 
 namespace cdk {
+int launch_attn_bwd_pst(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,
+                        void* dqkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,
+                        const int32_t* meta, const float* rope, cudaStream_t stream);
 int launch_attn_bwd_long(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,
                          void* dqkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,
                          const int32_t* meta, const float* rope, void* workspace, cudaStream_t stream);
@@ -1236,6 +1240,8 @@ extern "C" int cdk_attn_bwd_ws(const void* qkv, const void* out, const void* dou
   a.nseq = (int)nseq;
   dim3 grid((unsigned)a.nt, (unsigned)H, (unsigned)nseq);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (S <= kSeqMax && attn_path() == 5)
+    return launch_attn_bwd_pst(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid, meta, rope, s);
   if (S <= kSeqMax && (attn_path() == 0 || attn_path() == 4))
     return launch_attn_bwd_tc(qkv, out, dout, lse, dqkv, nseq, n_causal, S, H, bid, meta, rope, s);
   if (long_path(S) && workspace != nullptr && S % 4 == 0) {

@@ -1,0 +1,571 @@
+// Persistent tensor-core attention backward for sequences of at most 256
+// tokens, head_dim 64 (the pretraining shape; causal and block-prefix masks of
+// chessdecoder/models/model.py:158-171, gradient of the SDPA in
+// chessdecoder/export/backbone_causal.py:112-137).
+//
+// One CTA per SM walks the (head, sequence) items b, b + grid, ...  An item's
+// keys form key tiles kt of 128 rows, its queries query halves qh of 128 rows;
+// the work is a list of sub-units (kt, qs) with qs a 64-query sub-tile, taken
+// key-tile-major in pairs (qs = 2 qh, 2 qh + 1) over the query halves that can
+// see the key tile.  Per sub-unit:
+//   MMA-A   S^T = K_kt Q_qs^T, dP^T = V_kt dO_qs^T           (TMEM, N = 64)
+//   EW      P^T = exp2(S^T c - L), dS^T = P^T (dP^T - D)      (masked)
+//   MMA-B   dV_kt += P^T dO_qs (P^T read from TMEM), dK_kt += dS^T Q_qs
+//   (pair)  dQ_qh += dS K_kt  (dS read MN-major from the pair's dS^T tiles)
+// S^T | dP^T are double-buffered in TMEM, so the tensor core runs MMA-B / dQ
+// of one sub-unit and MMA-A of the next but one while the elementwise warps
+// work on the next.  dV / dK of a key tile and dQ of both query halves stay in
+// TMEM until complete and are written once (dK, dQ scaled by 1/8 with the
+// inverse RoPE rotation).  The operands of an item live in shared memory in
+// four 32 KB slots -- K|V of key tile 0 and 1, Q|dO of query half 0 and 1 --
+// each released as soon as the item's last product that reads it has retired,
+// so the next item's loads overlap this one.  D = rowsum(dO * O) comes from a
+// pass before (attn_dsum).
+//
+//   warp 0       producer: row metadata (L, D, block bounds) and TMA loads
+//   warp 1       TMEM allocation, MMA issue (lane 0)
+//   warps 2-9    elementwise + epilogues: thread = (key row r = TMEM lane,
+//                query half hq of the sub-tile: 32 queries)
+// TMEM: S^T|dP^T x 2 [0, 256) | dV [256, 320) | dK [320, 384) | dQ_0 [384, 448)
+// | dQ_1 [448, 512).  P^T (bf16) is written over the thread's own S^T columns
+// after it has read them: queries [0, 32) -> columns [0, 16), [32, 64) ->
+// [32, 48) of the buffer.  Every wait is bounded (cdk_common).
+#include "../../include/cdk.h"
+#include "cdk_common.cuh"
+
+namespace cdk {
+namespace pstbwd {
+
+constexpr int kHd = 64;
+constexpr int kMaxS = 256;
+constexpr int kBox = 64 * 128;  // one TMA box: 64 rows x 128 B
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kThreads = 320;   // warp 0 producer, warp 1 MMA, warps 2-9 elementwise
+constexpr int kMaxUnits = 8;    // sub-units of one item (two key tiles x two query halves x 2)
+
+struct Meta {
+  alignas(16) float L[kMaxS];   // base-2 log-sum-exp of each query row (0 past S)
+  alignas(16) float D[kMaxS];   // rowsum(dO * O) of each query row (0 past S)
+  int32_t first[kMaxS];         // first row of each key row's block (causal: the row; S past S)
+  int32_t bid[kMaxS];           // block id of each row (non-contiguous layouts only)
+  int32_t contig;               // 1: every block id is one contiguous run of rows
+};
+
+struct BwdSmem {
+  uint8_t KV[2][4 * kBox];      // key tile kt: K rows (2 boxes) | V rows (2 boxes)
+  uint8_t QO[2][4 * kBox];      // query half qh: Q rows (2 boxes) | dO rows (2 boxes)
+  uint8_t dST[2][2][128 * 128]; // [pair buffer][sub-tile]: 128 key rows x 64 queries (bf16, 128-B swizzle)
+  Meta meta[2];
+  uint64_t kvfull[2], kvempty[2], qfull[2], qempty[2], mfull[2], mempty[2];
+  uint64_t sa[2], ew[2], dq[2], kvdone, kvfree, dqdone, dqfree;
+  uint32_t tmem_base;
+  int abort;
+};
+static_assert(offsetof(BwdSmem, QO) % 1024 == 0 && offsetof(BwdSmem, dST) % 1024 == 0,
+              "TMA / UMMA operands with the 128-byte swizzle need 1024-byte alignment");
+static_assert(offsetof(BwdSmem, meta) % 16 == 0 && sizeof(Meta) % 16 == 0, "L / D are read as float4");
+
+struct Args {
+  const float* lse;       // [nseq, H, S]
+  const float* dsum;      // [nseq, H, S]
+  __nv_bfloat16* dqkv;
+  const int32_t* bid;     // [nseq - n_causal, S]
+  const int32_t* first;   // [nseq - n_causal, S]
+  const int32_t* q_lo;    // [nseq - n_causal][2 * nt64]; + nt64: lowest first row per 64-row tile
+  const float* rope;      // [>= S, 32, 2] (cos, sin) or null
+  int S, H, n_causal, nt64, n_items;
+};
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// tcgen05.wait::ld naming the loaded registers, so no use is scheduled before it.
+__device__ __forceinline__ void tmem_wait_ld_dep(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+        "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+        "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+        "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// The sub-units of an item: key tile kt (k-major), query sub-tile qs; pairs of
+// sub-tiles (2 qh, 2 qh + 1) from the first query half that can see the key
+// tile.  Returns the count; u_kt / u_qs filled.
+struct Units {
+  int n;
+  int8_t kt[kMaxUnits], qs[kMaxUnits];
+};
+
+__device__ __forceinline__ Units item_units(const Args& a, bool prefix, int pseq) {
+  Units u;
+  u.n = 0;
+  const int nkt = (a.S + 127) / 128;
+  for (int kt = 0; kt < nkt; ++kt) {
+    int qh0 = kt;
+    if (prefix) {
+      const int* ql = a.q_lo + (long long)pseq * 2 * a.nt64 + a.nt64;
+      int q0 = kt * 128;
+      for (int t = 2 * kt; t < min(2 * kt + 2, a.nt64); ++t) q0 = min(q0, ql[t]);
+      qh0 = q0 / 128;
+    }
+    for (int qh = qh0; qh < nkt; ++qh) {
+      u.kt[u.n] = (int8_t)kt;
+      u.qs[u.n] = (int8_t)(2 * qh);
+      u.kt[u.n + 1] = (int8_t)kt;
+      u.qs[u.n + 1] = (int8_t)(2 * qh + 1);
+      u.n += 2;
+    }
+  }
+  return u;
+}
+
+// dX (bf16) of 32 consecutive dims [c0, c0 + 32) of a row: value * 0.125 with the
+// inverse RoPE rotation of position pos when rope != null (scale_rope), or as is.
+__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t (&v)[32], bool scale_rope,
+                                            const float* rope, int pos, int c0) {
+  float f[32];
+  #pragma unroll
+  for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(v[e]) * (scale_rope ? 0.125f : 1.f);
+  if (scale_rope && rope != nullptr) {
+    const float4* cs = reinterpret_cast<const float4*>(rope + ((long long)pos * 32 + c0 / 2) * 2);
+    #pragma unroll
+    for (int p = 0; p < 8; ++p) {
+      const float4 t = cs[p];  // (cos, sin) of two consecutive pairs
+      float x0 = f[4 * p], x1 = f[4 * p + 1];
+      f[4 * p] = x0 * t.x + x1 * t.y;
+      f[4 * p + 1] = x1 * t.x - x0 * t.y;
+      x0 = f[4 * p + 2];
+      x1 = f[4 * p + 3];
+      f[4 * p + 2] = x0 * t.z + x1 * t.w;
+      f[4 * p + 3] = x1 * t.z - x0 * t.w;
+    }
+  }
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  #pragma unroll
+  for (int q = 0; q < 4; ++q)
+    d[q] = make_uint4(pack_bf16(f[8 * q], f[8 * q + 1]), pack_bf16(f[8 * q + 2], f[8 * q + 3]),
+                      pack_bf16(f[8 * q + 4], f[8 * q + 5]), pack_bf16(f[8 * q + 6], f[8 * q + 7]));
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_pst_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo,
+                        const Args a) {
+  extern __shared__ uint8_t raw[];
+  BwdSmem& sm = *reinterpret_cast<BwdSmem*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  const int S = a.S, H = a.H, E = H * kHd;
+  const int nkt = (S + 127) / 128;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int n_local = a.n_items > (int)blockIdx.x ? (a.n_items - (int)blockIdx.x + G - 1) / G : 0;
+  volatile int* abort_flag = &sm.abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.kvfull[s], 1);
+      mbar_init(&sm.kvempty[s], 1);
+      mbar_init(&sm.qfull[s], 1);
+      mbar_init(&sm.qempty[s], 1);
+      mbar_init(&sm.mfull[s], 32);
+      mbar_init(&sm.mempty[s], 256);
+      mbar_init(&sm.sa[s], 1);
+      mbar_init(&sm.ew[s], 256);
+      mbar_init(&sm.dq[s], 1);
+    }
+    mbar_init(&sm.kvdone, 1);
+    mbar_init(&sm.kvfree, 256);
+    mbar_init(&sm.dqdone, 1);
+    mbar_init(&sm.dqfree, 256);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ---- producer ----------------------------------------------------------
+    if (lane == 0) {
+      prefetch_tmap(&tqkv);
+      prefetch_tmap(&tdo);
+    }
+    for (int k = 0; k < n_local; ++k) {
+      const int item = (int)blockIdx.x + k * G;
+      const int seq = item / H, h = item - seq * H;
+      const bool prefix = seq >= a.n_causal;
+      const int pseq = seq - a.n_causal;
+      const int row0 = seq * S;
+      const long long lrow = ((long long)seq * H + h) * S;
+      // row metadata (double-buffered per item)
+      const int m = k & 1;
+      if (k >= 2) mbar_wait(&sm.mempty[m], ((k >> 1) - 1) & 1, abort_flag);
+      Meta& mt = sm.meta[m];
+      const int32_t* brow = prefix ? a.bid + (long long)pseq * S : nullptr;
+      const int32_t* frow = prefix ? a.first + (long long)pseq * S : nullptr;
+      bool runs_ok = true;  // a row whose id differs from the previous row's opens that id's first run
+      for (int i = lane; i < kMaxS; i += 32) {
+        const bool ok = i < S;
+        mt.L[i] = ok ? a.lse[lrow + i] : 0.f;
+        mt.D[i] = ok ? a.dsum[lrow + i] : 0.f;
+        mt.first[i] = ok ? (prefix ? frow[i] : i) : S;
+        const int b = ok ? (prefix ? brow[i] : i) : -1;
+        mt.bid[i] = b;
+        if (prefix && ok && i > 0 && b != brow[i - 1] && frow[i] != i) runs_ok = false;
+      }
+      runs_ok = __all_sync(0xffffffffu, runs_ok);
+      if (lane == 0) mt.contig = runs_ok ? 1 : 0;
+      mbar_arrive(&sm.mfull[m]);
+      // operand slots, in the order the item's first sub-units need them
+      auto load_kv = [&](int kt) {
+        if (k >= 1) mbar_wait(&sm.kvempty[kt], (k - 1) & 1, abort_flag);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&sm.kvfull[kt], 4 * kBox);
+          for (int b = 0; b < 2; ++b) {
+            const int r = row0 + kt * 128 + b * 64;
+            tma_load_2d(sm.KV[kt] + b * kBox, &tqkv, &sm.kvfull[kt], E + h * kHd, r);
+            tma_load_2d(sm.KV[kt] + (2 + b) * kBox, &tqkv, &sm.kvfull[kt], 2 * E + h * kHd, r);
+          }
+        }
+      };
+      auto load_q = [&](int qh) {
+        if (k >= 1) mbar_wait(&sm.qempty[qh], (k - 1) & 1, abort_flag);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&sm.qfull[qh], 4 * kBox);
+          for (int b = 0; b < 2; ++b) {
+            const int r = row0 + qh * 128 + b * 64;
+            tma_load_2d(sm.QO[qh] + b * kBox, &tqkv, &sm.qfull[qh], h * kHd, r);
+            tma_load_2d(sm.QO[qh] + (2 + b) * kBox, &tdo, &sm.qfull[qh], h * kHd, r);
+          }
+        }
+      };
+      load_kv(0);
+      load_q(0);
+      if (nkt > 1) {
+        load_q(1);
+        load_kv(1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issue -----------------------------------------------------------
+    if (lane == 0) {
+      const uint32_t id_s = make_idesc_bf16(128, 64, false, false);   // S^T, dP^T: N = 64 queries
+      const uint32_t id_kn = make_idesc_bf16(128, kHd, false, true);  // dV, dK: B read MN-major
+      const uint32_t id_nn = make_idesc_bf16(128, kHd, true, true);   // dQ: A (dS) and B (K) MN-major
+      int g_issued = 0;    // global index of the next sub-unit whose MMA-A is to be issued
+      int ka = 0, ua = 0;  // its item and unit
+      Units units_a;
+      bool have_a = false;
+      auto next_a = [&]() {  // advance (ka, ua) to the next sub-unit; false when none is left
+        while (true) {
+          if (!have_a) {
+            if (ka >= n_local) return false;
+            const int item = (int)blockIdx.x + ka * G;
+            const int seq = item / H;
+            units_a = item_units(a, seq >= a.n_causal, seq - a.n_causal);
+            have_a = true;
+            ua = 0;
+          }
+          if (ua < units_a.n) return true;
+          have_a = false;
+          ++ka;
+        }
+      };
+      // Issues MMA-A of the next sub-unit not yet issued, unless it belongs to
+      // an item after `max_item`: the next item's operands are loaded into
+      // slots this item releases, so its MMA-A waits for loads that can only
+      // start after this item's release commits.
+      auto issue_a = [&](int max_item) {
+        if (!next_a() || ka > max_item) return;
+        const int kt = units_a.kt[ua], qs = units_a.qs[ua], qh = qs >> 1;
+        const int b = g_issued & 1;
+        mbar_wait(&sm.kvfull[kt], ka & 1, abort_flag);
+        mbar_wait(&sm.qfull[qh], ka & 1, abort_flag);
+        tc_fence_after();
+        const uint32_t kb = smem_u32(sm.KV[kt]), vb = kb + 2 * kBox;
+        const uint32_t qb = smem_u32(sm.QO[qh]) + (qs & 1) * kBox, ob = smem_u32(sm.QO[qh]) + (2 + (qs & 1)) * kBox;
+        #pragma unroll
+        for (int kk = 0; kk < kHd / 16; ++kk) {
+          umma_f16(tmem + b * 128, make_sdesc(kb + kk * 32, 16, 1024), make_sdesc(qb + kk * 32, 16, 1024), id_s,
+                   kk > 0 ? 1u : 0u);
+          umma_f16(tmem + b * 128 + 64, make_sdesc(vb + kk * 32, 16, 1024), make_sdesc(ob + kk * 32, 16, 1024),
+                   id_s, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&sm.sa[b]);
+        ++g_issued;
+        ++ua;
+      };
+      issue_a(0);
+      issue_a(0);
+      int g = 0;   // global sub-unit index
+      int c = 0;   // global key-tile block index (dV / dK accumulations)
+      for (int k = 0; k < n_local; ++k) {
+        const int item = (int)blockIdx.x + k * G;
+        const int seq = item / H;
+        const Units un = item_units(a, seq >= a.n_causal, seq - a.n_causal);
+        // last sub-unit reading each query slot
+        int last_q[2] = {-1, -1};
+        for (int u = 0; u < un.n; ++u) last_q[un.qs[u] >> 1] = u;
+        uint32_t dq_seen = 0;
+        for (int u = 0; u < un.n; ++u, ++g) {
+          const int kt = un.kt[u], qs = un.qs[u], qh = qs >> 1;
+          const int b = g & 1, pb = (g >> 1) & 1;
+          const bool first_kt = u == 0 || un.kt[u - 1] != kt;
+          const bool last_kt = u == un.n - 1 || un.kt[u + 1] != kt;
+          mbar_wait(&sm.ew[b], (g >> 1) & 1, abort_flag);
+          if (first_kt && c > 0) mbar_wait(&sm.kvfree, (c - 1) & 1, abort_flag);
+          tc_fence_after();
+          const uint32_t qb = smem_u32(sm.QO[qh]) + (qs & 1) * kBox, ob = smem_u32(sm.QO[qh]) + (2 + (qs & 1)) * kBox;
+          const uint32_t dsb = smem_u32(sm.dST[pb][qs & 1]);
+          #pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {  // 64 queries, 16 per step
+            const uint32_t acc = (!first_kt || kk > 0) ? 1u : 0u;
+            const uint32_t pcol = (uint32_t)(b * 128 + kk * 8 + (kk >= 2 ? 16 : 0));
+            umma_f16_ts(tmem + 256, tmem + pcol, make_sdesc(ob + kk * 2048, 8192, 1024), id_kn, acc);
+            umma_f16(tmem + 320, make_sdesc(dsb + kk * 32, 16, 1024), make_sdesc(qb + kk * 2048, 8192, 1024), id_kn,
+                     acc);
+          }
+          if (qs & 1) {
+            // dQ_qh += dS K_kt over the pair's 128 queries (A: the two dS^T tiles, MN-major)
+            if (dq_seen == 0 && k > 0) mbar_wait(&sm.dqfree, (k - 1) & 1, abort_flag);
+            tc_fence_after();
+            const uint32_t pair = smem_u32(sm.dST[pb][0]);
+            const uint32_t kb = smem_u32(sm.KV[kt]);
+            const bool first_q = ((dq_seen >> qh) & 1u) == 0;
+            #pragma unroll 1
+            for (int kk = 0; kk < 8; ++kk)  // 128 keys
+              umma_f16(tmem + 384 + qh * 64, make_sdesc(pair + kk * 2048, 16384, 1024),
+                       make_sdesc(kb + kk * 2048, 8192, 1024), id_nn, (!first_q || kk > 0) ? 1u : 0u);
+            dq_seen |= 1u << qh;
+            tc_commit(&sm.dq[pb]);
+          }
+          if (last_kt) {
+            tc_commit(&sm.kvdone);
+            tc_commit(&sm.kvempty[kt]);
+            ++c;
+          }
+          if (u == last_q[0]) tc_commit(&sm.qempty[0]);
+          if (u == last_q[1]) tc_commit(&sm.qempty[1]);
+          if (u == un.n - 1) tc_commit(&sm.dqdone);
+          // keep MMA-A two sub-units ahead; across an item boundary only once
+          // every release commit of this item has been issued
+          const int max_item = u == un.n - 1 ? k + 1 : k;
+          while (g_issued < g + 3 && next_a() && ka <= max_item) issue_a(max_item);
+        }
+      }
+    }
+  } else {
+    // ---- elementwise + epilogues -------------------------------------------
+    const int quad = warp & 3;
+    const int hq = (warp - 2) >> 2;  // query half of the 64-query sub-tile
+    const int r = quad * 32 + lane;  // key row within the key tile = TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const float sl2 = 0.125f * kLog2e;
+    int g = 0, c = 0;
+    for (int k = 0; k < n_local; ++k) {
+      const int item = (int)blockIdx.x + k * G;
+      const int seq = item / H, h = item - seq * H;
+      const bool prefix = seq >= a.n_causal;
+      const Units un = item_units(a, prefix, seq - a.n_causal);
+      const int m = k & 1;
+      mbar_wait(&sm.mfull[m], (k >> 1) & 1, abort_flag);
+      const Meta& mt = sm.meta[m];
+      const bool contig = mt.contig != 0;
+      __nv_bfloat16* rowbase = a.dqkv + (long long)(seq * S) * 3 * E;
+      for (int u = 0; u < un.n; ++u, ++g) {
+        const int kt = un.kt[u], qs = un.qs[u];
+        const int b = g & 1, P = g >> 1, pb = P & 1;
+        const bool last_kt = u == un.n - 1 || un.kt[u + 1] != kt;
+        const int j = kt * 128 + r;
+        const bool jok = j < S;
+        const int fj = jok ? mt.first[j] : S;
+        const int bj = jok ? mt.bid[j] : -2;
+        const int q0 = qs * 64 + hq * 32;  // this thread's 32 queries
+        // keys see queries i >= first_j when blocks are contiguous; otherwise
+        // i >= j, or i >= first_j with the same block id
+        const int vis_lo = contig ? fj : j;
+        const bool full = jok && q0 >= vis_lo && q0 + 31 < S;
+        const bool none = !jok || q0 + 31 < fj || q0 >= S;
+        const bool none_w = __all_sync(0xffffffffu, none);
+        // the pair buffer is free once the dQ product of pair P - 2 has retired
+        if ((u & 1) == 0 && P >= 2) mbar_wait(&sm.dq[pb], ((P >> 1) - 1) & 1, abort_flag);
+        mbar_wait(&sm.sa[b], (g >> 1) & 1, abort_flag);
+        tc_fence_after();
+        uint32_t pk[16], dk[16];
+        if (none_w || none) {
+          #pragma unroll
+          for (int e = 0; e < 16; ++e) pk[e] = dk[e] = 0u;
+        }
+        if (!none_w) {
+          uint32_t su[32], du[32];
+          tmem_ld_x32_nowait(tmem + lane_off + b * 128 + hq * 32, su);
+          tmem_ld_x32_nowait(tmem + lane_off + b * 128 + 64 + hq * 32, du);
+          tmem_wait_ld_dep(su);
+          tmem_wait_ld_dep(du);
+          if (!none) {
+            const float4* L4 = reinterpret_cast<const float4*>(mt.L + q0);
+            const float4* D4 = reinterpret_cast<const float4*>(mt.D + q0);
+            #pragma unroll
+            for (int e4 = 0; e4 < 8; ++e4) {
+              const float4 l4 = L4[e4], d4 = D4[e4];
+              const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+              const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+              float pv[4], dsv[4];
+              #pragma unroll
+              for (int kq = 0; kq < 4; ++kq) {
+                const int e = e4 * 4 + kq;
+                const float p = ex2_approx(fmaf(__uint_as_float(su[e]), sl2, -lv[kq]));
+                pv[kq] = p;
+                dsv[kq] = p * (__uint_as_float(du[e]) - dv[kq]);
+              }
+              if (!full) {
+                #pragma unroll
+                for (int kq = 0; kq < 4; ++kq) {
+                  const int i = q0 + e4 * 4 + kq;
+                  const bool vis = i < S && (i >= vis_lo || (!contig && i >= fj && mt.bid[i] == bj));
+                  pv[kq] = vis ? pv[kq] : 0.f;
+                  dsv[kq] = vis ? dsv[kq] : 0.f;
+                }
+              }
+              pk[e4 * 2] = pack_bf16(pv[0], pv[1]);
+              pk[e4 * 2 + 1] = pack_bf16(pv[2], pv[3]);
+              dk[e4 * 2] = pack_bf16(dsv[0], dsv[1]);
+              dk[e4 * 2 + 1] = pack_bf16(dsv[2], dsv[3]);
+            }
+          }
+        }
+        // P^T over this thread's own (already read) S^T columns; dS^T into the pair buffer
+        tmem_st_x16(tmem + lane_off + b * 128 + hq * 32, pk);
+        uint8_t* dst = sm.dST[pb][qs & 1];
+        #pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = hq * 4 + q;  // 16-byte chunk of the 128-byte row
+          *reinterpret_cast<uint4*>(dst + r * 128 + ((chunk ^ (r & 7)) << 4)) =
+              make_uint4(dk[4 * q], dk[4 * q + 1], dk[4 * q + 2], dk[4 * q + 3]);
+        }
+        tmem_wait_st();
+        fence_proxy_async();
+        tc_fence_before();
+        mbar_arrive(&sm.ew[b]);
+        if (last_kt) {
+          // dV_kt, dK_kt complete: this thread stores dims [32 hq, 32 hq + 32) of key row j
+          mbar_wait(&sm.kvdone, c & 1, abort_flag);
+          tc_fence_after();
+          uint32_t vv[32], kv[32];
+          tmem_ld_x32_nowait(tmem + lane_off + 256 + hq * 32, vv);
+          tmem_ld_x32_nowait(tmem + lane_off + 320 + hq * 32, kv);
+          tmem_wait_ld_dep(vv);
+          tmem_wait_ld_dep(kv);
+          tc_fence_before();
+          mbar_arrive(&sm.kvfree);
+          ++c;
+          if (jok) {
+            __nv_bfloat16* rowp = rowbase + (long long)j * 3 * E;
+            store_row32(rowp + E + h * kHd + hq * 32, kv, true, a.rope, j, hq * 32);
+            store_row32(rowp + 2 * E + h * kHd + hq * 32, vv, false, nullptr, j, hq * 32);
+          }
+        }
+      }
+      mbar_arrive(&sm.mempty[m]);
+      // dQ of both query halves (lane = query row within the half)
+      mbar_wait(&sm.dqdone, k & 1, abort_flag);
+      tc_fence_after();
+      uint32_t q0v[32], q1v[32];
+      tmem_ld_x32_nowait(tmem + lane_off + 384 + hq * 32, q0v);
+      if (nkt > 1) tmem_ld_x32_nowait(tmem + lane_off + 448 + hq * 32, q1v);
+      tmem_wait_ld_dep(q0v);
+      if (nkt > 1) tmem_wait_ld_dep(q1v);
+      tc_fence_before();
+      mbar_arrive(&sm.dqfree);
+      if (r < S) store_row32(rowbase + (long long)r * 3 * E + h * kHd + hq * 32, q0v, true, a.rope, r, hq * 32);
+      if (nkt > 1 && 128 + r < S)
+        store_row32(rowbase + (long long)(128 + r) * 3 * E + h * kHd + hq * 32, q1v, true, a.rope, 128 + r,
+                    hq * 32);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace pstbwd
+
+int launch_attn_dsum(const void* out, const void* dout, float* dsum, int64_t T, int64_t S, int64_t H,
+                     cudaStream_t stream);
+
+// Host launcher used by cdk_attn_bwd for S <= 256.
+int launch_attn_bwd_pst(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,
+                        void* dqkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,
+                        const int32_t* meta, const float* rope, cudaStream_t stream) {
+  using namespace pstbwd;
+  if (S > kMaxS || S <= 0) return -20;
+  if (nseq * H > (int64_t)1 << 30) return -5;
+  CUtensorMap tq, tdo;
+  if (!make_tmap(&tq, qkv, 3 * H * kHd, nseq * S, 3 * H * kHd, 64, 64)) return -21;
+  if (!make_tmap(&tdo, dout, H * kHd, nseq * S, H * kHd, 64, 64)) return -21;
+  int rc = launch_attn_dsum(out, dout, dsum, nseq * S, S, H, stream);
+  if (rc != 0) return rc;
+  Args a;
+  a.lse = lse;
+  a.dsum = dsum;
+  a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv);
+  const int64_t np = nseq - n_causal;
+  const int nt64 = (int)((S + 63) / 64);
+  a.bid = bid;
+  a.q_lo = meta;
+  a.first = np > 0 ? meta + np * 2 * nt64 : nullptr;
+  a.rope = rope;
+  a.S = (int)S;
+  a.H = (int)H;
+  a.n_causal = (int)n_causal;
+  a.nt64 = nt64;
+  a.n_items = (int)(nseq * H);
+  const size_t smem = sizeof(BwdSmem) + 1024;
+  static int sm_count[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return -24;
+  if (sm_count[dev] == 0) {
+    cudaError_t e = cudaFuncSetAttribute(attn_bwd_pst_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    // tcgen05.alloc blocks until columns are free: one 512-column CTA per SM
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_bwd_pst_kernel, kThreads, smem);
+    if (e != cudaSuccess) return (int)e;
+    if (per_sm != 1) return -22;
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return (int)e;
+    sm_count[dev] = sms;
+  }
+  const int grid = (int)(nseq * H < sm_count[dev] ? nseq * H : sm_count[dev]);
+  attn_bwd_pst_kernel<<<grid, kThreads, smem, stream>>>(tq, tdo, a);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+}  // namespace cdk

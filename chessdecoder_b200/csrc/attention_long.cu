@@ -735,6 +735,16 @@ int launch_attn_fwd_long(const void* qkv, void* out, float* lse, int64_t nseq, i
 }  // namespace cdk
 
 namespace cdk {
+// D[seq, h, i] = rowsum(dO * O) of every query row (the pass before the backward kernels).
+int launch_attn_dsum(const void* out, const void* dout, float* dsum, int64_t T, int64_t S, int64_t H,
+                     cudaStream_t stream) {
+  tclong::attn_dsum_kernel<<<(unsigned)((T + 7) / 8), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(out), reinterpret_cast<const __nv_bfloat16*>(dout), dsum, T, (int)S,
+      (int)H);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
 // Host launcher used by cdk_attn_bwd for S > 256 (workspace: fp32 [nseq*S, E]).
 int launch_attn_bwd_long(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,
                          void* dqkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,

@@ -114,6 +114,31 @@ def param_specs(cfg: ModelConfig):
     return specs
 
 
+def reference_param_names(cfg: ModelConfig):
+    """Parameter names in the order of the reference model's ``parameters()``
+    (its construction order, chessdecoder/models/model.py:84-132: embedding;
+    per layer q, k, v, output projections, w1, w2, w3 (or the MoE variant's
+    router and experts), sa_norm, mlp_norm; final norm; board, policy and
+    thinking heads; WL / D value heads; Fourier encoder) -- the indices of a
+    ``torch.optim`` optimizer's ``state_dict`` built on those parameters."""
+    names = ["tok_embedding.weight"]
+    for i in range(cfg.num_layers):
+        p = f"layers.{i}."
+        names += [p + f"attn.{n}.weight" for n in ("q_proj", "k_proj", "v_proj", "output_proj")]
+        if cfg.moe_experts:
+            names += [p + "mlp.router.weight", p + "mlp.experts.w13", p + "mlp.experts.w2"]
+        else:
+            names += [p + "mlp.w1.weight", p + "mlp.w2.weight", p + "mlp.w3.weight"]
+        names += [p + "sa_norm.scale", p + "mlp_norm.scale"]
+    names.append("norm.scale")
+    for h in ("board_head", "policy_head", "thinking_policy_head"):
+        names += [h + ".weight", h + ".bias"]
+    for h in ("wl_head", "d_head"):
+        names += [f"{h}.mlp.0.weight", f"{h}.mlp.0.bias", f"{h}.mlp.2.weight", f"{h}.mlp.2.bias"]
+    names += ["fourier_encoder.frequencies", "fourier_encoder.proj.weight", "fourier_encoder.proj.bias"]
+    return names
+
+
 # Tensors that must stay adjacent (fused GEMM operands): q|k|v and w1|w3.
 _ALIGN = 64  # elements: every parameter starts on a 256-byte boundary
 
@@ -193,6 +218,49 @@ class ParamStore:
             sd["thinking_policy_head.weight"] = self.thinking_weight.clone()
             sd["thinking_policy_head.bias"] = self.thinking_bias.clone()
         return sd
+
+    # -- AdamW state in torch.optim.AdamW's state_dict layout ------------------
+    def optimizer_state_dict(self, lr, betas, eps, weight_decay) -> dict:
+        """The moments and step count as ``torch.optim.AdamW(model.parameters())
+        .state_dict()`` holds them (per-parameter index in the reference model's
+        parameter order; parameters that never had a step -- the thinking head
+        in pretraining -- have no entry), so a reference checkpoint's optimizer
+        can resume from it and the other way round."""
+        names = reference_param_names(self.cfg)
+        state = {}
+        if self.step > 0:
+            for i, n in enumerate(names):
+                if n in self.offsets:
+                    state[i] = {"step": torch.tensor(float(self.step)),
+                                "exp_avg": self._view(self.exp_avg, n).detach().clone(),
+                                "exp_avg_sq": self._view(self.exp_avg_sq, n).detach().clone()}
+        group = {"lr": lr, "betas": tuple(betas), "eps": eps, "weight_decay": weight_decay, "amsgrad": False,
+                 "maximize": False, "foreach": None, "capturable": False, "differentiable": False, "fused": None,
+                 "decoupled_weight_decay": True, "params": list(range(len(names)))}
+        return {"state": state, "param_groups": [group]}
+
+    def load_optimizer_state_dict(self, sd: dict):
+        """Moments and step count from an AdamW state_dict in the reference
+        parameter order (see ``optimizer_state_dict``).  Returns the param
+        group (its lr, betas, eps, weight_decay)."""
+        names = reference_param_names(self.cfg)
+        if len(sd["param_groups"]) != 1 or len(sd["param_groups"][0]["params"]) != len(names):
+            raise ValueError("optimizer state_dict does not match this model's parameters")
+        steps = set()
+        with torch.no_grad():
+            self.exp_avg.zero_()
+            self.exp_avg_sq.zero_()
+            for i, st in sd["state"].items():
+                n = names[int(i)]
+                if n not in self.offsets:
+                    continue  # e.g. a trained thinking head: pretraining leaves it out of AdamW
+                self._view(self.exp_avg, n).copy_(st["exp_avg"].reshape(self.offsets[n][1]))
+                self._view(self.exp_avg_sq, n).copy_(st["exp_avg_sq"].reshape(self.offsets[n][1]))
+                steps.add(int(float(st["step"])))
+        if len(steps) > 1:
+            raise ValueError(f"parameters at different AdamW steps {sorted(steps)}: one shared step count expected")
+        self.step = steps.pop() if steps else 0
+        return sd["param_groups"][0]
 
     def layer_grad_span(self, i: int):
         """[start, end) of layer i's gradients in the flat buffer."""
@@ -891,6 +959,33 @@ class TrainStep:
         losses = self.forward_backward(db, metrics)
         self.optimizer_step()
         return losses
+
+    # -- checkpoints (chessdecoder/utils/training.py:136-157, train/train.py:81-104) --
+    def optimizer_state_dict(self) -> dict:
+        return self.store.optimizer_state_dict(self.lr, self.betas, self.eps, self.wd)
+
+    def load_optimizer_state_dict(self, sd: dict):
+        """AdamW moments and step from a state_dict in the reference layout; the
+        configured learning rate is kept (train.py:95-96 re-applies it on resume)."""
+        g = self.store.load_optimizer_state_dict(sd)
+        self.betas, self.eps, self.wd = tuple(g["betas"]), g["eps"], g["weight_decay"]
+
+    def checkpoint(self, step: int, extra_state: Optional[dict] = None) -> dict:
+        """The dict save_training_checkpoint writes: step, model / optimizer /
+        scaler state (the bf16 step needs no loss scaling: an empty scaler
+        state, as a disabled GradScaler's), plus ``extra_state``."""
+        ck = {"step": step, "model_state_dict": self.store.state_dict(),
+              "optimizer_state_dict": self.optimizer_state_dict(), "scaler_state_dict": {}}
+        if extra_state:
+            ck.update(extra_state)
+        return ck
+
+    def load_checkpoint(self, ck: dict):
+        """Weights and optimizer state from a checkpoint dict (the reference's
+        or ``checkpoint()``'s); returns its step."""
+        self.store.load_state_dict({k: v.to(self.device) for k, v in ck["model_state_dict"].items()})
+        self.load_optimizer_state_dict(ck["optimizer_state_dict"])
+        return ck.get("step", 0)
 
     @staticmethod
     def total(losses, weights=(5.0, 1.0, 1.0, 1.0)):
