@@ -1121,7 +1121,7 @@ static int attn_path() {
   if (v && v[0] == 'l') return 3;                  // tcgen05 long-sequence kernels at any S
   return 0;                                        // tcgen05
 }
-static bool long_path(int64_t S) { return (S > kSeqMax && attn_path() == 0) || attn_path() == 3; }
+static bool long_path(int64_t S) { return (S > kSeqMax && (attn_path() == 0 || attn_path() == 5)) || attn_path() == 3; }
 static bool seq_path_enabled() { return attn_path() != 2; }
 
 namespace cdk {
