@@ -41,7 +41,7 @@ constexpr int kMaxS = 256;
 constexpr int kBox = 64 * 128;  // one TMA box: 64 rows x 128 B
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kThreads = 320;   // warp 0 producer, warp 1 MMA, warps 2-9 elementwise
-constexpr int kMaxUnits = 8;    // sub-units of one item (two key tiles x two query halves x 2)
+constexpr int kMaxUnits = 8;    // sub-units of one item (two key tiles x two query halves x 2; 3 bits each)
 
 struct Meta {
   alignas(16) float L[kMaxS];   // base-2 log-sum-exp of each query row (0 past S)
@@ -107,15 +107,19 @@ __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.
 
 // The sub-units of an item: key tile kt (k-major), query sub-tile qs; pairs of
 // sub-tiles (2 qh, 2 qh + 1) from the first query half that can see the key
-// tile.  Returns the count; u_kt / u_qs filled.
+// tile.  Packed into one register word (3 bits per sub-unit: kt << 2 | qs) so
+// that a runtime sub-unit index never touches local memory.
 struct Units {
   int n;
-  int8_t kt[kMaxUnits], qs[kMaxUnits];
+  uint32_t code;
+  __device__ __forceinline__ int kt(int u) const { return (int)((code >> (3 * u + 2)) & 1u); }
+  __device__ __forceinline__ int qs(int u) const { return (int)((code >> (3 * u)) & 3u); }
 };
 
 __device__ __forceinline__ Units item_units(const Args& a, bool prefix, int pseq) {
   Units u;
   u.n = 0;
+  u.code = 0;
   const int nkt = (a.S + 127) / 128;
   for (int kt = 0; kt < nkt; ++kt) {
     int qh0 = kt;
@@ -126,10 +130,8 @@ __device__ __forceinline__ Units item_units(const Args& a, bool prefix, int pseq
       qh0 = q0 / 128;
     }
     for (int qh = qh0; qh < nkt; ++qh) {
-      u.kt[u.n] = (int8_t)kt;
-      u.qs[u.n] = (int8_t)(2 * qh);
-      u.kt[u.n + 1] = (int8_t)kt;
-      u.qs[u.n + 1] = (int8_t)(2 * qh + 1);
+      u.code |= (uint32_t)((kt << 2) | (2 * qh)) << (3 * u.n);
+      u.code |= (uint32_t)((kt << 2) | (2 * qh + 1)) << (3 * (u.n + 1));
       u.n += 2;
     }
   }
@@ -297,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // start after this item's release commits.
       auto issue_a = [&](int max_item) {
         if (!next_a() || ka > max_item) return;
-        const int kt = units_a.kt[ua], qs = units_a.qs[ua], qh = qs >> 1;
+        const int kt = units_a.kt(ua), qs = units_a.qs(ua), qh = qs >> 1;
         const int b = g_issued & 1;
         mbar_wait(&sm.kvfull[kt], ka & 1, abort_flag);
         mbar_wait(&sm.qfull[qh], ka & 1, abort_flag);
@@ -324,14 +326,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int seq = item / H;
         const Units un = item_units(a, seq >= a.n_causal, seq - a.n_causal);
         // last sub-unit reading each query slot
-        int last_q[2] = {-1, -1};
-        for (int u = 0; u < un.n; ++u) last_q[un.qs[u] >> 1] = u;
+        int last_q0 = -1, last_q1 = -1;
+        for (int u = 0; u < un.n; ++u) {
+          if ((un.qs(u) >> 1) == 0) last_q0 = u;
+          else last_q1 = u;
+        }
         uint32_t dq_seen = 0;
         for (int u = 0; u < un.n; ++u, ++g) {
-          const int kt = un.kt[u], qs = un.qs[u], qh = qs >> 1;
+          const int kt = un.kt(u), qs = un.qs(u), qh = qs >> 1;
           const int b = g & 1, pb = (g >> 1) & 1;
-          const bool first_kt = u == 0 || un.kt[u - 1] != kt;
-          const bool last_kt = u == un.n - 1 || un.kt[u + 1] != kt;
+          const bool first_kt = u == 0 || un.kt(u - 1) != kt;
+          const bool last_kt = u == un.n - 1 || un.kt(u + 1) != kt;
           mbar_wait(&sm.ew[b], (g >> 1) & 1, abort_flag);
           if (first_kt && c > 0) mbar_wait(&sm.kvfree, (c - 1) & 1, abort_flag);
           tc_fence_after();
@@ -364,8 +369,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_commit(&sm.kvempty[kt]);
             ++c;
           }
-          if (u == last_q[0]) tc_commit(&sm.qempty[0]);
-          if (u == last_q[1]) tc_commit(&sm.qempty[1]);
+          if (u == last_q0) tc_commit(&sm.qempty[0]);
+          if (u == last_q1) tc_commit(&sm.qempty[1]);
           if (u == un.n - 1) tc_commit(&sm.dqdone);
           // keep MMA-A two sub-units ahead; across an item boundary only once
           // every release commit of this item has been issued
@@ -393,9 +398,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool contig = mt.contig != 0;
       __nv_bfloat16* rowbase = a.dqkv + (long long)(seq * S) * 3 * E;
       for (int u = 0; u < un.n; ++u, ++g) {
-        const int kt = un.kt[u], qs = un.qs[u];
+        const int kt = un.kt(u), qs = un.qs(u);
         const int b = g & 1, P = g >> 1, pb = P & 1;
-        const bool last_kt = u == un.n - 1 || un.kt[u + 1] != kt;
+        const bool last_kt = u == un.n - 1 || un.kt(u + 1) != kt;
         const int j = kt * 128 + r;
         const bool jok = j < S;
         const int fj = jok ? mt.first[j] : S;

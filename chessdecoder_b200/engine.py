@@ -143,6 +143,21 @@ def reference_param_names(cfg: ModelConfig):
 _ALIGN = 64  # elements: every parameter starts on a 256-byte boundary
 
 
+def flat_layout(cfg: ModelConfig):
+    """({name: (offset, shape, numel)}, total elements) of the flat parameter
+    buffers: param_specs order, every tensor 256-byte aligned except that
+    q|k|v and w1|w3 are packed back to back so the fused projections read one
+    [3E, E] / [2F, E] matrix."""
+    offsets = {}
+    off = 0
+    for name, shape in param_specs(cfg):
+        n = int(np.prod(shape))
+        offsets[name] = (off, shape, n)
+        pad = 0 if name.endswith(("q_proj.weight", "k_proj.weight", "mlp.w1.weight")) else _ALIGN
+        off += n if pad == 0 else (n + _ALIGN - 1) // _ALIGN * _ALIGN
+    return offsets, off
+
+
 class ParamStore:
     """All trainable parameters in one flat fp32 buffer, with matching flat
     gradient, AdamW moment and bf16 shadow buffers.  ``param(name)`` returns a
@@ -151,15 +166,7 @@ class ParamStore:
     def __init__(self, cfg: ModelConfig, device, optimizer_state: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
-        self.offsets = {}
-        off = 0
-        for name, shape in param_specs(cfg):
-            n = int(np.prod(shape))
-            self.offsets[name] = (off, shape, n)
-            # q/k/v and w1/w3 are packed back to back (no padding) so that the
-            # fused projections read one [3E,E] / [2F,E] matrix.
-            pad = 0 if name.endswith(("q_proj.weight", "k_proj.weight", "mlp.w1.weight")) else _ALIGN
-            off += n if pad == 0 else (n + _ALIGN - 1) // _ALIGN * _ALIGN
+        self.offsets, off = flat_layout(cfg)
         self.numel = off
         self.flat = torch.zeros(off, dtype=torch.float32, device=self.device)
         self.flat16 = torch.zeros(off, dtype=torch.bfloat16, device=self.device)
@@ -593,8 +600,12 @@ class Backbone:
                      w2=st.grad_of(p + "mlp.w2.weight"))
         return d
 
-    def forward(self, h, nseq, n_causal, S, bid32=None, meta=None, want_f32=False):
+    def forward(self, h, nseq, n_causal, S, bid32=None, meta=None, want_f32=False, rope=None):
+        """rope: optional [S, head_dim/2, 2] table whose row s rotates sequence
+        position s (the module's ``input_pos``: table = cache[input_pos]);
+        default the cache itself (position s = s)."""
         cfg = self.cfg
+        rope = self.rope if rope is None else rope
         E, F, H = cfg.embed_dim, cfg.ff, cfg.num_heads
         T = h.shape[0]
         dev = h.device
@@ -613,11 +624,11 @@ class Backbone:
             K.rmsnorm_fwd(x, w["s1"], y16=s.n1, rstd=s.r1)
             s.qkv = torch.empty(T, 3 * E, device=dev, dtype=torch.bfloat16)
             if f8 is None:
-                K.gemm(s.n1, w["wqkv"], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=self.rope, seq_len=S, rope_cols=2 * E)
+                K.gemm(s.n1, w["wqkv"], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=rope, seq_len=S, rope_cols=2 * E)
             else:
                 x8 = s.n1T = f8.cast(s.n1, f8.site(i, "qkv", "x"), E4)
                 s.n1 = None
-                K.gemm(x8, f8.weights[(i, "qkv")], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=self.rope, seq_len=S,
+                K.gemm(x8, f8.weights[(i, "qkv")], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=rope, seq_len=S,
                        rope_cols=2 * E, fp8=self._f8(i, "qkv", "x", E4, "w", E4))
             s.ao = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
             s.lse = torch.empty(nseq * H * S, device=dev)
@@ -661,12 +672,12 @@ class Backbone:
         hN32 = torch.empty(T, E, device=dev) if want_f32 else None
         rN = torch.empty(T, device=dev)
         K.rmsnorm_fwd(x, self.st.param("norm.scale"), y16=hN16, y32=hN32, rstd=rN)
-        return hN16, hN32, (saved, x, rN, nseq, n_causal, S, bid32, meta)
+        return hN16, hN32, (saved, x, rN, nseq, n_causal, S, bid32, meta, rope)
 
     def backward(self, dhN, ctx, on_layer_done: Optional[Callable[[int], None]] = None):
         """dhN: f32 [T,E] gradient of the final-norm output.  Accumulates every
         backbone weight gradient into the store; returns d(embedding output)."""
-        saved, xL, rN, nseq, n_causal, S, bid32, meta = ctx
+        saved, xL, rN, nseq, n_causal, S, bid32, meta, rope = ctx
         cfg, st = self.cfg, self.st
         E, F, H = cfg.embed_dim, cfg.ff, cfg.num_heads
         T = dhN.shape[0]
@@ -722,7 +733,7 @@ class Backbone:
                        fp8=self._f8(i, "o", "g", E5, "w", E4))
                 K.gemm(g8, s.aoT, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wo"],
                        fp8=self._f8(i, "o", "g", E5, "x", E4))
-            K.attn_bwd(s.qkv, s.ao, dao, s.lse, dsum, dqkv, nseq, n_causal, S, H, bid32, meta, rope=self.rope)
+            K.attn_bwd(s.qkv, s.ao, dao, s.lse, dsum, dqkv, nseq, n_causal, S, H, bid32, meta, rope=rope)
             if f8 is None:
                 K.gemm(dqkv, w["wqkv"], b_mn=True, kind=K.EPI_STORE_BF16, out=dn)
                 K.gemm(dqkv, s.n1, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wqkv"])

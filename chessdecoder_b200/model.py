@@ -39,6 +39,7 @@ import torch
 import torch.nn as nn
 
 from . import kernels as K
+from . import ops as _ops  # noqa: F401  (registers the cdk:: custom ops)
 from . import vocab as V
 from .engine import (Backbone, FrontEnd, ModelConfig, ParamStore, make_d_buckets, make_wl_buckets,
                      rope_table)
@@ -115,66 +116,14 @@ class FourierEncoder(_WeightsOnly):
 # ---------------------------------------------------------------------------
 # Linear on the tcgen05 GEMM (the heads)
 # ---------------------------------------------------------------------------
-def _pad_cols(n: int, mult: int) -> int:
-    return (n + mult - 1) // mult * mult
-
-
-class _LinearFn(torch.autograd.Function):
-    """y = x W^T + b with bf16 operands and fp32 accumulation / output;
-    dX, dW (fp32, split-K atomics) and db in the backward."""
-
-    @staticmethod
-    def forward(ctx, x, weight, bias):
-        n_out, n_in = weight.shape
-        lead = x.shape[:-1]
-        x2 = x.reshape(-1, n_in)
-        M = x2.shape[0]
-        if n_in % 8:
-            raise ValueError("chessdecoder_b200.Linear needs in_features % 8 == 0")
-        x16 = x2.to(torch.bfloat16).contiguous()
-        w16 = weight.detach().to(torch.bfloat16).contiguous()
-        out = torch.empty(M, _pad_cols(n_out, 4), device=x.device)
-        if M:
-            K.gemm(x16, w16, kind=K.EPI_STORE_F32, out=out,
-                   bias=None if bias is None else bias.detach().contiguous(), N=n_out)
-        ctx.save_for_backward(x16, w16)
-        ctx.has_bias = bias is not None
-        ctx.lead = lead
-        return out[:, :n_out].view(*lead, n_out)
-
-    @staticmethod
-    def backward(ctx, dy):
-        x16, w16 = ctx.saved_tensors
-        n_out, n_in = w16.shape
-        dy2 = dy.reshape(-1, n_out)
-        M = dy2.shape[0]
-        dy16 = torch.zeros(M, _pad_cols(n_out, 8), device=dy.device, dtype=torch.bfloat16)
-        dy16[:, :n_out] = dy2
-        dx = dw = db = None
-        if ctx.needs_input_grad[0]:
-            dx = torch.empty(M, n_in, device=dy.device)
-            if M:
-                K.gemm(dy16, w16, b_mn=True, kind=K.EPI_STORE_F32, out=dx, K=n_out)
-            else:
-                dx.zero_()
-            dx = dx.view(*ctx.lead, n_in)
-        if ctx.needs_input_grad[1]:
-            dw = torch.zeros(n_out, n_in, device=dy.device)
-            if M:
-                K.gemm(dy16, x16, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=dw, M=n_out, K=M)
-        if ctx.has_bias and ctx.needs_input_grad[2]:
-            db = dy2.float().sum(0)
-        return dx, dw, db
-
-
 class Linear(nn.Linear):
     """``nn.Linear`` (same parameters, init and state dict) whose forward is
-    the bf16 tcgen05 GEMM with an fp32 output."""
+    the bf16 tcgen05 GEMM with an fp32 output (the ``cdk::linear`` op)."""
 
     def forward(self, x):
         if not x.is_cuda:
             _cuda_only("Linear")
-        return _LinearFn.apply(x, self.weight, self.bias)
+        return torch.ops.cdk.linear(x, self.weight, self.bias)
 
 
 class ValueHead(nn.Module):
@@ -268,7 +217,7 @@ class _Core:
 
     def plain_leaves(self) -> bool:
         """True when no backbone parameter carries gradient hooks, so the
-        backward may write ``p.grad`` itself (see _BackboneFn.backward)."""
+        backward may write ``p.grad`` itself (see ops._bb_bwd)."""
         for i in self.backbone_idx:
             p = self.params[i]
             if p._backward_hooks or getattr(p, "_post_accumulate_grad_hooks", None):
@@ -302,56 +251,6 @@ class _Core:
         t.slot = torch.full((B * S,), -1, device=dev, dtype=torch.int32)
         t.slot[t.frows.long()] = torch.arange(t.frows.numel(), device=dev, dtype=torch.int32)
         return t
-
-
-class _BackboneFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, core: _Core, x, prefix: bool, bid32, inputs: _Inputs, *params):
-        B, S = x.shape
-        E = core.cfg.embed_dim
-        h0, fctx = core.front.forward(inputs, n_copies=1, snap=False)
-        meta = K.attn_meta(bid32, S) if prefix else None
-        n_causal = 0 if prefix else B
-        _, h32, bctx = core.backbone.forward(h0, B, n_causal, S, bid32 if prefix else None, meta, want_f32=True)
-        ctx.core, ctx.inputs, ctx.fctx, ctx.bctx = core, inputs, fctx, bctx
-        return h32.view(B, S, E)
-
-    @staticmethod
-    def backward(ctx, dh):
-        """All gradient writes of the hand-written backward accumulate (+=),
-        so a second backward before ``zero_grad`` (the two passes of one step,
-        or gradient accumulation) runs straight into the buffer that already
-        backs ``p.grad``.  The first one allocates the buffer and makes its
-        views the parameters' ``.grad``.  Autograd's own accumulation is used
-        instead (views returned as input gradients) when a parameter has
-        gradient hooks or a graph of the backward is being built."""
-        core = ctx.core
-        st = core.store
-        E = core.cfg.embed_dim
-        n_in = 5 + len(core.backbone_idx)
-        direct = core.plain_leaves() and not torch.is_grad_enabled()
-        buf = core.grad_buffer() if direct else None
-        fresh = buf is None
-        if fresh:
-            buf = torch.zeros(st.numel, device=dh.device)
-        st.grad = buf
-        try:
-            dh0 = core.backbone.backward(dh.reshape(-1, E).to(torch.float32).contiguous(), ctx.bctx)
-            core.front.backward(ctx.inputs, dh0, ctx.fctx, n_copies=1)
-        finally:
-            st.grad = None
-        ctx.bctx = ctx.fctx = None
-        views = [st._view(buf, core.names[i]) for i in core.backbone_idx]
-        if not direct:
-            return (None, None, None, None, None) + tuple(views)
-        if fresh:
-            for i, g in zip(core.backbone_idx, views):
-                p = core.params[i]
-                if p.grad is None:
-                    p.grad = g
-                else:
-                    p.grad.add_(g)
-        return (None,) * n_in
 
 
 # ---------------------------------------------------------------------------
@@ -396,8 +295,21 @@ class ChessDecoder(nn.Module):
         self.register_buffer("wl_bucket_centers", make_wl_buckets(n_buckets, wl_sigma))
         self.register_buffer("d_bucket_centers", make_d_buckets(n_buckets))
         self._core: Optional[_Core] = None
+        self._op_id = _ops.register_model(self)
 
     # -- flat parameter binding ------------------------------------------------
+    @staticmethod
+    def _is_backbone(name: str) -> bool:
+        return not name.startswith(_HEADS)
+
+    def _backbone_params(self):
+        """The backbone Parameters in the flat store's order (what the
+        ``cdk::backbone_fwd`` op receives), without binding the store."""
+        if self._core is not None and self._core.bound():
+            return self._core.backbone_params()
+        from .engine import param_specs
+        return [self.get_parameter(n) for n, _ in param_specs(self.cfg) if not n.startswith(_HEADS)]
+
     def _bind(self, device) -> _Core:
         core = self._core
         if core is None or core.device != device or not core.bound():
@@ -417,7 +329,11 @@ class ChessDecoder(nn.Module):
         mask_type "causal" or "prefix" (causal + bidirectional inside each
         block_id run); the Fourier encoding of ``wl_values`` / ``d_values``
         replaces the embedding at ``wl_positions`` / ``d_positions`` (d wins
-        where both are set).  ``input_pos`` must be None or arange(S)."""
+        where both are set).  ``input_pos`` ([S], or [B, S] with every row the
+        same) gives the RoPE position of each sequence position (model.py:
+        156-157); positions that differ between the sequences of a batch
+        raise NotImplementedError.  The backbone is the ``cdk::backbone_fwd``
+        op (chessdecoder_b200/ops.py)."""
         bsz, seq_len = x.shape
         prefix = mask_type != "causal"
         if prefix and block_id is None:
@@ -426,14 +342,10 @@ class ChessDecoder(nn.Module):
             _cuda_only("ChessDecoder.forward")
         if seq_len > self.cfg.max_seq_len:
             raise ValueError(f"sequence length {seq_len} exceeds max_seq_len {self.cfg.max_seq_len}")
-        if input_pos is not None:
-            ar = torch.arange(seq_len, device=input_pos.device)
-            if not bool((input_pos == ar).all()):
-                raise NotImplementedError("chessdecoder_b200.ChessDecoder supports input_pos = arange(S) only")
-        core = self._bind(x.device)
-        inputs = core.inputs(x, wl_values, d_values, wl_positions, d_positions)
-        bid32 = block_id.to(torch.int32).contiguous() if prefix else None
-        return _BackboneFn.apply(core, x, prefix, bid32, inputs, *core.backbone_params())
+        pos = input_pos.reshape(-1, seq_len) if input_pos is not None else None
+        h, _ = torch.ops.cdk.backbone_fwd(x, wl_values, d_values, wl_positions, d_positions,
+                                          block_id if prefix else None, pos, self._op_id, self._backbone_params())
+        return h
 
     def discretize_to_bucket(self, values, bucket_centers):
         """Nearest bucket centre (model.py:189-194; first index on ties)."""
@@ -446,31 +358,12 @@ def soft_bucket_loss(logits, target_values, bucket_centers, valid_mask):
     mean of -sum(soft * log_softmax(logits)); a constant 0 (no graph) when
     there are no rows or no valid rows."""
     N = target_values.shape[0]
-    if N == 0 or valid_mask.sum() == 0:
+    traced = torch.compiler.is_compiling() or torch._guards.detect_fake_mode(logits) is not None
+    if not traced and (N == 0 or valid_mask.sum() == 0):
         return torch.tensor(0.0, device=logits.device)
     if not logits.is_cuda:
         _cuda_only("soft_bucket_loss")
-    return _SoftBucketFn.apply(logits, target_values, bucket_centers, valid_mask)
-
-
-class _SoftBucketFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, logits, target, centers, valid):
-        lg = logits.detach().to(torch.float32).contiguous()
-        vf = valid.to(torch.float32).contiguous()
-        norm = 1.0 / (vf.sum() + 1e-8)
-        loss = torch.zeros(1, device=lg.device)
-        dl = torch.empty_like(lg)
-        K.soft_bucket_ce(lg, target.to(torch.float32).contiguous(), vf, centers.to(torch.float32).contiguous(),
-                         norm.reshape(1), 1.0, dlogits=dl, loss_out=loss)
-        ctx.save_for_backward(dl)
-        ctx.dtype = logits.dtype
-        return loss.reshape(())
-
-    @staticmethod
-    def backward(ctx, g):
-        (dl,) = ctx.saved_tensors
-        return (dl * g).to(ctx.dtype), None, None, None
+    return torch.ops.cdk.soft_bucket_ce(logits, target_values, bucket_centers, valid_mask)[0]
 
 
 def prepare_fourier_inputs(model, wl_targets, d_targets, wl_positions, d_positions):
