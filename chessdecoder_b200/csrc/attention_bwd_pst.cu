@@ -24,12 +24,12 @@
 //
 //   warp 0       producer: row metadata (L, D, block bounds) and TMA loads
 //   warp 1       TMEM allocation, MMA issue (lane 0)
-//   warps 2-9    elementwise + epilogues: thread = (key row r = TMEM lane,
-//                query half hq of the sub-tile: 32 queries)
+//   warps 2-17   elementwise + epilogues: thread = (key row r = TMEM lane,
+//                16-query group g of the sub-tile)
 // TMEM: S^T|dP^T x 2 [0, 256) | dV [256, 320) | dK [320, 384) | dQ_0 [384, 448)
 // | dQ_1 [448, 512).  P^T (bf16) is written over the thread's own S^T columns
-// after it has read them: queries [0, 32) -> columns [0, 16), [32, 64) ->
-// [32, 48) of the buffer.  Every wait is bounded (cdk_common).
+// after it has read them: queries [16 g, 16 g + 16) -> columns [16 g, 16 g + 8)
+// of the buffer.  Every wait is bounded (cdk_common).
 #include "../../include/cdk.h"
 #include "cdk_common.cuh"
 
@@ -40,7 +40,7 @@ constexpr int kHd = 64;
 constexpr int kMaxS = 256;
 constexpr int kBox = 64 * 128;  // one TMA box: 64 rows x 128 B
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kThreads = 320;   // warp 0 producer, warp 1 MMA, warps 2-9 elementwise
+constexpr int kThreads = 576;   // warp 0 producer, warp 1 MMA, warps 2-17 elementwise
 constexpr int kMaxUnits = 8;    // sub-units of one item (two key tiles x two query halves x 2; 3 bits each)
 
 struct Meta {
@@ -82,25 +82,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-
-// tcgen05.wait::ld naming the loaded registers, so no use is scheduled before it.
-__device__ __forceinline__ void tmem_wait_ld_dep(uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.wait::ld.sync.aligned;"
-      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-        "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
-        "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
-        "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
-      :
-      : "memory");
+__device__ __forceinline__ void tmem_wait_ld_dep16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -138,17 +126,17 @@ __device__ __forceinline__ Units item_units(const Args& a, bool prefix, int pseq
   return u;
 }
 
-// dX (bf16) of 32 consecutive dims [c0, c0 + 32) of a row: value * 0.125 with the
+// dX (bf16) of 16 consecutive dims [c0, c0 + 16) of a row: value * 0.125 with the
 // inverse RoPE rotation of position pos when rope != null (scale_rope), or as is.
-__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t (&v)[32], bool scale_rope,
+__device__ __forceinline__ void store_row16(__nv_bfloat16* dst, const uint32_t (&v)[16], bool scale_rope,
                                             const float* rope, int pos, int c0) {
-  float f[32];
+  float f[16];
   #pragma unroll
-  for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(v[e]) * (scale_rope ? 0.125f : 1.f);
+  for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]) * (scale_rope ? 0.125f : 1.f);
   if (scale_rope && rope != nullptr) {
     const float4* cs = reinterpret_cast<const float4*>(rope + ((long long)pos * 32 + c0 / 2) * 2);
     #pragma unroll
-    for (int p = 0; p < 8; ++p) {
+    for (int p = 0; p < 4; ++p) {
       const float4 t = cs[p];  // (cos, sin) of two consecutive pairs
       float x0 = f[4 * p], x1 = f[4 * p + 1];
       f[4 * p] = x0 * t.x + x1 * t.y;
@@ -161,7 +149,7 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t (
   }
   uint4* d = reinterpret_cast<uint4*>(dst);
   #pragma unroll
-  for (int q = 0; q < 4; ++q)
+  for (int q = 0; q < 2; ++q)
     d[q] = make_uint4(pack_bf16(f[8 * q], f[8 * q + 1]), pack_bf16(f[8 * q + 2], f[8 * q + 3]),
                       pack_bf16(f[8 * q + 4], f[8 * q + 5]), pack_bf16(f[8 * q + 6], f[8 * q + 7]));
 }
@@ -185,15 +173,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.qfull[s], 1);
       mbar_init(&sm.qempty[s], 1);
       mbar_init(&sm.mfull[s], 32);
-      mbar_init(&sm.mempty[s], 256);
+      mbar_init(&sm.mempty[s], 512);
       mbar_init(&sm.sa[s], 1);
-      mbar_init(&sm.ew[s], 256);
+      mbar_init(&sm.ew[s], 512);
       mbar_init(&sm.dq[s], 1);
     }
     mbar_init(&sm.kvdone, 1);
-    mbar_init(&sm.kvfree, 256);
+    mbar_init(&sm.kvfree, 512);
     mbar_init(&sm.dqdone, 1);
-    mbar_init(&sm.dqfree, 256);
+    mbar_init(&sm.dqfree, 512);
     sm.abort = 0;
     fence_mbar_init();
   }
@@ -345,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {  // 64 queries, 16 per step
             const uint32_t acc = (!first_kt || kk > 0) ? 1u : 0u;
-            const uint32_t pcol = (uint32_t)(b * 128 + kk * 8 + (kk >= 2 ? 16 : 0));
+            const uint32_t pcol = (uint32_t)(b * 128 + kk * 16);
             umma_f16_ts(tmem + 256, tmem + pcol, make_sdesc(ob + kk * 2048, 8192, 1024), id_kn, acc);
             umma_f16(tmem + 320, make_sdesc(dsb + kk * 32, 16, 1024), make_sdesc(qb + kk * 2048, 8192, 1024), id_kn,
                      acc);
@@ -382,11 +370,54 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---- elementwise + epilogues -------------------------------------------
     const int quad = warp & 3;
-    const int hq = (warp - 2) >> 2;  // query half of the 64-query sub-tile
+    const int g4 = (warp - 2) >> 2;  // 16-query group of the 64-query sub-tile
     const int r = quad * 32 + lane;  // key row within the key tile = TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const float sl2 = 0.125f * kLog2e;
     int g = 0, c = 0;
+    // The epilogues run one sub-unit late: after the last sub-unit of a key
+    // tile (or of an item) the warps go on with the next sub-unit, whose MMA-A
+    // is already in flight, while that tile's last products retire.
+    int kv_pend = -1, kv_j0 = 0, kv_h = 0;  // pending dV / dK store: block index, first key row, head
+    __nv_bfloat16* kv_rows = nullptr;
+    int dq_pend = -1, dq_h = 0;             // pending dQ store: item index, head
+    __nv_bfloat16* dq_rows = nullptr;
+    auto kv_epilogue = [&]() {
+      // dV, dK of the key tile complete: this thread stores dims [16 g, 16 g + 16) of its key row
+      mbar_wait(&sm.kvdone, kv_pend & 1, abort_flag);
+      tc_fence_after();
+      uint32_t vv[16], kv[16];
+      tmem_ld_x16_nowait(tmem + lane_off + 256 + g4 * 16, vv);
+      tmem_ld_x16_nowait(tmem + lane_off + 320 + g4 * 16, kv);
+      tmem_wait_ld_dep16(vv);
+      tmem_wait_ld_dep16(kv);
+      tc_fence_before();
+      mbar_arrive(&sm.kvfree);
+      const int j = kv_j0 + r;
+      if (j < S) {
+        __nv_bfloat16* rowp = kv_rows + (long long)j * 3 * E;
+        store_row16(rowp + E + kv_h * kHd + g4 * 16, kv, true, a.rope, j, g4 * 16);
+        store_row16(rowp + 2 * E + kv_h * kHd + g4 * 16, vv, false, nullptr, j, g4 * 16);
+      }
+      kv_pend = -1;
+    };
+    auto dq_epilogue = [&]() {
+      // dQ of both query halves (lane = query row within the half)
+      mbar_wait(&sm.dqdone, dq_pend & 1, abort_flag);
+      tc_fence_after();
+      uint32_t q0v[16], q1v[16];
+      tmem_ld_x16_nowait(tmem + lane_off + 384 + g4 * 16, q0v);
+      if (nkt > 1) tmem_ld_x16_nowait(tmem + lane_off + 448 + g4 * 16, q1v);
+      tmem_wait_ld_dep16(q0v);
+      if (nkt > 1) tmem_wait_ld_dep16(q1v);
+      tc_fence_before();
+      mbar_arrive(&sm.dqfree);
+      if (r < S) store_row16(dq_rows + (long long)r * 3 * E + dq_h * kHd + g4 * 16, q0v, true, a.rope, r, g4 * 16);
+      if (nkt > 1 && 128 + r < S)
+        store_row16(dq_rows + (long long)(128 + r) * 3 * E + dq_h * kHd + g4 * 16, q1v, true, a.rope, 128 + r,
+                    g4 * 16);
+      dq_pend = -1;
+    };
     for (int k = 0; k < n_local; ++k) {
       const int item = (int)blockIdx.x + k * G;
       const int seq = item / H, h = item - seq * H;
@@ -405,66 +436,73 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool jok = j < S;
         const int fj = jok ? mt.first[j] : S;
         const int bj = jok ? mt.bid[j] : -2;
-        const int q0 = qs * 64 + hq * 32;  // this thread's 32 queries
-        // keys see queries i >= first_j when blocks are contiguous; otherwise
-        // i >= j, or i >= first_j with the same block id
-        const int vis_lo = contig ? fj : j;
-        const bool full = jok && q0 >= vis_lo && q0 + 31 < S;
-        const bool none = !jok || q0 + 31 < fj || q0 >= S;
+        const int q0 = qs * 64 + g4 * 16;  // this thread's 16 queries
+        // a key row j sees the queries i >= first_j (< S) when the blocks are
+        // contiguous; otherwise i >= j, or first_j <= i < j with j's block id
+        // (the interval [first_j, S) is masked further below)
+        const bool none = !jok || q0 + 15 < fj || q0 >= S;
         const bool none_w = __all_sync(0xffffffffu, none);
         // the pair buffer is free once the dQ product of pair P - 2 has retired
         if ((u & 1) == 0 && P >= 2) mbar_wait(&sm.dq[pb], ((P >> 1) - 1) & 1, abort_flag);
         mbar_wait(&sm.sa[b], (g >> 1) & 1, abort_flag);
         tc_fence_after();
-        uint32_t pk[16], dk[16];
-        if (none_w || none) {
-          #pragma unroll
-          for (int e = 0; e < 16; ++e) pk[e] = dk[e] = 0u;
-        }
+        uint32_t pk[8], dk[8];
+        #pragma unroll
+        for (int e = 0; e < 8; ++e) pk[e] = dk[e] = 0u;
         if (!none_w) {
-          uint32_t su[32], du[32];
-          tmem_ld_x32_nowait(tmem + lane_off + b * 128 + hq * 32, su);
-          tmem_ld_x32_nowait(tmem + lane_off + b * 128 + 64 + hq * 32, du);
-          tmem_wait_ld_dep(su);
-          tmem_wait_ld_dep(du);
+          uint32_t su[16], du[16];
+          tmem_ld_x16_nowait(tmem + lane_off + b * 128 + g4 * 16, su);
+          tmem_ld_x16_nowait(tmem + lane_off + b * 128 + 64 + g4 * 16, du);
+          tmem_wait_ld_dep16(su);
+          tmem_wait_ld_dep16(du);
           if (!none) {
+            const int e_lo = max(fj - q0, 0), e_hi = min(S - q0, 16);
             const float4* L4 = reinterpret_cast<const float4*>(mt.L + q0);
             const float4* D4 = reinterpret_cast<const float4*>(mt.D + q0);
             #pragma unroll
-            for (int e4 = 0; e4 < 8; ++e4) {
+            for (int e4 = 0; e4 < 4; ++e4) {
               const float4 l4 = L4[e4], d4 = D4[e4];
-              const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-              const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
               float pv[4], dsv[4];
+              pv[0] = ex2_approx(fmaf(__uint_as_float(su[4 * e4 + 0]), sl2, -l4.x));
+              pv[1] = ex2_approx(fmaf(__uint_as_float(su[4 * e4 + 1]), sl2, -l4.y));
+              pv[2] = ex2_approx(fmaf(__uint_as_float(su[4 * e4 + 2]), sl2, -l4.z));
+              pv[3] = ex2_approx(fmaf(__uint_as_float(su[4 * e4 + 3]), sl2, -l4.w));
+              dsv[0] = pv[0] * (__uint_as_float(du[4 * e4 + 0]) - d4.x);
+              dsv[1] = pv[1] * (__uint_as_float(du[4 * e4 + 1]) - d4.y);
+              dsv[2] = pv[2] * (__uint_as_float(du[4 * e4 + 2]) - d4.z);
+              dsv[3] = pv[3] * (__uint_as_float(du[4 * e4 + 3]) - d4.w);
               #pragma unroll
               for (int kq = 0; kq < 4; ++kq) {
-                const int e = e4 * 4 + kq;
-                const float p = ex2_approx(fmaf(__uint_as_float(su[e]), sl2, -lv[kq]));
-                pv[kq] = p;
-                dsv[kq] = p * (__uint_as_float(du[e]) - dv[kq]);
-              }
-              if (!full) {
-                #pragma unroll
-                for (int kq = 0; kq < 4; ++kq) {
-                  const int i = q0 + e4 * 4 + kq;
-                  const bool vis = i < S && (i >= vis_lo || (!contig && i >= fj && mt.bid[i] == bj));
-                  pv[kq] = vis ? pv[kq] : 0.f;
-                  dsv[kq] = vis ? dsv[kq] : 0.f;
-                }
+                const int e = 4 * e4 + kq;
+                const bool vis = e >= e_lo && e < e_hi;
+                pv[kq] = vis ? pv[kq] : 0.f;
+                dsv[kq] = vis ? dsv[kq] : 0.f;
               }
               pk[e4 * 2] = pack_bf16(pv[0], pv[1]);
               pk[e4 * 2 + 1] = pack_bf16(pv[2], pv[3]);
               dk[e4 * 2] = pack_bf16(dsv[0], dsv[1]);
               dk[e4 * 2 + 1] = pack_bf16(dsv[2], dsv[3]);
             }
+            if (!contig) {
+              // a query before the key row sees it only within the key's block
+              #pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                const int i = q0 + e;
+                if (i < j && i >= fj && mt.bid[i] != bj) {
+                  const uint32_t keep = (e & 1) ? 0x0000ffffu : 0xffff0000u;
+                  pk[e >> 1] &= keep;
+                  dk[e >> 1] &= keep;
+                }
+              }
+            }
           }
         }
         // P^T over this thread's own (already read) S^T columns; dS^T into the pair buffer
-        tmem_st_x16(tmem + lane_off + b * 128 + hq * 32, pk);
+        tmem_st_x8(tmem + lane_off + b * 128 + g4 * 16, pk);
         uint8_t* dst = sm.dST[pb][qs & 1];
         #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = hq * 4 + q;  // 16-byte chunk of the 128-byte row
+        for (int q = 0; q < 2; ++q) {
+          const int chunk = g4 * 2 + q;  // 16-byte chunk of the 128-byte row
           *reinterpret_cast<uint4*>(dst + r * 128 + ((chunk ^ (r & 7)) << 4)) =
               make_uint4(dk[4 * q], dk[4 * q + 1], dk[4 * q + 2], dk[4 * q + 3]);
         }
@@ -472,41 +510,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async();
         tc_fence_before();
         mbar_arrive(&sm.ew[b]);
+        if (kv_pend >= 0) kv_epilogue();
+        if (dq_pend >= 0) dq_epilogue();
         if (last_kt) {
-          // dV_kt, dK_kt complete: this thread stores dims [32 hq, 32 hq + 32) of key row j
-          mbar_wait(&sm.kvdone, c & 1, abort_flag);
-          tc_fence_after();
-          uint32_t vv[32], kv[32];
-          tmem_ld_x32_nowait(tmem + lane_off + 256 + hq * 32, vv);
-          tmem_ld_x32_nowait(tmem + lane_off + 320 + hq * 32, kv);
-          tmem_wait_ld_dep(vv);
-          tmem_wait_ld_dep(kv);
-          tc_fence_before();
-          mbar_arrive(&sm.kvfree);
-          ++c;
-          if (jok) {
-            __nv_bfloat16* rowp = rowbase + (long long)j * 3 * E;
-            store_row32(rowp + E + h * kHd + hq * 32, kv, true, a.rope, j, hq * 32);
-            store_row32(rowp + 2 * E + h * kHd + hq * 32, vv, false, nullptr, j, hq * 32);
-          }
+          kv_pend = c++;
+          kv_j0 = kt * 128;
+          kv_h = h;
+          kv_rows = rowbase;
         }
       }
       mbar_arrive(&sm.mempty[m]);
-      // dQ of both query halves (lane = query row within the half)
-      mbar_wait(&sm.dqdone, k & 1, abort_flag);
-      tc_fence_after();
-      uint32_t q0v[32], q1v[32];
-      tmem_ld_x32_nowait(tmem + lane_off + 384 + hq * 32, q0v);
-      if (nkt > 1) tmem_ld_x32_nowait(tmem + lane_off + 448 + hq * 32, q1v);
-      tmem_wait_ld_dep(q0v);
-      if (nkt > 1) tmem_wait_ld_dep(q1v);
-      tc_fence_before();
-      mbar_arrive(&sm.dqfree);
-      if (r < S) store_row32(rowbase + (long long)r * 3 * E + h * kHd + hq * 32, q0v, true, a.rope, r, hq * 32);
-      if (nkt > 1 && 128 + r < S)
-        store_row32(rowbase + (long long)(128 + r) * 3 * E + h * kHd + hq * 32, q1v, true, a.rope, 128 + r,
-                    hq * 32);
+      dq_pend = k;
+      dq_h = h;
+      dq_rows = rowbase;
     }
+    if (kv_pend >= 0) kv_epilogue();
+    if (dq_pend >= 0) dq_epilogue();
   }
   tc_fence_before();
   __syncthreads();

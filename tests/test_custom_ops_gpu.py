@@ -53,8 +53,10 @@ def test_input_pos_matches_oracle(mask_type):
     (r * g).sum().backward()
     rp = dict(ref.named_parameters())
     for n, p in ours.named_parameters():
-        if p.grad is not None:
+        if rp[n].grad is not None and float(rp[n].grad.abs().max()) > 0:
             assert _cosine(p.grad, rp[n].grad) > 0.999, n
+        elif p.grad is not None:  # off the oracle's graph (no value placeholders): a zero gradient here
+            assert float(p.grad.abs().max()) == 0.0, n
     with pytest.raises(NotImplementedError):
         ours(b["input_ids"], input_pos=torch.stack([torch.arange(S), torch.arange(S) + 1, torch.arange(S)]).cuda())
 
