@@ -209,14 +209,26 @@ class DataParallelStep:
             step.grad_hook = self.reducer.ready
             step.grad_scale = 1.0 / self.world
 
-    def forward_backward(self, db, metrics=None):
-        losses = self.step_obj.forward_backward(db, metrics)
-        if self.reducer is not None:
+    def forward_backward(self, db, metrics=None, zero_grad=True, sync=True):
+        """sync=False: a micro-batch before the last of an accumulation (no
+        all-reduce; the last micro-batch's backward reduces the sum)."""
+        losses = self.step_obj.forward_backward(db, metrics, zero_grad=zero_grad, sync=sync)
+        if self.reducer is not None and sync:
             self.reducer.wait()
         return losses
 
-    def optimizer_step(self):
-        self.step_obj.optimizer_step()
+    def optimizer_step(self, accum: int = 1):
+        self.step_obj.optimizer_step(accum)
+
+    def step_accumulated(self, batches, metrics=None):
+        from .engine import prepare_batch
+        out = []
+        n = len(batches)
+        for i, b in enumerate(batches):
+            db = prepare_batch(b, self.step_obj.device)
+            out.append(self.forward_backward(db, metrics, zero_grad=i == 0, sync=i == n - 1))
+        self.optimizer_step(accum=n)
+        return out
 
     def step(self, batch, metrics=None):
         from .engine import prepare_batch

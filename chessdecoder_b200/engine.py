@@ -934,13 +934,19 @@ class TrainStep:
         self.grad_scale = 1.0
         self.partial = torch.empty(1024, device=self.device)
         self.loss_weights = loss_weights
+        self.grad_accum = 1  # micro-batches per optimizer step (config.yaml gradient_accumulation_steps)
 
-    def forward_backward(self, db: DeviceBatch, metrics=None):
-        """Loss forward + full backward into store.grad (zeroed here).  Returns
-        losses f32 [5] = (move, board, wl, d, thinking move) on the device
-        (the last is 0 outside the finetune step)."""
+    def forward_backward(self, db: DeviceBatch, metrics=None, zero_grad: bool = True, sync: bool = True):
+        """Loss forward + full backward into store.grad.  Returns losses f32
+        [5] = (move, board, wl, d, thinking move) on the device (the last is 0
+        outside the finetune step).  zero_grad=False accumulates onto the
+        gradients of earlier micro-batches (gradient accumulation,
+        chessdecoder/train/train.py:244-250); sync=False skips the
+        ``grad_hook`` (the data-parallel all-reduce runs during the last
+        micro-batch only, as average_gradients runs once per optimizer step)."""
         st = self.store
-        st.grad.zero_()
+        if zero_grad:
+            st.grad.zero_()
         B, S = db.B, db.S
         losses = torch.zeros(5, device=self.device)
         meta = K.attn_meta(db.bid, S)
@@ -949,27 +955,45 @@ class TrainStep:
         h0, fctx = self.front.forward(db, n_copies=2)
         hN16, _, bctx = self.backbone.forward(h0, 2 * B, B, S, db.bid, meta)
         dhN = self.heads.run(db, hN16, losses, metrics)
-        dh0 = self.backbone.backward(dhN, bctx, self.grad_hook)
+        hook = self.grad_hook if sync else None
+        dh0 = self.backbone.backward(dhN, bctx, hook)
         self.front.backward(db, dh0, fctx, n_copies=2)
         if self.fp8 is not None:
             self.fp8.end_step()
-        if self.grad_hook is not None:
-            self.grad_hook(-1)
+        if hook is not None:
+            hook(-1)
         return losses
 
-    def optimizer_step(self):
+    def optimizer_step(self, accum: int = 1):
+        """Clip + AdamW on the summed gradients of ``accum`` micro-batches:
+        the gradients are scaled by 1 / accum (the reference divides each
+        micro-batch's loss, train.py:244) and the data-parallel mean, and the
+        clip norm is taken on the scaled sum, as clip_grad_norm_ runs after the
+        accumulation (train.py:249-250)."""
         st = self.store
         st.step += 1
         K.sumsq(st.grad, self.partial)
         K.adamw(st.flat, st.grad, st.exp_avg, st.exp_avg_sq, st.flat16, self.partial, max_norm=self.max_norm,
                 lr=self.lr, beta1=self.betas[0], beta2=self.betas[1], eps=self.eps, wd=self.wd, step=st.step,
-                grad_scale=self.grad_scale)
+                grad_scale=self.grad_scale / accum)
 
     def step(self, batch: dict, metrics=None):
         db = prepare_batch(batch, self.device)
         losses = self.forward_backward(db, metrics)
         self.optimizer_step()
         return losses
+
+    def step_accumulated(self, batches, metrics=None):
+        """One optimizer step over micro-batches (gradient_accumulation_steps
+        = len(batches), train/config.yaml:25); returns each micro-batch's
+        losses f32 [5]."""
+        out = []
+        n = len(batches)
+        for i, b in enumerate(batches):
+            db = prepare_batch(b, self.device)
+            out.append(self.forward_backward(db, metrics, zero_grad=i == 0, sync=i == n - 1))
+        self.optimizer_step(accum=n)
+        return out
 
     # -- checkpoints (chessdecoder/utils/training.py:136-157, train/train.py:81-104) --
     def optimizer_state_dict(self) -> dict:
