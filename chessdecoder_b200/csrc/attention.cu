@@ -1105,9 +1105,11 @@ extern "C" int cdk_attn_prefix_meta(const int32_t* bid, int64_t nseq_prefix, int
   return e == cudaSuccess ? 0 : (int)e;
 }
 
-// Path selection.  S <= 256: the tcgen05 kernels (attention_tc.cu) by
-// default; CDK_ATTN_PATH=seq selects the mma.sync sequence-resident kernels and
-// CDK_ATTN_PATH=tiled the tiled kernels (the tests cover all three).  S > 256:
+// Path selection.  S <= 256: the persistent tcgen05 kernels (attention_pst.cu,
+// attention_bwd_pst.cu) by default; CDK_ATTN_PATH=tc selects the tcgen05
+// kernels with one CTA per (query tile, head, sequence) (attention_tc.cu),
+// CDK_ATTN_PATH=seq the mma.sync sequence-resident kernels and
+// CDK_ATTN_PATH=tiled the tiled kernels (the tests cover all of them).  S > 256:
 // the tcgen05 kernels of attention_long.cu by default (the backward needs the
 // caller's fp32 dQ workspace, cdk_attn_bwd_ws), the tiled kernels with
 // CDK_ATTN_PATH=tiled or seq or without a workspace.  CDK_ATTN_PATH=long takes
@@ -1116,7 +1118,7 @@ static int attn_path() {
   const char* v = getenv("CDK_ATTN_PATH");
   if (v && v[0] == 't' && v[1] == 'i') return 2;  // tiled
   if (v && v[0] == 't' && v[1] == 'c') return 4;  // one CTA per (query tile, head, sequence) tcgen05 kernels
-  if (v && v[0] == 'p') return 5;                  // persistent tcgen05 backward (S <= 256)
+  if (v && v[0] == 'p') return 5;                  // persistent tcgen05 kernels (the default at S <= 256)
   if (v && v[0] == 's') return 1;                  // seq (mma.sync)
   if (v && v[0] == 'l') return 3;                  // tcgen05 long-sequence kernels at any S
   return 0;                                        // tcgen05
@@ -1240,9 +1242,9 @@ extern "C" int cdk_attn_bwd_ws(const void* qkv, const void* out, const void* dou
   a.nseq = (int)nseq;
   dim3 grid((unsigned)a.nt, (unsigned)H, (unsigned)nseq);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (S <= kSeqMax && attn_path() == 5)
+  if (S <= kSeqMax && (attn_path() == 0 || attn_path() == 5))
     return launch_attn_bwd_pst(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid, meta, rope, s);
-  if (S <= kSeqMax && (attn_path() == 0 || attn_path() == 4))
+  if (S <= kSeqMax && attn_path() == 4)
     return launch_attn_bwd_tc(qkv, out, dout, lse, dqkv, nseq, n_causal, S, H, bid, meta, rope, s);
   if (long_path(S) && workspace != nullptr && S % 4 == 0) {
     if (workspace_bytes < cdk_attn_bwd_workspace(nseq, S, H) || (reinterpret_cast<uintptr_t>(workspace) & 15))

@@ -23,7 +23,7 @@
 // pass before (attn_dsum).
 //
 //   warp 0       producer: row metadata (L, D, block bounds) and TMA loads
-//   warp 1       TMEM allocation, MMA issue (lane 0)
+//   warp 1       TMEM allocation, MMA issue (whole warp, one elected lane)
 //   warps 2-17   elementwise + epilogues: thread = (key row r = TMEM lane,
 //                16-query group g of the sub-tile)
 // TMEM: S^T|dP^T x 2 [0, 256) | dV [256, 320) | dK [320, 384) | dQ_0 [384, 448)
@@ -258,7 +258,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---- MMA issue -----------------------------------------------------------
-    if (lane == 0) {
+    // the whole warp runs the issue loop; one elected lane issues (uniform operands)
+    {
       const uint32_t id_s = make_idesc_bf16(128, 64, false, false);   // S^T, dP^T: N = 64 queries
       const uint32_t id_kn = make_idesc_bf16(128, kHd, false, true);  // dV, dK: B read MN-major
       const uint32_t id_nn = make_idesc_bf16(128, kHd, true, true);   // dQ: A (dS) and B (K) MN-major
@@ -296,12 +297,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t qb = smem_u32(sm.QO[qh]) + (qs & 1) * kBox, ob = smem_u32(sm.QO[qh]) + (2 + (qs & 1)) * kBox;
         #pragma unroll
         for (int kk = 0; kk < kHd / 16; ++kk) {
-          umma_f16(tmem + b * 128, make_sdesc(kb + kk * 32, 16, 1024), make_sdesc(qb + kk * 32, 16, 1024), id_s,
+          umma_f16_w(tmem + b * 128, make_sdesc(kb + kk * 32, 16, 1024), make_sdesc(qb + kk * 32, 16, 1024), id_s,
                    kk > 0 ? 1u : 0u);
-          umma_f16(tmem + b * 128 + 64, make_sdesc(vb + kk * 32, 16, 1024), make_sdesc(ob + kk * 32, 16, 1024),
+          umma_f16_w(tmem + b * 128 + 64, make_sdesc(vb + kk * 32, 16, 1024), make_sdesc(ob + kk * 32, 16, 1024),
                    id_s, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&sm.sa[b]);
+        tc_commit_w(&sm.sa[b]);
         ++g_issued;
         ++ua;
       };
@@ -334,8 +335,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < 4; ++kk) {  // 64 queries, 16 per step
             const uint32_t acc = (!first_kt || kk > 0) ? 1u : 0u;
             const uint32_t pcol = (uint32_t)(b * 128 + kk * 16);
-            umma_f16_ts(tmem + 256, tmem + pcol, make_sdesc(ob + kk * 2048, 8192, 1024), id_kn, acc);
-            umma_f16(tmem + 320, make_sdesc(dsb + kk * 32, 16, 1024), make_sdesc(qb + kk * 2048, 8192, 1024), id_kn,
+            umma_f16_ts_w(tmem + 256, tmem + pcol, make_sdesc(ob + kk * 2048, 8192, 1024), id_kn, acc);
+            umma_f16_w(tmem + 320, make_sdesc(dsb + kk * 32, 16, 1024), make_sdesc(qb + kk * 2048, 8192, 1024), id_kn,
                      acc);
           }
           if (qs & 1) {
@@ -345,21 +346,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t pair = smem_u32(sm.dST[pb][0]);
             const uint32_t kb = smem_u32(sm.KV[kt]);
             const bool first_q = ((dq_seen >> qh) & 1u) == 0;
-            #pragma unroll 1
+            #pragma unroll
             for (int kk = 0; kk < 8; ++kk)  // 128 keys
-              umma_f16(tmem + 384 + qh * 64, make_sdesc(pair + kk * 2048, 16384, 1024),
+              umma_f16_w(tmem + 384 + qh * 64, make_sdesc(pair + kk * 2048, 16384, 1024),
                        make_sdesc(kb + kk * 2048, 8192, 1024), id_nn, (!first_q || kk > 0) ? 1u : 0u);
             dq_seen |= 1u << qh;
-            tc_commit(&sm.dq[pb]);
+            tc_commit_w(&sm.dq[pb]);
           }
           if (last_kt) {
-            tc_commit(&sm.kvdone);
-            tc_commit(&sm.kvempty[kt]);
+            tc_commit_w(&sm.kvdone);
+            tc_commit_w(&sm.kvempty[kt]);
             ++c;
           }
-          if (u == last_q0) tc_commit(&sm.qempty[0]);
-          if (u == last_q1) tc_commit(&sm.qempty[1]);
-          if (u == un.n - 1) tc_commit(&sm.dqdone);
+          if (u == last_q0) tc_commit_w(&sm.qempty[0]);
+          if (u == last_q1) tc_commit_w(&sm.qempty[1]);
+          if (u == un.n - 1) tc_commit_w(&sm.dqdone);
           // keep MMA-A two sub-units ahead; across an item boundary only once
           // every release commit of this item has been issued
           const int max_item = u == un.n - 1 ? k + 1 : k;

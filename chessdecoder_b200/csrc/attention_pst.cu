@@ -11,7 +11,7 @@
 //
 //   warp 0          producer: per item, the row metadata (block id, last
 //                   visible key) into the slot, then the TMA loads
-//   warp 1 / 2      MMA issuer of query tile 0 / 1 (lane 0):
+//   warp 1 / 2      MMA issuer of query tile 0 / 1 (whole warp, one elected lane):
 //                   S_t = Q_t K^T (M=128, N = keys <= 256) into TMEM region t,
 //                   then O_t = P_t V with P_t read from TMEM (A operand) and V
 //                   MN-major from its TMA tile
@@ -241,7 +241,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1 || warp == 2) {
     // ---- MMA issuer of query tile t --------------------------------------
     const int t = warp - 1;
-    if (lane == 0 && t < n_tiles) {
+    // the whole warp runs the issue loop; one elected lane issues (uniform operands)
+    if (t < n_tiles) {
       const uint32_t treg = tmem + (uint32_t)(t * 256);
       const uint32_t idesc_o = make_idesc_bf16(128, kHd, false, true);
       for (int k = 0; k < n_local; ++k) {
@@ -255,22 +256,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t kb = smem_u32(sm.slot[s].K);
         #pragma unroll
         for (int kk = 0; kk < kHd / 16; ++kk)
-          umma_f16(treg, make_sdesc(qa + kk * 32, 16, 1024), make_sdesc(kb + kk * 32, 16, 1024), idesc_s,
+          umma_f16_w(treg, make_sdesc(qa + kk * 32, 16, 1024), make_sdesc(kb + kk * 32, 16, 1024), idesc_s,
                    kk > 0 ? 1u : 0u);
-        tc_commit(&sm.sfull[t]);
+        tc_commit_w(&sm.sfull[t]);
         mbar_wait(&sm.pfull[t], k & 1, abort_flag);
         tc_fence_after();
         const uint32_t vb = smem_u32(sm.slot[s].V);
         // P of keys [0, nk/2) sits in columns [0, nk/4), P of keys [nk/2, nk)
         // in columns [nk/2, 3 nk/4): each half written over scores its own
         // thread has read
-        for (int kk = 0; kk < nk / 16; ++kk) {
-          const uint32_t acol = (uint32_t)(kk * 8 + (kk * 16 >= nk / 2 ? nk / 4 : 0));
-          umma_f16_ts(treg + 192, treg + acol, make_sdesc(vb + kk * 16 * 128, 8192, 1024), idesc_o,
-                      kk > 0 ? 1u : 0u);
+        for (int k4 = 0; k4 < nk / 64; ++k4) {  // nk is a multiple of 64
+          const uint64_t vd = make_sdesc(vb + k4 * 64 * 128, 8192, 1024);
+          #pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const int key0 = k4 * 64 + kk * 16;
+            const uint32_t acol = (uint32_t)(key0 / 2 + (key0 >= nk / 2 ? nk / 4 : 0));
+            umma_f16_ts_w(treg + 192, treg + acol, vd + (uint64_t)(kk * 16 * 128 / 16), idesc_o,
+                          (k4 > 0 || kk > 0) ? 1u : 0u);
+          }
         }
-        tc_commit(&sm.ofull[t]);
-        tc_commit(&sm.empty[s]);
+        tc_commit_w(&sm.ofull[t]);
+        tc_commit_w(&sm.empty[s]);
       }
     }
   } else if (warp >= 4) {

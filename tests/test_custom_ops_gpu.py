@@ -83,7 +83,10 @@ def test_module_under_torch_compile_matches_eager():
     for n, g in g_eager.items():
         p = dict(ours.named_parameters())[n]
         assert p.grad is not None, n
-        assert _cosine(p.grad, g) > 0.9999, n
+        if float(g.abs().max()) == 0.0:  # off this loss's graph (the Fourier encoder): zero in both
+            assert float(p.grad.abs().max()) == 0.0, n
+        else:
+            assert _cosine(p.grad, g) > 0.9999, n
 
 
 def test_backbone_activations_are_released():

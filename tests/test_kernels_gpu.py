@@ -210,7 +210,7 @@ def ref_attention(qkv, nseq, n_causal, S, H, bid):
     return o.transpose(1, 2).reshape(nseq * S, H * 64)
 
 
-@pytest.fixture(params=["default", "pst", "tc", "seq", "tiled", "long"])
+@pytest.fixture(params=["default", "tc", "seq", "tiled", "long"])
 def attn_path(request, monkeypatch):
     """Every attention implementation: the default (persistent tcgen05 forward
     for S <= 256), tcgen05 with one CTA per query tile (S <= 256), mma.sync
