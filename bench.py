@@ -864,6 +864,40 @@ def main():
     h2d = db_tmp.h2d_bytes
     e2e_value = tokens_step / (e2e_ms / 1000.0)
 
+    # ---- communication timeline (N > 1), outside the timed regions -------------
+    comm = None
+    if world > 1 and dp.reducer is not None:
+        red = dp.reducer
+        red.timing = True
+        recs = []
+        for i in range(3):
+            dp.forward_backward(dbs[i % len(dbs)])
+            recs.append(red.stats())
+            dp.optimizer_step()
+        red.timing = False
+        # the same steps with the all-reduce hooks detached: what the step costs
+        # on N GPUs without communication (gradients stay per-rank here)
+        hook = step.grad_hook
+        step.grad_hook = None
+        sync_all()
+        c0 = torch.cuda.Event(enable_timing=True)
+        c1 = torch.cuda.Event(enable_timing=True)
+        c0.record()
+        for i in range(3):
+            dp.forward_backward(dbs[i % len(dbs)])
+            dp.optimizer_step()
+        c1.record()
+        sync_all()
+        step.grad_hook = hook
+        tails = sorted(r["exposed_tail_ms"] for r in recs)
+        comm = {"buckets": recs[-1]["buckets"], "bytes_per_step": recs[-1]["bytes"],
+                "exposed_tail_ms": max_over_ranks(tails[1]),
+                "first_ready_to_last_done_ms": max_over_ranks(sorted(r["span_ms"] for r in recs)[1]),
+                "ready_to_done_ms_rank0": recs[-1]["ready_to_done_ms"],
+                "step_ms_without_allreduce": max_over_ranks(c0.elapsed_time(c1) / 3),
+                "timing": "CUDA events: bucket ready on the compute stream, all-reduce done on the comm stream, "
+                          "3 steps after the timed regions, median, max over ranks"}
+
     # ---- roofline of the dominant kernel (the tcgen05 GEMM) ---------------------
     peak_sust, peak_burst, peak_kind, peak_clk = measured_peaks()
     achieved = gemm_stats["tflops"]
@@ -933,6 +967,8 @@ def main():
                 "cpu_baseline": cpu}
         if eager is not None:
             line["gpu_eager_reference"] = eager
+        if comm is not None:
+            line["comm"] = comm
         if args.detail:
             line["gemm_by_shape"] = gemm_stats.get("by_shape")
             line["host_enqueue_ms_per_step"] = host_enqueue_ms

@@ -140,6 +140,12 @@ class BucketedAllReduce:
         self.stream = torch.cuda.Stream(device=flat.device) if self.cuda else None
         self.works = []
         self.launched = 0
+        # timing=True: CUDA events per bucket (ready on the compute stream, done
+        # on the comm stream) and at the end of the backward; read by stats()
+        self.timing = False
+        self._events = []
+        self._bwd_end = None
+        self._bytes = 0
 
     def ready(self, key):
         s, e = self.span_of[key]
@@ -160,22 +166,53 @@ class BucketedAllReduce:
         self.pending_start = None
         view = self.flat[s:e]
         if self.cuda:
-            ev = torch.cuda.current_stream(self.flat.device).record_event()
+            ev = torch.cuda.current_stream(self.flat.device).record_event(
+                torch.cuda.Event(enable_timing=self.timing))
             self.stream.wait_event(ev)
             with torch.cuda.stream(self.stream):
                 w = dist.all_reduce(view, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+                if self.timing:  # the comm stream waits for this collective, then marks its end
+                    w.wait()
+                    done = torch.cuda.Event(enable_timing=True)
+                    done.record(self.stream)
+                    self._events.append((ev, done))
+                    self._bytes += view.numel() * view.element_size()
         else:
             w = dist.all_reduce(view, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
         self.works.append(w)
         self.launched += 1
 
     def wait(self):
+        if self.timing and self.cuda:
+            self._bwd_end = torch.cuda.current_stream(self.flat.device).record_event(
+                torch.cuda.Event(enable_timing=True))
         self._flush()
         for w in self.works:
             w.wait()
         self.works = []
         if self.cuda:
             torch.cuda.current_stream(self.flat.device).wait_stream(self.stream)
+
+
+    def stats(self):
+        """Per-step communication timeline of the last step run with
+        ``timing=True`` (synchronises): buckets, bytes, ``ready_to_done_ms`` per
+        bucket, and ``exposed_tail_ms`` = end of the backward's last kernel ->
+        end of the last all-reduce (the part of the communication that the
+        backward does not hide).  Clears the recorded events."""
+        if not self._events:
+            return None
+        self._events[-1][1].synchronize()
+        if self._bwd_end is not None:
+            self._bwd_end.synchronize()
+        out = {"buckets": len(self._events), "bytes": self._bytes,
+               "ready_to_done_ms": [round(a.elapsed_time(b), 4) for a, b in self._events]}
+        first_ready = self._events[0][0]
+        out["span_ms"] = first_ready.elapsed_time(self._events[-1][1])
+        out["exposed_tail_ms"] = (self._bwd_end.elapsed_time(self._events[-1][1])
+                                  if self._bwd_end is not None else None)
+        self._events, self._bwd_end, self._bytes = [], None, 0
+        return out
 
 
 def step_spans(store) -> List[Tuple[object, int, int]]:
