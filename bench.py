@@ -927,7 +927,7 @@ def main():
     mfu_spec = flops / (dev_ms / 1000.0) / 2.25e15
     mfu_meas = flops / (dev_ms / 1000.0) / (peak_burst * 1e12)
     if args.fp8:
-        roofline["kernel"] = "gemm_bf16_kernel<..., F8> (tcgen05 kind::f8f6f4) + bf16 head GEMMs"
+        roofline["kernel"] = "gemm_bf16_kernel<..., F8> (tcgen05 kind::f8f6f4)"
         roofline["note"] = ("fp8 GEMMs measured against the bf16 sustained peak (no fp8 peak is measured on this "
                             "pool; the dense fp8 spec is 4.5 PFLOP/s)")
 
@@ -942,7 +942,7 @@ def main():
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None,
-                "dtype": "fp8 (e4m3 activations/weights, e5m2 grads) backbone linears; bf16 attention and heads"
+                "dtype": "fp8 (e4m3 activations/weights, e5m2 grads) backbone and head linears; bf16 attention"
                 if args.fp8 else "bf16", "data": "synthetic thinking-variation rows" if (args.moe or args.finetune)
                 else "synthetic",
                 "config": {"workload": ("ChessDecoder %s step (pass-1 causal + pass-2 prefix fwd, bwd, "

@@ -126,26 +126,42 @@ __device__ __forceinline__ Units item_units(const Args& a, bool prefix, int pseq
   return u;
 }
 
-// dX (bf16) of 16 consecutive dims [c0, c0 + 16) of a row: value * 0.125 with the
-// inverse RoPE rotation of position pos when rope != null (scale_rope), or as is.
-__device__ __forceinline__ void store_row16(__nv_bfloat16* dst, const uint32_t (&v)[16], bool scale_rope,
-                                            const float* rope, int pos, int c0) {
+// (cos, sin) pairs of the 16 dims [c0, c0 + 16) of position pos, or the
+// identity when rope == null.  Loaded before the epilogue's wait on the
+// accumulator so that the table read overlaps the last MMAs.
+struct Rope16 {
+  float4 cs[4];
+};
+__device__ __forceinline__ Rope16 load_rope16(const float* rope, int pos, int c0, bool ok) {
+  Rope16 r;
+  if (rope != nullptr && ok) {
+    const float4* p = reinterpret_cast<const float4*>(rope + ((long long)pos * 32 + c0 / 2) * 2);
+    #pragma unroll
+    for (int q = 0; q < 4; ++q) r.cs[q] = p[q];
+  } else {
+    #pragma unroll
+    for (int q = 0; q < 4; ++q) r.cs[q] = make_float4(1.f, 0.f, 1.f, 0.f);
+  }
+  return r;
+}
+
+// dX (bf16) of 16 consecutive dims of a row: value * scale, then the inverse
+// RoPE rotation given by rp (the identity for V or without RoPE).
+__device__ __forceinline__ void store_row16(__nv_bfloat16* dst, const uint32_t (&v)[16], float scale,
+                                            const Rope16& rp) {
   float f[16];
   #pragma unroll
-  for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]) * (scale_rope ? 0.125f : 1.f);
-  if (scale_rope && rope != nullptr) {
-    const float4* cs = reinterpret_cast<const float4*>(rope + ((long long)pos * 32 + c0 / 2) * 2);
-    #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const float4 t = cs[p];  // (cos, sin) of two consecutive pairs
-      float x0 = f[4 * p], x1 = f[4 * p + 1];
-      f[4 * p] = x0 * t.x + x1 * t.y;
-      f[4 * p + 1] = x1 * t.x - x0 * t.y;
-      x0 = f[4 * p + 2];
-      x1 = f[4 * p + 3];
-      f[4 * p + 2] = x0 * t.z + x1 * t.w;
-      f[4 * p + 3] = x1 * t.z - x0 * t.w;
-    }
+  for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]) * scale;
+  #pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float4 t = rp.cs[p];  // (cos, sin) of two consecutive pairs
+    float x0 = f[4 * p], x1 = f[4 * p + 1];
+    f[4 * p] = x0 * t.x + x1 * t.y;
+    f[4 * p + 1] = x1 * t.x - x0 * t.y;
+    x0 = f[4 * p + 2];
+    x1 = f[4 * p + 3];
+    f[4 * p + 2] = x0 * t.z + x1 * t.w;
+    f[4 * p + 3] = x1 * t.z - x0 * t.w;
   }
   uint4* d = reinterpret_cast<uint4*>(dst);
   #pragma unroll
@@ -385,6 +401,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __nv_bfloat16* dq_rows = nullptr;
     auto kv_epilogue = [&]() {
       // dV, dK of the key tile complete: this thread stores dims [16 g, 16 g + 16) of its key row
+      const int j = kv_j0 + r;
+      const Rope16 rk = load_rope16(a.rope, j, g4 * 16, j < S);
       mbar_wait(&sm.kvdone, kv_pend & 1, abort_flag);
       tc_fence_after();
       uint32_t vv[16], kv[16];
@@ -394,16 +412,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld_dep16(kv);
       tc_fence_before();
       mbar_arrive(&sm.kvfree);
-      const int j = kv_j0 + r;
       if (j < S) {
         __nv_bfloat16* rowp = kv_rows + (long long)j * 3 * E;
-        store_row16(rowp + E + kv_h * kHd + g4 * 16, kv, true, a.rope, j, g4 * 16);
-        store_row16(rowp + 2 * E + kv_h * kHd + g4 * 16, vv, false, nullptr, j, g4 * 16);
+        store_row16(rowp + E + kv_h * kHd + g4 * 16, kv, 0.125f, rk);
+        store_row16(rowp + 2 * E + kv_h * kHd + g4 * 16, vv, 1.f, load_rope16(nullptr, 0, 0, false));
       }
       kv_pend = -1;
     };
     auto dq_epilogue = [&]() {
       // dQ of both query halves (lane = query row within the half)
+      const Rope16 r0 = load_rope16(a.rope, r, g4 * 16, r < S);
+      const Rope16 r1 = load_rope16(a.rope, 128 + r, g4 * 16, nkt > 1 && 128 + r < S);
       mbar_wait(&sm.dqdone, dq_pend & 1, abort_flag);
       tc_fence_after();
       uint32_t q0v[16], q1v[16];
@@ -413,10 +432,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (nkt > 1) tmem_wait_ld_dep16(q1v);
       tc_fence_before();
       mbar_arrive(&sm.dqfree);
-      if (r < S) store_row16(dq_rows + (long long)r * 3 * E + dq_h * kHd + g4 * 16, q0v, true, a.rope, r, g4 * 16);
+      if (r < S) store_row16(dq_rows + (long long)r * 3 * E + dq_h * kHd + g4 * 16, q0v, 0.125f, r0);
       if (nkt > 1 && 128 + r < S)
-        store_row16(dq_rows + (long long)(128 + r) * 3 * E + dq_h * kHd + g4 * 16, q1v, true, a.rope, 128 + r,
-                    g4 * 16);
+        store_row16(dq_rows + (long long)(128 + r) * 3 * E + dq_h * kHd + g4 * 16, q1v, 0.125f, r1);
       dq_pend = -1;
     };
     for (int k = 0; k < n_local; ++k) {

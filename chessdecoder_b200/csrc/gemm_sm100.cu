@@ -1258,7 +1258,6 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   if (!aligned16(a) || !aligned16(b)) return -3;
   if (f8 ? ((lda % 16) || (ldb % 16)) : ((lda % 8) || (ldb % 8))) return -3;
   if (f8 && (!sa || !sb || a_fmt < 0 || a_fmt > 1 || b_fmt < 0 || b_fmt > 1)) return -13;
-  if (f8 && ((a_mn && M % 16) || (b_mn && N % 16))) return -13;  // MN-major pitch: 16-byte rows
   const int kind = epi->kind;
   if (kind < CDK_EPI_STORE_BF16 || kind > CDK_EPI_ACCUM_F32) return -4;
   const bool dual = kind == CDK_EPI_SWIGLU;

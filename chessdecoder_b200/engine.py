@@ -806,9 +806,10 @@ class Heads:
     """Board head on pass-1 rows, policy head on move rows, WL / D value heads,
     each with its loss and its gradient; accumulates dL/dhN."""
 
-    def __init__(self, store: ParamStore, cfg: ModelConfig, loss_weights=(5.0, 1.0, 1.0, 1.0)):
+    def __init__(self, store: ParamStore, cfg: ModelConfig, loss_weights=(5.0, 1.0, 1.0, 1.0), fp8=None):
         self.st = store
         self.cfg = cfg
+        self.fp8 = fp8  # Fp8Recipe with head sites: the head linears run on fp8 GEMMs
         self.w_move, self.w_board, self.w_wl, self.w_d = loss_weights[:4]
         self.w_think = loss_weights[4] if len(loss_weights) > 4 else 0.0
         if self.w_think and not cfg.finetune:
@@ -826,18 +827,25 @@ class Heads:
         dhN = torch.empty(T, E, device=dev)
         dhN[BS:].zero_()
         norms = db.norms
+        # fp8: the pass-1 and pass-2 rows quantised once each (the board head reads
+        # the former, the policy / thinking heads gather from the latter)
+        self._h8 = None
+        if self.fp8 is not None:
+            from .fp8 import _empty8
+            f = self.fp8
+            self._h8 = _empty8(T, E, torch.float8_e4m3fn, dev)
+            f.cast(hN16[:BS], f.head_site("h_causal", "x"), K.FP8_E4M3, out=self._h8[:BS])
+            f.cast(hN16[BS:], f.head_site("h_prefix", "x"), K.FP8_E4M3, out=self._h8[BS:])
         # ---- board head over pass-1 rows -----------------------------------
         nbv = V.board_vocab_size
         logits = torch.empty(BS, 44, device=dev)
-        K.gemm(hN16[:BS], st.bf16("board_head.weight"), kind=K.EPI_STORE_F32, out=logits,
-               bias=st.param("board_head.bias"), N=nbv)
+        xc8 = self._h8[:BS] if self._h8 is not None else None
+        self._lin_fwd("board_head", hN16[:BS], xc8, "h_causal", logits, N=nbv)
         dl = torch.empty(BS, 48, device=dev, dtype=torch.bfloat16)
         bam = metrics.get("board_argmax") if metrics is not None else None
         K.softmax_ce(logits, db.board_t, db.board_w, norms[1:2], self.w_board, dlogits=dl,
                      dbias=st.grad_of("board_head.bias"), loss_out=losses[1:2], argmax=bam, ncls=nbv)
-        K.gemm(dl, st.bf16("board_head.weight"), b_mn=True, kind=K.EPI_STORE_F32, out=dhN[:BS], K=nbv)
-        K.gemm(dl, hN16[:BS], a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=st.grad_of("board_head.weight"),
-               M=nbv, K=BS)
+        self._lin_bwd("board_head", dl, nbv, hN16[:BS], xc8, "h_causal", dhN[:BS])
         # ---- policy head over gathered move rows; thinking head (finetune) ----
         pam = metrics.get("move_argmax") if metrics is not None else None
         self._move_head("policy_head", db.prow, db.pt, norms[0:1], self.w_move, hN16, dhN, losses[0:1], pam)
@@ -860,17 +868,22 @@ class Heads:
             return
         st, E, dev = self.st, self.cfg.embed_dim, hN16.device
         nmv = V.move_vocab_size
-        hp = torch.empty(n, E, device=dev, dtype=torch.bfloat16)
-        K.gather_rows_bf16(hN16, rows, hp)
+        hp, hp8 = None, None
+        if self._h8 is None:
+            hp = torch.empty(n, E, device=dev, dtype=torch.bfloat16)
+            K.gather_rows_bf16(hN16, rows, hp)
+        else:  # gather the 8-bit rows (E bytes = E / 2 bf16-sized elements)
+            from .fp8 import _empty8
+            hp8 = _empty8(n, E, torch.float8_e4m3fn, dev)
+            K.gather_rows_bf16(self._h8.view(torch.bfloat16), rows, hp8.view(torch.bfloat16))
         lp = torch.empty(n, nmv, device=dev)
-        K.gemm(hp, st.bf16(f"{name}.weight"), kind=K.EPI_STORE_F32, out=lp, bias=st.param(f"{name}.bias"))
+        self._lin_fwd(name, hp, hp8, "h_prefix", lp)
         dlp = torch.empty(n, 1928, device=dev, dtype=torch.bfloat16)
         K.softmax_ce(lp, tgt, None, norm, weight, dlogits=dlp, dbias=st.grad_of(f"{name}.bias"), loss_out=loss,
                      argmax=argmax, ncls=nmv)
         dhp = torch.empty(n, E, device=dev)
-        K.gemm(dlp, st.bf16(f"{name}.weight"), b_mn=True, kind=K.EPI_STORE_F32, out=dhp, K=nmv)
+        self._lin_bwd(name, dlp, nmv, hp, hp8, "h_prefix", dhp)
         K.scatter_add_rows(dhp, rows, dhN)
-        K.gemm(dlp, hp, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=st.grad_of(f"{name}.weight"), M=nmv, K=n)
 
     def _value(self, name, rows, tgt, valid, centers, norm, weight, hN16, dhN, loss):
         n = rows.numel()
@@ -882,7 +895,11 @@ class Heads:
         x = torch.empty(n, E, device=dev, dtype=torch.bfloat16)
         K.gather_rows_bf16(hN16, rows, x)
         z1 = torch.empty(n, hv, device=dev)
-        K.gemm(x, st.bf16(f"{name}.mlp.0.weight"), kind=K.EPI_STORE_F32, out=z1, bias=st.param(f"{name}.mlp.0.bias"))
+        lin0 = f"{name}.mlp.0"
+        x8 = None
+        if self.fp8 is not None:
+            x8 = self.fp8.cast(x, self.fp8.head_site(lin0, "x"), K.FP8_E4M3)
+        self._lin_fwd(lin0, x, x8, lin0, z1)
         act = torch.empty(n, hv, device=dev)
         dlog = torch.empty(n, nb, device=dev)
         dz = torch.empty(n, hv, device=dev, dtype=torch.bfloat16)
@@ -895,10 +912,43 @@ class Heads:
                    K=n)
         # first Linear: dX = dz W1, dW1 += dz^T X
         dx = torch.empty(n, E, device=dev)
-        K.gemm(dz, st.bf16(f"{name}.mlp.0.weight"), b_mn=True, kind=K.EPI_STORE_F32, out=dx)
+        self._lin_bwd(lin0, dz, hv, x, x8, lin0, dx)
         K.scatter_add_rows(dx, rows, dhN)
-        K.gemm(dz, x, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=st.grad_of(f"{name}.mlp.0.weight"), M=hv,
-               K=n)
+
+    # ---- head linears: bf16 GEMMs, or the fp8 recipe's e4m3 / e5m2 GEMMs -------
+    def _lin_fwd(self, name, x16, x8, xsite, out, N=None):
+        """out (fp32) = x W^T + b."""
+        st, f = self.st, self.fp8
+        if f is None:
+            K.gemm(x16, st.bf16(f"{name}.weight"), kind=K.EPI_STORE_F32, out=out, bias=st.param(f"{name}.bias"), N=N)
+            return
+        K.gemm(x8, f.weights[("head", name)], kind=K.EPI_STORE_F32, out=out, bias=st.param(f"{name}.bias"), N=N,
+               fp8=(K.FP8_E4M3, K.FP8_E4M3, f.sinv(f.head_site(xsite, "x")), f.sinv(f.head_site(name, "w"))))
+
+    def _lin_bwd(self, name, g16, ncols, x16, x8, xsite, dx):
+        """dx (fp32) = g W and dW += g^T x for the bf16 logit gradient g [rows, >= ncols]."""
+        st, f = self.st, self.fp8
+        n = g16.shape[0]
+        gw = st.grad_of(f"{name}.weight")
+        if f is None:
+            K.gemm(g16, st.bf16(f"{name}.weight"), b_mn=True, kind=K.EPI_STORE_F32, out=dx, K=ncols)
+            K.gemm(g16, x16, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=gw, M=ncols, K=n)
+            return
+        gs, ws, xs = f.head_site(name, "g"), f.head_site(name, "w"), f.head_site(xsite, "x")
+        g8 = f.cast(g16[:, :ncols], gs, K.FP8_E5M2)
+        K.gemm(g8, f.weights[("head", name)], b_mn=True, kind=K.EPI_STORE_F32, out=dx, K=ncols,
+               fp8=(K.FP8_E5M2, K.FP8_E4M3, f.sinv(gs), f.sinv(ws)))
+        K.gemm(g8, x8, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=gw, M=ncols, K=n,
+               fp8=(K.FP8_E5M2, K.FP8_E4M3, f.sinv(gs), f.sinv(xs)))
+
+    def head_linears(self):
+        names = ["board_head", "policy_head", "wl_head.mlp.0", "d_head.mlp.0"]
+        return names + (["thinking_policy_head"] if self.cfg.finetune else [])
+
+    def cast_fp8_weights(self):
+        f = self.fp8
+        for name in self.head_linears():
+            f.weights[("head", name)] = f.cast(self.st.param(f"{name}.weight"), f.head_site(name, "w"), K.FP8_E4M3)
 
 
 # ---------------------------------------------------------------------------
@@ -925,10 +975,12 @@ class TrainStep:
             raise ValueError("the fp8 recipe covers the dense MLP only; the MoE variant runs in bf16")
         if fp8:
             from .fp8 import Fp8Recipe
-            self.fp8 = Fp8Recipe(cfg.num_layers, self.device)
+            heads = ["board_head", "policy_head", "wl_head.mlp.0", "d_head.mlp.0"]
+            self.fp8 = Fp8Recipe(cfg.num_layers, self.device,
+                                 heads=heads + (["thinking_policy_head"] if cfg.finetune else []))
         self.backbone = Backbone(self.store, cfg, self.fp8)
         self.front = FrontEnd(self.store, cfg)
-        self.heads = Heads(self.store, cfg, loss_weights)
+        self.heads = Heads(self.store, cfg, loss_weights, fp8=self.fp8)
         self.lr, self.wd, self.betas, self.eps, self.max_norm = lr, weight_decay, betas, eps, max_norm
         self.grad_hook: Optional[Callable[[int], None]] = None
         self.grad_scale = 1.0
@@ -952,6 +1004,7 @@ class TrainStep:
         meta = K.attn_meta(db.bid, S)
         if self.fp8 is not None:
             self.backbone.cast_fp8_weights()
+            self.heads.cast_fp8_weights()
         h0, fctx = self.front.forward(db, n_copies=2)
         hN16, _, bctx = self.backbone.forward(h0, 2 * B, B, S, db.bid, meta)
         dhN = self.heads.run(db, hN16, losses, metrics)

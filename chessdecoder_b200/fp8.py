@@ -17,9 +17,17 @@ records its amax, and ``end_step`` pushes those into the histories.  In the
 first step (empty histories) each cast first measures its own tensor's amax
 ("just in time").  Casts are saturating, round-to-nearest-even.
 
-The reference has no fp8 path: its linears run in fp16 under torch.autocast
-(chessdecoder/train/train.py:168).  Heads, norms, attention, softmax and the
+The heads' linears (board, policy, thinking, and the first Linear of the WL
+/ D value heads) follow the same recipe with ``heads=`` names: their weight and
+logit-gradient sites per head, and one input site per row set -- the pass-1
+rows (board head), the pass-2 rows (policy / thinking heads, quantised once
+for all pass-2 rows as the reference applies those heads to all of them), and
+each value head's gathered rows.  The value heads' second Linear (128 -> 100,
+inside the fused value-tail kernel), norms, attention, softmax and the
 optimizer stay as in the bf16 step.
+
+The reference has no fp8 path: its linears run in fp16 under torch.autocast
+(chessdecoder/train/train.py:168).
 """
 from __future__ import annotations
 
@@ -29,13 +37,15 @@ from . import kernels as K
 
 HIST_LEN = 16
 LINEARS = ("qkv", "o", "13", "2")
+# head input row sets: pass-1 rows, pass-2 rows, the value heads' gathered rows
+HEAD_INPUTS = ("h_causal", "h_prefix", "wl_head.mlp.0", "d_head.mlp.0")
 
 
 class Fp8Recipe:
     """Scaling state (device arrays, one entry per site) and the per-step fp8
     weight copies of a Backbone."""
 
-    def __init__(self, num_layers: int, device, hist_len: int = HIST_LEN):
+    def __init__(self, num_layers: int, device, hist_len: int = HIST_LEN, heads=()):
         self.device = torch.device(device)
         self.hist_len = hist_len
         self.index = {}
@@ -45,6 +55,14 @@ class Fp8Recipe:
                 for kind, fmax in (("x", 448.0), ("w", 448.0), ("g", 57344.0)):
                     self.index[(i, lin, kind)] = len(fm)
                     fm.append(fmax)
+        # heads: ("head", name, "w" | "g") per head linear, ("head", rows, "x") per input row set
+        for name in heads:
+            for kind, fmax in (("w", 448.0), ("g", 57344.0)):
+                self.index[("head", name, kind)] = len(fm)
+                fm.append(fmax)
+        for rows in HEAD_INPUTS if heads else ():
+            self.index[("head", rows, "x")] = len(fm)
+            fm.append(448.0)
         n = len(fm)
         self.n = n
         self.fmax = torch.tensor(fm, device=self.device)
@@ -58,12 +76,16 @@ class Fp8Recipe:
     def site(self, layer: int, lin: str, kind: str) -> int:
         return self.index[(layer, lin, kind)]
 
+    def head_site(self, name: str, kind: str) -> int:
+        return self.index[("head", name, kind)]
+
     def sinv(self, i: int) -> torch.Tensor:
         return self.scale_inv[i:i + 1]
 
-    def cast(self, x: torch.Tensor, i: int, fmt: int, transpose: bool = False):
+    def cast(self, x: torch.Tensor, i: int, fmt: int, transpose: bool = False, out=None):
         """8-bit copy [rows, cols] of a 2-D fp32 / bf16 tensor (and, with
-        transpose=True, also its [cols, rows] transpose: returns (x8, x8T))."""
+        transpose=True, also its [cols, rows] transpose: returns (x8, x8T)).
+        out: an 8-bit [rows, cols] destination (row pitch a multiple of 16 B)."""
         rows, cols = x.shape
         if self.steps == 0:
             K.fp8_amax(x, self.amax[i:i + 1])
@@ -73,7 +95,7 @@ class Fp8Recipe:
         else:
             amax = self.amax[i:i + 1]
         dt = torch.float8_e4m3fn if fmt == K.FP8_E4M3 else torch.float8_e5m2
-        x8 = _empty8(rows, cols, dt, self.device)
+        x8 = _empty8(rows, cols, dt, self.device) if out is None else out
         xt = _empty8(cols, rows, dt, self.device) if transpose else None
         K.fp8_cast(x, self.scale[i:i + 1], fmt, out=x8, out_t=xt, amax=amax)
         return (x8, xt) if transpose else x8

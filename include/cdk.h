@@ -79,8 +79,8 @@ int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b, int64_t l
  *      gradients, per-tensor delayed scaling; no counterpart in the reference,
  *      whose GEMMs run through torch.autocast fp16) ----------------------------
  * cdk_gemm_fp8: C = epilogue((A B^T) * (*scale_inv_a) * (*scale_inv_b)) with
- * 8-bit A and B laid out as in cdk_gemm_bf16 (a_mn / b_mn: MN-major, M / N a
- * multiple of 16 then; row pitch lda / ldb in bytes, a multiple of 16); a_fmt /
+ * 8-bit A and B laid out as in cdk_gemm_bf16 (a_mn / b_mn: MN-major; row
+ * pitch lda / ldb in bytes, a multiple of 16); a_fmt /
  * b_fmt: 0 = e4m3, 1 = e5m2 (they may differ).  Same epilogue kinds and
  * split-K rules as cdk_gemm_bf16. */
 int cdk_gemm_fp8(const void* a, int64_t lda, int a_mn, int a_fmt, const void* b, int64_t ldb, int b_mn, int b_fmt,

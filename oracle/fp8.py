@@ -15,8 +15,14 @@ the recipe itself rather than only against the fp32 step:
   conversion);
 * Y = (X8 W8^T) / (sX sW); dX = (dY8 W8) / (sdY sW); dW = (dY8^T X8) / (sdY sX),
   products of the 8-bit values accumulated in fp32;
-* heads, norms, attention, softmax, the Fourier encoder and the embedding stay
-  in fp32 here (the CUDA step runs them in bf16 / fp32).
+* the head linears follow the same recipe: the board head on the pass-1 rows,
+  the policy / thinking heads on all pass-2 rows (as the step applies them;
+  the CUDA step evaluates only the rows the loss reads, whose products are the
+  same, with the input scale taken over all pass-2 rows), the first Linear of
+  each value head on its gathered rows; biases are added in fp32;
+* the value heads' second Linear, norms, attention, softmax, the Fourier
+  encoder and the embedding stay in fp32 here (the CUDA step runs them in
+  bf16 / fp32).
 
 ``Fp8OracleChessDecoder`` is ``OracleChessDecoder`` with these linears; its
 construction order, weights and state-dict keys are the base model's.
@@ -64,8 +70,21 @@ def fp8_linear(x, w):
     return y.reshape(*shp[:-1], w.shape[0])
 
 
+def _fp8_head(lin):
+    def forward(x):
+        return fp8_linear(x, lin.weight) + lin.bias
+    return forward
+
+
 class Fp8OracleChessDecoder(OracleChessDecoder):
-    """OracleChessDecoder whose four backbone linears per layer follow the fp8 recipe."""
+    """OracleChessDecoder whose four backbone linears per layer and whose head
+    linears follow the fp8 recipe."""
+
+    def __init__(self, *args, **kwargs):
+        super().__init__(*args, **kwargs)
+        for lin in (self.board_head, self.policy_head, self.thinking_policy_head, self.wl_head.mlp[0],
+                    self.d_head.mlp[0]):
+            lin.forward = _fp8_head(lin)  # an instance attribute: parameters and state-dict keys unchanged
 
     def _layer(self, layer, x, mask, input_pos):
         B, S, E = x.shape

@@ -190,3 +190,42 @@ def test_fp8_gemm_mn_major(K, a_mn, b_mn, M, N, K_):
         torch.cuda.synchronize()
         assert rel_err(acc, ref) < 1e-5
     assert K.get_error() == 0
+
+
+def _t8_padded(x):
+    """Transposed copy of an 8-bit tensor whose row pitch is rounded up to 16 bytes."""
+    cols, rows = x.shape[0], x.shape[1]
+    buf = torch.zeros(rows, (cols + 15) // 16 * 16, dtype=torch.uint8, device=x.device)
+    buf[:, :cols] = x.view(torch.uint8).t()
+    return buf[:, :cols].view(x.dtype)
+
+
+@pytest.mark.parametrize("nv", [44, 1924, 128])
+def test_fp8_head_gemm_shapes(K, nv):
+    """The head linears on fp8: logits [rows, nv] = X W^T, dX = G W (W read
+    MN-major, K = nv), dW = G^T X (both MN-major, M = nv) -- vocabulary sizes
+    that are not multiples of 16 (board 44, moves 1924) with 16-byte pitches."""
+    g = torch.Generator(device=DEV).manual_seed(nv)
+    rows, E = 3000, 1024
+    X = _q((rows, E), 0, g, 1.0)
+    W = _q((nv, E), 0, g, 1.0)
+    G = _q((rows, nv), 1, g, 1.0)
+    Gp = _t8_padded(_t8_padded(G))  # [rows, nv] with a 16-byte pitch
+    Wt = W  # [nv, E]: K = nv rows, N = E (MN-major B of dX)
+    sa = torch.tensor([0.5], device=DEV)
+    sb = torch.tensor([0.25], device=DEV)
+    bias = torch.randn(nv, device=DEV)
+    y = torch.empty(rows, nv, device=DEV)
+    K.gemm(X, W, kind=K.EPI_STORE_F32, out=y, bias=bias, fp8=(0, 0, sa, sb))
+    ref_y = (X.float() @ W.float().t()) * 0.125 + bias
+    dx = torch.empty(rows, E, device=DEV)
+    K.gemm(Gp, Wt, b_mn=True, kind=K.EPI_STORE_F32, out=dx, K=nv, fp8=(1, 0, sa, sb))
+    ref_dx = (G.float() @ W.float()) * 0.125
+    dw = torch.zeros(nv, E, device=DEV)
+    K.gemm(Gp, X, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=dw, M=nv, K=rows, fp8=(1, 0, sa, sb))
+    ref_dw = (G.float().t() @ X.float()) * 0.125
+    torch.cuda.synchronize()
+    assert rel_err(y, ref_y) < 1e-5
+    assert rel_err(dx, ref_dx) < 1e-5
+    assert rel_err(dw, ref_dw) < 1e-5
+    assert K.get_error() == 0

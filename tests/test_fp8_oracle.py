@@ -55,3 +55,15 @@ def test_fp8_model_keeps_weights_and_tracks_fp32_model():
     l8 = step_losses(f8, batch)
     for n in ("move", "board", "wl", "d"):
         assert abs(float(l8[n]) - float(lb[n])) <= 3e-2 * abs(float(lb[n])), n
+
+
+def test_fp8_model_heads_follow_the_recipe():
+    from oracle.model import OracleChessDecoder  # noqa: F401
+    torch.manual_seed(0)
+    f8 = Fp8OracleChessDecoder(1968, embed_dim=64, num_heads=2, num_layers=1, max_seq_len=32, d_ff=96)
+    x = torch.randn(2, 7, 64)
+    for lin in (f8.board_head, f8.policy_head, f8.thinking_policy_head, f8.wl_head.mlp[0], f8.d_head.mlp[0]):
+        assert torch.equal(lin(x), fp8_linear(x, lin.weight) + lin.bias)
+    # the value head's second Linear stays fp32
+    h = f8.wl_head.mlp[1](f8.wl_head.mlp[0](x))
+    assert torch.allclose(f8.wl_head(x), f8.wl_head.mlp[2](h))
