@@ -61,6 +61,8 @@ SIGNATURES = {
     "cdk_attn_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
     "cdk_attn_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp]),
     "cdk_rmsnorm_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
+    "cdk_rmsnorm_fwd_q8": (_int, [_vp, _vp, _vp, _i64, _int, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
+    "cdk_rmsnorm_bwd_q8": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _vp, _vp, _vp, _i64, _i64, _vp]),
     "cdk_rmsnorm_bwd": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "cdk_fourier_features": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _i64, _vp, _vp, _vp]),
     "cdk_embed_fwd": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _vp]),
@@ -76,6 +78,7 @@ SIGNATURES = {
     "cdk_add_f32": (_int, [_vp, _vp, _vp, _i64, _vp]),
     "cdk_scale_f32": (_int, [_vp, _i64, _f32, _vp]),
     "cdk_swiglu_bwd": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _vp]),
+    "cdk_swiglu_bwd_q8": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _vp, _i64, _i64, _vp]),
     "cdk_gemm_f32": (_int, [_vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "cdk_sumsq": (_int, [_vp, _i64, _vp, _i64, _vp]),
     "cdk_adamw": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _f32, _f32, _f32, _f32, _f32, _f32, _i64, _f32,

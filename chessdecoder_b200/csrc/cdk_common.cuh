@@ -8,6 +8,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -391,6 +392,49 @@ __device__ __forceinline__ float warp_max(float v) {
   #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
+}
+
+// ---------------------------------------------------------------------------
+// Optional 8-bit output of an elementwise kernel (the fp8 recipe's casts fused
+// into the kernel that produces the tensor): q = saturate(v * (*qscale)) in
+// e4m3 (fmt 0) or e5m2 (fmt 1), round to nearest even, and
+// amax = max(amax, max |v|) over the tensor.
+// ---------------------------------------------------------------------------
+struct Q8Out {
+  uint8_t* q;           // null: no 8-bit output
+  long long ldq;        // row pitch in bytes
+  int fmt;
+  const float* qscale;  // device scalar
+  float* amax;          // device scalar (max-accumulated), may be null
+};
+
+__device__ __forceinline__ uint32_t q8_pack4(float a, float b, float c, float d, float s, int fmt) {
+  const __nv_fp8_interpretation_t t = fmt == 0 ? __NV_E4M3 : __NV_E5M2;
+  return (uint32_t)__nv_cvt_float_to_fp8(a * s, __NV_SATFINITE, t) |
+         ((uint32_t)__nv_cvt_float_to_fp8(b * s, __NV_SATFINITE, t) << 8) |
+         ((uint32_t)__nv_cvt_float_to_fp8(c * s, __NV_SATFINITE, t) << 16) |
+         ((uint32_t)__nv_cvt_float_to_fp8(d * s, __NV_SATFINITE, t) << 24);
+}
+
+__device__ __forceinline__ float abs_max4(float m, float a, float b, float c, float d) {
+  return fmaxf(fmaxf(m, fmaxf(fabsf(a), fabsf(b))), fmaxf(fabsf(c), fabsf(d)));
+}
+
+// Block-wide max of v, folded into *amax by one atomic per block.  Every
+// thread of the block must call it (it synchronises the block); blockDim.x is
+// a multiple of 32, at most 1024.  Non-negative floats order like their bits.
+__device__ __forceinline__ void block_amax_atomic(float v, float* amax) {
+  __shared__ float red[32];
+  v = warp_max(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
+    v = warp_max(v);
+    if (lane == 0 && v > 0.f) atomicMax(reinterpret_cast<int*>(amax), __float_as_int(v));
+  }
 }
 
 }  // namespace cdk

@@ -54,11 +54,15 @@ __global__ void scale_f32_kernel(float* __restrict__ x, long long n, float s) {
 // stored pre-activations gu = [g | u] (row pitch ldgu, u at column offset F),
 //   dg = du * u * silu'(g),  du_up = du * silu(g)   -> dgu = [dg | du_up].
 // Eight columns per thread, 16-byte loads and stores, fp32 math.
+template <bool QOUT>
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ du, long long lddu,
                                   const __nv_bfloat16* __restrict__ gu, long long ldgu,
-                                  __nv_bfloat16* __restrict__ dgu, long long lddgu, long long rows, int F) {
+                                  __nv_bfloat16* __restrict__ dgu, long long lddgu, long long rows, int F,
+                                  Q8Out q8) {
   const int f8 = F / 8;
   const long long total = rows * f8;
+  const float qs = QOUT ? *q8.qscale : 0.f;
+  float m = 0.f;  // max |dgu| of this thread's values (8-bit output)
   for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (long long)gridDim.x * blockDim.x) {
     const long long r = idx / f8;
@@ -69,17 +73,38 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ du, long lon
     const __nv_bfloat162* hd = reinterpret_cast<const __nv_bfloat162*>(&wd);
     const __nv_bfloat162* hg = reinterpret_cast<const __nv_bfloat162*>(&wg);
     const __nv_bfloat162* hu = reinterpret_cast<const __nv_bfloat162*>(&wu);
-    uint32_t og[4], ou[4];
+    float fg[8], fu[8];
     #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 d = __bfloat1622float2(hd[j]), g = __bfloat1622float2(hg[j]), u = __bfloat1622float2(hu[j]);
       const float s0 = 1.f / (1.f + __expf(-g.x)), s1 = 1.f / (1.f + __expf(-g.y));
-      og[j] = pack_bf16(d.x * u.x * (s0 * (1.f + g.x * (1.f - s0))), d.y * u.y * (s1 * (1.f + g.y * (1.f - s1))));
-      ou[j] = pack_bf16(d.x * g.x * s0, d.y * g.y * s1);
+      fg[2 * j] = d.x * u.x * (s0 * (1.f + g.x * (1.f - s0)));
+      fg[2 * j + 1] = d.y * u.y * (s1 * (1.f + g.y * (1.f - s1)));
+      fu[2 * j] = d.x * g.x * s0;
+      fu[2 * j + 1] = d.y * g.y * s1;
     }
-    *reinterpret_cast<uint4*>(dgu + r * lddgu + c) = make_uint4(og[0], og[1], og[2], og[3]);
-    *reinterpret_cast<uint4*>(dgu + r * lddgu + F + c) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+    if (QOUT) {
+      uint8_t* q = q8.q + r * q8.ldq;
+      *reinterpret_cast<uint2*>(q + c) = make_uint2(q8_pack4(fg[0], fg[1], fg[2], fg[3], qs, q8.fmt),
+                                                    q8_pack4(fg[4], fg[5], fg[6], fg[7], qs, q8.fmt));
+      *reinterpret_cast<uint2*>(q + F + c) = make_uint2(q8_pack4(fu[0], fu[1], fu[2], fu[3], qs, q8.fmt),
+                                                        q8_pack4(fu[4], fu[5], fu[6], fu[7], qs, q8.fmt));
+      #pragma unroll
+      for (int j = 0; j < 2; ++j)
+        m = abs_max4(abs_max4(m, fg[4 * j], fg[4 * j + 1], fg[4 * j + 2], fg[4 * j + 3]), fu[4 * j], fu[4 * j + 1],
+                     fu[4 * j + 2], fu[4 * j + 3]);
+    } else {
+      uint32_t og[4], ou[4];
+      #pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        og[j] = pack_bf16(fg[2 * j], fg[2 * j + 1]);
+        ou[j] = pack_bf16(fu[2 * j], fu[2 * j + 1]);
+      }
+      *reinterpret_cast<uint4*>(dgu + r * lddgu + c) = make_uint4(og[0], og[1], og[2], og[3]);
+      *reinterpret_cast<uint4*>(dgu + r * lddgu + F + c) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+    }
   }
+  if (QOUT && q8.amax) block_amax_atomic(m, q8.amax);
 }
 
 // C[M,N] = beta*C + sum_k A(m,k) B(n,k) + bias[n]
@@ -218,18 +243,50 @@ extern "C" int cdk_scale_f32(float* x, int64_t n, float s, void* stream) {
   return finish();
 }
 
+static int swiglu_bwd_impl(const void* du, int64_t lddu, const void* gu, int64_t ldgu, void* dgu, int64_t lddgu,
+                           int64_t rows, int64_t F, Q8Out q8, void* stream) {
+  long long blocks = (rows * (F / 8) + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  auto* d16 = reinterpret_cast<__nv_bfloat16*>(dgu);
+  auto* du16 = reinterpret_cast<const __nv_bfloat16*>(du);
+  auto* gu16 = reinterpret_cast<const __nv_bfloat16*>(gu);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (q8.q) swiglu_bwd_kernel<true><<<(unsigned)blocks, 256, 0, s>>>(du16, lddu, gu16, ldgu, d16, lddgu, rows, (int)F, q8);
+  else swiglu_bwd_kernel<false><<<(unsigned)blocks, 256, 0, s>>>(du16, lddu, gu16, ldgu, d16, lddgu, rows, (int)F, q8);
+  return finish();
+}
+
 extern "C" int cdk_swiglu_bwd(const void* du, int64_t lddu, const void* gu, int64_t ldgu, void* dgu, int64_t lddgu,
                               int64_t rows, int64_t F, void* stream) {
   if (rows == 0) return 0;
   if (!du || !gu || !dgu || F % 8 || lddu % 8 || ldgu % 8 || lddgu % 8 || rows < 0) return -1;
   if ((reinterpret_cast<uintptr_t>(du) | reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(dgu)) & 15)
     return -2;
-  long long blocks = (rows * (F / 8) + 255) / 256;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  swiglu_bwd_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const __nv_bfloat16*>(du), lddu, reinterpret_cast<const __nv_bfloat16*>(gu), ldgu,
-      reinterpret_cast<__nv_bfloat16*>(dgu), lddgu, rows, (int)F);
-  return finish();
+  Q8Out q8;
+  q8.q = nullptr;
+  q8.ldq = 0;
+  q8.fmt = 0;
+  q8.qscale = nullptr;
+  q8.amax = nullptr;
+  return swiglu_bwd_impl(du, lddu, gu, ldgu, dgu, lddgu, rows, F, q8, stream);
+}
+
+extern "C" int cdk_swiglu_bwd_q8(const void* du, int64_t lddu, const void* gu, int64_t ldgu, void* dgu8,
+                                 int64_t lddgu8, int fmt, const float* qscale, float* amax, int64_t rows, int64_t F,
+                                 void* stream) {
+  if (rows == 0) return 0;
+  if (!du || !gu || !dgu8 || !qscale || (fmt != 0 && fmt != 1) || F % 8 || lddu % 8 || ldgu % 8 || lddgu8 % 16 ||
+      lddgu8 < 2 * F || rows < 0)
+    return -1;
+  if ((reinterpret_cast<uintptr_t>(du) | reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(dgu8)) & 15)
+    return -2;
+  Q8Out q8;
+  q8.q = reinterpret_cast<uint8_t*>(dgu8);
+  q8.ldq = lddgu8;
+  q8.fmt = fmt;
+  q8.qscale = qscale;
+  q8.amax = amax;
+  return swiglu_bwd_impl(du, lddu, gu, ldgu, nullptr, 0, rows, F, q8, stream);
 }
 
 extern "C" int cdk_gemm_f32(const float* a, int64_t lda, int a_t, const float* b, int64_t ldb, int b_t, float* c,

@@ -619,16 +619,23 @@ class Backbone:
             w = self._w(i)
             s = LayerSaved()
             s.x = x
-            s.n1 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
             s.r1 = torch.empty(T, device=dev)
-            K.rmsnorm_fwd(x, w["s1"], y16=s.n1, rstd=s.r1)
+            # fp8 after the first step: the norm writes the e4m3 GEMM input itself
+            fq = f8.fused(f8.site(i, "qkv", "x"), E4, T, E) if f8 is not None else None
+            if fq is not None:
+                s.n1, s.n1T = None, fq[0]
+                K.rmsnorm_fwd(x, w["s1"], rstd=s.r1, q8=fq[1])
+            else:
+                s.n1 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+                K.rmsnorm_fwd(x, w["s1"], y16=s.n1, rstd=s.r1)
             s.qkv = torch.empty(T, 3 * E, device=dev, dtype=torch.bfloat16)
             if f8 is None:
                 K.gemm(s.n1, w["wqkv"], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=rope, seq_len=S, rope_cols=2 * E)
             else:
-                x8 = s.n1T = f8.cast(s.n1, f8.site(i, "qkv", "x"), E4)
-                s.n1 = None
-                K.gemm(x8, f8.weights[(i, "qkv")], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=rope, seq_len=S,
+                if fq is None:
+                    s.n1T = f8.cast(s.n1, f8.site(i, "qkv", "x"), E4)
+                    s.n1 = None
+                K.gemm(s.n1T, f8.weights[(i, "qkv")], kind=K.EPI_ROPE_BF16, out=s.qkv, rope=rope, seq_len=S,
                        rope_cols=2 * E, fp8=self._f8(i, "qkv", "x", E4, "w", E4))
             s.ao = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
             s.lse = torch.empty(nseq * H * S, device=dev)
@@ -646,9 +653,14 @@ class Backbone:
                 saved.append(s)
                 x = out
                 continue
-            s.n2 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
             s.r2 = torch.empty(T, device=dev)
-            K.rmsnorm_fwd(s.h1, w["s2"], y16=s.n2, rstd=s.r2)
+            fq = f8.fused(f8.site(i, "13", "x"), E4, T, E) if f8 is not None else None
+            if fq is not None:
+                s.n2, s.n2T = None, fq[0]
+                K.rmsnorm_fwd(s.h1, w["s2"], rstd=s.r2, q8=fq[1])
+            else:
+                s.n2 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+                K.rmsnorm_fwd(s.h1, w["s2"], y16=s.n2, rstd=s.r2)
             s.gu = torch.empty(T, 2 * F, device=dev, dtype=torch.bfloat16)
             s.u = torch.empty(T, F, device=dev, dtype=torch.bfloat16)
             out = torch.empty(T, E, device=dev)
@@ -656,9 +668,10 @@ class Backbone:
                 K.gemm(s.n2, w["w13"], kind=K.EPI_SWIGLU, out=s.u, out2=s.gu, half_n=F)
                 K.gemm(s.u, w["w2"], kind=K.EPI_RESID_F32, out=out, resid=s.h1)
             else:
-                n8 = s.n2T = f8.cast(s.n2, f8.site(i, "13", "x"), E4)
-                s.n2 = None
-                K.gemm(n8, f8.weights[(i, "13")], kind=K.EPI_SWIGLU, out=s.u, out2=s.gu, half_n=F,
+                if fq is None:
+                    s.n2T = f8.cast(s.n2, f8.site(i, "13", "x"), E4)
+                    s.n2 = None
+                K.gemm(s.n2T, f8.weights[(i, "13")], kind=K.EPI_SWIGLU, out=s.u, out2=s.gu, half_n=F,
                        fp8=self._f8(i, "13", "x", E4, "w", E4))
                 u8 = s.uT = f8.cast(s.u, f8.site(i, "2", "x"), E4)
                 s.u = None
@@ -684,7 +697,16 @@ class Backbone:
         dev = dhN.device
         dh = torch.empty(T, E, device=dev)
         dh16 = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
-        K.rmsnorm_bwd(dhN, xL, st.param("norm.scale"), rN, dx=dh, dx16=dh16, dscale=st.grad_of("norm.scale"))
+        f8 = self.fp8
+        E4, E5 = K.FP8_E4M3, K.FP8_E5M2
+        # fp8 after the first step: each norm backward writes the e5m2 dY of the
+        # linear below it (w2's from the final norm and from each sa_norm, the
+        # output projection's from each mlp_norm) and the SwiGLU backward that of
+        # w1|w3
+        fq = f8.fused(f8.site(cfg.num_layers - 1, "2", "g"), E5, T, E) if f8 is not None else None
+        g2_8 = fq[0] if fq is not None else None
+        K.rmsnorm_bwd(dhN, xL, st.param("norm.scale"), rN, dx=dh, dx16=None if fq else dh16,
+                      dscale=st.grad_of("norm.scale"), q8=fq[1] if fq else None)
         if on_layer_done is not None:
             on_layer_done(cfg.num_layers)  # heads + final norm done
         dgu = torch.empty(T, 2 * F, device=dev, dtype=torch.bfloat16)
@@ -695,8 +717,6 @@ class Backbone:
         dao = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
         dqkv = torch.empty(T, 3 * E, device=dev, dtype=torch.bfloat16)
         dsum = torch.empty(nseq * H * S, device=dev)
-        f8 = self.fp8
-        E4, E5 = K.FP8_E4M3, K.FP8_E5M2
         for i in reversed(range(cfg.num_layers)):
             s = saved[i]
             w, g = self._w(i), self._g(i)
@@ -710,25 +730,33 @@ class Backbone:
                 K.gemm(dgu, w["w13"], b_mn=True, kind=K.EPI_STORE_BF16, out=dn)
                 K.gemm(dgu, s.n2, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w13"])
             else:
-                g8 = f8.cast(dh16, f8.site(i, "2", "g"), E5)
+                g8 = g2_8 if g2_8 is not None else f8.cast(dh16, f8.site(i, "2", "g"), E5)
                 K.gemm(g8, f8.weights[(i, "2")], b_mn=True, kind=K.EPI_STORE_BF16, out=du,
                        fp8=self._f8(i, "2", "g", E5, "w", E4))
-                K.swiglu_bwd(du, s.gu, dgu)
+                fq = f8.fused(f8.site(i, "13", "g"), E5, T, 2 * F)
+                if fq is not None:
+                    K.swiglu_bwd(du, s.gu, q8=fq[1])
+                else:
+                    K.swiglu_bwd(du, s.gu, dgu)
                 K.gemm(g8, s.uT, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w2"],
                        fp8=self._f8(i, "2", "g", E5, "x", E4))
-                g8 = f8.cast(dgu, f8.site(i, "13", "g"), E5)
+                g8 = fq[0] if fq is not None else f8.cast(dgu, f8.site(i, "13", "g"), E5)
                 K.gemm(g8, f8.weights[(i, "13")], b_mn=True, kind=K.EPI_STORE_BF16, out=dn,
                        fp8=self._f8(i, "13", "g", E5, "w", E4))
                 K.gemm(g8, s.n2T, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["w13"],
                        fp8=self._f8(i, "13", "g", E5, "x", E4))
+            go_8 = None
             if not cfg.moe_experts:
-                K.rmsnorm_bwd(dn, s.h1, w["s2"], s.r2, dx=dh1, dx16=dh1_16, dscale=g["s2"], dres=dh)
+                fq = f8.fused(f8.site(i, "o", "g"), E5, T, E) if f8 is not None else None
+                go_8 = fq[0] if fq is not None else None
+                K.rmsnorm_bwd(dn, s.h1, w["s2"], s.r2, dx=dh1, dx16=None if fq else dh1_16, dscale=g["s2"], dres=dh,
+                              q8=fq[1] if fq else None)
             # attention block
             if f8 is None:
                 K.gemm(dh1_16, w["wo"], b_mn=True, kind=K.EPI_STORE_BF16, out=dao)
                 K.gemm(dh1_16, s.ao, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wo"])
             else:
-                g8 = f8.cast(dh1_16, f8.site(i, "o", "g"), E5)
+                g8 = go_8 if go_8 is not None else f8.cast(dh1_16, f8.site(i, "o", "g"), E5)
                 K.gemm(g8, f8.weights[(i, "o")], b_mn=True, kind=K.EPI_STORE_BF16, out=dao,
                        fp8=self._f8(i, "o", "g", E5, "w", E4))
                 K.gemm(g8, s.aoT, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wo"],
@@ -743,7 +771,10 @@ class Backbone:
                        fp8=self._f8(i, "qkv", "g", E5, "w", E4))
                 K.gemm(g8, s.n1T, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wqkv"],
                        fp8=self._f8(i, "qkv", "g", E5, "x", E4))
-            K.rmsnorm_bwd(dn, s.x, w["s1"], s.r1, dx=dh, dx16=dh16, dscale=g["s1"], dres=dh1)
+            fq = f8.fused(f8.site(i - 1, "2", "g"), E5, T, E) if (f8 is not None and i > 0) else None
+            g2_8 = fq[0] if fq is not None else None
+            K.rmsnorm_bwd(dn, s.x, w["s1"], s.r1, dx=dh, dx16=None if fq else dh16, dscale=g["s1"], dres=dh1,
+                          q8=fq[1] if fq else None)
             if on_layer_done is not None:
                 on_layer_done(i)
         return dh

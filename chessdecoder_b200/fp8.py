@@ -100,6 +100,16 @@ class Fp8Recipe:
         K.fp8_cast(x, self.scale[i:i + 1], fmt, out=x8, out_t=xt, amax=amax)
         return (x8, xt) if transpose else x8
 
+    def fused(self, i: int, fmt: int, rows: int, cols: int):
+        """(out8, q8) for a kernel that writes site i's 8-bit copy itself (the
+        cast fused into the producer, amax recorded there), or None in the first
+        step, whose just-in-time scale needs the tensor's amax before any cast."""
+        if self.steps == 0:
+            return None
+        dt = torch.float8_e4m3fn if fmt == K.FP8_E4M3 else torch.float8_e5m2
+        out = _empty8(rows, cols, dt, self.device)
+        return out, (out, fmt, self.scale[i:i + 1], self.amax[i:i + 1])
+
     def cast_weights(self, layer: int, ws: dict):
         """ws: linear name -> fp32 weight [N, K] (views of the master store)."""
         for lin, w in ws.items():

@@ -290,20 +290,33 @@ def attn_bwd(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid32=None, 
 # RMSNorm
 # ---------------------------------------------------------------------------
 @_timed("rmsnorm_fwd")
-def rmsnorm_fwd(x, scale, y16=None, y32=None, rstd=None, eps=1e-6):
+def rmsnorm_fwd(x, scale, y16=None, y32=None, rstd=None, eps=1e-6, q8=None):
+    """q8 = (out8, fmt, qscale, amax): the output written as 8-bit (fp8 recipe) in place of y16 / y32."""
     _need_cuda(x, scale)
     rows, dim = x.shape
-    rc = lib().cdk_rmsnorm_fwd(_p(x), _p(scale), _p(y16), _p(y32), _p(rstd), rows, dim, eps, _stream())
+    if q8 is None:
+        rc = lib().cdk_rmsnorm_fwd(_p(x), _p(scale), _p(y16), _p(y32), _p(rstd), rows, dim, eps, _stream())
+    else:
+        o8, fmt, qs, amax = q8
+        rc = lib().cdk_rmsnorm_fwd_q8(_p(x), _p(scale), _p(o8), o8.stride(0), fmt, _p(qs), _p(amax), _p(rstd), rows,
+                                      dim, eps, _stream())
     _check(rc, "rmsnorm_fwd")
     _count(1)
 
 
 @_timed("rmsnorm_bwd")
-def rmsnorm_bwd(dy, x, scale, rstd, dx=None, dx16=None, dscale=None, dres=None):
+def rmsnorm_bwd(dy, x, scale, rstd, dx=None, dx16=None, dscale=None, dres=None, q8=None):
+    """q8 = (out8, fmt, qscale, amax): dx written as 8-bit (fp8 recipe) in place of dx16."""
     _need_cuda(dy, x, scale, rstd)
     rows, dim = x.shape
-    rc = lib().cdk_rmsnorm_bwd(_p(dy), int(dy.dtype == torch.float32), _p(x), _p(scale), _p(rstd), _p(dres), _p(dx),
-                               _p(dx16), _p(dscale), rows, dim, _stream())
+    if q8 is None:
+        rc = lib().cdk_rmsnorm_bwd(_p(dy), int(dy.dtype == torch.float32), _p(x), _p(scale), _p(rstd), _p(dres),
+                                   _p(dx), _p(dx16), _p(dscale), rows, dim, _stream())
+    else:
+        o8, fmt, qs, amax = q8
+        rc = lib().cdk_rmsnorm_bwd_q8(_p(dy), int(dy.dtype == torch.float32), _p(x), _p(scale), _p(rstd), _p(dres),
+                                      _p(dx), _p(o8), o8.stride(0), fmt, _p(qs), _p(amax), _p(dscale), rows, dim,
+                                      _stream())
     _check(rc, "rmsnorm_bwd")
     _count(1)
 
@@ -428,11 +441,18 @@ def add_f32(a, b, out):
 
 
 @_timed("swiglu_bwd")
-def swiglu_bwd(du, gu, dgu):
-    """dgu = [du*u*silu'(g) | du*silu(g)] from du [T,F] and gu = [g | u] [T,2F] (all bf16)."""
-    _need_cuda(du, gu, dgu)
+def swiglu_bwd(du, gu, dgu=None, q8=None):
+    """dgu = [du*u*silu'(g) | du*silu(g)] from du [T,F] and gu = [g | u] [T,2F] (all bf16);
+    q8 = (out8, fmt, qscale, amax): dgu written as 8-bit (fp8 recipe) instead."""
+    _need_cuda(du, gu)
     rows, F = du.shape
-    rc = lib().cdk_swiglu_bwd(_p(du), du.stride(0), _p(gu), gu.stride(0), _p(dgu), dgu.stride(0), rows, F, _stream())
+    if q8 is None:
+        rc = lib().cdk_swiglu_bwd(_p(du), du.stride(0), _p(gu), gu.stride(0), _p(dgu), dgu.stride(0), rows, F,
+                                  _stream())
+    else:
+        o8, fmt, qs, amax = q8
+        rc = lib().cdk_swiglu_bwd_q8(_p(du), du.stride(0), _p(gu), gu.stride(0), _p(o8), o8.stride(0), fmt, _p(qs),
+                                     _p(amax), rows, F, _stream())
     _check(rc, "swiglu_bwd")
     _count(1)
 

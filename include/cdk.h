@@ -173,6 +173,18 @@ int cdk_rmsnorm_fwd(const float* x, const float* scale, void* y_bf16, float* y_f
 int cdk_rmsnorm_bwd(const void* dy, int dy_is_f32, const float* x, const float* scale, const float* rstd,
                     const float* dres, float* dx, void* dx_bf16, float* dscale, int64_t rows, int64_t dim,
                     void* stream);
+/* The fp8 recipe's casts fused into the norms: the normalised output (forward)
+ * or dx (backward) written as 8-bit q = saturate(v * (*qscale)) in e4m3 (fmt 0)
+ * or e5m2 (fmt 1) with row pitch ldq bytes (a multiple of 16, 16-byte aligned
+ * base) in place of the bf16 copy, and amax = max(amax, max |v|) (amax may be
+ * null).  dim a multiple of 256.  The recipe (per-tensor delayed scaling) has
+ * no counterpart in the reference, whose linears run under torch.autocast fp16
+ * (chessdecoder/train/train.py:168). */
+int cdk_rmsnorm_fwd_q8(const float* x, const float* scale, void* y8, int64_t ldy8, int fmt, const float* qscale,
+                       float* amax, float* rstd, int64_t rows, int64_t dim, float eps, void* stream);
+int cdk_rmsnorm_bwd_q8(const void* dy, int dy_is_f32, const float* x, const float* scale, const float* rstd,
+                       const float* dres, float* dx, void* dx8, int64_t ldx8, int fmt, const float* qscale,
+                       float* amax, float* dscale, int64_t rows, int64_t dim, void* stream);
 
 /* ---- embedding + Fourier value injection (model.py:24-36, 174-180) and the
  *      bucket snapping of utils/training.py:114-133 / model.py:189-194 ------ */
@@ -229,6 +241,9 @@ int cdk_scale_f32(float* x, int64_t n, float s, void* stream);
  * [rows, F]; gu = [g | u] bf16 [rows, 2F]; dgu = [du*u*silu'(g) | du*silu(g)] bf16. */
 int cdk_swiglu_bwd(const void* du, int64_t lddu, const void* gu, int64_t ldgu, void* dgu, int64_t lddgu,
                    int64_t rows, int64_t F, void* stream);
+/* The same with dgu written as 8-bit (fp8 recipe; see cdk_rmsnorm_fwd_q8), pitch lddgu8 bytes. */
+int cdk_swiglu_bwd_q8(const void* du, int64_t lddu, const void* gu, int64_t ldgu, void* dgu8, int64_t lddgu8, int fmt,
+                      const float* qscale, float* amax, int64_t rows, int64_t F, void* stream);
 /* fp32 SIMT GEMM for small / precision-sensitive contractions (Fourier
  * projection, value-head second Linear): C = (accumulate ? C : 0) + op(A) op(B)^T + bias,
  * A(m,k) = a_t ? A[k*lda+m] : A[m*lda+k],  B(n,k) = b_t ? B[k*ldb+n] : B[n*ldb+k]. */

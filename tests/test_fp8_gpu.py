@@ -229,3 +229,73 @@ def test_fp8_head_gemm_shapes(K, nv):
     assert rel_err(dx, ref_dx) < 1e-5
     assert rel_err(dw, ref_dw) < 1e-5
     assert K.get_error() == 0
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+@pytest.mark.parametrize("rows", [1, 1000, 4103])
+def test_rmsnorm_fused_8bit_outputs(K, fmt, rows):
+    """The fp8 recipe's casts fused into the norms: the 8-bit output is exactly
+    the saturating cast of the fp32 result the same kernel computes, and amax
+    is its max |.| (max-accumulated onto a prior value)."""
+    g = torch.Generator(device=DEV).manual_seed(rows + fmt)
+    E = 1024
+    x = torch.randn(rows, E, generator=g, device=DEV) * 3
+    sc = torch.rand(E, generator=g, device=DEV) + 0.5
+    qs = torch.tensor([FMAX[fmt] / 40.0], device=DEV)
+    # forward
+    y32 = torch.empty(rows, E, device=DEV)
+    r = torch.empty(rows, device=DEV)
+    K.rmsnorm_fwd(x, sc, y32=y32, rstd=r)
+    y8 = torch.empty(rows, E, dtype=TD[fmt], device=DEV)
+    amax = torch.tensor([0.5], device=DEV)
+    r2 = torch.empty(rows, device=DEV)
+    K.rmsnorm_fwd(x, sc, rstd=r2, q8=(y8, fmt, qs, amax))
+    torch.cuda.synchronize()
+    assert torch.equal(y8.view(torch.uint8), ref_cast(y32, qs, fmt).view(torch.uint8))
+    assert torch.equal(r, r2)
+    assert float(amax) == max(0.5, float(y32.abs().max()))
+    # backward (bf16 dy, fp32 residual gradient)
+    dy = (torch.randn(rows, E, generator=g, device=DEV)).to(torch.bfloat16)
+    dres = torch.randn(rows, E, generator=g, device=DEV)
+    dx = torch.empty(rows, E, device=DEV)
+    ds = torch.zeros(E, device=DEV)
+    K.rmsnorm_bwd(dy, x, sc, r, dx=dx, dscale=ds, dres=dres)
+    dx2 = torch.empty(rows, E, device=DEV)
+    ds2 = torch.zeros(E, device=DEV)
+    d8 = torch.empty(rows, E, dtype=TD[fmt], device=DEV)
+    amax2 = torch.zeros(1, device=DEV)
+    K.rmsnorm_bwd(dy, x, sc, r, dx=dx2, dscale=ds2, dres=dres, q8=(d8, fmt, qs, amax2))
+    torch.cuda.synchronize()
+    # the two instantiations may contract the fp32 arithmetic differently (last-bit differences)
+    assert torch.allclose(dx, dx2, rtol=1e-5, atol=1e-6)
+    assert torch.allclose(ds, ds2, rtol=1e-5, atol=1e-4)
+    # the 8-bit output is the saturating cast of the fp32 dx the same launch wrote
+    assert torch.equal(d8.view(torch.uint8), ref_cast(dx2, qs, fmt).view(torch.uint8))
+    assert float(amax2) == float(dx2.abs().max())
+    assert K.get_error() == 0
+
+
+def test_swiglu_bwd_fused_8bit_output(K):
+    g = torch.Generator(device=DEV).manual_seed(11)
+    T, F = 3000, 1536
+    du = torch.randn(T, F, generator=g, device=DEV).to(torch.bfloat16)
+    gu = (torch.randn(T, 2 * F, generator=g, device=DEV) * 2).to(torch.bfloat16)
+    dgu = torch.empty(T, 2 * F, device=DEV, dtype=torch.bfloat16)
+    K.swiglu_bwd(du, gu, dgu)
+    d8 = torch.empty(T, 2 * F, device=DEV, dtype=torch.float8_e5m2)
+    qs = torch.tensor([64.0], device=DEV)
+    amax = torch.zeros(1, device=DEV)
+    K.swiglu_bwd(du, gu, q8=(d8, 1, qs, amax))
+    torch.cuda.synchronize()
+    # the same fp32 values as the bf16 form, before rounding: compare through the fp32 formula
+    d, gg, u = du.float(), gu[:, :F].float(), gu[:, F:].float()
+    s = torch.sigmoid(gg)
+    ref = torch.cat([d * u * s * (1 + gg * (1 - s)), d * gg * s], 1)
+    deq = d8.float() / 64.0
+    assert ((deq - ref).abs() <= 0.126 * ref.abs() + 1e-6).float().mean().item() > 0.999
+    exact = (d8.view(torch.uint8) == ref_cast(ref, qs, 1).view(torch.uint8)).float().mean().item()
+    assert exact > 0.999, exact
+    assert abs(float(amax) - float(ref.abs().max())) <= 1e-5 * float(ref.abs().max())
+    # the bf16 form of the same kernel agrees with the 8-bit one to bf16 / e5m2 rounding
+    assert ((dgu.float() - deq).abs() <= 0.13 * dgu.float().abs() + 1e-6).float().mean().item() > 0.999
+    assert K.get_error() == 0
