@@ -55,6 +55,7 @@ struct BwdSmem {
   uint8_t KV[2][4 * kBox];      // key tile kt: K rows (2 boxes) | V rows (2 boxes)
   uint8_t QO[2][4 * kBox];      // query half qh: Q rows (2 boxes) | dO rows (2 boxes)
   uint8_t dST[2][2][128 * 128]; // [pair buffer][sub-tile]: 128 key rows x 64 queries (bf16, 128-B swizzle)
+  uint8_t stage[4][32 * 128];   // epilogue transposition, per TMEM lane quadrant: 32 rows x 64 dims bf16
   Meta meta[2];
   uint64_t kvfull[2], kvempty[2], qfull[2], qempty[2], mfull[2], mempty[2];
   uint64_t sa[2], ew[2], dq[2], kvdone, kvfree, dqdone, dqfree;
@@ -64,6 +65,7 @@ struct BwdSmem {
 static_assert(offsetof(BwdSmem, QO) % 1024 == 0 && offsetof(BwdSmem, dST) % 1024 == 0,
               "TMA / UMMA operands with the 128-byte swizzle need 1024-byte alignment");
 static_assert(offsetof(BwdSmem, meta) % 16 == 0 && sizeof(Meta) % 16 == 0, "L / D are read as float4");
+static_assert(offsetof(BwdSmem, stage) % 128 == 0, "staging rows are read as 16-byte chunks");
 
 struct Args {
   const float* lse;       // [nseq, H, S]
@@ -145,10 +147,10 @@ __device__ __forceinline__ Rope16 load_rope16(const float* rope, int pos, int c0
   return r;
 }
 
-// dX (bf16) of 16 consecutive dims of a row: value * scale, then the inverse
-// RoPE rotation given by rp (the identity for V or without RoPE).
-__device__ __forceinline__ void store_row16(__nv_bfloat16* dst, const uint32_t (&v)[16], float scale,
-                                            const Rope16& rp) {
+// 16 consecutive dims of a dX row: value * scale, then the inverse RoPE
+// rotation given by rp (the identity for V or without RoPE), packed to bf16.
+__device__ __forceinline__ void rotate_pack16(const uint32_t (&v)[16], float scale, const Rope16& rp,
+                                              uint32_t (&w)[8]) {
   float f[16];
   #pragma unroll
   for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]) * scale;
@@ -163,11 +165,38 @@ __device__ __forceinline__ void store_row16(__nv_bfloat16* dst, const uint32_t (
     f[4 * p + 2] = x0 * t.z + x1 * t.w;
     f[4 * p + 3] = x1 * t.z - x0 * t.w;
   }
-  uint4* d = reinterpret_cast<uint4*>(dst);
   #pragma unroll
-  for (int q = 0; q < 2; ++q)
-    d[q] = make_uint4(pack_bf16(f[8 * q], f[8 * q + 1]), pack_bf16(f[8 * q + 2], f[8 * q + 3]),
-                      pack_bf16(f[8 * q + 4], f[8 * q + 5]), pack_bf16(f[8 * q + 6], f[8 * q + 7]));
+  for (int q = 0; q < 8; ++q) w[q] = pack_bf16(f[2 * q], f[2 * q + 1]);
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Stores one 32-row x 64-dim bf16 block of dQ, dK or dV (the rows of one TMEM
+// lane quadrant; each of the quadrant's 4 warps holds 16 dims of every row).
+// Row-per-thread stores would touch 32 rows per instruction; instead the four
+// warps transpose the block through shared memory (128-byte rows, chunks
+// XOR-swizzled by the row) and each warp stores 8 whole rows, 4 per
+// instruction.  All 128 threads of the quadrant call it (two named barriers).
+__device__ __forceinline__ void quad_store(uint8_t* stg, int bar_id, int lane, int g4, const uint32_t (&w)[8],
+                                           __nv_bfloat16* row0, long long pitch, int rows_valid) {
+  #pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int chunk = g4 * 2 + q;
+    *reinterpret_cast<uint4*>(stg + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
+        make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  }
+  named_bar_sync(bar_id, 128);
+  #pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int rr = g4 * 8 + it * 4 + (lane >> 3), c = lane & 7;
+    if (rr < rows_valid) {
+      const uint4 x = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((c ^ (rr & 7)) << 4));
+      *reinterpret_cast<uint4*>(row0 + (long long)rr * pitch + c * 8) = x;
+    }
+  }
+  named_bar_sync(bar_id, 128);  // the staging rows are free again
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -390,6 +419,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int g4 = (warp - 2) >> 2;  // 16-query group of the 64-query sub-tile
     const int r = quad * 32 + lane;  // key row within the key tile = TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    uint8_t* stg = sm.stage[quad];
+    const int qbar = 1 + quad;  // named barrier of the 4 warps that own this lane quadrant
     const float sl2 = 0.125f * kLog2e;
     int g = 0, c = 0;
     // The epilogues run one sub-unit late: after the last sub-unit of a key
@@ -412,11 +443,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld_dep16(kv);
       tc_fence_before();
       mbar_arrive(&sm.kvfree);
-      if (j < S) {
-        __nv_bfloat16* rowp = kv_rows + (long long)j * 3 * E;
-        store_row16(rowp + E + kv_h * kHd + g4 * 16, kv, 0.125f, rk);
-        store_row16(rowp + 2 * E + kv_h * kHd + g4 * 16, vv, 1.f, load_rope16(nullptr, 0, 0, false));
-      }
+      const int jq = kv_j0 + quad * 32;  // first key row of this quadrant
+      const int nvalid = min(max(S - jq, 0), 32);
+      __nv_bfloat16* row0 = kv_rows + (long long)jq * 3 * E + kv_h * kHd;
+      uint32_t w[8];
+      rotate_pack16(kv, 0.125f, rk, w);
+      quad_store(stg, qbar, lane, g4, w, row0 + E, 3 * E, nvalid);
+      rotate_pack16(vv, 1.f, load_rope16(nullptr, 0, 0, false), w);
+      quad_store(stg, qbar, lane, g4, w, row0 + 2 * E, 3 * E, nvalid);
       kv_pend = -1;
     };
     auto dq_epilogue = [&]() {
@@ -432,9 +466,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (nkt > 1) tmem_wait_ld_dep16(q1v);
       tc_fence_before();
       mbar_arrive(&sm.dqfree);
-      if (r < S) store_row16(dq_rows + (long long)r * 3 * E + dq_h * kHd + g4 * 16, q0v, 0.125f, r0);
-      if (nkt > 1 && 128 + r < S)
-        store_row16(dq_rows + (long long)(128 + r) * 3 * E + dq_h * kHd + g4 * 16, q1v, 0.125f, r1);
+      uint32_t w[8];
+      rotate_pack16(q0v, 0.125f, r0, w);
+      quad_store(stg, qbar, lane, g4, w, dq_rows + (long long)(quad * 32) * 3 * E + dq_h * kHd, 3 * E,
+                 min(max(S - quad * 32, 0), 32));
+      if (nkt > 1) {
+        rotate_pack16(q1v, 0.125f, r1, w);
+        quad_store(stg, qbar, lane, g4, w, dq_rows + (long long)(128 + quad * 32) * 3 * E + dq_h * kHd, 3 * E,
+                   min(max(S - 128 - quad * 32, 0), 32));
+      }
       dq_pend = -1;
     };
     for (int k = 0; k < n_local; ++k) {
