@@ -199,6 +199,41 @@ __device__ __forceinline__ void quad_store(uint8_t* stg, int bar_id, int lane, i
   named_bar_sync(bar_id, 128);  // the staging rows are free again
 }
 
+// P^T and dS^T of one thread's 16 queries: P = exp2(S * scale - L),
+// dS = P (dP - D), bf16-packed; with MASK, queries outside [e_lo, e_hi) get 0.
+template <bool MASK>
+__device__ __forceinline__ void ew16(const uint32_t (&su)[16], const uint32_t (&du)[16], const float* L, const float* D,
+                                     float sl2, int e_lo, int e_hi, uint32_t (&pk)[8], uint32_t (&dk)[8]) {
+  const float4* L4 = reinterpret_cast<const float4*>(L);
+  const float4* D4 = reinterpret_cast<const float4*>(D);
+  #pragma unroll
+  for (int e4 = 0; e4 < 4; ++e4) {
+    const float4 l4 = L4[e4], d4 = D4[e4];
+    float pv[4], dsv[4];
+    pv[0] = ex2_approx(fmaf(__uint_as_float(su[4 * e4 + 0]), sl2, -l4.x));
+    pv[1] = ex2_approx(fmaf(__uint_as_float(su[4 * e4 + 1]), sl2, -l4.y));
+    pv[2] = ex2_approx(fmaf(__uint_as_float(su[4 * e4 + 2]), sl2, -l4.z));
+    pv[3] = ex2_approx(fmaf(__uint_as_float(su[4 * e4 + 3]), sl2, -l4.w));
+    dsv[0] = pv[0] * (__uint_as_float(du[4 * e4 + 0]) - d4.x);
+    dsv[1] = pv[1] * (__uint_as_float(du[4 * e4 + 1]) - d4.y);
+    dsv[2] = pv[2] * (__uint_as_float(du[4 * e4 + 2]) - d4.z);
+    dsv[3] = pv[3] * (__uint_as_float(du[4 * e4 + 3]) - d4.w);
+    if (MASK) {
+      #pragma unroll
+      for (int kq = 0; kq < 4; ++kq) {
+        const int e = 4 * e4 + kq;
+        const bool vis = e >= e_lo && e < e_hi;
+        pv[kq] = vis ? pv[kq] : 0.f;
+        dsv[kq] = vis ? dsv[kq] : 0.f;
+      }
+    }
+    pk[e4 * 2] = pack_bf16(pv[0], pv[1]);
+    pk[e4 * 2 + 1] = pack_bf16(pv[2], pv[3]);
+    dk[e4 * 2] = pack_bf16(dsv[0], dsv[1]);
+    dk[e4 * 2 + 1] = pack_bf16(dsv[2], dsv[3]);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_pst_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo,
                         const Args a) {
@@ -501,6 +536,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // (the interval [first_j, S) is masked further below)
         const bool none = !jok || q0 + 15 < fj || q0 >= S;
         const bool none_w = __all_sync(0xffffffffu, none);
+        // every lane's 16 queries visible (below the diagonal): no interval mask
+        const bool full_w = __all_sync(0xffffffffu, jok && fj <= q0 && q0 + 16 <= S);
         // the pair buffer is free once the dQ product of pair P - 2 has retired
         if ((u & 1) == 0 && P >= 2) mbar_wait(&sm.dq[pb], ((P >> 1) - 1) & 1, abort_flag);
         mbar_wait(&sm.sa[b], (g >> 1) & 1, abort_flag);
@@ -516,32 +553,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld_dep16(du);
           if (!none) {
             const int e_lo = max(fj - q0, 0), e_hi = min(S - q0, 16);
-            const float4* L4 = reinterpret_cast<const float4*>(mt.L + q0);
-            const float4* D4 = reinterpret_cast<const float4*>(mt.D + q0);
-            #pragma unroll
-            for (int e4 = 0; e4 < 4; ++e4) {
-              const float4 l4 = L4[e4], d4 = D4[e4];
-              float pv[4], dsv[4];
-              pv[0] = ex2_approx(fmaf(__uint_as_float(su[4 * e4 + 0]), sl2, -l4.x));
-              pv[1] = ex2_approx(fmaf(__uint_as_float(su[4 * e4 + 1]), sl2, -l4.y));
-              pv[2] = ex2_approx(fmaf(__uint_as_float(su[4 * e4 + 2]), sl2, -l4.z));
-              pv[3] = ex2_approx(fmaf(__uint_as_float(su[4 * e4 + 3]), sl2, -l4.w));
-              dsv[0] = pv[0] * (__uint_as_float(du[4 * e4 + 0]) - d4.x);
-              dsv[1] = pv[1] * (__uint_as_float(du[4 * e4 + 1]) - d4.y);
-              dsv[2] = pv[2] * (__uint_as_float(du[4 * e4 + 2]) - d4.z);
-              dsv[3] = pv[3] * (__uint_as_float(du[4 * e4 + 3]) - d4.w);
-              #pragma unroll
-              for (int kq = 0; kq < 4; ++kq) {
-                const int e = 4 * e4 + kq;
-                const bool vis = e >= e_lo && e < e_hi;
-                pv[kq] = vis ? pv[kq] : 0.f;
-                dsv[kq] = vis ? dsv[kq] : 0.f;
-              }
-              pk[e4 * 2] = pack_bf16(pv[0], pv[1]);
-              pk[e4 * 2 + 1] = pack_bf16(pv[2], pv[3]);
-              dk[e4 * 2] = pack_bf16(dsv[0], dsv[1]);
-              dk[e4 * 2 + 1] = pack_bf16(dsv[2], dsv[3]);
-            }
+            if (full_w) ew16<false>(su, du, mt.L + q0, mt.D + q0, sl2, e_lo, e_hi, pk, dk);
+            else ew16<true>(su, du, mt.L + q0, mt.D + q0, sl2, e_lo, e_hi, pk, dk);
             if (!contig) {
               // a query before the key row sees it only within the key's block
               #pragma unroll
