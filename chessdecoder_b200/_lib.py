@@ -56,6 +56,8 @@ SIGNATURES = {
     "cdk_moe_gather_sum": (_int, [_vp, _vp, _vp, _i64, _i64, _int, _vp]),
     "cdk_attn_bwd_workspace": (_i64, [_i64, _i64, _i64]),
     "cdk_attn_bwd_ws": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _vp]),
+    "cdk_attn_bwd_q8": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp,
+                               _vp]),
     "cdk_attn_prefix_meta": (_int, [_vp, _i64, _i64, _vp, _vp]),
     "cdk_attn_meta_elems": (_i64, [_i64, _i64]),
     "cdk_attn_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),

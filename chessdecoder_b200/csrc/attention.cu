@@ -1197,7 +1197,7 @@ extern "C" int cdk_attn_fwd(const void* qkv, void* out, float* lse, int64_t nseq
 namespace cdk {
 int launch_attn_bwd_pst(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,
                         void* dqkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,
-                        const int32_t* meta, const float* rope, cudaStream_t stream);
+                        const int32_t* meta, const float* rope, cudaStream_t stream, const Q8Out* q8 = nullptr);
 int launch_attn_bwd_long(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,
                          void* dqkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,
                          const int32_t* meta, const float* rope, void* workspace, cudaStream_t stream);
@@ -1212,6 +1212,29 @@ extern "C" int cdk_attn_bwd(const void* qkv, const void* out, const void* dout, 
                             void* dqkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,
                             const int32_t* meta, const float* rope, void* stream) {
   return cdk_attn_bwd_ws(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid, meta, rope, nullptr, 0, stream);
+}
+
+extern "C" int cdk_attn_bwd_q8(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,
+                               void* dqkv8, int64_t ld8, int fmt, const float* qscale, float* amax, int64_t nseq,
+                               int64_t n_causal, int64_t S, int64_t H, const int32_t* bid, const int32_t* meta,
+                               const float* rope, void* stream) {
+  int rc = attn_check(qkv, nseq, n_causal, S, H, meta);
+  if (rc) return rc;
+  if (!out || !dout || !lse || !dsum || !dqkv8 || !qscale || (fmt != 0 && fmt != 1)) return -1;
+  if (n_causal < nseq && !bid) return -3;
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(dout) & 15) ||
+      (reinterpret_cast<uintptr_t>(dqkv8) & 15) || (ld8 % 16) || ld8 < 3 * H * kHd)
+    return -4;
+  // only the persistent S <= 256 kernel writes the 8-bit form
+  if (S > kSeqMax || !(attn_path() == 0 || attn_path() == 5)) return -20;
+  Q8Out q8;
+  q8.q = reinterpret_cast<uint8_t*>(dqkv8);
+  q8.ldq = ld8;
+  q8.fmt = fmt;
+  q8.qscale = qscale;
+  q8.amax = amax;
+  return launch_attn_bwd_pst(qkv, out, dout, lse, dsum, nullptr, nseq, n_causal, S, H, bid, meta, rope,
+                             reinterpret_cast<cudaStream_t>(stream), &q8);
 }
 
 extern "C" int cdk_attn_bwd_ws(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,

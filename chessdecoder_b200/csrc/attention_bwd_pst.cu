@@ -75,6 +75,7 @@ struct Args {
   const int32_t* first;   // [nseq - n_causal, S]
   const int32_t* q_lo;    // [nseq - n_causal][2 * nt64]; + nt64: lowest first row per 64-row tile
   const float* rope;      // [>= S, 32, 2] (cos, sin) or null
+  Q8Out q8;               // q8.q set: dq|dk|dv written as 8-bit (fp8 recipe) instead of bf16
   int S, H, n_causal, nt64, n_items;
 };
 
@@ -149,9 +150,7 @@ __device__ __forceinline__ Rope16 load_rope16(const float* rope, int pos, int c0
 
 // 16 consecutive dims of a dX row: value * scale, then the inverse RoPE
 // rotation given by rp (the identity for V or without RoPE), packed to bf16.
-__device__ __forceinline__ void rotate_pack16(const uint32_t (&v)[16], float scale, const Rope16& rp,
-                                              uint32_t (&w)[8]) {
-  float f[16];
+__device__ __forceinline__ void rotate16(const uint32_t (&v)[16], float scale, const Rope16& rp, float (&f)[16]) {
   #pragma unroll
   for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]) * scale;
   #pragma unroll
@@ -165,6 +164,11 @@ __device__ __forceinline__ void rotate_pack16(const uint32_t (&v)[16], float sca
     f[4 * p + 2] = x0 * t.z + x1 * t.w;
     f[4 * p + 3] = x1 * t.z - x0 * t.w;
   }
+}
+__device__ __forceinline__ void rotate_pack16(const uint32_t (&v)[16], float scale, const Rope16& rp,
+                                              uint32_t (&w)[8]) {
+  float f[16];
+  rotate16(v, scale, rp, f);
   #pragma unroll
   for (int q = 0; q < 8; ++q) w[q] = pack_bf16(f[2 * q], f[2 * q + 1]);
 }
@@ -197,6 +201,28 @@ __device__ __forceinline__ void quad_store(uint8_t* stg, int bar_id, int lane, i
     }
   }
   named_bar_sync(bar_id, 128);  // the staging rows are free again
+}
+
+// The same block written as 8-bit values q = saturate(v * qs) (64-byte rows:
+// each of the quadrant's 4 warps holds one 16-byte chunk of every row, chunks
+// XOR-swizzled by the row); returns max |v| of this thread's 16 values.
+__device__ __forceinline__ float quad_store_q8(uint8_t* stg, int bar_id, int lane, int g4, const float (&f)[16],
+                                               float qs, int fmt, uint8_t* row0, long long pitch, int rows_valid) {
+  uint32_t w[4];
+  float m = 0.f;
+  #pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    w[q] = q8_pack4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3], qs, fmt);
+    m = abs_max4(m, f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+  }
+  *reinterpret_cast<uint4*>(stg + lane * 64 + ((g4 ^ (lane & 3)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+  named_bar_sync(bar_id, 128);
+  const int rr = g4 * 8 + (lane >> 2), c = lane & 3;
+  if (rr < rows_valid)
+    *reinterpret_cast<uint4*>(row0 + (long long)rr * pitch + c * 16) =
+        *reinterpret_cast<const uint4*>(stg + rr * 64 + ((c ^ (rr & 3)) << 4));
+  named_bar_sync(bar_id, 128);
+  return m;
 }
 
 // P^T and dS^T of one thread's 16 queries: P = exp2(S * scale - L),
@@ -234,6 +260,7 @@ __device__ __forceinline__ void ew16(const uint32_t (&su)[16], const uint32_t (&
   }
 }
 
+template <bool Q8>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_pst_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo,
                         const Args a) {
@@ -462,9 +489,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     // tile (or of an item) the warps go on with the next sub-unit, whose MMA-A
     // is already in flight, while that tile's last products retire.
     int kv_pend = -1, kv_j0 = 0, kv_h = 0;  // pending dV / dK store: block index, first key row, head
-    __nv_bfloat16* kv_rows = nullptr;
+    long long kv_row0 = 0;  // global row of the pending key tile's sequence start
     int dq_pend = -1, dq_h = 0;             // pending dQ store: item index, head
-    __nv_bfloat16* dq_rows = nullptr;
+    long long dq_row0 = 0;
+    // one 32-row x 64-dim block of dQ / dK / dV (rows from global row row0, columns
+    // [col, col + 64) of q|k|v): bf16, or 8-bit with its amax (fp8 recipe)
+    float q8m = 0.f;
+    auto emit = [&](const uint32_t (&v)[16], float scale, const Rope16& rp, long long row0, int col, int nvalid) {
+      const bool mine = lane < nvalid;  // this thread's own row (row0 + lane) lies inside the sequence
+      if constexpr (Q8) {
+        float f[16];
+        rotate16(v, scale, rp, f);
+        const float qm = quad_store_q8(stg, qbar, lane, g4, f, *a.q8.qscale, a.q8.fmt,
+                                       a.q8.q + row0 * a.q8.ldq + col, a.q8.ldq, nvalid);
+        if (mine) q8m = fmaxf(q8m, qm);
+      } else {
+        uint32_t w[8];
+        rotate_pack16(v, scale, rp, w);
+        quad_store(stg, qbar, lane, g4, w, a.dqkv + row0 * 3 * E + col, 3 * E, nvalid);
+      }
+    };
     auto kv_epilogue = [&]() {
       // dV, dK of the key tile complete: this thread stores dims [16 g, 16 g + 16) of its key row
       const int j = kv_j0 + r;
@@ -480,12 +524,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&sm.kvfree);
       const int jq = kv_j0 + quad * 32;  // first key row of this quadrant
       const int nvalid = min(max(S - jq, 0), 32);
-      __nv_bfloat16* row0 = kv_rows + (long long)jq * 3 * E + kv_h * kHd;
-      uint32_t w[8];
-      rotate_pack16(kv, 0.125f, rk, w);
-      quad_store(stg, qbar, lane, g4, w, row0 + E, 3 * E, nvalid);
-      rotate_pack16(vv, 1.f, load_rope16(nullptr, 0, 0, false), w);
-      quad_store(stg, qbar, lane, g4, w, row0 + 2 * E, 3 * E, nvalid);
+      emit(kv, 0.125f, rk, kv_row0 + jq, E + kv_h * kHd, nvalid);
+      emit(vv, 1.f, load_rope16(nullptr, 0, 0, false), kv_row0 + jq, 2 * E + kv_h * kHd, nvalid);
       kv_pend = -1;
     };
     auto dq_epilogue = [&]() {
@@ -501,15 +541,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (nkt > 1) tmem_wait_ld_dep16(q1v);
       tc_fence_before();
       mbar_arrive(&sm.dqfree);
-      uint32_t w[8];
-      rotate_pack16(q0v, 0.125f, r0, w);
-      quad_store(stg, qbar, lane, g4, w, dq_rows + (long long)(quad * 32) * 3 * E + dq_h * kHd, 3 * E,
-                 min(max(S - quad * 32, 0), 32));
-      if (nkt > 1) {
-        rotate_pack16(q1v, 0.125f, r1, w);
-        quad_store(stg, qbar, lane, g4, w, dq_rows + (long long)(128 + quad * 32) * 3 * E + dq_h * kHd, 3 * E,
-                   min(max(S - 128 - quad * 32, 0), 32));
-      }
+      emit(q0v, 0.125f, r0, dq_row0 + quad * 32, dq_h * kHd, min(max(S - quad * 32, 0), 32));
+      if (nkt > 1) emit(q1v, 0.125f, r1, dq_row0 + 128 + quad * 32, dq_h * kHd, min(max(S - 128 - quad * 32, 0), 32));
       dq_pend = -1;
     };
     for (int k = 0; k < n_local; ++k) {
@@ -521,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&sm.mfull[m], (k >> 1) & 1, abort_flag);
       const Meta& mt = sm.meta[m];
       const bool contig = mt.contig != 0;
-      __nv_bfloat16* rowbase = a.dqkv + (long long)(seq * S) * 3 * E;
+      const long long rowbase = (long long)seq * S;
       for (int u = 0; u < un.n; ++u, ++g) {
         const int kt = un.kt(u), qs = un.qs(u);
         const int b = g & 1, P = g >> 1, pb = P & 1;
@@ -588,16 +621,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           kv_pend = c++;
           kv_j0 = kt * 128;
           kv_h = h;
-          kv_rows = rowbase;
+          kv_row0 = rowbase;
         }
       }
       mbar_arrive(&sm.mempty[m]);
       dq_pend = k;
       dq_h = h;
-      dq_rows = rowbase;
+      dq_row0 = rowbase;
     }
     if (kv_pend >= 0) kv_epilogue();
     if (dq_pend >= 0) dq_epilogue();
+    if (Q8 && a.q8.amax) {
+      const float m = warp_max(q8m);
+      if (lane == 0 && m > 0.f) atomicMax(reinterpret_cast<int*>(a.q8.amax), __float_as_int(m));
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -616,7 +653,7 @@ int launch_attn_dsum(const void* out, const void* dout, float* dsum, int64_t T, 
 // Host launcher used by cdk_attn_bwd for S <= 256.
 int launch_attn_bwd_pst(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum,
                         void* dqkv, int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid,
-                        const int32_t* meta, const float* rope, cudaStream_t stream) {
+                        const int32_t* meta, const float* rope, cudaStream_t stream, const Q8Out* q8) {
   using namespace pstbwd;
   if (S > kMaxS || S <= 0) return -20;
   if (nseq * H > (int64_t)1 << 30) return -5;
@@ -629,6 +666,13 @@ int launch_attn_bwd_pst(const void* qkv, const void* out, const void* dout, cons
   a.lse = lse;
   a.dsum = dsum;
   a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv);
+  a.q8.q = nullptr;
+  a.q8.ldq = 0;
+  a.q8.fmt = 0;
+  a.q8.qscale = nullptr;
+  a.q8.amax = nullptr;
+  if (q8 != nullptr) a.q8 = *q8;
+  if (a.q8.q == nullptr && dqkv == nullptr) return -1;
   const int64_t np = nseq - n_causal;
   const int nt64 = (int)((S + 63) / 64);
   a.bid = bid;
@@ -646,20 +690,23 @@ int launch_attn_bwd_pst(const void* qkv, const void* out, const void* dout, cons
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return -24;
   if (sm_count[dev] == 0) {
-    cudaError_t e = cudaFuncSetAttribute(attn_bwd_pst_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return (int)e;
-    // tcgen05.alloc blocks until columns are free: one 512-column CTA per SM
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_bwd_pst_kernel, kThreads, smem);
-    if (e != cudaSuccess) return (int)e;
-    if (per_sm != 1) return -22;
+    for (auto k : {attn_bwd_pst_kernel<false>, attn_bwd_pst_kernel<true>}) {
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return (int)e;
+      // tcgen05.alloc blocks until columns are free: one 512-column CTA per SM
+      int per_sm = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem);
+      if (e != cudaSuccess) return (int)e;
+      if (per_sm != 1) return -22;
+    }
     int sms = 0;
-    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return (int)e;
     sm_count[dev] = sms;
   }
   const int grid = (int)(nseq * H < sm_count[dev] ? nseq * H : sm_count[dev]);
-  attn_bwd_pst_kernel<<<grid, kThreads, smem, stream>>>(tq, tdo, a);
+  if (a.q8.q) attn_bwd_pst_kernel<true><<<grid, kThreads, smem, stream>>>(tq, tdo, a);
+  else attn_bwd_pst_kernel<false><<<grid, kThreads, smem, stream>>>(tq, tdo, a);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : (int)e;
 }

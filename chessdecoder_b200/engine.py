@@ -761,12 +761,18 @@ class Backbone:
                        fp8=self._f8(i, "o", "g", E5, "w", E4))
                 K.gemm(g8, s.aoT, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wo"],
                        fp8=self._f8(i, "o", "g", E5, "x", E4))
-            K.attn_bwd(s.qkv, s.ao, dao, s.lse, dsum, dqkv, nseq, n_causal, S, H, bid32, meta, rope=rope)
+            fq = f8.fused(f8.site(i, "qkv", "g"), E5, T, 3 * E) if f8 is not None else None
+            if fq is not None and K.attn_bwd_q8(s.qkv, s.ao, dao, s.lse, dsum, fq[1], nseq, n_causal, S, H, bid32,
+                                               meta, rope=rope):
+                gqkv8 = fq[0]  # the attention backward wrote the e5m2 dY of the q|k|v projection itself
+            else:
+                gqkv8 = None
+                K.attn_bwd(s.qkv, s.ao, dao, s.lse, dsum, dqkv, nseq, n_causal, S, H, bid32, meta, rope=rope)
             if f8 is None:
                 K.gemm(dqkv, w["wqkv"], b_mn=True, kind=K.EPI_STORE_BF16, out=dn)
                 K.gemm(dqkv, s.n1, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wqkv"])
             else:
-                g8 = f8.cast(dqkv, f8.site(i, "qkv", "g"), E5)
+                g8 = gqkv8 if gqkv8 is not None else f8.cast(dqkv, f8.site(i, "qkv", "g"), E5)
                 K.gemm(g8, f8.weights[(i, "qkv")], b_mn=True, kind=K.EPI_STORE_BF16, out=dn,
                        fp8=self._f8(i, "qkv", "g", E5, "w", E4))
                 K.gemm(g8, s.n1T, a_mn=True, b_mn=True, kind=K.EPI_ATOMIC_F32, out=g["wqkv"],

@@ -286,6 +286,21 @@ def attn_bwd(qkv, out, dout, lse, dsum, dqkv, nseq, n_causal, S, H, bid32=None, 
     _count(2)
 
 
+def attn_bwd_q8(qkv, out, dout, lse, dsum, q8, nseq, n_causal, S, H, bid32=None, meta=None, rope=None) -> bool:
+    """The backward with dq|dk|dv written as 8-bit values: q8 = (out8, fmt,
+    qscale, amax).  False (nothing launched) where only the bf16 form exists
+    (S > 256, or a non-default kernel path); the caller then uses attn_bwd."""
+    _need_cuda(qkv, out, dout, lse, dsum)
+    o8, fmt, qs, amax = q8
+    rc = lib().cdk_attn_bwd_q8(_p(qkv), _p(out), _p(dout), _p(lse), _p(dsum), _p(o8), o8.stride(0), fmt, _p(qs),
+                               _p(amax), nseq, n_causal, S, H, _p(bid32), _p(meta), _p(rope), _stream())
+    if rc == -20:
+        return False
+    _check(rc, "attn_bwd_q8")
+    _count(2)
+    return True
+
+
 # ---------------------------------------------------------------------------
 # RMSNorm
 # ---------------------------------------------------------------------------

@@ -164,6 +164,14 @@ int64_t cdk_attn_bwd_workspace(int64_t nseq, int64_t S, int64_t H);
 int cdk_attn_bwd_ws(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum, void* dqkv,
                     int64_t nseq, int64_t n_causal, int64_t S, int64_t H, const int32_t* bid, const int32_t* meta,
                     const float* rope, void* workspace, int64_t workspace_bytes, void* stream);
+/* cdk_attn_bwd_q8: the backward with dq|dk|dv written as 8-bit values
+ * (fp8 recipe, see cdk_rmsnorm_fwd_q8): dqkv8 [nseq*S, 3*H*64] with row pitch
+ * ld8 bytes, saturate(v * (*qscale)) in e4m3 (fmt 0) / e5m2 (fmt 1), amax =
+ * max(amax, max |v|).  S <= 256 on the default kernel path only; returns -20
+ * otherwise (the caller then uses cdk_attn_bwd_ws and a separate cast). */
+int cdk_attn_bwd_q8(const void* qkv, const void* out, const void* dout, const float* lse, float* dsum, void* dqkv8,
+                    int64_t ld8, int fmt, const float* qscale, float* amax, int64_t nseq, int64_t n_causal, int64_t S,
+                    int64_t H, const int32_t* bid, const int32_t* meta, const float* rope, void* stream);
 
 /* ---- RMSNorm (torchtune RMSNorm, eps 1e-6; reference restatement at
  *      chessdecoder/export/backbone_causal.py:61-64) ------------------------ */

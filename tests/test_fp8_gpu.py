@@ -299,3 +299,48 @@ def test_swiglu_bwd_fused_8bit_output(K):
     # the bf16 form of the same kernel agrees with the 8-bit one to bf16 / e5m2 rounding
     assert ((dgu.float() - deq).abs() <= 0.13 * dgu.float().abs() + 1e-6).float().mean().item() > 0.999
     assert K.get_error() == 0
+
+
+@pytest.mark.parametrize("S", [200, 256, 320])
+def test_attention_backward_fused_8bit_output(K, S):
+    """The persistent backward writing dq|dk|dv as e5m2 (fp8 recipe): equal to
+    the cast of the bf16 form up to the double rounding, amax its max |.|;
+    S > 256 has no 8-bit form (False, nothing launched)."""
+    g = torch.Generator(device=DEV).manual_seed(S)
+    nseq, ncaus, H = 6, 3, 4
+    E = H * 64
+    qkv = (torch.randn(nseq * S, 3 * E, generator=g, device=DEV) * 0.8).to(torch.bfloat16)
+    bid = (torch.arange(S, device=DEV) + 1000).repeat(nseq - ncaus, 1)
+    bid[:, 10:78] = 0
+    bid[:, 81:149] = 1
+    bid32 = bid.to(torch.int32).contiguous()
+    meta = K.attn_meta(bid32, S)
+    out = torch.empty(nseq * S, E, device=DEV, dtype=torch.bfloat16)
+    lse = torch.empty(nseq * H * S, device=DEV)
+    K.attn_fwd(qkv, out, lse, nseq, ncaus, S, H, bid32, meta)
+    dout = torch.randn(nseq * S, E, generator=g, device=DEV).to(torch.bfloat16)
+    dsum = torch.empty(nseq * H * S, device=DEV)
+    dqkv = torch.empty_like(qkv)
+    K.attn_bwd(qkv, out, dout, lse, dsum, dqkv, nseq, ncaus, S, H, bid32, meta)
+    qs = torch.tensor([1024.0], device=DEV)
+    amax = torch.zeros(1, device=DEV)
+    d8 = torch.empty(nseq * S, 3 * E, device=DEV, dtype=torch.float8_e5m2)
+    done = K.attn_bwd_q8(qkv, out, dout, lse, dsum, (d8, 1, qs, amax), nseq, ncaus, S, H, bid32, meta)
+    torch.cuda.synchronize()
+    if S > 256:
+        assert not done
+        return
+    assert done
+    ref = dqkv.float()
+    # the kernel rounds its fp32 values to e5m2 once; the reference rounds the bf16
+    # form again: the two differ only where a value sits within a bf16 step of an
+    # e5m2 rounding boundary, and then by one code
+    got, want = d8.view(torch.uint8), ref_cast(ref, qs, 1).view(torch.uint8)
+    exact = (got == want).float().mean().item()
+    assert exact > 0.97, exact
+    diff = (got.int() & 0x7F) - (want.int() & 0x7F)
+    assert int(diff.abs().max()) <= 1
+    deq = d8.float() / 1024.0
+    assert ((deq - ref).abs() <= 0.13 * ref.abs() + 1e-6).float().mean().item() > 0.999
+    assert abs(float(amax) - float(ref.abs().max())) <= 1e-2 * float(ref.abs().max())
+    assert K.get_error() == 0
