@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp runs the issue loop; one elected lane issues (uniform operands)
       const uint32_t id_s = make_idesc_bf16(kBQ, kBK, false, false);
       const uint32_t id_o = make_idesc_bf16(kBQ, kHd, false, true);
       const uint32_t qa = smem_u32(sm.Q);
@@ -150,9 +150,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const uint32_t kb = smem_u32(sm.K[st]);
           #pragma unroll
           for (int kk = 0; kk < kHd / 16; ++kk)
-            umma_f16(tmem + sb * kBK, make_sdesc(qa + kk * 32, 16, 1024), make_sdesc(kb + kk * 32, 16, 1024), id_s,
+            umma_f16_w(tmem + sb * kBK, make_sdesc(qa + kk * 32, 16, 1024), make_sdesc(kb + kk * 32, 16, 1024), id_s,
                      kk > 0 ? 1u : 0u);
-          tc_commit(&sm.bar_s[sb]);
+          tc_commit_w(&sm.bar_s[sb]);
         }
         if (j >= 1) {
           const int pj = j - 1, pbuf = pj & 1, st = pj % kStages;
@@ -162,10 +162,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const uint32_t vb = smem_u32(sm.V[st]);
           #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_f16(tmem + 256, make_sdesc(pb + (kk >> 2) * (128 * 128) + (kk & 3) * 32, 16, 1024),
+            umma_f16_w(tmem + 256, make_sdesc(pb + (kk >> 2) * (128 * 128) + (kk & 3) * 32, 16, 1024),
                      make_sdesc(vb + kk * 16 * 128, 8192, 1024), id_o, (pj > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(&sm.bar_o);
-          tc_commit(&sm.bar_empty[st]);
+          tc_commit_w(&sm.bar_o);
+          tc_commit_w(&sm.bar_empty[st]);
         }
       }
     }
@@ -429,7 +429,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp runs the issue loop; one elected lane issues (uniform operands)
       const uint32_t kb = smem_u32(sm.K), vb = smem_u32(sm.V);
       const uint32_t id_s = make_idesc_bf16(128, 64, false, false);   // N = 64 queries
       const uint32_t id_kn = make_idesc_bf16(128, kHd, false, true);  // dV, dK: B read MN-major
@@ -442,12 +442,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint32_t qb = smem_u32(sm.Q[st]), ob = smem_u32(sm.dO[st]);
         #pragma unroll
         for (int kk = 0; kk < kHd / 16; ++kk) {
-          umma_f16(tmem + b * 128, make_sdesc(kb + kk * 32, 16, 1024), make_sdesc(qb + kk * 32, 16, 1024), id_s,
+          umma_f16_w(tmem + b * 128, make_sdesc(kb + kk * 32, 16, 1024), make_sdesc(qb + kk * 32, 16, 1024), id_s,
                    kk > 0 ? 1u : 0u);
-          umma_f16(tmem + b * 128 + 64, make_sdesc(vb + kk * 32, 16, 1024), make_sdesc(ob + kk * 32, 16, 1024),
+          umma_f16_w(tmem + b * 128 + 64, make_sdesc(vb + kk * 32, 16, 1024), make_sdesc(ob + kk * 32, 16, 1024),
                    id_s, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&sm.bar_sa[b]);
+        tc_commit_w(&sm.bar_sa[b]);
       };
       if (ns > 0) issue_a(0);
       if (ns > 1) issue_a(1);
@@ -459,21 +459,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {  // 64 queries: A = P^T / dS^T columns of 16 queries in TMEM
           const uint32_t acc = (s > 0 || kk > 0) ? 1u : 0u;
-          umma_f16_ts(tmem + 256, tmem + 448 + kk * 8, make_sdesc(ob + kk * 2048, 8192, 1024), id_kn, acc);
-          umma_f16_ts(tmem + 320, tmem + 480 + kk * 8, make_sdesc(qb + kk * 2048, 8192, 1024), id_kn, acc);
+          umma_f16_ts_w(tmem + 256, tmem + 448 + kk * 8, make_sdesc(ob + kk * 2048, 8192, 1024), id_kn, acc);
+          umma_f16_ts_w(tmem + 320, tmem + 480 + kk * 8, make_sdesc(qb + kk * 2048, 8192, 1024), id_kn, acc);
         }
-        tc_commit(&sm.bar_b[b]);
-        tc_commit(&sm.bar_empty[st]);
+        tc_commit_w(&sm.bar_b[b]);
+        tc_commit_w(&sm.bar_empty[st]);
         if (hh == 1) {
           // dQ_t = dS K: A = the tile's dS^T pair read MN-major (queries 0-63 | 64-127)
           if (t >= 1) mbar_wait(&sm.bar_dqfree, (t - 1) & 1, abort_flag);
           tc_fence_after();
           const uint32_t pair = smem_u32(sm.dST[t & 1][0]);
-          #pragma unroll 1
+          #pragma unroll
           for (int kk = 0; kk < 8; ++kk)  // 128 keys
-            umma_f16(tmem + 384, make_sdesc(pair + kk * 2048, 16384, 1024), make_sdesc(kb + kk * 2048, 8192, 1024),
+            umma_f16_w(tmem + 384, make_sdesc(pair + kk * 2048, 16384, 1024), make_sdesc(kb + kk * 2048, 8192, 1024),
                      id_nn, kk > 0 ? 1u : 0u);
-          tc_commit(&sm.bar_dq);
+          tc_commit_w(&sm.bar_dq);
         }
         if (s + 2 < ns) issue_a(s + 2);
       }
