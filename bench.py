@@ -972,7 +972,8 @@ def main():
         if args.detail:
             line["gemm_by_shape"] = gemm_stats.get("by_shape")
             line["host_enqueue_ms_per_step"] = host_enqueue_ms
-            line["ops_ms_per_step"] = {k: [n // args.steps, ms / args.steps] for k, (n, ms) in op_stats.items()}
+            # collected over the GEMM-timer pass (gemm_steps steps), as the GEMM breakdown
+            line["ops_ms_per_step"] = {k: [n // gemm_steps, ms / gemm_steps] for k, (n, ms) in op_stats.items()}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
