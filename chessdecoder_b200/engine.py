@@ -100,15 +100,17 @@ def param_specs(cfg: ModelConfig):
     specs.append(("norm.scale", (E,)))
     X = cfg.moe_experts
     for i in reversed(range(L)):
+        # per layer the MLP block (its gradients are final first) then the attention block
         p = f"layers.{i}."
-        specs += [(p + "attn.q_proj.weight", (E, E)), (p + "attn.k_proj.weight", (E, E)),
-                  (p + "attn.v_proj.weight", (E, E)), (p + "attn.output_proj.weight", (E, E))]
         if X:
             specs += [(p + "mlp.router.weight", (X, E)), (p + "mlp.experts.w13", (X, 2 * F, E)),
                       (p + "mlp.experts.w2", (X, E, F))]
         else:
             specs += [(p + "mlp.w1.weight", (F, E)), (p + "mlp.w3.weight", (F, E)), (p + "mlp.w2.weight", (E, F))]
-        specs += [(p + "sa_norm.scale", (E,)), (p + "mlp_norm.scale", (E,))]
+        specs += [(p + "mlp_norm.scale", (E,))]
+        specs += [(p + "attn.q_proj.weight", (E, E)), (p + "attn.k_proj.weight", (E, E)),
+                  (p + "attn.v_proj.weight", (E, E)), (p + "attn.output_proj.weight", (E, E))]
+        specs += [(p + "sa_norm.scale", (E,))]
     specs += [("fourier_encoder.frequencies", (1, nf)), ("fourier_encoder.proj.weight", (E, 2 * nf)),
               ("fourier_encoder.proj.bias", (E,)), ("tok_embedding.weight", (cfg.vocab_size, E))]
     return specs
@@ -269,12 +271,21 @@ class ParamStore:
         self.step = steps.pop() if steps else 0
         return sd["param_groups"][0]
 
-    def layer_grad_span(self, i: int):
-        """[start, end) of layer i's gradients in the flat buffer."""
+    def layer_grad_span(self, i: int, part: Optional[str] = None):
+        """[start, end) of layer i's gradients in the flat buffer; part "mlp"
+        (the MLP block and its norm, final first in the backward) or "attn"
+        (the attention block and its norm)."""
         p = f"layers.{i}."
-        s = self.offsets[p + "attn.q_proj.weight"][0]
-        o, _, n = self.offsets[p + "mlp_norm.scale"]
-        return s, (o + n + _ALIGN - 1) // _ALIGN * _ALIGN
+        first_mlp = p + ("mlp.router.weight" if self.cfg.moe_experts else "mlp.w1.weight")
+        s = self.offsets[first_mlp][0]
+        m = self.offsets[p + "attn.q_proj.weight"][0]
+        o, _, n = self.offsets[p + "sa_norm.scale"]
+        e = (o + n + _ALIGN - 1) // _ALIGN * _ALIGN
+        if part == "mlp":
+            return s, m
+        if part == "attn":
+            return m, e
+        return s, e
 
 
 def init_reference_weights(cfg: ModelConfig, seed: int = 0) -> dict:
@@ -751,6 +762,8 @@ class Backbone:
                 go_8 = fq[0] if fq is not None else None
                 K.rmsnorm_bwd(dn, s.h1, w["s2"], s.r2, dx=dh1, dx16=None if fq else dh1_16, dscale=g["s2"], dres=dh,
                               q8=fq[1] if fq else None)
+            if on_layer_done is not None:
+                on_layer_done(("mlp", i))  # the MLP block's gradients (and its norm's) are final
             # attention block
             if f8 is None:
                 K.gemm(dh1_16, w["wo"], b_mn=True, kind=K.EPI_STORE_BF16, out=dao)
