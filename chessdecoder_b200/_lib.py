@@ -42,6 +42,7 @@ SIGNATURES = {
     "cdk_get_error": (_int, [C.POINTER(C.c_int), _int]),
     "cdk_gemm_bf16": (_int, [_vp, _i64, _int, _vp, _i64, _int, _i64, _i64, _i64, C.POINTER(CdkGemmEpilogue), _int,
                              _vp]),
+    "cdk_gemm_pair_clusters": (_int, []),
     "cdk_gemm_fp8": (_int, [_vp, _i64, _int, _int, _vp, _i64, _int, _int, _i64, _i64, _i64, _vp, _vp,
                             C.POINTER(CdkGemmEpilogue), _int, _vp]),
     "cdk_fp8_cast": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _int, _vp, _i64, _vp, _i64, _vp, _vp]),

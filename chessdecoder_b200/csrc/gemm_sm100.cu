@@ -49,6 +49,15 @@ struct GemmCfg {
   static constexpr int kStagesTE = BN == 256 ? 3 : 5;
   static constexpr int kSmemBytesTE = kStagesTE * kStageBytes + 1024 + kTeSlots * kTeSlotBytes + kBarrierBytes;
   static constexpr int kSmemBytesTE2 = kStages * kStageBytes + 1024 + kTe2Slots * kTe2SlotBytes + kBarrierBytes;
+  // CTA-pair form (BN = 256): each CTA holds its 128 A rows and half of the B
+  // rows of a stage, so a stage is 32 KB and the ring six deep (five with the
+  // TMA-fed epilogue's 64 KB of slots)
+  static constexpr int kStageBytesPair = kBytesA + kBytesB / 2;
+  static constexpr int stages_pair(int tem) { return tem == 1 ? 5 : 6; }
+  static constexpr int smem_pair(int tem) {
+    return stages_pair(tem) * kStageBytesPair + 1024 + (tem == 1 ? kTeSlots * kTeSlotBytes : kTe2Slots * kTe2SlotBytes) +
+           kBarrierBytes;
+  }
 };
 
 struct EpiDev {
@@ -75,10 +84,19 @@ struct GemmParams {
   int dual;      // SWIGLU: B tile = rows [n0, n0+BN/2) and [n0+b_off, ...)
   int b_off;
   uint32_t idesc_f8;           // fp8 instantiations: kind::f8f6f4 descriptor (operand formats)
+  int pair;                    // 1: clusters of 2 CTAs issuing 2-SM (M=256) MMAs; m_tiles counts 256-row tiles
   const float* scale_inv_a;    // fp8: dequantisation factors (device scalars), else null
   const float* scale_inv_b;
   EpiDev epi;
 };
+
+// Unit walk of a CTA: one unit per CTA pair in the 2-SM form (both CTAs walk
+// the same units), each CTA's own 128-row tile of the unit's 256 rows.
+__device__ __forceinline__ int unit_start(const GemmParams& p) { return p.pair ? (int)blockIdx.x >> 1 : (int)blockIdx.x; }
+__device__ __forceinline__ int unit_stride(const GemmParams& p) { return p.pair ? (int)gridDim.x >> 1 : (int)gridDim.x; }
+__device__ __forceinline__ int tile_row0(const GemmParams& p, int mt) {
+  return (p.pair ? mt * 2 + (int)cluster_ctarank() : mt) * kBM;
+}
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
 
@@ -556,18 +574,18 @@ __device__ __forceinline__ void te_tile(TeCursor& c, const GemmParams& p) {
   const int units = p.m_tiles * p.n_tiles;
   while (c.u < units) {
     const int mt = c.u / p.n_tiles, nt = c.u - mt * p.n_tiles;
-    c.m0 = mt * kBM;
+    c.m0 = tile_row0(p, mt);
     c.n0 = nt * BN;
     c.nch = min(BN, p.N - c.n0) / te_cols(p);
     c.j = 0;
     if (c.nch > 0) return;
-    c.u += gridDim.x;
+    c.u += unit_stride(p);
   }
 }
 template <int BN>
 __device__ __forceinline__ void te_next(TeCursor& c, const GemmParams& p) {
   if (++c.j == c.nch) {
-    c.u += gridDim.x;
+    c.u += unit_stride(p);
     te_tile<BN>(c, p);
   }
 }
@@ -585,7 +603,7 @@ __device__ void te_stream(const CUtensorMap* te_in, const CUtensorMap* te_out, c
   const int sbytes = dsw ? 32768 : 16384;
   const int nslots = area / sbytes;
   const int w = te_cols(p);
-  TeCursor L{(int)blockIdx.x, 0, 0, 0, 0};
+  TeCursor L{unit_start(p), 0, 0, 0, 0};
   te_tile<BN>(L, p);
   TeCursor S = L;
   int kl = 0, ks = 0;
@@ -705,10 +723,10 @@ __device__ void te2_stream(const CUtensorMap* map_a, const CUtensorMap* map_b, c
   const int n_step = sw ? BN / 2 : BN;
   const int box = red ? 32 : 64;
   int k = 0;
-  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+  for (int u = unit_start(p); u < units; u += unit_stride(p)) {
     const int rem = u % tiles_mn;
     const int mt = rem / p.n_tiles, nt = rem - mt * p.n_tiles;
-    const int m0 = mt * kBM, n0 = nt * n_step;
+    const int m0 = tile_row0(p, mt), n0 = nt * n_step;
     const int nq = min(n_step, p.N - n0) / box;
     for (int j = 0; j < nq; ++j) {
       for (int o = 0; o < (sw ? 3 : 1); ++o, ++k) {
@@ -833,7 +851,11 @@ __device__ __forceinline__ void epi_te2_tile(const EpiDev& e, const GemmParams& 
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, int TEM = 0>
+// PAIR: clusters of two CTAs; the even CTA issues M=256 MMAs over both CTAs'
+// shared memory (its 128 A rows and B rows [n0, n0+BN/2), the odd CTA's 128 A
+// rows and B rows [n0+BN/2, n0+BN)), and each CTA's TMEM receives its own 128
+// accumulator rows, so the epilogue warps are the same in both.
+template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, int TEM = 0, bool PAIR = false>
 __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap te_in, const __grid_constant__ CUtensorMap te_out,
@@ -842,7 +864,10 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   // TEM 1: TMA-fed form with 64 KB of slots (3-stage ring at BN=256); TEM 4: the
   // same for the residual add with 2 x 16 KB slots and the full ring
   constexpr bool TE = TEM == 1 || TEM == 4;
-  constexpr int kStages = TEM == 1 ? Cfg::kStagesTE : Cfg::kStages;
+  static_assert(!PAIR || (BN == 256 && !A_MN && !F8 && (TEM == 1 || TEM == 2 || TEM == 4)), "pair form");
+  constexpr int kStages = PAIR ? Cfg::stages_pair(TEM) : TEM == 1 ? Cfg::kStagesTE : Cfg::kStages;
+  constexpr int kBytesB = PAIR ? Cfg::kBytesB / 2 : Cfg::kBytesB;
+  constexpr int kStageBytes = Cfg::kBytesA + kBytesB;
   constexpr bool TE2 = TEM == 2 || TEM == 3;  // store-only / reduce-add forms share the slots and the stream
   constexpr int kSlotArea =
       TEM == 1 ? kTeSlots * kTeSlotBytes : TEM == 4 ? 32768 : TE2 ? kTe2Slots * kTe2SlotBytes : 0;
@@ -850,8 +875,8 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * Cfg::kBytesA;
-  uint8_t* te_slots = smem + kStages * Cfg::kStageBytes;  // TE: 8 x 8 KB / store-only: 2 x 16 KB, 1024-aligned
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * Cfg::kStageBytes + kSlotArea);
+  uint8_t* te_slots = smem + kStages * kStageBytes;  // TE: 8 x 8 KB / store-only: 2 x 16 KB, 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kSlotArea);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
@@ -872,7 +897,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 256);
+      mbar_init(&tempty[a], PAIR ? 512 : 256);  // pair: both CTAs' epilogue threads, on the even CTA's barrier
     }
     if constexpr (TE) {
       for (int a = 0; a < kSlotBars; ++a) {
@@ -894,13 +919,20 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
     prefetch_tmap(&tma_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, Cfg::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_holder, Cfg::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, Cfg::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's barriers are initialised before any signal reaches them
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
 
   const int tiles_mn = p.m_tiles * p.n_tiles;
   const int units = tiles_mn * p.splits;
@@ -910,19 +942,39 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      for (int u = unit_start(p); u < units; u += unit_stride(p)) {
         const int ks = u / tiles_mn;
         const int rem = u - ks * tiles_mn;
         const int mt = rem / p.n_tiles;
         const int nt = rem - mt * p.n_tiles;
-        const int m0 = mt * kBM, n0 = nt * n_step;
+        const int m0 = tile_row0(p, mt), n0 = nt * n_step;
         const int kt0 = ks * p.k_per_split;
         const int kt1 = min(kt0 + p.k_per_split, p.k_tiles);
         for (int kt = kt0; kt < kt1; ++kt) {
           mbar_wait(&empty[stage], phase ^ 1u, abort_flag);
-          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
           uint8_t* a_dst = sA + stage * Cfg::kBytesA;
-          uint8_t* b_dst = sB + stage * Cfg::kBytesB;
+          uint8_t* b_dst = sB + stage * kBytesB;
+          if constexpr (PAIR) {
+            // both CTAs' loads complete on the even CTA's barrier, which expects both
+            const uint32_t bar0 = mapa_shared(&full[stage], 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
+            const int k0 = kt * kBK;
+            tma_load_2d_pair(a_dst, &tma_a, bar0, k0, m0);
+            if constexpr (B_MN) {  // this CTA's BN/2 columns as 64-column groups of kBK k rows
+              #pragma unroll
+              for (int i = 0; i < BN / 128; ++i)
+                tma_load_2d_pair(b_dst + i * 8192, &tma_b, bar0, n0 + (int)rank * (BN / 2) + 64 * i, k0);
+            } else {
+              tma_load_2d_pair(b_dst, &tma_b, bar0, k0,
+                               p.dual ? n0 + (rank ? p.b_off : 0) : n0 + (int)rank * (BN / 2));
+            }
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
+          mbar_arrive_expect_tx(&full[stage], kStageBytes);
           const int k0 = kt * (F8 ? 2 * kBK : kBK);  // element coordinate of this 128-byte k block
           // MN-major operands arrive as 128-byte-wide MN groups (64 bf16 / 128 fp8
           // elements) of kRowsK k rows each
@@ -951,14 +1003,25 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
           }
         }
       }
+      if constexpr (PAIR) {
+        // the even CTA's MMAs read this CTA's stages: wait until the last use of
+        // each has been released before the CTA may leave
+        for (int i = 0; i < kStages; ++i) {
+          mbar_wait(&empty[stage], phase ^ 1u, abort_flag);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN, B_MN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(PAIR ? 2 * kBM : kBM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
-      for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      for (int u = unit_start(p); u < units; u += unit_stride(p), ++local) {
         const int ks = u / tiles_mn;
         const int kt0 = ks * p.k_per_split;
         const int kt1 = min(kt0 + p.k_per_split, p.k_tiles);
@@ -971,7 +1034,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
           mbar_wait(&full[stage], phase, abort_flag);
           tc_fence_after();
           const uint32_t a_base = smem_u32(sA + stage * Cfg::kBytesA);
-          const uint32_t b_base = smem_u32(sB + stage * Cfg::kBytesB);
+          const uint32_t b_base = smem_u32(sB + stage * kBytesB);
           #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             // MN-major: one MMA consumes 16 (bf16) / 32 (fp8) k rows of 128 B
@@ -981,15 +1044,18 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
             const uint64_t bd =
                 B_MN ? make_sdesc(b_base + kk * kKStep, kLbo, 1024) : make_sdesc(b_base + kk * 32, 16, 1024);
             if constexpr (F8) umma_f8(d_tmem, ad, bd, p.idesc_f8, (kt > kt0 || kk > 0) ? 1u : 0u);
+            else if constexpr (PAIR) umma_f16_pair(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
             else umma_f16(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit(&empty[stage]);
+          if constexpr (PAIR) tc_commit_pair(&empty[stage]);
+          else tc_commit(&empty[stage]);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        tc_commit(&tfull[acc]);
+        if constexpr (PAIR) tc_commit_pair(&tfull[acc]);
+        else tc_commit(&tfull[acc]);
       }
     }
   } else if (TEM && warp == 10) {
@@ -1005,30 +1071,30 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const EpiDev& e = p.epi;
-    uint32_t* stg = reinterpret_cast<uint32_t*>(smem + kStages * Cfg::kStageBytes + Cfg::kBarrierBytes) +
+    uint32_t* stg = reinterpret_cast<uint32_t*>(smem + kStages * kStageBytes + Cfg::kBarrierBytes) +
                     (warp - 2) * kStgWords;
     float sc = 1.f;
     if constexpr (F8) sc = *p.scale_inv_a * *p.scale_inv_b;
     int local = 0;
     int te_k = 0;  // TE: chunks of the CTA's earlier tiles
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+    for (int u = unit_start(p); u < units; u += unit_stride(p), ++local) {
       const int rem = u % tiles_mn;
       const int mt = rem / p.n_tiles;
       const int nt = rem - mt * p.n_tiles;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (e.kind == CDK_EPI_RESID_F32 || e.kind == CDK_EPI_ACCUM_F32 || e.kind == CDK_EPI_DSWIGLU) {
-        if (local == 0) epi_prefetch<BN>(e, p, mt * kBM + quad * 32 + lane, nt * BN, half);
-        const int un = u + gridDim.x;
+        if (local == 0) epi_prefetch<BN>(e, p, tile_row0(p, mt) + quad * 32 + lane, nt * BN, half);
+        const int un = u + unit_stride(p);
         if (un < units) {
           const int rn = un % tiles_mn;
           const int mtn = rn / p.n_tiles;
-          epi_prefetch<BN>(e, p, mtn * kBM + quad * 32 + lane, (rn - mtn * p.n_tiles) * BN, half);
+          epi_prefetch<BN>(e, p, tile_row0(p, mtn) + quad * 32 + lane, (rn - mtn * p.n_tiles) * BN, half);
         }
       }
       mbar_wait(&tfull[acc], acc_phase, abort_flag);
       tc_fence_after();
-      const int row = mt * kBM + quad * 32 + lane;
+      const int row = tile_row0(p, mt) + quad * 32 + lane;
       const bool row_ok = row < p.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
 
@@ -1041,7 +1107,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
         epi_te2_tile<BN>(e, p, tbase, quad * 32 + lane, row, sc, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN,
                          half, te_k, te_slots, sdone, sfull, abort_flag);
       } else if constexpr (VEC) {
-        const int row0 = mt * kBM + quad * 32;
+        const int row0 = tile_row0(p, mt) + quad * 32;
         if (row0 < p.M)
           epi_vec<BN, F8>(e, p, tbase, row0, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN, half, stg, lane,
                           sc);
@@ -1057,16 +1123,19 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
         default: break;
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(&tempty[acc], 0));
+      else mbar_arrive(&tempty[acc]);
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // neither CTA leaves while the pair's MMAs or signals may touch it
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    else tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
 }
 
@@ -1178,19 +1247,20 @@ static int num_sms(int dev) {
   return cache[dev];
 }
 
-template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, int TE = 0>
+template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, int TE = 0, bool PAIR = false>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& te_in,
                        const CUtensorMap& te_out, const GemmParams& p, int grid, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   constexpr int threads = TE ? kThreadsTE : kThreads;
-  constexpr int smem = TE == 1 ? Cfg::kSmemBytesTE : TE >= 2 ? Cfg::kSmemBytesTE2 : Cfg::kSmemBytes;
+  constexpr int smem =
+      PAIR ? Cfg::smem_pair(TE) : TE == 1 ? Cfg::kSmemBytesTE : TE >= 2 ? Cfg::kSmemBytesTE2 : Cfg::kSmemBytes;
   static_assert(TE != 4 || Cfg::kSmemBytesTE2 == Cfg::kStages * Cfg::kStageBytes + 1024 + 32768 + Cfg::kBarrierBytes,
                 "TEM 4 uses the store-only form's layout");
   static_assert(smem <= 232448, "shared memory");
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  auto kfn = gemm_bf16_kernel<BN, A_MN, B_MN, VEC, F8, TE>;
+  auto kfn = gemm_bf16_kernel<BN, A_MN, B_MN, VEC, F8, TE, PAIR>;
   if (dev < 64 && !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
@@ -1201,10 +1271,76 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     if (per_sm * Cfg::kTmemCols > 512) return -12;
     attr_set[dev] = true;
   }
-  kfn<<<grid, threads, smem, stream>>>(ta, tb, te_in, te_out, p);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? 0 : (int)e;
+  if constexpr (PAIR) {
+    if (!p.pair || (grid & 1)) return -14;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tb, te_in, te_out, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : (int)e;
+  } else {
+    if (p.pair) return -14;
+    kfn<<<grid, threads, smem, stream>>>(ta, tb, te_in, te_out, p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : (int)e;
+  }
 }
+
+// Clusters of two CTAs with the pair form's shared memory that can be resident
+// at once (0 if the query fails).
+static int pair_clusters(int dev) {
+  static int cache[64] = {0};
+  if (dev < 0 || dev >= 64) return 0;
+  if (!cache[dev]) {
+    using Cfg = GemmCfg<256>;
+    auto kfn = gemm_bf16_kernel<256, false, false, true, false, 2, true>;
+    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::smem_pair(2)) != cudaSuccess)
+      return 0;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(kThreadsTE);
+    cfg.dynamicSmemBytes = Cfg::smem_pair(2);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      return 0;
+    }
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+// CTA-pair form (K-major A): on by default for the store / RoPE and residual
+// epilogues; CDK_GEMM_PAIR=0 turns it off, CDK_GEMM_PAIR=all also uses it for
+// the SwiGLU forward and backward epilogues (which their epilogues, not their
+// operand traffic, limit: the pair form measured no faster there).
+static int pair_mode() {
+  static const int m = [] {
+    const char* v = getenv("CDK_GEMM_PAIR");
+    if (v && v[0] == '0') return 0;
+    if (v && std::strcmp(v, "all") == 0) return 2;
+    return 1;
+  }();
+  return m;
+}
+static bool pair_enabled() { return pair_mode() > 0; }
 
 template <int BN>
 static int dispatch_major(bool a_mn, bool b_mn, int te, const CUtensorMap& ta, const CUtensorMap& tb,
@@ -1226,6 +1362,13 @@ static int dispatch_major(bool a_mn, bool b_mn, int te, const CUtensorMap& ta, c
     if (a_mn && !b_mn) return launch_gemm<BN, true, false, false, true>(ta, tb, ti, to, p, grid, s);
     return launch_gemm<BN, true, true, false, true>(ta, tb, ti, to, p, grid, s);
   }
+  if constexpr (BN == 256) {
+    if (p.pair && te == 2 && !a_mn && !b_mn) return launch_gemm<256, false, false, true, false, 2, true>(ta, tb, ti, to, p, grid, s);
+    if (p.pair && te == 4 && !a_mn && !b_mn) return launch_gemm<256, false, false, true, false, 4, true>(ta, tb, ti, to, p, grid, s);
+    if (p.pair && te == 2 && !a_mn && b_mn) return launch_gemm<256, false, true, true, false, 2, true>(ta, tb, ti, to, p, grid, s);
+    if (p.pair && te == 1 && !a_mn && b_mn) return launch_gemm<256, false, true, true, false, 1, true>(ta, tb, ti, to, p, grid, s);
+  }
+  if (p.pair) return -14;
   // TMA-fed epilogue (residual add / SwiGLU backward; K-major A)
   if (te == 1 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, false, 1>(ta, tb, ti, to, p, grid, s);
   if (te == 4 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, false, 4>(ta, tb, ti, to, p, grid, s);
@@ -1338,6 +1481,7 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   p.k_tiles = (int)k_tiles;
   p.k_per_split = (int)k_per;
   p.dual = dual ? 1 : 0;
+  p.pair = 0;
   p.b_off = dual ? (int)N : 0;
   p.idesc_f8 = f8 ? make_idesc_f8(kBM, BN, a_fmt, b_fmt, a_mn != 0, b_mn != 0) : 0u;
   p.scale_inv_a = f8 ? sa : nullptr;
@@ -1410,12 +1554,26 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
                       CU_TENSOR_MAP_SWIZZLE_128B);
   }
 
-  const long long units = m_tiles * n_tiles * splits;
-  const int grid = (int)(units < sms ? units : sms);
+  long long units = m_tiles * n_tiles * splits;
+  int grid = (int)(units < sms ? units : sms);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // the residual add keeps the full mainloop ring (its mainloop is the slower half)
   // unless CDK_GEMM_TE_RESID_SLOTS=4 asks for the 4-slot / 3-stage layout
   const int tem = te ? (kind == CDK_EPI_RESID_F32 && !te_resid_deep() ? 4 : 1) : te2 ? 2 : te3 ? 3 : 0;
+  // CTA-pair form: 256-row units, B split between the two CTAs of a cluster
+  // (M a multiple of 256: no CTA of a pair holds a tile wholly below the last row)
+  // (B MN-major: the 64-column groups are loaded as before, half of them per CTA)
+  if (BN == 256 && !f8 && !a_mn && splits == 1 && (b_mn ? (tem == 1 || tem == 2) : (tem == 2 || tem == 4)) &&
+      M % (2 * kBM) == 0 && pair_enabled() && ((!dual && tem != 1) || pair_mode() == 2)) {
+    const int clusters = pair_clusters(dev);
+    if (clusters > 0) {
+      if (!b_mn && !make_tmap(&tb, b, K, dual ? 2 * N : N, ldb, kBK, BN / 2)) return -11;
+      p.pair = 1;
+      p.m_tiles = (int)((M + 2 * kBM - 1) / (2 * kBM));
+      units = (long long)p.m_tiles * n_tiles;
+      grid = 2 * (int)(units < clusters ? units : clusters);
+    }
+  }
   if (BN == 256) return dispatch_major<256>(a_mn, b_mn, tem, ta, tb, te_in, te_out, p, grid, s);
   return dispatch_major<128>(a_mn, b_mn, tem, ta, tb, te_in, te_out, p, grid, s);
 }
@@ -1424,6 +1582,12 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
 extern "C" int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, int64_t M,
                              int64_t N, int64_t K, const CdkGemmEpilogue* epi, int split_k, void* stream) {
   return cdk::gemm_impl(a, lda, a_mn, b, ldb, b_mn, M, N, K, epi, split_k, stream, false, 0, 0, nullptr, nullptr);
+}
+
+extern "C" int cdk_gemm_pair_clusters(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  return cdk::pair_enabled() ? cdk::pair_clusters(dev) : 0;
 }
 
 extern "C" int cdk_gemm_fp8(const void* a, int64_t lda, int a_mn, int a_fmt, const void* b, int64_t ldb, int b_mn,

@@ -137,6 +137,12 @@ FP8_E4M3, FP8_E5M2 = 0, 1
 FP8_MAX = {FP8_E4M3: 448.0, FP8_E5M2: 57344.0}
 
 
+def gemm_pair_clusters() -> int:
+    """Clusters of two CTAs the CTA-pair GEMM form keeps resident on the
+    current device (0: the form is off or unavailable)."""
+    return int(lib().cdk_gemm_pair_clusters())
+
+
 def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False, kind: int = EPI_STORE_BF16,
          out: torch.Tensor, bias=None, resid=None, out2=None, aux=None, half_n: int = 0, rope=None,
          seq_len: int = 0, rope_cols: int = 0, split_k: int = 0, M=None, N=None, K=None, fp8=None) -> torch.Tensor:

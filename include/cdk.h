@@ -74,6 +74,13 @@ typedef struct CdkGemmEpilogue {
 /* split_k: 0 = automatic (ATOMIC_F32 only), 1 = none, >1 = forced (ATOMIC_F32 only). */
 int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, int64_t M, int64_t N,
                   int64_t K, const CdkGemmEpilogue* epi, int split_k, void* stream);
+/* cdk_gemm_pair_clusters: clusters of two CTAs that the CTA-pair GEMM form
+ * (M = 256 MMAs over two SMs) keeps resident on the current device, or 0 when
+ * that form is off (environment CDK_GEMM_PAIR=0) or unavailable.  The pair
+ * form serves bf16 GEMMs with K-major A, M a multiple of 256, no split-K and a
+ * ROPE_BF16, STORE_BF16 or RESID_F32 (K-major B) epilogue; SWIGLU and DSWIGLU
+ * too with CDK_GEMM_PAIR=all.  Results equal the one-CTA form's bit for bit. */
+int cdk_gemm_pair_clusters(void);
 
 /* ---- fp8 (the fp8 training variant: e4m3 weights / activations, e5m2
  *      gradients, per-tensor delayed scaling; no counterpart in the reference,
