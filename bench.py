@@ -10,9 +10,10 @@ the backward (weak scaling: per-GPU batch fixed).
 
   value : tokens/s over all ranks, batch already in HBM, device time (CUDA
           events around K steps, max over ranks)
-  e2e   : the same step through the public API (TrainStep.step /
-          DataParallelStep.step) from pinned host batches, host index
-          preparation + host-to-device copies + the loss read-back inside the
+  e2e   : the same step through the public training loop (TrainStep.run /
+          DataParallelStep.run: batch i+1 prepared and enqueued while step i
+          runs) from pinned host batches, host index preparation +
+          host-to-device copies + every step's loss read-back inside the
           timed region
   --impl reference : the reference step on the host CPU (fp32 oracle port of
           chessdecoder/train/train.py:157-253; the reference's own model
@@ -853,9 +854,9 @@ def main():
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(args.steps):
-        losses = dp.step(host_pool[i % len(host_pool)])
-        lv = losses.cpu()  # device -> host read of the step's loss
+    # the public training loop: batch i+1 prepared and enqueued while step i
+    # runs; every step's losses are read back to the host (one step behind)
+    for i, lv in dp.run(host_pool[i % len(host_pool)] for i in range(args.steps)):
         d2h += lv.numel() * lv.element_size()
     e1.record()
     sync_all()

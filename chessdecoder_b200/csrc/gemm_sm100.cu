@@ -53,10 +53,13 @@ struct GemmCfg {
   // rows of a stage, so a stage is 32 KB and the ring six deep (five with the
   // TMA-fed epilogue's 64 KB of slots)
   static constexpr int kStageBytesPair = kBytesA + kBytesB / 2;
-  static constexpr int stages_pair(int tem) { return tem == 1 ? 5 : 6; }
-  static constexpr int smem_pair(int tem) {
-    return stages_pair(tem) * kStageBytesPair + 1024 + (tem == 1 ? kTeSlots * kTeSlotBytes : kTe2Slots * kTe2SlotBytes) +
-           kBarrierBytes;
+  // (pair = 2: the SwiGLU store form, three output boxes per 64 columns,
+  // trades a stage for two more 16 KB output slots)
+  static constexpr int stages_pair(int tem, int pair) { return tem == 1 || pair == 2 ? 5 : 6; }
+  static constexpr int te2_slots_pair(int pair) { return pair == 2 ? 4 : kTe2Slots; }
+  static constexpr int smem_pair(int tem, int pair) {
+    return stages_pair(tem, pair) * kStageBytesPair + 1024 +
+           (tem == 1 ? kTeSlots * kTeSlotBytes : te2_slots_pair(pair) * kTe2SlotBytes) + kBarrierBytes;
   }
 };
 
@@ -712,7 +715,7 @@ __device__ __forceinline__ void epi_te_tile(const EpiDev& e, uint32_t tbase, int
 // k % 2; the epilogue warps wait until the TMA store of box k - 2 has left the
 // slot (sfree), write their rows, and arrive on sdone; the streaming thread
 // stores the box and frees the slot once the store has read it.
-template <int BN>
+template <int BN, int NS = kTe2Slots>
 __device__ void te2_stream(const CUtensorMap* map_a, const CUtensorMap* map_b, const GemmParams& p, uint8_t* slots,
                            uint64_t* sdone, uint64_t* sfree, volatile int* abort_flag) {
   const bool sw = p.epi.kind == CDK_EPI_SWIGLU;
@@ -730,8 +733,8 @@ __device__ void te2_stream(const CUtensorMap* map_a, const CUtensorMap* map_b, c
     const int nq = min(n_step, p.N - n0) / box;
     for (int j = 0; j < nq; ++j) {
       for (int o = 0; o < (sw ? 3 : 1); ++o, ++k) {
-        const int slot = k & (kTe2Slots - 1);
-        mbar_wait(&sdone[slot], (k / kTe2Slots) & 1, abort_flag);
+        const int slot = k & (NS - 1);
+        mbar_wait(&sdone[slot], (k / NS) & 1, abort_flag);
         const uint8_t* src = slots + slot * kTe2SlotBytes;
         const int x = n0 + j * box;
         if (red) tma_reduce_add_2d(map_b, src, x, m0);
@@ -748,10 +751,12 @@ __device__ void te2_stream(const CUtensorMap* map_a, const CUtensorMap* map_b, c
 
 // One thread's 32 bf16 (64 bytes) of row r into box k: half h owns 16-byte
 // pieces 4h .. 4h+3 of the 128-byte row (128-byte swizzle: piece q at q ^ (r & 7)).
+template <int NS = kTe2Slots>
 __device__ __forceinline__ void te2_put(uint8_t* slots, uint64_t* sdone, uint64_t* sfree, int k, int r, int half,
                                         const uint32_t (&w)[16], volatile int* abort_flag) {
-  const int slot = k & (kTe2Slots - 1);
-  if (k >= kTe2Slots) mbar_wait(&sfree[slot], ((k / kTe2Slots) - 1) & 1, abort_flag);
+  static_assert((NS & (NS - 1)) == 0, "slots: a power of two");
+  const int slot = k & (NS - 1);
+  if (k >= NS) mbar_wait(&sfree[slot], ((k / NS) - 1) & 1, abort_flag);
   uint4* row = reinterpret_cast<uint4*>(slots + slot * kTe2SlotBytes + r * 128);
   #pragma unroll
   for (int q = 0; q < 4; ++q) row[(half * 4 + q) ^ (r & 7)] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
@@ -759,7 +764,7 @@ __device__ __forceinline__ void te2_put(uint8_t* slots, uint64_t* sdone, uint64_
   mbar_arrive(&sdone[slot]);
 }
 
-template <int BN>
+template <int BN, int NS = kTe2Slots>
 __device__ __forceinline__ void epi_te2_tile(const EpiDev& e, const GemmParams& p, uint32_t tbase, int r, int row, float sc,
                                              int n0, int half, int& k, uint8_t* slots, uint64_t* sdone,
                                              uint64_t* sfree, volatile int* abort_flag) {
@@ -777,7 +782,7 @@ __device__ __forceinline__ void epi_te2_tile(const EpiDev& e, const GemmParams& 
       #pragma unroll
       for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(__uint_as_float(a[i]) * sc);
       if (j + 1 < nb) tmem_ld_x16_nowait(tbase + (j + 1) * 32 + half * kC, a);
-      te2_put(slots, sdone, sfree, k++, r, half, w, abort_flag);
+      te2_put<NS>(slots, sdone, sfree, k++, r, half, w, abort_flag);
     }
     return;
   }
@@ -826,7 +831,7 @@ __device__ __forceinline__ void epi_te2_tile(const EpiDev& e, const GemmParams& 
       uint32_t w[16];
       #pragma unroll
       for (int i = 0; i < 16; ++i) w[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
-      te2_put(slots, sdone, sfree, k++, r, half, w, abort_flag);
+      te2_put<NS>(slots, sdone, sfree, k++, r, half, w, abort_flag);
     } else {
       uint32_t b0[kC], b1[kC];
       tmem_ld_x16_nowait(tbase + BN / 2 + c0, b0);
@@ -844,18 +849,19 @@ __device__ __forceinline__ void epi_te2_tile(const EpiDev& e, const GemmParams& 
         wu[i] = pack_bf16(u0, u1);
         wh[i] = pack_bf16(silu_f(g0) * u0, silu_f(g1) * u1);
       }
-      te2_put(slots, sdone, sfree, k++, r, half, wg, abort_flag);
-      te2_put(slots, sdone, sfree, k++, r, half, wu, abort_flag);
-      te2_put(slots, sdone, sfree, k++, r, half, wh, abort_flag);
+      te2_put<NS>(slots, sdone, sfree, k++, r, half, wg, abort_flag);
+      te2_put<NS>(slots, sdone, sfree, k++, r, half, wu, abort_flag);
+      te2_put<NS>(slots, sdone, sfree, k++, r, half, wh, abort_flag);
     }
   }
 }
 
-// PAIR: clusters of two CTAs; the even CTA issues M=256 MMAs over both CTAs'
-// shared memory (its 128 A rows and B rows [n0, n0+BN/2), the odd CTA's 128 A
-// rows and B rows [n0+BN/2, n0+BN)), and each CTA's TMEM receives its own 128
-// accumulator rows, so the epilogue warps are the same in both.
-template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, int TEM = 0, bool PAIR = false>
+// PAIR (1, or 2 with four output slots): clusters of two CTAs; the even CTA
+// issues M=256 MMAs over both CTAs' shared memory (its 128 A rows and B rows
+// [n0, n0+BN/2), the odd CTA's 128 A rows and B rows [n0+BN/2, n0+BN)), and
+// each CTA's TMEM receives its own 128 accumulator rows, so the epilogue warps
+// are the same in both.
+template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, int TEM = 0, int PAIR = 0>
 __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap te_in, const __grid_constant__ CUtensorMap te_out,
@@ -865,12 +871,14 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   // same for the residual add with 2 x 16 KB slots and the full ring
   constexpr bool TE = TEM == 1 || TEM == 4;
   static_assert(!PAIR || (BN == 256 && !A_MN && !F8 && (TEM == 1 || TEM == 2 || TEM == 4)), "pair form");
-  constexpr int kStages = PAIR ? Cfg::stages_pair(TEM) : TEM == 1 ? Cfg::kStagesTE : Cfg::kStages;
+  static_assert(PAIR != 2 || TEM == 2, "wide output slots: store-only form");
+  constexpr int kStages = PAIR ? Cfg::stages_pair(TEM, PAIR) : TEM == 1 ? Cfg::kStagesTE : Cfg::kStages;
   constexpr int kBytesB = PAIR ? Cfg::kBytesB / 2 : Cfg::kBytesB;
   constexpr int kStageBytes = Cfg::kBytesA + kBytesB;
   constexpr bool TE2 = TEM == 2 || TEM == 3;  // store-only / reduce-add forms share the slots and the stream
+  constexpr int kNs2 = PAIR && TEM == 2 ? Cfg::te2_slots_pair(PAIR) : kTe2Slots;  // store-only output slots
   constexpr int kSlotArea =
-      TEM == 1 ? kTeSlots * kTeSlotBytes : TEM == 4 ? 32768 : TE2 ? kTe2Slots * kTe2SlotBytes : 0;
+      TEM == 1 ? kTeSlots * kTeSlotBytes : TEM == 4 ? 32768 : TE2 ? kNs2 * kTe2SlotBytes : 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -880,7 +888,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
-  constexpr int kSlotBars = TEM == 1 ? kTeSlots : TEM == 4 ? 2 : TE2 ? kTe2Slots : 0;
+  constexpr int kSlotBars = TEM == 1 ? kTeSlots : TEM == 4 ? 2 : TE2 ? kNs2 : 0;
   uint64_t* sfull = tempty + 2;      // TE / store-only forms
   uint64_t* sdone = sfull + kSlotBars;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sdone + kSlotBars);
@@ -906,7 +914,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
       }
     }
     if constexpr (TE2) {  // sfull = slot freed by the store (streaming thread), sdone = box written (256)
-      for (int a = 0; a < kTe2Slots; ++a) {
+      for (int a = 0; a < kNs2; ++a) {
         mbar_init(&sfull[a], 1);
         mbar_init(&sdone[a], 256);
       }
@@ -919,7 +927,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
     prefetch_tmap(&tma_b);
   }
   if (warp == 1) {
-    if constexpr (PAIR) {
+    if constexpr (PAIR != 0) {
       tmem_alloc_pair(tmem_holder, Cfg::kTmemCols);
       tmem_relinquish_pair();
     } else {
@@ -929,7 +937,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if constexpr (PAIR) cluster_sync();  // the peer's barriers are initialised before any signal reaches them
+  if constexpr (PAIR != 0) cluster_sync();  // the peer's barriers are initialised before any signal reaches them
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
@@ -954,7 +962,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
           mbar_wait(&empty[stage], phase ^ 1u, abort_flag);
           uint8_t* a_dst = sA + stage * Cfg::kBytesA;
           uint8_t* b_dst = sB + stage * kBytesB;
-          if constexpr (PAIR) {
+          if constexpr (PAIR != 0) {
             // both CTAs' loads complete on the even CTA's barrier, which expects both
             const uint32_t bar0 = mapa_shared(&full[stage], 0);
             if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
@@ -1003,7 +1011,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
           }
         }
       }
-      if constexpr (PAIR) {
+      if constexpr (PAIR != 0) {
         // the even CTA's MMAs read this CTA's stages: wait until the last use of
         // each has been released before the CTA may leave
         for (int i = 0; i < kStages; ++i) {
@@ -1044,17 +1052,17 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
             const uint64_t bd =
                 B_MN ? make_sdesc(b_base + kk * kKStep, kLbo, 1024) : make_sdesc(b_base + kk * 32, 16, 1024);
             if constexpr (F8) umma_f8(d_tmem, ad, bd, p.idesc_f8, (kt > kt0 || kk > 0) ? 1u : 0u);
-            else if constexpr (PAIR) umma_f16_pair(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+            else if constexpr (PAIR != 0) umma_f16_pair(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
             else umma_f16(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
           }
-          if constexpr (PAIR) tc_commit_pair(&empty[stage]);
+          if constexpr (PAIR != 0) tc_commit_pair(&empty[stage]);
           else tc_commit(&empty[stage]);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        if constexpr (PAIR) tc_commit_pair(&tfull[acc]);
+        if constexpr (PAIR != 0) tc_commit_pair(&tfull[acc]);
         else tc_commit(&tfull[acc]);
       }
     }
@@ -1064,7 +1072,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
       prefetch_tmap(&te_in);
       prefetch_tmap(&te_out);
       if constexpr (TE) te_stream<BN>(&te_in, &te_out, p, te_slots, sfull, sdone, abort_flag, kSlotArea);
-      else te2_stream<BN>(&te_in, &te_out, p, te_slots, sdone, sfull, abort_flag);
+      else te2_stream<BN, kNs2>(&te_in, &te_out, p, te_slots, sdone, sfull, abort_flag);
     }
   } else {
     // ---------------- epilogue warps ----------------
@@ -1104,7 +1112,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
                     kSlotArea);
         te_k += nch;
       } else if constexpr (TE2) {
-        epi_te2_tile<BN>(e, p, tbase, quad * 32 + lane, row, sc, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN,
+        epi_te2_tile<BN, kNs2>(e, p, tbase, quad * 32 + lane, row, sc, e.kind == CDK_EPI_SWIGLU ? nt * (BN / 2) : nt * BN,
                          half, te_k, te_slots, sdone, sfull, abort_flag);
       } else if constexpr (VEC) {
         const int row0 = tile_row0(p, mt) + quad * 32;
@@ -1123,18 +1131,18 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
         default: break;
       }
       tc_fence_before();
-      if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(&tempty[acc], 0));
+      if constexpr (PAIR != 0) mbar_arrive_cluster(mapa_shared(&tempty[acc], 0));
       else mbar_arrive(&tempty[acc]);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if constexpr (PAIR) cluster_sync();  // neither CTA leaves while the pair's MMAs or signals may touch it
+  if constexpr (PAIR != 0) cluster_sync();  // neither CTA leaves while the pair's MMAs or signals may touch it
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    if constexpr (PAIR != 0) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
     else tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
 }
@@ -1247,13 +1255,13 @@ static int num_sms(int dev) {
   return cache[dev];
 }
 
-template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, int TE = 0, bool PAIR = false>
+template <int BN, bool A_MN, bool B_MN, bool VEC, bool F8 = false, int TE = 0, int PAIR = 0>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& te_in,
                        const CUtensorMap& te_out, const GemmParams& p, int grid, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   constexpr int threads = TE ? kThreadsTE : kThreads;
   constexpr int smem =
-      PAIR ? Cfg::smem_pair(TE) : TE == 1 ? Cfg::kSmemBytesTE : TE >= 2 ? Cfg::kSmemBytesTE2 : Cfg::kSmemBytes;
+      PAIR ? Cfg::smem_pair(TE, PAIR) : TE == 1 ? Cfg::kSmemBytesTE : TE >= 2 ? Cfg::kSmemBytesTE2 : Cfg::kSmemBytes;
   static_assert(TE != 4 || Cfg::kSmemBytesTE2 == Cfg::kStages * Cfg::kStageBytes + 1024 + 32768 + Cfg::kBarrierBytes,
                 "TEM 4 uses the store-only form's layout");
   static_assert(smem <= 232448, "shared memory");
@@ -1271,7 +1279,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     if (per_sm * Cfg::kTmemCols > 512) return -12;
     attr_set[dev] = true;
   }
-  if constexpr (PAIR) {
+  if constexpr (PAIR != 0) {
     if (!p.pair || (grid & 1)) return -14;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -1303,8 +1311,8 @@ static int pair_clusters(int dev) {
   if (dev < 0 || dev >= 64) return 0;
   if (!cache[dev]) {
     using Cfg = GemmCfg<256>;
-    auto kfn = gemm_bf16_kernel<256, false, false, true, false, 2, true>;
-    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::smem_pair(2)) != cudaSuccess)
+    auto kfn = gemm_bf16_kernel<256, false, false, true, false, 2, 1>;
+    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::smem_pair(2, 1)) != cudaSuccess)
       return 0;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -1314,7 +1322,7 @@ static int pair_clusters(int dev) {
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(2);
     cfg.blockDim = dim3(kThreadsTE);
-    cfg.dynamicSmemBytes = Cfg::smem_pair(2);
+    cfg.dynamicSmemBytes = Cfg::smem_pair(2, 1);
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
@@ -1327,10 +1335,10 @@ static int pair_clusters(int dev) {
   return cache[dev];
 }
 
-// CTA-pair form (K-major A): on by default for the store / RoPE and residual
-// epilogues; CDK_GEMM_PAIR=0 turns it off, CDK_GEMM_PAIR=all also uses it for
-// the SwiGLU forward and backward epilogues (which their epilogues, not their
-// operand traffic, limit: the pair form measured no faster there).
+// CTA-pair form (K-major A): on by default for the store / RoPE, SwiGLU and
+// residual epilogues; CDK_GEMM_PAIR=0 turns it off, CDK_GEMM_PAIR=all also
+// uses it for the SwiGLU backward epilogue (which its TMA-fed operand stream,
+// not the mainloop, limits: the pair form measured no faster there).
 static int pair_mode() {
   static const int m = [] {
     const char* v = getenv("CDK_GEMM_PAIR");
@@ -1363,10 +1371,12 @@ static int dispatch_major(bool a_mn, bool b_mn, int te, const CUtensorMap& ta, c
     return launch_gemm<BN, true, true, false, true>(ta, tb, ti, to, p, grid, s);
   }
   if constexpr (BN == 256) {
-    if (p.pair && te == 2 && !a_mn && !b_mn) return launch_gemm<256, false, false, true, false, 2, true>(ta, tb, ti, to, p, grid, s);
-    if (p.pair && te == 4 && !a_mn && !b_mn) return launch_gemm<256, false, false, true, false, 4, true>(ta, tb, ti, to, p, grid, s);
-    if (p.pair && te == 2 && !a_mn && b_mn) return launch_gemm<256, false, true, true, false, 2, true>(ta, tb, ti, to, p, grid, s);
-    if (p.pair && te == 1 && !a_mn && b_mn) return launch_gemm<256, false, true, true, false, 1, true>(ta, tb, ti, to, p, grid, s);
+    if (p.pair && te == 2 && !a_mn && !b_mn && p.dual)
+      return launch_gemm<256, false, false, true, false, 2, 2>(ta, tb, ti, to, p, grid, s);
+    if (p.pair && te == 2 && !a_mn && !b_mn) return launch_gemm<256, false, false, true, false, 2, 1>(ta, tb, ti, to, p, grid, s);
+    if (p.pair && te == 4 && !a_mn && !b_mn) return launch_gemm<256, false, false, true, false, 4, 1>(ta, tb, ti, to, p, grid, s);
+    if (p.pair && te == 2 && !a_mn && b_mn) return launch_gemm<256, false, true, true, false, 2, 1>(ta, tb, ti, to, p, grid, s);
+    if (p.pair && te == 1 && !a_mn && b_mn) return launch_gemm<256, false, true, true, false, 1, 1>(ta, tb, ti, to, p, grid, s);
   }
   if (p.pair) return -14;
   // TMA-fed epilogue (residual add / SwiGLU backward; K-major A)
@@ -1564,7 +1574,7 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   // (M a multiple of 256: no CTA of a pair holds a tile wholly below the last row)
   // (B MN-major: the 64-column groups are loaded as before, half of them per CTA)
   if (BN == 256 && !f8 && !a_mn && splits == 1 && (b_mn ? (tem == 1 || tem == 2) : (tem == 2 || tem == 4)) &&
-      M % (2 * kBM) == 0 && pair_enabled() && ((!dual && tem != 1) || pair_mode() == 2)) {
+      M % (2 * kBM) == 0 && pair_enabled() && (tem != 1 || pair_mode() == 2)) {
     const int clusters = pair_clusters(dev);
     if (clusters > 0) {
       if (!b_mn && !make_tmap(&tb, b, K, dual ? 2 * N : N, ldb, kBK, BN / 2)) return -11;

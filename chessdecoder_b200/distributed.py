@@ -279,3 +279,9 @@ class DataParallelStep:
         losses = self.forward_backward(db, metrics)
         self.optimizer_step()
         return losses
+
+    def run(self, batches, metrics=None):
+        """Pipelined loop over host batches (engine.TrainStep.run): yields
+        (i, host losses) for every batch, one step behind the device."""
+        from .engine import pipelined_steps
+        return pipelined_steps(self.step, batches, metrics)

@@ -1004,6 +1004,32 @@ class Heads:
 # ---------------------------------------------------------------------------
 # The training step
 # ---------------------------------------------------------------------------
+def pipelined_steps(step_fn, batches, metrics=None):
+    """Runs step_fn(batch, metrics) -> device losses over `batches`, keeping
+    one step in flight: each step's losses are copied to pinned host memory
+    behind its kernels and read after the next step has been enqueued, so the
+    host's batch preparation and launches overlap the device's work.  Yields
+    (i, host losses) in order; every step's losses are read."""
+    pending = None
+    for i, b in enumerate(batches):
+        losses = step_fn(b, metrics)
+        host = torch.empty(losses.shape, dtype=losses.dtype, pin_memory=losses.is_cuda)
+        host.copy_(losses, non_blocking=True)
+        ev = None
+        if losses.is_cuda:
+            ev = torch.cuda.Event()
+            ev.record()
+        if pending is not None:
+            if pending[2] is not None:
+                pending[2].synchronize()
+            yield pending[0], pending[1]
+        pending = (i, host, ev)
+    if pending is not None:
+        if pending[2] is not None:
+            pending[2].synchronize()
+        yield pending[0], pending[1]
+
+
 class TrainStep:
     """One optimizer step of ChessDecoder pretraining on B200.
 
@@ -1085,6 +1111,16 @@ class TrainStep:
         losses = self.forward_backward(db, metrics)
         self.optimizer_step()
         return losses
+
+    def run(self, batches, metrics=None):
+        """Training loop over host batches: yields (i, losses f32 [5] on the
+        host) for every batch, one step behind the device — batch i+1 is
+        prepared and its step enqueued while step i runs, then step i's losses
+        (copied into pinned memory at the end of its step) are read.  The
+        reference's loop overlaps the same way: its DataLoader workers build
+        the next batch and it reads losses only every log_every_n_steps
+        (train/train.py:150, 327)."""
+        return pipelined_steps(self.step, batches, metrics)
 
     def step_accumulated(self, batches, metrics=None):
         """One optimizer step over micro-batches (gradient_accumulation_steps

@@ -105,3 +105,22 @@ def test_ctypes_signatures_match_header_arity():
         n = 0 if params in ("", "void") else params.count(",") + 1
         assert name in _lib.SIGNATURES, name
         assert len(_lib.SIGNATURES[name][1]) == n, (name, n, len(_lib.SIGNATURES[name][1]))
+
+
+def test_pipelined_steps_reads_every_step_in_order():
+    """engine.pipelined_steps keeps one step in flight and yields every step's
+    losses in order (host tensors on a CPU-only run)."""
+    import torch
+    from chessdecoder_b200.engine import pipelined_steps
+    calls = []
+
+    def fake_step(b, metrics):
+        calls.append(b)
+        return torch.full((5,), float(b))
+
+    it = pipelined_steps(fake_step, iter(range(4)))
+    i0, l0 = next(it)
+    assert calls == [0, 1] and i0 == 0 and torch.equal(l0, torch.zeros(5))  # step 1 enqueued before step 0 is read
+    rest = list(it)
+    assert [i for i, _ in rest] == [1, 2, 3] and [float(l[0]) for _, l in rest] == [1.0, 2.0, 3.0]
+    assert list(pipelined_steps(fake_step, iter([]))) == []

@@ -61,3 +61,19 @@ def test_checkpoint_resume_continues_identically():
         pa, pb = a.store.param(n), b.store.param(n)
         assert torch.allclose(pa, pb, rtol=1e-4, atol=1e-6), n
     assert torch.allclose(a.store.exp_avg_sq, b.store.exp_avg_sq, rtol=1e-3, atol=1e-12)
+
+
+def test_pipelined_loop_equals_stepwise():
+    """TrainStep.run (batch i+1 enqueued before step i's losses are read)
+    gives the losses and parameters of step() with a read after each (equal
+    up to the order of the weight-gradient GEMMs' atomic split-K sums)."""
+    from chessdecoder_b200 import data
+    from chessdecoder_b200.config import step_from_config
+    a, b = step_from_config(CONF), step_from_config(CONF)
+    batches = data.synthetic_batches(4, 2, 256, seed=33)
+    seq = [a.step(x).cpu() for x in batches]
+    got = list(b.run(iter(batches)))
+    assert [i for i, _ in got] == list(range(len(batches)))
+    for (_, lv), ref in zip(got, seq):
+        assert torch.allclose(lv, ref, rtol=1e-3, atol=1e-5)
+    assert ((a.store.flat - b.store.flat).norm() / a.store.flat.norm()).item() < 1e-4
