@@ -365,6 +365,13 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                : "r"(addr));
 }
 
+// Logistic sigmoid 1 / (1 + e^-x) through the fast-division intrinsic (at most
+// 2 ulp from the correctly rounded quotient; the IEEE-exact division costs
+// several times more and made the SwiGLU-backward GEMM epilogue its bottleneck).
+// For x < -87 the denominator exceeds 2^126 and the intrinsic returns 0, where
+// the exact value is below 1e-38.
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

@@ -53,13 +53,15 @@ struct GemmCfg {
   // rows of a stage, so a stage is 32 KB and the ring six deep (five with the
   // TMA-fed epilogue's 64 KB of slots)
   static constexpr int kStageBytesPair = kBytesA + kBytesB / 2;
-  // (pair = 2: the SwiGLU store form, three output boxes per 64 columns,
-  // trades a stage for two more 16 KB output slots)
+  // pair = 2: the SwiGLU store form (three output boxes per 64 columns)
+  // trades a stage for two more 16 KB output slots
   static constexpr int stages_pair(int tem, int pair) { return tem == 1 || pair == 2 ? 5 : 6; }
   static constexpr int te2_slots_pair(int pair) { return pair == 2 ? 4 : kTe2Slots; }
+  static constexpr int slot_area_pair(int tem, int pair) {
+    return tem == 1 ? kTeSlots * kTeSlotBytes : te2_slots_pair(pair) * kTe2SlotBytes;
+  }
   static constexpr int smem_pair(int tem, int pair) {
-    return stages_pair(tem, pair) * kStageBytesPair + 1024 +
-           (tem == 1 ? kTeSlots * kTeSlotBytes : te2_slots_pair(pair) * kTe2SlotBytes) + kBarrierBytes;
+    return stages_pair(tem, pair) * kStageBytesPair + 1024 + slot_area_pair(tem, pair) + kBarrierBytes;
   }
 };
 
@@ -101,7 +103,7 @@ __device__ __forceinline__ int tile_row0(const GemmParams& p, int mt) {
   return (p.pair ? mt * 2 + (int)cluster_ctarank() : mt) * kBM;
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return x * sigmoid_fast(x); }
 
 // ---- epilogue store helpers (one thread = one row, kC consecutive columns) --
 constexpr int kC = 16;  // columns per epilogue chunk (one tcgen05.ld.32x32b.x16)
@@ -383,7 +385,7 @@ __device__ __forceinline__ void epi_vec(const EpiDev& e, const GemmParams& p, ui
       float dg[kC], du[kC];
       #pragma unroll
       for (int i = 0; i < kC; ++i) {
-        const float sg = 1.f / (1.f + __expf(-g[i]));
+        const float sg = sigmoid_fast(g[i]);
         du[i] = v[i] * g[i] * sg;
         dg[i] = v[i] * up[i] * (sg * (1.f + g[i] * (1.f - sg)));
       }
@@ -550,7 +552,7 @@ __device__ __forceinline__ void epi_tile(const EpiDev& e, const GemmParams& p, u
       #pragma unroll
       for (int i = 0; i < kC; ++i) {
         const float g = r[i], up = a2[i];
-        const float sg = 1.f / (1.f + __expf(-g));
+        const float sg = sigmoid_fast(g);
         du[i] = v[i] * g * sg;
         dg[i] = v[i] * up * (sg * (1.f + g * (1.f - sg)));
       }
@@ -695,7 +697,7 @@ __device__ __forceinline__ void epi_te_tile(const EpiDev& e, uint32_t tbase, int
           const float2 g = __bfloat1622float2(hg[i]), u = __bfloat1622float2(hu[i]);
           const int ai = (q & 1) * 8 + 2 * i;
           const float d0 = __uint_as_float(acc[ai]) * sc, d1 = __uint_as_float(acc[ai + 1]) * sc;
-          const float s0 = 1.f / (1.f + __expf(-g.x)), s1 = 1.f / (1.f + __expf(-g.y));
+          const float s0 = sigmoid_fast(g.x), s1 = sigmoid_fast(g.y);
           og[i] = pack_bf16(d0 * u.x * (s0 * (1.f + g.x * (1.f - s0))), d1 * u.y * (s1 * (1.f + g.y * (1.f - s1))));
           ou[i] = pack_bf16(d0 * g.x * s0, d1 * g.y * s1);
         }
@@ -878,7 +880,8 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   constexpr bool TE2 = TEM == 2 || TEM == 3;  // store-only / reduce-add forms share the slots and the stream
   constexpr int kNs2 = PAIR && TEM == 2 ? Cfg::te2_slots_pair(PAIR) : kTe2Slots;  // store-only output slots
   constexpr int kSlotArea =
-      TEM == 1 ? kTeSlots * kTeSlotBytes : TEM == 4 ? 32768 : TE2 ? kNs2 * kTe2SlotBytes : 0;
+      PAIR != 0 && TEM != 4 ? Cfg::slot_area_pair(TEM, PAIR)
+      : TEM == 1 ? kTeSlots * kTeSlotBytes : TEM == 4 ? 32768 : TE2 ? kNs2 * kTe2SlotBytes : 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -888,7 +891,8 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
-  constexpr int kSlotBars = TEM == 1 ? kTeSlots : TEM == 4 ? 2 : TE2 ? kNs2 : 0;
+  // TMA-fed form: a barrier pair per slot of its smallest box (16 KB)
+  constexpr int kSlotBars = TEM == 1 ? kSlotArea / 16384 : TEM == 4 ? 2 : TE2 ? kNs2 : 0;
   uint64_t* sfull = tempty + 2;      // TE / store-only forms
   uint64_t* sdone = sfull + kSlotBars;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sdone + kSlotBars);
@@ -1335,20 +1339,15 @@ static int pair_clusters(int dev) {
   return cache[dev];
 }
 
-// CTA-pair form (K-major A): on by default for the store / RoPE, SwiGLU and
-// residual epilogues; CDK_GEMM_PAIR=0 turns it off, CDK_GEMM_PAIR=all also
-// uses it for the SwiGLU backward epilogue (which its TMA-fed operand stream,
-// not the mainloop, limits: the pair form measured no faster there).
-static int pair_mode() {
-  static const int m = [] {
+// CTA-pair form (K-major A): on by default; CDK_GEMM_PAIR=0 keeps every GEMM
+// on the one-CTA form.
+static bool pair_enabled() {
+  static const bool on = [] {
     const char* v = getenv("CDK_GEMM_PAIR");
-    if (v && v[0] == '0') return 0;
-    if (v && std::strcmp(v, "all") == 0) return 2;
-    return 1;
+    return !(v && v[0] == '0');
   }();
-  return m;
+  return on;
 }
-static bool pair_enabled() { return pair_mode() > 0; }
 
 template <int BN>
 static int dispatch_major(bool a_mn, bool b_mn, int te, const CUtensorMap& ta, const CUtensorMap& tb,
@@ -1574,7 +1573,7 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   // (M a multiple of 256: no CTA of a pair holds a tile wholly below the last row)
   // (B MN-major: the 64-column groups are loaded as before, half of them per CTA)
   if (BN == 256 && !f8 && !a_mn && splits == 1 && (b_mn ? (tem == 1 || tem == 2) : (tem == 2 || tem == 4)) &&
-      M % (2 * kBM) == 0 && pair_enabled() && (tem != 1 || pair_mode() == 2)) {
+      M % (2 * kBM) == 0 && pair_enabled()) {
     const int clusters = pair_clusters(dev);
     if (clusters > 0) {
       if (!b_mn && !make_tmap(&tb, b, K, dual ? 2 * N : N, ldb, kBK, BN / 2)) return -11;

@@ -77,7 +77,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ du, long lon
     #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 d = __bfloat1622float2(hd[j]), g = __bfloat1622float2(hg[j]), u = __bfloat1622float2(hu[j]);
-      const float s0 = 1.f / (1.f + __expf(-g.x)), s1 = 1.f / (1.f + __expf(-g.y));
+      const float s0 = sigmoid_fast(g.x), s1 = sigmoid_fast(g.y);
       fg[2 * j] = d.x * u.x * (s0 * (1.f + g.x * (1.f - s0)));
       fg[2 * j + 1] = d.y * u.y * (s1 * (1.f + g.y * (1.f - s1)));
       fu[2 * j] = d.x * g.x * s0;

@@ -78,8 +78,8 @@ int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b, int64_t l
  * (M = 256 MMAs over two SMs) keeps resident on the current device, or 0 when
  * that form is off (environment CDK_GEMM_PAIR=0) or unavailable.  The pair
  * form serves bf16 GEMMs with K-major A, M a multiple of 256, no split-K and a
- * ROPE_BF16, STORE_BF16, SWIGLU or RESID_F32 (K-major B) epilogue; DSWIGLU
- * too with CDK_GEMM_PAIR=all.  Results equal the one-CTA form's bit for bit. */
+ * ROPE_BF16, STORE_BF16, SWIGLU, RESID_F32 (K-major B) or DSWIGLU (MN-major B)
+ * epilogue.  Results equal the one-CTA form's bit for bit. */
 int cdk_gemm_pair_clusters(void);
 
 /* ---- fp8 (the fp8 training variant: e4m3 weights / activations, e5m2

@@ -3,7 +3,7 @@ forward GEMMs of the training step (QKV projection with RoPE, gate|up
 projection with SwiGLU, output and down projections with the fp32 residual
 add, plain bf16 store) and the backward's input-gradient GEMMs (MN-major
 weight operand: plain bf16 store, SwiGLU backward epilogue) computed with the pair form on for every form that can
-use it (CDK_GEMM_PAIR=all) and off (CDK_GEMM_PAIR=0), each in its own process
+use it (the default) and off (CDK_GEMM_PAIR=0), each in its own process
 because the switch is read once per process.  The pair form must reproduce the one-CTA form bit for bit (each
 output element is the same sequence of K=16 products accumulated in fp32) and
 match a PyTorch fp32 statement of the operation (bf16 outputs: relative
@@ -60,7 +60,7 @@ def _child(out_path):
 
 def _run(tmp_path, pair):
     out = tmp_path / f"pair{pair}.pt"
-    env = dict(os.environ, CDK_GEMM_PAIR="all" if pair else "0")
+    env = dict(os.environ, CDK_GEMM_PAIR="1" if pair else "0")
     subprocess.run([sys.executable, __file__, str(out)], env=env, cwd=ROOT, check=True, timeout=600)
     return torch.load(out)
 
