@@ -872,7 +872,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   // TEM 1: TMA-fed form with 64 KB of slots (3-stage ring at BN=256); TEM 4: the
   // same for the residual add with 2 x 16 KB slots and the full ring
   constexpr bool TE = TEM == 1 || TEM == 4;
-  static_assert(!PAIR || (BN == 256 && !A_MN && !F8 && (TEM == 1 || TEM == 2 || TEM == 4)), "pair form");
+  static_assert(!PAIR || (BN == 256 && !A_MN && !F8 && (TEM == 1 || TEM == 2)), "pair form");
   static_assert(PAIR != 2 || TEM == 2, "wide output slots: store-only form");
   constexpr int kStages = PAIR ? Cfg::stages_pair(TEM, PAIR) : TEM == 1 ? Cfg::kStagesTE : Cfg::kStages;
   constexpr int kBytesB = PAIR ? Cfg::kBytesB / 2 : Cfg::kBytesB;
@@ -880,7 +880,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   constexpr bool TE2 = TEM == 2 || TEM == 3;  // store-only / reduce-add forms share the slots and the stream
   constexpr int kNs2 = PAIR && TEM == 2 ? Cfg::te2_slots_pair(PAIR) : kTe2Slots;  // store-only output slots
   constexpr int kSlotArea =
-      PAIR != 0 && TEM != 4 ? Cfg::slot_area_pair(TEM, PAIR)
+      PAIR != 0 ? Cfg::slot_area_pair(TEM, PAIR)
       : TEM == 1 ? kTeSlots * kTeSlotBytes : TEM == 4 ? 32768 : TE2 ? kNs2 * kTe2SlotBytes : 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1373,9 +1373,9 @@ static int dispatch_major(bool a_mn, bool b_mn, int te, const CUtensorMap& ta, c
     if (p.pair && te == 2 && !a_mn && !b_mn && p.dual)
       return launch_gemm<256, false, false, true, false, 2, 2>(ta, tb, ti, to, p, grid, s);
     if (p.pair && te == 2 && !a_mn && !b_mn) return launch_gemm<256, false, false, true, false, 2, 1>(ta, tb, ti, to, p, grid, s);
-    if (p.pair && te == 4 && !a_mn && !b_mn) return launch_gemm<256, false, false, true, false, 4, 1>(ta, tb, ti, to, p, grid, s);
     if (p.pair && te == 2 && !a_mn && b_mn) return launch_gemm<256, false, true, true, false, 2, 1>(ta, tb, ti, to, p, grid, s);
     if (p.pair && te == 1 && !a_mn && b_mn) return launch_gemm<256, false, true, true, false, 1, 1>(ta, tb, ti, to, p, grid, s);
+    if (p.pair && te == 1 && !a_mn && !b_mn) return launch_gemm<256, false, false, true, false, 1, 1>(ta, tb, ti, to, p, grid, s);
   }
   if (p.pair) return -14;
   // TMA-fed epilogue (residual add / SwiGLU backward; K-major A)
@@ -1568,16 +1568,19 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // the residual add keeps the full mainloop ring (its mainloop is the slower half)
   // unless CDK_GEMM_TE_RESID_SLOTS=4 asks for the 4-slot / 3-stage layout
-  const int tem = te ? (kind == CDK_EPI_RESID_F32 && !te_resid_deep() ? 4 : 1) : te2 ? 2 : te3 ? 3 : 0;
+  int tem = te ? (kind == CDK_EPI_RESID_F32 && !te_resid_deep() ? 4 : 1) : te2 ? 2 : te3 ? 3 : 0;
   // CTA-pair form: 256-row units, B split between the two CTAs of a cluster
   // (M a multiple of 256: no CTA of a pair holds a tile wholly below the last row)
   // (B MN-major: the 64-column groups are loaded as before, half of them per CTA)
-  if (BN == 256 && !f8 && !a_mn && splits == 1 && (b_mn ? (tem == 1 || tem == 2) : (tem == 2 || tem == 4)) &&
+  // (its 32 KB stages leave room for the residual's 64 KB four-slot layout,
+  // which the one-CTA form can only have at three stages)
+  if (BN == 256 && !f8 && !a_mn && splits == 1 && (b_mn ? (tem == 1 || tem == 2) : tem >= 1 && tem != 3) &&
       M % (2 * kBM) == 0 && pair_enabled()) {
     const int clusters = pair_clusters(dev);
     if (clusters > 0) {
       if (!b_mn && !make_tmap(&tb, b, K, dual ? 2 * N : N, ldb, kBK, BN / 2)) return -11;
       p.pair = 1;
+      if (tem == 4) tem = 1;
       p.m_tiles = (int)((M + 2 * kBM - 1) / (2 * kBM));
       units = (long long)p.m_tiles * n_tiles;
       grid = 2 * (int)(units < clusters ? units : clusters);
