@@ -872,7 +872,7 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   // TEM 1: TMA-fed form with 64 KB of slots (3-stage ring at BN=256); TEM 4: the
   // same for the residual add with 2 x 16 KB slots and the full ring
   constexpr bool TE = TEM == 1 || TEM == 4;
-  static_assert(!PAIR || (BN == 256 && !A_MN && !F8 && (TEM == 1 || TEM == 2)), "pair form");
+  static_assert(!PAIR || (BN == 256 && !F8 && (A_MN ? B_MN && TEM == 3 : TEM == 1 || TEM == 2)), "pair form");
   static_assert(PAIR != 2 || TEM == 2, "wide output slots: store-only form");
   constexpr int kStages = PAIR ? Cfg::stages_pair(TEM, PAIR) : TEM == 1 ? Cfg::kStagesTE : Cfg::kStages;
   constexpr int kBytesB = PAIR ? Cfg::kBytesB / 2 : Cfg::kBytesB;
@@ -971,7 +971,12 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
             const uint32_t bar0 = mapa_shared(&full[stage], 0);
             if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
             const int k0 = kt * kBK;
-            tma_load_2d_pair(a_dst, &tma_a, bar0, k0, m0);
+            if constexpr (A_MN) {  // this CTA's 128 rows as two 64-row groups of kBK k rows
+              tma_load_2d_pair(a_dst, &tma_a, bar0, m0, k0);
+              tma_load_2d_pair(a_dst + 8192, &tma_a, bar0, m0 + 64, k0);
+            } else {
+              tma_load_2d_pair(a_dst, &tma_a, bar0, k0, m0);
+            }
             if constexpr (B_MN) {  // this CTA's BN/2 columns as 64-column groups of kBK k rows
               #pragma unroll
               for (int i = 0; i < BN / 128; ++i)
@@ -1376,6 +1381,7 @@ static int dispatch_major(bool a_mn, bool b_mn, int te, const CUtensorMap& ta, c
     if (p.pair && te == 2 && !a_mn && b_mn) return launch_gemm<256, false, true, true, false, 2, 1>(ta, tb, ti, to, p, grid, s);
     if (p.pair && te == 1 && !a_mn && b_mn) return launch_gemm<256, false, true, true, false, 1, 1>(ta, tb, ti, to, p, grid, s);
     if (p.pair && te == 1 && !a_mn && !b_mn) return launch_gemm<256, false, false, true, false, 1, 1>(ta, tb, ti, to, p, grid, s);
+    if (p.pair && te == 3 && a_mn && b_mn) return launch_gemm<256, true, true, false, false, 3, 1>(ta, tb, ti, to, p, grid, s);
   }
   if (p.pair) return -14;
   // TMA-fed epilogue (residual add / SwiGLU backward; K-major A)
@@ -1443,27 +1449,27 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   const int bk = f8 ? 2 * kBK : kBK;  // elements per 128-byte k block
   const long long k_tiles = (K + bk - 1) / bk;
 
-  int splits = 1;
-  if (kind == CDK_EPI_ATOMIC_F32) {
-    if (split_k > 0) {
-      splits = split_k;
-    } else {
-      // Pick the split that best fills whole waves while keeping >= 8 k-tiles per unit.
-      const long long tiles = m_tiles * n_tiles;
-      double best = -1.0;
-      for (int s = 1; s <= 32; ++s) {
-        if (k_tiles / s < 8 && s > 1) break;
-        const long long units = tiles * s;
-        const long long waves = (units + sms - 1) / sms;
-        const double eff = (double)units / (double)(waves * sms);
-        if (eff > best + 0.02) {
-          best = eff;
-          splits = s;
-        }
-        if (eff > 0.97) break;
+  // Split-K (ATOMIC_F32 only): the split that best fills whole waves of `slots`
+  // (SMs, or CTA pairs) with `tiles` output tiles while keeping >= 8 k-tiles per unit.
+  auto choose_splits = [&](long long tiles, long long slots) {
+    int best_s = 1;
+    if (kind != CDK_EPI_ATOMIC_F32) return 1;
+    if (split_k > 0) return split_k;
+    double best = -1.0;
+    for (int s = 1; s <= 32; ++s) {
+      if (k_tiles / s < 8 && s > 1) break;
+      const long long units = tiles * s;
+      const long long waves = (units + slots - 1) / slots;
+      const double eff = (double)units / (double)(waves * slots);
+      if (eff > best + 0.02) {
+        best = eff;
+        best_s = s;
       }
+      if (eff > 0.97) break;
     }
-  }
+    return best_s;
+  };
+  int splits = choose_splits(m_tiles * n_tiles, sms);
   long long k_per = (k_tiles + splits - 1) / splits;
   splits = (int)((k_tiles + k_per - 1) / k_per);
 
@@ -1573,16 +1579,24 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   // (M a multiple of 256: no CTA of a pair holds a tile wholly below the last row)
   // (B MN-major: the 64-column groups are loaded as before, half of them per CTA)
   // (its 32 KB stages leave room for the residual's 64 KB four-slot layout,
-  // which the one-CTA form can only have at three stages)
-  if (BN == 256 && !f8 && !a_mn && splits == 1 && (b_mn ? (tem == 1 || tem == 2) : tem >= 1 && tem != 3) &&
-      M % (2 * kBM) == 0 && pair_enabled()) {
+  // which the one-CTA form can only have at three stages).  Weight gradients
+  // (both operands MN-major, split-K reduce-add) re-choose the split for the
+  // pairs.
+  const bool pair_form = a_mn ? (b_mn && tem == 3) : splits == 1 && (b_mn ? (tem == 1 || tem == 2) : tem >= 1 && tem != 3);
+  if (BN == 256 && !f8 && pair_form && M % (2 * kBM) == 0 && pair_enabled()) {
     const int clusters = pair_clusters(dev);
     if (clusters > 0) {
       if (!b_mn && !make_tmap(&tb, b, K, dual ? 2 * N : N, ldb, kBK, BN / 2)) return -11;
       p.pair = 1;
       if (tem == 4) tem = 1;
       p.m_tiles = (int)((M + 2 * kBM - 1) / (2 * kBM));
-      units = (long long)p.m_tiles * n_tiles;
+      if (kind == CDK_EPI_ATOMIC_F32) {
+        int s2 = choose_splits((long long)p.m_tiles * n_tiles, clusters);
+        const long long kp = (k_tiles + s2 - 1) / s2;
+        p.k_per_split = (int)kp;
+        p.splits = (int)((k_tiles + kp - 1) / kp);
+      }
+      units = (long long)p.m_tiles * n_tiles * p.splits;
       grid = 2 * (int)(units < clusters ? units : clusters);
     }
   }

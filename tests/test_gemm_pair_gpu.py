@@ -1,13 +1,16 @@
 """CTA-pair GEMM form (two SMs per 256-row tile, M=256 tcgen05 MMAs): the
 forward GEMMs of the training step (QKV projection with RoPE, gate|up
 projection with SwiGLU, output and down projections with the fp32 residual
-add, plain bf16 store) and the backward's input-gradient GEMMs (MN-major
-weight operand: plain bf16 store, SwiGLU backward epilogue) computed with the pair form on for every form that can
+add, plain bf16 store), the backward's input-gradient GEMMs (MN-major
+weight operand: plain bf16 store, SwiGLU backward epilogue) and its
+weight-gradient GEMMs (both operands MN-major, split-K bulk reduce-add) computed with the pair form on for every form that can
 use it (the default) and off (CDK_GEMM_PAIR=0), each in its own process
 because the switch is read once per process.  The pair form must reproduce the one-CTA form bit for bit (each
 output element is the same sequence of K=16 products accumulated in fp32) and
 match a PyTorch fp32 statement of the operation (bf16 outputs: relative
-Frobenius error <= 1e-2; fp32 outputs: <= 2e-3).
+Frobenius error <= 1e-2; fp32 outputs: <= 2e-3).  The weight gradients sum
+split-K partial products in an order that depends on the split, so the two
+forms agree there to 1e-5 (relative) instead of bit for bit.
 """
 import os
 import subprocess
@@ -23,6 +26,8 @@ ROOT = Path(__file__).resolve().parents[1]
 # (M, N, K): the step's shapes at a smaller token count, a K that is not a
 # multiple of 64, an M that is not a multiple of 256 (one-CTA form in both runs)
 SHAPES = [(4096, 3072, 1024), (2048, 1024, 1536), (1024, 1024, 200), (1280, 512, 512), (1000, 1024, 512)]
+# weight gradients dW [M, N] = dY^T X over K tokens
+WGRAD = [(3072, 1024, 8192), (1024, 1536, 4096), (1000, 512, 2048)]
 
 
 def _inputs(M, N, K, seed):
@@ -30,6 +35,12 @@ def _inputs(M, N, K, seed):
     bf = lambda *s: (torch.randn(*s, generator=g, device="cuda") * 0.1).to(torch.bfloat16)  # noqa: E731
     return (bf(M, K), bf(N, K), bf(2 * N, K), torch.randn(M, N, generator=g, device="cuda"), bf(K, N),
             bf(M, 2 * N))
+
+
+def _wgrad_inputs(M, N, K, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return ((torch.randn(K, M, generator=g, device="cuda") * 0.1).to(torch.bfloat16),
+            (torch.randn(K, N, generator=g, device="cuda") * 0.1).to(torch.bfloat16))
 
 
 def _child(out_path):
@@ -54,6 +65,12 @@ def _child(out_path):
         Kn.gemm(X, Wt, b_mn=True, kind=Kn.EPI_DSWIGLU, out=dgu, aux=gu_in, half_n=N, N=N)
         torch.cuda.synchronize()
         res[i] = {k: v.cpu() for k, v in dict(store=o, rope=r, u=u, gu=gu, resid=y, dx=dx, dgu=dgu).items()}
+    for i, (M, N, K) in enumerate(WGRAD):
+        dY, X = _wgrad_inputs(M, N, K, 77 + i)
+        dw = torch.zeros(M, N, device="cuda")
+        Kn.gemm(dY, X, a_mn=True, b_mn=True, kind=Kn.EPI_ATOMIC_F32, out=dw)
+        torch.cuda.synchronize()
+        res[("w", i)] = dw.cpu()
     res["error"] = Kn.get_error()
     torch.save(res, out_path)
 
@@ -95,6 +112,12 @@ def test_pair_form_matches_one_cta_form(tmp_path):
         sg = torch.sigmoid(g)
         assert rel(on[i]["dgu"][:, :N], du * up * (sg * (1 + g * (1 - sg)))) < 1e-2
         assert rel(on[i]["dgu"][:, N:], du * g * sg) < 1e-2
+    for i, (M, N, K) in enumerate(WGRAD):
+        dY, X = (t.cpu() for t in _wgrad_inputs(M, N, K, 77 + i))
+        ref = dY.float().t() @ X.float()
+        a, b = on[("w", i)], off[("w", i)]
+        assert ((a - ref).norm() / ref.norm()).item() < 2e-3, (M, N, K)
+        assert ((a - b).norm() / b.norm()).item() < 1e-5, (M, N, K)
 
 
 if __name__ == "__main__":
