@@ -314,21 +314,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pseq = seq - a.n_causal;
       const int row0 = seq * S;
       const long long lrow = ((long long)seq * H + h) * S;
-      // row metadata (double-buffered per item)
+      // row metadata (double-buffered per item): all of a lane's global loads
+      // first (one round trip, overlapping the wait for the buffer); causal
+      // rows: block id = first row of the block = row
+      constexpr int kJ = kMaxS / 32;
+      float Lv[kJ], Dv[kJ];
+      int fv[kJ], bv[kJ];
+      #pragma unroll
+      for (int j = 0; j < kJ; ++j) {
+        const int i = lane + 32 * j;
+        Lv[j] = 0.f;
+        Dv[j] = 0.f;
+        fv[j] = bv[j] = i;
+        if (i < S) {
+          Lv[j] = __ldg(a.lse + lrow + i);
+          Dv[j] = __ldg(a.dsum + lrow + i);
+          if (prefix) {
+            const long long o = (long long)pseq * S + i;
+            fv[j] = __ldg(a.first + o);
+            bv[j] = __ldg(a.bid + o);
+          }
+        }
+      }
       const int m = k & 1;
       if (k >= 2) mbar_wait(&sm.mempty[m], ((k >> 1) - 1) & 1, abort_flag);
       Meta& mt = sm.meta[m];
-      const int32_t* brow = prefix ? a.bid + (long long)pseq * S : nullptr;
-      const int32_t* frow = prefix ? a.first + (long long)pseq * S : nullptr;
       bool runs_ok = true;  // a row whose id differs from the previous row's opens that id's first run
-      for (int i = lane; i < kMaxS; i += 32) {
+      #pragma unroll
+      for (int j = 0; j < kJ; ++j) {
+        const int i = lane + 32 * j;
         const bool ok = i < S;
-        mt.L[i] = ok ? a.lse[lrow + i] : 0.f;
-        mt.D[i] = ok ? a.dsum[lrow + i] : 0.f;
-        mt.first[i] = ok ? (prefix ? frow[i] : i) : S;
-        const int b = ok ? (prefix ? brow[i] : i) : -1;
+        // the previous row's id: lane - 1's, or lane 31's of the previous group
+        int prev = __shfl_up_sync(0xffffffffu, bv[j], 1);
+        const int prev31 = __shfl_sync(0xffffffffu, bv[j > 0 ? j - 1 : 0], 31);
+        if (lane == 0) prev = prev31;
+        mt.L[i] = Lv[j];
+        mt.D[i] = Dv[j];
+        mt.first[i] = ok ? fv[j] : S;
+        const int b = ok ? bv[j] : -1;
         mt.bid[i] = b;
-        if (prefix && ok && i > 0 && b != brow[i - 1] && frow[i] != i) runs_ok = false;
+        if (prefix && ok && i > 0 && b != prev && fv[j] != i) runs_ok = false;
       }
       runs_ok = __all_sync(0xffffffffu, runs_ok);
       if (lane == 0) mt.contig = runs_ok ? 1 : 0;

@@ -9,8 +9,9 @@
 // run while this one computes.  The item's two 128-row query tiles are two
 // independent pipelines:
 //
-//   warp 0          producer: per item, the row metadata (block id, last
-//                   visible key) into the slot, then the TMA loads
+//   warp 0          producer: per item, the TMA loads, then (while they
+//                   fly) the row metadata (block id, last visible key) into
+//                   the slot
 //   warp 1 / 2      MMA issuer of query tile 0 / 1 (whole warp, one elected lane):
 //                   S_t = Q_t K^T (M=128, N = keys <= 256) into TMEM region t,
 //                   then O_t = P_t V with P_t read from TMEM (A operand) and V
@@ -58,7 +59,9 @@ struct FwdSmem {
   int32_t contig[2];       // 1: every block id of the sequence is one contiguous run of rows
   float red_max[2][2][128];  // [tile][key half][row]: partial row maxima of the two threads of a row
   float red_sum[2][2][128];  // partial row sums
-  uint64_t full[2], empty[2];
+  // per item slot: Q|K landed, V landed, row metadata written; Q|K free again
+  // (the item's S products done), V and metadata free again (P V products done)
+  uint64_t qk_full[2], v_full[2], meta_full[2], qk_empty[2], v_empty[2];
   uint64_t sfull[2], pfull[2], ofull[2], oempty[2];
   uint32_t tmem_base;
   int abort;
@@ -175,8 +178,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&sm.full[s], 32);
-      mbar_init(&sm.empty[s], n_tiles);
+      mbar_init(&sm.qk_full[s], 1);
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.meta_full[s], 32);
+      mbar_init(&sm.qk_empty[s], n_tiles);
+      mbar_init(&sm.v_empty[s], n_tiles);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.sfull[t], 1);
@@ -206,37 +212,66 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int seq = item / H, h = item - seq * H;
       const bool prefix = seq >= a.n_causal;
       const int pseq = seq - a.n_causal;
-      if (u > 0) mbar_wait(&sm.empty[s], (u - 1) & 1, abort_flag);
+      const int row0 = seq * S;
+      // Q and K as soon as the S products of the item two back have read the
+      // slot's, V (and then the row metadata, which the softmax reads until P
+      // is formed) once its P V products have.  The last query tile sees every
+      // key, so K and V are always ceil(S / 64) boxes.
+      if (u > 0) mbar_wait(&sm.qk_empty[s], (u - 1) & 1, abort_flag);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&sm.qk_full[s], (uint32_t)(2 * nq64) * kBox);
+        for (int b = 0; b < nq64; ++b) {
+          tma_load_2d(sm.slot[s].Q + b * kBox, &tqkv, &sm.qk_full[s], h * kHd, row0 + b * 64);
+          tma_load_2d(sm.slot[s].K + b * kBox, &tqkv, &sm.qk_full[s], E + h * kHd, row0 + b * 64);
+        }
+      }
+      __syncwarp();
+      // the item's row metadata into registers first (all of a lane's loads in
+      // one round trip, overlapping the wait for the slot's V); causal rows:
+      // block id = row, last visible key = row
+      constexpr int kJ = kMaxS / 32;
+      int bv[kJ], lv[kJ], fv[kJ];
+      #pragma unroll
+      for (int j = 0; j < kJ; ++j) {
+        const int i = lane + 32 * j;
+        bv[j] = lv[j] = fv[j] = i;
+        if (prefix && i < S) {
+          const long long o = (long long)pseq * S + i;
+          bv[j] = __ldg(a.bid + o);
+          lv[j] = __ldg(a.last + o);
+          fv[j] = __ldg(a.first + o);
+        }
+      }
       const int nk0 = tile_keys(a, 0, prefix, pseq);
       const int nk1 = n_tiles > 1 ? tile_keys(a, 1, prefix, pseq) : 0;
-      const int32_t* brow = prefix ? a.bid + (long long)pseq * S : nullptr;
-      const int32_t* lrow = prefix ? a.last + (long long)pseq * S : nullptr;
-      const int32_t* frow = prefix ? a.first + (long long)pseq * S : nullptr;
+      if (u > 0) mbar_wait(&sm.v_empty[s], (u - 1) & 1, abort_flag);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&sm.v_full[s], (uint32_t)nq64 * kBox);
+        for (int b = 0; b < nq64; ++b)
+          tma_load_2d(sm.slot[s].V + b * kBox, &tqkv, &sm.v_full[s], 2 * E + h * kHd, row0 + b * 64);
+      }
+      __syncwarp();
       bool runs_ok = true;  // a row whose id differs from the previous row's opens the id's first run
-      for (int i = lane; i < kMaxS; i += 32) {
+      #pragma unroll
+      for (int j = 0; j < kJ; ++j) {
+        const int i = lane + 32 * j;
         const bool ok = i < S;
-        const int b = ok ? (prefix ? brow[i] : i) : -1;
+        // the previous row's id: lane - 1's, or lane 31's of the previous group
+        int prev = __shfl_up_sync(0xffffffffu, bv[j], 1);
+        const int prev31 = __shfl_sync(0xffffffffu, bv[j > 0 ? j - 1 : 0], 31);
+        if (lane == 0) prev = prev31;
+        const int b = ok ? bv[j] : -1;
         sm.bid[s][i] = b;
-        sm.hi[s][i] = ok ? (prefix ? max(i, lrow[i]) : i) : -1;
-        if (prefix && ok && i > 0 && b != brow[i - 1] && frow[i] != i) runs_ok = false;
+        sm.hi[s][i] = ok ? max(i, lv[j]) : -1;
+        if (prefix && ok && i > 0 && b != prev && fv[j] != i) runs_ok = false;
       }
       runs_ok = __all_sync(0xffffffffu, runs_ok);
       if (lane == 0) {
         sm.nk[s][0] = nk0;
         sm.nk[s][1] = nk1;
         sm.contig[s] = runs_ok ? 1 : 0;
-        const int nkb = (max(nk0, nk1) + 63) / 64;
-        const int row0 = seq * S;
-        mbar_arrive_expect_tx(&sm.full[s], (uint32_t)(nq64 + 2 * nkb) * kBox);
-        for (int b = 0; b < nq64; ++b)
-          tma_load_2d(sm.slot[s].Q + b * kBox, &tqkv, &sm.full[s], h * kHd, row0 + b * 64);
-        for (int b = 0; b < nkb; ++b) {
-          tma_load_2d(sm.slot[s].K + b * kBox, &tqkv, &sm.full[s], E + h * kHd, row0 + b * 64);
-          tma_load_2d(sm.slot[s].V + b * kBox, &tqkv, &sm.full[s], 2 * E + h * kHd, row0 + b * 64);
-        }
-      } else {
-        mbar_arrive(&sm.full[s]);
       }
+      mbar_arrive(&sm.meta_full[s]);  // 32 arrivals: the slot's metadata is written
     }
   } else if (warp == 1 || warp == 2) {
     // ---- MMA issuer of query tile t --------------------------------------
@@ -247,7 +282,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc_o = make_idesc_bf16(128, kHd, false, true);
       for (int k = 0; k < n_local; ++k) {
         const int s = k & 1, u = k >> 1;
-        mbar_wait(&sm.full[s], u & 1, abort_flag);
+        mbar_wait(&sm.meta_full[s], u & 1, abort_flag);
+        mbar_wait(&sm.qk_full[s], u & 1, abort_flag);
         if (k > 0) mbar_wait(&sm.oempty[t], (k - 1) & 1, abort_flag);
         tc_fence_after();
         const int nk = sm.nk[s][t];
@@ -259,7 +295,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_f16_w(treg, make_sdesc(qa + kk * 32, 16, 1024), make_sdesc(kb + kk * 32, 16, 1024), idesc_s,
                    kk > 0 ? 1u : 0u);
         tc_commit_w(&sm.sfull[t]);
+        tc_commit_w(&sm.qk_empty[s]);
         mbar_wait(&sm.pfull[t], k & 1, abort_flag);
+        mbar_wait(&sm.v_full[s], u & 1, abort_flag);
         tc_fence_after();
         const uint32_t vb = smem_u32(sm.slot[s].V);
         // P of keys [0, nk/2) sits in columns [0, nk/4), P of keys [nk/2, nk)
@@ -276,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         tc_commit_w(&sm.ofull[t]);
-        tc_commit_w(&sm.empty[s]);
+        tc_commit_w(&sm.v_empty[s]);
       }
     }
   } else if (warp >= 4) {
@@ -297,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = k & 1, u = k >> 1;
         const int item = (int)blockIdx.x + k * G;
         const int seq = item / H, h = item - seq * H;
-        mbar_wait(&sm.full[s], u & 1, abort_flag);  // row metadata of the slot
+        mbar_wait(&sm.meta_full[s], u & 1, abort_flag);  // row metadata of the slot
         const int nk = sm.nk[s][t];
         const int* bid = sm.bid[s];
         const int my_bid = row_ok ? bid[i] : -2;
