@@ -917,12 +917,13 @@ def main():
                 "timing": f"CUDA events around each GEMM launch, {gemm_steps} steps after the timed region"}
     # DRAM bytes (read + write) of one launch of the largest GEMM shape, QKV + RoPE
     # (M=32768, N=3072, K=1024), from one `ncu --set full --clock-control none`
-    # capture of `python bench.py --probe gemm --kind rope` (TMA-stored
-    # epilogue): 73.5 MB read (the algorithmic A + W bytes, no re-reads) + 146.4 MB
-    # written inside the launch; the launch's algorithmic bytes are 275 MB.
-    roofline["traffic"] = 219.9e6
-    roofline["traffic_launch"] = {"shape": "M32768 N3072 K1024 (QKV + RoPE epilogue)",
-                                  "dram_read": 73.5e6, "dram_write": 146.4e6, "algorithmic_bytes": 275.0e6}
+    # capture of `python bench.py --probe gemm --kind rope` (CTA-pair form,
+    # TMA-stored epilogue): 73.5 MB read (the algorithmic A + W bytes, no
+    # re-reads) + 147.6 MB written inside the launch; the launch's algorithmic
+    # bytes are 275 MB.
+    roofline["traffic"] = 221.1e6
+    roofline["traffic_launch"] = {"shape": "M32768 N3072 K1024 (QKV + RoPE epilogue, CTA pair)",
+                                  "dram_read": 73.5e6, "dram_write": 147.6e6, "algorithmic_bytes": 275.0e6}
 
     flops = step_flops(cfg, pool, args.seq)
     mfu_spec = flops / (dev_ms / 1000.0) / 2.25e15
