@@ -1033,7 +1033,10 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
+    // the whole warp runs the issue loop and one elected lane issues: operands
+    // stay warp-uniform (one thread of a diverged warp computing descriptors
+    // issues an MMA per 75-150 cycles, about what an N=256 MMA takes)
+    if (rank == 0) {
       constexpr uint32_t idesc = make_idesc_bf16(PAIR ? 2 * kBM : kBM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
@@ -1060,19 +1063,19 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
                 A_MN ? make_sdesc(a_base + kk * kKStep, kLbo, 1024) : make_sdesc(a_base + kk * 32, 16, 1024);
             const uint64_t bd =
                 B_MN ? make_sdesc(b_base + kk * kKStep, kLbo, 1024) : make_sdesc(b_base + kk * 32, 16, 1024);
-            if constexpr (F8) umma_f8(d_tmem, ad, bd, p.idesc_f8, (kt > kt0 || kk > 0) ? 1u : 0u);
-            else if constexpr (PAIR != 0) umma_f16_pair(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
-            else umma_f16(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+            if constexpr (F8) umma_f8_w(d_tmem, ad, bd, p.idesc_f8, (kt > kt0 || kk > 0) ? 1u : 0u);
+            else if constexpr (PAIR != 0) umma_f16_pair_w(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+            else umma_f16_w(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
           }
-          if constexpr (PAIR != 0) tc_commit_pair(&empty[stage]);
-          else tc_commit(&empty[stage]);
+          if constexpr (PAIR != 0) tc_commit_pair_w(&empty[stage]);
+          else tc_commit_w(&empty[stage]);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        if constexpr (PAIR != 0) tc_commit_pair(&tfull[acc]);
-        else tc_commit(&tfull[acc]);
+        if constexpr (PAIR != 0) tc_commit_pair_w(&tfull[acc]);
+        else tc_commit_w(&tfull[acc]);
       }
     }
   } else if (TEM && warp == 10) {
