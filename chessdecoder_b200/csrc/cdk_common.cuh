@@ -514,6 +514,17 @@ __device__ __forceinline__ void umma_f16_pair_w(uint32_t tmem_d, uint64_t adesc,
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// 8-bit operands (kind::f8f6f4), M=256 over the pair; as umma_f16_pair_w.
+__device__ __forceinline__ void umma_f8_pair_w(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive on the barrier at this shared-memory offset in both CTAs of the pair
 // (CTA mask 0b11) once every MMA issued so far by the warp is done (one
 // elected lane of a converged warp).

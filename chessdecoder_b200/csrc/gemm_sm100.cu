@@ -872,7 +872,8 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
   // TEM 1: TMA-fed form with 64 KB of slots (3-stage ring at BN=256); TEM 4: the
   // same for the residual add with 2 x 16 KB slots and the full ring
   constexpr bool TE = TEM == 1 || TEM == 4;
-  static_assert(!PAIR || (BN == 256 && !F8 && (A_MN ? B_MN && TEM == 3 : TEM == 1 || TEM == 2)), "pair form");
+  static_assert(!PAIR || (BN == 256 && (A_MN ? !F8 && B_MN && TEM == 3 : TEM == 1 || TEM == 2 || TEM == 3)),
+                "pair form");
   static_assert(PAIR != 2 || TEM == 2, "wide output slots: store-only form");
   constexpr int kStages = PAIR ? Cfg::stages_pair(TEM, PAIR) : TEM == 1 ? Cfg::kStagesTE : Cfg::kStages;
   constexpr int kBytesB = PAIR ? Cfg::kBytesB / 2 : Cfg::kBytesB;
@@ -970,17 +971,18 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
             // both CTAs' loads complete on the even CTA's barrier, which expects both
             const uint32_t bar0 = mapa_shared(&full[stage], 0);
             if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
-            const int k0 = kt * kBK;
+            const int k0 = kt * (F8 ? 2 * kBK : kBK);  // element coordinate of this 128-byte k block
             if constexpr (A_MN) {  // this CTA's 128 rows as two 64-row groups of kBK k rows
               tma_load_2d_pair(a_dst, &tma_a, bar0, m0, k0);
               tma_load_2d_pair(a_dst + 8192, &tma_a, bar0, m0 + 64, k0);
             } else {
               tma_load_2d_pair(a_dst, &tma_a, bar0, k0, m0);
             }
-            if constexpr (B_MN) {  // this CTA's BN/2 columns as 64-column groups of kBK k rows
+            if constexpr (B_MN) {  // this CTA's BN/2 columns as 128-byte-wide groups (64 bf16 / 128 fp8)
+              constexpr int kGrpE = F8 ? 128 : 64, kGrpB = F8 ? 16384 : 8192;
               #pragma unroll
-              for (int i = 0; i < BN / 128; ++i)
-                tma_load_2d_pair(b_dst + i * 8192, &tma_b, bar0, n0 + (int)rank * (BN / 2) + 64 * i, k0);
+              for (int i = 0; i < (BN / 2) / kGrpE; ++i)
+                tma_load_2d_pair(b_dst + i * kGrpB, &tma_b, bar0, n0 + (int)rank * (BN / 2) + kGrpE * i, k0);
             } else {
               tma_load_2d_pair(b_dst, &tma_b, bar0, k0,
                                p.dual ? n0 + (rank ? p.b_off : 0) : n0 + (int)rank * (BN / 2));
@@ -1063,7 +1065,8 @@ __global__ void __launch_bounds__(TEM ? kThreadsTE : kThreads, 1)
                 A_MN ? make_sdesc(a_base + kk * kKStep, kLbo, 1024) : make_sdesc(a_base + kk * 32, 16, 1024);
             const uint64_t bd =
                 B_MN ? make_sdesc(b_base + kk * kKStep, kLbo, 1024) : make_sdesc(b_base + kk * 32, 16, 1024);
-            if constexpr (F8) umma_f8_w(d_tmem, ad, bd, p.idesc_f8, (kt > kt0 || kk > 0) ? 1u : 0u);
+            if constexpr (F8 && PAIR != 0) umma_f8_pair_w(d_tmem, ad, bd, p.idesc_f8, (kt > kt0 || kk > 0) ? 1u : 0u);
+            else if constexpr (F8) umma_f8_w(d_tmem, ad, bd, p.idesc_f8, (kt > kt0 || kk > 0) ? 1u : 0u);
             else if constexpr (PAIR != 0) umma_f16_pair_w(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
             else umma_f16_w(d_tmem, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
           }
@@ -1364,6 +1367,17 @@ static int dispatch_major(bool a_mn, bool b_mn, int te, const CUtensorMap& ta, c
   const CUtensorMap &ti = te_in, &to = te_out;
   // the coalesced epilogues (forward kinds and bf16 stores) have their own instantiations
   if (p.scale_inv_a != nullptr) {  // fp8 operands
+    if (p.pair) {
+      if constexpr (BN == 256) {
+        if (te == 2 && !a_mn && !b_mn && p.dual)
+          return launch_gemm<256, false, false, true, true, 2, 2>(ta, tb, ti, to, p, grid, s);
+        if (te == 2 && !a_mn && !b_mn) return launch_gemm<256, false, false, true, true, 2, 1>(ta, tb, ti, to, p, grid, s);
+        if (te == 1 && !a_mn && !b_mn) return launch_gemm<256, false, false, true, true, 1, 1>(ta, tb, ti, to, p, grid, s);
+        if (te == 2 && !a_mn && b_mn) return launch_gemm<256, false, true, true, true, 2, 1>(ta, tb, ti, to, p, grid, s);
+        if (te == 3 && !a_mn && !b_mn) return launch_gemm<256, false, false, false, true, 3, 1>(ta, tb, ti, to, p, grid, s);
+      }
+      return -14;
+    }
     if (te == 1 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, true, 1>(ta, tb, ti, to, p, grid, s);
     if (te == 4 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, true, 4>(ta, tb, ti, to, p, grid, s);
     if (te == 2 && !a_mn && !b_mn) return launch_gemm<BN, false, false, true, true, 2>(ta, tb, ti, to, p, grid, s);
@@ -1385,6 +1399,7 @@ static int dispatch_major(bool a_mn, bool b_mn, int te, const CUtensorMap& ta, c
     if (p.pair && te == 1 && !a_mn && b_mn) return launch_gemm<256, false, true, true, false, 1, 1>(ta, tb, ti, to, p, grid, s);
     if (p.pair && te == 1 && !a_mn && !b_mn) return launch_gemm<256, false, false, true, false, 1, 1>(ta, tb, ti, to, p, grid, s);
     if (p.pair && te == 3 && a_mn && b_mn) return launch_gemm<256, true, true, false, false, 3, 1>(ta, tb, ti, to, p, grid, s);
+    if (p.pair && te == 3 && !a_mn && !b_mn) return launch_gemm<256, false, false, false, false, 3, 1>(ta, tb, ti, to, p, grid, s);
   }
   if (p.pair) return -14;
   // TMA-fed epilogue (residual add / SwiGLU backward; K-major A)
@@ -1585,12 +1600,20 @@ static int gemm_impl(const void* a, int64_t lda, int a_mn, const void* b, int64_
   // which the one-CTA form can only have at three stages).  Weight gradients
   // (both operands MN-major, split-K reduce-add) re-choose the split for the
   // pairs.
-  const bool pair_form = a_mn ? (b_mn && tem == 3) : splits == 1 && (b_mn ? (tem == 1 || tem == 2) : tem >= 1 && tem != 3);
-  if (BN == 256 && !f8 && pair_form && M % (2 * kBM) == 0 && pair_enabled()) {
+  // (8-bit operands: K-major A; the forward, residual, dX and K-major
+  // weight-gradient forms)
+  const bool pair_form =
+      a_mn ? (!f8 && b_mn && tem == 3)
+           : tem == 3 ? !b_mn
+                      : splits == 1 && (b_mn ? (tem == 2 || (!f8 && tem == 1)) : tem == 1 || tem == 2 || tem == 4);
+  if (BN == 256 && pair_form && M % (2 * kBM) == 0 && pair_enabled()) {
     const int clusters = pair_clusters(dev);
     if (clusters > 0) {
-      if (!b_mn && !make_tmap(&tb, b, K, dual ? 2 * N : N, ldb, kBK, BN / 2)) return -11;
+      if (!b_mn && (f8 ? !make_tmap_u8(&tb, b, K, dual ? 2 * N : N, ldb, bk, BN / 2)
+                       : !make_tmap(&tb, b, K, dual ? 2 * N : N, ldb, kBK, BN / 2)))
+        return -11;
       p.pair = 1;
+      if (f8) p.idesc_f8 = make_idesc_f8(2 * kBM, BN, a_fmt, b_fmt, false, b_mn != 0);
       if (tem == 4) tem = 1;
       p.m_tiles = (int)((M + 2 * kBM - 1) / (2 * kBM));
       if (kind == CDK_EPI_ATOMIC_F32) {

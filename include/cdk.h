@@ -77,9 +77,11 @@ int cdk_gemm_bf16(const void* a, int64_t lda, int a_mn, const void* b, int64_t l
 /* cdk_gemm_pair_clusters: clusters of two CTAs that the CTA-pair GEMM form
  * (M = 256 MMAs over two SMs) keeps resident on the current device, or 0 when
  * that form is off (environment CDK_GEMM_PAIR=0) or unavailable.  The pair
- * form serves bf16 GEMMs with K-major A, M a multiple of 256, no split-K and a
- * ROPE_BF16, STORE_BF16, SWIGLU, RESID_F32 (K-major B) or DSWIGLU (MN-major B)
- * epilogue.  Results equal the one-CTA form's bit for bit. */
+ * form serves GEMMs with M a multiple of 256: bf16 and 8-bit with K-major A
+ * (ROPE_BF16, STORE_BF16, SWIGLU, RESID_F32; DSWIGLU and STORE_BF16 with B
+ * MN-major; ATOMIC_F32 with K-major B), and bf16 ATOMIC_F32 with both operands
+ * MN-major (split-K chosen for the pairs).  Results equal the one-CTA form's
+ * bit for bit, except the split-K sums, whose order follows the split. */
 int cdk_gemm_pair_clusters(void);
 
 /* ---- fp8 (the fp8 training variant: e4m3 weights / activations, e5m2

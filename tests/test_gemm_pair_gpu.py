@@ -3,7 +3,9 @@ forward GEMMs of the training step (QKV projection with RoPE, gate|up
 projection with SwiGLU, output and down projections with the fp32 residual
 add, plain bf16 store), the backward's input-gradient GEMMs (MN-major
 weight operand: plain bf16 store, SwiGLU backward epilogue) and its
-weight-gradient GEMMs (both operands MN-major, split-K bulk reduce-add) computed with the pair form on for every form that can
+weight-gradient GEMMs (both operands MN-major, split-K bulk reduce-add), and
+the fp8 recipe's forms with 8-bit operands (e4m3 x e4m3 store, SwiGLU and
+residual; e5m2 x e4m3 dX with the weight MN-major) computed with the pair form on for every form that can
 use it (the default) and off (CDK_GEMM_PAIR=0), each in its own process
 because the switch is read once per process.  The pair form must reproduce the one-CTA form bit for bit (each
 output element is the same sequence of K=16 products accumulated in fp32) and
@@ -71,6 +73,25 @@ def _child(out_path):
         Kn.gemm(dY, X, a_mn=True, b_mn=True, kind=Kn.EPI_ATOMIC_F32, out=dw)
         torch.cuda.synchronize()
         res[("w", i)] = dw.cpu()
+    sc = torch.ones(1, device="cuda")
+    for i, (M, N, K) in enumerate(SHAPES[:3]):
+        g = torch.Generator(device="cuda").manual_seed(555 + i)
+        q = lambda *sh: (torch.randn(*sh, generator=g, device="cuda") * 2).to(torch.float8_e4m3fn)  # noqa: E731
+        X8, W8, W13_8 = q(M, K if K % 16 == 0 else 256), q(N, K if K % 16 == 0 else 256), q(2 * N, K if K % 16 == 0 else 256)
+        h = torch.randn(M, N, generator=g, device="cuda")
+        o = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        Kn.gemm(X8, W8, kind=Kn.EPI_STORE_BF16, out=o, fp8=(0, 0, sc, sc))
+        u = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        gu = torch.empty(M, 2 * N, device="cuda", dtype=torch.bfloat16)
+        Kn.gemm(X8, W13_8, kind=Kn.EPI_SWIGLU, out=u, out2=gu, half_n=N, fp8=(0, 0, sc, sc))
+        y = torch.empty(M, N, device="cuda")
+        Kn.gemm(X8, W8, kind=Kn.EPI_RESID_F32, out=y, resid=h, fp8=(0, 0, sc, sc))
+        G8 = (torch.randn(M, N, generator=g, device="cuda")).to(torch.float8_e5m2)
+        Wd = q(N, N)  # [K = N rows, N] read MN-major
+        dx = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        Kn.gemm(G8, Wd, b_mn=True, kind=Kn.EPI_STORE_BF16, out=dx, fp8=(1, 0, sc, sc))
+        torch.cuda.synchronize()
+        res[("f8", i)] = {k: v.cpu() for k, v in dict(store=o, u=u, gu=gu, resid=y, dx=dx).items()}
     res["error"] = Kn.get_error()
     torch.save(res, out_path)
 
@@ -112,6 +133,9 @@ def test_pair_form_matches_one_cta_form(tmp_path):
         sg = torch.sigmoid(g)
         assert rel(on[i]["dgu"][:, :N], du * up * (sg * (1 + g * (1 - sg)))) < 1e-2
         assert rel(on[i]["dgu"][:, N:], du * g * sg) < 1e-2
+    for i in range(3):
+        for k in ("store", "u", "gu", "resid", "dx"):
+            assert torch.equal(on[("f8", i)][k], off[("f8", i)][k]), ("fp8", i, k)
     for i, (M, N, K) in enumerate(WGRAD):
         dY, X = (t.cpu() for t in _wgrad_inputs(M, N, K, 77 + i))
         ref = dY.float().t() @ X.float()
