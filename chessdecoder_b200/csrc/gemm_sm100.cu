@@ -1,15 +1,22 @@
-// Warp-specialised persistent bf16 GEMM for sm_100a: TMA -> shared-memory ring
-// -> tcgen05.mma (one elected thread) -> double-buffered TMEM accumulators ->
-// eight epilogue warps with fused epilogues (RoPE, SwiGLU, residual add,
-// split-K atomic accumulation).
+// Warp-specialised persistent bf16 / fp8 GEMM for sm_100a: TMA -> shared-memory
+// ring -> tcgen05.mma (issued by one elect.sync lane of the MMA warp) ->
+// double-buffered TMEM accumulators -> eight epilogue warps with fused
+// epilogues (RoPE, SwiGLU forward / backward, residual add, split-K bulk
+// reduce-add).
 //
 // Replaces the nn.Linear forward/backward calls of the reference model
 // (chessdecoder/models/model.py:96-108, 119-136) that PyTorch dispatches to
-// cuBLAS.  Roles inside one CTA (320 threads, one CTA per SM):
+// cuBLAS.  Roles inside one CTA (320 threads, 352 with the TMA-fed / TMA-stored
+// epilogues, one CTA per SM):
 //   warp 0      TMA producer (lane 0)
-//   warp 1      TMEM allocator + MMA issuer (lane 0)
+//   warp 1      TMEM allocator + MMA issuer (whole warp, one elected lane)
 //   warps 2..9  epilogue; warp w owns TMEM lanes 32*(w%4) .. +31, warps w and
 //               w+4 split the columns of those rows
+//   warp 10     epilogue operand / output streaming (lane 0), when present
+// CTA-pair form (the default where M is a multiple of 256): clusters of two
+// CTAs walk 256-row units; each loads its 128 A rows and half of the B tile,
+// the even CTA issues tcgen05.mma.cta_group::2 with M=256, and each CTA's
+// epilogue reads its own 128 accumulator rows.
 #include "../../include/cdk.h"
 #include "cdk_common.cuh"
 
